@@ -1,0 +1,477 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gaussian-canvas rasterizer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one 1920x1080 frame per rank, N=200,000
+2D Gaussians (means uniform, log-scale ~ N(ln 2, 0.3), rot ~ U[0, pi),
+opacity = sigmoid(N(0,1)), rgb ~ U[0,1], seeded synthetic data), 16x16 tiles,
+3-sigma tile lists, fp32.  One step = preprocess -> deterministic binning ->
+forward render -> backward (dL/dimage ~ N(0,1)) producing gradients of mean,
+conic, scale, rotation, opacity and rgb.  The metric is rasterized Mpix/s of
+fwd+bwd (H*W*frames / time); fwd-only Mpix/s and ms/frame are reported too.
+
+value: device-resident inputs, per-step CUDA events on the launch stream, L2
+flushed (256 MiB write) between steps outside the events, max over ranks.
+e2e:   the public autograd API (oss_cuda.rasterize_gaussians + backward) with
+pinned host inputs copied in and image + gradients copied out every step.
+Multi-GPU: every rank renders its own frame (weak scaling, no collective on
+the data path).  --impl reference times the CPU restatement of the reference
+algorithm (oracle/) on the host cores on a bounded band of tile rows.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "open-supersampling_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "rasterized Mpix/s and ms/frame fwd & fwd+bwd at 1080p, 200k Gaussians"
+UNIT = "Mpix/s"
+CONFIGS = {
+    # name: (H, W, N, log-scale mean, log-scale sd)
+    "config2": (1080, 1920, 200_000, math.log(2.0), 0.3),
+    "config1": (540, 960, 16_384, math.log(1.5), 0.3),
+}
+SURVEY_FLOPS_FWD = 15.0  # FP32 flops per pixel-Gaussian evaluation, forward (+1 exp)
+SURVEY_FLOPS_BWD = 40.0  # backward (+1 exp)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="config2")
+    ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- setup
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def make_inputs(h, w, n, ls_mean, ls_sd, seed):
+    rng = np.random.default_rng(seed)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    scale = np.exp(rng.standard_normal((n, 2)) * ls_sd + ls_mean).astype(np.float32)
+    rot = (rng.random(n) * math.pi).astype(np.float32)
+    opacity = (1.0 / (1.0 + np.exp(-rng.standard_normal(n)))).astype(np.float32)
+    rgb = rng.random((n, 3)).astype(np.float32)
+    grad = rng.standard_normal((3, h, w)).astype(np.float32)
+    return dict(xy=xy, scale=scale, rot=rot, opacity=opacity, rgb=rgb, grad=grad)
+
+
+class ClockSampler:
+    """SM clock and throttle reasons of this process's GPU via NVML, sampled
+    every 20 ms on a background thread during the timed region."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self._handle = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # noqa: BLE001 - clocks are reported, not required
+            self.error = repr(exc)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for name, mask in self.REASONS.items():
+                    if bits & mask:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._handle is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- device pipeline
+
+class Pipeline:
+    """The hot path over the C ABI, with a CUDA event between each stage."""
+
+    def __init__(self, inp, h, w, mode, device):
+        from oss_cuda import _lib
+
+        self.lib = _lib.lib()
+        self._lib = _lib
+        self.h, self.w, self.mode = h, w, mode
+        self.n = inp["xy"].shape[0]
+        self.d = {k: torch.from_numpy(v).to(device) for k, v in inp.items()}
+        self.ntx = (w + 15) // 16
+        self.nty = (h + 15) // 16
+        self.tiles = self.ntx * self.nty
+        f32 = dict(device=device, dtype=torch.float32)
+        i32 = dict(device=device, dtype=torch.int32)
+        n = self.n
+        self.conic = torch.empty((n, 3), **f32)
+        self.aabb = torch.empty((n, 4), **i32)
+        self.pair_offset = torch.empty((n + 1,), **i32)
+        self.geo = torch.empty((n, 8), **f32)
+        self.total = torch.empty((1,), device=device, dtype=torch.int64)
+        self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device=device,
+                                        dtype=torch.uint8)
+        self.image = torch.empty((3, h, w), **f32)
+        self.grads = {k: torch.empty(s, **f32) for k, s in
+                      (("d_xy", (n, 2)), ("d_conic", (n, 3)), ("d_rgb", (n, 3)), ("d_opacity", (n,)),
+                       ("d_scale", (n, 2)), ("d_rot", (n,)))}
+        self.tile_offsets = torch.empty((self.tiles + 1,), **i32)
+        self.capacity = 0
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        self.device = device
+
+    def _ensure(self, pairs):
+        if pairs > self.capacity:
+            dev = self.device
+            self.capacity = int(pairs * 1.1) + 1024
+            self.gid_sorted = torch.empty((self.capacity,), device=dev, dtype=torch.int32)
+            nb = max(self.lib.oss_bin_pairs_scratch_bytes(self.n, self.capacity, self.tiles),
+                     self.lib.oss_render_backward_scratch_bytes(self.capacity, 3))
+            self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
+
+    def step(self):
+        lib, chk, d, ev = self.lib, self._lib.check, self.d, self.events
+        s = torch.cuda.current_stream().cuda_stream
+        n, h, w = self.n, self.h, self.w
+        ev[0].record()
+        chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
+                                   d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
+                                   self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
+                                   self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
+        ev[1].record()
+        pairs = int(self.total.item())  # the path's one host sync
+        self._ensure(pairs)
+        self.pairs = pairs
+        ev[2].record()
+        chk(lib.oss_bin_pairs(n, h, w, self.mode, self.aabb.data_ptr(), self.pair_offset.data_ptr(), pairs,
+                              self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.scratch.data_ptr(),
+                              self.scratch.numel(), s), "bin")
+        ev[3].record()
+        chk(lib.oss_render_forward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(), d["opacity"].data_ptr(),
+                                   self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.image.data_ptr(),
+                                   s), "forward")
+        ev[4].record()
+        chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
+                                          d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
+                                          pairs, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
+                                          d["grad"].data_ptr(), self.scratch.data_ptr(), s), "backward_pairs")
+        ev[5].record()
+        g = self.grads
+        chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), d["rgb"].data_ptr(),
+                                      d["opacity"].data_ptr(), d["scale"].data_ptr(), d["rot"].data_ptr(),
+                                      g["d_xy"].data_ptr(), g["d_conic"].data_ptr(), g["d_rgb"].data_ptr(),
+                                      g["d_opacity"].data_ptr(), g["d_scale"].data_ptr(), g["d_rot"].data_ptr(), s),
+            "reduce")
+        ev[6].record()
+
+    def stage_ms(self):
+        ev = self.events
+        return {"prepare": ev[0].elapsed_time(ev[1]), "host_sync": ev[1].elapsed_time(ev[2]),
+                "bin": ev[2].elapsed_time(ev[3]), "forward": ev[3].elapsed_time(ev[4]),
+                "backward_pairs": ev[4].elapsed_time(ev[5]), "reduce": ev[5].elapsed_time(ev[6]),
+                "fwd_path": ev[0].elapsed_time(ev[4]), "total": ev[0].elapsed_time(ev[6])}
+
+    def launches_per_step(self):
+        """Kernels of liboss_b200.so launched by one step (see csrc/)."""
+        scan = 3
+        bits = max(0, int(self.tiles - 1).bit_length())
+        passes = (bits + 7) // 8
+        prepare = 1 + scan
+        binning = 1 + scan + passes * (1 + scan + 1)
+        return prepare + binning + 1 + 1 + 1
+
+    def evaluations(self):
+        """Pixel-Gaussian evaluations: sum over tiles of valid pixels x list length."""
+        offs = self.tile_offsets.cpu().numpy().astype(np.int64)
+        lens = np.diff(offs)
+        ty, tx = np.divmod(np.arange(self.tiles), self.ntx)
+        rows = np.minimum(16, self.h - ty * 16)
+        cols = np.minimum(16, self.w - tx * 16)
+        return int(np.sum(lens * rows * cols))
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+def cpu_sample(inp, h, w, mode_name, budget_s, threads=None):
+    """Oracle (CPU restatement) fwd+bwd: full preprocess + binning, raster on a band of
+    tile rows sized to about budget_s, extrapolated linearly to the frame."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as orc
+
+    if threads:
+        orc.set_num_threads(threads)
+    mode = orc.MODES[mode_name]
+    ntx, nty, t_all = orc.tiles(h, w)
+    feat = inp["rgb"]
+    t0 = time.perf_counter()
+    conic, _, _, gid, offs = orc.lists(inp["xy"], inp["scale"], inp["rot"], h, w, mode)
+    t_bin = time.perf_counter() - t0
+
+    def band(rows):
+        lo, hi = 0, min(nty, rows) * ntx
+        t1 = time.perf_counter()
+        orc.render_forward(inp["xy"], conic, feat, gid, offs, h, w, inp["opacity"], (lo, hi))
+        orc.render_backward(inp["xy"], conic, feat, gid, offs, inp["grad"], h, w, inp["opacity"], (lo, hi))
+        return time.perf_counter() - t1
+
+    t_row = band(1)
+    rows = max(1, min(nty, int(budget_s / max(t_row, 1e-6))))
+    t_band = band(rows) if rows > 1 else t_row
+    frac = rows / nty
+    t_frame = t_bin + t_band / frac
+    return {
+        "value": h * w / t_frame / 1e6,
+        "unit": UNIT,
+        "cores": orc.num_threads(),
+        "kind": "port",
+        "sample": (f"oracle/oss_oracle.c: preprocess+binning of all {inp['xy'].shape[0]} Gaussians "
+                   f"({t_bin:.3f} s) + fwd+bwd on {rows}/{nty} tile rows ({t_band:.3f} s), raster time "
+                   f"scaled by {1 / frac:.2f} to the full frame"),
+        "ms_per_frame": t_frame * 1e3,
+    }
+
+
+# ----------------------------------------------------------------------------- arms
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    h, w, n, lsm, lss = CONFIGS[args.config]
+    inp = make_inputs(h, w, n, lsm, lss, seed=1234)
+    budget = max(0.2, min(5.0, 120.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_sample(inp, h, w, args.binning, budget)
+    vals, last = [], None
+    for _ in range(args.steps):
+        last = cpu_sample(inp, h, w, args.binning, budget)
+        vals.append(last["value"])
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": h * w / value / 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {w}x{h}, N={n}, F=3, 16x16 tiles, {args.binning} lists, fwd+bwd"},
+        "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    line["cpu_baseline"]["value"] = value
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    from oss_cuda import _lib, rasterize_gaussians
+
+    h, w, n, lsm, lss = CONFIGS[args.config]
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = make_inputs(h, w, n, lsm, lss, seed=1234 + rank)
+    mode = _lib.BINNING_MODES[args.binning]
+    pipe = Pipeline(inp, h, w, mode, device)
+    flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
+    for _ in range(max(3, args.warmup)):
+        pipe.step()
+        flush.zero_()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    stages = {k: 0.0 for k in pipe.stage_ms()}
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clocks:
+        wall0 = time.perf_counter()
+        for _ in range(K):
+            flush.zero_()
+            pipe.step()
+            torch.cuda.synchronize()  # per-step events are read below; keeps host and device in step
+            for k, v in pipe.stage_ms().items():
+                stages[k] += v
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    total_ms = torch.tensor([stages["total"], stages["fwd_path"]], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    step_ms = float(total_ms[0]) / K
+    fwd_ms = float(total_ms[1]) / K
+    pixels = h * w * world
+    value = pixels / (step_ms * 1e-3) / 1e6
+    stage_avg = {k: v / K for k, v in stages.items()}
+
+    # roofline of the dominant kernel (FP32 SIMT; no tensor cores on this path)
+    evals = pipe.evaluations()
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    sm_max = float(peaks.get("sm_max_mhz", 1965.0))
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    fp32_peak = sms * 128 * 2 * sm_max * 1e6 / 1e12  # TFLOP/s, FMA = 2 flops
+    mufu_peak = sms * 16 * sm_max * 1e6  # exp2 per second
+    if stage_avg["backward_pairs"] >= stage_avg["forward"]:
+        kname, kms, fpe = "k_render_bwd (backward per-pair partials)", stage_avg["backward_pairs"], SURVEY_FLOPS_BWD
+    else:
+        kname, kms, fpe = "k_render_fwd (forward render)", stage_avg["forward"], SURVEY_FLOPS_FWD
+    achieved = evals * fpe / (kms * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "dram_traffic_config2.txt"
+    if tfile.exists() and args.config == "config2" and args.binning == "tight3sigma":
+        for line in tfile.read_text().splitlines():
+            if line.startswith(kname.split()[0] + " "):
+                traffic = float(line.split()[1])
+    roofline = {
+        "bound": "fp32", "kernel": kname, "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+        "frac": achieved / fp32_peak, "traffic": traffic,
+        "peak_note": f"FP32 FMA peak {sms} SMs x 128 lanes x 2 x {sm_max:.0f} MHz (max SM clock of "
+                     "MEASURED_PEAKS.json); MEASURED_PEAKS.json holds no FP32 figure",
+        "evaluations": evals, "flops_per_evaluation": fpe,
+        "mufu_frac": (evals / (kms * 1e-3)) / mufu_peak,
+        "ms": kms,
+    }
+    # HBM roofline of the memory-bound stages (preprocess + binning)
+    pairs = pipe.pairs
+    bin_bytes = n * (20 + 32 + 32 + 4) + pairs * 4 * 6 + pipe.tiles * 4 * 3
+    hbm = {"stages": "prepare+bin", "bytes": bin_bytes,
+           "achieved_gbs": bin_bytes / ((stage_avg["prepare"] + stage_avg["bin"]) * 1e-3) / 1e9,
+           "peak_gbs": peaks.get("hbm_gbs")}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE config distributions)",
+        "config": {"workload": f"{args.config}: {w}x{h}, N={n}, F=3 rgb x opacity, 16x16 tiles, {args.binning} "
+                               "lists, fwd+bwd per frame, one frame per rank",
+                   "l2": "256 MiB flush between steps (outside the step events)", "pairs": pairs,
+                   "frames_per_rank": 1},
+        "fwd_mpix_s": pixels / (fwd_ms * 1e-3) / 1e6, "fwd_ms_per_frame": fwd_ms, "fwdbwd_ms_per_frame": step_ms,
+        "stages_ms": stage_avg, "roofline": roofline, "hbm_stages": hbm,
+        "gpu_launches": pipe.launches_per_step() * K,
+        "clocks": clocks.summary(), "wall_s": wall,
+    }
+
+    # e2e: public autograd API, host buffers in and out
+    if not args.no_e2e:
+        host = {k: torch.from_numpy(v).pin_memory() for k, v in inp.items()}
+        outs = {"image": torch.empty((3, h, w), dtype=torch.float32).pin_memory()}
+        for k, s in (("xy", (n, 2)), ("scale", (n, 2)), ("rot", (n,)), ("rgb", (n, 3)), ("opacity", (n,))):
+            outs["d_" + k] = torch.empty(s, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            d = {k: v.to(device, non_blocking=True) for k, v in host.items()}
+            leaves = [d[k].requires_grad_(True) for k in ("xy", "scale", "rot", "rgb", "opacity")]
+            img = rasterize_gaussians(leaves[0], leaves[1], leaves[2], leaves[3], h, w, binning=args.binning,
+                                      opacity=leaves[4])
+            gr = torch.autograd.grad(img, leaves, d["grad"])
+            outs["image"].copy_(img.detach(), non_blocking=True)
+            for k, gt in zip(("xy", "scale", "rot", "rgb", "opacity"), gr):
+                outs["d_" + k].copy_(gt, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        ke = max(3, min(K, 50))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(ke):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([e0.elapsed_time(e1) / ke], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        h2d = sum(v.numel() * 4 for v in host.values())
+        d2h = sum(v.numel() * 4 for v in outs.values())
+        line["e2e"] = {"value": pixels / (float(e2e_ms[0]) * 1e-3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms[0]), "steps": ke,
+                       "api": "oss_cuda.rasterize_gaussians + torch.autograd.grad"}
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_sample(inp, h, w, args.binning, budget_s=8.0).items()
+                                if k != "ms_per_frame"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,205 @@
+/*
+ * oss_raster.h -- C ABI of the B200 (sm_100a) 2D Gaussian-canvas tile rasterizer
+ * and canvas warp.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL means the legacy default stream).  Nothing
+ * here allocates device memory: buffers that are outputs or scratch are passed
+ * in by the caller, and the *_scratch_bytes() functions say how large scratch
+ * must be.  All work is enqueued on `stream`; no entry point synchronises the
+ * host except where its comment says so.
+ *
+ * Every function returns OSS_OK (0) or an OSS_ERR_* code; oss_last_error()
+ * returns a message for the last failure on the calling host thread.
+ *
+ * Array layouts (row-major, fp32 unless stated):
+ *   xy[n][2], scale[n][2], rot[n], feat[n][f], opacity[n]
+ *   conic[n][3]      = (a, b, d) of the inverse covariance
+ *   aabb[n][4]       = (tx0, ty0, tx1, ty1) int32 tile rectangle, half-open
+ *   image[f][h][w]   planar, pixel (px, py) evaluated at integer coordinates
+ *   geo[n][8]        = (x, y, A, B, D, a, b, d) with (A, B, D) = (a, 2b, d) * (-0.5*log2 e)
+ *   tile id          = ty * ceil(w/16) + tx, tiles are 16x16 pixels
+ *
+ * Binning modes (oss_bin_mode):
+ *   OSS_BIN_TIGHT3SIGMA  tile AABB of the q = 9 ellipse (the reference's
+ *                        pair_construction_only lists, rasterizer_fwd.cu:74-108)
+ *   OSS_BIN_EXACT        tile AABB of the q = 208 ellipse: every pixel outside
+ *                        the lists has exp(-q/2) == 0 in fp32, so images equal the
+ *                        reference's full-tail sum (rasterizer.py:294-300)
+ *   OSS_BIN_FULL         every Gaussian in every tile (the reference forward's
+ *                        build_full_tile_pairs, rasterizer_fwd.cu:135-149)
+ */
+#ifndef OSS_RASTER_H
+#define OSS_RASTER_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OSS_API __attribute__((visibility("default")))
+#else
+#define OSS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum oss_status {
+    OSS_OK = 0,
+    OSS_ERR_INVALID = 1,   /* bad argument: shape, null pointer, tile size */
+    OSS_ERR_CUDA = 2,      /* a CUDA runtime call or kernel launch failed */
+    OSS_ERR_RANGE = 3,     /* a size exceeds the int32 range the kernels index with */
+    OSS_ERR_SCRATCH = 4    /* scratch buffer smaller than *_scratch_bytes() */
+};
+
+enum oss_bin_mode {
+    OSS_BIN_TIGHT3SIGMA = 0,
+    OSS_BIN_EXACT = 1,
+    OSS_BIN_FULL = 2
+};
+
+#define OSS_TILE 16
+#define OSS_MAX_CHANNELS 64
+
+/* Message for the last error on this host thread ("" if none). */
+OSS_API const char* oss_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+OSS_API int oss_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Per-Gaussian preprocess: conic, tile AABB, pair count.
+ * Replaces _C.preprocess_only (reference oss/cuda/src/bindings.cpp:73 ->
+ * rasterizer_fwd.cu:325-379, kernel preprocess_gaussians rasterizer_fwd.cu:38-109).
+ * tile_size must be 16.  mode selects the AABB radius (see oss_bin_mode).
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode,
+                   const float* xy, const float* scale, const float* rot,
+                   float* conic, int32_t* aabb, int32_t* pair_count, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Render prepare: preprocess + gid-major pair-offset scan + geo records.
+ * First half of _C.rasterize_forward (rasterizer_fwd.cu:478-545) and of
+ * _C.pair_construction_only (rasterizer_fwd.cu:381-444).
+ * Outputs: conic[n*3], aabb[n*4], pair_offset[n+1] (exclusive scan of the pair
+ * counts; pair_offset[n] = total, valid only if total <= INT32_MAX),
+ * geo[n*8], total_pairs[1] (int64, on the device).
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_render_prepare_scratch_bytes(int64_t n);
+OSS_API int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode,
+                       const float* xy, const float* scale, const float* rot,
+                       float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
+                       int64_t* total_pairs, void* scratch, int64_t scratch_bytes,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Deterministic tile binning of the pairs described by (aabb, pair_offset):
+ * gid_sorted[total_pairs] lists, per tile in ascending tile id, the Gaussians
+ * overlapping that tile in ascending gid order; tile_offsets[T+1] brackets them.
+ * Bit-exact with the reference's sort of (tile << 32 | gid) keys plus
+ * searchsorted (rasterizer_fwd.cu:446-475) for the same AABBs.
+ * total_pairs is the host value of oss_render_prepare's total.
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles);
+OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
+                  const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                  int32_t* gid_sorted, int32_t* tile_offsets,
+                  void* scratch, int64_t scratch_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Forward additive render: image[c][p] = sum over the tile list of p of
+ *   feat'[g][c] * exp(-q_g(p)/2),  feat' = feat * opacity (opacity may be NULL).
+ * Replaces the rasterize_sum loop of _C.rasterize_forward
+ * (rasterizer_fwd.cu:151-322, host loop :570-587).  Writes every pixel.
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
+                       const float* geo, const float* feat, const float* opacity,
+                       const int32_t* gid_sorted, const int32_t* tile_offsets,
+                       float* image, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Deterministic backward for lists made by oss_bin_pairs: per-pair partial
+ * gradients in a fixed order, then a per-Gaussian reduction in gid-major order,
+ * fused with the d_conic -> (d_scale, d_rot) chain rule and the opacity unfold.
+ * Same gradients as _C.rasterize_backward + _C.conic_to_scale_rot_grad
+ * (rasterizer_bwd.cu:32-154) without atomics.
+ * d_feat is the gradient w.r.t. feat (not feat'); d_opacity, d_scale, d_rot
+ * may be NULL.
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f);
+OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
+                        const float* geo, const float* feat, const float* opacity,
+                        const float* scale, const float* rot,
+                        const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                        const int32_t* gid_sorted, const int32_t* tile_offsets,
+                        const float* grad_image,
+                        float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                        float* d_scale, float* d_rot,
+                        void* scratch, int64_t scratch_bytes, void* stream);
+
+/* The two halves of oss_render_backward, for callers that keep the per-pair
+ * partials: oss_render_backward_pairs writes pairgrad[total_pairs][stride]
+ * (stride = oss_pair_grad_stride(f) floats: d_xy(2), d_conic(3), d_feat'(f),
+ * zero padding) in gid-major pair order; oss_reduce_pair_grads sums them per
+ * Gaussian.  pairgrad is the scratch of oss_render_backward. */
+OSS_API int oss_pair_grad_stride(int64_t f);
+OSS_API int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w,
+                              const float* geo, const float* feat, const float* opacity,
+                              const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                              const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* grad_image, float* pairgrad, void* stream);
+OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
+                          const int32_t* pair_offset, const float* feat, const float* opacity,
+                          const float* scale, const float* rot,
+                          float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                          float* d_scale, float* d_rot, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Backward for arbitrary caller lists (per-pair partial sums, then fp32 atomics):
+ * replaces _C.rasterize_backward (bindings.cpp:66 -> rasterizer_bwd.cu:157-247).
+ * d_xy, d_conic, d_feat are zeroed here.  geo_scratch holds n*8 floats.
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_rasterize_backward_lists(int64_t n, int64_t f, int64_t h, int64_t w,
+                                 const float* xy, const float* conic, const float* feat,
+                                 const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                 const float* grad_image,
+                                 float* d_xy, float* d_conic, float* d_feat,
+                                 float* geo_scratch, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Geo records from caller conics (for oss_render_forward with an explicit conic).
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_make_geo(int64_t n, const float* xy, const float* conic, float* geo, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * d_conic -> (d_scale, d_rot): replaces _C.conic_to_scale_rot_grad
+ * (bindings.cpp:67 -> rasterizer_bwd.cu:115-154, 249-289).
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_conic_to_scale_rot_grad(int64_t n, const float* scale, const float* rot,
+                                const float* d_conic, float* d_scale, float* d_rot,
+                                void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Full-frame lists: gid_sorted[t*n + i] = i, tile_offsets[t] = t*n
+ * (build_full_tile_pairs, rasterizer_fwd.cu:135-149).  n*T must fit int32.
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_full_tile_pairs(int64_t n, int64_t num_tiles, int32_t* gid_sorted,
+                        int32_t* tile_offsets, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Stable counting sort of gid by tile_id: replaces _C.tile_bin_counting_sort
+ * (bindings.cpp:75 -> tile_bin_counting_sort.cu:71-128).  Entries with a tile
+ * id outside [0, num_tiles) go after all valid ones, in input order;
+ * tile_offsets[num_tiles] = n as in the reference (:40-48).  Within a tile the
+ * input order is kept (the reference's atomic cursor leaves it unspecified).
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_tile_bin_counting_sort_scratch_bytes(int64_t n, int64_t num_tiles);
+OSS_API int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles,
+                               const int32_t* tile_id, const int32_t* gid,
+                               int32_t* sorted_gid, int32_t* tile_offsets,
+                               void* scratch, int64_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OSS_RASTER_H */

@@ -1,0 +1,369 @@
+// extern "C" entry points of liboss_b200.so (declared in include/oss_raster.h).
+// Argument checks mirror the reference's TORCH_CHECKs (rasterizer_fwd.cu:489-522,
+// rasterizer_bwd.cu:170-213, tile_bin_counting_sort.cu:76-81) and come back as
+// status codes plus oss_last_error() text.
+#include <climits>
+#include <cstdint>
+#include <string>
+
+#include "internal.h"
+#include "oss_common.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+#define OSS_CUDA_TRY(expr)                                                                       \
+    do {                                                                                         \
+        cudaError_t oss_err_ = (expr);                                                           \
+        if (oss_err_ != cudaSuccess) {                                                           \
+            return fail(OSS_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(oss_err_)); \
+        }                                                                                        \
+    } while (0)
+
+#define OSS_CHECK(cond, code, msg)          \
+    do {                                            \
+        if (!(cond)) return fail((code), (msg));    \
+    } while (0)
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+struct Grid {
+    int n, h, w, ntx, nty, tiles;
+};
+
+// Shared size checks: n, h, w non-negative and within int32; tile count within int32.
+int check_grid(int64_t n, int64_t h, int64_t w, Grid& g) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");
+    OSS_CHECK(h >= 0 && w >= 0, OSS_ERR_INVALID, "H and W must be non-negative");
+    OSS_CHECK(n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    OSS_CHECK(h <= INT_MAX, OSS_ERR_RANGE, "H exceeds int32 range");
+    OSS_CHECK(w <= INT_MAX, OSS_ERR_RANGE, "W exceeds int32 range");
+    const int64_t ntx = (w + oss::kTile - 1) / oss::kTile;
+    const int64_t nty = (h + oss::kTile - 1) / oss::kTile;
+    OSS_CHECK(ntx * nty <= INT_MAX, OSS_ERR_RANGE, "number of tiles exceeds int32 range");
+    g.n = static_cast<int>(n);
+    g.h = static_cast<int>(h);
+    g.w = static_cast<int>(w);
+    g.ntx = static_cast<int>(ntx);
+    g.nty = static_cast<int>(nty);
+    g.tiles = static_cast<int>(ntx * nty);
+    return OSS_OK;
+}
+
+int check_mode(int32_t mode) {
+    OSS_CHECK(mode == OSS_BIN_TIGHT3SIGMA || mode == OSS_BIN_EXACT || mode == OSS_BIN_FULL, OSS_ERR_INVALID,
+              "binning mode must be 0 (tight3sigma), 1 (exact) or 2 (full)");
+    return OSS_OK;
+}
+
+int check_gaussian_inputs(int n, const float* xy, const float* scale, const float* rot) {
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(xy != nullptr && scale != nullptr && rot != nullptr, OSS_ERR_INVALID, "xy, scale and rot must be non-null");
+    OSS_CHECK(aligned(xy, 8) && aligned(scale, 8), OSS_ERR_INVALID, "xy and scale must be 8-byte aligned");
+    return OSS_OK;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* oss_last_error(void) { return g_last_error.c_str(); }
+
+int oss_abi_version(void) { return 1; }
+
+int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
+                   const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
+                   void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(tile_size == oss::kTile, OSS_ERR_INVALID, "tile_size must be 16");
+    if ((rc = check_mode(mode)) != OSS_OK) return rc;
+    if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(conic != nullptr && aabb != nullptr && pair_count != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
+    OSS_CHECK(aligned(aabb, 16), OSS_ERR_INVALID, "aabb must be 16-byte aligned");
+    OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_count, nullptr,
+                                        as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_scratch_bytes(n < 0 ? 0 : n); }
+
+int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
+                       const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
+                       int64_t* total_pairs, void* scratch, int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    if ((rc = check_mode(mode)) != OSS_OK) return rc;
+    if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
+    OSS_CHECK(pair_offset != nullptr && total_pairs != nullptr, OSS_ERR_INVALID, "pair_offset and total_pairs must be non-null");
+    OSS_CHECK(scratch_bytes >= oss_render_prepare_scratch_bytes(n), OSS_ERR_SCRATCH, "render_prepare scratch too small");
+    if (g.n > 0) {
+        OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
+        OSS_CHECK(aligned(aabb, 16) && aligned(geo, 16), OSS_ERR_INVALID, "aabb and geo must be 16-byte aligned");
+    }
+    cudaStream_t s = as_stream(stream);
+    OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo, s));
+    OSS_CUDA_TRY(oss::scan_exclusive_i32(pair_offset, pair_offset, g.n, true, total_pairs, scratch, s));
+    return OSS_OK;
+}
+
+int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles) {
+    (void)n;
+    if (total_pairs < 0) total_pairs = 0;
+    if (num_tiles < 0) num_tiles = 0;
+    const uint32_t key_limit = num_tiles > 0 ? static_cast<uint32_t>(num_tiles - 1) : 0u;
+    return oss::arena_bytes(total_pairs, 4) * 2 + oss::arena_bytes(num_tiles, 4) + oss::scan_scratch_bytes(num_tiles) +
+           oss::radix_scratch_bytes(total_pairs, key_limit);
+}
+
+int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, const int32_t* pair_offset,
+                  int64_t total_pairs, int32_t* gid_sorted, int32_t* tile_offsets, void* scratch,
+                  int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    if ((rc = check_mode(mode)) != OSS_OK) return rc;
+    OSS_CHECK(total_pairs >= 0, OSS_ERR_INVALID, "total pair count must be non-negative");
+    OSS_CHECK(total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(tile_offsets != nullptr, OSS_ERR_INVALID, "tile_offsets must be non-null");
+    OSS_CHECK(total_pairs == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
+    cudaStream_t s = as_stream(stream);
+    if (mode == OSS_BIN_FULL) {
+        OSS_CHECK(static_cast<int64_t>(g.n) * g.tiles == total_pairs, OSS_ERR_INVALID,
+                  "full-frame binning needs total_pairs == N * num_tiles");
+        if (g.tiles == 0) {
+            OSS_CUDA_TRY(cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t), s));
+            return OSS_OK;
+        }
+        OSS_CUDA_TRY(oss::launch_full_tile_pairs(g.n, g.tiles, gid_sorted, tile_offsets, s));
+        return OSS_OK;
+    }
+    OSS_CHECK(scratch_bytes >= oss_bin_pairs_scratch_bytes(n, total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "bin_pairs scratch too small");
+    OSS_CHECK(g.n == 0 || (aabb != nullptr && pair_offset != nullptr && aligned(aabb, 16)), OSS_ERR_INVALID,
+              "aabb (16-byte aligned) and pair_offset must be non-null");
+    oss::Arena arena{static_cast<char*>(scratch), scratch_bytes, 0};
+    uint32_t* keys = arena.take<uint32_t>(total_pairs);
+    int32_t* vals = arena.take<int32_t>(total_pairs);
+    int32_t* tile_count = arena.take<int32_t>(g.tiles);
+    void* scan_scratch = arena.base + arena.used;
+    arena.used += oss::scan_scratch_bytes(g.tiles);
+    void* radix_scratch = arena.base + arena.used;
+    if (g.tiles > 0) OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * g.tiles, s));
+    OSS_CUDA_TRY(oss::launch_expand_pairs(g.n, g.ntx, aabb, pair_offset, keys, vals, tile_count, s));
+    OSS_CUDA_TRY(oss::scan_exclusive_i32(tile_count, tile_offsets, g.tiles, true, nullptr, scan_scratch, s));
+    const uint32_t key_limit = g.tiles > 0 ? static_cast<uint32_t>(g.tiles - 1) : 0u;
+    OSS_CUDA_TRY(oss::radix_sort_pairs(keys, vals, total_pairs, key_limit, gid_sorted, radix_scratch, s));
+    return OSS_OK;
+}
+
+int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                       const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
+                       void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0, OSS_ERR_INVALID, "F must be non-negative");
+    OSS_CHECK(f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be <= 64");
+    if (g.tiles == 0 || f == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && image != nullptr, OSS_ERR_INVALID, "tile_offsets and image must be non-null");
+    OSS_CHECK(g.n == 0 || (geo != nullptr && feat != nullptr && aligned(geo, 16)), OSS_ERR_INVALID,
+              "geo (16-byte aligned) and feat must be non-null");
+    OSS_CUDA_TRY(oss::launch_render_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
+                                            tile_offsets, image, as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f) {
+    if (total_pairs < 0) total_pairs = 0;
+    if (f < 0) f = 0;
+    return oss::arena_bytes(total_pairs * oss::backward_pair_stride(static_cast<int>(f)), 4);
+}
+
+int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                        const float* opacity, const float* scale, const float* rot, const int32_t* aabb,
+                        const int32_t* pair_offset, int64_t total_pairs, const int32_t* gid_sorted,
+                        const int32_t* tile_offsets, const float* grad_image, float* d_xy, float* d_conic,
+                        float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* scratch,
+                        int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_render_backward_scratch_bytes(total_pairs, f), OSS_ERR_SCRATCH,
+              "render_backward scratch too small");
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
+              OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
+    OSS_CHECK(d_xy != nullptr && d_conic != nullptr, OSS_ERR_INVALID, "d_xy and d_conic must be non-null");
+    OSS_CHECK(f == 0 || (feat != nullptr && d_feat != nullptr), OSS_ERR_INVALID, "feat and d_feat must be non-null");
+    OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
+              "d_scale needs scale, rot and d_rot");
+    float* pairgrad = static_cast<float*>(scratch);
+    rc = oss_render_backward_pairs(n, f, h, w, geo, feat, opacity, aabb, pair_offset, total_pairs, gid_sorted,
+                                   tile_offsets, grad_image, pairgrad, stream);
+    if (rc != OSS_OK) return rc;
+    return oss_reduce_pair_grads(n, f, pairgrad, pair_offset, feat, opacity, scale, rot, d_xy, d_conic, d_feat,
+                                 d_opacity, d_scale, d_rot, stream);
+}
+
+int oss_pair_grad_stride(int64_t f) {
+    return oss::backward_pair_stride(static_cast<int>(f < 0 ? 0 : (f > OSS_MAX_CHANNELS ? OSS_MAX_CHANNELS : f)));
+}
+
+int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                              const float* opacity, const int32_t* aabb, const int32_t* pair_offset,
+                              int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* grad_image, float* pairgrad, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    if (g.n == 0 || total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
+              OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
+    OSS_CHECK(f == 0 || feat != nullptr, OSS_ERR_INVALID, "feat must be non-null");
+    OSS_CHECK(pairgrad != nullptr && aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
+              "lists and grad_image must be non-null");
+    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
+                                                   tile_offsets, grad_image, aabb, pair_offset, pairgrad,
+                                                   oss_pair_grad_stride(f), nullptr, nullptr, nullptr,
+                                                   as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int32_t* pair_offset, const float* feat,
+                          const float* opacity, const float* scale, const float* rot, float* d_xy, float* d_conic,
+                          float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(pair_offset != nullptr && d_xy != nullptr && d_conic != nullptr, OSS_ERR_INVALID,
+              "pair_offset, d_xy and d_conic must be non-null");
+    OSS_CHECK(f == 0 || (feat != nullptr && d_feat != nullptr), OSS_ERR_INVALID, "feat and d_feat must be non-null");
+    OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
+              "d_scale needs scale, rot and d_rot");
+    OSS_CHECK(pairgrad == nullptr || aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CUDA_TRY(oss::launch_reduce_gaussian_grads(static_cast<int>(n), static_cast<int>(f), pairgrad,
+                                                   oss_pair_grad_stride(f), pair_offset, feat, opacity, scale, rot,
+                                                   d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot,
+                                                   as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_rasterize_backward_lists(int64_t n, int64_t f, int64_t h, int64_t w, const float* xy, const float* conic,
+                                 const float* feat, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                 const float* grad_image, float* d_xy, float* d_conic, float* d_feat,
+                                 float* geo_scratch, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(xy != nullptr && aligned(xy, 8) && conic != nullptr, OSS_ERR_INVALID, "xy (8-byte aligned) and conic must be non-null");
+    OSS_CHECK(d_xy != nullptr && d_conic != nullptr && (f == 0 || (d_feat != nullptr && feat != nullptr)),
+              OSS_ERR_INVALID, "gradient outputs must be non-null");
+    OSS_CHECK(geo_scratch != nullptr && aligned(geo_scratch, 16), OSS_ERR_INVALID, "geo_scratch must be 16-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    OSS_CUDA_TRY(cudaMemsetAsync(d_xy, 0, sizeof(float) * 2 * g.n, s));
+    OSS_CUDA_TRY(cudaMemsetAsync(d_conic, 0, sizeof(float) * 3 * g.n, s));
+    if (f > 0) OSS_CUDA_TRY(cudaMemsetAsync(d_feat, 0, sizeof(float) * f * g.n, s));
+    if (f == 0 || g.tiles == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID, "tile_offsets and grad_image must be non-null");
+    OSS_CUDA_TRY(oss::launch_make_geo(g.n, xy, conic, geo_scratch, s));
+    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, geo_scratch, feat, nullptr,
+                                                   gid_sorted, tile_offsets, grad_image, nullptr, nullptr, nullptr, 0,
+                                                   d_xy, d_conic, d_feat, s));
+    return OSS_OK;
+}
+
+int oss_make_geo(int64_t n, const float* xy, const float* conic, float* geo, void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(xy != nullptr && aligned(xy, 8) && conic != nullptr && geo != nullptr && aligned(geo, 16),
+              OSS_ERR_INVALID, "xy (8-byte aligned), conic and geo (16-byte aligned) must be non-null");
+    OSS_CUDA_TRY(oss::launch_make_geo(static_cast<int>(n), xy, conic, geo, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_conic_to_scale_rot_grad(int64_t n, const float* scale, const float* rot, const float* d_conic, float* d_scale,
+                                float* d_rot, void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");
+    OSS_CHECK(n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(scale != nullptr && aligned(scale, 8) && rot != nullptr && d_conic != nullptr && d_scale != nullptr &&
+                  aligned(d_scale, 8) && d_rot != nullptr,
+              OSS_ERR_INVALID, "pointers must be non-null (scale, d_scale 8-byte aligned)");
+    OSS_CUDA_TRY(oss::launch_conic_to_scale_rot_grad(static_cast<int>(n), scale, rot, d_conic, d_scale, d_rot,
+                                                     as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_full_tile_pairs(int64_t n, int64_t num_tiles, int32_t* gid_sorted, int32_t* tile_offsets, void* stream) {
+    OSS_CHECK(n >= 0 && num_tiles >= 0, OSS_ERR_INVALID, "N and num_tiles must be non-negative");
+    OSS_CHECK(num_tiles <= INT_MAX, OSS_ERR_RANGE, "number of tiles exceeds int32 range");
+    OSS_CHECK(n == 0 || num_tiles <= INT_MAX / n, OSS_ERR_RANGE, "full-frame raster pair count exceeds int32 range");
+    OSS_CHECK(tile_offsets != nullptr, OSS_ERR_INVALID, "tile_offsets must be non-null");
+    cudaStream_t s = as_stream(stream);
+    if (num_tiles == 0) {
+        OSS_CUDA_TRY(cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t), s));
+        return OSS_OK;
+    }
+    OSS_CHECK(n == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
+    OSS_CUDA_TRY(oss::launch_full_tile_pairs(static_cast<int>(n), static_cast<int>(num_tiles), gid_sorted,
+                                             tile_offsets, s));
+    return OSS_OK;
+}
+
+int64_t oss_tile_bin_counting_sort_scratch_bytes(int64_t n, int64_t num_tiles) {
+    if (n < 0) n = 0;
+    if (num_tiles < 0) num_tiles = 0;
+    const uint32_t key_limit = static_cast<uint32_t>(num_tiles > INT_MAX ? INT_MAX : num_tiles);
+    return oss::arena_bytes(n, 4) * 2 + oss::arena_bytes(num_tiles, 4) + oss::scan_scratch_bytes(num_tiles) +
+           oss::radix_scratch_bytes(n, key_limit);
+}
+
+int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles, const int32_t* tile_id, const int32_t* gid,
+                               int32_t* sorted_gid, int32_t* tile_offsets, void* scratch, int64_t scratch_bytes,
+                               void* stream) {
+    OSS_CHECK(num_tiles > 0, OSS_ERR_INVALID, "num_tiles must be positive");
+    OSS_CHECK(num_tiles <= INT_MAX, OSS_ERR_RANGE, "num_tiles exceeds int32 range");
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");
+    OSS_CHECK(n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    OSS_CHECK(tile_offsets != nullptr, OSS_ERR_INVALID, "tile_offsets must be non-null");
+    OSS_CHECK(n == 0 || (tile_id != nullptr && gid != nullptr && sorted_gid != nullptr), OSS_ERR_INVALID,
+              "tile_id, gid and sorted_gid must be non-null");
+    OSS_CHECK(scratch_bytes >= oss_tile_bin_counting_sort_scratch_bytes(n, num_tiles), OSS_ERR_SCRATCH,
+              "tile_bin_counting_sort scratch too small");
+    const int tiles = static_cast<int>(num_tiles);
+    cudaStream_t s = as_stream(stream);
+    oss::Arena arena{static_cast<char*>(scratch), scratch_bytes, 0};
+    uint32_t* keys = arena.take<uint32_t>(n);
+    int32_t* vals = arena.take<int32_t>(n);
+    int32_t* tile_count = arena.take<int32_t>(tiles);
+    void* scan_scratch = arena.base + arena.used;
+    arena.used += oss::scan_scratch_bytes(tiles);
+    void* radix_scratch = arena.base + arena.used;
+    OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * tiles, s));
+    OSS_CUDA_TRY(oss::launch_tile_keys(static_cast<int>(n), tiles, tile_id, gid, keys, vals, tile_count, s));
+    OSS_CUDA_TRY(oss::scan_exclusive_i32(tile_count, tile_offsets, tiles, false, nullptr, scan_scratch, s));
+    OSS_CUDA_TRY(oss::launch_set_i32(tile_offsets + tiles, static_cast<int32_t>(n), s));
+    OSS_CUDA_TRY(oss::radix_sort_pairs(keys, vals, n, static_cast<uint32_t>(tiles), sorted_gid, radix_scratch, s));
+    return OSS_OK;
+}
+
+}  // extern "C"

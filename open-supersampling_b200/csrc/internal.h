@@ -1,0 +1,80 @@
+// Host-side launchers shared between the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace oss {
+
+// Scratch carving: 256-byte aligned sub-buffers of one caller buffer.
+struct Arena {
+    char* base;
+    int64_t size;
+    int64_t used;
+    template <typename T>
+    T* take(int64_t count) {
+        const int64_t bytes = ((count * static_cast<int64_t>(sizeof(T)) + 255) / 256) * 256;
+        T* p = reinterpret_cast<T*>(base + used);
+        used += bytes;
+        return p;
+    }
+};
+
+inline int64_t arena_bytes(int64_t count, int64_t elem) { return ((count * elem + 255) / 256) * 256; }
+
+// ---- scan.cu ---------------------------------------------------------------
+// Exclusive scan of n int32 values (in may alias out).  The int64 total goes to
+// total_out (device, may be null); out[n] = (int32)total if write_tail.
+int64_t scan_scratch_bytes(int64_t n);
+cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool write_tail,
+                               int64_t* total_out, void* scratch, cudaStream_t stream);
+
+// ---- radix.cu --------------------------------------------------------------
+// Stable LSD sort of (key, val) pairs by key in [0, key_limit].  The sorted vals
+// land in vals_out; keys are not kept.  key scratch is consumed.
+int64_t radix_scratch_bytes(int64_t n, uint32_t key_limit);
+cudaError_t radix_sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, uint32_t key_limit,
+                             int32_t* vals_out, void* scratch, cudaStream_t stream);
+
+// ---- preprocess.cu ---------------------------------------------------------
+cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
+                              const float* rot, float* conic, int32_t* aabb, int32_t* count,
+                              float* geo, cudaStream_t stream);
+cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
+cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
+                                           const float* d_conic, float* d_scale, float* d_rot,
+                                           cudaStream_t stream);
+
+// ---- binning.cu ------------------------------------------------------------
+cudaError_t launch_expand_pairs(int n, int ntx, const int32_t* aabb, const int32_t* pair_offset,
+                                uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
+cudaError_t launch_full_tile_pairs(int n, int num_tiles, int32_t* gid_sorted, int32_t* tile_offsets,
+                                   cudaStream_t stream);
+cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const int32_t* gid,
+                             uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
+cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
+
+// ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
+cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat,
+                                  const float* opacity, const int32_t* gid_sorted,
+                                  const int32_t* tile_offsets, float* image, cudaStream_t stream);
+
+// Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows of
+// pair_stride floats at pair_offset[g] + local tile index.  Atomic mode: adds
+// into d_xy / d_conic / d_feat.
+cudaError_t launch_render_backward_tiles(int f, int h, int w, const float* geo, const float* feat,
+                                         const float* opacity, const int32_t* gid_sorted,
+                                         const int32_t* tile_offsets, const float* grad_image,
+                                         const int32_t* aabb, const int32_t* pair_offset,
+                                         float* pairgrad, int pair_stride,
+                                         float* d_xy, float* d_conic, float* d_feat,
+                                         cudaStream_t stream);
+int backward_pair_stride(int f);
+cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,
+                                         const int32_t* pair_offset, const float* feat,
+                                         const float* opacity, const float* scale, const float* rot,
+                                         float* d_xy, float* d_conic, float* d_feat,
+                                         float* d_opacity, float* d_scale, float* d_rot,
+                                         cudaStream_t stream);
+
+}  // namespace oss

@@ -1,0 +1,101 @@
+// Per-Gaussian preprocess (conic, tile AABB, pair count, raster record) and the
+// per-Gaussian d_conic -> (d_scale, d_rot) chain rule.  One thread per Gaussian,
+// fully coalesced SoA loads: these kernels are HBM-bound (20 B in, 32-64 B out).
+#include "internal.h"
+#include "oss_common.cuh"
+
+namespace oss {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, const Conic& k) {
+    float4* rec = reinterpret_cast<float4*>(geo + static_cast<int64_t>(g) * 8);
+    rec[0] = make_float4(x, y, k.a * kNegHalfLog2e, (2.0f * k.b) * kNegHalfLog2e);
+    rec[1] = make_float4(k.d * kNegHalfLog2e, k.a, k.b, k.d);
+}
+
+__global__ void __launch_bounds__(kThreads) k_preprocess(int n, int ntx, int nty, int mode,
+                                                          const float2* __restrict__ xy,
+                                                          const float2* __restrict__ scale,
+                                                          const float* __restrict__ rot,
+                                                          float* __restrict__ conic,
+                                                          int4* __restrict__ aabb,
+                                                          int32_t* __restrict__ count,
+                                                          float* __restrict__ geo) {
+    const int g = blockIdx.x * kThreads + threadIdx.x;
+    if (g >= n) return;
+    const float2 c = xy[g];
+    const float2 s = scale[g];
+    const Conic k = conic_from_scale_rot(s.x, s.y, rot[g]);
+    conic[3 * g + 0] = k.a;
+    conic[3 * g + 1] = k.b;
+    conic[3 * g + 2] = k.d;
+    int cnt;
+    int4 box;
+    if (mode == OSS_BIN_FULL) {
+        box = make_int4(0, 0, ntx, nty);
+        cnt = ntx * nty;
+    } else {
+        box = tile_aabb(c.x, c.y, s.x, s.y, k, mode_tau(mode), mode_fallback(mode), ntx, nty, cnt);
+    }
+    aabb[g] = box;
+    count[g] = cnt;
+    if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
+}
+
+__global__ void __launch_bounds__(kThreads) k_make_geo(int n, const float2* __restrict__ xy,
+                                                        const float* __restrict__ conic, float* __restrict__ geo) {
+    const int g = blockIdx.x * kThreads + threadIdx.x;
+    if (g >= n) return;
+    const float2 c = xy[g];
+    Conic k;
+    k.a = conic[3 * g + 0];
+    k.b = conic[3 * g + 1];
+    k.d = conic[3 * g + 2];
+    write_geo(geo, g, c.x, c.y, k);
+}
+
+__global__ void __launch_bounds__(kThreads) k_conic_to_scale_rot_grad(int n, const float2* __restrict__ scale,
+                                                                       const float* __restrict__ rot,
+                                                                       const float* __restrict__ d_conic,
+                                                                       float2* __restrict__ d_scale,
+                                                                       float* __restrict__ d_rot) {
+    const int g = blockIdx.x * kThreads + threadIdx.x;
+    if (g >= n) return;
+    const float2 s = scale[g];
+    float dsx, dsy, dr;
+    conic_grad_to_scale_rot(s.x, s.y, rot[g], d_conic[3 * g], d_conic[3 * g + 1], d_conic[3 * g + 2], dsx, dsy,
+                            dr);
+    d_scale[g] = make_float2(dsx, dsy);
+    d_rot[g] = dr;
+}
+
+}  // namespace
+
+cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
+                              const float* rot, float* conic, int32_t* aabb, int32_t* count, float* geo,
+                              cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_preprocess<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(
+        n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
+        conic, reinterpret_cast<int4*>(aabb), count, geo);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_make_geo<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(
+        n, reinterpret_cast<const float2*>(xy), conic, geo);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot, const float* d_conic,
+                                           float* d_scale, float* d_rot, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_conic_to_scale_rot_grad<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(
+        n, reinterpret_cast<const float2*>(scale), rot, d_conic, reinterpret_cast<float2*>(d_scale), d_rot);
+    return cudaGetLastError();
+}
+
+}  // namespace oss

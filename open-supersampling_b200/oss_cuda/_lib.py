@@ -1,0 +1,109 @@
+"""ctypes binding of liboss_b200.so, the C ABI declared in include/oss_raster.h.
+
+Loading is strict: if the shared library is missing or fails to load, every
+op raises.  There is no CPU or PyTorch fallback on the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_NAME = "liboss_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+OSS_OK = 0
+OSS_BIN_TIGHT3SIGMA = 0
+OSS_BIN_EXACT = 1
+OSS_BIN_FULL = 2
+BINNING_MODES = {"tight3sigma": OSS_BIN_TIGHT3SIGMA, "exact": OSS_BIN_EXACT, "full": OSS_BIN_FULL}
+TILE = 16
+MAX_CHANNELS = 64
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_p = ctypes.c_void_p
+
+# name -> (restype, argtypes); must match include/oss_raster.h
+SIGNATURES = {
+    "oss_last_error": (ctypes.c_char_p, []),
+    "oss_abi_version": (ctypes.c_int, []),
+    "oss_preprocess": (ctypes.c_int, [_i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_prepare_scratch_bytes": (_i64, [_i64]),
+    "oss_render_prepare": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
+    "oss_bin_pairs": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _i64, _p, _p, _p, _i64, _p]),
+    "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_backward_scratch_bytes": (_i64, [_i64, _i64]),
+    "oss_render_backward": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
+    ),
+    "oss_pair_grad_stride": (ctypes.c_int, [_i64]),
+    "oss_render_backward_pairs": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p]),
+    "oss_reduce_pair_grads": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_rasterize_backward_lists": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p],
+    ),
+    "oss_make_geo": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
+    "oss_conic_to_scale_rot_grad": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p]),
+    "oss_full_tile_pairs": (ctypes.c_int, [_i64, _i64, _p, _p, _p]),
+    "oss_tile_bin_counting_sort_scratch_bytes": (_i64, [_i64, _i64]),
+    "oss_tile_bin_counting_sort": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
+}
+
+_LIB = None
+_LOAD_ERROR: str | None = None
+
+
+def _load():
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None or _LOAD_ERROR is not None:
+        return _LIB
+    path = os.environ.get("OSS_B200_LIB", str(LIB_PATH))
+    try:
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+    except OSError as exc:  # missing or unloadable .so
+        _LOAD_ERROR = f"{path}: {exc}"
+    except AttributeError as exc:  # stale .so without a symbol
+        _LOAD_ERROR = f"{path}: missing symbol ({exc})"
+    return _LIB
+
+
+def available() -> bool:
+    return _load() is not None
+
+
+def load_error() -> str | None:
+    _load()
+    return _LOAD_ERROR
+
+
+def lib():
+    """The loaded library; raises RuntimeError if it is not built."""
+    handle = _load()
+    if handle is None:
+        raise RuntimeError(
+            "oss_cuda extension not compiled (liboss_b200.so failed to load: "
+            f"{_LOAD_ERROR}). Run: python open-supersampling_b200/build.py"
+        )
+    return handle
+
+
+def check(rc: int, what: str) -> None:
+    if rc != OSS_OK:
+        msg = lib().oss_last_error().decode("utf-8", "replace")
+        raise RuntimeError(f"{what}: {msg} (status {rc})")
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a tensor (None for an absent optional operand)."""
+    if t is None:
+        return None
+    return t.data_ptr()

@@ -1,0 +1,208 @@
+"""Host orchestration of the render pipeline over the C ABI.
+
+prepare -> (one 8-byte device->host read of the pair total) -> bin -> forward;
+backward reuses the binning of its forward.  PyTorch only provides device
+memory, the current stream and autograd plumbing; every kernel is in
+liboss_b200.so.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+INT32_MAX = 2**31 - 1
+
+
+def binning_mode(binning: str | None) -> int:
+    """Map a binning name to its C-ABI code.
+
+    Default ("exact") reproduces the reference op's full-tail sum; the
+    environment variable OSS_RASTER_BINNING overrides the default.
+    """
+    name = binning if binning is not None else os.environ.get("OSS_RASTER_BINNING", "exact")
+    name = name.strip().lower()
+    if name not in _lib.BINNING_MODES:
+        raise ValueError(f"binning must be one of {sorted(_lib.BINNING_MODES)}; got {name!r}")
+    return _lib.BINNING_MODES[name]
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def check_float_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be CUDA")
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be fp32")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def check_int_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be CUDA")
+    if t.dtype != torch.int32:
+        raise RuntimeError(f"{name} must be int32")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def aligned(t: torch.Tensor, nbytes: int) -> torch.Tensor:
+    """Return t, or an aligned copy if its data pointer is not nbytes-aligned."""
+    if t.numel() > 0 and t.data_ptr() % nbytes != 0:
+        return t.clone()
+    return t
+
+
+def check_gaussians(xy, scale, rot, feat=None) -> tuple[int, int]:
+    check_float_cuda(xy, "xy")
+    check_float_cuda(scale, "scale")
+    check_float_cuda(rot, "rot")
+    if xy.dim() != 2 or xy.size(1) != 2:
+        raise RuntimeError("xy must be (N,2)")
+    if scale.dim() != 2 or scale.size(1) != 2:
+        raise RuntimeError("scale must be (N,2)")
+    if rot.dim() != 1:
+        raise RuntimeError("rot must be (N,)")
+    if xy.size(0) != scale.size(0):
+        raise RuntimeError("xy/scale N mismatch")
+    if xy.size(0) != rot.size(0):
+        raise RuntimeError("xy/rot N mismatch")
+    f = 0
+    if feat is not None:
+        check_float_cuda(feat, "feat")
+        if feat.dim() != 2:
+            raise RuntimeError("feat must be (N,F)")
+        if xy.size(0) != feat.size(0):
+            raise RuntimeError("xy/feat N mismatch")
+        f = int(feat.size(1))
+        if f > _lib.MAX_CHANNELS:
+            raise RuntimeError("F must be <= 64")
+    n = int(xy.size(0))
+    if n > INT32_MAX:
+        raise RuntimeError("N exceeds int32 range")
+    return n, f
+
+
+def check_hw(h: int, w: int, tile_size: int) -> tuple[int, int, int, int]:
+    if h < 0 or w < 0:
+        raise RuntimeError("H and W must be non-negative")
+    if tile_size != _lib.TILE:
+        raise RuntimeError("tile_size must be 16")
+    if h > INT32_MAX:
+        raise RuntimeError("H exceeds int32 range")
+    if w > INT32_MAX:
+        raise RuntimeError("W exceeds int32 range")
+    ntx = (w + _lib.TILE - 1) // _lib.TILE
+    nty = (h + _lib.TILE - 1) // _lib.TILE
+    if ntx * nty > INT32_MAX:
+        raise RuntimeError("number of tiles exceeds int32 range")
+    return ntx, nty, ntx * nty, 0
+
+
+@dataclass
+class Binned:
+    """Per-Gaussian records and per-tile lists of one render."""
+
+    n: int
+    h: int
+    w: int
+    mode: int
+    conic: torch.Tensor        # (N, 3)
+    aabb: torch.Tensor         # (N, 4) int32
+    pair_offset: torch.Tensor  # (N+1,) int32, gid-major pair offsets
+    geo: torch.Tensor          # (N, 8) raster records
+    total_pairs: int
+    gid_sorted: torch.Tensor   # (P,) int32
+    tile_offsets: torch.Tensor  # (T+1,) int32
+
+
+def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: int, w: int, mode: int) -> Binned:
+    """Preprocess + deterministic tile binning.  One host sync (the pair total)
+    except in full mode, where the total N*T is known up front."""
+    lib = _lib.lib()
+    n = int(xy.size(0))
+    _, _, num_tiles, _ = check_hw(h, w, _lib.TILE)
+    if mode == _lib.OSS_BIN_FULL and n > 0 and num_tiles > INT32_MAX // n:
+        raise RuntimeError("full-frame raster pair count exceeds int32 range")
+    dev = xy.device
+    xy = aligned(xy, 8)
+    scale = aligned(scale, 8)
+    stream = stream_of(xy)
+    f32 = dict(device=dev, dtype=torch.float32)
+    i32 = dict(device=dev, dtype=torch.int32)
+    conic = torch.empty((n, 3), **f32)
+    aabb = torch.empty((n, 4), **i32)
+    pair_offset = torch.empty((n + 1,), **i32)
+    geo = torch.empty((n, 8), **f32)
+    total = torch.empty((1,), device=dev, dtype=torch.int64)
+    scratch = torch.empty((max(1, lib.oss_render_prepare_scratch_bytes(n)),), device=dev, dtype=torch.uint8)
+    _lib.check(
+        lib.oss_render_prepare(n, h, w, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(), conic.data_ptr(),
+                               aabb.data_ptr(), pair_offset.data_ptr(), geo.data_ptr(), total.data_ptr(),
+                               scratch.data_ptr(), scratch.numel(), stream),
+        "oss_render_prepare",
+    )
+    if mode == _lib.OSS_BIN_FULL:
+        total_pairs = n * num_tiles
+    else:
+        total_pairs = int(total.item())
+    if total_pairs > INT32_MAX:
+        raise RuntimeError("total pair count exceeds int32 range")
+    gid_sorted = torch.empty((total_pairs,), **i32)
+    tile_offsets = torch.empty((num_tiles + 1,), **i32)
+    nbytes = lib.oss_bin_pairs_scratch_bytes(n, total_pairs, num_tiles)
+    scratch2 = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
+    _lib.check(
+        lib.oss_bin_pairs(n, h, w, mode, aabb.data_ptr(), pair_offset.data_ptr(), total_pairs,
+                          gid_sorted.data_ptr(), tile_offsets.data_ptr(), scratch2.data_ptr(), scratch2.numel(),
+                          stream),
+        "oss_bin_pairs",
+    )
+    return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
+
+
+def render_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None) -> torch.Tensor:
+    lib = _lib.lib()
+    f = int(feat.size(1))
+    image = torch.empty((f, b.h, b.w), device=feat.device, dtype=torch.float32)
+    _lib.check(
+        lib.oss_render_forward(b.n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                               b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(), image.data_ptr(),
+                               stream_of(feat)),
+        "oss_render_forward",
+    )
+    return image
+
+
+def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, scale: torch.Tensor,
+                    rot: torch.Tensor, grad_image: torch.Tensor):
+    """Deterministic gradients (d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot)."""
+    lib = _lib.lib()
+    dev = feat.device
+    n, f = b.n, int(feat.size(1))
+    f32 = dict(device=dev, dtype=torch.float32)
+    d_xy = torch.empty((n, 2), **f32)
+    d_conic = torch.empty((n, 3), **f32)
+    d_feat = torch.empty((n, f), **f32)
+    d_opacity = torch.empty((n,), **f32) if opacity is not None else None
+    d_scale = torch.empty((n, 2), **f32)
+    d_rot = torch.empty((n,), **f32)
+    nbytes = lib.oss_render_backward_scratch_bytes(b.total_pairs, f)
+    scratch = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
+    scale = aligned(scale, 8)
+    _lib.check(
+        lib.oss_render_backward(n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                                scale.data_ptr(), rot.data_ptr(), b.aabb.data_ptr(), b.pair_offset.data_ptr(),
+                                b.total_pairs, b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(),
+                                grad_image.data_ptr(), d_xy.data_ptr(), d_conic.data_ptr(), d_feat.data_ptr(),
+                                _lib.ptr(d_opacity), d_scale.data_ptr(), d_rot.data_ptr(), scratch.data_ptr(),
+                                scratch.numel(), stream_of(feat)),
+        "oss_render_backward",
+    )
+    return d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot

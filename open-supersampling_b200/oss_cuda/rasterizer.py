@@ -1,0 +1,81 @@
+"""OSS custom rasterizer -- autograd Function over the B200 C-ABI kernels.
+
+Drop-in for reference oss/cuda/oss_cuda/rasterizer.py: the same
+``rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True)``
+call and ``_COMPILED`` / ``_C`` attributes.  The backward is the deterministic
+per-pair reduction (no atomics) over the forward's own binning, fused with
+the d_conic -> (d_scale, d_rot) chain rule.
+
+Keyword-only additions (defaults keep the reference call's results):
+  binning  "exact" (default) | "tight3sigma" | "full"
+  opacity  (N,) tensor folded into feat as feat * opacity[:, None], with its
+           gradient returned (the fold gaussian_temporal/rasterizer.py:47 does
+           in PyTorch)
+"""
+from __future__ import annotations
+
+from importlib import import_module
+
+import torch
+from torch.autograd import Function
+
+from . import _raster
+
+try:
+    from . import _C
+
+    _COMPILED = True
+except ImportError:
+    try:
+        _C = import_module("oss_cuda._C")
+        _COMPILED = True
+    except ImportError:
+        _C = None
+        _COMPILED = False
+
+
+class _RasterizeGaussians(Function):
+    @staticmethod
+    def forward(ctx, xy, scale, rot, feat, opacity, h, w, tile_size, topk_norm, mode):
+        if not _COMPILED:
+            raise RuntimeError(
+                "oss_cuda extension not compiled. Run: python open-supersampling_b200/build.py"
+            )
+        del topk_norm
+        with torch.cuda.device(xy.device):
+            b = _raster.bin_gaussians(xy, scale, rot, h, w, mode)
+            out = _raster.render_forward(b, _raster.aligned(feat, 4), opacity)
+        ctx.save_for_backward(xy, scale, rot, feat, opacity, b.conic, b.aabb, b.pair_offset, b.geo, b.gid_sorted,
+                              b.tile_offsets)
+        ctx.meta = (b.n, b.h, b.w, b.mode, b.total_pairs)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, gid_sorted, tile_offsets = ctx.saved_tensors
+        n, h, w, mode, total_pairs = ctx.meta
+        b = _raster.Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
+        grad = grad_out.contiguous()
+        if grad.dtype != torch.float32:
+            grad = grad.float()
+        with torch.cuda.device(xy.device):
+            d_xy, _d_conic, d_feat, d_opacity, d_scale, d_rot = _raster.render_backward(
+                b, _raster.aligned(feat, 4), opacity, scale, rot, grad
+            )
+        return d_xy, d_scale, d_rot, d_feat, d_opacity, None, None, None, None, None
+
+
+def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True, *, binning=None, opacity=None):
+    """Render (F, H, W) = sum_g feat[g] * exp(-q_g / 2) on the GPU, differentiably.
+
+    Reference: oss/cuda/oss_cuda/rasterizer.py:68-70.
+    """
+    h, w, tile_size = int(h), int(w), int(tile_size)
+    _raster.check_gaussians(xy, scale, rot, feat)
+    _raster.check_hw(h, w, tile_size)
+    if opacity is not None:
+        _raster.check_float_cuda(opacity, "opacity")
+        if opacity.dim() != 1 or opacity.size(0) != xy.size(0):
+            raise RuntimeError("opacity must be (N,)")
+    mode = _raster.binning_mode(binning)
+    return _RasterizeGaussians.apply(xy, scale, rot, feat, opacity, h, w, tile_size, bool(topk_norm), mode)

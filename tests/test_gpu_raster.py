@@ -1,0 +1,335 @@
+"""GPU parity of the rasterizer path against the CPU oracle and golden vectors.
+
+Integer/index outputs (AABBs, counts, tile lists) must be bit-exact; images and
+gradients must agree within |a - b| <= 1e-5 + 1e-4 |b| (conftest.ATOL/RTOL).
+Every call goes through oss_cuda -> liboss_b200.so (the C ABI).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as orc
+from conftest import assert_close, golden_case, load_golden
+
+pytestmark = pytest.mark.gpu
+
+MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT, "full": orc.FULL}
+
+
+def dev(a, dtype=torch.float32):
+    return torch.as_tensor(np.asarray(a), dtype=dtype).cuda().contiguous()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def random_gaussians(n, h, w, f, seed, scale_lo=0.5, scale_hi=5.5):
+    rng = np.random.default_rng(seed)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    scale = (rng.random((n, 2)) * (scale_hi - scale_lo) + scale_lo).astype(np.float32)
+    rot = (rng.random(n) * 6.28).astype(np.float32)
+    feat = rng.standard_normal((n, f)).astype(np.float32)
+    return xy, scale, rot, feat
+
+
+def baseline_gaussians(n, h, w, seed, log_scale_mean, log_scale_sd=0.3):
+    """BASELINE.json config distributions: uniform means, log-normal scales,
+    rot U[0, pi), opacity sigmoid(N(0,1)), rgb U[0,1]."""
+    rng = np.random.default_rng(seed)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    scale = np.exp(rng.standard_normal((n, 2)) * log_scale_sd + log_scale_mean).astype(np.float32)
+    rot = (rng.random(n) * math.pi).astype(np.float32)
+    opacity = (1.0 / (1.0 + np.exp(-rng.standard_normal(n)))).astype(np.float32)
+    rgb = rng.random((n, 3)).astype(np.float32)
+    return xy, scale, rot, opacity, rgb
+
+
+# ------------------------------------------------------------------ preprocess
+
+@pytest.mark.parametrize("n", [1, 32, 256, 16384])
+@pytest.mark.parametrize("hw", [(128, 128), (270, 480), (540, 960)])
+def test_preprocess_bit_exact(cuda_device, n, hw):
+    from oss_cuda._test_helpers import preprocess_only
+
+    h, w = hw
+    xy, scale, rot, _ = random_gaussians(n, h, w, 1, seed=n + h)
+    conic, aabb, count = preprocess_only(dev(xy), dev(scale), dev(rot), h, w, 16)
+    c_ref, a_ref, n_ref = orc.preprocess(xy, scale, rot, h, w, orc.TIGHT)
+    np.testing.assert_array_equal(host(conic), c_ref)
+    np.testing.assert_array_equal(host(aabb), a_ref)
+    np.testing.assert_array_equal(host(count), n_ref)
+
+
+def test_preprocess_known_answers_and_nonfinite(cuda_device):
+    from oss_cuda._test_helpers import preprocess_only
+
+    xy = dev([[64.0, 64.0], [-100.0, -100.0], [10.0, 10.0], [20.0, 20.0], [math.nan, 5.0], [math.inf, 3.0]])
+    scale = dev([[3.0, 3.0], [2.0, 2.0], [3.0, 3.0], [math.inf, 2.0], [2.0, 2.0], [1.0, 1.0]])
+    rot = dev([0.0, 0.0, math.nan, 0.3, 0.1, 0.2])
+    conic, aabb, count = preprocess_only(xy, scale, rot, 128, 128, 16)
+    c = host(conic)
+    assert abs(c[0, 0] - 1 / 9) <= 1e-7 and abs(c[0, 2] - 1 / 9) <= 1e-7
+    assert host(aabb)[0].tolist() == [3, 3, 5, 5] and host(count)[0] == 4
+    assert host(aabb)[1].tolist() == [0, 0, 0, 0] and host(count)[1] == 0
+    assert host(aabb)[2].tolist() == [0, 0, 0, 0] and host(count)[2] == 0  # NaN rot
+    c_ref, a_ref, n_ref = orc.preprocess(host(xy), host(scale), host(rot), 128, 128, orc.TIGHT)
+    np.testing.assert_array_equal(host(aabb), a_ref)
+    np.testing.assert_array_equal(host(count), n_ref)
+    np.testing.assert_array_equal(np.isnan(c), np.isnan(c_ref))
+
+
+# ------------------------------------------------------------------ binning
+
+@pytest.mark.parametrize("n,h,w", [(0, 64, 64), (1, 16, 16), (4, 64, 64), (64, 256, 256), (257, 37, 91),
+                                   (4096, 540, 960), (16384, 540, 960), (200_000, 1080, 1920)])
+def test_pair_construction_bit_exact(cuda_device, n, h, w):
+    from oss_cuda._test_helpers import pair_construction_only
+
+    xy, scale, rot, _ = random_gaussians(n, h, w, 1, seed=7 + n, scale_lo=0.5, scale_hi=4.0)
+    gid, offs, conic, total = pair_construction_only(dev(xy), dev(scale), dev(rot), h, w, 16)
+    _, _, _, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, orc.TIGHT)
+    assert total == g_ref.size
+    np.testing.assert_array_equal(host(offs), o_ref)
+    np.testing.assert_array_equal(host(gid), g_ref)
+
+
+def test_pair_construction_matches_reference_list_builder(cuda_device):
+    from oss_cuda._test_helpers import pair_construction_only
+
+    data = load_golden("tight_lists.npz")
+    for name in data["names"]:
+        c = golden_case(data, str(name))
+        h, w = (int(v) for v in c["hw"])
+        gid, offs, conic, total = pair_construction_only(dev(c["xy"]), dev(c["scale"]), dev(c["rot"]), h, w)
+        np.testing.assert_array_equal(host(gid), c["gid"])
+        np.testing.assert_array_equal(host(offs), c["offsets"])
+        assert_close(host(conic), c["conic"], atol=1e-6, rtol=1e-6, what="conic")
+
+
+@pytest.mark.parametrize("n,t", [(0, 1), (1, 1), (1000, 1), (5000, 37), (100_000, 8160), (300_000, 32400),
+                                 (70_000, 70_000)])
+def test_tile_bin_counting_sort_bit_exact(cuda_device, n, t):
+    from oss_cuda import tile_bin_counting_sort
+
+    rng = np.random.default_rng(n + t)
+    tile_id = rng.integers(-2, t + 2, size=n).astype(np.int32)
+    gid = rng.integers(0, 1 << 30, size=n).astype(np.int32)
+    out, offs = tile_bin_counting_sort(dev(tile_id, torch.int32), dev(gid, torch.int32), t)
+    o_ref, f_ref = orc.tile_bin_counting_sort(tile_id, gid, t)
+    np.testing.assert_array_equal(host(offs), f_ref)
+    np.testing.assert_array_equal(host(out), o_ref)
+
+
+# ------------------------------------------------------------------ forward
+
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full"])
+@pytest.mark.parametrize("n,h,w,f", [(0, 32, 32, 3), (1, 32, 32, 1), (16, 64, 128, 3), (256, 256, 256, 12),
+                                     (300, 37, 53, 64), (4096, 270, 480, 3)])
+def test_forward_matches_oracle(cuda_device, mode, n, h, w, f):
+    from oss_cuda.rasterizer import _C
+
+    if mode == "full" and n * h * w > 2e7:
+        pytest.skip("full-frame lists are O(N*tiles)")
+    xy, scale, rot, feat = random_gaussians(n, h, w, f, seed=n * 3 + f)
+    out, gid, offs, conic = _C.rasterize_forward(dev(xy), dev(scale), dev(rot), dev(feat), h, w, 16, True,
+                                                 binning=mode)
+    c_ref, _, _, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, MODES[mode])
+    np.testing.assert_array_equal(host(gid), g_ref)
+    np.testing.assert_array_equal(host(offs), o_ref)
+    np.testing.assert_array_equal(host(conic), c_ref)
+    ref = orc.render_forward(xy, c_ref, feat, g_ref, o_ref, h, w)
+    assert out.shape == (f, h, w)
+    assert_close(host(out), ref, what=f"image {mode}")
+
+
+@pytest.mark.parametrize("n", [0, 1, 16, 256, 4096])
+@pytest.mark.parametrize("hw", [(32, 32), (64, 128), (256, 256), (270, 480), (540, 960)])
+@pytest.mark.parametrize("f", [1, 3, 12, 64])
+def test_reference_equivalence_grid(cuda_device, n, hw, f):
+    """tests/cuda/test_rasterizer_equivalence.py grid: the reference-signature
+    call (default binning) against the full-tail sum, at 1e-5 instead of 5e-3."""
+    from oss_cuda import rasterize_gaussians
+
+    h, w = hw
+    if n * h * w * f > 270_000_000:
+        pytest.skip("too large for fast suite")
+    xy, scale, rot, feat = random_gaussians(n, h, w, f, seed=0xC0DA + n + f)
+    out = rasterize_gaussians(dev(xy), dev(scale), dev(rot), dev(feat), h, w, tile_size=16, topk_norm=True)
+    ref = orc.render(xy, scale, rot, feat, h, w, orc.EXACT)
+    assert out.shape == (f, h, w)
+    assert_close(host(out), ref, what="image")
+
+
+def test_forward_matches_reference_golden(cuda_device):
+    from oss_cuda import rasterize_gaussians
+
+    data = load_golden("render_cases.npz")
+    for name in data["names"]:
+        c = golden_case(data, str(name))
+        h, w = (int(v) for v in c["hw"])
+        for binning in ("exact", "full"):
+            out = rasterize_gaussians(dev(c["xy"]), dev(c["scale"]), dev(c["rot"]), dev(c["feat"]), h, w,
+                                      binning=binning)
+            assert_close(host(out), c["image"], what=f"{name} {binning}")
+
+
+# ------------------------------------------------------------------ backward
+
+def run_autograd(xy, scale, rot, feat, grad, h, w, binning, opacity=None):
+    from oss_cuda import rasterize_gaussians
+
+    leaves = [dev(a).requires_grad_(True) for a in (xy, scale, rot, feat)]
+    op = dev(opacity).requires_grad_(True) if opacity is not None else None
+    out = rasterize_gaussians(*leaves, h, w, binning=binning, opacity=op)
+    out.backward(dev(grad))
+    grads = [host(t.grad) for t in leaves]
+    if op is not None:
+        grads.append(host(op.grad))
+    return host(out), grads
+
+
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full"])
+@pytest.mark.parametrize("n,h,w,f", [(1, 16, 16, 1), (16, 32, 32, 3), (256, 64, 128, 3), (200, 37, 53, 12),
+                                     (64, 48, 48, 64), (4096, 270, 480, 3)])
+def test_backward_matches_oracle(cuda_device, mode, n, h, w, f):
+    if mode == "full" and n * h * w > 2e7:
+        pytest.skip("full-frame lists are O(N*tiles)")
+    xy, scale, rot, feat = random_gaussians(n, h, w, f, seed=n + 11 * f)
+    grad = np.random.default_rng(n).standard_normal((f, h, w)).astype(np.float32)
+    _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(xy, scale, rot, feat, grad, h, w, mode)
+    r_xy, r_scale, r_rot, r_feat, _, _ = orc.render_grads(xy, scale, rot, feat, grad, h, w, MODES[mode])
+    assert_close(d_xy, r_xy, what="d_xy")
+    assert_close(d_scale, r_scale, what="d_scale")
+    assert_close(d_rot, r_rot, what="d_rot")
+    assert_close(d_feat, r_feat, what="d_feat")
+
+
+def test_backward_with_opacity_matches_oracle(cuda_device):
+    n, h, w = 3000, 135, 240
+    xy, scale, rot, opacity, rgb = baseline_gaussians(n, h, w, seed=5, log_scale_mean=math.log(2.0))
+    grad = np.random.default_rng(5).standard_normal((3, h, w)).astype(np.float32)
+    img, (d_xy, d_scale, d_rot, d_rgb, d_op) = run_autograd(xy, scale, rot, rgb, grad, h, w, "tight3sigma",
+                                                            opacity=opacity)
+    conic, _, _, gid, offs = orc.lists(xy, scale, rot, h, w, orc.TIGHT)
+    assert_close(img, orc.render_forward(xy, conic, rgb, gid, offs, h, w, opacity), what="image")
+    r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, gid, offs, grad, h, w, opacity)
+    r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
+    assert_close(d_xy, r_xy, what="d_xy")
+    assert_close(d_scale, r_scale, what="d_scale")
+    assert_close(d_rot, r_rot, what="d_rot")
+    assert_close(d_rgb, r_rgb, what="d_rgb")
+    assert_close(d_op, r_op, what="d_opacity")
+
+
+def test_backward_matches_reference_golden(cuda_device):
+    data = load_golden("render_cases.npz")
+    for name in data["names"]:
+        c = golden_case(data, str(name))
+        h, w = (int(v) for v in c["hw"])
+        _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
+                                                         "exact")
+        assert_close(d_xy, c["d_xy"], what=f"{name} d_xy")
+        assert_close(d_scale, c["d_scale"], what=f"{name} d_scale")
+        assert_close(d_rot, c["d_rot"], what=f"{name} d_rot")
+        assert_close(d_feat, c["d_feat"], what=f"{name} d_feat")
+
+
+def test_rasterize_backward_lists_dconic(cuda_device):
+    """tests/cuda/test_rasterizer_backward_equivalence.py:97-145 against the
+    golden d_conic of the reference's conic= override."""
+    from oss_cuda.rasterizer import _C
+
+    data = load_golden("render_cases.npz")
+    for name in data["names"]:
+        c = golden_case(data, str(name))
+        h, w = (int(v) for v in c["hw"])
+        xy, scale, rot, feat = (dev(c[k]) for k in ("xy", "scale", "rot", "feat"))
+        _, gid, offs, _ = _C.rasterize_forward(xy, scale, rot, feat, h, w, 16, True)
+        d_xy, d_conic, d_feat = _C.rasterize_backward(xy, scale, rot, feat, dev(c["conic"]), gid, offs,
+                                                      dev(c["grad"]), h, w, 16)
+        assert_close(host(d_conic), c["d_conic"], what=f"{name} d_conic")
+        d_scale, d_rot = _C.conic_to_scale_rot_grad(scale, rot, d_conic)
+        assert_close(host(d_scale), c["d_scale"], what=f"{name} d_scale")
+        assert_close(host(d_rot), c["d_rot"], what=f"{name} d_rot")
+        assert_close(host(d_feat), c["d_feat"], what=f"{name} d_feat")
+
+
+def test_conic_to_scale_rot_known_answer(cuda_device):
+    from oss_cuda.rasterizer import _C
+
+    d_scale, d_rot = _C.conic_to_scale_rot_grad(dev([[2.0, 4.0]]), dev([0.0]), dev([[3.0, 5.0, 7.0]]))
+    assert abs(host(d_scale)[0, 0] + 0.75) <= 1e-6 and abs(host(d_scale)[0, 1] + 0.21875) <= 1e-6
+    assert abs(host(d_rot)[0] - 0.9375) <= 1e-6
+
+
+def test_deterministic_bitwise(cuda_device):
+    n, h, w, f = 20000, 270, 480, 3
+    xy, scale, rot, feat = random_gaussians(n, h, w, f, seed=3)
+    grad = np.random.default_rng(3).standard_normal((f, h, w)).astype(np.float32)
+    a = run_autograd(xy, scale, rot, feat, grad, h, w, "tight3sigma")
+    b = run_autograd(xy, scale, rot, feat, grad, h, w, "tight3sigma")
+    np.testing.assert_array_equal(a[0], b[0])
+    for x, y in zip(a[1], b[1]):
+        np.testing.assert_array_equal(x, y)
+
+
+def test_kernel_does_not_reenter_python(cuda_device):
+    from oss_cuda import rasterizer as oss_rast
+
+    xy = torch.tensor([[16.0, 16.0]], device="cuda", requires_grad=True)
+    scale = torch.tensor([[3.0, 4.0]], device="cuda", requires_grad=True)
+    rot = torch.tensor([0.25], device="cuda", requires_grad=True)
+    feat = torch.tensor([[1.0, -0.5]], device="cuda", requires_grad=True)
+    out = oss_rast.rasterize_gaussians(xy, scale, rot, feat, 32, 32, 16, True)
+    out.sum().backward()
+    assert out.shape == (2, 32, 32)
+    assert all(t.grad is not None for t in (xy, scale, rot, feat))
+    assert not hasattr(oss_rast, "_phase1" + "_ref_forward")
+
+
+# ------------------------------------------------------------------ BASELINE config sizes
+
+def test_config1_full_size_parity(cuda_device):
+    """Config 1: 540x960, N=16384, BASELINE distributions, 3-sigma lists."""
+    from oss_cuda import rasterize_gaussians
+
+    h, w, n = 540, 960, 16384
+    xy, scale, rot, opacity, rgb = baseline_gaussians(n, h, w, seed=1, log_scale_mean=math.log(1.5))
+    out = rasterize_gaussians(dev(xy), dev(scale), dev(rot), dev(rgb), h, w, binning="tight3sigma",
+                              opacity=dev(opacity))
+    conic, _, _, gid, offs = orc.lists(xy, scale, rot, h, w, orc.TIGHT)
+    assert gid.size > 0
+    assert_close(host(out), orc.render_forward(xy, conic, rgb, gid, offs, h, w, opacity), what="config1 image")
+
+
+def test_config2_full_size_parity(cuda_device):
+    """Config 2: 1920x1080, N=200k, fwd+bwd, bit-exact lists, full-size oracle."""
+    from oss_cuda.rasterizer import _C
+
+    h, w, n = 1080, 1920, 200_000
+    xy, scale, rot, opacity, rgb = baseline_gaussians(n, h, w, seed=2, log_scale_mean=math.log(2.0))
+    grad = np.random.default_rng(2).standard_normal((3, h, w)).astype(np.float32)
+    _, gid, offs, _ = _C.rasterize_forward(dev(xy), dev(scale), dev(rot), dev(rgb), h, w, 16, True,
+                                           binning="tight3sigma")
+    conic, _, _, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, orc.TIGHT)
+    np.testing.assert_array_equal(host(offs), o_ref)
+    np.testing.assert_array_equal(host(gid), g_ref)
+    img, (d_xy, d_scale, d_rot, d_rgb, d_op) = run_autograd(xy, scale, rot, rgb, grad, h, w, "tight3sigma",
+                                                            opacity=opacity)
+    assert_close(img, orc.render_forward(xy, conic, rgb, g_ref, o_ref, h, w, opacity), what="config2 image")
+    r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, g_ref, o_ref, grad, h, w, opacity)
+    r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
+    assert_close(d_xy, r_xy, what="config2 d_xy")
+    assert_close(d_scale, r_scale, what="config2 d_scale")
+    assert_close(d_rot, r_rot, what="config2 d_rot")
+    assert_close(d_rgb, r_rgb, what="config2 d_rgb")
+    assert_close(d_op, r_op, what="config2 d_opacity")
+    # size-independent identity: <grad, image> == <d_feat', feat'> (image is linear in feat')
+    lhs = float(np.sum(grad.astype(np.float64) * img))
+    rhs = float(np.sum(d_op.astype(np.float64) * opacity))
+    assert abs(lhs - rhs) <= 1e-4 * max(1.0, abs(lhs))

@@ -1,0 +1,197 @@
+"""Pin the CPU oracle against the reference's known answers and golden vectors.
+
+CPU only.  Known answers come from the reference's gtests
+(tests/cuda/cpp/test_preprocess.cu:67-107, test_build_pairs.cu:82-135,
+test_rasterize.cu:104-164, test_rasterize_backward.cu:19-247); golden vectors
+come from its PyTorch implementation (tests/golden/make_golden.py).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+import oracle as orc
+from conftest import assert_close, golden_case, load_golden
+
+RENDER = load_golden("render_cases.npz")
+TIGHT = load_golden("tight_lists.npz")
+OVERLAP = load_golden("overlap_cases.npz")
+
+
+# --- known-answer tests from the reference gtests --------------------------------
+
+def test_kat_preprocess_single_point_at_center():
+    conic, aabb, count = orc.preprocess([[64.0, 64.0]], [[3.0, 3.0]], [0.0], 128, 128)
+    assert abs(conic[0, 0] - 1.0 / 9.0) <= 1e-7 and abs(conic[0, 1]) <= 1e-7 and abs(conic[0, 2] - 1.0 / 9.0) <= 1e-7
+    assert aabb[0].tolist() == [3, 3, 5, 5]
+    assert count[0] == 4
+
+
+def test_kat_preprocess_offscreen_and_nan_rot():
+    _, aabb, count = orc.preprocess([[-100.0, -100.0], [10.0, 10.0]], [[2.0, 2.0], [3.0, 3.0]], [0.0, math.nan],
+                                    128, 128)
+    assert aabb.tolist() == [[0, 0, 0, 0], [0, 0, 0, 0]]
+    assert count.tolist() == [0, 0]
+
+
+def test_kat_build_pairs_layout():
+    # test_build_pairs.cu: a 1x1 box at (2,2) of a 4-wide grid is tile 10; a 2x2
+    # box at the origin covers tiles 0,1,4,5 in row-major order; no pairs -> empty.
+    gid, offs = orc.pair_construction([[2, 2, 3, 3]], [1], 64, 64)
+    assert gid.tolist() == [0] and offs[10] == 0 and offs[11] == 1
+    gid, offs = orc.pair_construction([[0, 0, 2, 2]], [4], 64, 64)
+    assert gid.tolist() == [0, 0, 0, 0]
+    assert [int(offs[t + 1] - offs[t]) for t in (0, 1, 4, 5)] == [1, 1, 1, 1]
+    gid, offs = orc.pair_construction([[0, 0, 0, 0]], [0], 64, 64)
+    assert gid.size == 0 and int(offs[-1]) == 0
+
+
+def _gauss(px, py, cx, cy, sigma):
+    return math.exp(-0.5 * ((px - cx) ** 2 + (py - cy) ** 2) / sigma**2)
+
+
+def test_kat_rasterize_single_and_additive():
+    # test_rasterize.cu:104-164, full-frame lists; exact here instead of 5e-3.
+    xy = np.array([[16.0, 16.0], [8.0, 8.0]], np.float32)
+    conic = np.array([[1 / 9, 0, 1 / 9], [0.25, 0, 0.25]], np.float32)
+    feat = np.array([[1.0], [2.0]], np.float32)
+    gid, offs = orc.full_pairs(2, 32, 32)
+    out = orc.render_forward(xy, conic, feat, gid, offs, 32, 32)
+    ref = np.array([[_gauss(x, y, 16, 16, 3) + 2 * _gauss(x, y, 8, 8, 2) for x in range(32)] for y in range(32)])
+    assert_close(out[0], ref, atol=1e-6, rtol=1e-6, what="additive")
+    gid, offs = orc.full_pairs(1, 32, 32)
+    out = orc.render_forward(xy[:1] * 0 - 100, conic[1:], feat[:1], gid, offs, 32, 32)
+    assert np.abs(out).max() < 1e-30
+
+
+def test_kat_backward_dfeat_and_dxy_analytic():
+    # test_rasterize_backward.cu:19-207
+    xy = np.array([[8.0, 8.0]], np.float32)
+    conic, _, _ = orc.preprocess(xy, [[2.0, 2.0]], [0.0], 16, 16)
+    gid, offs = np.array([0], np.int32), np.array([0, 1], np.int32)
+    ones = np.ones((1, 16, 16), np.float32)
+    _, _, d_feat, _ = orc.render_backward(xy, conic, [[1.0]], gid, offs, ones, 16, 16)
+    expected = sum(_gauss(x, y, 8, 8, 2) for x in range(16) for y in range(16))
+    assert abs(d_feat[0, 0] - expected) < 1e-4
+    grad = np.zeros((1, 16, 16), np.float32)
+    grad[0, 8, 9] = 2.0
+    d_xy, d_conic, d_feat, _ = orc.render_backward(xy, [[0.25, 0.0, 0.25]], [[3.0]], gid, offs, grad, 16, 16)
+    w = math.exp(-0.125)
+    assert abs(d_feat[0, 0] - 2 * w) < 1e-5
+    assert abs(d_xy[0, 0] - 1.5 * w) < 1e-5 and abs(d_xy[0, 1]) < 1e-5
+    assert abs(d_conic[0, 0] + 3 * w) < 1e-5 and abs(d_conic[0, 1]) < 1e-5 and abs(d_conic[0, 2]) < 1e-5
+
+
+def test_kat_conic_to_scale_rot():
+    d_scale, d_rot = orc.conic_to_scale_rot_grad([[2.0, 4.0]], [0.0], [[3.0, 5.0, 7.0]])
+    assert abs(d_scale[0, 0] + 0.75) <= 1e-6 and abs(d_scale[0, 1] + 0.21875) <= 1e-6
+    assert abs(d_rot[0] - 0.9375) <= 1e-6
+
+
+# --- golden vectors from the reference PyTorch implementation -------------------
+
+@pytest.mark.parametrize("name", [str(n) for n in RENDER["names"]])
+@pytest.mark.parametrize("mode", [orc.FULL, orc.EXACT])
+def test_oracle_matches_reference_render(name, mode):
+    c = golden_case(RENDER, name)
+    h, w = (int(v) for v in c["hw"])
+    img = orc.render(c["xy"], c["scale"], c["rot"], c["feat"], h, w, mode)
+    assert_close(img, c["image"], what=f"image {name}")
+    d_xy, d_scale, d_rot, d_feat, _, _ = orc.render_grads(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
+                                                          mode)
+    assert_close(d_xy, c["d_xy"], what="d_xy")
+    assert_close(d_scale, c["d_scale"], what="d_scale")
+    assert_close(d_rot, c["d_rot"], what="d_rot")
+    assert_close(d_feat, c["d_feat"], what="d_feat")
+
+
+@pytest.mark.parametrize("name", [str(n) for n in RENDER["names"]])
+def test_oracle_matches_reference_dconic(name):
+    c = golden_case(RENDER, name)
+    h, w = (int(v) for v in c["hw"])
+    conic, _, _ = orc.preprocess(c["xy"], c["scale"], c["rot"], h, w)
+    assert_close(conic, c["conic"], atol=1e-6, rtol=1e-6, what="conic")
+    gid, offs = orc.full_pairs(conic.shape[0], h, w)
+    _, d_conic, _, _ = orc.render_backward(c["xy"], c["conic"], c["feat"], gid, offs, c["grad"], h, w)
+    assert_close(d_conic, c["d_conic"], what="d_conic")
+
+
+@pytest.mark.parametrize("name", [str(n) for n in TIGHT["names"]])
+def test_oracle_tight_lists_match_reference_list_builder(name):
+    c = golden_case(TIGHT, name)
+    h, w = (int(v) for v in c["hw"])
+    conic, aabb, count, gid, offs = orc.lists(c["xy"], c["scale"], c["rot"], h, w, orc.TIGHT)
+    assert_close(conic, c["conic"], atol=1e-6, rtol=1e-6, what="conic")
+    np.testing.assert_array_equal(aabb, c["aabb"])
+    np.testing.assert_array_equal(count, c["count"])
+    np.testing.assert_array_equal(gid, c["gid"])
+    np.testing.assert_array_equal(offs, c["offsets"])
+
+
+def test_oracle_tile_bin_counting_sort_semantics():
+    rng = np.random.default_rng(7)
+    n, t = 5000, 37
+    tile_id = rng.integers(-3, t + 3, size=n).astype(np.int32)
+    gid = rng.integers(0, 1 << 20, size=n).astype(np.int32)
+    out, offs = orc.tile_bin_counting_sort(tile_id, gid, t)
+    valid = (tile_id >= 0) & (tile_id < t)
+    counts = np.bincount(tile_id[valid], minlength=t)
+    np.testing.assert_array_equal(offs[:t], np.concatenate([[0], np.cumsum(counts)[:-1]]))
+    assert offs[t] == n
+    order = np.argsort(np.where(valid, tile_id, t), kind="stable")
+    np.testing.assert_array_equal(out, gid[order])
+
+
+def overlap_oracle(xy, scale, rot, feat, grad, h, w, overlap, mode=orc.EXACT):
+    """V6Rasterizer._render_overlapped (oss/sr/v6/rasterizer.py:159-234) over oracle renders."""
+    tile = 16.0
+    origins = ((0, 0), (-overlap, 0), (0, -overlap), (-overlap, -overlap))
+    f = feat.shape[1]
+    accum = np.zeros((f, h, w), np.float32)
+    wsum = np.zeros((1, h, w), np.float32)
+    masks, crops = [], []
+    for oy, ox in origins:
+        ch = -(-(h - min(oy, 0)) // 16) * 16
+        cw = -(-(w - min(ox, 0)) // 16) * 16
+        lxy = xy.copy()
+        lxy[:, 0] -= float(ox)
+        lxy[:, 1] -= float(oy)
+        img = orc.render(lxy, scale, rot, feat, ch, cw, mode)
+        ys, xs = -min(oy, 0), -min(ox, 0)
+        img = img[:, ys:ys + h, xs:xs + w]
+        py = np.remainder(np.arange(h, dtype=np.float32) + 0.5 - oy, tile)
+        px = np.remainder(np.arange(w, dtype=np.float32) + 0.5 - ox, tile)
+        dy = np.minimum(py, tile - py)
+        dx = np.minimum(px, tile - px)
+        ramp = lambda t: 0.5 - 0.5 * np.cos(t * math.pi)
+        m = (ramp(np.clip(dy / overlap, 0, 1))[:, None] * ramp(np.clip(dx / overlap, 0, 1))[None, :])[None]
+        accum += img * m
+        wsum += m
+        masks.append(m.astype(np.float32))
+        crops.append((oy, ox, ch, cw, lxy))
+    den = np.maximum(wsum, 1e-6)
+    image = accum / den
+    grads = [np.zeros_like(xy), np.zeros_like(scale), np.zeros_like(rot), np.zeros_like(feat)]
+    for m, (oy, ox, ch, cw, lxy) in zip(masks, crops):
+        g = np.zeros((f, ch, cw), np.float32)
+        ys, xs = -min(oy, 0), -min(ox, 0)
+        g[:, ys:ys + h, xs:xs + w] = grad * m / den
+        d_xy, d_scale, d_rot, d_feat, _, _ = orc.render_grads(lxy, scale, rot, feat, g, ch, cw, mode)
+        for acc, d in zip(grads, (d_xy, d_scale, d_rot, d_feat)):
+            acc += d
+    return image, grads
+
+
+@pytest.mark.parametrize("name", [str(n) for n in OVERLAP["names"]])
+def test_oracle_overlap_matches_reference(name):
+    c = golden_case(OVERLAP, name)
+    h, w = (int(v) for v in c["hw"])
+    image, (d_xy, d_scale, d_rot, d_feat) = overlap_oracle(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
+                                                           int(c["overlap"]))
+    assert_close(image, c["image"], what="overlap image")
+    assert_close(d_xy, c["d_xy"], what="overlap d_xy")
+    assert_close(d_scale, c["d_scale"], what="overlap d_scale")
+    assert_close(d_rot, c["d_rot"], what="overlap d_rot")
+    assert_close(d_feat, c["d_feat"], what="overlap d_feat")
