@@ -198,6 +198,35 @@ OSS_API int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles,
                                int32_t* sorted_gid, int32_t* tile_offsets,
                                void* scratch, int64_t scratch_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * GS-STVSR canvas warp: replaces oss/sr/v6/canvas_warp.py:177-254 (warp_canvas)
+ * with covariance_resampling.py:76-116.  motion_lr[2][h_lr][w_lr] is the LR
+ * motion of the canvas (the reference uses the first batch item, :66-77) and
+ * is multiplied by alpha before use (extrapolation at t + alpha).  The HR
+ * motion is F.interpolate(bilinear, align_corners=False) of it when
+ * (h_lr, w_lr) != (h, w), evaluated per Gaussian without an HR buffer.
+ * recon is the 2x2 row-major Sigma_recon (HOST pointer, 4 floats).
+ * Gaussians whose warped centre leaves [0,w)x[0,h) are dropped; the others are
+ * written in input order to out_*; out_count (device int32) receives their
+ * number.  colors is [n][f].
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_warp_canvas_scratch_bytes(int64_t n);
+OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h, int64_t w,
+                            const float* motion_lr, float alpha, const float* recon,
+                            const float* positions, const float* scales, const float* rotations,
+                            const float* opacities, const float* colors,
+                            float* out_positions, float* out_scales, float* out_rotations,
+                            float* out_opacities, float* out_colors, int32_t* out_count,
+                            void* scratch, int64_t scratch_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Position-only warp: replaces oss/gaussian/canvas/warp.py:28-91
+ * (warp_positions); motion[2][h][w] at the output resolution, times alpha
+ * (warp_canvas(canvas, motion, alpha), :94-137).  in_frame is uint8 [n].
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, float alpha,
+                               const float* xy, float* out_xy, uint8_t* in_frame, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

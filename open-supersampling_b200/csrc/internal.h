@@ -54,6 +54,16 @@ cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const
                              uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
 cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
 
+// ---- warp.cu ---------------------------------------------------------------
+int64_t warp_scratch_bytes(int64_t n);
+cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                               const float* recon4, const float* pos, const float* scales, const float* rots,
+                               const float* ops, const float* colors, float* out_pos, float* out_scales,
+                               float* out_rots, float* out_ops, float* out_colors, int32_t* out_count,
+                               void* scratch, cudaStream_t stream);
+cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, float alpha, const float* xy,
+                                  float* out_xy, uint8_t* in_frame, cudaStream_t stream);
+
 // ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat,
                                   const float* opacity, const int32_t* gid_sorted,

@@ -1,0 +1,141 @@
+"""Canvas warp on the GPU through liboss_b200.so.
+
+warp_canvas   -- drop-in for oss/sr/v6/canvas_warp.py:177-254 (GS-STVSR:
+                 motion sample, J = I + grad(motion), J S J^T + Sigma_recon,
+                 re-decomposition, in-frame compaction), with an added
+                 ``alpha`` that scales the motion (extrapolation at t + alpha).
+warp_positions -- drop-in for oss/gaussian/canvas/warp.py:28-91.
+
+Forward only: the kernels do not record an autograd graph, so a call with
+inputs that require grad under grad mode raises instead of silently cutting
+the graph.
+"""
+from __future__ import annotations
+
+from typing import Tuple
+
+import torch
+
+from oss_cuda import _lib
+from oss_cuda._raster import aligned, stream_of
+
+from .canvas import CanvasState
+
+
+def _validate_canvas(canvas) -> int:
+    # same checks and messages as canvas_warp.py:28-52
+    count = int(canvas.count)
+    if count < 0:
+        raise ValueError(f"canvas.count must be non-negative; got {canvas.count}")
+    if canvas.positions.ndim != 2 or canvas.positions.shape[-1] != 2:
+        raise ValueError(f"canvas.positions must be (N, 2); got {tuple(canvas.positions.shape)}")
+    if canvas.scales.ndim != 2 or canvas.scales.shape[-1] != 2:
+        raise ValueError(f"canvas.scales must be (N, 2); got {tuple(canvas.scales.shape)}")
+    if canvas.rotations.ndim != 1:
+        raise ValueError(f"canvas.rotations must be (N,); got {tuple(canvas.rotations.shape)}")
+    if canvas.opacities.ndim != 1:
+        raise ValueError(f"canvas.opacities must be (N,); got {tuple(canvas.opacities.shape)}")
+    if canvas.colors.ndim != 2:
+        raise ValueError(f"canvas.colors must be (N, F); got {tuple(canvas.colors.shape)}")
+    lengths = tuple(t.shape[0] for t in (canvas.positions, canvas.scales, canvas.rotations, canvas.opacities,
+                                         canvas.colors))
+    if count > min(lengths):
+        raise ValueError(f"canvas.count={count} exceeds tensor lengths {lengths}")
+    return count
+
+
+def _validate_motion(motion_lr: torch.Tensor, output_hw) -> tuple[int, int]:
+    if motion_lr.ndim != 4 or motion_lr.shape[1] != 2:
+        raise ValueError(f"motion_lr must be (B, 2, H, W); got {tuple(motion_lr.shape)}")
+    if motion_lr.shape[0] < 1:
+        raise ValueError("motion_lr batch dimension must be non-empty")
+    h_hr, w_hr = int(output_hw[0]), int(output_hw[1])
+    if h_hr <= 0 or w_hr <= 0:
+        raise ValueError(f"output_hw must be positive; got {output_hw}")
+    return h_hr, w_hr
+
+
+def _no_grad_inputs(*tensors) -> None:
+    if torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
+        raise RuntimeError("oss_b200 warp kernels are forward-only; call under torch.no_grad() or detach inputs")
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return aligned(t.detach().to(dtype=torch.float32).contiguous(), 8)
+
+
+def _recon4(sigma_recon) -> list[float]:
+    if isinstance(sigma_recon, torch.Tensor):
+        if sigma_recon.shape[-2:] != (2, 2) or sigma_recon.numel() != 4:
+            raise ValueError("sigma_recon tensor must be a single (2, 2) matrix for the CUDA warp")
+        return [float(v) for v in sigma_recon.detach().float().reshape(4).cpu()]
+    s = float(sigma_recon)
+    return [s, 0.0, 0.0, s]
+
+
+def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
+                sigma_recon: torch.Tensor | float = 0.5, alpha: float = 1.0) -> CanvasState:
+    """Warp canvas positions by alpha * motion and resample covariances.
+
+    Returns a fresh CanvasState holding the Gaussians whose warped centre
+    stays inside the frame, in input order (one device->host read of the
+    count, as the reference's ``.item()`` at canvas_warp.py:253).
+    """
+    h, w = _validate_motion(motion_lr, output_hw)
+    count = _validate_canvas(canvas)
+    src = [canvas.positions[:count], canvas.scales[:count], canvas.rotations[:count], canvas.opacities[:count],
+           canvas.colors[:count]]
+    _no_grad_inputs(motion_lr, *src)
+    if count == 0:
+        return CanvasState(*(t.clone() for t in src), count=0)
+    dev = canvas.positions.device
+    if dev.type != "cuda" or motion_lr.device != dev:
+        raise RuntimeError("warp_canvas needs canvas and motion_lr on the same CUDA device")
+    out_dtypes = [t.dtype for t in src]
+    pos, sc, rt, op, col = (_f32(t) for t in src)
+    motion = _f32(motion_lr[0])
+    f = int(col.shape[1])
+    lib = _lib.lib()
+    with torch.cuda.device(dev):
+        f32 = dict(device=dev, dtype=torch.float32)
+        outs = [torch.empty((count, 2), **f32), torch.empty((count, 2), **f32), torch.empty((count,), **f32),
+                torch.empty((count,), **f32), torch.empty((count, f), **f32)]
+        out_count = torch.empty((1,), device=dev, dtype=torch.int32)
+        scratch = torch.empty((lib.oss_warp_canvas_scratch_bytes(count),), device=dev, dtype=torch.uint8)
+        recon = (torch.tensor(_recon4(sigma_recon), dtype=torch.float32))
+        _lib.check(
+            lib.oss_warp_canvas(count, f, motion.shape[1], motion.shape[2], h, w, motion.data_ptr(), float(alpha),
+                                recon.data_ptr(), pos.data_ptr(), sc.data_ptr(), rt.data_ptr(), op.data_ptr(),
+                                col.data_ptr() if f > 0 else None, *(o.data_ptr() if o.numel() else None for o in outs),
+                                out_count.data_ptr(), scratch.data_ptr(), scratch.numel(), stream_of(pos)),
+            "oss_warp_canvas",
+        )
+        k = int(out_count.item())
+    res = [o[:k].to(dtype=dt) for o, dt in zip(outs, out_dtypes)]
+    return CanvasState(*res, count=k)
+
+
+def warp_positions(xy: torch.Tensor, motion: torch.Tensor, hw: Tuple[int, int],
+                   alpha: float = 1.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(new_xy, in_frame) for a motion field (2, H, W) at the frame resolution."""
+    if xy.ndim != 2 or xy.shape[1] != 2:
+        raise ValueError(f"xy must be (N, 2); got {tuple(xy.shape)}")
+    if motion.ndim != 3 or motion.shape[0] != 2:
+        raise ValueError(f"motion must be (2, H, W); got {tuple(motion.shape)}")
+    h, w = int(hw[0]), int(hw[1])
+    if motion.shape[1] != h or motion.shape[2] != w:
+        raise ValueError(f"motion spatial dims {tuple(motion.shape[1:])} disagree with hw={hw}")
+    _no_grad_inputs(xy, motion)
+    n = int(xy.shape[0])
+    if n == 0:
+        return xy.clone(), torch.zeros((0,), dtype=torch.bool, device=xy.device)
+    if xy.device.type != "cuda":
+        raise RuntimeError("warp_positions needs CUDA tensors")
+    p, m = _f32(xy), _f32(motion)
+    lib = _lib.lib()
+    with torch.cuda.device(xy.device):
+        out = torch.empty((n, 2), device=xy.device, dtype=torch.float32)
+        flag = torch.empty((n,), device=xy.device, dtype=torch.uint8)
+        _lib.check(lib.oss_warp_positions(n, h, w, m.data_ptr(), float(alpha), p.data_ptr(), out.data_ptr(),
+                                          flag.data_ptr(), stream_of(p)), "oss_warp_positions")
+    return out.to(dtype=xy.dtype), flag.bool()

@@ -49,6 +49,13 @@ SIGNATURES = {
     "oss_make_geo": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
     "oss_conic_to_scale_rot_grad": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p]),
     "oss_full_tile_pairs": (ctypes.c_int, [_i64, _i64, _p, _p, _p]),
+    "oss_warp_canvas_scratch_bytes": (_i64, [_i64]),
+    "oss_warp_canvas": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+         _p, _i64, _p],
+    ),
+    "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
     "oss_tile_bin_counting_sort_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_tile_bin_counting_sort": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
 }

@@ -56,7 +56,39 @@ def lib():
         _lib.orc_tile_bin_counting_sort.argtypes = [i64, i64, p, p, p, p]
         _lib.orc_num_threads.restype = i32
         _lib.orc_set_num_threads.argtypes = [i32]
+        f32 = ctypes.c_float
+        _lib.orc_warp_canvas.argtypes = [i64, i32, i32, i32, i32, i32, p, f32, p, p, p, p, p, p, p, p, p, p, p]
+        _lib.orc_warp_canvas.restype = i64
+        _lib.orc_warp_positions.argtypes = [i64, i32, i32, p, f32, p, p, p]
     return _lib
+
+
+def warp_canvas(positions, scales, rotations, opacities, colors, motion_lr, hw, sigma_recon=0.5, alpha=1.0):
+    """GS-STVSR canvas warp (oss/sr/v6/canvas_warp.py:177-254) with motion
+    pre-multiplied by alpha; returns the compacted canvas arrays and count."""
+    pos, sc, rt, op, col = _f32(positions), _f32(scales), _f32(rotations), _f32(opacities), _f32(colors)
+    m = _f32(motion_lr)
+    if m.ndim == 4:
+        m = np.ascontiguousarray(m[0])
+    n, f = col.shape
+    h, w = int(hw[0]), int(hw[1])
+    rec = np.asarray(sigma_recon, np.float32)
+    rec = _f32(np.eye(2, dtype=np.float32) * rec) if rec.ndim == 0 else _f32(rec.reshape(2, 2))
+    outs = [np.empty((n, 2), np.float32), np.empty((n, 2), np.float32), np.empty((n,), np.float32),
+            np.empty((n,), np.float32), np.empty((n, f), np.float32)]
+    k = lib().orc_warp_canvas(n, f, m.shape[1], m.shape[2], h, w, _p(m), float(alpha), _p(rec), _p(pos), _p(sc),
+                              _p(rt), _p(op), _p(col), *(_p(o) for o in outs))
+    return tuple(o[:k] for o in outs) + (int(k),)
+
+
+def warp_positions(xy, motion, hw, alpha=1.0):
+    """oss/gaussian/canvas/warp.py:28-91 with motion * alpha; (new_xy, in_frame)."""
+    xy, m = _f32(xy), _f32(motion)
+    n = xy.shape[0]
+    out = np.empty((n, 2), np.float32)
+    flag = np.empty((n,), np.uint8)
+    lib().orc_warp_positions(n, int(hw[0]), int(hw[1]), _p(m), float(alpha), _p(xy), _p(out), _p(flag))
+    return out, flag.astype(bool)
 
 
 def _f32(a) -> np.ndarray:

@@ -357,3 +357,164 @@ void orc_set_num_threads(int t) {
     (void)t;
 #endif
 }
+
+/* ------------------------------------------------------------------------
+ * Canvas warp, oss/sr/v6/canvas_warp.py:177-254 (GS-STVSR), restated per
+ * Gaussian without materialising the HR motion field.
+ * motion_lr[2][hl][wl] is the first batch item; alpha pre-multiplies it (the
+ * extrapolation-alpha composition warp_canvas(canvas, alpha * motion_lr, hw)).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const float* m;
+    int hl, wl, h, w;
+    float alpha, scale_y, scale_x;
+    int same;
+} orc_field;
+
+static float orc_lr(const orc_field* f, int ch, int y, int x) {
+    return f->alpha * f->m[((int64_t)ch * f->hl + y) * f->wl + x];
+}
+
+/* F.interpolate(bilinear, align_corners=False) texel of the HR field
+ * (aten area_pixel_compute_source_index + linear weights) */
+static float orc_hr(const orc_field* f, int ch, int i, int j) {
+    if (f->same) return orc_lr(f, ch, i, j);
+    float sy = f->scale_y * ((float)i + 0.5f) - 0.5f;
+    if (sy < 0.0f) sy = 0.0f;
+    float sx = f->scale_x * ((float)j + 0.5f) - 0.5f;
+    if (sx < 0.0f) sx = 0.0f;
+    const int y0 = (int)sy, x0 = (int)sx;
+    const int y1 = y0 + (y0 < f->hl - 1 ? 1 : 0), x1 = x0 + (x0 < f->wl - 1 ? 1 : 0);
+    float ly1 = sy - (float)y0;
+    if (ly1 > 1.0f) ly1 = 1.0f;
+    float lx1 = sx - (float)x0;
+    if (lx1 > 1.0f) lx1 = 1.0f;
+    const float ly0 = 1.0f - ly1, lx0 = 1.0f - lx1;
+    return ly0 * (lx0 * orc_lr(f, ch, y0, x0) + lx1 * orc_lr(f, ch, y0, x1)) +
+           ly1 * (lx0 * orc_lr(f, ch, y1, x0) + lx1 * orc_lr(f, ch, y1, x1));
+}
+
+/* kind 0: HR motion; 1: d/dx central difference; 2: d/dy (replicate pad) */
+static float orc_field_at(const orc_field* f, int kind, int ch, int i, int j) {
+    if (kind == 0) return orc_hr(f, ch, i, j);
+    if (kind == 1) {
+        const int jp = j + 1 < f->w ? j + 1 : f->w - 1, jm = j - 1 >= 0 ? j - 1 : 0;
+        return (orc_hr(f, ch, i, jp) - orc_hr(f, ch, i, jm)) * 0.5f;
+    }
+    const int ip = i + 1 < f->h ? i + 1 : f->h - 1, im = i - 1 >= 0 ? i - 1 : 0;
+    return (orc_hr(f, ch, ip, j) - orc_hr(f, ch, im, j)) * 0.5f;
+}
+
+/* F.grid_sample(bilinear, align_corners=False) at pixel position (x, y);
+ * border != 0 clips the source coordinate (padding_mode="border"), else
+ * out-of-range taps read 0 (padding_mode="zeros"). */
+static float orc_grid_sample(const orc_field* f, int kind, int ch, float x, float y, int border) {
+    const float gx = (x / (float)f->w) * 2.0f - 1.0f;
+    const float gy = (y / (float)f->h) * 2.0f - 1.0f;
+    float ix = ((gx + 1.0f) * (float)f->w - 1.0f) / 2.0f;
+    float iy = ((gy + 1.0f) * (float)f->h - 1.0f) / 2.0f;
+    if (border) {
+        ix = fminf((float)(f->w - 1), fmaxf(ix, 0.0f));
+        iy = fminf((float)(f->h - 1), fmaxf(iy, 0.0f));
+    }
+    const float x0 = floorf(ix), y0 = floorf(iy);
+    const float wx = ix - x0, wy = iy - y0;
+    const float ex = 1.0f - wx, sy = 1.0f - wy;
+    const float wts[4] = {sy * ex, sy * wx, wy * ex, wy * wx};
+    /* every tap out of range (or NaN coordinates): zero padding */
+    if (!(x0 > -2.0f && x0 < (float)f->w && y0 > -2.0f && y0 < (float)f->h)) return 0.0f;
+    const int xs[4] = {(int)x0, (int)x0 + 1, (int)x0, (int)x0 + 1};
+    const int ys[4] = {(int)y0, (int)y0, (int)y0 + 1, (int)y0 + 1};
+    float out = 0.0f;
+    for (int k = 0; k < 4; ++k) {
+        if (xs[k] >= 0 && xs[k] < f->w && ys[k] >= 0 && ys[k] < f->h)
+            out += orc_field_at(f, kind, ch, ys[k], xs[k]) * wts[k];
+    }
+    return out;
+}
+
+/*
+ * Per Gaussian: new position, in-frame flag, and (for non-identity Jacobians)
+ * the resampled covariance J S J^T + recon (+ symmetrise + 1e-7 ridge,
+ * covariance_resampling.py:76-116) decomposed largest axis first
+ * (canvas_warp.py:148-166).  recon is 2x2 row-major.  Survivors are compacted
+ * in input order; returns their count.  colors is [n][f].
+ */
+int64_t orc_warp_canvas(int64_t n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                        const float* recon, const float* pos, const float* scales, const float* rots,
+                        const float* ops, const float* colors, float* out_pos, float* out_scales, float* out_rots,
+                        float* out_ops, float* out_colors) {
+    orc_field fld = {motion, hl, wl, h, w, alpha, (float)hl / (float)h, (float)wl / (float)w,
+                     (hl == h && wl == w) ? 1 : 0};
+    int64_t k = 0;
+    for (int64_t g = 0; g < n; ++g) {
+        const float x = pos[2 * g], y = pos[2 * g + 1];
+        const float nx = x + orc_grid_sample(&fld, 0, 0, x, y, 0);
+        const float ny = y + orc_grid_sample(&fld, 0, 1, x, y, 0);
+        const int in_frame = nx >= 0.0f && nx < (float)w && ny >= 0.0f && ny < (float)h;
+        const float j00 = 1.0f + orc_grid_sample(&fld, 1, 0, x, y, 1);
+        const float j10 = 0.0f + orc_grid_sample(&fld, 1, 1, x, y, 1);
+        const float j01 = 0.0f + orc_grid_sample(&fld, 2, 0, x, y, 1);
+        const float j11 = 1.0f + orc_grid_sample(&fld, 2, 1, x, y, 1);
+        float s0 = scales[2 * g], s1 = scales[2 * g + 1], r = rots[g];
+        const float dev = fmaxf(fmaxf(fabsf(j00 - 1.0f), fabsf(j01)), fmaxf(fabsf(j10), fabsf(j11 - 1.0f)));
+        if (!(dev < 1.0e-5f)) {
+            const float c = (float)cos((double)r), s = (float)sin((double)r);
+            const float a0 = fmaxf(s0, 0.0f), a1 = fmaxf(s1, 0.0f);
+            const float v0 = a0 * a0, v1 = a1 * a1;
+            /* R diag(v) R^T with R = [[c, -s], [s, c]] */
+            const float p00 = c * v0, p01 = -s * v1, p10 = s * v0, p11 = c * v1;
+            const float q00 = p00 * c + p01 * (-s), q01 = p00 * s + p01 * c;
+            const float q10 = p10 * c + p11 * (-s), q11 = p10 * s + p11 * c;
+            /* J S J^T */
+            const float t00 = j00 * q00 + j01 * q10, t01 = j00 * q01 + j01 * q11;
+            const float t10 = j10 * q00 + j11 * q10, t11 = j10 * q01 + j11 * q11;
+            float u00 = t00 * j00 + t01 * j01, u01 = t00 * j10 + t01 * j11;
+            float u10 = t10 * j00 + t11 * j01, u11 = t10 * j10 + t11 * j11;
+            u00 += recon[0];
+            u01 += recon[1];
+            u10 += recon[2];
+            u11 += recon[3];
+            /* _ensure_positive_definite: symmetrise + 1e-7 I */
+            const float m01 = 0.5f * (u01 + u10);
+            float e00 = 0.5f * (u00 + u00) + 1.0e-7f, e11 = 0.5f * (u11 + u11) + 1.0e-7f;
+            float e01 = m01 + 0.0f;
+            /* _scales_rotations_from_covariance */
+            const float a = 0.5f * (e00 + e00), b = 0.5f * (e01 + e01), cc = 0.5f * (e11 + e11);
+            const float ht = 0.5f * (a + cc), hd = 0.5f * (a - cc);
+            const float rad = sqrtf(hd * hd + b * b + 1.0e-12f);
+            float eig0 = ht + rad, eig1 = ht - rad;
+            if (eig0 < 1.0e-12f) eig0 = 1.0e-12f;
+            if (eig1 < 1.0e-12f) eig1 = 1.0e-12f;
+            s0 = sqrtf(eig0);
+            s1 = sqrtf(eig1);
+            r = 0.5f * atan2f(2.0f * b, a - cc);
+        }
+        if (in_frame) {
+            out_pos[2 * k] = nx;
+            out_pos[2 * k + 1] = ny;
+            out_scales[2 * k] = s0;
+            out_scales[2 * k + 1] = s1;
+            out_rots[k] = r;
+            out_ops[k] = ops[g];
+            for (int c = 0; c < f; ++c) out_colors[k * f + c] = colors[g * f + c];
+            ++k;
+        }
+    }
+    return k;
+}
+
+/* warp_positions, oss/gaussian/canvas/warp.py:28-91: motion given at the
+ * output resolution (hl == h, wl == w), scaled by alpha; no compaction. */
+void orc_warp_positions(int64_t n, int h, int w, const float* motion, float alpha, const float* xy, float* out_xy,
+                        uint8_t* in_frame) {
+    orc_field fld = {motion, h, w, h, w, alpha, 1.0f, 1.0f, 1};
+    for (int64_t g = 0; g < n; ++g) {
+        const float x = xy[2 * g], y = xy[2 * g + 1];
+        const float nx = x + orc_grid_sample(&fld, 0, 0, x, y, 0);
+        const float ny = y + orc_grid_sample(&fld, 0, 1, x, y, 0);
+        out_xy[2 * g] = nx;
+        out_xy[2 * g + 1] = ny;
+        in_frame[g] = nx >= 0.0f && nx < (float)w && ny >= 0.0f && ny < (float)h;
+    }
+}

@@ -48,6 +48,16 @@ def golden_case(data: dict, name: str) -> dict:
     return {k[len(pre):]: v for k, v in data.items() if k.startswith(pre)}
 
 
+def assert_close_grad(actual, expected, what=""):
+    """Gradient parity: the image bar plus an absolute slack of 1e-6 of the
+    tensor's largest magnitude.  Gradients are fp32 sums of up to 256 x (list
+    length) terms; elements that cancel to a small value (d_rot is a difference
+    of d_conic terms) keep the summation noise of their large terms."""
+    e = np.asarray(expected, dtype=np.float64)
+    scale = float(np.abs(e).max()) if e.size else 0.0
+    assert_close(actual, expected, atol=ATOL + 1e-6 * scale, rtol=RTOL, what=what)
+
+
 def assert_close(actual, expected, atol=ATOL, rtol=RTOL, what=""):
     a = np.asarray(actual, dtype=np.float64)
     e = np.asarray(expected, dtype=np.float64)

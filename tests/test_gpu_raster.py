@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import oracle as orc
-from conftest import assert_close, golden_case, load_golden
+from conftest import assert_close, assert_close_grad, golden_case, load_golden
 
 pytestmark = pytest.mark.gpu
 
@@ -203,10 +203,10 @@ def test_backward_matches_oracle(cuda_device, mode, n, h, w, f):
     grad = np.random.default_rng(n).standard_normal((f, h, w)).astype(np.float32)
     _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(xy, scale, rot, feat, grad, h, w, mode)
     r_xy, r_scale, r_rot, r_feat, _, _ = orc.render_grads(xy, scale, rot, feat, grad, h, w, MODES[mode])
-    assert_close(d_xy, r_xy, what="d_xy")
-    assert_close(d_scale, r_scale, what="d_scale")
-    assert_close(d_rot, r_rot, what="d_rot")
-    assert_close(d_feat, r_feat, what="d_feat")
+    assert_close_grad(d_xy, r_xy, what="d_xy")
+    assert_close_grad(d_scale, r_scale, what="d_scale")
+    assert_close_grad(d_rot, r_rot, what="d_rot")
+    assert_close_grad(d_feat, r_feat, what="d_feat")
 
 
 def test_backward_with_opacity_matches_oracle(cuda_device):
@@ -219,11 +219,11 @@ def test_backward_with_opacity_matches_oracle(cuda_device):
     assert_close(img, orc.render_forward(xy, conic, rgb, gid, offs, h, w, opacity), what="image")
     r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, gid, offs, grad, h, w, opacity)
     r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
-    assert_close(d_xy, r_xy, what="d_xy")
-    assert_close(d_scale, r_scale, what="d_scale")
-    assert_close(d_rot, r_rot, what="d_rot")
-    assert_close(d_rgb, r_rgb, what="d_rgb")
-    assert_close(d_op, r_op, what="d_opacity")
+    assert_close_grad(d_xy, r_xy, what="d_xy")
+    assert_close_grad(d_scale, r_scale, what="d_scale")
+    assert_close_grad(d_rot, r_rot, what="d_rot")
+    assert_close_grad(d_rgb, r_rgb, what="d_rgb")
+    assert_close_grad(d_op, r_op, what="d_opacity")
 
 
 def test_backward_matches_reference_golden(cuda_device):
@@ -233,10 +233,10 @@ def test_backward_matches_reference_golden(cuda_device):
         h, w = (int(v) for v in c["hw"])
         _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
                                                          "exact")
-        assert_close(d_xy, c["d_xy"], what=f"{name} d_xy")
-        assert_close(d_scale, c["d_scale"], what=f"{name} d_scale")
-        assert_close(d_rot, c["d_rot"], what=f"{name} d_rot")
-        assert_close(d_feat, c["d_feat"], what=f"{name} d_feat")
+        assert_close_grad(d_xy, c["d_xy"], what=f"{name} d_xy")
+        assert_close_grad(d_scale, c["d_scale"], what=f"{name} d_scale")
+        assert_close_grad(d_rot, c["d_rot"], what=f"{name} d_rot")
+        assert_close_grad(d_feat, c["d_feat"], what=f"{name} d_feat")
 
 
 def test_rasterize_backward_lists_dconic(cuda_device):
@@ -252,11 +252,11 @@ def test_rasterize_backward_lists_dconic(cuda_device):
         _, gid, offs, _ = _C.rasterize_forward(xy, scale, rot, feat, h, w, 16, True)
         d_xy, d_conic, d_feat = _C.rasterize_backward(xy, scale, rot, feat, dev(c["conic"]), gid, offs,
                                                       dev(c["grad"]), h, w, 16)
-        assert_close(host(d_conic), c["d_conic"], what=f"{name} d_conic")
+        assert_close_grad(host(d_conic), c["d_conic"], what=f"{name} d_conic")
         d_scale, d_rot = _C.conic_to_scale_rot_grad(scale, rot, d_conic)
-        assert_close(host(d_scale), c["d_scale"], what=f"{name} d_scale")
-        assert_close(host(d_rot), c["d_rot"], what=f"{name} d_rot")
-        assert_close(host(d_feat), c["d_feat"], what=f"{name} d_feat")
+        assert_close_grad(host(d_scale), c["d_scale"], what=f"{name} d_scale")
+        assert_close_grad(host(d_rot), c["d_rot"], what=f"{name} d_rot")
+        assert_close_grad(host(d_feat), c["d_feat"], what=f"{name} d_feat")
 
 
 def test_conic_to_scale_rot_known_answer(cuda_device):
@@ -324,11 +324,11 @@ def test_config2_full_size_parity(cuda_device):
     assert_close(img, orc.render_forward(xy, conic, rgb, g_ref, o_ref, h, w, opacity), what="config2 image")
     r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, g_ref, o_ref, grad, h, w, opacity)
     r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
-    assert_close(d_xy, r_xy, what="config2 d_xy")
-    assert_close(d_scale, r_scale, what="config2 d_scale")
-    assert_close(d_rot, r_rot, what="config2 d_rot")
-    assert_close(d_rgb, r_rgb, what="config2 d_rgb")
-    assert_close(d_op, r_op, what="config2 d_opacity")
+    assert_close_grad(d_xy, r_xy, what="config2 d_xy")
+    assert_close_grad(d_scale, r_scale, what="config2 d_scale")
+    assert_close_grad(d_rot, r_rot, what="config2 d_rot")
+    assert_close_grad(d_rgb, r_rgb, what="config2 d_rgb")
+    assert_close_grad(d_op, r_op, what="config2 d_opacity")
     # size-independent identity: <grad, image> == <d_feat', feat'> (image is linear in feat')
     lhs = float(np.sum(grad.astype(np.float64) * img))
     rhs = float(np.sum(d_op.astype(np.float64) * opacity))

@@ -184,6 +184,36 @@ def overlap_oracle(xy, scale, rot, feat, grad, h, w, overlap, mode=orc.EXACT):
     return image, grads
 
 
+WARP = load_golden("warp_cases.npz")
+
+
+def sigma_of(scales, rots):
+    c, s = np.cos(rots.astype(np.float64)), np.sin(rots.astype(np.float64))
+    r = np.stack([np.stack([c, -s], -1), np.stack([s, c], -1)], -2)
+    d = np.zeros(r.shape)
+    d[..., 0, 0] = scales[:, 0].astype(np.float64) ** 2
+    d[..., 1, 1] = scales[:, 1].astype(np.float64) ** 2
+    return r @ d @ np.swapaxes(r, -1, -2)
+
+
+@pytest.mark.parametrize("name", [str(n) for n in WARP["names"]])
+def test_oracle_warp_matches_reference(name):
+    c = golden_case(WARP, name)
+    pos, sc, rt, op, col, k = orc.warp_canvas(c["positions"], c["scales"], c["rotations"], c["opacities"],
+                                              c["colors"], c["motion"], c["hw"], float(c["recon"]), float(c["alpha"]))
+    assert k == int(c["out_count"])
+    assert_close(pos, c["out_positions"], what="positions")
+    assert_close(sc, c["out_scales"], atol=2e-5, what="scales")
+    # rotations are compared through the covariance they parameterise (angle is
+    # ill-conditioned for near-isotropic Gaussians)
+    assert_close(sigma_of(sc, rt), sigma_of(c["out_scales"], c["out_rotations"]), atol=2e-5, what="covariance")
+    np.testing.assert_array_equal(op, c["out_opacities"])
+    np.testing.assert_array_equal(col, c["out_colors"])
+    new_xy, in_frame = orc.warp_positions(c["positions"], c["pw_motion_hr"], c["hw"], float(c["alpha"]))
+    assert_close(new_xy, c["pw_xy"], what="warp_positions")
+    np.testing.assert_array_equal(in_frame, c["pw_in_frame"])
+
+
 @pytest.mark.parametrize("name", [str(n) for n in OVERLAP["names"]])
 def test_oracle_overlap_matches_reference(name):
     c = golden_case(OVERLAP, name)
