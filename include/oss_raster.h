@@ -199,6 +199,27 @@ OSS_API int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles,
                                void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * oss_tile_bin_counting_sort without any allocation -- no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory (a
+ * per-frame hook inside a host application with a fixed device memory budget,
+ * or an embedding host that owns all device allocations), since the counting
+ * sort needs scratch.  Same inputs, outputs and results as
+ * oss_tile_bin_counting_sort, but the scratch is a fixed 4.5 MiB array in the
+ * library's device image (held by every GPU that loads the library until
+ * process exit).  Limits: n <= 262144 entries and num_tiles <= 65536; larger
+ * calls fail with OSS_ERR_RANGE.  Calls no cudaMalloc/cudaFree.
+ * The first call on each device looks up that device's address of the array
+ * (cudaGetSymbolAddress, with the device current); make that first call before
+ * any stream capture.  All calls share the one array: calls whose GPU work
+ * overlaps (e.g. on two streams at once) race and must be serialised by the
+ * caller.  Each call clears what must start at zero.
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_tile_bin_counting_sort_noalloc(int64_t n, int64_t num_tiles,
+                                               const int32_t* tile_id, const int32_t* gid,
+                                               int32_t* sorted_gid, int32_t* tile_offsets,
+                                               void* stream);
+
+/* ---------------------------------------------------------------------------
  * GS-STVSR canvas warp: replaces oss/sr/v6/canvas_warp.py:177-254 (warp_canvas)
  * with covariance_resampling.py:76-116.  motion_lr[2][h_lr][w_lr] is the LR
  * motion of the canvas (the reference uses the first batch item, :66-77) and

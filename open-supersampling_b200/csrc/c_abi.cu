@@ -4,6 +4,7 @@
 // status codes plus oss_last_error() text.
 #include <climits>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "internal.h"
@@ -417,3 +418,65 @@ int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles, const int32_t* tile
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free tile binning.
+//
+// Some callers cannot call cudaMalloc: a hook that runs inside a host
+// application's per-frame loop (a game or capture plugin with a fixed device
+// memory budget, where the allocator's implicit device synchronisation would
+// stall the frame), or an embedding host that owns every device allocation
+// itself.  They still need tile binning, whose counting sort wants scratch
+// memory (key/value ping-pong buffers, per-tile counts, digit histograms).
+// oss_tile_bin_counting_sort_noalloc takes that scratch from the fixed array
+// below, which is part of the library's device image: every GPU that loads
+// the library holds these 4.5 MiB until the process exits, and nothing is
+// allocated per call.  The caller still passes inputs and outputs.
+namespace {
+
+constexpr int64_t kNoAllocMaxN = 262144;       // entries per call
+constexpr int64_t kNoAllocMaxTiles = 65536;    // tiles per call
+constexpr int64_t kNoAllocScratchBytes = 4718592;  // 4.5 MiB >= scratch need at both maxima (4.38 MiB)
+
+static __device__ __align__(256) unsigned char g_tile_bin_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_tile_bin_scratch on the current device.  In host code
+// the array's name only stands in for the symbol, so its address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    OSS_CUDA_TRY(cudaGetDevice(&dev));
+    OSS_CHECK(dev >= 0 && dev < kNoAllocMaxDevices, OSS_ERR_INVALID, "device index out of range for the no-alloc scratch");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        OSS_CUDA_TRY(cudaGetSymbolAddress(&p, g_tile_bin_scratch));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return OSS_OK;
+}
+
+}  // namespace
+
+extern "C" int oss_tile_bin_counting_sort_noalloc(int64_t n, int64_t num_tiles, const int32_t* tile_id,
+                                                  const int32_t* gid, int32_t* sorted_gid, int32_t* tile_offsets,
+                                                  void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");
+    OSS_CHECK(num_tiles > 0, OSS_ERR_INVALID, "num_tiles must be positive");
+    OSS_CHECK(n <= kNoAllocMaxN, OSS_ERR_RANGE,
+              "N exceeds the no-alloc maximum of 262144 entries; use oss_tile_bin_counting_sort with caller scratch");
+    OSS_CHECK(num_tiles <= kNoAllocMaxTiles, OSS_ERR_RANGE,
+              "num_tiles exceeds the no-alloc maximum of 65536; use oss_tile_bin_counting_sort with caller scratch");
+    OSS_CHECK(oss_tile_bin_counting_sort_scratch_bytes(n, num_tiles) <= kNoAllocScratchBytes, OSS_ERR_RANGE,
+              "scratch need exceeds the no-alloc array");
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != OSS_OK) return rc;
+    return oss_tile_bin_counting_sort(n, num_tiles, tile_id, gid, sorted_gid, tile_offsets, scratch,
+                                      kNoAllocScratchBytes, stream);
+}

@@ -56,6 +56,7 @@ SIGNATURES = {
          _p, _i64, _p],
     ),
     "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
+    "oss_tile_bin_counting_sort_noalloc": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p]),
     "oss_tile_bin_counting_sort_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_tile_bin_counting_sort": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
 }
