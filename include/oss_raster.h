@@ -204,7 +204,7 @@ OSS_API int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles,
  * per-frame hook inside a host application with a fixed device memory budget,
  * or an embedding host that owns all device allocations), since the counting
  * sort needs scratch.  Same inputs, outputs and results as
- * oss_tile_bin_counting_sort, but the scratch is a fixed 4.5 MiB array in the
+ * oss_tile_bin_counting_sort, but the scratch is a fixed 5 MiB array in the
  * library's device image (held by every GPU that loads the library until
  * process exit).  Limits: n <= 262144 entries and num_tiles <= 65536; larger
  * calls fail with OSS_ERR_RANGE.  Calls no cudaMalloc/cudaFree.

@@ -93,11 +93,11 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
     OSS_CHECK(conic != nullptr && aabb != nullptr && pair_count != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
     OSS_CHECK(aligned(aabb, 16), OSS_ERR_INVALID, "aabb must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_count, nullptr,
-                                        as_stream(stream)));
+                                        nullptr, as_stream(stream)));
     return OSS_OK;
 }
 
-int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_scratch_bytes(n < 0 ? 0 : n); }
+int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_fused_scratch_bytes(n < 0 ? 0 : n); }
 
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
                        const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
@@ -114,8 +114,12 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
         OSS_CHECK(aligned(aabb, 16) && aligned(geo, 16), OSS_ERR_INVALID, "aabb and geo must be 16-byte aligned");
     }
     cudaStream_t s = as_stream(stream);
-    OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo, s));
-    OSS_CUDA_TRY(oss::scan_exclusive_i32(pair_offset, pair_offset, g.n, true, total_pairs, scratch, s));
+    long long* block_sums = static_cast<long long*>(scratch);
+    OSS_CHECK(g.n == 0 || (block_sums != nullptr && aligned(block_sums, 8)), OSS_ERR_INVALID,
+              "scratch must be 8-byte aligned");
+    OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
+                                        block_sums, s));
+    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, s));
     return OSS_OK;
 }
 
@@ -430,13 +434,13 @@ int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles, const int32_t* tile
 // memory (key/value ping-pong buffers, per-tile counts, digit histograms).
 // oss_tile_bin_counting_sort_noalloc takes that scratch from the fixed array
 // below, which is part of the library's device image: every GPU that loads
-// the library holds these 4.5 MiB until the process exits, and nothing is
+// the library holds these 5 MiB until the process exits, and nothing is
 // allocated per call.  The caller still passes inputs and outputs.
 namespace {
 
 constexpr int64_t kNoAllocMaxN = 262144;       // entries per call
 constexpr int64_t kNoAllocMaxTiles = 65536;    // tiles per call
-constexpr int64_t kNoAllocScratchBytes = 4718592;  // 4.5 MiB >= scratch need at both maxima (4.38 MiB)
+constexpr int64_t kNoAllocScratchBytes = 5242880;  // 5 MiB >= scratch need at both maxima (4.51 MiB)
 
 static __device__ __align__(256) unsigned char g_tile_bin_scratch[kNoAllocScratchBytes];
 

@@ -29,6 +29,15 @@ int64_t scan_scratch_bytes(int64_t n);
 cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool write_tail,
                                int64_t* total_out, void* scratch, cudaStream_t stream);
 
+// Preprocess tiling shared with the fused pair-count scan: each preprocess CTA
+// handles kPrepTile Gaussians and writes their count sum to block_sums.
+constexpr int kPrepThreads = 256;
+constexpr int kPrepTile = 1024;
+int64_t scan_fused_scratch_bytes(int64_t n);
+// Second half of the fused scan: out[0..n) = exclusive scan, out[n] = total.
+cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t n, const long long* block_sums,
+                                       int64_t* total_out, cudaStream_t stream);
+
 // ---- radix.cu --------------------------------------------------------------
 // Stable LSD sort of (key, val) pairs by key in [0, key_limit].  The sorted vals
 // land in vals_out; keys are not kept.  key scratch is consumed.
@@ -39,7 +48,7 @@ cudaError_t radix_sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, uint32_t 
 // ---- preprocess.cu ---------------------------------------------------------
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count,
-                              float* geo, cudaStream_t stream);
+                              float* geo, long long* block_sums, cudaStream_t stream);
 cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
 cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
                                            const float* d_conic, float* d_scale, float* d_rot,

@@ -15,33 +15,55 @@ __device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, c
     rec[1] = make_float4(k.d * kNegHalfLog2e, k.a, k.b, k.d);
 }
 
-__global__ void __launch_bounds__(kThreads) k_preprocess(int n, int ntx, int nty, int mode,
-                                                          const float2* __restrict__ xy,
-                                                          const float2* __restrict__ scale,
-                                                          const float* __restrict__ rot,
-                                                          float* __restrict__ conic,
-                                                          int4* __restrict__ aabb,
-                                                          int32_t* __restrict__ count,
-                                                          float* __restrict__ geo) {
-    const int g = blockIdx.x * kThreads + threadIdx.x;
-    if (g >= n) return;
-    const float2 c = xy[g];
-    const float2 s = scale[g];
-    const Conic k = conic_from_scale_rot(s.x, s.y, rot[g]);
-    conic[3 * g + 0] = k.a;
-    conic[3 * g + 1] = k.b;
-    conic[3 * g + 2] = k.d;
-    int cnt;
-    int4 box;
-    if (mode == OSS_BIN_FULL) {
-        box = make_int4(0, 0, ntx, nty);
-        cnt = ntx * nty;
-    } else {
-        box = tile_aabb(c.x, c.y, s.x, s.y, k, mode_tau(mode), mode_fallback(mode), ntx, nty, cnt);
+// One CTA per kPrepTile Gaussians (kPrepTile / kPrepThreads per thread, strided
+// for coalescing).  With block_sums non-null the CTA also writes the sum of its
+// pair counts: the reduce half of the gid-major pair-offset scan.
+__global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int nty, int mode,
+                                                              const float2* __restrict__ xy,
+                                                              const float2* __restrict__ scale,
+                                                              const float* __restrict__ rot,
+                                                              float* __restrict__ conic,
+                                                              int4* __restrict__ aabb,
+                                                              int32_t* __restrict__ count,
+                                                              float* __restrict__ geo,
+                                                              long long* __restrict__ block_sums) {
+    long long local = 0;
+#pragma unroll
+    for (int it = 0; it < kPrepTile / kPrepThreads; ++it) {
+        const int g = blockIdx.x * kPrepTile + it * kPrepThreads + threadIdx.x;
+        if (g >= n) break;
+        const float2 c = xy[g];
+        const float2 s = scale[g];
+        const Conic k = conic_from_scale_rot(s.x, s.y, rot[g]);
+        conic[3 * g + 0] = k.a;
+        conic[3 * g + 1] = k.b;
+        conic[3 * g + 2] = k.d;
+        int cnt;
+        int4 box;
+        if (mode == OSS_BIN_FULL) {
+            box = make_int4(0, 0, ntx, nty);
+            cnt = ntx * nty;
+        } else {
+            box = tile_aabb(c.x, c.y, s.x, s.y, k, mode_tau(mode), mode_fallback(mode), ntx, nty, cnt);
+        }
+        aabb[g] = box;
+        count[g] = cnt;
+        local += cnt;
+        if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
     }
-    aabb[g] = box;
-    count[g] = cnt;
-    if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
+    if (block_sums != nullptr) {
+        __shared__ long long s_part[kPrepThreads / 32];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
+        if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = local;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            long long tot = 0;
+#pragma unroll
+            for (int w = 0; w < kPrepThreads / 32; ++w) tot += s_part[w];
+            block_sums[blockIdx.x] = tot;
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads) k_make_geo(int n, const float2* __restrict__ xy,
@@ -75,11 +97,11 @@ __global__ void __launch_bounds__(kThreads) k_conic_to_scale_rot_grad(int n, con
 
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count, float* geo,
-                              cudaStream_t stream) {
+                              long long* block_sums, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    k_preprocess<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(
+    k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPrepThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
-        conic, reinterpret_cast<int4*>(aabb), count, geo);
+        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums);
     return cudaGetLastError();
 }
 

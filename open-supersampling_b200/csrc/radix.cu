@@ -12,9 +12,9 @@ namespace {
 
 constexpr int kRadixThreads = 256;
 constexpr int kRadixWarps = kRadixThreads / 32;
-constexpr int kRadixItems = 8;                                  // rounds of 32 per warp
-constexpr int kWarpSpan = 32 * kRadixItems;                     // 256 items per warp
-constexpr int kSegment = kRadixWarps * kWarpSpan;               // 2048 items per CTA
+constexpr int kRadixItems = 4;                                  // rounds of 32 per warp
+constexpr int kWarpSpan = 32 * kRadixItems;                     // 128 items per warp
+constexpr int kSegment = kRadixWarps * kWarpSpan;               // 1024 items per CTA
 constexpr int kMaxDigits = 256;
 
 __global__ void __launch_bounds__(kRadixThreads) k_radix_upsweep(const uint32_t* __restrict__ keys, int64_t n,

@@ -32,6 +32,63 @@ struct BwdCfg {
     static constexpr int SG = ((FC + 3) / 4) * 4;  // staged grad floats per pixel
 };
 
+__device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, float b, float d) {
+    const bool finite = isfinite(x) && isfinite(y) && isfinite(a) && isfinite(b) && isfinite(d);
+    return finite && a > 0.0f && d > 0.0f && (a * d - b * b) >= 1.0e-3f * (a * d);
+}
+
+// Per-pair sums over one full 16x16 tile: the 16 column offsets dx are hoisted
+// into registers, each row hoists B*dy and D*dy*dy, and the column loop is
+// fully unrolled.  CHECK keeps the reference's q >= 0 test per pixel.
+template <int FC, bool CHECK>
+__device__ __forceinline__ void bwd_full_tile(const float* __restrict__ s_go, float fx0, float fy0, float gx, float gy,
+                                              float A, float B, float D, const float (&fv)[FC], float (&dF)[FC],
+                                              float& Sx, float& Sy, float& Sxx, float& Sxy, float& Syy) {
+    constexpr int SG = BwdCfg<FC>::SG;
+    float dxs[kTile];
+#pragma unroll
+    for (int c = 0; c < kTile; ++c) dxs[c] = (fx0 + static_cast<float>(c)) - gx;
+#pragma unroll 1
+    for (int r = 0; r < kTile; ++r) {
+        const float dy = (fy0 + static_cast<float>(r)) - gy;
+        const float bdy = B * dy;
+        const float ddy2 = (D * dy) * dy;
+        float rowG = 0.0f, rowGx = 0.0f;
+        const float* go_row = s_go + r * kTile * SG;
+#pragma unroll
+        for (int c = 0; c < kTile; ++c) {
+            const float dx = dxs[c];
+            const float q = fmaf(dx, fmaf(A, dx, bdy), ddy2);
+            const float w = CHECK ? (q <= 0.0f ? ex2_ftz(q) : 0.0f) : ex2_ftz(q);
+            const float4* go4 = reinterpret_cast<const float4*>(go_row + c * SG);
+            float go[SG];
+#pragma unroll
+            for (int v = 0; v < SG / 4; ++v) {
+                const float4 t = go4[v];
+                go[4 * v + 0] = t.x;
+                go[4 * v + 1] = t.y;
+                go[4 * v + 2] = t.z;
+                go[4 * v + 3] = t.w;
+            }
+            float dLdw = 0.0f;
+#pragma unroll
+            for (int k = 0; k < FC; ++k) {
+                dLdw = fmaf(go[k], fv[k], dLdw);
+                dF[k] = fmaf(w, go[k], dF[k]);
+            }
+            const float gw = w * dLdw;
+            const float gdx = gw * dx;
+            rowGx += gdx;
+            Sxx = fmaf(gdx, dx, Sxx);
+            rowG += gw;
+        }
+        Sx += rowGx;
+        Sxy = fmaf(rowGx, dy, Sxy);
+        Sy = fmaf(rowG, dy, Sy);
+        Syy = fmaf(rowG * dy, dy, Syy);
+    }
+}
+
 template <int FC, bool DETERMINISTIC>
 __global__ void __launch_bounds__(kBwdThreads) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
@@ -71,18 +128,30 @@ __global__ void __launch_bounds__(kBwdThreads) k_render_bwd(
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const bool full = nrow == kTile && ncol == kTile;
     for (int base = start + warp * 32; base < end; base += kBwdThreads) {
+        // Only a tile's last batch is partial; its idle lanes run on a neutral
+        // entry (zero geometry and features) so the warp stays converged.
         const int j = base + lane;
-        if (j >= end) continue;  // only the last batch of a tile is partial
-        const int g = gid_sorted[j];
-        const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-        const float4 g0 = rec[0];
-        const float4 g1 = rec[1];
-        const float op = opacity != nullptr ? opacity[g] : 1.0f;
+        const bool active = j < end;
+        int g = 0;
+        float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         float fv[FC];
-        const float* fg = feat + static_cast<int64_t>(g) * F;
 #pragma unroll
-        for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+        for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
+        if (active) {
+            g = gid_sorted[j];
+            const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
+            g0 = rec[0];
+            g1 = rec[1];
+            const float op = opacity != nullptr ? opacity[g] : 1.0f;
+            const float* fg = feat + static_cast<int64_t>(g) * F;
+#pragma unroll
+            for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+        }
+        const bool regular = !active || regular_conic_bwd(g0.x, g0.y, g1.y, g1.z, g1.w);
+        const bool warp_regular = __all_sync(0xffffffffu, regular);
 
         float dF[FC];
 #pragma unroll
@@ -90,7 +159,14 @@ __global__ void __launch_bounds__(kBwdThreads) k_render_bwd(
         float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f;
         const float A = g0.z, B = g0.w, D = g1.x;
 
-        for (int r = 0; r < nrow; ++r) {
+        if (full) {
+            const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
+            if (warp_regular) {
+                bwd_full_tile<FC, false>(s_go, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            } else {
+                bwd_full_tile<FC, true>(s_go, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            }
+        } else for (int r = 0; r < nrow; ++r) {
             const float dy = static_cast<float>(ty0 + r) - g0.y;
             float rowG = 0.0f, rowGx = 0.0f;
             const float* go_row = s_go + r * kTile * SG;
@@ -126,6 +202,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_render_bwd(
             Sy = fmaf(rowG, dy, Sy);
             Syy = fmaf(rowG * dy, dy, Syy);
         }
+        if (!active) continue;
         // raw conic (a, b, d) sits in g1.yzw
         const float dxy_x = fmaf(g1.y, Sx, g1.z * Sy);
         const float dxy_y = fmaf(g1.z, Sx, g1.w * Sy);

@@ -2,38 +2,85 @@
 // rasterizer_fwd.cu:151-322, as plain fp32 SIMT -- the weights are dynamic and
 // mostly small, so there is no dense contraction for tensor cores to take).
 //
-// One CTA per 16x16 tile, one thread per pixel.  The tile's list is staged in
-// batches into shared memory (geometry float4 + [D, feat'...] record); every
-// thread then walks the batch in list order with broadcast shared loads:
-//   q' = dx*(A*dx + B*dy) + D*dy*dy   (= -0.5*log2(e) * q)
-//   w  = 2^q'  (MUFU ex2), skipped unless q' <= 0   (the reference's
-//        isfinite(q) && q >= 0 test, rasterizer_fwd.cu:245)
-//   acc[c] += w * feat'[c]
-// Per evaluation: 2 LDS.128 (broadcast), ~9 FP32 ops + F FMAs, 1 MUFU.
+// One CTA per 16x16 tile; each thread owns PX pixels of one column (rows
+// ly, ly + 16/PX, ...).  The tile's list is staged in batches into shared
+// memory as a geometry float4 (x, y, A, B) plus a [D, feat'...] record; every
+// thread walks the batch in list order with broadcast shared loads.  With
+//   q' = dy*(D*dy + B*dx) + A*dx*dx   (= -0.5*log2(e) * q)
+// the per-Gaussian terms B*dx and A*dx*dx are shared by the thread's PX
+// pixels, so a pixel costs 1 FADD + 2 FFMA for q', one MUFU ex2 and F FFMAs.
+//
+// The reference zeroes a weight when q is non-finite or negative
+// (rasterizer_fwd.cu:245).  A batch whose conics are all finite and
+// well-conditioned (det >= 1e-3 * a * d, i.e. axis ratio below ~60) has
+// q' <= 0 at every pixel even after fp32 rounding, so it runs without the
+// per-pixel test; other batches keep it.
 #include "internal.h"
 #include "oss_common.cuh"
 
 namespace oss {
 namespace {
 
-constexpr int kFwdThreads = kTilePixels;  // 256
-
 template <int FC>
 struct FwdCfg {
-    static constexpr int S = ((1 + FC + 3) / 4) * 4;  // floats per [D, feat'] record
+    static constexpr int PX = FC <= 4 ? 4 : (FC <= 16 ? 2 : 1);  // pixels per thread
+    static constexpr int NT = kTilePixels / PX;                   // threads per tile
+    static constexpr int S = ((1 + FC + 3) / 4) * 4;             // floats per [D, feat'] record
     static constexpr int BATCH = S <= 20 ? 256 : (S <= 36 ? 128 : 64);
 };
 
+// Well-conditioned conic test shared by both raster kernels (see file comment).
+__device__ __forceinline__ bool regular_conic(float x, float y, float a, float b, float d) {
+    const bool finite = isfinite(x) && isfinite(y) && isfinite(a) && isfinite(b) && isfinite(d);
+    return finite && a > 0.0f && d > 0.0f && (a * d - b * b) >= 1.0e-3f * (a * d);
+}
+
+template <int FC, bool CHECK>
+__device__ __forceinline__ void fwd_batch(int cnt, const float4* __restrict__ s_geo, const float* __restrict__ s_df,
+                                          float fpx, const float (&fpy)[FwdCfg<FC>::PX],
+                                          float (&acc)[FwdCfg<FC>::PX][FC]) {
+    constexpr int PX = FwdCfg<FC>::PX;
+    constexpr int S = FwdCfg<FC>::S;
+#pragma unroll 2
+    for (int j = 0; j < cnt; ++j) {
+        const float4 g0 = s_geo[j];
+        const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
+        float r[S];
+#pragma unroll
+        for (int v = 0; v < S / 4; ++v) {
+            const float4 t = df4[v];
+            r[4 * v + 0] = t.x;
+            r[4 * v + 1] = t.y;
+            r[4 * v + 2] = t.z;
+            r[4 * v + 3] = t.w;
+        }
+        const float dx = fpx - g0.x;
+        const float bdx = g0.w * dx;
+        const float adx2 = (g0.z * dx) * dx;
+#pragma unroll
+        for (int k = 0; k < PX; ++k) {
+            const float dy = fpy[k] - g0.y;
+            const float q = fmaf(dy, fmaf(r[0], dy, bdx), adx2);
+            const float w = CHECK ? (q <= 0.0f ? ex2_ftz(q) : 0.0f) : ex2_ftz(q);
+#pragma unroll
+            for (int c = 0; c < FC; ++c) acc[k][c] = fmaf(w, r[1 + c], acc[k][c]);
+        }
+    }
+}
+
 template <int FC>
-__global__ void __launch_bounds__(kFwdThreads) k_render_fwd(int F, int H, int W, int ntx,
-                                                             const float* __restrict__ geo,
-                                                             const float* __restrict__ feat,
-                                                             const float* __restrict__ opacity,
-                                                             const int32_t* __restrict__ gid_sorted,
-                                                             const int32_t* __restrict__ tile_offsets,
-                                                             float* __restrict__ image) {
+__global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int W, int ntx,
+                                                                const float* __restrict__ geo,
+                                                                const float* __restrict__ feat,
+                                                                const float* __restrict__ opacity,
+                                                                const int32_t* __restrict__ gid_sorted,
+                                                                const int32_t* __restrict__ tile_offsets,
+                                                                float* __restrict__ image) {
+    constexpr int PX = FwdCfg<FC>::PX;
+    constexpr int NT = FwdCfg<FC>::NT;
     constexpr int S = FwdCfg<FC>::S;
     constexpr int BATCH = FwdCfg<FC>::BATCH;
+    constexpr int ROWSTEP = kTile / PX;
     __shared__ float4 s_geo[BATCH];
     __shared__ __align__(16) float s_df[BATCH * S];
 
@@ -41,58 +88,56 @@ __global__ void __launch_bounds__(kFwdThreads) k_render_fwd(int F, int H, int W,
     const int tx0 = (tile % ntx) * kTile;
     const int ty0 = (tile / ntx) * kTile;
     const int px = tx0 + (threadIdx.x & (kTile - 1));
-    const int py = ty0 + (threadIdx.x >> 4);
+    const int ly = threadIdx.x >> 4;  // 0 .. ROWSTEP-1
     const float fpx = static_cast<float>(px);
-    const float fpy = static_cast<float>(py);
-
-    float acc[FC];
+    float fpy[PX];
 #pragma unroll
-    for (int c = 0; c < FC; ++c) acc[c] = 0.0f;
+    for (int k = 0; k < PX; ++k) fpy[k] = static_cast<float>(ty0 + ly + k * ROWSTEP);
+
+    float acc[PX][FC];
+#pragma unroll
+    for (int k = 0; k < PX; ++k)
+#pragma unroll
+        for (int c = 0; c < FC; ++c) acc[k][c] = 0.0f;
 
     const int start = tile_offsets[tile];
     const int end = tile_offsets[tile + 1];
     for (int b = start; b < end; b += BATCH) {
         const int cnt = min(BATCH, end - b);
         __syncthreads();  // the previous batch has been consumed
-        for (int j = threadIdx.x; j < cnt; j += kFwdThreads) {
+        bool regular = true;
+        for (int j = threadIdx.x; j < cnt; j += NT) {
             const int g = gid_sorted[b + j];
             const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-            s_geo[j] = rec[0];
+            const float4 g0 = rec[0];
+            const float4 g1 = rec[1];
+            s_geo[j] = g0;
+            regular = regular && regular_conic(g0.x, g0.y, g1.y, g1.z, g1.w);
             const float op = opacity != nullptr ? opacity[g] : 1.0f;
             float* df = s_df + j * S;
-            df[0] = rec[1].x;
+            df[0] = g1.x;
             const float* fg = feat + static_cast<int64_t>(g) * F;
 #pragma unroll
             for (int c = 0; c < FC; ++c) df[1 + c] = c < F ? fg[c] * op : 0.0f;
         }
-        __syncthreads();
-#pragma unroll 4
-        for (int j = 0; j < cnt; ++j) {
-            const float4 g0 = s_geo[j];
-            const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
-            float r[S];
-#pragma unroll
-            for (int v = 0; v < S / 4; ++v) {
-                const float4 t = df4[v];
-                r[4 * v + 0] = t.x;
-                r[4 * v + 1] = t.y;
-                r[4 * v + 2] = t.z;
-                r[4 * v + 3] = t.w;
-            }
-            const float dx = fpx - g0.x;
-            const float dy = fpy - g0.y;
-            const float q = q_scaled(g0.z, g0.w, r[0], dx, dy);
-            const float w = q <= 0.0f ? ex2_ftz(q) : 0.0f;
-#pragma unroll
-            for (int c = 0; c < FC; ++c) acc[c] = fmaf(w, r[1 + c], acc[c]);
+        if (__syncthreads_and(regular ? 1 : 0)) {
+            fwd_batch<FC, false>(cnt, s_geo, s_df, fpx, fpy, acc);
+        } else {
+            fwd_batch<FC, true>(cnt, s_geo, s_df, fpx, fpy, acc);
         }
     }
-    if (px < W && py < H) {
+    if (px < W) {
         const int64_t plane = static_cast<int64_t>(H) * W;
-        const int64_t pix = static_cast<int64_t>(py) * W + px;
 #pragma unroll
-        for (int c = 0; c < FC; ++c) {
-            if (c < F) image[c * plane + pix] = acc[c];
+        for (int k = 0; k < PX; ++k) {
+            const int py = ty0 + ly + k * ROWSTEP;
+            if (py < H) {
+                const int64_t pix = static_cast<int64_t>(py) * W + px;
+#pragma unroll
+                for (int c = 0; c < FC; ++c) {
+                    if (c < F) image[c * plane + pix] = acc[k][c];
+                }
+            }
         }
     }
 }
@@ -101,8 +146,8 @@ template <int FC>
 cudaError_t launch_fwd_fc(int f, int h, int w, int ntx, int num_tiles, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
                           cudaStream_t stream) {
-    k_render_fwd<FC><<<static_cast<unsigned>(num_tiles), kFwdThreads, 0, stream>>>(f, h, w, ntx, geo, feat, opacity,
-                                                                                  gid_sorted, tile_offsets, image);
+    k_render_fwd<FC><<<static_cast<unsigned>(num_tiles), FwdCfg<FC>::NT, 0, stream>>>(
+        f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, image);
     return cudaGetLastError();
 }
 

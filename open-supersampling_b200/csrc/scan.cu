@@ -1,7 +1,15 @@
-// Device-wide exclusive scan of int32 counts (reduce -> scan block sums -> apply).
-// Used for the gid-major pair offsets, the per-tile list offsets and the radix
-// digit offsets.  Sums are carried in int64 so an int32 overflow of the total is
-// detected by the caller instead of wrapping silently.
+// Device-wide exclusive scan of int32 counts.
+//
+// Three shapes, picked by size:
+//  * n <= 8192: one CTA of 1024 threads (a single launch);
+//  * up to 2048 blocks of 2048 values: per-block reduce, then an apply kernel in
+//    which every CTA sums the block totals before it (each CTA re-reads at most
+//    2048 int64 from L2) and scans its own block -- two launches, no waiting;
+//  * larger: reduce, scan of the block totals by one CTA, apply.
+// Sums are carried in int64 so an int32 overflow of the total is detected by
+// the caller instead of wrapping silently.  The same apply kernel finishes the
+// gid-major pair-offset scan whose per-block reduce is fused into the
+// preprocess kernel (scan_apply_with_block_sums).
 #include "internal.h"
 #include "oss_common.cuh"
 
@@ -12,6 +20,9 @@ constexpr int kScanThreads = 256;
 constexpr int kScanItems = 8;
 constexpr int kScanTile = kScanThreads * kScanItems;  // 2048 values per block
 constexpr int kScanBlocksThreads = 1024;
+constexpr int kSingleItems = 8;
+constexpr int64_t kSingleMax = kScanBlocksThreads * kSingleItems;  // 8192 (32 KB of static shared memory)
+constexpr int64_t kRedundantMaxBlocks = 2048;
 
 // Exclusive block scan of one int64 per thread; returns the block total in `total`.
 template <int NT>
@@ -81,40 +92,96 @@ __global__ void __launch_bounds__(kScanBlocksThreads) k_scan_blocks(long long* _
     }
 }
 
-__global__ void __launch_bounds__(kScanThreads) k_scan_apply(const int32_t* in, int32_t* out, int64_t n,
-                                                              const long long* __restrict__ block_sums,
-                                                              const long long* __restrict__ total_ll,
-                                                              int write_tail) {
-    __shared__ int32_t s_val[kScanTile];
+// Scan of one block of TILE = NT * ITEMS values.  prefix_mode 0: the block's
+// exclusive offset is block_sums[blockIdx.x] (already scanned); prefix_mode 1:
+// block_sums holds raw per-block totals and the CTA sums those before it.
+// The last block writes the grand total (out[n] if write_tail, total_out).
+template <int NT, int ITEMS>
+__global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* out, int64_t n,
+                                                   const long long* __restrict__ block_sums, int prefix_mode,
+                                                   int64_t nb, int write_tail, int64_t* __restrict__ total_out) {
+    constexpr int TILE = NT * ITEMS;
+    __shared__ int32_t s_val[TILE];
     __shared__ long long s_warp[32];
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
+    __shared__ long long s_prefix;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * TILE;
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        const int64_t i = base + k * kScanThreads + threadIdx.x;
-        s_val[k * kScanThreads + threadIdx.x] = i < n ? in[i] : 0;
+    for (int k = 0; k < ITEMS; ++k) {
+        const int64_t i = base + k * NT + threadIdx.x;
+        s_val[k * NT + threadIdx.x] = i < n ? in[i] : 0;
+    }
+    long long prefix;
+    if (prefix_mode == 1) {
+        long long part = 0;
+        for (int64_t i = threadIdx.x; i < blockIdx.x; i += NT) part += block_sums[i];
+        long long tot;
+        block_exclusive_scan<NT>(part, s_warp, tot);
+        prefix = tot;
+    } else {
+        prefix = block_sums[blockIdx.x];
     }
     __syncthreads();
-    int32_t v[kScanItems];
+    int32_t v[ITEMS];
     long long local = 0;
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        v[k] = s_val[threadIdx.x * kScanItems + k];
+    for (int k = 0; k < ITEMS; ++k) {
+        v[k] = s_val[threadIdx.x * ITEMS + k];
+        local += v[k];
+    }
+    long long block_total;
+    long long run = block_exclusive_scan<NT>(local, s_warp, block_total) + prefix;
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k) {
+        s_val[threadIdx.x * ITEMS + k] = static_cast<int32_t>(run);
+        run += v[k];
+    }
+    if (threadIdx.x == 0) s_prefix = prefix + block_total;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k) {
+        const int64_t i = base + k * NT + threadIdx.x;
+        if (i < n) out[i] = s_val[k * NT + threadIdx.x];
+    }
+    if (blockIdx.x == nb - 1 && threadIdx.x == 0) {
+        const long long total = s_prefix;
+        if (write_tail) out[n] = static_cast<int32_t>(total);
+        if (total_out != nullptr) *total_out = static_cast<int64_t>(total);
+    }
+}
+
+// Whole scan in one CTA for n <= kSingleMax.
+__global__ void __launch_bounds__(kScanBlocksThreads) k_scan_single(const int32_t* in, int32_t* out, int64_t n,
+                                                                     int write_tail, int64_t* __restrict__ total_out) {
+    __shared__ int32_t s_val[kSingleMax];
+    __shared__ long long s_warp[32];
+    for (int k = 0; k < kSingleItems; ++k) {
+        const int64_t i = k * kScanBlocksThreads + threadIdx.x;
+        s_val[i] = i < n ? in[i] : 0;
+    }
+    __syncthreads();
+    int32_t v[kSingleItems];
+    long long local = 0;
+#pragma unroll
+    for (int k = 0; k < kSingleItems; ++k) {
+        v[k] = s_val[threadIdx.x * kSingleItems + k];
         local += v[k];
     }
     long long total;
-    long long run = block_exclusive_scan<kScanThreads>(local, s_warp, total) + block_sums[blockIdx.x];
+    long long run = block_exclusive_scan<kScanBlocksThreads>(local, s_warp, total);
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        s_val[threadIdx.x * kScanItems + k] = static_cast<int32_t>(run);
+    for (int k = 0; k < kSingleItems; ++k) {
+        s_val[threadIdx.x * kSingleItems + k] = static_cast<int32_t>(run);
         run += v[k];
     }
     __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        const int64_t i = base + k * kScanThreads + threadIdx.x;
-        if (i < n) out[i] = s_val[k * kScanThreads + threadIdx.x];
+    for (int k = 0; k < kSingleItems; ++k) {
+        const int64_t i = k * kScanBlocksThreads + threadIdx.x;
+        if (i < n) out[i] = s_val[i];
     }
-    if (write_tail && blockIdx.x == 0 && threadIdx.x == 0) out[n] = static_cast<int32_t>(*total_ll);
+    if (threadIdx.x == 0) {
+        if (write_tail) out[n] = static_cast<int32_t>(total);
+        if (total_out != nullptr) *total_out = static_cast<int64_t>(total);
+    }
 }
 
 __global__ void k_scan_empty(int32_t* out, int write_tail, int64_t* total_out) {
@@ -129,10 +196,14 @@ int64_t scan_scratch_bytes(int64_t n) {
     return arena_bytes(nb + 1, sizeof(long long)) + arena_bytes(1, sizeof(long long));
 }
 
-cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool write_tail,
-                               int64_t* total_out, void* scratch, cudaStream_t stream) {
+cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool write_tail, int64_t* total_out,
+                               void* scratch, cudaStream_t stream) {
     if (n == 0) {
         k_scan_empty<<<1, 1, 0, stream>>>(out, write_tail ? 1 : 0, total_out);
+        return cudaGetLastError();
+    }
+    if (n <= kSingleMax) {
+        k_scan_single<<<1, kScanBlocksThreads, 0, stream>>>(in, out, n, write_tail ? 1 : 0, total_out);
         return cudaGetLastError();
     }
     const int64_t nb = div_up(n, kScanTile);
@@ -140,9 +211,28 @@ cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool 
     long long* block_sums = arena.take<long long>(nb + 1);
     long long* total_ll = arena.take<long long>(1);
     k_scan_reduce<<<static_cast<unsigned>(nb), kScanThreads, 0, stream>>>(in, n, block_sums);
-    k_scan_blocks<<<1, kScanBlocksThreads, 0, stream>>>(block_sums, nb, total_ll, total_out);
-    k_scan_apply<<<static_cast<unsigned>(nb), kScanThreads, 0, stream>>>(in, out, n, block_sums, total_ll,
-                                                                         write_tail ? 1 : 0);
+    if (nb <= kRedundantMaxBlocks) {
+        k_scan_apply<kScanThreads, kScanItems><<<static_cast<unsigned>(nb), kScanThreads, 0, stream>>>(
+            in, out, n, block_sums, 1, nb, write_tail ? 1 : 0, total_out);
+        return cudaGetLastError();
+    }
+    k_scan_blocks<<<1, kScanBlocksThreads, 0, stream>>>(block_sums, nb, total_ll, nullptr);
+    k_scan_apply<kScanThreads, kScanItems><<<static_cast<unsigned>(nb), kScanThreads, 0, stream>>>(
+        in, out, n, block_sums, 0, nb, write_tail ? 1 : 0, total_out);
+    return cudaGetLastError();
+}
+
+int64_t scan_fused_scratch_bytes(int64_t n) { return arena_bytes(div_up(n, kPrepTile) + 1, sizeof(long long)); }
+
+cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t n, const long long* block_sums,
+                                       int64_t* total_out, cudaStream_t stream) {
+    if (n == 0) {
+        k_scan_empty<<<1, 1, 0, stream>>>(out, 1, total_out);
+        return cudaGetLastError();
+    }
+    const int64_t nb = div_up(n, kPrepTile);
+    k_scan_apply<kPrepThreads, kPrepTile / kPrepThreads><<<static_cast<unsigned>(nb), kPrepThreads, 0, stream>>>(
+        in, out, n, block_sums, 1, nb, 1, total_out);
     return cudaGetLastError();
 }
 

@@ -38,7 +38,7 @@ def _call_noalloc(tile_id: torch.Tensor, gid: torch.Tensor, num_tiles: int):
 def test_noalloc_matches_allocating_entry_point(cuda_device):
     from oss_cuda import tile_bin_counting_sort
 
-    for seed, n, num_tiles in ((11, MAX_N, 8160), (12, 5000, 37)):
+    for seed, n, num_tiles in ((11, MAX_N, MAX_TILES), (12, 5000, 37)):
         rng = np.random.default_rng(seed)
         tile_id = torch.from_numpy(rng.integers(-2, num_tiles + 2, size=n).astype(np.int32)).to(cuda_device)
         gid = torch.from_numpy(rng.integers(0, 1 << 30, size=n).astype(np.int32)).to(cuda_device)
