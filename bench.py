@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="config2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5"], default="config2")
     ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -149,23 +149,32 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- device pipeline
 
-class Pipeline:
-    """The hot path over the C ABI, with a CUDA event between each stage."""
+def scan_launches(n: int) -> int:
+    """Kernels one device scan of n values launches (csrc/scan.cu size classes)."""
+    if n <= 8192:
+        return 1
+    return 2 if -(-n // 2048) <= 2048 else 3
 
-    def __init__(self, inp, h, w, mode, device):
+
+class Pipeline:
+    """The hot path over the C ABI, with a CUDA event between each stage.
+
+    Buffers are sized for up to `capacity_n` Gaussians and grow for pairs; each
+    step takes its inputs (xy, scale, rot, opacity, rgb[, grad]) as device tensors.
+    """
+
+    def __init__(self, capacity_n, h, w, mode, device):
         from oss_cuda import _lib
 
         self.lib = _lib.lib()
         self._lib = _lib
         self.h, self.w, self.mode = h, w, mode
-        self.n = inp["xy"].shape[0]
-        self.d = {k: torch.from_numpy(v).to(device) for k, v in inp.items()}
         self.ntx = (w + 15) // 16
         self.nty = (h + 15) // 16
         self.tiles = self.ntx * self.nty
         f32 = dict(device=device, dtype=torch.float32)
         i32 = dict(device=device, dtype=torch.int32)
-        n = self.n
+        n = capacity_n
         self.conic = torch.empty((n, 3), **f32)
         self.aabb = torch.empty((n, 4), **i32)
         self.pair_offset = torch.empty((n + 1,), **i32)
@@ -181,6 +190,8 @@ class Pipeline:
         self.capacity = 0
         self.events = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
         self.device = device
+        self.n = n
+        self.pairs = 0
 
     def _ensure(self, pairs):
         if pairs > self.capacity:
@@ -191,10 +202,11 @@ class Pipeline:
                      self.lib.oss_render_backward_scratch_bytes(self.capacity, 3))
             self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
 
-    def step(self):
-        lib, chk, d, ev = self.lib, self._lib.check, self.d, self.events
+    def step(self, d, backward=True):
+        lib, chk, ev = self.lib, self._lib.check, self.events
         s = torch.cuda.current_stream().cuda_stream
-        n, h, w = self.n, self.h, self.w
+        n, h, w = int(d["xy"].shape[0]), self.h, self.w
+        self.n_step = n
         ev[0].record()
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
                                    d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
@@ -213,6 +225,8 @@ class Pipeline:
                                    self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.image.data_ptr(),
                                    s), "forward")
         ev[4].record()
+        if not backward:
+            return
         chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
                                           pairs, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
@@ -233,14 +247,19 @@ class Pipeline:
                 "backward_pairs": ev[4].elapsed_time(ev[5]), "reduce": ev[5].elapsed_time(ev[6]),
                 "fwd_path": ev[0].elapsed_time(ev[4]), "total": ev[0].elapsed_time(ev[6])}
 
-    def launches_per_step(self):
+    def launches_per_step(self, backward=True):
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
-        scan = 3
-        bits = max(0, int(self.tiles - 1).bit_length())
+        bits = max(0, int(self.tiles - 1).bit_length())  # radix.cu make_plan
         passes = (bits + 7) // 8
-        prepare = 1 + scan
-        binning = 1 + scan + passes * (1 + scan + 1)
-        return prepare + binning + 1 + 1 + 1
+        nseg = -(-self.pairs // 1024)
+        radix, shift = 0, 0
+        for i in range(passes):
+            b = -(-(bits - shift) // (passes - i))
+            shift += b
+            radix += 1 + scan_launches((1 << b) * nseg) + 1
+        prepare = 2
+        binning = 1 + scan_launches(self.tiles) + radix
+        return prepare + binning + 1 + (2 if backward else 0)
 
     def evaluations(self):
         """Pixel-Gaussian evaluations: sum over tiles of valid pixels x list length."""
@@ -327,10 +346,11 @@ def run_ours(args, rank, world, local):
     device = torch.device("cuda", torch.cuda.current_device())
     inp = make_inputs(h, w, n, lsm, lss, seed=1234 + rank)
     mode = _lib.BINNING_MODES[args.binning]
-    pipe = Pipeline(inp, h, w, mode, device)
+    pipe = Pipeline(n, h, w, mode, device)
+    dev_inp = {k: torch.from_numpy(v).to(device) for k, v in inp.items()}
     flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
     for _ in range(max(3, args.warmup)):
-        pipe.step()
+        pipe.step(dev_inp)
         flush.zero_()
     torch.cuda.synchronize()
 
@@ -346,7 +366,7 @@ def run_ours(args, rank, world, local):
         wall0 = time.perf_counter()
         for _ in range(K):
             flush.zero_()
-            pipe.step()
+            pipe.step(dev_inp)
             torch.cuda.synchronize()  # per-step events are read below; keeps host and device in step
             for k, v in pipe.stage_ms().items():
                 stages[k] += v
@@ -458,12 +478,187 @@ def run_ours(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- configs 3-5
+
+def smooth_motion(h, w, seed, max_mag=16.0):
+    """Sum of 8 random sinusoids per channel, frequencies <= 1/64 px^-1, |m| <= max_mag."""
+    rng = np.random.default_rng(seed)
+    yy, xx = np.meshgrid(np.arange(h, dtype=np.float64), np.arange(w, dtype=np.float64), indexing="ij")
+    out = np.zeros((2, h, w))
+    for ch in range(2):
+        amp = rng.random(8)
+        fx = (rng.random(8) - 0.5) * (2.0 / 64.0)
+        fy = (rng.random(8) - 0.5) * (2.0 / 64.0)
+        ph = rng.random(8) * 2 * math.pi
+        out[ch] = sum(amp[k] * np.sin(2 * math.pi * (fx[k] * xx + fy[k] * yy) + ph[k]) for k in range(8))
+        out[ch] *= max_mag / amp.sum()
+    return out.astype(np.float32)
+
+
+def rank_frames(total, rank, world):
+    from oss_b200.distributed import frame_shard
+
+    return list(frame_shard(total, rank, world))
+
+
+def timed(step, K, W, device, world):
+    """W warm-up steps, then K steps each bracketed by CUDA events on the current
+    stream with a 256 MiB L2 flush between them; returns (ms per step, max over
+    ranks), clock summary."""
+    flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
+    for _ in range(max(3, W)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    with ClockSampler(device.index) as clocks:
+        for _ in range(K):
+            flush.zero_()
+            e0.record()
+            step()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+    ms = torch.tensor([total / K], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms[0]), clocks.summary()
+
+
+def base_line(args, world, value, ms, workload, scaling, clocks, **extra):
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": {"workload": workload, "l2": "256 MiB flush between steps (outside the step events)"},
+            "clocks": clocks}
+    line.update(extra)
+    return line
+
+
+def run_config3(args, rank, world):
+    """Config 3: canvas warp + render at alpha in {1.0, 0.5}; 1080p, N=200k, LR motion
+    540x960 (smooth random flow, |m| <= 16 px), batch 8 frames split across ranks."""
+    from oss_b200 import CanvasState, warp_canvas
+    from oss_cuda import _lib
+
+    h, w, n, lsm, lss = CONFIGS["config2"]
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = {k: torch.from_numpy(v).to(device) for k, v in make_inputs(h, w, n, lsm, lss, seed=1234).items()}
+    canvas = CanvasState(inp["xy"], inp["scale"], inp["rot"], inp["opacity"], inp["rgb"], n)
+    frames = rank_frames(8, rank, world)
+    motions = [torch.from_numpy(smooth_motion(540, 960, 300 + f)[None]).to(device) for f in frames]
+    pipe = Pipeline(n, h, w, _lib.BINNING_MODES[args.binning], device)
+
+    def step_at(alpha):
+        def step():
+            with torch.no_grad():
+                for m in motions:
+                    c = warp_canvas(canvas, m, (h, w), 0.5, alpha)
+                    pipe.step({"xy": c.positions, "scale": c.scales, "rot": c.rotations, "opacity": c.opacities,
+                               "rgb": c.colors}, backward=False)
+        return step
+
+    ms1, clocks = timed(step_at(1.0), args.steps, args.warmup, device, world)
+    ms05, _ = timed(step_at(0.5), args.steps, args.warmup, device, world)
+    value = 8 * h * w / (ms1 * 1e-3) / 1e6
+    return base_line(args, world, value, ms1, f"config3: warp (GS-STVSR, LR 540x960 -> {w}x{h}) + forward render, "
+                     f"N={n}, alpha=1.0, batch 8 frames split over {world} rank(s), {args.binning} lists",
+                     "strong", clocks, alpha_0p5={"value": 8 * h * w / (ms05 * 1e-3) / 1e6, "ms_per_step": ms05},
+                     ms_per_frame=ms1 / max(1, len(frames)))
+
+
+def run_config4(args, rank, world):
+    """Config 4: 3840x2160, N=1M (log-scale ln 2.5, sd 0.5), 4-phase feathered overlap o=4,
+    per-frame integer spawner offset U{0..15}^2, fwd+bwd, batch 4 frames split across ranks."""
+    from oss_b200 import render_overlapped
+
+    h, w, n = 2160, 3840, 1_000_000
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = {k: torch.from_numpy(v).to(device) for k, v in
+           make_inputs(h, w, n, math.log(2.5), 0.5, seed=4321).items()}
+    frames = rank_frames(4, rank, world)
+    rng = np.random.default_rng(77)
+    offsets = rng.integers(0, 16, size=(4, 2)).astype(np.float32)
+
+    def step():
+        for f in frames:
+            xy = (inp["xy"] + torch.from_numpy(offsets[f]).to(device)).requires_grad_(True)
+            leaves = [xy] + [inp[k].detach().requires_grad_(True) for k in ("scale", "rot", "rgb", "opacity")]
+            img = render_overlapped(leaves[0], leaves[1], leaves[2], leaves[3], h, w, 4, binning=args.binning,
+                                    opacity=leaves[4])
+            torch.autograd.grad(img, leaves, inp["grad"])
+
+    if frames:
+        ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    else:
+        ms, clocks = timed(lambda: None, args.steps, args.warmup, device, world)
+    value = 4 * h * w / (ms * 1e-3) / 1e6
+    return base_line(args, world, value, ms, f"config4: {w}x{h}, N={n}, overlap 4 (4 phase renders), spawner "
+                     f"offset per frame, fwd+bwd, batch 4 frames split over {world} rank(s), {args.binning} lists",
+                     "strong", clocks, ms_per_frame=ms / max(1, len(frames)))
+
+
+def run_config5(args, rank, world):
+    """Config 5: 64 frames at 1080p split across ranks; each frame renders its own 200k
+    canvas plus a shared 50k canvas (fwd+bwd); the shared canvas's per-Gaussian
+    gradients (xy 2, scale 2, rot 1, opacity 1, rgb 3) are summed over the rank's
+    frames and all-reduced over NCCL once per step."""
+    from oss_cuda import _lib
+
+    h, w, lsm, lss = 1080, 1920, math.log(2.0), 0.3
+    n_own, n_shared = 200_000, 50_000
+    device = torch.device("cuda", torch.cuda.current_device())
+    shared = make_inputs(h, w, n_shared, lsm, lss, seed=555)
+    frames = rank_frames(64, rank, world)
+    per_frame = []
+    for f in frames:
+        own = make_inputs(h, w, n_own, lsm, lss, seed=10_000 + f)
+        per_frame.append({k: torch.from_numpy(np.concatenate([own[k], shared[k]]) if k != "grad" else own[k]).to(device)
+                          for k in own})
+    pipe = Pipeline(n_own + n_shared, h, w, _lib.BINNING_MODES[args.binning], device)
+    from oss_b200.distributed import pack_shared_grads, reduce_shared_grads
+
+    d_shared = torch.zeros((n_shared, 9), device=device, dtype=torch.float32)
+    ar_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    sl = slice(n_own, n_own + n_shared)
+
+    def step():
+        d_shared.zero_()
+        for d in per_frame:
+            pipe.step(d)
+            d_shared.add_(pack_shared_grads(pipe.grads, sl))
+        ar_events[0].record()
+        reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
+        ar_events[1].record()
+
+    ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    allreduce = None
+    if world > 1:
+        torch.cuda.synchronize()
+        allreduce = ar_events[0].elapsed_time(ar_events[1])
+    value = 64 * h * w / (ms * 1e-3) / 1e6
+    return base_line(args, world, value, ms, f"config5: 64 frames {w}x{h} split over {world} rank(s), each own "
+                     f"N={n_own} + shared N={n_shared}, fwd+bwd, NCCL all-reduce of the shared canvas gradients "
+                     f"({n_shared}x9 fp32), {args.binning} lists", "strong", clocks,
+                     allreduce_ms_last_step=allreduce, frames_per_rank=len(frames))
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.config in ("config3", "config4", "config5"):
+            line = {"config3": run_config3, "config4": run_config4, "config5": run_config5}[args.config](
+                args, rank, world)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
         else:
             run_ours(args, rank, world, local)
     finally:

@@ -1,0 +1,195 @@
+"""v6 active-mask-aware feature rasterizer on the B200 kernels.
+
+Drop-in for oss/sr/v6/rasterizer.py:17-345 (``V6Rasterizer``): the same
+constructor arguments, ``forward(canvas, active_mask, output_hw,
+return_weight_sum)`` contract, sanitisation rules, weight-sum channel, the
+4-phase feathered overlap render and the batch expand.  Every render goes
+through ``oss_cuda.rasterize_gaussians`` (liboss_b200.so); the masking,
+sanitising and feather compositing are elementwise PyTorch glue around it.
+
+``spawn_offset`` shifts all means by a per-frame integer
+offset before rendering, the effect of the spawner offset of
+oss/sr/v6/model.py:795-820 on the rasterized canvas.
+"""
+from __future__ import annotations
+
+import math
+from typing import Tuple
+
+import torch
+import torch.nn as nn
+
+from oss_cuda import rasterize_gaussians
+
+TILE_SIZE = 16
+_MIN_PIXEL_SCALE = 1.0e-3
+
+
+def render(xy, scale, rot, feat, h, w, binning=None, opacity=None):
+    """One render through the native op, with the scale floor the reference's
+    oss_cuda backend applies before calling it (rasterizer.py:186-195)."""
+    return rasterize_gaussians(xy, scale.clamp_min(_MIN_PIXEL_SCALE), rot, feat, h, w, TILE_SIZE, True,
+                               binning=binning, opacity=opacity)
+
+
+def cosine_ramp(t: torch.Tensor) -> torch.Tensor:
+    return 0.5 - 0.5 * torch.cos(t * math.pi)
+
+
+def phase_feather_mask(h: int, w: int, origin: Tuple[int, int], overlap: int, device) -> torch.Tensor:
+    """Weight of one phase-shifted render: a cosine ramp over the distance to the
+    nearest tile edge of that phase's grid (rasterizer.py:212-234)."""
+    if overlap <= 0:
+        return torch.ones((1, h, w), device=device, dtype=torch.float32)
+    tile = float(TILE_SIZE)
+    oy, ox = float(origin[0]), float(origin[1])
+    py = torch.remainder(torch.arange(h, device=device, dtype=torch.float32) + 0.5 - oy, tile)
+    px = torch.remainder(torch.arange(w, device=device, dtype=torch.float32) + 0.5 - ox, tile)
+    wy = cosine_ramp((torch.minimum(py, tile - py) / float(overlap)).clamp(0.0, 1.0))
+    wx = cosine_ramp((torch.minimum(px, tile - px) / float(overlap)).clamp(0.0, 1.0))
+    return (wy.view(1, h, 1) * wx.view(1, 1, w)).to(torch.float32)
+
+
+def render_overlapped(xy, scale, rot, feat, h, w, overlap, binning=None, opacity=None):
+    """Feathered overlapping-tile render (rasterizer.py:159-210): four renders whose
+    16-px tile grids are shifted by (0|-o, 0|-o), each cropped back to (h, w) and
+    blended by its feather mask, then normalised by the mask sum."""
+    device = xy.device
+    f = int(feat.shape[1])
+    accum = torch.zeros((f, h, w), device=device, dtype=torch.float32)
+    wsum = torch.zeros((1, h, w), device=device, dtype=torch.float32)
+    for oy, ox in ((0, 0), (-overlap, 0), (0, -overlap), (-overlap, -overlap)):
+        crop_h = -(-(h - min(oy, 0)) // TILE_SIZE) * TILE_SIZE
+        crop_w = -(-(w - min(ox, 0)) // TILE_SIZE) * TILE_SIZE
+        shift = torch.tensor([float(ox), float(oy)], device=device, dtype=xy.dtype)
+        img = render(xy - shift, scale, rot, feat, crop_h, crop_w, binning, opacity)
+        ys, xs = -min(oy, 0), -min(ox, 0)
+        img = img[:, ys:ys + h, xs:xs + w]
+        mask = phase_feather_mask(h, w, (oy, ox), overlap, device)
+        accum = accum + img * mask
+        wsum = wsum + mask
+    return accum / wsum.clamp_min(1.0e-6)
+
+
+class V6Rasterizer(nn.Module):
+    """Renders the active subset of a v6 canvas to an HR feature image.
+
+    Same arguments as the reference class plus ``binning`` (list mode of the
+    native op; the default reproduces the reference's full-tail sum).
+    """
+
+    def __init__(self, token_dim: int, latent_rank: int = 64, tile_size: int = TILE_SIZE, overlap: int = 0,
+                 binning: str | None = None) -> None:
+        super().__init__()
+        if token_dim <= 0:
+            raise ValueError(f"token_dim must be positive; got {token_dim}")
+        if latent_rank <= 0:
+            raise ValueError(f"latent_rank must be positive; got {latent_rank}")
+        if tile_size != TILE_SIZE:
+            raise ValueError(f"tile_size must match the underlying renderer ({TILE_SIZE}); got {tile_size}")
+        if overlap < 0:
+            raise ValueError(f"overlap must be >= 0; got {overlap}")
+        self.token_dim = int(token_dim)
+        self.latent_rank = int(latent_rank)
+        self.feature_dim = self.latent_rank if self.latent_rank < 64 else self.token_dim
+        self.tile_size = int(tile_size)
+        self.overlap = int(overlap)
+        self.binning = binning
+
+    def forward(self, canvas, active_mask: torch.Tensor, output_hw: Tuple[int, int],
+                return_weight_sum: bool | None = None, spawn_offset: torch.Tensor | None = None):
+        if return_weight_sum is None:
+            return_weight_sum = self.latent_rank < 64
+        h, w = int(output_hw[0]), int(output_hw[1])
+        if h <= 0 or w <= 0:
+            raise ValueError(f"output_hw must be positive; got {output_hw}")
+        batch, mask = self._normalize_active_mask(canvas, active_mask)
+        device, out_dtype = canvas.colors.device, canvas.colors.dtype
+
+        def zeros():
+            feats = torch.zeros((batch, self.feature_dim, h, w), device=device, dtype=out_dtype)
+            if return_weight_sum:
+                return feats, torch.zeros((batch, 1, h, w), device=device, dtype=out_dtype)
+            return feats
+
+        n_live = max(0, min(int(canvas.count), int(canvas.positions.shape[0])))
+        if n_live == 0 or not bool(mask[:n_live].any().item()):
+            return zeros()
+        live = mask[:n_live].to(device=device, dtype=torch.bool)
+        colors = self._token_features(canvas.colors[:n_live])
+        feat_dtype = colors.dtype
+        pos = canvas.positions[:n_live][live].to(torch.float32)
+        scl = canvas.scales[:n_live][live].to(torch.float32)
+        rot = canvas.rotations[:n_live][live].to(torch.float32)
+        feat = colors[live].to(torch.float32)
+        pos, scl, rot, feat = self._sanitize(pos, scl, rot, feat, (h, w))
+        if pos.shape[0] == 0:
+            return zeros()
+        if spawn_offset is not None:
+            pos = pos + spawn_offset.to(device=device, dtype=torch.float32).view(1, 2)
+        if return_weight_sum:
+            feat = torch.cat([feat, torch.ones((feat.shape[0], 1), device=device, dtype=feat.dtype)], dim=-1)
+        if self.overlap > 0:
+            img = render_overlapped(pos.contiguous(), scl.contiguous(), rot.contiguous(), feat.contiguous(), h, w,
+                                    self.overlap, self.binning)
+        else:
+            img = render(pos.contiguous(), scl.contiguous(), rot.contiguous(), feat.contiguous(), h, w,
+                         self.binning)
+        img = img.to(dtype=feat_dtype)
+        feats = img[: self.feature_dim].unsqueeze(0).expand(batch, -1, -1, -1)
+        if return_weight_sum:
+            return feats, img[self.feature_dim: self.feature_dim + 1].unsqueeze(0).expand(batch, -1, -1, -1)
+        return feats
+
+    @staticmethod
+    def _sanitize(pos, scl, rot, feat, hw):
+        """Drop non-finite entries and those whose 3*max|scale| disc misses the frame;
+        clamp |scale| to [1e-3, max(h, w)], positions into the frame, wrap rotations
+        (rasterizer.py:244-291)."""
+        h, w = hw
+        finite = (torch.isfinite(pos).all(-1) & torch.isfinite(scl).all(-1) & torch.isfinite(rot)
+                  & torch.isfinite(feat).all(-1))
+        scl = scl.abs().clamp(min=_MIN_PIXEL_SCALE, max=float(max(h, w)))
+        r = 3.0 * scl.amax(dim=-1)
+        inside = ((pos[:, 0] + r >= 0.0) & (pos[:, 0] - r < float(w)) & (pos[:, 1] + r >= 0.0)
+                  & (pos[:, 1] - r < float(h)))
+        keep = finite & inside
+        if not bool(keep.any().item()):
+            return pos[:0], scl[:0], rot[:0], feat[:0]
+        pos, scl, rot, feat = pos[keep], scl[keep], rot[keep], feat[keep]
+        hi = pos.new_tensor([max(float(w) - 1.0e-4, 0.0), max(float(h) - 1.0e-4, 0.0)])
+        pos = torch.minimum(pos.clamp_min(0.0), hi)
+        rot = torch.atan2(torch.sin(rot), torch.cos(rot))
+        return pos, scl, rot, feat
+
+    @staticmethod
+    def _normalize_active_mask(canvas, active_mask: torch.Tensor):
+        n = canvas.positions.shape[0]
+        if active_mask.device != canvas.positions.device:
+            active_mask = active_mask.to(device=canvas.positions.device)
+        if active_mask.ndim == 1:
+            if active_mask.shape[0] != n:
+                raise ValueError(f"active_mask must have length {n}; got {active_mask.shape[0]}")
+            return 1, active_mask.to(dtype=torch.bool)
+        if active_mask.ndim == 2:
+            b, m = active_mask.shape
+            if m != n:
+                raise ValueError(f"active_mask must have trailing length {n}; got {m}")
+            mask = active_mask.to(dtype=torch.bool)
+            if b == 0:
+                raise ValueError("active_mask batch dimension must be positive")
+            if b > 1 and not torch.equal(mask, mask[:1].expand_as(mask)):
+                raise ValueError("batched active_mask rows must be identical because v6 renders the shared "
+                                 "per-rank canvas once and expands it across B")
+            return int(b), mask[0]
+        raise ValueError(f"active_mask must be (N,) or (B, N); got {tuple(active_mask.shape)}")
+
+    def _token_features(self, colors: torch.Tensor) -> torch.Tensor:
+        if colors.ndim != 2:
+            raise ValueError(f"canvas.colors must be (N, F); got {tuple(colors.shape)}")
+        f = self.feature_dim
+        if colors.shape[-1] == f:
+            return colors
+        if colors.shape[-1] > f:
+            return colors[..., :f]
+        return torch.nn.functional.pad(colors, (0, f - colors.shape[-1]))

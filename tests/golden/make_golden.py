@@ -218,6 +218,57 @@ def overlap_cases():
     np.savez_compressed(OUT / "overlap_cases.npz", **out)
 
 
+def v6_cases():
+    """V6Rasterizer.forward (oss/sr/v6/rasterizer.py:56-157): active mask, live count,
+    sanitisation (non-finite drop, |scale| clamp, frame-overlap cull, position clamp,
+    rotation wrap), weight-sum channel, optional overlap, batch expand; plus gradients
+    of a weighted sum of the outputs w.r.t. the canvas tensors."""
+    from oss.sr.v6.model import CanvasState
+    from oss.sr.v6.rasterizer import V6Rasterizer
+
+    cases = [("a", 40, 48, 64, 8, 4, 0, True), ("b", 30, 40, 56, 3, 64, 4, None), ("c", 25, 33, 47, 5, 64, 0, False)]
+    out = {}
+    for i, (name, n, h, w, f, rank, ov, rws) in enumerate(cases):
+        g = torch.Generator().manual_seed(SEED + 500 + i)
+        pos = torch.rand(n, 2, generator=g) * torch.tensor([w * 1.3, h * 1.3]) - torch.tensor([w * 0.15, h * 0.15])
+        scales = torch.rand(n, 2, generator=g) * 4.0 + 0.3
+        scales[::7, 0] *= -1.0                      # negative scales are |.|-clamped
+        scales[3, 1] = 1e-5                          # below the 1e-3 floor
+        rots = torch.rand(n, generator=g) * 12.0 - 6.0
+        cols = torch.randn(n, f, generator=g)
+        ops = torch.rand(n, generator=g)
+        pos[5, 0] = float("nan")                     # non-finite entries are dropped
+        cols[6, 0] = float("inf")
+        pos[8] = torch.tensor([-500.0, 10.0])        # far off-screen: culled
+        count = n - 3                                # the last 3 entries are not live
+        mask = torch.rand(n, generator=g) > 0.2
+        leaves = [t.clone().requires_grad_(True) for t in (pos, scales, rots, cols)]
+        canvas = CanvasState(positions=leaves[0], scales=leaves[1], rotations=leaves[2], opacities=ops,
+                             colors=leaves[3], count=count)
+        r = V6Rasterizer(token_dim=f, latent_rank=rank, overlap=ov)
+        r.renderer.force_backend = "reference"
+        res = r(canvas, mask, output_hw=(h, w), return_weight_sum=rws)
+        feats, wsum = (res if isinstance(res, tuple) else (res, None))
+        wf = torch.randn(feats.shape[1:], generator=g)
+        loss = (feats[0] * wf).sum()
+        if wsum is not None:
+            ww = torch.randn(wsum.shape[1:], generator=g)
+            loss = loss + (wsum[0] * ww).sum()
+            out[f"{name}_ww"] = ww.numpy()
+            out[f"{name}_wsum"] = wsum.detach().numpy()
+        loss.backward()
+        out[f"{name}_wf"] = wf.numpy()
+        out[f"{name}_feats"] = feats.detach().numpy()
+        for k, t in zip(("positions", "scales", "rotations", "colors"), leaves):
+            out[f"{name}_{k}"] = t.detach().numpy()
+            out[f"{name}_d_{k}"] = t.grad.numpy()
+        out[f"{name}_opacities"] = ops.numpy()
+        out[f"{name}_mask"] = mask.numpy()
+        out[f"{name}_meta"] = np.array([count, h, w, f, rank, ov, -1 if rws is None else int(rws)], np.int64)
+    out["names"] = np.array([c[0] for c in cases])
+    np.savez_compressed(OUT / "v6_cases.npz", **out)
+
+
 def main():
     root = _ref_root()
     sys.path.insert(0, str(root))
@@ -226,6 +277,7 @@ def main():
     tight_lists()
     warp_cases()
     overlap_cases()
+    v6_cases()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
