@@ -279,8 +279,10 @@ def cpu_sample(inp, h, w, mode_name, budget_s, threads=None):
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
 
-    if threads:
-        orc.set_num_threads(threads)
+    # all host threads this process may use (torchrun sets OMP_NUM_THREADS=1 per rank)
+    if not threads:
+        threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    orc.set_num_threads(threads)
     mode = orc.MODES[mode_name]
     ntx, nty, t_all = orc.tiles(h, w)
     feat = inp["rgb"]
