@@ -199,8 +199,9 @@ class Pipeline:
             self.capacity = int(pairs * 1.1) + 1024
             self.gid_sorted = torch.empty((self.capacity,), device=dev, dtype=torch.int32)
             nb = max(self.lib.oss_bin_pairs_scratch_bytes(self.n, self.capacity, self.tiles),
-                     self.lib.oss_render_backward_scratch_bytes(self.capacity, 3))
+                     self.lib.oss_render_backward_scratch_bytes(self.capacity, 3, self.tiles))
             self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
+            self.pg_bytes = ((self.capacity * self.lib.oss_pair_grad_stride(3) * 4 + 255) // 256) * 256
 
     def step(self, d, backward=True):
         lib, chk, ev = self.lib, self._lib.check, self.events
@@ -230,7 +231,9 @@ class Pipeline:
         chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
                                           pairs, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
-                                          d["grad"].data_ptr(), self.scratch.data_ptr(), s), "backward_pairs")
+                                          d["grad"].data_ptr(), self.scratch.data_ptr(),
+                                          self.scratch.data_ptr() + self.pg_bytes, self.scratch.numel() - self.pg_bytes,
+                                          s), "backward_pairs")
         ev[5].record()
         g = self.grads
         chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), d["rgb"].data_ptr(),
@@ -259,7 +262,7 @@ class Pipeline:
             radix += 1 + scan_launches((1 << b) * nseg) + 1
         prepare = 2
         binning = 1 + scan_launches(self.tiles) + radix
-        return prepare + binning + 1 + (2 if backward else 0)
+        return prepare + binning + 1 + (3 if backward else 0)
 
     def evaluations(self):
         """Pixel-Gaussian evaluations: sum over tiles of valid pixels x list length."""

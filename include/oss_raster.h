@@ -125,7 +125,7 @@ OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
  * d_feat is the gradient w.r.t. feat (not feat'); d_opacity, d_scale, d_rot
  * may be NULL.
  * ------------------------------------------------------------------------- */
-OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f);
+OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_t num_tiles);
 OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
                         const float* geo, const float* feat, const float* opacity,
                         const float* scale, const float* rot,
@@ -140,13 +140,16 @@ OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
  * partials: oss_render_backward_pairs writes pairgrad[total_pairs][stride]
  * (stride = oss_pair_grad_stride(f) floats: d_xy(2), d_conic(3), d_feat'(f),
  * zero padding) in gid-major pair order; oss_reduce_pair_grads sums them per
- * Gaussian.  pairgrad is the scratch of oss_render_backward. */
+ * Gaussian.  The scratch of oss_render_backward is pairgrad followed by the
+ * work-item table oss_render_backward_pairs needs. */
 OSS_API int oss_pair_grad_stride(int64_t f);
+OSS_API int64_t oss_render_backward_pairs_scratch_bytes(int64_t total_pairs, int64_t num_tiles);
 OSS_API int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w,
                               const float* geo, const float* feat, const float* opacity,
                               const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
                               const int32_t* gid_sorted, const int32_t* tile_offsets,
-                              const float* grad_image, float* pairgrad, void* stream);
+                              const float* grad_image, float* pairgrad,
+                              void* scratch, int64_t scratch_bytes, void* stream);
 OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
                           const int32_t* pair_offset, const float* feat, const float* opacity,
                           const float* scale, const float* rot,
@@ -156,14 +159,16 @@ OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
 /* ---------------------------------------------------------------------------
  * Backward for arbitrary caller lists (per-pair partial sums, then fp32 atomics):
  * replaces _C.rasterize_backward (bindings.cpp:66 -> rasterizer_bwd.cu:157-247).
- * d_xy, d_conic, d_feat are zeroed here.  geo_scratch holds n*8 floats.
+ * d_xy, d_conic, d_feat are zeroed here.  total_pairs = tile_offsets[T], the
+ * length of gid_sorted.
  * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_rasterize_backward_lists_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles);
 OSS_API int oss_rasterize_backward_lists(int64_t n, int64_t f, int64_t h, int64_t w,
                                  const float* xy, const float* conic, const float* feat,
-                                 const int32_t* gid_sorted, const int32_t* tile_offsets,
-                                 const float* grad_image,
+                                 const int32_t* gid_sorted, int64_t total_pairs,
+                                 const int32_t* tile_offsets, const float* grad_image,
                                  float* d_xy, float* d_conic, float* d_feat,
-                                 float* geo_scratch, void* stream);
+                                 void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Geo records from caller conics (for oss_render_forward with an explicit conic).

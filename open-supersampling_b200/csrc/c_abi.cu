@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 1; }
+int oss_abi_version(void) { return 2; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -190,10 +190,17 @@ int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* 
     return OSS_OK;
 }
 
-int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f) {
+int64_t oss_render_backward_pairs_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
+    if (total_pairs < 0) total_pairs = 0;
+    if (num_tiles < 0) num_tiles = 0;
+    return oss::backward_items_scratch_bytes(total_pairs, num_tiles);
+}
+
+int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_t num_tiles) {
     if (total_pairs < 0) total_pairs = 0;
     if (f < 0) f = 0;
-    return oss::arena_bytes(total_pairs * oss::backward_pair_stride(static_cast<int>(f)), 4);
+    return oss::arena_bytes(total_pairs * oss::backward_pair_stride(static_cast<int>(f)), 4) +
+           oss_render_backward_pairs_scratch_bytes(total_pairs, num_tiles);
 }
 
 int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
@@ -207,7 +214,7 @@ int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float*
     if (rc != OSS_OK) return rc;
     OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
     OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
-    OSS_CHECK(scratch_bytes >= oss_render_backward_scratch_bytes(total_pairs, f), OSS_ERR_SCRATCH,
+    OSS_CHECK(scratch_bytes >= oss_render_backward_scratch_bytes(total_pairs, f, g.tiles), OSS_ERR_SCRATCH,
               "render_backward scratch too small");
     if (g.n == 0) return OSS_OK;
     OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
@@ -217,8 +224,10 @@ int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float*
     OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
               "d_scale needs scale, rot and d_rot");
     float* pairgrad = static_cast<float*>(scratch);
+    const int64_t pg_bytes = oss::arena_bytes(total_pairs * oss::backward_pair_stride(static_cast<int>(f)), 4);
+    void* items = static_cast<char*>(scratch) + pg_bytes;
     rc = oss_render_backward_pairs(n, f, h, w, geo, feat, opacity, aabb, pair_offset, total_pairs, gid_sorted,
-                                   tile_offsets, grad_image, pairgrad, stream);
+                                   tile_offsets, grad_image, pairgrad, items, scratch_bytes - pg_bytes, stream);
     if (rc != OSS_OK) return rc;
     return oss_reduce_pair_grads(n, f, pairgrad, pair_offset, feat, opacity, scale, rot, d_xy, d_conic, d_feat,
                                  d_opacity, d_scale, d_rot, stream);
@@ -231,22 +240,26 @@ int oss_pair_grad_stride(int64_t f) {
 int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
                               const float* opacity, const int32_t* aabb, const int32_t* pair_offset,
                               int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
-                              const float* grad_image, float* pairgrad, void* stream) {
+                              const float* grad_image, float* pairgrad, void* scratch, int64_t scratch_bytes,
+                              void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
     OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
     OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "render_backward_pairs scratch too small");
     if (g.n == 0 || total_pairs == 0 || g.tiles == 0) return OSS_OK;
     OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
               OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
     OSS_CHECK(f == 0 || feat != nullptr, OSS_ERR_INVALID, "feat must be non-null");
     OSS_CHECK(pairgrad != nullptr && aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
     OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
               "lists and grad_image must be non-null");
-    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
-                                                   tile_offsets, grad_image, aabb, pair_offset, pairgrad,
-                                                   oss_pair_grad_stride(f), nullptr, nullptr, nullptr,
+    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, opacity,
+                                                   gid_sorted, tile_offsets, grad_image, aabb, pair_offset, pairgrad,
+                                                   oss_pair_grad_stride(f), nullptr, nullptr, nullptr, scratch,
                                                    as_stream(stream)));
     return OSS_OK;
 }
@@ -270,29 +283,40 @@ int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int
     return OSS_OK;
 }
 
+int64_t oss_rasterize_backward_lists_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles) {
+    if (n < 0) n = 0;
+    return oss::arena_bytes(n * 8, 4) + oss_render_backward_pairs_scratch_bytes(total_pairs, num_tiles);
+}
+
 int oss_rasterize_backward_lists(int64_t n, int64_t f, int64_t h, int64_t w, const float* xy, const float* conic,
-                                 const float* feat, const int32_t* gid_sorted, const int32_t* tile_offsets,
-                                 const float* grad_image, float* d_xy, float* d_conic, float* d_feat,
-                                 float* geo_scratch, void* stream) {
+                                 const float* feat, const int32_t* gid_sorted, int64_t total_pairs,
+                                 const int32_t* tile_offsets, const float* grad_image, float* d_xy, float* d_conic,
+                                 float* d_feat, void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
     OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_rasterize_backward_lists_scratch_bytes(n, total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "rasterize_backward_lists scratch too small");
     if (g.n == 0) return OSS_OK;
     OSS_CHECK(xy != nullptr && aligned(xy, 8) && conic != nullptr, OSS_ERR_INVALID, "xy (8-byte aligned) and conic must be non-null");
     OSS_CHECK(d_xy != nullptr && d_conic != nullptr && (f == 0 || (d_feat != nullptr && feat != nullptr)),
               OSS_ERR_INVALID, "gradient outputs must be non-null");
-    OSS_CHECK(geo_scratch != nullptr && aligned(geo_scratch, 16), OSS_ERR_INVALID, "geo_scratch must be 16-byte aligned");
+    OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
     cudaStream_t s = as_stream(stream);
     OSS_CUDA_TRY(cudaMemsetAsync(d_xy, 0, sizeof(float) * 2 * g.n, s));
     OSS_CUDA_TRY(cudaMemsetAsync(d_conic, 0, sizeof(float) * 3 * g.n, s));
     if (f > 0) OSS_CUDA_TRY(cudaMemsetAsync(d_feat, 0, sizeof(float) * f * g.n, s));
-    if (f == 0 || g.tiles == 0) return OSS_OK;
-    OSS_CHECK(tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID, "tile_offsets and grad_image must be non-null");
-    OSS_CUDA_TRY(oss::launch_make_geo(g.n, xy, conic, geo_scratch, s));
-    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, geo_scratch, feat, nullptr,
+    if (f == 0 || g.tiles == 0 || total_pairs == 0) return OSS_OK;
+    OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
+              "lists and grad_image must be non-null");
+    float* geo = static_cast<float*>(scratch);
+    void* items = static_cast<char*>(scratch) + oss::arena_bytes(static_cast<int64_t>(g.n) * 8, 4);
+    OSS_CUDA_TRY(oss::launch_make_geo(g.n, xy, conic, geo, s));
+    OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, nullptr,
                                                    gid_sorted, tile_offsets, grad_image, nullptr, nullptr, nullptr, 0,
-                                                   d_xy, d_conic, d_feat, s));
+                                                   d_xy, d_conic, d_feat, items, s));
     return OSS_OK;
 }
 

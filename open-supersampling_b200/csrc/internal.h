@@ -80,15 +80,17 @@ cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const f
 
 // Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows of
 // pair_stride floats at pair_offset[g] + local tile index.  Atomic mode: adds
-// into d_xy / d_conic / d_feat.
-cudaError_t launch_render_backward_tiles(int f, int h, int w, const float* geo, const float* feat,
-                                         const float* opacity, const int32_t* gid_sorted,
+// into d_xy / d_conic / d_feat.  items_scratch holds the work-item table
+// (backward_items_scratch_bytes).
+cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo,
+                                         const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image,
                                          const int32_t* aabb, const int32_t* pair_offset,
                                          float* pairgrad, int pair_stride,
-                                         float* d_xy, float* d_conic, float* d_feat,
+                                         float* d_xy, float* d_conic, float* d_feat, void* items_scratch,
                                          cudaStream_t stream);
 int backward_pair_stride(int f);
+int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles);
 cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,
                                          const int32_t* pair_offset, const float* feat,
                                          const float* opacity, const float* scale, const float* rot,

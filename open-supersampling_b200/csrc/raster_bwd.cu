@@ -1,35 +1,45 @@
 // Backward of the additive tile render (the reference's rasterize_backward,
 // rasterizer_bwd.cu:32-113), re-organised so that no per-pixel atomics remain.
 //
-// One CTA (4 warps) per tile.  The tile's dL/dimage block is staged once in
-// shared memory.  Each lane owns one list entry (Gaussian) and walks all valid
-// pixels of the tile, keeping the per-pair sums in registers:
+// Work is cut into items: up to 32 list entries of one tile.  One warp runs one
+// item.  It stages the tile's dL/dimage block into its own shared-memory slot
+// (rows padded so that lanes on different rows hit different banks), then each
+// lane owns one list entry and walks the tile's pixels, keeping the per-pair
+// sums in registers:
 //   g = w * sum_c go_c f'_c      (w = exp(-q/2), dL/dq = -g/2)
 //   Sx = sum g dx, Sy = sum g dy, Sxx = sum g dx^2, Sxy = sum g dx dy,
 //   Syy = sum g dy^2, dF_c = sum w go_c
 // from which d_xy = (a Sx + b Sy, b Sx + d Sy) and
 // d_conic = (-Sxx/2, -Sxy, -Syy/2) -- the reference's per-pixel terms
-// (rasterizer_bwd.cu:89-108) summed over the tile.  The dy-dependent factors
-// are hoisted per pixel row, so an evaluation costs ~16 FP32 ops + 1 MUFU.
+// (rasterizer_bwd.cu:89-108) summed over the tile.
+//
+// A tile's last item is usually partial.  With r < 32 entries it runs k lanes
+// per entry (k = 2, 4, 8 or 16, the largest with r*k <= 32), each lane taking
+// 16/k rows, and the k partial sums are combined by a fixed xor-shuffle tree:
+// the split depends only on r, so results are bitwise reproducible.
 //
 // Deterministic mode writes each pair's partial row at its gid-major pair slot
 // (pair_offset[g] + local tile index, the order oss_bin_pairs expanded it in);
 // k_reduce_gaussian then sums a Gaussian's rows in that fixed order and applies
-// the conic -> (scale, rot) chain rule and the opacity unfold.
-// Atomic mode (caller-supplied lists) adds the pair partials with fp32 atomics:
-// (F+5) atomics per pair instead of the reference's (F+5) per pixel-pair.
+// the conic -> (scale, rot) chain rule and the opacity unfold.  Atomic mode
+// (caller-supplied lists) adds each pair's partials with fp32 atomics: (F+5)
+// atomics per pair instead of the reference's (F+5) per pixel-pair.
 #include "internal.h"
 #include "oss_common.cuh"
 
 namespace oss {
 namespace {
 
-constexpr int kBwdWarps = 4;
-constexpr int kBwdThreads = kBwdWarps * 32;
+constexpr int kItemEntries = 32;
 
 template <int FC>
 struct BwdCfg {
-    static constexpr int SG = ((FC + 3) / 4) * 4;  // staged grad floats per pixel
+    static constexpr int SG = ((FC + 3) / 4) * 4;        // staged grad floats per pixel
+    static constexpr int ROW = kTile * SG + 4;            // floats per staged row (+4: bank spread)
+    static constexpr int SLOT = kTile * ROW;              // floats per warp slot
+    static constexpr int WARPS = SLOT * 4 * 4 <= 200 * 1024 ? 4 : 2;  // warps (slots) per CTA
+    static constexpr int THREADS = WARPS * 32;
+    static constexpr int MIN_CTAS = FC <= 4 ? 8 : 1;  // 8 x 4 warps per SM for the common F <= 4
 };
 
 __device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, float b, float d) {
@@ -37,24 +47,27 @@ __device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, flo
     return finite && a > 0.0f && d > 0.0f && (a * d - b * b) >= 1.0e-3f * (a * d);
 }
 
-// Per-pair sums over one full 16x16 tile: the 16 column offsets dx are hoisted
-// into registers, each row hoists B*dy and D*dy*dy, and the column loop is
-// fully unrolled.  CHECK keeps the reference's q >= 0 test per pixel.
+// Per-pair sums over rows [r0, r1) of a full 16-wide tile row span: the 16
+// column offsets dx are hoisted into registers, each row hoists B*dy and
+// D*dy*dy, and the column loop is fully unrolled.  CHECK keeps the reference's
+// q >= 0 test per pixel.
 template <int FC, bool CHECK>
-__device__ __forceinline__ void bwd_full_tile(const float* __restrict__ s_go, float fx0, float fy0, float gx, float gy,
-                                              float A, float B, float D, const float (&fv)[FC], float (&dF)[FC],
-                                              float& Sx, float& Sy, float& Sxx, float& Sxy, float& Syy) {
+__device__ __forceinline__ void bwd_rows_full(const float* __restrict__ s_go, int r0, int r1, float fx0, float fy0,
+                                              float gx, float gy, float A, float B, float D, const float (&fv)[FC],
+                                              float (&dF)[FC], float& Sx, float& Sy, float& Sxx, float& Sxy,
+                                              float& Syy) {
     constexpr int SG = BwdCfg<FC>::SG;
+    constexpr int ROW = BwdCfg<FC>::ROW;
     float dxs[kTile];
 #pragma unroll
     for (int c = 0; c < kTile; ++c) dxs[c] = (fx0 + static_cast<float>(c)) - gx;
 #pragma unroll 1
-    for (int r = 0; r < kTile; ++r) {
+    for (int r = r0; r < r1; ++r) {
         const float dy = (fy0 + static_cast<float>(r)) - gy;
         const float bdy = B * dy;
         const float ddy2 = (D * dy) * dy;
         float rowG = 0.0f, rowGx = 0.0f;
-        const float* go_row = s_go + r * kTile * SG;
+        const float* go_row = s_go + r * ROW;
 #pragma unroll
         for (int c = 0; c < kTile; ++c) {
             const float dx = dxs[c];
@@ -89,158 +102,225 @@ __device__ __forceinline__ void bwd_full_tile(const float* __restrict__ s_go, fl
     }
 }
 
+// Same sums for a tile cut by the image border (ncol < 16 or rows beyond H).
+template <int FC>
+__device__ __forceinline__ void bwd_rows_edge(const float* __restrict__ s_go, int r0, int r1, int ncol, int tx0,
+                                              int ty0, float gx, float gy, float A, float B, float D,
+                                              const float (&fv)[FC], float (&dF)[FC], float& Sx, float& Sy,
+                                              float& Sxx, float& Sxy, float& Syy) {
+    constexpr int SG = BwdCfg<FC>::SG;
+    constexpr int ROW = BwdCfg<FC>::ROW;
+    for (int r = r0; r < r1; ++r) {
+        const float dy = static_cast<float>(ty0 + r) - gy;
+        float rowG = 0.0f, rowGx = 0.0f;
+        const float* go_row = s_go + r * ROW;
+        for (int c = 0; c < ncol; ++c) {
+            const float dx = static_cast<float>(tx0 + c) - gx;
+            const float q = q_scaled(A, B, D, dx, dy);
+            const float w = q <= 0.0f ? ex2_ftz(q) : 0.0f;
+            const float4* go4 = reinterpret_cast<const float4*>(go_row + c * SG);
+            float go[SG];
+#pragma unroll
+            for (int v = 0; v < SG / 4; ++v) {
+                const float4 t = go4[v];
+                go[4 * v + 0] = t.x;
+                go[4 * v + 1] = t.y;
+                go[4 * v + 2] = t.z;
+                go[4 * v + 3] = t.w;
+            }
+            float dLdw = 0.0f;
+#pragma unroll
+            for (int k = 0; k < FC; ++k) {
+                dLdw = fmaf(go[k], fv[k], dLdw);
+                dF[k] = fmaf(w, go[k], dF[k]);
+            }
+            const float gw = w * dLdw;
+            const float gdx = gw * dx;
+            rowGx += gdx;
+            Sxx = fmaf(gdx, dx, Sxx);
+            rowG += gw;
+        }
+        Sx += rowGx;
+        Sxy = fmaf(rowGx, dy, Sxy);
+        Sy = fmaf(rowG, dy, Sy);
+        Syy = fmaf(rowG * dy, dy, Syy);
+    }
+}
+
+__device__ __forceinline__ float group_sum(float v, int k) {
+    for (int m = 1; m < k; m <<= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
 template <int FC, bool DETERMINISTIC>
-__global__ void __launch_bounds__(kBwdThreads) k_render_bwd(
+__global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
     const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted,
-    const int32_t* __restrict__ tile_offsets, const float* __restrict__ grad_image, const int4* __restrict__ aabb,
-    const int32_t* __restrict__ pair_offset, float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy,
-    float* __restrict__ d_conic, float* __restrict__ d_feat) {
+    const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ item_offsets, int num_tiles,
+    const float* __restrict__ grad_image, const int4* __restrict__ aabb, const int32_t* __restrict__ pair_offset,
+    float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy, float* __restrict__ d_conic,
+    float* __restrict__ d_feat) {
     constexpr int SG = BwdCfg<FC>::SG;
-    extern __shared__ float4 s_go4[];
-    float* s_go = reinterpret_cast<float*>(s_go4);
+    constexpr int ROW = BwdCfg<FC>::ROW;
+    extern __shared__ float4 s_mem4[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * BwdCfg<FC>::WARPS + warp;
+    if (item >= item_offsets[num_tiles]) return;  // uniform per warp
+    float* s_go = reinterpret_cast<float*>(s_mem4) + warp * BwdCfg<FC>::SLOT;
 
-    const int tile = blockIdx.x;
+    // tile of this item: the last t with item_offsets[t] <= item (empty tiles
+    // share their successor's offset, so the match always has items)
+    int lo = 0, hi = num_tiles - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (item_offsets[mid] <= item) lo = mid;
+        else hi = mid - 1;
+    }
+    const int tile = lo;
+    const int first = tile_offsets[tile] + (item - item_offsets[tile]) * kItemEntries;
+    const int r = min(kItemEntries, tile_offsets[tile + 1] - first);
     const int tile_x = tile % ntx;
     const int tile_y = tile / ntx;
     const int tx0 = tile_x * kTile;
     const int ty0 = tile_y * kTile;
     const int nrow = min(kTile, H - ty0);
     const int ncol = min(kTile, W - tx0);
-    const int start = tile_offsets[tile];
-    const int end = tile_offsets[tile + 1];
-    if (start >= end) return;  // uniform per CTA
 
-    // stage dL/dimage of this tile: s_go[pixel * SG + c]
+    // stage this tile's dL/dimage (zero outside the image): all of a lane's
+    // loads are issued before any store, so staging costs one L2 round trip
     const int64_t plane = static_cast<int64_t>(H) * W;
-    for (int idx = threadIdx.x; idx < SG * kTilePixels; idx += kBwdThreads) {
-        const int c = idx / kTilePixels;
-        const int p = idx - c * kTilePixels;
-        const int ly = p >> 4;
-        const int lx = p & (kTile - 1);
-        float v = 0.0f;
-        if (c < F && ly < nrow && lx < ncol) {
-            v = grad_image[c * plane + static_cast<int64_t>(ty0 + ly) * W + (tx0 + lx)];
+    {
+        constexpr int kPerLane = kTilePixels / 32;  // 8 pixels per lane and channel
+        const float* gbase = grad_image + static_cast<int64_t>(ty0) * W + tx0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < SG; c0 += 4) {  // groups of 4 channels: 32 loads in flight per lane
+            float v[4][kPerLane];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+                for (int i = 0; i < kPerLane; ++i) {
+                    const int p = i * 32 + lane;
+                    const int ly = p >> 4, lx = p & (kTile - 1);
+                    const int c = c0 + cc;
+                    v[cc][i] = (c < F && ly < nrow && lx < ncol)
+                                   ? __ldg(gbase + c * plane + static_cast<int64_t>(ly) * W + lx)
+                                   : 0.0f;
+                }
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+                for (int i = 0; i < kPerLane; ++i) {
+                    const int p = i * 32 + lane;
+                    s_go[(p >> 4) * ROW + (p & (kTile - 1)) * SG + c0 + cc] = v[cc][i];
+                }
+            }
         }
-        s_go[p * SG + c] = v;
     }
-    __syncthreads();
+    __syncwarp();
 
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const bool full = nrow == kTile && ncol == kTile;
-    for (int base = start + warp * 32; base < end; base += kBwdThreads) {
-        // Only a tile's last batch is partial; its idle lanes run on a neutral
-        // entry (zero geometry and features) so the warp stays converged.
-        const int j = base + lane;
-        const bool active = j < end;
-        int g = 0;
-        float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        float fv[FC];
-#pragma unroll
-        for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
-        if (active) {
-            g = gid_sorted[j];
-            const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-            g0 = rec[0];
-            g1 = rec[1];
-            const float op = opacity != nullptr ? opacity[g] : 1.0f;
-            const float* fg = feat + static_cast<int64_t>(g) * F;
-#pragma unroll
-            for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
-        }
-        const bool regular = !active || regular_conic_bwd(g0.x, g0.y, g1.y, g1.z, g1.w);
-        const bool warp_regular = __all_sync(0xffffffffu, regular);
+    // lanes per entry (k) and this lane's entry and row band
+    const int k = r > 16 ? 1 : (r > 8 ? 2 : (r > 4 ? 4 : (r > 2 ? 8 : 16)));
+    const int e = lane / k;
+    const int band = lane - e * k;
+    const int rows_per = kTile / k;
+    const int r0 = band * rows_per;
+    const int r1 = min(r0 + rows_per, nrow);
+    const bool active = e < r;
 
-        float dF[FC];
+    int g = 0;
+    float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float fv[FC];
 #pragma unroll
-        for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
-        float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f;
-        const float A = g0.z, B = g0.w, D = g1.x;
+    for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
+    if (active) {  // idle lanes run on a neutral entry so the warp stays converged
+        g = gid_sorted[first + e];
+        const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
+        g0 = rec[0];
+        g1 = rec[1];
+        const float op = opacity != nullptr ? opacity[g] : 1.0f;
+        const float* fg = feat + static_cast<int64_t>(g) * F;
+#pragma unroll
+        for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+    }
+    const bool regular = !active || regular_conic_bwd(g0.x, g0.y, g1.y, g1.z, g1.w);
+    const bool warp_regular = __all_sync(0xffffffffu, regular);
 
-        if (full) {
-            const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
-            if (warp_regular) {
-                bwd_full_tile<FC, false>(s_go, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
-            } else {
-                bwd_full_tile<FC, true>(s_go, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
-            }
-        } else for (int r = 0; r < nrow; ++r) {
-            const float dy = static_cast<float>(ty0 + r) - g0.y;
-            float rowG = 0.0f, rowGx = 0.0f;
-            const float* go_row = s_go + r * kTile * SG;
-#pragma unroll 4
-            for (int cc = 0; cc < ncol; ++cc) {
-                const float dx = static_cast<float>(tx0 + cc) - g0.x;
-                const float q = q_scaled(A, B, D, dx, dy);
-                const float w = q <= 0.0f ? ex2_ftz(q) : 0.0f;
-                const float4* go4 = reinterpret_cast<const float4*>(go_row + cc * SG);
-                float go[SG];
+    float dF[FC];
 #pragma unroll
-                for (int v = 0; v < SG / 4; ++v) {
-                    const float4 t = go4[v];
-                    go[4 * v + 0] = t.x;
-                    go[4 * v + 1] = t.y;
-                    go[4 * v + 2] = t.z;
-                    go[4 * v + 3] = t.w;
-                }
-                float dLdw = 0.0f;
-#pragma unroll
-                for (int c = 0; c < FC; ++c) {
-                    dLdw = fmaf(go[c], fv[c], dLdw);
-                    dF[c] = fmaf(w, go[c], dF[c]);
-                }
-                const float gw = w * dLdw;
-                const float gdx = gw * dx;
-                rowGx += gdx;
-                Sxx = fmaf(gdx, dx, Sxx);
-                rowG += gw;
-            }
-            Sx += rowGx;
-            Sxy = fmaf(rowGx, dy, Sxy);
-            Sy = fmaf(rowG, dy, Sy);
-            Syy = fmaf(rowG * dy, dy, Syy);
-        }
-        if (!active) continue;
-        // raw conic (a, b, d) sits in g1.yzw
-        const float dxy_x = fmaf(g1.y, Sx, g1.z * Sy);
-        const float dxy_y = fmaf(g1.z, Sx, g1.w * Sy);
-        const float dca = -0.5f * Sxx;
-        const float dcb = -Sxy;
-        const float dcd = -0.5f * Syy;
-        if (DETERMINISTIC) {
-            const int4 box = aabb[g];
-            const int local = (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
-            float* row = pairgrad + (static_cast<int64_t>(pair_offset[g]) + local) * pstride;
-            if (FC <= 3) {
-                float4* row4 = reinterpret_cast<float4*>(row);
-                row4[0] = make_float4(dxy_x, dxy_y, dca, dcb);
-                row4[1] = make_float4(dcd, dF[0], FC > 1 ? dF[FC > 1 ? 1 : 0] : 0.0f,
-                                      FC > 2 ? dF[FC > 2 ? 2 : 0] : 0.0f);
-            } else {
-                row[0] = dxy_x;
-                row[1] = dxy_y;
-                row[2] = dca;
-                row[3] = dcb;
-                row[4] = dcd;
-#pragma unroll
-                for (int c = 0; c < FC; ++c) {
-                    if (c < F) row[5 + c] = dF[c];
-                }
-            }
+    for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
+    float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f;
+    const float A = g0.z, B = g0.w, D = g1.x;
+    if (ncol == kTile) {
+        const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
+        if (warp_regular) {
+            bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
         } else {
-            atomicAdd(&d_xy[2 * g + 0], dxy_x);
-            atomicAdd(&d_xy[2 * g + 1], dxy_y);
-            atomicAdd(&d_conic[3 * g + 0], dca);
-            atomicAdd(&d_conic[3 * g + 1], dcb);
-            atomicAdd(&d_conic[3 * g + 2], dcd);
+            bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+        }
+    } else {
+        bwd_rows_edge<FC>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+    }
+    if (k > 1) {  // combine the k row bands of each entry (all lanes take part)
+        Sx = group_sum(Sx, k);
+        Sy = group_sum(Sy, k);
+        Sxx = group_sum(Sxx, k);
+        Sxy = group_sum(Sxy, k);
+        Syy = group_sum(Syy, k);
+#pragma unroll
+        for (int c = 0; c < FC; ++c) dF[c] = group_sum(dF[c], k);
+    }
+    if (!active || band != 0) return;
+
+    // raw conic (a, b, d) sits in g1.yzw
+    const float dxy_x = fmaf(g1.y, Sx, g1.z * Sy);
+    const float dxy_y = fmaf(g1.z, Sx, g1.w * Sy);
+    const float dca = -0.5f * Sxx;
+    const float dcb = -Sxy;
+    const float dcd = -0.5f * Syy;
+    if (DETERMINISTIC) {
+        const int4 box = aabb[g];
+        const int local = (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
+        float* row = pairgrad + (static_cast<int64_t>(pair_offset[g]) + local) * pstride;
+        if (FC <= 3) {
+            float4* row4 = reinterpret_cast<float4*>(row);
+            row4[0] = make_float4(dxy_x, dxy_y, dca, dcb);
+            row4[1] = make_float4(dcd, dF[0], FC > 1 ? dF[FC > 1 ? 1 : 0] : 0.0f,
+                                  FC > 2 ? dF[FC > 2 ? 2 : 0] : 0.0f);
+        } else {
+            row[0] = dxy_x;
+            row[1] = dxy_y;
+            row[2] = dca;
+            row[3] = dcb;
+            row[4] = dcd;
 #pragma unroll
             for (int c = 0; c < FC; ++c) {
-                if (c < F) atomicAdd(&d_feat[static_cast<int64_t>(g) * F + c], dF[c]);
+                if (c < F) row[5 + c] = dF[c];
             }
         }
+    } else {
+        atomicAdd(&d_xy[2 * g + 0], dxy_x);
+        atomicAdd(&d_xy[2 * g + 1], dxy_y);
+        atomicAdd(&d_conic[3 * g + 0], dca);
+        atomicAdd(&d_conic[3 * g + 1], dcb);
+        atomicAdd(&d_conic[3 * g + 2], dcd);
+#pragma unroll
+        for (int c = 0; c < FC; ++c) {
+            if (c < F) atomicAdd(&d_feat[static_cast<int64_t>(g) * F + c], dF[c]);
+        }
     }
+}
+
+// Work items of the backward: every tile has ceil(L / 32) items of up to 32
+// consecutive list entries.  item_offsets (an exclusive scan of those counts,
+// item_offsets[T] = total) maps an item to its tile by binary search.
+__global__ void __launch_bounds__(256) k_item_counts(int num_tiles, const int32_t* __restrict__ tile_offsets,
+                                                      int32_t* __restrict__ counts) {
+    const int t = blockIdx.x * 256 + threadIdx.x;
+    if (t >= num_tiles) return;
+    counts[t] = (tile_offsets[t + 1] - tile_offsets[t] + kItemEntries - 1) / kItemEntries;
 }
 
 template <int FC>
@@ -295,9 +375,9 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
 #pragma unroll
     for (int c = 0; c < FC; ++c) {
         if (c < F) {
-            const int64_t k = static_cast<int64_t>(g) * F + c;
-            d_feat[k] = dF[c] * op;
-            dop = fmaf(dF[c], feat[k], dop);
+            const int64_t kk = static_cast<int64_t>(g) * F + c;
+            d_feat[kk] = dF[c] * op;
+            dop = fmaf(dF[c], feat[kk], dop);
         }
     }
     if (d_opacity != nullptr) d_opacity[g] = dop;
@@ -311,22 +391,24 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
 }
 
 template <int FC>
-cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int num_tiles, const float* geo, const float* feat,
+cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
-                          const float* grad_image, const int32_t* aabb, const int32_t* pair_offset, float* pairgrad,
-                          int pstride, float* d_xy, float* d_conic, float* d_feat, cudaStream_t stream) {
-    const int smem = kTilePixels * BwdCfg<FC>::SG * static_cast<int>(sizeof(float));
+                          const int32_t* item_offsets, int num_tiles, const float* grad_image, const int32_t* aabb,
+                          const int32_t* pair_offset, float* pairgrad, int pstride, float* d_xy, float* d_conic,
+                          float* d_feat, cudaStream_t stream) {
+    const int smem = BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT * static_cast<int>(sizeof(float));
+    const unsigned blocks = static_cast<unsigned>(div_up(max_items, BwdCfg<FC>::WARPS));
     if (pairgrad != nullptr) {
         auto kern = k_render_bwd<FC, true>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        kern<<<static_cast<unsigned>(num_tiles), kBwdThreads, smem, stream>>>(
-            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, grad_image,
+        kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
+            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets, num_tiles, grad_image,
             reinterpret_cast<const int4*>(aabb), pair_offset, pairgrad, pstride, d_xy, d_conic, d_feat);
     } else {
         auto kern = k_render_bwd<FC, false>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        kern<<<static_cast<unsigned>(num_tiles), kBwdThreads, smem, stream>>>(
-            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, grad_image,
+        kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
+            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets, num_tiles, grad_image,
             reinterpret_cast<const int4*>(aabb), pair_offset, pairgrad, pstride, d_xy, d_conic, d_feat);
     }
     return cudaGetLastError();
@@ -347,21 +429,41 @@ cudaError_t launch_reduce_fc(int n, int f, const float* pairgrad, int pstride, c
 
 int backward_pair_stride(int f) { return ((5 + f + 3) / 4) * 4; }
 
+int64_t backward_max_items(int64_t total_pairs, int64_t num_tiles) {
+    return num_tiles + (total_pairs + kItemEntries - 1) / kItemEntries;
+}
+
+int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
+    (void)total_pairs;
+    return arena_bytes(num_tiles, sizeof(int32_t)) + arena_bytes(num_tiles + 1, sizeof(int32_t)) +
+           scan_scratch_bytes(num_tiles);
+}
+
 #define OSS_DISPATCH_FC(f, CALL) \
     ((f) <= 1 ? CALL(1) : (f) <= 3 ? CALL(3) : (f) <= 4 ? CALL(4) : (f) <= 8 ? CALL(8) : (f) <= 16 ? CALL(16) : (f) <= 32 ? CALL(32) : CALL(64))
 
-cudaError_t launch_render_backward_tiles(int f, int h, int w, const float* geo, const float* feat,
+cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo, const float* feat,
                                          const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
                                          const int32_t* pair_offset, float* pairgrad, int pair_stride, float* d_xy,
-                                         float* d_conic, float* d_feat, cudaStream_t stream) {
+                                         float* d_conic, float* d_feat, void* items_scratch, cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
-    if (num_tiles == 0) return cudaSuccess;
-#define OSS_BWD_CALL(FC)                                                                                     \
-    launch_bwd_fc<FC>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, grad_image, aabb, \
-                      pair_offset, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
+    if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
+    const int64_t max_items = backward_max_items(total_pairs, num_tiles);
+    Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
+    int32_t* counts = arena.take<int32_t>(num_tiles);
+    int32_t* item_offsets = arena.take<int32_t>(num_tiles + 1);
+    void* scan_scratch = arena.base + arena.used;
+    k_item_counts<<<static_cast<unsigned>(div_up(num_tiles, 256)), 256, 0, stream>>>(num_tiles, tile_offsets, counts);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    err = scan_exclusive_i32(counts, item_offsets, num_tiles, true, nullptr, scan_scratch, stream);
+    if (err != cudaSuccess) return err;
+#define OSS_BWD_CALL(FC)                                                                                          \
+    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets,       \
+                      num_tiles, grad_image, aabb, pair_offset, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
     return OSS_DISPATCH_FC(f, OSS_BWD_CALL);
 #undef OSS_BWD_CALL
 }

@@ -95,13 +95,15 @@ def rasterize_backward(xy, scale, rot, feat, conic, gaussian_idx_sorted, tile_of
         d_xy = torch.empty((n, 2), **f32)
         d_conic = torch.empty((n, 3), **f32)
         d_feat = torch.empty((n, f), **f32)
-        geo = torch.empty((max(n, 1), 8), **f32)
+        total = int(gaussian_idx_sorted.numel())
+        nbytes = lib.oss_rasterize_backward_lists_scratch_bytes(n, total, num_tiles)
+        scratch = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
         xy_a = aligned(xy, 8)
         _lib.check(
             lib.oss_rasterize_backward_lists(n, f, h, w, xy_a.data_ptr(), conic.data_ptr(), feat.data_ptr(),
-                                             gaussian_idx_sorted.data_ptr(), tile_offsets.data_ptr(),
+                                             gaussian_idx_sorted.data_ptr(), total, tile_offsets.data_ptr(),
                                              grad_out.data_ptr(), d_xy.data_ptr(), d_conic.data_ptr(),
-                                             d_feat.data_ptr(), geo.data_ptr(), stream_of(xy)),
+                                             d_feat.data_ptr(), scratch.data_ptr(), scratch.numel(), stream_of(xy)),
             "rasterize_backward",
         )
     return d_xy, d_conic, d_feat

@@ -193,7 +193,8 @@ def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
     d_opacity = torch.empty((n,), **f32) if opacity is not None else None
     d_scale = torch.empty((n, 2), **f32)
     d_rot = torch.empty((n,), **f32)
-    nbytes = lib.oss_render_backward_scratch_bytes(b.total_pairs, f)
+    num_tiles = int(b.tile_offsets.numel()) - 1
+    nbytes = lib.oss_render_backward_scratch_bytes(b.total_pairs, f, num_tiles)
     scratch = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
     scale = aligned(scale, 8)
     _lib.check(
