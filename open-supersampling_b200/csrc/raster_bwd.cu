@@ -39,12 +39,93 @@ struct BwdCfg {
     static constexpr int SLOT = kTile * ROW;              // floats per warp slot
     static constexpr int WARPS = SLOT * 4 * 4 <= 200 * 1024 ? 4 : 2;  // warps (slots) per CTA
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int MIN_CTAS = FC <= 4 ? 8 : 1;  // 8 x 4 warps per SM for the common F <= 4
+    static constexpr int MIN_CTAS = FC <= 4 ? 6 : 1;  // 6 x 4 warps per SM (<= 80 registers) for F <= 4
+    // F <= 4 runs the packed f32x2 path: the staged block is interleaved by
+    // column pairs, [go_k(c), go_k(c+1)] for k = 0..SG-1 per pair of columns.
+    static constexpr bool PAIRED = FC <= 4;
 };
+
+// Shared-memory index of staged channel k at tile row r, column c.
+template <int FC>
+__device__ __forceinline__ int go_index(int r, int c, int k) {
+    constexpr int SG = BwdCfg<FC>::SG;
+    if (BwdCfg<FC>::PAIRED) return r * BwdCfg<FC>::ROW + (c >> 1) * 2 * SG + 2 * k + (c & 1);
+    return r * BwdCfg<FC>::ROW + c * SG + k;
+}
 
 __device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, float b, float d) {
     const bool finite = isfinite(x) && isfinite(y) && isfinite(a) && isfinite(b) && isfinite(d);
     return finite && a > 0.0f && d > 0.0f && (a * d - b * b) >= 1.0e-3f * (a * d);
+}
+
+// Packed-f32x2 version of the full-row sums for F <= 4: every FP32 operation
+// works on two adjacent columns at once (__ffma2_rn / __fmul2_rn / __fadd2_rn),
+// halving the FP32 instructions per pixel; exp2 stays one MUFU op per pixel.
+template <int FC, bool CHECK>
+__device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go, int r0, int r1, float fx0, float fy0,
+                                                 float gx, float gy, float A, float B, float D, const float (&fv)[FC],
+                                                 float (&dF)[FC], float& Sx, float& Sy, float& Sxx, float& Sxy,
+                                                 float& Syy) {
+    constexpr int SG = BwdCfg<FC>::SG;
+    constexpr int ROW = BwdCfg<FC>::ROW;
+    float2 dx2[kTile / 2];
+#pragma unroll
+    for (int j = 0; j < kTile / 2; ++j) {
+        dx2[j] = make_float2((fx0 + static_cast<float>(2 * j)) - gx, (fx0 + static_cast<float>(2 * j + 1)) - gx);
+    }
+    const float2 A2 = make_float2(A, A);
+    float2 f2[FC], dF2[FC];
+#pragma unroll
+    for (int k = 0; k < FC; ++k) {
+        f2[k] = make_float2(fv[k], fv[k]);
+        dF2[k] = make_float2(0.0f, 0.0f);
+    }
+    float2 Sxx2 = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+    for (int r = r0; r < r1; ++r) {
+        const float dy = (fy0 + static_cast<float>(r)) - gy;
+        const float bdy = B * dy;
+        const float ddy = (D * dy) * dy;
+        const float2 bdy2 = make_float2(bdy, bdy);
+        const float2 ddy2 = make_float2(ddy, ddy);
+        float2 rowG2 = make_float2(0.0f, 0.0f), rowGx2 = make_float2(0.0f, 0.0f);
+        const float* go_row = s_go + r * ROW;
+#pragma unroll
+        for (int j = 0; j < kTile / 2; ++j) {
+            const float2 dx = dx2[j];
+            const float2 q = __ffma2_rn(dx, __ffma2_rn(A2, dx, bdy2), ddy2);
+            float2 w;
+            w.x = CHECK ? (q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f) : ex2_ftz(q.x);
+            w.y = CHECK ? (q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f) : ex2_ftz(q.y);
+            const float4* go4 = reinterpret_cast<const float4*>(go_row + j * 2 * SG);
+            float2 go2[SG];
+#pragma unroll
+            for (int v = 0; v < SG / 2; ++v) {
+                const float4 t = go4[v];
+                go2[2 * v] = make_float2(t.x, t.y);
+                go2[2 * v + 1] = make_float2(t.z, t.w);
+            }
+            float2 dLdw = __fmul2_rn(go2[0], f2[0]);
+#pragma unroll
+            for (int k = 1; k < FC; ++k) dLdw = __ffma2_rn(go2[k], f2[k], dLdw);
+#pragma unroll
+            for (int k = 0; k < FC; ++k) dF2[k] = __ffma2_rn(w, go2[k], dF2[k]);
+            const float2 gw = __fmul2_rn(w, dLdw);
+            const float2 gdx = __fmul2_rn(gw, dx);
+            rowGx2 = __fadd2_rn(rowGx2, gdx);
+            Sxx2 = __ffma2_rn(gdx, dx, Sxx2);
+            rowG2 = __fadd2_rn(rowG2, gw);
+        }
+        const float rowGx = rowGx2.x + rowGx2.y;
+        const float rowG = rowG2.x + rowG2.y;
+        Sx += rowGx;
+        Sxy = fmaf(rowGx, dy, Sxy);
+        Sy = fmaf(rowG, dy, Sy);
+        Syy = fmaf(rowG * dy, dy, Syy);
+    }
+    Sxx += Sxx2.x + Sxx2.y;
+#pragma unroll
+    for (int k = 0; k < FC; ++k) dF[k] += dF2[k].x + dF2[k].y;
 }
 
 // Per-pair sums over rows [r0, r1) of a full 16-wide tile row span: the 16
@@ -118,16 +199,10 @@ __device__ __forceinline__ void bwd_rows_edge(const float* __restrict__ s_go, in
             const float dx = static_cast<float>(tx0 + c) - gx;
             const float q = q_scaled(A, B, D, dx, dy);
             const float w = q <= 0.0f ? ex2_ftz(q) : 0.0f;
-            const float4* go4 = reinterpret_cast<const float4*>(go_row + c * SG);
-            float go[SG];
+            float go[FC];
 #pragma unroll
-            for (int v = 0; v < SG / 4; ++v) {
-                const float4 t = go4[v];
-                go[4 * v + 0] = t.x;
-                go[4 * v + 1] = t.y;
-                go[4 * v + 2] = t.z;
-                go[4 * v + 3] = t.w;
-            }
+            for (int k = 0; k < FC; ++k) go[k] = s_go[go_index<FC>(r, c, k)];
+            (void)go_row;
             float dLdw = 0.0f;
 #pragma unroll
             for (int k = 0; k < FC; ++k) {
@@ -213,7 +288,7 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
 #pragma unroll
                 for (int i = 0; i < kPerLane; ++i) {
                     const int p = i * 32 + lane;
-                    s_go[(p >> 4) * ROW + (p & (kTile - 1)) * SG + c0 + cc] = v[cc][i];
+                    s_go[go_index<FC>(p >> 4, p & (kTile - 1), c0 + cc)] = v[cc][i];
                 }
             }
         }
@@ -256,9 +331,19 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
     if (ncol == kTile) {
         const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
         if (warp_regular) {
-            bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            if constexpr (BwdCfg<FC>::PAIRED) {
+                bwd_rows_full_pk<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                            Syy);
+            } else {
+                bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            }
         } else {
-            bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            if constexpr (BwdCfg<FC>::PAIRED) {
+                bwd_rows_full_pk<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                           Syy);
+            } else {
+                bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            }
         }
     } else {
         bwd_rows_edge<FC>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
