@@ -159,8 +159,12 @@ def scan_launches(n: int) -> int:
 class Pipeline:
     """The hot path over the C ABI, with a CUDA event between each stage.
 
-    Buffers are sized for up to `capacity_n` Gaussians and grow for pairs; each
-    step takes its inputs (xy, scale, rot, opacity, rgb[, grad]) as device tensors.
+    Buffers are sized for up to `capacity_n` Gaussians and for a pair capacity
+    taken from the first step (one host read of the pair total, then +10%);
+    later steps launch without any host synchronisation -- binning checks the
+    device-side total against the capacity and raises `overflow` instead -- so
+    a step can be captured in a CUDA graph.  Each step takes its inputs (xy,
+    scale, rot, opacity, rgb[, grad]) as device tensors.
     """
 
     def __init__(self, capacity_n, h, w, mode, device):
@@ -180,6 +184,8 @@ class Pipeline:
         self.pair_offset = torch.empty((n + 1,), **i32)
         self.geo = torch.empty((n, 8), **f32)
         self.total = torch.empty((1,), device=device, dtype=torch.int64)
+        self.tile_count = torch.empty((max(1, self.tiles),), **i32)
+        self.overflow = torch.zeros((1,), **i32)
         self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device=device,
                                         dtype=torch.uint8)
         self.image = torch.empty((3, h, w), **f32)
@@ -203,45 +209,70 @@ class Pipeline:
             self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
             self.pg_bytes = ((self.capacity * self.lib.oss_pair_grad_stride(3) * 4 + 255) // 256) * 256
 
-    def step(self, d, backward=True):
-        lib, chk, ev = self.lib, self._lib.check, self.events
+    def _mark(self, i, timed):
+        if timed:
+            self.events[i].record()
+
+    def step(self, d, backward=True, sync=False, timed=True):
+        """One pass of the hot path.  sync=True reads the pair total on the host
+        (and grows the capacity); the first step always does."""
+        lib, chk = self.lib, self._lib.check
         s = torch.cuda.current_stream().cuda_stream
         n, h, w = int(d["xy"].shape[0]), self.h, self.w
         self.n_step = n
-        ev[0].record()
+        self._mark(0, timed)
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
                                    d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
                                    self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
-                                   self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
-        ev[1].record()
-        pairs = int(self.total.item())  # the path's one host sync
-        self._ensure(pairs)
-        self.pairs = pairs
-        ev[2].record()
-        chk(lib.oss_bin_pairs(n, h, w, self.mode, self.aabb.data_ptr(), self.pair_offset.data_ptr(), pairs,
-                              self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.scratch.data_ptr(),
-                              self.scratch.numel(), s), "bin")
-        ev[3].record()
+                                   self.tile_count.data_ptr(), self.prep_scratch.data_ptr(),
+                                   self.prep_scratch.numel(), s), "prepare")
+        self._mark(1, timed)
+        if sync or self.capacity == 0:
+            self.pairs = int(self.total.item())
+            self._ensure(self.pairs)
+        self._mark(2, timed)
+        chk(lib.oss_bin_pairs(n, h, w, self.mode, self.aabb.data_ptr(), self.pair_offset.data_ptr(),
+                              self.tile_count.data_ptr(), self.total.data_ptr(), self.capacity,
+                              self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
+                              self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
+        self._mark(3, timed)
         chk(lib.oss_render_forward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(), d["opacity"].data_ptr(),
                                    self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.image.data_ptr(),
                                    s), "forward")
-        ev[4].record()
+        self._mark(4, timed)
         if not backward:
             return
         chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
-                                          pairs, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
+                                          self.capacity, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
                                           d["grad"].data_ptr(), self.scratch.data_ptr(),
                                           self.scratch.data_ptr() + self.pg_bytes, self.scratch.numel() - self.pg_bytes,
                                           s), "backward_pairs")
-        ev[5].record()
+        self._mark(5, timed)
         g = self.grads
         chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), d["rgb"].data_ptr(),
                                       d["opacity"].data_ptr(), d["scale"].data_ptr(), d["rot"].data_ptr(),
                                       g["d_xy"].data_ptr(), g["d_conic"].data_ptr(), g["d_rgb"].data_ptr(),
                                       g["d_opacity"].data_ptr(), g["d_scale"].data_ptr(), g["d_rot"].data_ptr(), s),
             "reduce")
-        ev[6].record()
+        self._mark(6, timed)
+
+    def check_overflow(self):
+        """Host read of the overflow flag of the last step (a synchronisation)."""
+        if int(self.overflow.item()) != 0:
+            raise RuntimeError(f"pair capacity {self.capacity} exceeded ({int(self.total.item())} pairs)")
+
+    def capture(self, d, backward=True):
+        """CUDA graph of one sync-free step (capacity must already be sized)."""
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.step(d, backward=backward, timed=False)  # warm the capture stream
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(graph):
+            self.step(d, backward=backward, timed=False)
+        return graph
 
     def stage_ms(self):
         ev = self.events
@@ -252,17 +283,10 @@ class Pipeline:
 
     def launches_per_step(self, backward=True):
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
-        bits = max(0, int(self.tiles - 1).bit_length())  # radix.cu make_plan
-        passes = (bits + 7) // 8
-        nseg = -(-self.pairs // 1024)
-        radix, shift = 0, 0
-        for i in range(passes):
-            b = -(-(bits - shift) // (passes - i))
-            shift += b
-            radix += 1 + scan_launches((1 << b) * nseg) + 1
-        prepare = 2
-        binning = 1 + scan_launches(self.tiles) + radix
-        return prepare + binning + 1 + (3 if backward else 0)
+        prepare = 2                                   # k_preprocess, k_scan_apply
+        binning = scan_launches(self.tiles) + 2       # tile-offset scan, k_scatter_pairs, k_sort_tiles
+        bwd = 1 + scan_launches(self.tiles) + 1 + 1   # k_item_counts, item scan, k_render_bwd, k_reduce_gaussian
+        return prepare + binning + 1 + (bwd if backward else 0)
 
     def evaluations(self):
         """Pixel-Gaussian evaluations: sum over tiles of valid pixels x list length."""
@@ -355,38 +379,62 @@ def run_ours(args, rank, world, local):
     dev_inp = {k: torch.from_numpy(v).to(device) for k, v in inp.items()}
     flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
     for _ in range(max(3, args.warmup)):
-        pipe.step(dev_inp)
+        pipe.step(dev_inp, sync=True)  # sizes the pair capacity from the device total
         flush.zero_()
     torch.cuda.synchronize()
+    pipe.check_overflow()
 
     K = args.steps
-    stages = {k: 0.0 for k in pipe.stage_ms()}
     dist = None
     if world > 1:
         import torch.distributed as dist
 
+    # per-stage breakdown: eager sync-free steps with an event between stages
+    ks = max(3, min(K, 20))
+    stages = {k: 0.0 for k in pipe.stage_ms()}
+    for _ in range(ks):
+        flush.zero_()
+        pipe.step(dev_inp)
+        torch.cuda.synchronize()
+        for k, v in pipe.stage_ms().items():
+            stages[k] += v
+    stage_avg = {k: v / ks for k, v in stages.items()}
+
+    # timed: the same step replayed from a CUDA graph (fwd+bwd, then fwd only),
+    # one start/end event pair per step, L2 flushed between steps
+    graphs = {"fwdbwd": pipe.capture(dev_inp), "fwd": pipe.capture(dev_inp, backward=False)}
+    for g in graphs.values():
+        for _ in range(3):
+            flush.zero_()
+            g.replay()
+    torch.cuda.synchronize()
+    timed = {}
+    if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(device.index) as clocks:
         wall0 = time.perf_counter()
-        for _ in range(K):
-            flush.zero_()
-            pipe.step(dev_inp)
-            torch.cuda.synchronize()  # per-step events are read below; keeps host and device in step
-            for k, v in pipe.stage_ms().items():
-                stages[k] += v
-        torch.cuda.synchronize()
+        for name, g in graphs.items():
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+            for e0, e1 in ev:
+                flush.zero_()
+                e0.record()
+                g.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            timed[name] = sum(e0.elapsed_time(e1) for e0, e1 in ev)
         wall = time.perf_counter() - wall0
+    pipe.check_overflow()
     if world > 1:
         dist.barrier()
-    total_ms = torch.tensor([stages["total"], stages["fwd_path"]], device=device, dtype=torch.float64)
+    total_ms = torch.tensor([timed["fwdbwd"], timed["fwd"]], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
     step_ms = float(total_ms[0]) / K
     fwd_ms = float(total_ms[1]) / K
     pixels = h * w * world
     value = pixels / (step_ms * 1e-3) / 1e6
-    stage_avg = {k: v / K for k, v in stages.items()}
+    del graphs
 
     # roofline of the dominant kernel (FP32 SIMT; no tensor cores on this path)
     evals = pipe.evaluations()
@@ -418,7 +466,9 @@ def run_ours(args, rank, world, local):
     }
     # HBM roofline of the memory-bound stages (preprocess + binning)
     pairs = pipe.pairs
-    bin_bytes = n * (20 + 32 + 32 + 4) + pairs * 4 * 6 + pipe.tiles * 4 * 3
+    # preprocess: 20 B in, conic 12 + aabb 16 + pair offset 4 + geo 32 out; binning: unsorted list written,
+    # read and written sorted (12 B per pair), tile counts and offsets
+    bin_bytes = n * (20 + 12 + 16 + 4 + 32) + pairs * 4 * 3 + pipe.tiles * 4 * 4
     hbm = {"stages": "prepare+bin", "bytes": bin_bytes,
            "achieved_gbs": bin_bytes / ((stage_avg["prepare"] + stage_avg["bin"]) * 1e-3) / 1e9,
            "peak_gbs": peaks.get("hbm_gbs")}
@@ -432,8 +482,10 @@ def run_ours(args, rank, world, local):
                    "l2": "256 MiB flush between steps (outside the step events)", "pairs": pairs,
                    "frames_per_rank": 1},
         "fwd_mpix_s": pixels / (fwd_ms * 1e-3) / 1e6, "fwd_ms_per_frame": fwd_ms, "fwdbwd_ms_per_frame": step_ms,
+        "timing": "CUDA-graph replay of the sync-free step (C ABI calls captured once); stages_ms from eager "
+                  f"steps with an event between stages ({ks} steps)",
         "stages_ms": stage_avg, "roofline": roofline, "hbm_stages": hbm,
-        "gpu_launches": pipe.launches_per_step() * K,
+        "gpu_launches": (pipe.launches_per_step() + pipe.launches_per_step(backward=False)) * K,
         "clocks": clocks.summary(), "wall_s": wall,
     }
 
@@ -565,7 +617,7 @@ def run_config3(args, rank, world):
                 for m in motions:
                     c = warp_canvas(canvas, m, (h, w), 0.5, alpha)
                     pipe.step({"xy": c.positions, "scale": c.scales, "rot": c.rotations, "opacity": c.opacities,
-                               "rgb": c.colors}, backward=False)
+                               "rgb": c.colors}, backward=False, sync=True)
         return step
 
     ms1, clocks = timed(step_at(1.0), args.steps, args.warmup, device, world)
@@ -635,7 +687,7 @@ def run_config5(args, rank, world):
     def step():
         d_shared.zero_()
         for d in per_frame:
-            pipe.step(d)
+            pipe.step(d, sync=True)
             d_shared.add_(pack_shared_grads(pipe.grads, sl))
         ar_events[0].record()
         reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks

@@ -77,32 +77,47 @@ OSS_API int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, i
                    float* conic, int32_t* aabb, int32_t* pair_count, void* stream);
 
 /* ---------------------------------------------------------------------------
- * Render prepare: preprocess + gid-major pair-offset scan + geo records.
+ * Render prepare: preprocess + gid-major pair-offset scan + geo records +
+ * per-tile pair counts.
  * First half of _C.rasterize_forward (rasterizer_fwd.cu:478-545) and of
  * _C.pair_construction_only (rasterizer_fwd.cu:381-444).
  * Outputs: conic[n*3], aabb[n*4], pair_offset[n+1] (exclusive scan of the pair
  * counts; pair_offset[n] = total, valid only if total <= INT32_MAX),
- * geo[n*8], total_pairs[1] (int64, on the device).
+ * geo[n*8], total_pairs[1] (int64, on the device) and tile_count[num_tiles]
+ * (int32: how many Gaussians each tile's list will hold; input to
+ * oss_bin_pairs, which consumes it).  tile_count may be NULL in OSS_BIN_FULL
+ * mode, where it is not computed.
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_prepare_scratch_bytes(int64_t n);
 OSS_API int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode,
                        const float* xy, const float* scale, const float* rot,
                        float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                       int64_t* total_pairs, void* scratch, int64_t scratch_bytes,
+                       int64_t* total_pairs, int32_t* tile_count, void* scratch, int64_t scratch_bytes,
                        void* stream);
 
 /* ---------------------------------------------------------------------------
- * Deterministic tile binning of the pairs described by (aabb, pair_offset):
- * gid_sorted[total_pairs] lists, per tile in ascending tile id, the Gaussians
- * overlapping that tile in ascending gid order; tile_offsets[T+1] brackets them.
- * Bit-exact with the reference's sort of (tile << 32 | gid) keys plus
- * searchsorted (rasterizer_fwd.cu:446-475) for the same AABBs.
- * total_pairs is the host value of oss_render_prepare's total.
+ * Deterministic tile binning of the pairs described by (aabb, pair_offset,
+ * tile_count) from oss_render_prepare: gid_sorted lists, per tile in ascending
+ * tile id, the Gaussians overlapping that tile in ascending gid order;
+ * tile_offsets[T+1] brackets them.  Bit-exact with the reference's sort of
+ * (tile << 32 | gid) keys plus searchsorted (rasterizer_fwd.cu:446-475) for the
+ * same AABBs.
+ *
+ * No host synchronisation: the pair total is read on the device from
+ * total_pairs (oss_render_prepare's int64 output) and compared with capacity,
+ * the length of gid_sorted.  If it fits, *overflow = 0.  If it does not,
+ * *overflow = 1 and every tile list and every Gaussian's pair range
+ * (pair_offset) is emptied, so the forward and backward that follow stay in
+ * bounds and produce a zero image and zero gradients; the caller re-runs with
+ * capacity >= the total once it reads the flag.  In OSS_BIN_FULL mode the
+ * total is n * num_tiles, checked on the host (capacity below it is an error).
+ * tile_count is consumed (its contents are unspecified afterwards).
  * ------------------------------------------------------------------------- */
-OSS_API int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles);
+OSS_API int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles);
 OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
-                  const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
-                  int32_t* gid_sorted, int32_t* tile_offsets,
+                  const int32_t* aabb, int32_t* pair_offset, int32_t* tile_count,
+                  const int64_t* total_pairs, int64_t capacity,
+                  int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow,
                   void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -123,7 +138,9 @@ OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
  * Same gradients as _C.rasterize_backward + _C.conic_to_scale_rot_grad
  * (rasterizer_bwd.cu:32-154) without atomics.
  * d_feat is the gradient w.r.t. feat (not feat'); d_opacity, d_scale, d_rot
- * may be NULL.
+ * may be NULL.  total_pairs may be the exact pair count or any upper bound of
+ * it, such as the capacity given to oss_bin_pairs: the kernels take the list
+ * lengths from tile_offsets and pair_offset on the device.
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_t num_tiles);
 OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,

@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 2; }
+int oss_abi_version(void) { return 3; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -93,7 +93,7 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
     OSS_CHECK(conic != nullptr && aabb != nullptr && pair_count != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
     OSS_CHECK(aligned(aabb, 16), OSS_ERR_INVALID, "aabb must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_count, nullptr,
-                                        nullptr, as_stream(stream)));
+                                        nullptr, nullptr, as_stream(stream)));
     return OSS_OK;
 }
 
@@ -101,13 +101,16 @@ int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_fused_scr
 
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
                        const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                       int64_t* total_pairs, void* scratch, int64_t scratch_bytes, void* stream) {
+                       int64_t* total_pairs, int32_t* tile_count, void* scratch, int64_t scratch_bytes,
+                       void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
     if ((rc = check_mode(mode)) != OSS_OK) return rc;
     if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
     OSS_CHECK(pair_offset != nullptr && total_pairs != nullptr, OSS_ERR_INVALID, "pair_offset and total_pairs must be non-null");
+    OSS_CHECK(mode == OSS_BIN_FULL || g.tiles == 0 || tile_count != nullptr, OSS_ERR_INVALID,
+              "tile_count must be non-null");
     OSS_CHECK(scratch_bytes >= oss_render_prepare_scratch_bytes(n), OSS_ERR_SCRATCH, "render_prepare scratch too small");
     if (g.n > 0) {
         OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
@@ -117,36 +120,38 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
     long long* block_sums = static_cast<long long*>(scratch);
     OSS_CHECK(g.n == 0 || (block_sums != nullptr && aligned(block_sums, 8)), OSS_ERR_INVALID,
               "scratch must be 8-byte aligned");
+    int32_t* counts = mode == OSS_BIN_FULL ? nullptr : tile_count;
+    if (counts != nullptr && g.tiles > 0) OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * g.tiles, s));
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
-                                        block_sums, s));
+                                        block_sums, counts, s));
     OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, s));
     return OSS_OK;
 }
 
-int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t total_pairs, int64_t num_tiles) {
+int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
     (void)n;
-    if (total_pairs < 0) total_pairs = 0;
+    if (capacity < 0) capacity = 0;
     if (num_tiles < 0) num_tiles = 0;
-    const uint32_t key_limit = num_tiles > 0 ? static_cast<uint32_t>(num_tiles - 1) : 0u;
-    return oss::arena_bytes(total_pairs, 4) * 2 + oss::arena_bytes(num_tiles, 4) + oss::scan_scratch_bytes(num_tiles) +
-           oss::radix_scratch_bytes(total_pairs, key_limit);
+    return oss::tile_lists_scratch_bytes(capacity, num_tiles);
 }
 
-int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, const int32_t* pair_offset,
-                  int64_t total_pairs, int32_t* gid_sorted, int32_t* tile_offsets, void* scratch,
-                  int64_t scratch_bytes, void* stream) {
+int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, int32_t* pair_offset,
+                  int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, int32_t* gid_sorted,
+                  int32_t* tile_offsets, int32_t* overflow, void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
     if ((rc = check_mode(mode)) != OSS_OK) return rc;
-    OSS_CHECK(total_pairs >= 0, OSS_ERR_INVALID, "total pair count must be non-negative");
-    OSS_CHECK(total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
-    OSS_CHECK(tile_offsets != nullptr, OSS_ERR_INVALID, "tile_offsets must be non-null");
-    OSS_CHECK(total_pairs == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
+    OSS_CHECK(capacity >= 0, OSS_ERR_INVALID, "capacity must be non-negative");
+    OSS_CHECK(capacity <= INT_MAX, OSS_ERR_RANGE, "capacity exceeds int32 range");
+    OSS_CHECK(tile_offsets != nullptr && overflow != nullptr, OSS_ERR_INVALID,
+              "tile_offsets and overflow must be non-null");
+    OSS_CHECK(capacity == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
     cudaStream_t s = as_stream(stream);
     if (mode == OSS_BIN_FULL) {
-        OSS_CHECK(static_cast<int64_t>(g.n) * g.tiles == total_pairs, OSS_ERR_INVALID,
-                  "full-frame binning needs total_pairs == N * num_tiles");
+        OSS_CHECK(static_cast<int64_t>(g.n) * g.tiles <= capacity, OSS_ERR_RANGE,
+                  "full-frame binning needs capacity >= N * num_tiles");
+        OSS_CUDA_TRY(cudaMemsetAsync(overflow, 0, sizeof(int32_t), s));
         if (g.tiles == 0) {
             OSS_CUDA_TRY(cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t), s));
             return OSS_OK;
@@ -154,22 +159,14 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
         OSS_CUDA_TRY(oss::launch_full_tile_pairs(g.n, g.tiles, gid_sorted, tile_offsets, s));
         return OSS_OK;
     }
-    OSS_CHECK(scratch_bytes >= oss_bin_pairs_scratch_bytes(n, total_pairs, g.tiles), OSS_ERR_SCRATCH,
+    OSS_CHECK(scratch_bytes >= oss_bin_pairs_scratch_bytes(n, capacity, g.tiles), OSS_ERR_SCRATCH,
               "bin_pairs scratch too small");
-    OSS_CHECK(g.n == 0 || (aabb != nullptr && pair_offset != nullptr && aligned(aabb, 16)), OSS_ERR_INVALID,
-              "aabb (16-byte aligned) and pair_offset must be non-null");
-    oss::Arena arena{static_cast<char*>(scratch), scratch_bytes, 0};
-    uint32_t* keys = arena.take<uint32_t>(total_pairs);
-    int32_t* vals = arena.take<int32_t>(total_pairs);
-    int32_t* tile_count = arena.take<int32_t>(g.tiles);
-    void* scan_scratch = arena.base + arena.used;
-    arena.used += oss::scan_scratch_bytes(g.tiles);
-    void* radix_scratch = arena.base + arena.used;
-    if (g.tiles > 0) OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * g.tiles, s));
-    OSS_CUDA_TRY(oss::launch_expand_pairs(g.n, g.ntx, aabb, pair_offset, keys, vals, tile_count, s));
-    OSS_CUDA_TRY(oss::scan_exclusive_i32(tile_count, tile_offsets, g.tiles, true, nullptr, scan_scratch, s));
-    const uint32_t key_limit = g.tiles > 0 ? static_cast<uint32_t>(g.tiles - 1) : 0u;
-    OSS_CUDA_TRY(oss::radix_sort_pairs(keys, vals, total_pairs, key_limit, gid_sorted, radix_scratch, s));
+    OSS_CHECK(g.n == 0 || g.tiles == 0 ||
+                  (aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr && tile_count != nullptr &&
+                   total_pairs != nullptr && scratch != nullptr),
+              OSS_ERR_INVALID, "aabb (16-byte aligned), pair_offset, tile_count, total_pairs and scratch must be non-null");
+    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
+                                       gid_sorted, tile_offsets, overflow, scratch, s));
     return OSS_OK;
 }
 

@@ -48,20 +48,28 @@ cudaError_t radix_sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, uint32_t 
 // ---- preprocess.cu ---------------------------------------------------------
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count,
-                              float* geo, long long* block_sums, cudaStream_t stream);
+                              float* geo, long long* block_sums, int32_t* tile_count, cudaStream_t stream);
 cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
 cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
                                            const float* d_conic, float* d_scale, float* d_rot,
                                            cudaStream_t stream);
 
 // ---- binning.cu ------------------------------------------------------------
-cudaError_t launch_expand_pairs(int n, int ntx, const int32_t* aabb, const int32_t* pair_offset,
-                                uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
 cudaError_t launch_full_tile_pairs(int n, int num_tiles, int32_t* gid_sorted, int32_t* tile_offsets,
                                    cudaStream_t stream);
 cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const int32_t* gid,
                              uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
 cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
+
+// ---- tile_lists.cu --------------------------------------------------------
+// Per-tile lists from the preprocess tile counts (consumed): scan, atomic
+// scatter, per-tile sort.  The pair total is read from *total_pairs on the
+// device; above capacity every list and pair range is emptied and *overflow = 1.
+int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles);
+cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
+                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
+                             int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,
+                             cudaStream_t stream);
 
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);

@@ -17,7 +17,9 @@ __device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, c
 
 // One CTA per kPrepTile Gaussians (kPrepTile / kPrepThreads per thread, strided
 // for coalescing).  With block_sums non-null the CTA also writes the sum of its
-// pair counts: the reduce half of the gid-major pair-offset scan.
+// pair counts: the reduce half of the gid-major pair-offset scan.  With
+// tile_count non-null every Gaussian adds one to each tile of its rectangle
+// (fire-and-forget reductions): the per-tile list lengths.
 __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int nty, int mode,
                                                               const float2* __restrict__ xy,
                                                               const float2* __restrict__ scale,
@@ -26,7 +28,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
                                                               int4* __restrict__ aabb,
                                                               int32_t* __restrict__ count,
                                                               float* __restrict__ geo,
-                                                              long long* __restrict__ block_sums) {
+                                                              long long* __restrict__ block_sums,
+                                                              int32_t* __restrict__ tile_count) {
     long long local = 0;
 #pragma unroll
     for (int it = 0; it < kPrepTile / kPrepThreads; ++it) {
@@ -50,6 +53,11 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
         count[g] = cnt;
         local += cnt;
         if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
+        if (tile_count != nullptr && cnt > 0) {
+            for (int ty = box.y; ty < box.w; ++ty) {
+                for (int tx = box.x; tx < box.z; ++tx) atomicAdd(&tile_count[ty * ntx + tx], 1);
+            }
+        }
     }
     if (block_sums != nullptr) {
         __shared__ long long s_part[kPrepThreads / 32];
@@ -97,11 +105,11 @@ __global__ void __launch_bounds__(kThreads) k_conic_to_scale_rot_grad(int n, con
 
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count, float* geo,
-                              long long* block_sums, cudaStream_t stream) {
+                              long long* block_sums, int32_t* tile_count, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
     k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPrepThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
-        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums);
+        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count);
     return cudaGetLastError();
 }
 

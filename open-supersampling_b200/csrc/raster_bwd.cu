@@ -189,7 +189,6 @@ __device__ __forceinline__ void bwd_rows_edge(const float* __restrict__ s_go, in
                                               int ty0, float gx, float gy, float A, float B, float D,
                                               const float (&fv)[FC], float (&dF)[FC], float& Sx, float& Sy,
                                               float& Sxx, float& Sxy, float& Syy) {
-    constexpr int SG = BwdCfg<FC>::SG;
     constexpr int ROW = BwdCfg<FC>::ROW;
     for (int r = r0; r < r1; ++r) {
         const float dy = static_cast<float>(ty0 + r) - gy;
@@ -236,7 +235,6 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
     float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy, float* __restrict__ d_conic,
     float* __restrict__ d_feat) {
     constexpr int SG = BwdCfg<FC>::SG;
-    constexpr int ROW = BwdCfg<FC>::ROW;
     extern __shared__ float4 s_mem4[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;

@@ -1,0 +1,273 @@
+// Per-tile Gaussian lists by scatter + per-tile sort.
+//
+// The reference builds its tile lists by sorting (tile << 32 | gid) keys
+// (rasterizer_fwd.cu:461-468): each tile's list holds, ascending, the gids of
+// the Gaussians whose tile rectangle covers the tile.  Here the per-tile counts
+// come from the preprocess kernel, their exclusive scan gives every tile its
+// list offset, each (Gaussian, tile) pair claims a slot of its tile with an
+// atomic (in no particular order), and every tile's list is then sorted.  A
+// Gaussian covers a tile at most once, so a sorted list is unique: the output
+// is the reference's list whatever order the atomics ran in.
+//
+// The pair total is read on the device and checked against the caller's
+// capacity; on overflow every list and every Gaussian's pair range is emptied
+// and a flag is raised, so nothing downstream reads or writes past capacity and
+// the host need not wait for the total before launching.
+#include <limits.h>
+
+#include "internal.h"
+#include "oss_common.cuh"
+
+namespace oss {
+namespace {
+
+constexpr int kScatterThreads = 256;
+constexpr int kScatterWarps = kScatterThreads / 32;
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortBuf = 8192;                    // ints of shared memory per CTA (32 KB)
+constexpr int kWarpCap = kSortBuf / kSortWarps;   // lists up to 1024 sorted by one warp
+constexpr int kCtaCap = kSortBuf;                 // lists up to 8192 sorted by the CTA
+constexpr int kWindowBits = kSortBuf * 32;        // gid window of the bitmap path
+
+// One warp per 32 consecutive Gaussians.  The warp's pairs are dealt round-robin
+// to its lanes (lane j of round r takes the warp's pair 32 r + j); the owning
+// Gaussian is found by a binary search over the lanes' pair prefix.
+__global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
+    int n, int ntx, int num_tiles, const int4* __restrict__ aabb, int32_t* __restrict__ pair_offset,
+    int32_t* __restrict__ tile_count, int32_t* __restrict__ tile_offsets, const int64_t* __restrict__ total_pairs,
+    int64_t capacity, int32_t* __restrict__ unsorted, int32_t* __restrict__ overflow) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kScatterThreads;
+    if (*total_pairs > capacity) {
+        // empty every list and every pair range; the image and gradients come out zero
+        for (int64_t i = tid; i <= num_tiles; i += nthreads) tile_offsets[i] = 0;
+        for (int64_t i = tid; i <= n; i += nthreads) pair_offset[i] = 0;
+        if (tid == 0) *overflow = 1;
+        return;
+    }
+    if (tid == 0) *overflow = 0;
+    const int lane = threadIdx.x & 31;
+    const int g0 = (blockIdx.x * kScatterWarps + (threadIdx.x >> 5)) * 32;
+    const int g = g0 + lane;
+    int4 box = make_int4(0, 0, 0, 0);
+    if (g < n) box = aabb[g];
+    const int bw = box.z > box.x ? box.z - box.x : 0;
+    const int bh = box.w > box.y ? box.w - box.y : 0;
+    const int cnt = bw * bh;
+    // inclusive then exclusive warp prefix of the pair counts
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+    }
+    const int start = incl - cnt;
+    const int warp_total = __shfl_sync(0xffffffffu, incl, 31);
+    for (int base = 0; base < warp_total; base += 32) {
+        const int j = base + lane;
+        int owner = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int cand = owner + step;
+            const int s = __shfl_sync(0xffffffffu, start, cand);
+            if (s <= j) owner = cand;
+        }
+        const int o_start = __shfl_sync(0xffffffffu, start, owner);
+        const int o_x = __shfl_sync(0xffffffffu, box.x, owner);
+        const int o_y = __shfl_sync(0xffffffffu, box.y, owner);
+        const int o_w = __shfl_sync(0xffffffffu, bw, owner);
+        if (j < warp_total) {
+            const int k = j - o_start;
+            const int dy = k / o_w;
+            const int t = (o_y + dy) * ntx + o_x + (k - dy * o_w);
+            const int slot = atomicSub(&tile_count[t], 1) - 1;
+            unsorted[tile_offsets[t] + slot] = g0 + owner;
+        }
+    }
+}
+
+__device__ __forceinline__ int next_pow2(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+// Ascending bitonic sort of s[0..lp), lp a power of two, by `nt` cooperating
+// threads (a warp or the CTA) with index `tid`.
+template <bool kCta>
+__device__ __forceinline__ void bitonic_sort(int32_t* s, int lp, int tid, int nt) {
+    for (int k = 2; k <= lp; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < (lp >> 1); i += nt) {
+                const int a = (i << 1) - (i & (j - 1));
+                const int b = a + j;
+                const int32_t x = s[a];
+                const int32_t y = s[b];
+                const bool ascending = (a & k) == 0;
+                if ((x > y) == ascending) {
+                    s[a] = y;
+                    s[b] = x;
+                }
+            }
+            if (kCta) {
+                __syncthreads();
+            } else {
+                __syncwarp();
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ int block_exclusive_sum(int v, int* s_warp, int& total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+        const int c = s_warp[w];
+        before += w < warp ? c : 0;
+        total += c;
+    }
+    __syncthreads();
+    return before + x - v;
+}
+
+// Lists longer than kCtaCap: the CTA marks the gids of one window of the gid
+// range in a shared bitmap and writes the set bits out in order, window by
+// window.  Cost per window: one pass over the list plus the bitmap.
+__device__ void bitmap_sort(const int32_t* __restrict__ in, int32_t* __restrict__ out, int len, int n,
+                            int32_t* s_buf, int* s_warp) {
+    uint32_t* bm = reinterpret_cast<uint32_t*>(s_buf);
+    constexpr int kWordsPerThread = kSortBuf / kSortThreads;
+    int written = 0;
+    for (int64_t base = 0; base < n; base += kWindowBits) {
+        for (int i = threadIdx.x; i < kSortBuf; i += kSortThreads) bm[i] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < len; i += kSortThreads) {
+            const int64_t r = static_cast<int64_t>(in[i]) - base;
+            if (r >= 0 && r < kWindowBits) atomicOr(&bm[r >> 5], 1u << (r & 31));
+        }
+        __syncthreads();
+        const int w0 = threadIdx.x * kWordsPerThread;
+        int cnt = 0;
+#pragma unroll 8
+        for (int w = 0; w < kWordsPerThread; ++w) cnt += __popc(bm[w0 + w]);
+        int total;
+        int pos = written + block_exclusive_sum(cnt, s_warp, total);
+        for (int w = 0; w < kWordsPerThread; ++w) {
+            uint32_t bits = bm[w0 + w];
+            while (bits != 0u) {
+                const int b = __ffs(static_cast<int>(bits)) - 1;
+                bits &= bits - 1u;
+                out[pos++] = static_cast<int32_t>(base + (w0 + w) * 32 + b);
+            }
+        }
+        written += total;
+        __syncthreads();
+    }
+}
+
+// One warp per tile; lists above kWarpCap are sorted afterwards by the whole CTA.
+__global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tiles,
+                                                              const int32_t* __restrict__ tile_offsets,
+                                                              const int32_t* __restrict__ unsorted,
+                                                              int32_t* __restrict__ gid_sorted) {
+    __shared__ int32_t s_buf[kSortBuf];
+    __shared__ int s_warp[kSortWarps];
+    __shared__ int s_big;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_big = 0;
+    __syncthreads();
+    const int t = blockIdx.x * kSortWarps + warp;
+    int off = 0;
+    int len = 0;
+    if (t < num_tiles) {
+        off = tile_offsets[t];
+        len = tile_offsets[t + 1] - off;
+    }
+    const int32_t* src = unsorted + off;
+    int32_t* dst = gid_sorted + off;
+    if (len <= 32) {
+        // rank of each value among the (distinct) values of the warp
+        const int32_t v = lane < len ? src[lane] : INT_MAX;
+        int rank = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, v, j) < v ? 1 : 0;
+        if (lane < len) dst[rank] = v;
+    } else if (len <= kWarpCap) {
+        int32_t* s = s_buf + warp * kWarpCap;
+        const int lp = next_pow2(len);
+        for (int i = lane; i < lp; i += 32) s[i] = i < len ? src[i] : INT_MAX;
+        __syncwarp();
+        bitonic_sort<false>(s, lp, lane, 32);
+        for (int i = lane; i < len; i += 32) dst[i] = s[i];
+    } else if (lane == 0) {
+        atomicOr(&s_big, 1 << warp);
+    }
+    __syncthreads();
+    const int big = s_big;
+    for (int wv = 0; wv < kSortWarps; ++wv) {
+        if ((big >> wv & 1) == 0) continue;
+        const int bt = blockIdx.x * kSortWarps + wv;
+        const int boff = tile_offsets[bt];
+        const int blen = tile_offsets[bt + 1] - boff;
+        if (blen <= kCtaCap) {
+            const int lp = next_pow2(blen);
+            for (int i = threadIdx.x; i < lp; i += kSortThreads) s_buf[i] = i < blen ? unsorted[boff + i] : INT_MAX;
+            __syncthreads();
+            bitonic_sort<true>(s_buf, lp, threadIdx.x, kSortThreads);
+            for (int i = threadIdx.x; i < blen; i += kSortThreads) gid_sorted[boff + i] = s_buf[i];
+            __syncthreads();
+        } else {
+            bitmap_sort(unsorted + boff, gid_sorted + boff, blen, n, s_buf, s_warp);
+        }
+    }
+}
+
+__global__ void k_empty_lists(int num_tiles, int32_t* __restrict__ tile_offsets, int32_t* __restrict__ overflow) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i <= num_tiles) tile_offsets[i] = 0;
+    if (i == 0 && overflow != nullptr) *overflow = 0;
+}
+
+}  // namespace
+
+int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles) {
+    return arena_bytes(capacity, sizeof(int32_t)) + scan_scratch_bytes(num_tiles);
+}
+
+cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
+                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, int32_t* gid_sorted,
+                             int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream) {
+    if (n == 0 || num_tiles == 0) {
+        k_empty_lists<<<static_cast<unsigned>(div_up(static_cast<int64_t>(num_tiles) + 1, 256)), 256, 0, stream>>>(
+            num_tiles, tile_offsets, overflow);
+        return cudaGetLastError();
+    }
+    Arena arena{static_cast<char*>(scratch), tile_lists_scratch_bytes(capacity, num_tiles), 0};
+    int32_t* unsorted = arena.take<int32_t>(capacity);
+    void* scan_scratch = arena.base + arena.used;
+    cudaError_t err = scan_exclusive_i32(tile_count, tile_offsets, num_tiles, true, nullptr, scan_scratch, stream);
+    if (err != cudaSuccess) return err;
+    k_scatter_pairs<<<static_cast<unsigned>(div_up(n, kScatterThreads)), kScatterThreads, 0, stream>>>(
+        n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, tile_count, tile_offsets, total_pairs,
+        capacity, unsorted, overflow);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    k_sort_tiles<<<static_cast<unsigned>(div_up(num_tiles, kSortWarps)), kSortThreads, 0, stream>>>(
+        n, num_tiles, tile_offsets, unsorted, gid_sorted);
+    return cudaGetLastError();
+}
+
+}  // namespace oss

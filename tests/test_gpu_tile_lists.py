@@ -1,0 +1,225 @@
+"""Tile lists by scatter + per-tile sort: bit-exact against the oracle's sorted
+(tile << 32 | gid) lists in every sort tier, the device-side capacity check,
+and the sync-free path captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as orc
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT}
+
+
+def dev(a, dtype=torch.float32):
+    return torch.as_tensor(np.asarray(a), dtype=dtype).cuda().contiguous()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def clustered(n, h, w, seed, scale, spread=0.0):
+    """n Gaussians of about `scale` px around the frame centre (+- spread px)."""
+    rng = np.random.default_rng(seed)
+    xy = (np.array([w, h]) / 2 + (rng.random((n, 2)) - 0.5) * 2 * spread).astype(np.float32)
+    s = (scale * (0.8 + 0.4 * rng.random((n, 2)))).astype(np.float32)
+    rot = (rng.random(n) * 3.14).astype(np.float32)
+    return xy, s, rot
+
+
+class Lists:
+    """prepare + bin over the C ABI with an explicit pair capacity."""
+
+    def __init__(self, xy, scale, rot, h, w, mode):
+        from oss_cuda import _lib
+
+        self.lib, self.chk = _lib.lib(), _lib.check
+        self.n, self.h, self.w, self.mode = int(xy.shape[0]), h, w, mode
+        self.tiles = ((w + 15) // 16) * ((h + 15) // 16)
+        i32 = dict(device="cuda", dtype=torch.int32)
+        f32 = dict(device="cuda", dtype=torch.float32)
+        n = self.n
+        self.xy, self.scale, self.rot = dev(xy), dev(scale), dev(rot)
+        self.conic = torch.empty((n, 3), **f32)
+        self.aabb = torch.empty((n, 4), **i32)
+        self.pair_offset = torch.empty((n + 1,), **i32)
+        self.geo = torch.empty((n, 8), **f32)
+        self.total = torch.empty((1,), device="cuda", dtype=torch.int64)
+        self.tile_count = torch.empty((max(1, self.tiles),), **i32)
+        self.tile_offsets = torch.empty((self.tiles + 1,), **i32)
+        self.overflow = torch.full((1,), -1, **i32)
+        self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device="cuda",
+                                        dtype=torch.uint8)
+
+    def set_capacity(self, capacity):
+        self.capacity = capacity
+        self.gid = torch.full((max(1, capacity),), -7, device="cuda", dtype=torch.int32)
+        nb = self.lib.oss_bin_pairs_scratch_bytes(self.n, capacity, self.tiles)
+        self.scratch = torch.empty((max(1, nb),), device="cuda", dtype=torch.uint8)
+
+    def run(self):
+        s = torch.cuda.current_stream().cuda_stream
+        self.chk(self.lib.oss_render_prepare(self.n, self.h, self.w, self.mode, self.xy.data_ptr(),
+                                             self.scale.data_ptr(), self.rot.data_ptr(), self.conic.data_ptr(),
+                                             self.aabb.data_ptr(), self.pair_offset.data_ptr(), self.geo.data_ptr(),
+                                             self.total.data_ptr(), self.tile_count.data_ptr(),
+                                             self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
+        self.chk(self.lib.oss_bin_pairs(self.n, self.h, self.w, self.mode, self.aabb.data_ptr(),
+                                        self.pair_offset.data_ptr(), self.tile_count.data_ptr(),
+                                        self.total.data_ptr(), self.capacity, self.gid.data_ptr(),
+                                        self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
+                                        self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
+
+
+def check_lists(xy, scale, rot, h, w, mode, slack=0):
+    _, _, _, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, MODES[mode])
+    L = Lists(xy, scale, rot, h, w, MODES[mode])
+    L.set_capacity(int(g_ref.size) + slack)
+    L.run()
+    assert int(L.overflow.item()) == 0
+    assert int(L.total.item()) == g_ref.size
+    np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
+    np.testing.assert_array_equal(host(L.gid)[:g_ref.size], g_ref)
+    return o_ref
+
+
+# list lengths chosen to land in each sort tier: <= 32 (warp ranks), <= 1024 (warp
+# bitonic), <= 8192 (CTA bitonic), > 8192 (bitmap, one or two gid windows)
+@pytest.mark.parametrize("n,h,w,scale,tier_len", [
+    (30, 32, 32, 20.0, 30),
+    (700, 32, 48, 30.0, 700),
+    (5000, 48, 48, 40.0, 5000),
+    (20000, 32, 32, 40.0, 20000),
+    (300_000, 16, 16, 10.0, 300_000),
+])
+def test_sort_tiers_bit_exact(cuda_device, n, h, w, scale, tier_len):
+    xy, s, rot = clustered(n, h, w, seed=n, scale=scale)
+    o_ref = check_lists(xy, s, rot, h, w, "tight3sigma")
+    assert np.diff(o_ref).max() == tier_len
+
+
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact"])
+def test_mixed_tiers_in_one_frame(cuda_device, mode):
+    """Long lists (a dense cluster of large Gaussians) next to short ones in the
+    same CTA's group of tiles."""
+    rng = np.random.default_rng(3)
+    h, w = 256, 384
+    xy_c, s_c, rot_c = clustered(12_000, h, w, seed=5, scale=6.0, spread=40.0)
+    n2 = 4000
+    xy_r = (rng.random((n2, 2)) * np.array([w, h])).astype(np.float32)
+    s_r = np.exp(rng.standard_normal((n2, 2)) * 0.3 + np.log(1.5)).astype(np.float32)
+    rot_r = (rng.random(n2) * 3.14).astype(np.float32)
+    perm = rng.permutation(12_000 + n2)
+    xy = np.concatenate([xy_c, xy_r])[perm]
+    s = np.concatenate([s_c, s_r])[perm]
+    rot = np.concatenate([rot_c, rot_r])[perm]
+    o_ref = check_lists(xy, s, rot, h, w, mode, slack=1000)
+    lens = np.diff(o_ref)
+    assert lens.max() > 1024 and lens.min() <= 1024
+
+
+@pytest.mark.parametrize("n,h,w", [(0, 64, 64), (1, 16, 16), (5, 1, 1), (257, 37, 91), (200_000, 1080, 1920)])
+def test_lists_edge_sizes(cuda_device, n, h, w):
+    rng = np.random.default_rng(n)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    s = (rng.random((n, 2)) * 3.5 + 0.5).astype(np.float32)
+    rot = (rng.random(n) * 6.28).astype(np.float32)
+    check_lists(xy, s, rot, h, w, "tight3sigma", slack=17)
+
+
+def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
+    from oss_cuda import _lib
+
+    h, w, n = 96, 160, 3000
+    rng = np.random.default_rng(11)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    s = (rng.random((n, 2)) * 3.0 + 0.5).astype(np.float32)
+    rot = (rng.random(n) * 6.28).astype(np.float32)
+    feat = dev(rng.random((n, 3)))
+    _, _, _, g_ref, o_ref = orc.lists(xy, s, rot, h, w, orc.TIGHT)
+    L = Lists(xy, s, rot, h, w, orc.TIGHT)
+    L.set_capacity(int(g_ref.size) - 1)
+    L.run()
+    assert int(L.overflow.item()) == 1
+    assert int(L.total.item()) == g_ref.size
+    assert not host(L.tile_offsets).any()
+    assert not host(L.pair_offset).any()
+    # downstream stages stay in bounds and produce zeros
+    lib, s_ = L.lib, torch.cuda.current_stream().cuda_stream
+    img = torch.full((3, h, w), 5.0, device="cuda")
+    _lib.check(lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
+                                      L.tile_offsets.data_ptr(), img.data_ptr(), s_), "forward")
+    assert not host(img).any()
+    grad = dev(rng.standard_normal((3, h, w)))
+    nb = lib.oss_render_backward_scratch_bytes(L.capacity, 3, L.tiles)
+    scratch = torch.empty((nb,), device="cuda", dtype=torch.uint8)
+    outs = [torch.full(sh, 9.0, device="cuda") for sh in ((n, 2), (n, 3), (n, 3))]
+    _lib.check(lib.oss_render_backward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, None, None,
+                                       L.aabb.data_ptr(), L.pair_offset.data_ptr(), L.capacity, L.gid.data_ptr(),
+                                       L.tile_offsets.data_ptr(), grad.data_ptr(), outs[0].data_ptr(),
+                                       outs[1].data_ptr(), outs[2].data_ptr(), None, None, None, scratch.data_ptr(),
+                                       scratch.numel(), s_), "backward")
+    for t in outs:
+        assert not host(t).any()
+    # the same buffers with enough room: flag cleared, lists exact
+    L.set_capacity(int(g_ref.size))
+    L.run()
+    assert int(L.overflow.item()) == 0
+    np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
+    np.testing.assert_array_equal(host(L.gid), g_ref)
+
+
+def test_sync_free_path_replays_in_cuda_graph(cuda_device):
+    """prepare -> bin -> forward captured once, replayed on new Gaussians copied
+    into the same input buffers: lists and image follow the new inputs."""
+    from oss_cuda import _lib
+
+    h, w, n = 128, 192, 4000
+    rng = np.random.default_rng(21)
+
+    def draw():
+        xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+        s = (rng.random((n, 2)) * 3.0 + 0.5).astype(np.float32)
+        rot = (rng.random(n) * 6.28).astype(np.float32)
+        return xy, s, rot, rng.random((n, 3)).astype(np.float32)
+
+    xy0, s0, r0, f0 = draw()
+    L = Lists(xy0, s0, r0, h, w, orc.TIGHT)
+    feat = dev(f0)
+    img = torch.empty((3, h, w), device="cuda")
+    L.set_capacity(4 * int(orc.lists(xy0, s0, r0, h, w, orc.TIGHT)[3].size))
+
+    def step():
+        L.run()
+        _lib.check(L.lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
+                                            L.tile_offsets.data_ptr(), img.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream), "forward")
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        xy, s, rot, f = draw()
+        L.xy.copy_(dev(xy))
+        L.scale.copy_(dev(s))
+        L.rot.copy_(dev(rot))
+        feat.copy_(dev(f))
+        graph.replay()
+        torch.cuda.synchronize()
+        c_ref, _, _, g_ref, o_ref = orc.lists(xy, s, rot, h, w, orc.TIGHT)
+        assert int(L.overflow.item()) == 0
+        np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
+        np.testing.assert_array_equal(host(L.gid)[:g_ref.size], g_ref)
+        assert_close(host(img), orc.render_forward(xy, c_ref, f, g_ref, o_ref, h, w), what="graph image")
+    del graph
