@@ -184,7 +184,7 @@ class Pipeline:
         self.pair_offset = torch.empty((n + 1,), **i32)
         self.geo = torch.empty((n, 8), **f32)
         self.total = torch.empty((1,), device=device, dtype=torch.int64)
-        self.tile_count = torch.empty((max(1, self.tiles),), **i32)
+        self.tile_count = torch.empty((max(1, self.lib.oss_tile_count_elems(self.tiles)),), **i32)
         self.overflow = torch.zeros((1,), **i32)
         self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device=device,
                                         dtype=torch.uint8)
@@ -224,8 +224,8 @@ class Pipeline:
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
                                    d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
                                    self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
-                                   self.tile_count.data_ptr(), self.prep_scratch.data_ptr(),
-                                   self.prep_scratch.numel(), s), "prepare")
+                                   self.tile_count.data_ptr(), self.tile_offsets.data_ptr(),
+                                   self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
         self._mark(1, timed)
         if sync or self.capacity == 0:
             self.pairs = int(self.total.item())
@@ -283,8 +283,8 @@ class Pipeline:
 
     def launches_per_step(self, backward=True):
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
-        prepare = 2                                   # k_preprocess, k_scan_apply
-        binning = scan_launches(self.tiles) + 2       # tile-offset scan, k_scatter_pairs, k_sort_tiles
+        prepare = 2                                   # k_preprocess, k_prepare_scan (pair + tile offsets)
+        binning = 2                                   # k_scatter_pairs, k_sort_tiles
         bwd = 1 + scan_launches(self.tiles) + 1 + 1   # k_item_counts, item scan, k_render_bwd, k_reduce_gaussian
         return prepare + binning + 1 + (bwd if backward else 0)
 

@@ -78,40 +78,43 @@ OSS_API int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, i
 
 /* ---------------------------------------------------------------------------
  * Render prepare: preprocess + gid-major pair-offset scan + geo records +
- * per-tile pair counts.
+ * per-tile pair counts and list offsets.
  * First half of _C.rasterize_forward (rasterizer_fwd.cu:478-545) and of
  * _C.pair_construction_only (rasterizer_fwd.cu:381-444).
  * Outputs: conic[n*3], aabb[n*4], pair_offset[n+1] (exclusive scan of the pair
  * counts; pair_offset[n] = total, valid only if total <= INT32_MAX),
- * geo[n*8], total_pairs[1] (int64, on the device) and tile_count[num_tiles]
- * (int32: how many Gaussians each tile's list will hold; input to
- * oss_bin_pairs, which consumes it).  tile_count may be NULL in OSS_BIN_FULL
- * mode, where it is not computed.
+ * geo[n*8], total_pairs[1] (int64, on the device), tile_offsets[T+1] (int32:
+ * where each tile's list will start; tile_offsets[T] = total) and
+ * tile_count[oss_tile_count_elems(T)] (the per-tile list lengths in the
+ * layout oss_bin_pairs reads; it consumes them).  In OSS_BIN_FULL mode
+ * tile_count and tile_offsets are not written and may be NULL.
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_prepare_scratch_bytes(int64_t n);
+OSS_API int64_t oss_tile_count_elems(int64_t num_tiles);
 OSS_API int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode,
                        const float* xy, const float* scale, const float* rot,
                        float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                       int64_t* total_pairs, int32_t* tile_count, void* scratch, int64_t scratch_bytes,
-                       void* stream);
+                       int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets,
+                       void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Deterministic tile binning of the pairs described by (aabb, pair_offset,
- * tile_count) from oss_render_prepare: gid_sorted lists, per tile in ascending
- * tile id, the Gaussians overlapping that tile in ascending gid order;
- * tile_offsets[T+1] brackets them.  Bit-exact with the reference's sort of
- * (tile << 32 | gid) keys plus searchsorted (rasterizer_fwd.cu:446-475) for the
- * same AABBs.
+ * tile_count, tile_offsets) from oss_render_prepare: gid_sorted lists, per
+ * tile in ascending tile id, the Gaussians overlapping that tile in ascending
+ * gid order; tile_offsets[T+1] brackets them.  Bit-exact with the reference's
+ * sort of (tile << 32 | gid) keys plus searchsorted (rasterizer_fwd.cu:446-475)
+ * for the same AABBs.
  *
  * No host synchronisation: the pair total is read on the device from
  * total_pairs (oss_render_prepare's int64 output) and compared with capacity,
  * the length of gid_sorted.  If it fits, *overflow = 0.  If it does not,
  * *overflow = 1 and every tile list and every Gaussian's pair range
- * (pair_offset) is emptied, so the forward and backward that follow stay in
- * bounds and produce a zero image and zero gradients; the caller re-runs with
- * capacity >= the total once it reads the flag.  In OSS_BIN_FULL mode the
- * total is n * num_tiles, checked on the host (capacity below it is an error).
- * tile_count is consumed (its contents are unspecified afterwards).
+ * (tile_offsets, pair_offset) is emptied, so the forward and backward that
+ * follow stay in bounds and produce a zero image and zero gradients; the
+ * caller re-runs with capacity >= the total once it reads the flag.  In
+ * OSS_BIN_FULL mode tile_offsets is written here and the total n * num_tiles
+ * is checked on the host (a capacity below it is an error).  tile_count is
+ * consumed (its contents are unspecified afterwards).
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles);
 OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,

@@ -99,18 +99,23 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
 
 int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_fused_scratch_bytes(n < 0 ? 0 : n); }
 
+int64_t oss_tile_count_elems(int64_t num_tiles) {
+    return (num_tiles < 0 ? 0 : num_tiles) * oss::kTileCountStride;
+}
+
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
                        const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                       int64_t* total_pairs, int32_t* tile_count, void* scratch, int64_t scratch_bytes,
-                       void* stream) {
+                       int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets, void* scratch,
+                       int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
     if ((rc = check_mode(mode)) != OSS_OK) return rc;
     if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
     OSS_CHECK(pair_offset != nullptr && total_pairs != nullptr, OSS_ERR_INVALID, "pair_offset and total_pairs must be non-null");
-    OSS_CHECK(mode == OSS_BIN_FULL || g.tiles == 0 || tile_count != nullptr, OSS_ERR_INVALID,
-              "tile_count must be non-null");
+    const bool lists = mode != OSS_BIN_FULL && g.tiles > 0;
+    OSS_CHECK(!lists || (tile_count != nullptr && tile_offsets != nullptr), OSS_ERR_INVALID,
+              "tile_count and tile_offsets must be non-null");
     OSS_CHECK(scratch_bytes >= oss_render_prepare_scratch_bytes(n), OSS_ERR_SCRATCH, "render_prepare scratch too small");
     if (g.n > 0) {
         OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
@@ -120,19 +125,21 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
     long long* block_sums = static_cast<long long*>(scratch);
     OSS_CHECK(g.n == 0 || (block_sums != nullptr && aligned(block_sums, 8)), OSS_ERR_INVALID,
               "scratch must be 8-byte aligned");
-    int32_t* counts = mode == OSS_BIN_FULL ? nullptr : tile_count;
-    if (counts != nullptr && g.tiles > 0) OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * g.tiles, s));
+    int32_t* counts = lists ? tile_count : nullptr;
+    if (counts != nullptr) {
+        OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
+    }
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
                                         block_sums, counts, s));
-    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, s));
+    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, counts,
+                                                 oss::kTileCountStride, g.tiles, lists ? tile_offsets : nullptr, s));
     return OSS_OK;
 }
 
 int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
     (void)n;
-    if (capacity < 0) capacity = 0;
-    if (num_tiles < 0) num_tiles = 0;
-    return oss::tile_lists_scratch_bytes(capacity, num_tiles);
+    (void)num_tiles;
+    return oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity);
 }
 
 int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, int32_t* pair_offset,
@@ -163,7 +170,7 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
               "bin_pairs scratch too small");
     OSS_CHECK(g.n == 0 || g.tiles == 0 ||
                   (aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr && tile_count != nullptr &&
-                   total_pairs != nullptr && scratch != nullptr),
+                   total_pairs != nullptr && (capacity == 0 || scratch != nullptr)),
               OSS_ERR_INVALID, "aabb (16-byte aligned), pair_offset, tile_count, total_pairs and scratch must be non-null");
     OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
                                        gid_sorted, tile_offsets, overflow, scratch, s));

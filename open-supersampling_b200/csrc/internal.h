@@ -35,8 +35,15 @@ constexpr int kPrepThreads = 256;
 constexpr int kPrepTile = 1024;
 int64_t scan_fused_scratch_bytes(int64_t n);
 // Second half of the fused scan: out[0..n) = exclusive scan, out[n] = total.
+// With tile_count non-null the same launch also scans the per-tile pair counts
+// (spaced count_stride ints apart) into tile_offsets[0..num_tiles].
 cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t n, const long long* block_sums,
-                                       int64_t* total_out, cudaStream_t stream);
+                                       int64_t* total_out, const int32_t* tile_count, int count_stride,
+                                       int64_t num_tiles, int32_t* tile_offsets, cudaStream_t stream);
+
+// Per-tile pair counters are spaced one 128-byte line apart: the preprocess and
+// scatter atomics then spread over num_tiles lines instead of num_tiles / 32.
+constexpr int kTileCountStride = 32;
 
 // ---- radix.cu --------------------------------------------------------------
 // Stable LSD sort of (key, val) pairs by key in [0, key_limit].  The sorted vals
@@ -62,10 +69,11 @@ cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const
 cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
 
 // ---- tile_lists.cu --------------------------------------------------------
-// Per-tile lists from the preprocess tile counts (consumed): scan, atomic
-// scatter, per-tile sort.  The pair total is read from *total_pairs on the
-// device; above capacity every list and pair range is emptied and *overflow = 1.
-int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles);
+// Per-tile lists from the tile counts and offsets of render prepare (the
+// counts are consumed): atomic scatter, then a per-tile sort.  The pair total
+// is read from *total_pairs on the device; above capacity every list and pair
+// range is emptied and *overflow = 1.
+int64_t tile_lists_scratch_bytes(int64_t capacity);
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
                              int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
                              int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,

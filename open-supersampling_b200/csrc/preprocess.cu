@@ -19,7 +19,8 @@ __device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, c
 // for coalescing).  With block_sums non-null the CTA also writes the sum of its
 // pair counts: the reduce half of the gid-major pair-offset scan.  With
 // tile_count non-null every Gaussian adds one to each tile of its rectangle
-// (fire-and-forget reductions): the per-tile list lengths.
+// (fire-and-forget reductions into counters kTileCountStride ints apart): the
+// per-tile list lengths.
 __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int nty, int mode,
                                                               const float2* __restrict__ xy,
                                                               const float2* __restrict__ scale,
@@ -55,7 +56,9 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
         if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
         if (tile_count != nullptr && cnt > 0) {
             for (int ty = box.y; ty < box.w; ++ty) {
-                for (int tx = box.x; tx < box.z; ++tx) atomicAdd(&tile_count[ty * ntx + tx], 1);
+                for (int tx = box.x; tx < box.z; ++tx) {
+                    atomicAdd(&tile_count[static_cast<int64_t>(ty * ntx + tx) * kTileCountStride], 1);
+                }
             }
         }
     }

@@ -9,6 +9,10 @@
 //   q' = dy*(D*dy + B*dx) + A*dx*dx   (= -0.5*log2(e) * q)
 // the per-Gaussian terms B*dx and A*dx*dx are shared by the thread's PX
 // pixels, so a pixel costs 1 FADD + 2 FFMA for q', one MUFU ex2 and F FFMAs.
+// With PX even the pixels are processed in pairs on the packed f32x2 pipe
+// (FADD2 / FFMA2: two IEEE round-to-nearest operations per instruction, the
+// same results as the scalar form), which halves the FP32 issue slots and
+// leaves the ex2 (MUFU, 16 per SM per clock) as the bound.
 //
 // The reference zeroes a weight when q is non-finite or negative
 // (rasterizer_fwd.cu:245).  A batch whose conics are all finite and
@@ -68,6 +72,52 @@ __device__ __forceinline__ void fwd_batch(int cnt, const float4* __restrict__ s_
     }
 }
 
+// fwd_batch on pixel pairs: acc2[p][c] holds pixels 2p and 2p+1.
+template <int FC, bool CHECK>
+__device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__ s_geo,
+                                             const float* __restrict__ s_df, float fpx,
+                                             const float2 (&fpy2)[FwdCfg<FC>::PX / 2],
+                                             float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
+    constexpr int NP = FwdCfg<FC>::PX / 2;
+    constexpr int S = FwdCfg<FC>::S;
+#pragma unroll 2
+    for (int j = 0; j < cnt; ++j) {
+        const float4 g0 = s_geo[j];
+        const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
+        float r[S];
+#pragma unroll
+        for (int v = 0; v < S / 4; ++v) {
+            const float4 t = df4[v];
+            r[4 * v + 0] = t.x;
+            r[4 * v + 1] = t.y;
+            r[4 * v + 2] = t.z;
+            r[4 * v + 3] = t.w;
+        }
+        const float dx = fpx - g0.x;
+        const float bdx = g0.w * dx;
+        const float adx2 = (g0.z * dx) * dx;
+        const float2 ngy = make_float2(-g0.y, -g0.y);  // fpy + (-gy) == fpy - gy exactly
+        const float2 D2 = make_float2(r[0], r[0]);
+        const float2 b2 = make_float2(bdx, bdx);
+        const float2 a2 = make_float2(adx2, adx2);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const float2 dy = __fadd2_rn(fpy2[p], ngy);
+            const float2 q = __ffma2_rn(dy, __ffma2_rn(D2, dy, b2), a2);
+            float2 w;
+            if (CHECK) {
+                w.x = q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f;
+                w.y = q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f;
+            } else {
+                w.x = ex2_ftz(q.x);
+                w.y = ex2_ftz(q.y);
+            }
+#pragma unroll
+            for (int c = 0; c < FC; ++c) acc2[p][c] = __ffma2_rn(w, make_float2(r[1 + c], r[1 + c]), acc2[p][c]);
+        }
+    }
+}
+
 template <int FC>
 __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int W, int ntx,
                                                                 const float* __restrict__ geo,
@@ -94,11 +144,21 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
 #pragma unroll
     for (int k = 0; k < PX; ++k) fpy[k] = static_cast<float>(ty0 + ly + k * ROWSTEP);
 
+    constexpr bool PK = PX % 2 == 0;
+    constexpr int NP = PK ? PX / 2 : 1;
     float acc[PX][FC];
+    float2 acc2[NP][FC];
+    float2 fpy2[NP];
 #pragma unroll
     for (int k = 0; k < PX; ++k)
 #pragma unroll
         for (int c = 0; c < FC; ++c) acc[k][c] = 0.0f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        fpy2[p] = PK ? make_float2(fpy[2 * p], fpy[2 * p + 1]) : make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < FC; ++c) acc2[p][c] = make_float2(0.0f, 0.0f);
+    }
 
     const int start = tile_offsets[tile];
     const int end = tile_offsets[tile + 1];
@@ -120,11 +180,29 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
 #pragma unroll
             for (int c = 0; c < FC; ++c) df[1 + c] = c < F ? fg[c] * op : 0.0f;
         }
-        if (__syncthreads_and(regular ? 1 : 0)) {
-            fwd_batch<FC, false>(cnt, s_geo, s_df, fpx, fpy, acc);
+        const bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
+        if constexpr (PK) {
+            if (all_regular) {
+                fwd_batch_pk<FC, false>(cnt, s_geo, s_df, fpx, fpy2, acc2);
+            } else {
+                fwd_batch_pk<FC, true>(cnt, s_geo, s_df, fpx, fpy2, acc2);
+            }
         } else {
-            fwd_batch<FC, true>(cnt, s_geo, s_df, fpx, fpy, acc);
+            if (all_regular) {
+                fwd_batch<FC, false>(cnt, s_geo, s_df, fpx, fpy, acc);
+            } else {
+                fwd_batch<FC, true>(cnt, s_geo, s_df, fpx, fpy, acc);
+            }
         }
+    }
+    if constexpr (PK) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p)
+#pragma unroll
+            for (int c = 0; c < FC; ++c) {
+                acc[2 * p][c] = acc2[p][c].x;
+                acc[2 * p + 1][c] = acc2[p][c].y;
+            }
     }
     if (px < W) {
         const int64_t plane = static_cast<int64_t>(H) * W;

@@ -92,19 +92,20 @@ __global__ void __launch_bounds__(kScanBlocksThreads) k_scan_blocks(long long* _
     }
 }
 
-// Scan of one block of TILE = NT * ITEMS values.  prefix_mode 0: the block's
-// exclusive offset is block_sums[blockIdx.x] (already scanned); prefix_mode 1:
+// Scan of block `blk` of TILE = NT * ITEMS values.  prefix_mode 0: the block's
+// exclusive offset is block_sums[blk] (already scanned); prefix_mode 1:
 // block_sums holds raw per-block totals and the CTA sums those before it.
 // The last block writes the grand total (out[n] if write_tail, total_out).
 template <int NT, int ITEMS>
-__global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* out, int64_t n,
-                                                   const long long* __restrict__ block_sums, int prefix_mode,
-                                                   int64_t nb, int write_tail, int64_t* __restrict__ total_out) {
+__device__ __forceinline__ void scan_apply_block(const int32_t* in, int32_t* out, int64_t n,
+                                                 const long long* __restrict__ block_sums, int prefix_mode,
+                                                 int64_t nb, int write_tail, int64_t* __restrict__ total_out,
+                                                 int64_t blk) {
     constexpr int TILE = NT * ITEMS;
     __shared__ int32_t s_val[TILE];
     __shared__ long long s_warp[32];
     __shared__ long long s_prefix;
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * TILE;
+    const int64_t base = blk * TILE;
 #pragma unroll
     for (int k = 0; k < ITEMS; ++k) {
         const int64_t i = base + k * NT + threadIdx.x;
@@ -113,12 +114,12 @@ __global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* o
     long long prefix;
     if (prefix_mode == 1) {
         long long part = 0;
-        for (int64_t i = threadIdx.x; i < blockIdx.x; i += NT) part += block_sums[i];
+        for (int64_t i = threadIdx.x; i < blk; i += NT) part += block_sums[i];
         long long tot;
         block_exclusive_scan<NT>(part, s_warp, tot);
         prefix = tot;
     } else {
-        prefix = block_sums[blockIdx.x];
+        prefix = block_sums[blk];
     }
     __syncthreads();
     int32_t v[ITEMS];
@@ -142,10 +143,77 @@ __global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* o
         const int64_t i = base + k * NT + threadIdx.x;
         if (i < n) out[i] = s_val[k * NT + threadIdx.x];
     }
-    if (blockIdx.x == nb - 1 && threadIdx.x == 0) {
+    if (blk == nb - 1 && threadIdx.x == 0) {
         const long long total = s_prefix;
         if (write_tail) out[n] = static_cast<int32_t>(total);
         if (total_out != nullptr) *total_out = static_cast<int64_t>(total);
+    }
+}
+
+template <int NT, int ITEMS>
+__global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* out, int64_t n,
+                                                   const long long* __restrict__ block_sums, int prefix_mode,
+                                                   int64_t nb, int write_tail, int64_t* __restrict__ total_out) {
+    scan_apply_block<NT, ITEMS>(in, out, n, block_sums, prefix_mode, nb, write_tail, total_out, blockIdx.x);
+}
+
+// Block `blk` of the tile-offset scan over counters spaced `stride` ints apart:
+// offsets[t] = sum of the counts before t, offsets[num_tiles] = the total.  The
+// block sums every count before its own range itself (at most num_tiles reads),
+// so the blocks need no second pass.
+template <int NT, int ITEMS>
+__device__ __forceinline__ void strided_scan_block(const int32_t* __restrict__ count, int stride,
+                                                   int64_t num_tiles, int32_t* __restrict__ offsets, int64_t blk,
+                                                   int64_t nblk) {
+    constexpr int TILE = NT * ITEMS;
+    __shared__ long long s_warp[32];
+    const int64_t base = blk * TILE;
+    // every count before this block; unrolled so the strided loads overlap
+    long long part = 0;
+    int64_t t = threadIdx.x;
+    for (; t + 7 * NT < base; t += 8 * NT) {
+        int32_t c[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) c[u] = count[(t + u * NT) * stride];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) part += c[u];
+    }
+    for (; t < base; t += NT) part += count[t * stride];
+    long long prefix;
+    block_exclusive_scan<NT>(part, s_warp, prefix);
+    int32_t v[ITEMS];
+    long long local = 0;
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k) {
+        const int64_t t = base + static_cast<int64_t>(threadIdx.x) * ITEMS + k;
+        v[k] = t < num_tiles ? count[t * stride] : 0;
+        local += v[k];
+    }
+    long long block_total;
+    long long run = block_exclusive_scan<NT>(local, s_warp, block_total) + prefix;
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k) {
+        const int64_t t = base + static_cast<int64_t>(threadIdx.x) * ITEMS + k;
+        if (t < num_tiles) offsets[t] = static_cast<int32_t>(run);
+        run += v[k];
+    }
+    if (blk == nblk - 1 && threadIdx.x == 0) offsets[num_tiles] = static_cast<int32_t>(prefix + block_total);
+}
+
+// The scan launch of render prepare: blocks [0, nb) finish the gid-major
+// pair-offset scan (block sums from the preprocess kernel), blocks [nb, nb +
+// ntb) scan the per-tile pair counts into the tile list offsets.
+template <int NT, int ITEMS>
+__global__ void __launch_bounds__(NT) k_prepare_scan(const int32_t* in, int32_t* out, int64_t n,
+                                                     const long long* __restrict__ block_sums, int64_t nb,
+                                                     int64_t* __restrict__ total_out,
+                                                     const int32_t* __restrict__ tile_count, int count_stride,
+                                                     int64_t num_tiles, int32_t* __restrict__ tile_offsets,
+                                                     int64_t ntb) {
+    if (blockIdx.x < nb) {
+        scan_apply_block<NT, ITEMS>(in, out, n, block_sums, 1, nb, 1, total_out, blockIdx.x);
+    } else {
+        strided_scan_block<NT, ITEMS>(tile_count, count_stride, num_tiles, tile_offsets, blockIdx.x - nb, ntb);
     }
 }
 
@@ -225,14 +293,18 @@ cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool 
 int64_t scan_fused_scratch_bytes(int64_t n) { return arena_bytes(div_up(n, kPrepTile) + 1, sizeof(long long)); }
 
 cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t n, const long long* block_sums,
-                                       int64_t* total_out, cudaStream_t stream) {
+                                       int64_t* total_out, const int32_t* tile_count, int count_stride,
+                                       int64_t num_tiles, int32_t* tile_offsets, cudaStream_t stream) {
+    constexpr int kItems = kPrepTile / kPrepThreads;
+    const int64_t ntb = tile_count != nullptr ? div_up(num_tiles, kPrepTile) : 0;
     if (n == 0) {
         k_scan_empty<<<1, 1, 0, stream>>>(out, 1, total_out);
-        return cudaGetLastError();
+        if (ntb == 0) return cudaGetLastError();
     }
     const int64_t nb = div_up(n, kPrepTile);
-    k_scan_apply<kPrepThreads, kPrepTile / kPrepThreads><<<static_cast<unsigned>(nb), kPrepThreads, 0, stream>>>(
-        in, out, n, block_sums, 1, nb, 1, total_out);
+    if (nb + ntb == 0) return cudaGetLastError();
+    k_prepare_scan<kPrepThreads, kItems><<<static_cast<unsigned>(nb + ntb), kPrepThreads, 0, stream>>>(
+        in, out, n, block_sums, nb, total_out, tile_count, count_stride, num_tiles, tile_offsets, ntb);
     return cudaGetLastError();
 }
 

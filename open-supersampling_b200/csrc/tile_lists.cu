@@ -3,11 +3,11 @@
 // The reference builds its tile lists by sorting (tile << 32 | gid) keys
 // (rasterizer_fwd.cu:461-468): each tile's list holds, ascending, the gids of
 // the Gaussians whose tile rectangle covers the tile.  Here the per-tile counts
-// come from the preprocess kernel, their exclusive scan gives every tile its
-// list offset, each (Gaussian, tile) pair claims a slot of its tile with an
-// atomic (in no particular order), and every tile's list is then sorted.  A
-// Gaussian covers a tile at most once, so a sorted list is unique: the output
-// is the reference's list whatever order the atomics ran in.
+// and their exclusive scan (the list offsets) come from render prepare, each
+// (Gaussian, tile) pair claims a slot of its tile with an atomic (in no
+// particular order), and every tile's list is then sorted.  A Gaussian covers a
+// tile at most once, so a sorted list is unique: the output is the reference's
+// list whatever order the atomics ran in.
 //
 // The pair total is read on the device and checked against the caller's
 // capacity; on overflow every list and every Gaussian's pair range is emptied
@@ -26,8 +26,8 @@ constexpr int kScatterWarps = kScatterThreads / 32;
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kSortBuf = 8192;                    // ints of shared memory per CTA (32 KB)
-constexpr int kWarpCap = kSortBuf / kSortWarps;   // lists up to 1024 sorted by one warp
-constexpr int kCtaCap = kSortBuf;                 // lists up to 8192 sorted by the CTA
+constexpr int kWarpCap = 1024;                    // lists up to 1024 sorted by one warp in registers
+constexpr int kCtaCap = kSortBuf;                 // lists up to 8192 sorted by the CTA in shared memory
 constexpr int kWindowBits = kSortBuf * 32;        // gid window of the bitmap path
 
 // One warp per 32 consecutive Gaussians.  The warp's pairs are dealt round-robin
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
             const int k = j - o_start;
             const int dy = k / o_w;
             const int t = (o_y + dy) * ntx + o_x + (k - dy * o_w);
-            const int slot = atomicSub(&tile_count[t], 1) - 1;
+            const int slot = atomicSub(&tile_count[static_cast<int64_t>(t) * kTileCountStride], 1) - 1;
             unsorted[tile_offsets[t] + slot] = g0 + owner;
         }
     }
@@ -93,10 +93,11 @@ __device__ __forceinline__ int next_pow2(int v) {
     return p;
 }
 
-// Ascending bitonic sort of s[0..lp), lp a power of two, by `nt` cooperating
-// threads (a warp or the CTA) with index `tid`.
-template <bool kCta>
-__device__ __forceinline__ void bitonic_sort(int32_t* s, int lp, int tid, int nt) {
+// Ascending bitonic sort of s[0..lp) in shared memory, lp a power of two, by the
+// CTA's threads.
+__device__ __forceinline__ void cta_bitonic_sort(int32_t* s, int lp) {
+    const int tid = threadIdx.x;
+    constexpr int nt = kSortThreads;
     for (int k = 2; k <= lp; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
             for (int i = tid; i < (lp >> 1); i += nt) {
@@ -110,12 +111,59 @@ __device__ __forceinline__ void bitonic_sort(int32_t* s, int lp, int tid, int nt
                     s[b] = x;
                 }
             }
-            if (kCta) {
-                __syncthreads();
+            __syncthreads();
+        }
+    }
+}
+
+// Ascending bitonic sort of the 32 * R values a warp holds, element r * 32 + lane
+// in v[r] of that lane: distances below 32 pair lanes through shuffles,
+// distances of 32 and more pair registers of the same lane.
+template <int R>
+__device__ __forceinline__ void warp_bitonic(int32_t (&v)[R], int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32 * R; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32) {
+                const int jr = j >> 5;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    if ((r & jr) == 0) {
+                        const bool asc = ((r * 32) & k) == 0;  // k >= 64 here: lane bits do not reach it
+                        const int32_t a = v[r];
+                        const int32_t b = v[r | jr];
+                        v[r] = asc ? min(a, b) : max(a, b);
+                        v[r | jr] = asc ? max(a, b) : min(a, b);
+                    }
+                }
             } else {
-                __syncwarp();
+                const bool lower = (lane & j) == 0;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int32_t p = __shfl_xor_sync(0xffffffffu, v[r], j);
+                    const bool asc = ((r * 32 + lane) & k) == 0;
+                    v[r] = lower == asc ? min(v[r], p) : max(v[r], p);
+                }
             }
         }
+    }
+}
+
+template <int R>
+__device__ __forceinline__ void warp_sort_list(const int32_t* __restrict__ src, int32_t* __restrict__ dst, int len,
+                                               int lane) {
+    int32_t v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int e = r * 32 + lane;
+        v[r] = e < len ? src[e] : INT_MAX;
+    }
+    warp_bitonic<R>(v, lane);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int e = r * 32 + lane;
+        if (e < len) dst[e] = v[r];
     }
 }
 
@@ -205,13 +253,16 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tile
 #pragma unroll
         for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, v, j) < v ? 1 : 0;
         if (lane < len) dst[rank] = v;
+    } else if (len <= 64) {
+        warp_sort_list<2>(src, dst, len, lane);
+    } else if (len <= 128) {
+        warp_sort_list<4>(src, dst, len, lane);
+    } else if (len <= 256) {
+        warp_sort_list<8>(src, dst, len, lane);
+    } else if (len <= 512) {
+        warp_sort_list<16>(src, dst, len, lane);
     } else if (len <= kWarpCap) {
-        int32_t* s = s_buf + warp * kWarpCap;
-        const int lp = next_pow2(len);
-        for (int i = lane; i < lp; i += 32) s[i] = i < len ? src[i] : INT_MAX;
-        __syncwarp();
-        bitonic_sort<false>(s, lp, lane, 32);
-        for (int i = lane; i < len; i += 32) dst[i] = s[i];
+        warp_sort_list<32>(src, dst, len, lane);
     } else if (lane == 0) {
         atomicOr(&s_big, 1 << warp);
     }
@@ -226,7 +277,7 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tile
             const int lp = next_pow2(blen);
             for (int i = threadIdx.x; i < lp; i += kSortThreads) s_buf[i] = i < blen ? unsorted[boff + i] : INT_MAX;
             __syncthreads();
-            bitonic_sort<true>(s_buf, lp, threadIdx.x, kSortThreads);
+            cta_bitonic_sort(s_buf, lp);
             for (int i = threadIdx.x; i < blen; i += kSortThreads) gid_sorted[boff + i] = s_buf[i];
             __syncthreads();
         } else {
@@ -243,9 +294,7 @@ __global__ void k_empty_lists(int num_tiles, int32_t* __restrict__ tile_offsets,
 
 }  // namespace
 
-int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles) {
-    return arena_bytes(capacity, sizeof(int32_t)) + scan_scratch_bytes(num_tiles);
-}
+int64_t tile_lists_scratch_bytes(int64_t capacity) { return arena_bytes(capacity, sizeof(int32_t)); }
 
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
                              int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, int32_t* gid_sorted,
@@ -255,15 +304,11 @@ cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb,
             num_tiles, tile_offsets, overflow);
         return cudaGetLastError();
     }
-    Arena arena{static_cast<char*>(scratch), tile_lists_scratch_bytes(capacity, num_tiles), 0};
-    int32_t* unsorted = arena.take<int32_t>(capacity);
-    void* scan_scratch = arena.base + arena.used;
-    cudaError_t err = scan_exclusive_i32(tile_count, tile_offsets, num_tiles, true, nullptr, scan_scratch, stream);
-    if (err != cudaSuccess) return err;
+    int32_t* unsorted = static_cast<int32_t*>(scratch);
     k_scatter_pairs<<<static_cast<unsigned>(div_up(n, kScatterThreads)), kScatterThreads, 0, stream>>>(
         n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, tile_count, tile_offsets, total_pairs,
         capacity, unsorted, overflow);
-    err = cudaGetLastError();
+    cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     k_sort_tiles<<<static_cast<unsigned>(div_up(num_tiles, kSortWarps)), kSortThreads, 0, stream>>>(
         n, num_tiles, tile_offsets, unsorted, gid_sorted);

@@ -30,7 +30,9 @@ SIGNATURES = {
     "oss_abi_version": (ctypes.c_int, []),
     "oss_preprocess": (ctypes.c_int, [_i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p]),
     "oss_render_prepare_scratch_bytes": (_i64, [_i64]),
-    "oss_render_prepare": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_tile_count_elems": (_i64, [_i64]),
+    "oss_render_prepare": (
+        ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_bin_pairs": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _p]),
     "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),

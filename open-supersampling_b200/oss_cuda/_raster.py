@@ -141,12 +141,14 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     pair_offset = torch.empty((n + 1,), **i32)
     geo = torch.empty((n, 8), **f32)
     total = torch.empty((1,), device=dev, dtype=torch.int64)
-    tile_count = torch.empty((max(1, num_tiles),), **i32)
+    tile_count = torch.empty((max(1, lib.oss_tile_count_elems(num_tiles)),), **i32)
+    tile_offsets = torch.empty((num_tiles + 1,), **i32)
     scratch = torch.empty((max(1, lib.oss_render_prepare_scratch_bytes(n)),), device=dev, dtype=torch.uint8)
     _lib.check(
         lib.oss_render_prepare(n, h, w, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(), conic.data_ptr(),
                                aabb.data_ptr(), pair_offset.data_ptr(), geo.data_ptr(), total.data_ptr(),
-                               tile_count.data_ptr(), scratch.data_ptr(), scratch.numel(), stream),
+                               tile_count.data_ptr(), tile_offsets.data_ptr(), scratch.data_ptr(), scratch.numel(),
+                               stream),
         "oss_render_prepare",
     )
     if mode == _lib.OSS_BIN_FULL:
@@ -156,7 +158,6 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     if total_pairs > INT32_MAX:
         raise RuntimeError("total pair count exceeds int32 range")
     gid_sorted = torch.empty((total_pairs,), **i32)
-    tile_offsets = torch.empty((num_tiles + 1,), **i32)
     overflow = torch.empty((1,), **i32)
     nbytes = lib.oss_bin_pairs_scratch_bytes(n, total_pairs, num_tiles)
     scratch2 = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)

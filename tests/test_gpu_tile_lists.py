@@ -51,7 +51,7 @@ class Lists:
         self.pair_offset = torch.empty((n + 1,), **i32)
         self.geo = torch.empty((n, 8), **f32)
         self.total = torch.empty((1,), device="cuda", dtype=torch.int64)
-        self.tile_count = torch.empty((max(1, self.tiles),), **i32)
+        self.tile_count = torch.empty((max(1, self.lib.oss_tile_count_elems(self.tiles)),), **i32)
         self.tile_offsets = torch.empty((self.tiles + 1,), **i32)
         self.overflow = torch.full((1,), -1, **i32)
         self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device="cuda",
@@ -69,7 +69,8 @@ class Lists:
                                              self.scale.data_ptr(), self.rot.data_ptr(), self.conic.data_ptr(),
                                              self.aabb.data_ptr(), self.pair_offset.data_ptr(), self.geo.data_ptr(),
                                              self.total.data_ptr(), self.tile_count.data_ptr(),
-                                             self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
+                                             self.tile_offsets.data_ptr(), self.prep_scratch.data_ptr(),
+                                             self.prep_scratch.numel(), s), "prepare")
         self.chk(self.lib.oss_bin_pairs(self.n, self.h, self.w, self.mode, self.aabb.data_ptr(),
                                         self.pair_offset.data_ptr(), self.tile_count.data_ptr(),
                                         self.total.data_ptr(), self.capacity, self.gid.data_ptr(),
