@@ -208,6 +208,9 @@ class Pipeline:
                      self.lib.oss_render_backward_scratch_bytes(self.capacity, 3, self.tiles))
             self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
             self.pg_bytes = ((self.capacity * self.lib.oss_pair_grad_stride(3) * 4 + 255) // 256) * 256
+            self.records = torch.empty((self.capacity, self.lib.oss_entry_record_floats(3)), device=dev,
+                                       dtype=torch.float32)
+            self.slots = torch.empty((self.capacity,), device=dev, dtype=torch.int32)
 
     def _mark(self, i, timed):
         if timed:
@@ -236,21 +239,23 @@ class Pipeline:
                               self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
                               self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
         self._mark(3, timed)
+        rec = (self.records.data_ptr(), self.slots.data_ptr()) if backward else (None, None)
         chk(lib.oss_render_forward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(), d["opacity"].data_ptr(),
                                    self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.image.data_ptr(),
-                                   s), "forward")
+                                   self.aabb.data_ptr(), self.pair_offset.data_ptr(), rec[0], rec[1], s), "forward")
         self._mark(4, timed)
         if not backward:
             return
         chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
                                           self.capacity, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
-                                          d["grad"].data_ptr(), self.scratch.data_ptr(),
+                                          rec[0], rec[1], d["grad"].data_ptr(), self.scratch.data_ptr(),
                                           self.scratch.data_ptr() + self.pg_bytes, self.scratch.numel() - self.pg_bytes,
                                           s), "backward_pairs")
         self._mark(5, timed)
         g = self.grads
-        chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), d["rgb"].data_ptr(),
+        chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), self.geo.data_ptr(),
+                                      d["rgb"].data_ptr(),
                                       d["opacity"].data_ptr(), d["scale"].data_ptr(), d["rot"].data_ptr(),
                                       g["d_xy"].data_ptr(), g["d_conic"].data_ptr(), g["d_rgb"].data_ptr(),
                                       g["d_opacity"].data_ptr(), g["d_scale"].data_ptr(), g["d_rot"].data_ptr(), s),
@@ -285,7 +290,7 @@ class Pipeline:
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
         prepare = 2                                   # k_preprocess, k_prepare_scan (pair + tile offsets)
         binning = 2                                   # k_scatter_pairs, k_sort_tiles
-        bwd = 1 + scan_launches(self.tiles) + 1 + 1   # k_item_counts, item scan, k_render_bwd, k_reduce_gaussian
+        bwd = 4                                       # k_item_block_sums, k_item_table, k_render_bwd, k_reduce_gaussian
         return prepare + binning + 1 + (bwd if backward else 0)
 
     def evaluations(self):

@@ -128,11 +128,20 @@ OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
  *   feat'[g][c] * exp(-q_g(p)/2),  feat' = feat * opacity (opacity may be NULL).
  * Replaces the rasterize_sum loop of _C.rasterize_forward
  * (rasterizer_fwd.cu:151-322, host loop :570-587).  Writes every pixel.
+ *
+ * Entry records (optional, both NULL or both set): for every list entry e in
+ * list order, records[e][oss_entry_record_floats(f)] = (x, y, A, B, D,
+ * feat'(f), zero padding) of its Gaussian and slots[e] = its gid-major pair
+ * slot pair_offset[g] + local tile index (needs aabb and pair_offset).  The
+ * backward reads them instead of gathering per-Gaussian data a second time.
+ * records and slots hold capacity entries (any upper bound of the pair total).
  * ------------------------------------------------------------------------- */
+OSS_API int oss_entry_record_floats(int64_t f);
 OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
                        const float* geo, const float* feat, const float* opacity,
                        const int32_t* gid_sorted, const int32_t* tile_offsets,
-                       float* image, void* stream);
+                       float* image, const int32_t* aabb, const int32_t* pair_offset,
+                       float* records, int32_t* slots, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Deterministic backward for lists made by oss_bin_pairs: per-pair partial
@@ -143,7 +152,8 @@ OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
  * d_feat is the gradient w.r.t. feat (not feat'); d_opacity, d_scale, d_rot
  * may be NULL.  total_pairs may be the exact pair count or any upper bound of
  * it, such as the capacity given to oss_bin_pairs: the kernels take the list
- * lengths from tile_offsets and pair_offset on the device.
+ * lengths from tile_offsets and pair_offset on the device.  records/slots are
+ * the forward's entry records (NULL: gathered through gid_sorted instead).
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_t num_tiles);
 OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
@@ -151,6 +161,7 @@ OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
                         const float* scale, const float* rot,
                         const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
                         const int32_t* gid_sorted, const int32_t* tile_offsets,
+                        const float* records, const int32_t* slots,
                         const float* grad_image,
                         float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
                         float* d_scale, float* d_rot,
@@ -158,20 +169,23 @@ OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,
 
 /* The two halves of oss_render_backward, for callers that keep the per-pair
  * partials: oss_render_backward_pairs writes pairgrad[total_pairs][stride]
- * (stride = oss_pair_grad_stride(f) floats: d_xy(2), d_conic(3), d_feat'(f),
- * zero padding) in gid-major pair order; oss_reduce_pair_grads sums them per
- * Gaussian.  The scratch of oss_render_backward is pairgrad followed by the
- * work-item table oss_render_backward_pairs needs. */
+ * (stride = oss_pair_grad_stride(f) floats: Sx, Sy (the dq-weighted offset
+ * sums), d_conic(3), d_feat'(f), zero padding) in gid-major pair order;
+ * oss_reduce_pair_grads sums them per Gaussian and applies the conic from geo
+ * (d_xy = (a Sx + b Sy, b Sx + d Sy)).  The scratch of oss_render_backward is
+ * pairgrad followed by the work-item table oss_render_backward_pairs needs. */
 OSS_API int oss_pair_grad_stride(int64_t f);
 OSS_API int64_t oss_render_backward_pairs_scratch_bytes(int64_t total_pairs, int64_t num_tiles);
 OSS_API int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w,
                               const float* geo, const float* feat, const float* opacity,
                               const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
                               const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* records, const int32_t* slots,
                               const float* grad_image, float* pairgrad,
                               void* scratch, int64_t scratch_bytes, void* stream);
 OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
-                          const int32_t* pair_offset, const float* feat, const float* opacity,
+                          const int32_t* pair_offset, const float* geo,
+                          const float* feat, const float* opacity,
                           const float* scale, const float* rot,
                           float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
                           float* d_scale, float* d_rot, void* stream);

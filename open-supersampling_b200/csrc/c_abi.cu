@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 3; }
+int oss_abi_version(void) { return 4; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -177,8 +177,13 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
     return OSS_OK;
 }
 
+int oss_entry_record_floats(int64_t f) {
+    return oss::entry_record_floats(static_cast<int>(f < 1 ? 1 : (f > OSS_MAX_CHANNELS ? OSS_MAX_CHANNELS : f)));
+}
+
 int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
                        const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
+                       const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
                        void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
@@ -189,8 +194,13 @@ int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* 
     OSS_CHECK(tile_offsets != nullptr && image != nullptr, OSS_ERR_INVALID, "tile_offsets and image must be non-null");
     OSS_CHECK(g.n == 0 || (geo != nullptr && feat != nullptr && aligned(geo, 16)), OSS_ERR_INVALID,
               "geo (16-byte aligned) and feat must be non-null");
+    OSS_CHECK((records == nullptr) == (slots == nullptr), OSS_ERR_INVALID, "records and slots go together");
+    OSS_CHECK(records == nullptr || (aligned(records, 16) && aabb != nullptr && aligned(aabb, 16) &&
+                                     pair_offset != nullptr),
+              OSS_ERR_INVALID, "records (16-byte aligned) need aabb (16-byte aligned) and pair_offset");
     OSS_CUDA_TRY(oss::launch_render_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
-                                            tile_offsets, image, as_stream(stream)));
+                                            tile_offsets, image, aabb, pair_offset, records, slots,
+                                            as_stream(stream)));
     return OSS_OK;
 }
 
@@ -210,9 +220,9 @@ int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_
 int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
                         const float* opacity, const float* scale, const float* rot, const int32_t* aabb,
                         const int32_t* pair_offset, int64_t total_pairs, const int32_t* gid_sorted,
-                        const int32_t* tile_offsets, const float* grad_image, float* d_xy, float* d_conic,
-                        float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* scratch,
-                        int64_t scratch_bytes, void* stream) {
+                        const int32_t* tile_offsets, const float* records, const int32_t* slots,
+                        const float* grad_image, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                        float* d_scale, float* d_rot, void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
@@ -231,9 +241,10 @@ int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float*
     const int64_t pg_bytes = oss::arena_bytes(total_pairs * oss::backward_pair_stride(static_cast<int>(f)), 4);
     void* items = static_cast<char*>(scratch) + pg_bytes;
     rc = oss_render_backward_pairs(n, f, h, w, geo, feat, opacity, aabb, pair_offset, total_pairs, gid_sorted,
-                                   tile_offsets, grad_image, pairgrad, items, scratch_bytes - pg_bytes, stream);
+                                   tile_offsets, records, slots, grad_image, pairgrad, items, scratch_bytes - pg_bytes,
+                                   stream);
     if (rc != OSS_OK) return rc;
-    return oss_reduce_pair_grads(n, f, pairgrad, pair_offset, feat, opacity, scale, rot, d_xy, d_conic, d_feat,
+    return oss_reduce_pair_grads(n, f, pairgrad, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, d_feat,
                                  d_opacity, d_scale, d_rot, stream);
 }
 
@@ -244,8 +255,8 @@ int oss_pair_grad_stride(int64_t f) {
 int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
                               const float* opacity, const int32_t* aabb, const int32_t* pair_offset,
                               int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
-                              const float* grad_image, float* pairgrad, void* scratch, int64_t scratch_bytes,
-                              void* stream) {
+                              const float* records, const int32_t* slots, const float* grad_image, float* pairgrad,
+                              void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
@@ -261,27 +272,31 @@ int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const 
     OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
     OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
               "lists and grad_image must be non-null");
+    OSS_CHECK((records == nullptr) == (slots == nullptr), OSS_ERR_INVALID, "records and slots go together");
+    OSS_CHECK(records == nullptr || aligned(records, 16), OSS_ERR_INVALID, "records must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, opacity,
-                                                   gid_sorted, tile_offsets, grad_image, aabb, pair_offset, pairgrad,
-                                                   oss_pair_grad_stride(f), nullptr, nullptr, nullptr, scratch,
-                                                   as_stream(stream)));
+                                                   gid_sorted, tile_offsets, grad_image, aabb, pair_offset, records,
+                                                   slots, pairgrad, oss_pair_grad_stride(f), nullptr, nullptr, nullptr,
+                                                   scratch, as_stream(stream)));
     return OSS_OK;
 }
 
-int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int32_t* pair_offset, const float* feat,
-                          const float* opacity, const float* scale, const float* rot, float* d_xy, float* d_conic,
-                          float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* stream) {
+int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int32_t* pair_offset, const float* geo,
+                          const float* feat, const float* opacity, const float* scale, const float* rot, float* d_xy,
+                          float* d_conic, float* d_feat, float* d_opacity, float* d_scale, float* d_rot,
+                          void* stream) {
     OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
     OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
     if (n == 0) return OSS_OK;
     OSS_CHECK(pair_offset != nullptr && d_xy != nullptr && d_conic != nullptr, OSS_ERR_INVALID,
               "pair_offset, d_xy and d_conic must be non-null");
+    OSS_CHECK(geo != nullptr && aligned(geo, 16), OSS_ERR_INVALID, "geo must be 16-byte aligned");
     OSS_CHECK(f == 0 || (feat != nullptr && d_feat != nullptr), OSS_ERR_INVALID, "feat and d_feat must be non-null");
     OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
               "d_scale needs scale, rot and d_rot");
     OSS_CHECK(pairgrad == nullptr || aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_reduce_gaussian_grads(static_cast<int>(n), static_cast<int>(f), pairgrad,
-                                                   oss_pair_grad_stride(f), pair_offset, feat, opacity, scale, rot,
+                                                   oss_pair_grad_stride(f), pair_offset, geo, feat, opacity, scale, rot,
                                                    d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot,
                                                    as_stream(stream)));
     return OSS_OK;
@@ -319,8 +334,8 @@ int oss_rasterize_backward_lists(int64_t n, int64_t f, int64_t h, int64_t w, con
     void* items = static_cast<char*>(scratch) + oss::arena_bytes(static_cast<int64_t>(g.n) * 8, 4);
     OSS_CUDA_TRY(oss::launch_make_geo(g.n, xy, conic, geo, s));
     OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, nullptr,
-                                                   gid_sorted, tile_offsets, grad_image, nullptr, nullptr, nullptr, 0,
-                                                   d_xy, d_conic, d_feat, items, s));
+                                                   gid_sorted, tile_offsets, grad_image, nullptr, nullptr, nullptr,
+                                                   nullptr, nullptr, 0, d_xy, d_conic, d_feat, items, s));
     return OSS_OK;
 }
 

@@ -90,25 +90,31 @@ cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, floa
                                   float* out_xy, uint8_t* in_frame, cudaStream_t stream);
 
 // ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
+// Entry records (forward -> backward): floats per record for f channels.
+int entry_record_floats(int f);
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat,
                                   const float* opacity, const int32_t* gid_sorted,
-                                  const int32_t* tile_offsets, float* image, cudaStream_t stream);
+                                  const int32_t* tile_offsets, float* image, const int32_t* aabb,
+                                  const int32_t* pair_offset, float* records, int32_t* slots,
+                                  cudaStream_t stream);
 
-// Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows of
-// pair_stride floats at pair_offset[g] + local tile index.  Atomic mode: adds
-// into d_xy / d_conic / d_feat.  items_scratch holds the work-item table
-// (backward_items_scratch_bytes).
+// Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows
+// (Sx, Sy, d_conic, dF) of pair_stride floats at pair_offset[g] + local tile
+// index, entries read from the forward's records/slots when records != null.
+// Atomic mode: adds into d_xy / d_conic / d_feat.  items_scratch holds the
+// work-item table (backward_items_scratch_bytes).
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo,
                                          const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image,
                                          const int32_t* aabb, const int32_t* pair_offset,
+                                         const float* records, const int32_t* slots,
                                          float* pairgrad, int pair_stride,
                                          float* d_xy, float* d_conic, float* d_feat, void* items_scratch,
                                          cudaStream_t stream);
 int backward_pair_stride(int f);
 int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles);
 cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,
-                                         const int32_t* pair_offset, const float* feat,
+                                         const int32_t* pair_offset, const float* geo, const float* feat,
                                          const float* opacity, const float* scale, const float* rot,
                                          float* d_xy, float* d_conic, float* d_feat,
                                          float* d_opacity, float* d_scale, float* d_rot,

@@ -1,7 +1,8 @@
 // Backward of the additive tile render (the reference's rasterize_backward,
 // rasterizer_bwd.cu:32-113), re-organised so that no per-pixel atomics remain.
 //
-// Work is cut into items: up to 32 list entries of one tile.  One warp runs one
+// Work is cut into items: up to 32 list entries of one tile, listed in an item
+// table (tile, first entry, count) built by one small kernel.  One warp runs one
 // item.  It stages the tile's dL/dimage block into its own shared-memory slot
 // (rows padded so that lanes on different rows hit different banks), then each
 // lane owns one list entry and walks the tile's pixels, keeping the per-pair
@@ -11,17 +12,20 @@
 //   Syy = sum g dy^2, dF_c = sum w go_c
 // from which d_xy = (a Sx + b Sy, b Sx + d Sy) and
 // d_conic = (-Sxx/2, -Sxy, -Syy/2) -- the reference's per-pixel terms
-// (rasterizer_bwd.cu:89-108) summed over the tile.
+// (rasterizer_bwd.cu:89-108) summed over the tile.  The entry's data comes from
+// the forward's entry records (one coalesced load) when the caller kept them,
+// else it is gathered through gid_sorted.
 //
 // A tile's last item is usually partial.  With r < 32 entries it runs k lanes
 // per entry (k = 2, 4, 8 or 16, the largest with r*k <= 32), each lane taking
 // 16/k rows, and the k partial sums are combined by a fixed xor-shuffle tree:
 // the split depends only on r, so results are bitwise reproducible.
 //
-// Deterministic mode writes each pair's partial row at its gid-major pair slot
-// (pair_offset[g] + local tile index, the order oss_bin_pairs expanded it in);
-// k_reduce_gaussian then sums a Gaussian's rows in that fixed order and applies
-// the conic -> (scale, rot) chain rule and the opacity unfold.  Atomic mode
+// Deterministic mode writes each pair's partial row (Sx, Sy, d_conic, dF) at its
+// gid-major pair slot (pair_offset[g] + local tile index, the order of the
+// reference's build_tile_pairs); k_reduce_gaussian then sums a Gaussian's rows in
+// that fixed order, applies the conic to (Sx, Sy) -- d_xy is linear in them --
+// and the conic -> (scale, rot) chain rule and the opacity unfold.  Atomic mode
 // (caller-supplied lists) adds each pair's partials with fp32 atomics: (F+5)
 // atomics per pair instead of the reference's (F+5) per pixel-pair.
 #include "internal.h"
@@ -226,33 +230,30 @@ __device__ __forceinline__ float group_sum(float v, int k) {
     return v;
 }
 
-template <int FC, bool DETERMINISTIC>
+// Entry sources and pair-gradient sinks of the backward kernel.
+enum BwdMode { kAtomicGather = 0, kDetGather = 1, kDetRecords = 2 };
+
+template <int FC, int MODE>
 __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
-    const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted,
-    const int32_t* __restrict__ tile_offsets, const int32_t* __restrict__ item_offsets, int num_tiles,
-    const float* __restrict__ grad_image, const int4* __restrict__ aabb, const int32_t* __restrict__ pair_offset,
+    const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted, const int4* __restrict__ items,
+    const int32_t* __restrict__ num_items, const float* __restrict__ grad_image, const int4* __restrict__ aabb,
+    const int32_t* __restrict__ pair_offset, const float* __restrict__ records, const int32_t* __restrict__ slots,
     float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy, float* __restrict__ d_conic,
     float* __restrict__ d_feat) {
     constexpr int SG = BwdCfg<FC>::SG;
+    constexpr int RS = 4 + ((1 + FC + 3) / 4) * 4;  // entry record floats (the forward's layout)
     extern __shared__ float4 s_mem4[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int item = blockIdx.x * BwdCfg<FC>::WARPS + warp;
-    if (item >= item_offsets[num_tiles]) return;  // uniform per warp
+    if (item >= *num_items) return;  // uniform per warp
     float* s_go = reinterpret_cast<float*>(s_mem4) + warp * BwdCfg<FC>::SLOT;
 
-    // tile of this item: the last t with item_offsets[t] <= item (empty tiles
-    // share their successor's offset, so the match always has items)
-    int lo = 0, hi = num_tiles - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (item_offsets[mid] <= item) lo = mid;
-        else hi = mid - 1;
-    }
-    const int tile = lo;
-    const int first = tile_offsets[tile] + (item - item_offsets[tile]) * kItemEntries;
-    const int r = min(kItemEntries, tile_offsets[tile + 1] - first);
+    const int4 it = items[item];
+    const int tile = it.x;
+    const int first = it.y;
+    const int r = it.z;
     const int tile_x = tile % ntx;
     const int tile_y = tile / ntx;
     const int tx0 = tile_x * kTile;
@@ -303,22 +304,42 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
     const bool active = e < r;
 
     int g = 0;
+    int slot = 0;
     float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float fv[FC];
 #pragma unroll
     for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
     if (active) {  // idle lanes run on a neutral entry so the warp stays converged
-        g = gid_sorted[first + e];
-        const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-        g0 = rec[0];
-        g1 = rec[1];
-        const float op = opacity != nullptr ? opacity[g] : 1.0f;
-        const float* fg = feat + static_cast<int64_t>(g) * F;
+        if (MODE == kDetRecords) {
+            const float4* rec = reinterpret_cast<const float4*>(records + static_cast<int64_t>(first + e) * RS);
+            g0 = rec[0];
+            float rv[RS - 4];
 #pragma unroll
-        for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+            for (int v = 0; v < (RS - 4) / 4; ++v) {
+                const float4 t = rec[1 + v];
+                rv[4 * v + 0] = t.x;
+                rv[4 * v + 1] = t.y;
+                rv[4 * v + 2] = t.z;
+                rv[4 * v + 3] = t.w;
+            }
+            g1.x = rv[0];
+#pragma unroll
+            for (int c = 0; c < FC; ++c) fv[c] = rv[1 + c];
+            slot = slots[first + e];
+        } else {
+            g = gid_sorted[first + e];
+            const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
+            g0 = rec[0];
+            g1 = rec[1];
+            const float op = opacity != nullptr ? opacity[g] : 1.0f;
+            const float* fg = feat + static_cast<int64_t>(g) * F;
+#pragma unroll
+            for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+        }
     }
-    const bool regular = !active || regular_conic_bwd(g0.x, g0.y, g1.y, g1.z, g1.w);
+    // the same test on (-A, -B/2, -D) = k (a, b, d) with k = 0.5 log2(e) > 0 (records carry no raw conic)
+    const bool regular = !active || regular_conic_bwd(g0.x, g0.y, -g0.z, -0.5f * g0.w, -g1.x);
     const bool warp_regular = __all_sync(0xffffffffu, regular);
 
     float dF[FC];
@@ -357,24 +378,23 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
     }
     if (!active || band != 0) return;
 
-    // raw conic (a, b, d) sits in g1.yzw
-    const float dxy_x = fmaf(g1.y, Sx, g1.z * Sy);
-    const float dxy_y = fmaf(g1.z, Sx, g1.w * Sy);
     const float dca = -0.5f * Sxx;
     const float dcb = -Sxy;
     const float dcd = -0.5f * Syy;
-    if (DETERMINISTIC) {
-        const int4 box = aabb[g];
-        const int local = (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
-        float* row = pairgrad + (static_cast<int64_t>(pair_offset[g]) + local) * pstride;
+    if (MODE != kAtomicGather) {
+        if (MODE == kDetGather) {
+            const int4 box = aabb[g];
+            slot = pair_offset[g] + (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
+        }
+        float* row = pairgrad + static_cast<int64_t>(slot) * pstride;
         if (FC <= 3) {
             float4* row4 = reinterpret_cast<float4*>(row);
-            row4[0] = make_float4(dxy_x, dxy_y, dca, dcb);
+            row4[0] = make_float4(Sx, Sy, dca, dcb);
             row4[1] = make_float4(dcd, dF[0], FC > 1 ? dF[FC > 1 ? 1 : 0] : 0.0f,
                                   FC > 2 ? dF[FC > 2 ? 2 : 0] : 0.0f);
         } else {
-            row[0] = dxy_x;
-            row[1] = dxy_y;
+            row[0] = Sx;
+            row[1] = Sy;
             row[2] = dca;
             row[3] = dcb;
             row[4] = dcd;
@@ -384,8 +404,9 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
             }
         }
     } else {
-        atomicAdd(&d_xy[2 * g + 0], dxy_x);
-        atomicAdd(&d_xy[2 * g + 1], dxy_y);
+        // raw conic (a, b, d) sits in g1.yzw
+        atomicAdd(&d_xy[2 * g + 0], fmaf(g1.y, Sx, g1.z * Sy));
+        atomicAdd(&d_xy[2 * g + 1], fmaf(g1.z, Sx, g1.w * Sy));
         atomicAdd(&d_conic[3 * g + 0], dca);
         atomicAdd(&d_conic[3 * g + 1], dcb);
         atomicAdd(&d_conic[3 * g + 2], dcd);
@@ -397,18 +418,91 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
 }
 
 // Work items of the backward: every tile has ceil(L / 32) items of up to 32
-// consecutive list entries.  item_offsets (an exclusive scan of those counts,
-// item_offsets[T] = total) maps an item to its tile by binary search.
-__global__ void __launch_bounds__(256) k_item_counts(int num_tiles, const int32_t* __restrict__ tile_offsets,
-                                                      int32_t* __restrict__ counts) {
-    const int t = blockIdx.x * 256 + threadIdx.x;
-    if (t >= num_tiles) return;
-    counts[t] = (tile_offsets[t + 1] - tile_offsets[t] + kItemEntries - 1) / kItemEntries;
+// consecutive list entries, item k of tile t = (t, first entry, count).  Two
+// parallel launches build the table: per block of kItemSpan tiles the item
+// total, then per block the prefix of the earlier totals, a block scan and the
+// writes; the last block also stores the item count.
+constexpr int kItemThreads = 256;
+constexpr int kItemTilesPerThread = 4;
+constexpr int kItemSpan = kItemThreads * kItemTilesPerThread;
+
+__device__ __forceinline__ int tile_items(const int32_t* __restrict__ tile_offsets, int t) {
+    return (tile_offsets[t + 1] - tile_offsets[t] + kItemEntries - 1) / kItemEntries;
+}
+
+// Exclusive block scan of one int per thread; `total` receives the block sum.
+__device__ __forceinline__ int item_block_scan(int v, int* s_warp, int& total) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+#pragma unroll
+    for (int w = 0; w < kItemThreads / 32; ++w) {
+        const int c = s_warp[w];
+        before += w < warp ? c : 0;
+        total += c;
+    }
+    __syncthreads();
+    return before + x - v;
+}
+
+__global__ void __launch_bounds__(kItemThreads) k_item_block_sums(int num_tiles,
+                                                                   const int32_t* __restrict__ tile_offsets,
+                                                                   int32_t* __restrict__ block_items) {
+    __shared__ int s_warp[kItemThreads / 32];
+    const int t0 = blockIdx.x * kItemSpan + threadIdx.x * kItemTilesPerThread;
+    int local = 0;
+#pragma unroll
+    for (int k = 0; k < kItemTilesPerThread; ++k) local += t0 + k < num_tiles ? tile_items(tile_offsets, t0 + k) : 0;
+    int total;
+    item_block_scan(local, s_warp, total);
+    if (threadIdx.x == 0) block_items[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kItemThreads) k_item_table(int num_tiles, const int32_t* __restrict__ tile_offsets,
+                                                              const int32_t* __restrict__ block_items,
+                                                              int4* __restrict__ items, int32_t* __restrict__ num_items) {
+    __shared__ int s_warp[kItemThreads / 32];
+    int part = 0;
+    for (int b = threadIdx.x; b < static_cast<int>(blockIdx.x); b += kItemThreads) part += block_items[b];
+    int prefix;
+    item_block_scan(part, s_warp, prefix);
+    const int t0 = blockIdx.x * kItemSpan + threadIdx.x * kItemTilesPerThread;
+    int beg[kItemTilesPerThread + 1];
+#pragma unroll
+    for (int k = 0; k <= kItemTilesPerThread; ++k) beg[k] = t0 + k <= num_tiles ? tile_offsets[t0 + k] : 0;
+    int cnt[kItemTilesPerThread];
+    int local = 0;
+#pragma unroll
+    for (int k = 0; k < kItemTilesPerThread; ++k) {
+        cnt[k] = t0 + k < num_tiles ? (beg[k + 1] - beg[k] + kItemEntries - 1) / kItemEntries : 0;
+        local += cnt[k];
+    }
+    int total;
+    int run = prefix + item_block_scan(local, s_warp, total);
+#pragma unroll
+    for (int k = 0; k < kItemTilesPerThread; ++k) {
+        const int len = beg[k + 1] - beg[k];
+        for (int i = 0; i < cnt[k]; ++i) {
+            items[run + i] = make_int4(t0 + k, beg[k] + i * kItemEntries, min(kItemEntries, len - i * kItemEntries), 0);
+        }
+        run += cnt[k];
+    }
+    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) *num_items = prefix + total;
 }
 
 template <int FC>
 __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const float* __restrict__ pairgrad, int pstride,
                                                          const int32_t* __restrict__ pair_offset,
+                                                         const float* __restrict__ geo,
                                                          const float* __restrict__ feat,
                                                          const float* __restrict__ opacity,
                                                          const float* __restrict__ scale, const float* __restrict__ rot,
@@ -448,8 +542,10 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
             }
         }
     }
-    d_xy[2 * g + 0] = s0;
-    d_xy[2 * g + 1] = s1;
+    // (s0, s1) = (sum Sx, sum Sy); the raw conic (a, b, d) is geo[g][5..7]
+    const float4 k1 = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8)[1];
+    d_xy[2 * g + 0] = fmaf(k1.y, s0, k1.z * s1);
+    d_xy[2 * g + 1] = fmaf(k1.z, s0, k1.w * s1);
     d_conic[3 * g + 0] = s2;
     d_conic[3 * g + 1] = s3;
     d_conic[3 * g + 2] = s4;
@@ -473,38 +569,51 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
     }
 }
 
-template <int FC>
-cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
-                          const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
-                          const int32_t* item_offsets, int num_tiles, const float* grad_image, const int32_t* aabb,
-                          const int32_t* pair_offset, float* pairgrad, int pstride, float* d_xy, float* d_conic,
-                          float* d_feat, cudaStream_t stream) {
+template <int FC, int MODE>
+cudaError_t launch_bwd_mode(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
+                            const float* opacity, const int32_t* gid_sorted, const int4* items,
+                            const int32_t* num_items, const float* grad_image, const int32_t* aabb,
+                            const int32_t* pair_offset, const float* records, const int32_t* slots, float* pairgrad,
+                            int pstride, float* d_xy, float* d_conic, float* d_feat, cudaStream_t stream) {
     const int smem = BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT * static_cast<int>(sizeof(float));
     const unsigned blocks = static_cast<unsigned>(div_up(max_items, BwdCfg<FC>::WARPS));
-    if (pairgrad != nullptr) {
-        auto kern = k_render_bwd<FC, true>;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
-            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets, num_tiles, grad_image,
-            reinterpret_cast<const int4*>(aabb), pair_offset, pairgrad, pstride, d_xy, d_conic, d_feat);
-    } else {
-        auto kern = k_render_bwd<FC, false>;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
-            f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets, num_tiles, grad_image,
-            reinterpret_cast<const int4*>(aabb), pair_offset, pairgrad, pstride, d_xy, d_conic, d_feat);
-    }
+    auto kern = k_render_bwd<FC, MODE>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
+        f, h, w, ntx, geo, feat, opacity, gid_sorted, items, num_items, grad_image,
+        reinterpret_cast<const int4*>(aabb), pair_offset, records, slots, pairgrad, pstride, d_xy, d_conic, d_feat);
     return cudaGetLastError();
 }
 
 template <int FC>
+cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
+                          const float* opacity, const int32_t* gid_sorted, const int4* items, const int32_t* num_items,
+                          const float* grad_image, const int32_t* aabb, const int32_t* pair_offset,
+                          const float* records, const int32_t* slots, float* pairgrad, int pstride, float* d_xy,
+                          float* d_conic, float* d_feat, cudaStream_t stream) {
+    if (pairgrad == nullptr) {
+        return launch_bwd_mode<FC, kAtomicGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
+                                                  num_items, grad_image, aabb, pair_offset, records, slots, pairgrad,
+                                                  pstride, d_xy, d_conic, d_feat, stream);
+    }
+    if (records != nullptr) {
+        return launch_bwd_mode<FC, kDetRecords>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
+                                                num_items, grad_image, aabb, pair_offset, records, slots, pairgrad,
+                                                pstride, d_xy, d_conic, d_feat, stream);
+    }
+    return launch_bwd_mode<FC, kDetGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items,
+                                           grad_image, aabb, pair_offset, records, slots, pairgrad, pstride, d_xy,
+                                           d_conic, d_feat, stream);
+}
+
+template <int FC>
 cudaError_t launch_reduce_fc(int n, int f, const float* pairgrad, int pstride, const int32_t* pair_offset,
-                             const float* feat, const float* opacity, const float* scale, const float* rot,
-                             float* d_xy, float* d_conic, float* d_feat, float* d_opacity, float* d_scale,
-                             float* d_rot, cudaStream_t stream) {
+                             const float* geo, const float* feat, const float* opacity, const float* scale,
+                             const float* rot, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                             float* d_scale, float* d_rot, cudaStream_t stream) {
     k_reduce_gaussian<FC><<<static_cast<unsigned>(div_up(n, 256)), 256, 0, stream>>>(
-        n, f, pairgrad, pstride, pair_offset, feat, opacity, scale, rot, d_xy, d_conic, d_feat, d_opacity, d_scale,
-        d_rot);
+        n, f, pairgrad, pstride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, d_feat, d_opacity,
+        d_scale, d_rot);
     return cudaGetLastError();
 }
 
@@ -517,9 +626,8 @@ int64_t backward_max_items(int64_t total_pairs, int64_t num_tiles) {
 }
 
 int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
-    (void)total_pairs;
-    return arena_bytes(num_tiles, sizeof(int32_t)) + arena_bytes(num_tiles + 1, sizeof(int32_t)) +
-           scan_scratch_bytes(num_tiles);
+    return arena_bytes(backward_max_items(total_pairs, num_tiles), sizeof(int4)) + arena_bytes(1, sizeof(int32_t)) +
+           arena_bytes(div_up(num_tiles, kItemSpan), sizeof(int32_t));
 }
 
 #define OSS_DISPATCH_FC(f, CALL) \
@@ -528,38 +636,41 @@ int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo, const float* feat,
                                          const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
-                                         const int32_t* pair_offset, float* pairgrad, int pair_stride, float* d_xy,
-                                         float* d_conic, float* d_feat, void* items_scratch, cudaStream_t stream) {
+                                         const int32_t* pair_offset, const float* records, const int32_t* slots,
+                                         float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
+                                         void* items_scratch, cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
     if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
     const int64_t max_items = backward_max_items(total_pairs, num_tiles);
     Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
-    int32_t* counts = arena.take<int32_t>(num_tiles);
-    int32_t* item_offsets = arena.take<int32_t>(num_tiles + 1);
-    void* scan_scratch = arena.base + arena.used;
-    k_item_counts<<<static_cast<unsigned>(div_up(num_tiles, 256)), 256, 0, stream>>>(num_tiles, tile_offsets, counts);
+    int4* items = arena.take<int4>(max_items);
+    int32_t* num_items = arena.take<int32_t>(1);
+    const int item_blocks = static_cast<int>(div_up(num_tiles, kItemSpan));
+    int32_t* block_items = arena.take<int32_t>(item_blocks);
+    k_item_block_sums<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(num_tiles, tile_offsets,
+                                                                                         block_items);
+    k_item_table<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(num_tiles, tile_offsets,
+                                                                                    block_items, items, num_items);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    err = scan_exclusive_i32(counts, item_offsets, num_tiles, true, nullptr, scan_scratch, stream);
-    if (err != cudaSuccess) return err;
 #define OSS_BWD_CALL(FC)                                                                                          \
-    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, tile_offsets, item_offsets,       \
-                      num_tiles, grad_image, aabb, pair_offset, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
+    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items, grad_image,     \
+                      aabb, pair_offset, records, slots, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
     return OSS_DISPATCH_FC(f, OSS_BWD_CALL);
 #undef OSS_BWD_CALL
 }
 
 cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,
-                                         const int32_t* pair_offset, const float* feat, const float* opacity,
-                                         const float* scale, const float* rot, float* d_xy, float* d_conic,
-                                         float* d_feat, float* d_opacity, float* d_scale, float* d_rot,
-                                         cudaStream_t stream) {
+                                         const int32_t* pair_offset, const float* geo, const float* feat,
+                                         const float* opacity, const float* scale, const float* rot, float* d_xy,
+                                         float* d_conic, float* d_feat, float* d_opacity, float* d_scale,
+                                         float* d_rot, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
 #define OSS_RED_CALL(FC)                                                                                          \
-    launch_reduce_fc<FC>(n, f, pairgrad, pair_stride, pair_offset, feat, opacity, scale, rot, d_xy, d_conic, d_feat, \
-                         d_opacity, d_scale, d_rot, stream)
+    launch_reduce_fc<FC>(n, f, pairgrad, pair_stride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, \
+                         d_feat, d_opacity, d_scale, d_rot, stream)
     return OSS_DISPATCH_FC(f, OSS_RED_CALL);
 #undef OSS_RED_CALL
 }

@@ -14,6 +14,11 @@
 // same results as the scalar form), which halves the FP32 issue slots and
 // leaves the ex2 (MUFU, 16 per SM per clock) as the bound.
 //
+// With `records` non-null the staging pass also writes, for every list entry in
+// list order, the record the backward reads instead of gathering it again:
+// [x, y, A, B | D, feat'(F) | zero padding] (entry_record_floats(F) floats), and
+// the entry's gid-major pair slot pair_offset[g] + (local tile index).
+//
 // The reference zeroes a weight when q is non-finite or negative
 // (rasterizer_fwd.cu:245).  A batch whose conics are all finite and
 // well-conditioned (det >= 1e-3 * a * d, i.e. axis ratio below ~60) has
@@ -125,7 +130,11 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
                                                                 const float* __restrict__ opacity,
                                                                 const int32_t* __restrict__ gid_sorted,
                                                                 const int32_t* __restrict__ tile_offsets,
-                                                                float* __restrict__ image) {
+                                                                float* __restrict__ image,
+                                                                const int4* __restrict__ aabb,
+                                                                const int32_t* __restrict__ pair_offset,
+                                                                float* __restrict__ records,
+                                                                int32_t* __restrict__ slots) {
     constexpr int PX = FwdCfg<FC>::PX;
     constexpr int NT = FwdCfg<FC>::NT;
     constexpr int S = FwdCfg<FC>::S;
@@ -179,6 +188,18 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
             const float* fg = feat + static_cast<int64_t>(g) * F;
 #pragma unroll
             for (int c = 0; c < FC; ++c) df[1 + c] = c < F ? fg[c] * op : 0.0f;
+#pragma unroll
+            for (int c = 1 + FC; c < S; ++c) df[c] = 0.0f;
+            if (records != nullptr) {
+                const int e = b + j;
+                float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(e) * (4 + S));
+                rec[0] = g0;
+                const float4* df4 = reinterpret_cast<const float4*>(df);
+#pragma unroll
+                for (int v = 0; v < S / 4; ++v) rec[1 + v] = df4[v];
+                const int4 box = aabb[g];
+                slots[e] = pair_offset[g] + (tile / ntx - box.y) * (box.z - box.x) + (tile % ntx - box.x);
+            }
         }
         const bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
         if constexpr (PK) {
@@ -223,28 +244,50 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
 template <int FC>
 cudaError_t launch_fwd_fc(int f, int h, int w, int ntx, int num_tiles, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
+                          const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
                           cudaStream_t stream) {
     k_render_fwd<FC><<<static_cast<unsigned>(num_tiles), FwdCfg<FC>::NT, 0, stream>>>(
-        f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, image);
+        f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, image, reinterpret_cast<const int4*>(aabb),
+        pair_offset, records, slots);
     return cudaGetLastError();
+}
+
+template <int FC>
+constexpr int record_floats_fc() {
+    return 4 + FwdCfg<FC>::S;
 }
 
 }  // namespace
 
+int entry_record_floats(int f) {
+    if (f <= 1) return record_floats_fc<1>();
+    if (f <= 3) return record_floats_fc<3>();
+    if (f <= 4) return record_floats_fc<4>();
+    if (f <= 8) return record_floats_fc<8>();
+    if (f <= 16) return record_floats_fc<16>();
+    if (f <= 32) return record_floats_fc<32>();
+    return record_floats_fc<64>();
+}
+
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat, const float* opacity,
                                   const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
+                                  const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
                                   cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
     if (num_tiles == 0 || f == 0) return cudaSuccess;
-    if (f <= 1) return launch_fwd_fc<1>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    if (f <= 3) return launch_fwd_fc<3>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    if (f <= 4) return launch_fwd_fc<4>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    if (f <= 8) return launch_fwd_fc<8>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    if (f <= 16) return launch_fwd_fc<16>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    if (f <= 32) return launch_fwd_fc<32>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
-    return launch_fwd_fc<64>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, stream);
+#define OSS_FWD_CALL(FC)                                                                                           \
+    launch_fwd_fc<FC>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, aabb,          \
+                      pair_offset, records, slots, stream)
+    if (f <= 1) return OSS_FWD_CALL(1);
+    if (f <= 3) return OSS_FWD_CALL(3);
+    if (f <= 4) return OSS_FWD_CALL(4);
+    if (f <= 8) return OSS_FWD_CALL(8);
+    if (f <= 16) return OSS_FWD_CALL(16);
+    if (f <= 32) return OSS_FWD_CALL(32);
+    return OSS_FWD_CALL(64);
+#undef OSS_FWD_CALL
 }
 
 }  // namespace oss

@@ -35,17 +35,19 @@ SIGNATURES = {
         ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_bin_pairs": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _p]),
-    "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_entry_record_floats": (ctypes.c_int, [_i64]),
+    "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_render_backward_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_render_backward": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
+        [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+         _i64, _p],
     ),
     "oss_pair_grad_stride": (ctypes.c_int, [_i64]),
     "oss_render_backward_pairs_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_render_backward_pairs": (
-        ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _i64, _p]),
-    "oss_reduce_pair_grads": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+        ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_reduce_pair_grads": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_rasterize_backward_lists_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_rasterize_backward_lists": (
         ctypes.c_int,

@@ -171,22 +171,34 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
 
 
-def render_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None) -> torch.Tensor:
+def render_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, records: bool = False):
+    """(F, H, W) image; with records=True also the per-entry records and pair
+    slots the backward reads (returns (image, records, slots))."""
     lib = _lib.lib()
     f = int(feat.size(1))
-    image = torch.empty((f, b.h, b.w), device=feat.device, dtype=torch.float32)
+    dev = feat.device
+    image = torch.empty((f, b.h, b.w), device=dev, dtype=torch.float32)
+    rec = slots = None
+    if records and b.mode != _lib.OSS_BIN_FULL and b.total_pairs > 0:
+        rec = torch.empty((b.total_pairs, lib.oss_entry_record_floats(f)), device=dev, dtype=torch.float32)
+        slots = torch.empty((b.total_pairs,), device=dev, dtype=torch.int32)
     _lib.check(
         lib.oss_render_forward(b.n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
                                b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(), image.data_ptr(),
+                               b.aabb.data_ptr(), b.pair_offset.data_ptr(), _lib.ptr(rec), _lib.ptr(slots),
                                stream_of(feat)),
         "oss_render_forward",
     )
+    if records:
+        return image, rec, slots
     return image
 
 
 def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, scale: torch.Tensor,
-                    rot: torch.Tensor, grad_image: torch.Tensor):
-    """Deterministic gradients (d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot)."""
+                    rot: torch.Tensor, grad_image: torch.Tensor, records: torch.Tensor | None = None,
+                    slots: torch.Tensor | None = None):
+    """Deterministic gradients (d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot);
+    records/slots are the forward's entry records (None: gathered again)."""
     lib = _lib.lib()
     dev = feat.device
     n, f = b.n, int(feat.size(1))
@@ -204,8 +216,9 @@ def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
     _lib.check(
         lib.oss_render_backward(n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
                                 scale.data_ptr(), rot.data_ptr(), b.aabb.data_ptr(), b.pair_offset.data_ptr(),
-                                b.total_pairs, b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(),
-                                grad_image.data_ptr(), d_xy.data_ptr(), d_conic.data_ptr(), d_feat.data_ptr(),
+                                b.total_pairs, b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(), _lib.ptr(records),
+                                _lib.ptr(slots), grad_image.data_ptr(), d_xy.data_ptr(), d_conic.data_ptr(),
+                                d_feat.data_ptr(),
                                 _lib.ptr(d_opacity), d_scale.data_ptr(), d_rot.data_ptr(), scratch.data_ptr(),
                                 scratch.numel(), stream_of(feat)),
         "oss_render_backward",

@@ -44,15 +44,20 @@ class _RasterizeGaussians(Function):
         del topk_norm
         with torch.cuda.device(xy.device):
             b = _raster.bin_gaussians(xy, scale, rot, h, w, mode)
-            out = _raster.render_forward(b, _raster.aligned(feat, 4), opacity)
+            # the entry records the backward reads are written only when a gradient can follow
+            if any(ctx.needs_input_grad[:5]):
+                out, records, slots = _raster.render_forward(b, _raster.aligned(feat, 4), opacity, records=True)
+            else:
+                out, records, slots = _raster.render_forward(b, _raster.aligned(feat, 4), opacity), None, None
         ctx.save_for_backward(xy, scale, rot, feat, opacity, b.conic, b.aabb, b.pair_offset, b.geo, b.gid_sorted,
-                              b.tile_offsets)
+                              b.tile_offsets, records, slots)
         ctx.meta = (b.n, b.h, b.w, b.mode, b.total_pairs)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, gid_sorted, tile_offsets = ctx.saved_tensors
+        (xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, gid_sorted, tile_offsets, records,
+         slots) = ctx.saved_tensors
         n, h, w, mode, total_pairs = ctx.meta
         b = _raster.Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
         grad = grad_out.contiguous()
@@ -60,7 +65,7 @@ class _RasterizeGaussians(Function):
             grad = grad.float()
         with torch.cuda.device(xy.device):
             d_xy, _d_conic, d_feat, d_opacity, d_scale, d_rot = _raster.render_backward(
-                b, _raster.aligned(feat, 4), opacity, scale, rot, grad
+                b, _raster.aligned(feat, 4), opacity, scale, rot, grad, records, slots
             )
         return d_xy, d_scale, d_rot, d_feat, d_opacity, None, None, None, None, None
 

@@ -44,7 +44,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_clean_error_state():
     lib = _lib.lib()
-    assert lib.oss_abi_version() == 3
+    assert lib.oss_abi_version() == 4
 
 
 def test_rejects_tile_size_other_than_16():
@@ -65,7 +65,8 @@ def test_rejects_bad_sizes_and_modes():
     assert lib.oss_render_prepare(1, 32, 32, 7, None, None, None, None, None, None, None, None, None, None, None,
                                   0, None) == 1
     assert "binning mode" in lib.oss_last_error().decode()
-    assert lib.oss_render_forward(1, 65, 32, 32, None, None, None, None, None, None, None) == 1
+    assert lib.oss_render_forward(1, 65, 32, 32, None, None, None, None, None, None, None, None, None, None,
+                                  None) == 1
     assert lib.oss_last_error().decode() == "F must be <= 64"
     assert lib.oss_full_tile_pairs(1 << 20, 1 << 12, None, None, None) == 3
     assert "full-frame" in lib.oss_last_error().decode()
@@ -99,7 +100,8 @@ def test_scratch_sizes_are_monotone():
     a = lib.oss_bin_pairs_scratch_bytes(1000, 10_000, 500)
     b = lib.oss_bin_pairs_scratch_bytes(1000, 20_000, 500)
     assert 0 < a < b
-    assert lib.oss_render_backward_scratch_bytes(1000, 3, 10) >= 1000 * 8 * 4 + (10 + 32) * 8
+    assert lib.oss_render_backward_scratch_bytes(1000, 3, 10) >= 1000 * 8 * 4 + (10 + 32) * 16
+    assert lib.oss_entry_record_floats(3) == 8 and lib.oss_entry_record_floats(64) % 4 == 0
     assert lib.oss_tile_bin_counting_sort_scratch_bytes(0, 1) > 0
 
 

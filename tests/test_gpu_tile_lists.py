@@ -155,7 +155,8 @@ def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
     lib, s_ = L.lib, torch.cuda.current_stream().cuda_stream
     img = torch.full((3, h, w), 5.0, device="cuda")
     _lib.check(lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
-                                      L.tile_offsets.data_ptr(), img.data_ptr(), s_), "forward")
+                                      L.tile_offsets.data_ptr(), img.data_ptr(), None, None, None, None, s_),
+               "forward")
     assert not host(img).any()
     grad = dev(rng.standard_normal((3, h, w)))
     nb = lib.oss_render_backward_scratch_bytes(L.capacity, 3, L.tiles)
@@ -163,7 +164,7 @@ def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
     outs = [torch.full(sh, 9.0, device="cuda") for sh in ((n, 2), (n, 3), (n, 3))]
     _lib.check(lib.oss_render_backward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, None, None,
                                        L.aabb.data_ptr(), L.pair_offset.data_ptr(), L.capacity, L.gid.data_ptr(),
-                                       L.tile_offsets.data_ptr(), grad.data_ptr(), outs[0].data_ptr(),
+                                       L.tile_offsets.data_ptr(), None, None, grad.data_ptr(), outs[0].data_ptr(),
                                        outs[1].data_ptr(), outs[2].data_ptr(), None, None, None, scratch.data_ptr(),
                                        scratch.numel(), s_), "backward")
     for t in outs:
@@ -199,7 +200,7 @@ def test_sync_free_path_replays_in_cuda_graph(cuda_device):
     def step():
         L.run()
         _lib.check(L.lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
-                                            L.tile_offsets.data_ptr(), img.data_ptr(),
+                                            L.tile_offsets.data_ptr(), img.data_ptr(), None, None, None, None,
                                             torch.cuda.current_stream().cuda_stream), "forward")
 
     side = torch.cuda.Stream()
