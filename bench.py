@@ -235,7 +235,7 @@ class Pipeline:
             self._ensure(self.pairs)
         self._mark(2, timed)
         chk(lib.oss_bin_pairs(n, h, w, self.mode, self.aabb.data_ptr(), self.pair_offset.data_ptr(),
-                              self.tile_count.data_ptr(), self.total.data_ptr(), self.capacity,
+                              self.tile_count.data_ptr(), self.total.data_ptr(), self.capacity, None, None,
                               self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
                               self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
         self._mark(3, timed)

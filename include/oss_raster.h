@@ -120,8 +120,22 @@ OSS_API int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t
 OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
                   const int32_t* aabb, int32_t* pair_offset, int32_t* tile_count,
                   const int64_t* total_pairs, int64_t capacity,
+                  const int32_t* sort_key, const int32_t* key_order,
                   int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow,
                   void* scratch, int64_t scratch_bytes, void* stream);
+/* sort_key / key_order (both NULL, or both set; not in OSS_BIN_FULL mode):
+ * order every tile list by sort_key[g] (a permutation of [0, n)) instead of
+ * gid; key_order[k] = the gid with key k.  oss_depth_order makes them for the
+ * alpha-blend mode (rank and order of the Gaussians by depth). */
+
+/* ---------------------------------------------------------------------------
+ * Stable depth order for the alpha-blend lists: order[i] = the gid at position
+ * i of the Gaussians sorted by (depth, gid) ascending, rank[g] = its position
+ * (-0.0 counts as +0.0; -inf first, +inf last).
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_depth_order_scratch_bytes(int64_t n);
+OSS_API int oss_depth_order(int64_t n, const float* depth, int32_t* order, int32_t* rank,
+                    void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Forward additive render: image[c][p] = sum over the tile list of p of
@@ -189,6 +203,39 @@ OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
                           const float* scale, const float* rot,
                           float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
                           float* d_scale, float* d_rot, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Alpha-blend mode (blend="alpha"; no reference counterpart -- the reference
+ * rasterizer is additive only).  Over lists ordered by (depth, gid) (sort_key
+ * = rank from oss_depth_order), per pixel front to back:
+ *   a = min(0.99, opacity * exp(-q/2)) (0 for q < 0 or non-finite); entries
+ *   with a < 1/255 are skipped; compositing stops before the first entry whose
+ *   T (1 - a) would fall below 1e-4; C += feat a T; T *= 1 - a;
+ *   image = C + T * background (background: device f floats, NULL = 0;
+ *   opacity NULL = 1).
+ * The forward also writes t_final[h][w] (final T) and n_contrib[h][w] (1 +
+ * the tile-list position of the last composited entry), which the backward
+ * needs.  The backward writes deterministic per-pair rows into scratch
+ * (oss_render_alpha_backward_scratch_bytes) and reduces them per Gaussian:
+ * d_xy, d_conic, d_feat (w.r.t. feat), d_opacity, and d_scale / d_rot when
+ * d_scale is non-null.  total_pairs may be any upper bound of the pair count.
+ * ------------------------------------------------------------------------- */
+OSS_API int oss_render_alpha_forward(int64_t n, int64_t f, int64_t h, int64_t w,
+                             const float* geo, const float* feat, const float* opacity,
+                             const float* background, const int32_t* gid_sorted,
+                             const int32_t* tile_offsets, float* image, float* t_final,
+                             int32_t* n_contrib, void* stream);
+OSS_API int oss_alpha_pair_grad_stride(int64_t f);
+OSS_API int64_t oss_render_alpha_backward_scratch_bytes(int64_t total_pairs, int64_t f);
+OSS_API int oss_render_alpha_backward(int64_t n, int64_t f, int64_t h, int64_t w,
+                              const float* geo, const float* feat, const float* opacity,
+                              const float* background, const float* scale, const float* rot,
+                              const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                              const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* t_final, const int32_t* n_contrib,
+                              const float* grad_image, float* d_xy, float* d_conic, float* d_feat,
+                              float* d_opacity, float* d_scale, float* d_rot,
+                              void* scratch, int64_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Backward for arbitrary caller lists (per-pair partial sums, then fp32 atomics):

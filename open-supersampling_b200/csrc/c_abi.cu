@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 4; }
+int oss_abi_version(void) { return 5; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -143,8 +143,9 @@ int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_til
 }
 
 int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, int32_t* pair_offset,
-                  int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, int32_t* gid_sorted,
-                  int32_t* tile_offsets, int32_t* overflow, void* scratch, int64_t scratch_bytes, void* stream) {
+                  int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, const int32_t* sort_key,
+                  const int32_t* key_order, int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow,
+                  void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
@@ -172,8 +173,90 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
                   (aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr && tile_count != nullptr &&
                    total_pairs != nullptr && (capacity == 0 || scratch != nullptr)),
               OSS_ERR_INVALID, "aabb (16-byte aligned), pair_offset, tile_count, total_pairs and scratch must be non-null");
+    OSS_CHECK((sort_key == nullptr) == (key_order == nullptr), OSS_ERR_INVALID,
+              "sort_key and key_order go together");
+    OSS_CHECK(mode != OSS_BIN_FULL || sort_key == nullptr, OSS_ERR_INVALID, "full-frame lists take no sort key");
     OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
-                                       gid_sorted, tile_offsets, overflow, scratch, s));
+                                       sort_key, key_order, gid_sorted, tile_offsets, overflow, scratch, s));
+    return OSS_OK;
+}
+
+int64_t oss_depth_order_scratch_bytes(int64_t n) { return oss::depth_order_scratch_bytes(n < 0 ? 0 : n); }
+
+int oss_depth_order(int64_t n, const float* depth, int32_t* order, int32_t* rank, void* scratch,
+                    int64_t scratch_bytes, void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");
+    OSS_CHECK(n <= INT_MAX, OSS_ERR_RANGE, "N exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_depth_order_scratch_bytes(n), OSS_ERR_SCRATCH, "depth_order scratch too small");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(depth != nullptr && order != nullptr && rank != nullptr && scratch != nullptr, OSS_ERR_INVALID,
+              "depth, order, rank and scratch must be non-null");
+    OSS_CUDA_TRY(oss::depth_order(static_cast<int>(n), depth, order, rank, scratch, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_render_alpha_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                             const float* opacity, const float* background, const int32_t* gid_sorted,
+                             const int32_t* tile_offsets, float* image, float* t_final, int32_t* n_contrib,
+                             void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    if (g.tiles == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && t_final != nullptr && n_contrib != nullptr && (f == 0 || image != nullptr),
+              OSS_ERR_INVALID, "tile_offsets, image, t_final and n_contrib must be non-null");
+    OSS_CHECK(g.n == 0 || (geo != nullptr && aligned(geo, 16) && (f == 0 || feat != nullptr)), OSS_ERR_INVALID,
+              "geo (16-byte aligned) and feat must be non-null");
+    OSS_CUDA_TRY(oss::launch_render_alpha_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, background,
+                                                  gid_sorted, tile_offsets, image, t_final, n_contrib,
+                                                  as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_alpha_pair_grad_stride(int64_t f) {
+    return oss::alpha_pair_stride(static_cast<int>(f < 0 ? 0 : (f > OSS_MAX_CHANNELS ? OSS_MAX_CHANNELS : f)));
+}
+
+int64_t oss_render_alpha_backward_scratch_bytes(int64_t total_pairs, int64_t f) {
+    if (total_pairs < 0) total_pairs = 0;
+    return oss::arena_bytes(total_pairs * oss_alpha_pair_grad_stride(f), 4);
+}
+
+int oss_render_alpha_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                              const float* opacity, const float* background, const float* scale, const float* rot,
+                              const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                              const int32_t* gid_sorted, const int32_t* tile_offsets, const float* t_final,
+                              const int32_t* n_contrib, const float* grad_image, float* d_xy, float* d_conic,
+                              float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* scratch,
+                              int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_render_alpha_backward_scratch_bytes(total_pairs, f), OSS_ERR_SCRATCH,
+              "render_alpha_backward scratch too small");
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
+              OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
+    OSS_CHECK(d_xy != nullptr && d_conic != nullptr && (f == 0 || (feat != nullptr && d_feat != nullptr)),
+              OSS_ERR_INVALID, "gradient outputs must be non-null");
+    OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
+              "d_scale needs scale, rot and d_rot");
+    cudaStream_t s = as_stream(stream);
+    float* pairgrad = static_cast<float*>(scratch);
+    if (g.tiles > 0 && total_pairs > 0) {
+        OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
+        OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && t_final != nullptr && n_contrib != nullptr &&
+                      grad_image != nullptr,
+                  OSS_ERR_INVALID, "lists, t_final, n_contrib and grad_image must be non-null");
+        OSS_CUDA_TRY(oss::launch_render_alpha_backward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, background,
+                                                       gid_sorted, tile_offsets, t_final, n_contrib, grad_image, aabb,
+                                                       pair_offset, pairgrad, s));
+    }
+    OSS_CUDA_TRY(oss::launch_reduce_alpha_grads(g.n, static_cast<int>(f), pairgrad, pair_offset, geo, scale, rot, d_xy,
+                                                d_conic, d_feat, d_opacity, d_scale, d_rot, s));
     return OSS_OK;
 }
 

@@ -73,11 +73,18 @@ cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
 // counts are consumed): atomic scatter, then a per-tile sort.  The pair total
 // is read from *total_pairs on the device; above capacity every list and pair
 // range is emptied and *overflow = 1.
+// With sort_key (a permutation of [0, n)) the lists are ordered by key and
+// mapped back to gids through key_order (key -> gid).
 int64_t tile_lists_scratch_bytes(int64_t capacity);
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
                              int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
-                             int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,
-                             cudaStream_t stream);
+                             const int32_t* sort_key, const int32_t* key_order, int32_t* gid_sorted,
+                             int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream);
+// Stable order of the Gaussians by depth (ties by gid): order[i] = gid of rank i,
+// rank[gid] = its position.
+int64_t depth_order_scratch_bytes(int64_t n);
+cudaError_t depth_order(int n, const float* depth, int32_t* order, int32_t* rank, void* scratch,
+                        cudaStream_t stream);
 
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);
@@ -119,5 +126,25 @@ cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, in
                                          float* d_xy, float* d_conic, float* d_feat,
                                          float* d_opacity, float* d_scale, float* d_rot,
                                          cudaStream_t stream);
+
+// ---- raster_alpha.cu -------------------------------------------------------
+// Front-to-back alpha compositing over (depth, gid)-ordered lists, its
+// back-to-front backward into per-pair rows (Sx, Sy, d_conic(3), dF(F),
+// d_opacity) of alpha_pair_stride(f) floats, and the per-Gaussian reduce.
+int alpha_pair_stride(int f);
+cudaError_t launch_render_alpha_forward(int f, int h, int w, const float* geo, const float* feat,
+                                        const float* opacity, const float* background, const int32_t* gid_sorted,
+                                        const int32_t* tile_offsets, float* image, float* t_final,
+                                        int32_t* n_contrib, cudaStream_t stream);
+cudaError_t launch_render_alpha_backward(int f, int h, int w, const float* geo, const float* feat,
+                                         const float* opacity, const float* background,
+                                         const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                         const float* t_final, const int32_t* n_contrib, const float* grad_image,
+                                         const int32_t* aabb, const int32_t* pair_offset, float* pairgrad,
+                                         cudaStream_t stream);
+cudaError_t launch_reduce_alpha_grads(int n, int f, const float* pairgrad, const int32_t* pair_offset,
+                                      const float* geo, const float* scale, const float* rot, float* d_xy,
+                                      float* d_conic, float* d_feat, float* d_opacity, float* d_scale,
+                                      float* d_rot, cudaStream_t stream);
 
 }  // namespace oss

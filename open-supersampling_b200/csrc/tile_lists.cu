@@ -9,6 +9,10 @@
 // tile at most once, so a sorted list is unique: the output is the reference's
 // list whatever order the atomics ran in.
 //
+// With a sort key (a permutation of [0, n), e.g. a Gaussian's rank by depth)
+// the lists hold keys while they are sorted and are mapped back to gids through
+// key_order on output: the lists come out ordered by key instead of gid.
+//
 // The pair total is read on the device and checked against the caller's
 // capacity; on overflow every list and every Gaussian's pair range is emptied
 // and a flag is raised, so nothing downstream reads or writes past capacity and
@@ -36,7 +40,8 @@ constexpr int kWindowBits = kSortBuf * 32;        // gid window of the bitmap pa
 __global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
     int n, int ntx, int num_tiles, const int4* __restrict__ aabb, int32_t* __restrict__ pair_offset,
     int32_t* __restrict__ tile_count, int32_t* __restrict__ tile_offsets, const int64_t* __restrict__ total_pairs,
-    int64_t capacity, int32_t* __restrict__ unsorted, int32_t* __restrict__ overflow) {
+    int64_t capacity, const int32_t* __restrict__ sort_key, int32_t* __restrict__ unsorted,
+    int32_t* __restrict__ overflow) {
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x;
     const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kScatterThreads;
     if (*total_pairs > capacity) {
@@ -51,7 +56,11 @@ __global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
     const int g0 = (blockIdx.x * kScatterWarps + (threadIdx.x >> 5)) * 32;
     const int g = g0 + lane;
     int4 box = make_int4(0, 0, 0, 0);
-    if (g < n) box = aabb[g];
+    int key = g;
+    if (g < n) {
+        box = aabb[g];
+        if (sort_key != nullptr) key = sort_key[g];
+    }
     const int bw = box.z > box.x ? box.z - box.x : 0;
     const int bh = box.w > box.y ? box.w - box.y : 0;
     const int cnt = bw * bh;
@@ -77,12 +86,13 @@ __global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
         const int o_x = __shfl_sync(0xffffffffu, box.x, owner);
         const int o_y = __shfl_sync(0xffffffffu, box.y, owner);
         const int o_w = __shfl_sync(0xffffffffu, bw, owner);
+        const int o_key = __shfl_sync(0xffffffffu, key, owner);
         if (j < warp_total) {
             const int k = j - o_start;
             const int dy = k / o_w;
             const int t = (o_y + dy) * ntx + o_x + (k - dy * o_w);
             const int slot = atomicSub(&tile_count[static_cast<int64_t>(t) * kTileCountStride], 1) - 1;
-            unsorted[tile_offsets[t] + slot] = g0 + owner;
+            unsorted[tile_offsets[t] + slot] = o_key;
         }
     }
 }
@@ -152,7 +162,7 @@ __device__ __forceinline__ void warp_bitonic(int32_t (&v)[R], int lane) {
 
 template <int R>
 __device__ __forceinline__ void warp_sort_list(const int32_t* __restrict__ src, int32_t* __restrict__ dst, int len,
-                                               int lane) {
+                                               int lane, const int32_t* __restrict__ key_order) {
     int32_t v[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -163,7 +173,7 @@ __device__ __forceinline__ void warp_sort_list(const int32_t* __restrict__ src, 
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int e = r * 32 + lane;
-        if (e < len) dst[e] = v[r];
+        if (e < len) dst[e] = key_order != nullptr ? key_order[v[r]] : v[r];
     }
 }
 
@@ -194,7 +204,7 @@ __device__ __forceinline__ int block_exclusive_sum(int v, int* s_warp, int& tota
 // range in a shared bitmap and writes the set bits out in order, window by
 // window.  Cost per window: one pass over the list plus the bitmap.
 __device__ void bitmap_sort(const int32_t* __restrict__ in, int32_t* __restrict__ out, int len, int n,
-                            int32_t* s_buf, int* s_warp) {
+                            int32_t* s_buf, int* s_warp, const int32_t* __restrict__ key_order) {
     uint32_t* bm = reinterpret_cast<uint32_t*>(s_buf);
     constexpr int kWordsPerThread = kSortBuf / kSortThreads;
     int written = 0;
@@ -217,7 +227,8 @@ __device__ void bitmap_sort(const int32_t* __restrict__ in, int32_t* __restrict_
             while (bits != 0u) {
                 const int b = __ffs(static_cast<int>(bits)) - 1;
                 bits &= bits - 1u;
-                out[pos++] = static_cast<int32_t>(base + (w0 + w) * 32 + b);
+                const int32_t v = static_cast<int32_t>(base + (w0 + w) * 32 + b);
+                out[pos++] = key_order != nullptr ? key_order[v] : v;
             }
         }
         written += total;
@@ -229,6 +240,7 @@ __device__ void bitmap_sort(const int32_t* __restrict__ in, int32_t* __restrict_
 __global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tiles,
                                                               const int32_t* __restrict__ tile_offsets,
                                                               const int32_t* __restrict__ unsorted,
+                                                              const int32_t* __restrict__ key_order,
                                                               int32_t* __restrict__ gid_sorted) {
     __shared__ int32_t s_buf[kSortBuf];
     __shared__ int s_warp[kSortWarps];
@@ -252,17 +264,17 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tile
         int rank = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, v, j) < v ? 1 : 0;
-        if (lane < len) dst[rank] = v;
+        if (lane < len) dst[rank] = key_order != nullptr ? key_order[v] : v;
     } else if (len <= 64) {
-        warp_sort_list<2>(src, dst, len, lane);
+        warp_sort_list<2>(src, dst, len, lane, key_order);
     } else if (len <= 128) {
-        warp_sort_list<4>(src, dst, len, lane);
+        warp_sort_list<4>(src, dst, len, lane, key_order);
     } else if (len <= 256) {
-        warp_sort_list<8>(src, dst, len, lane);
+        warp_sort_list<8>(src, dst, len, lane, key_order);
     } else if (len <= 512) {
-        warp_sort_list<16>(src, dst, len, lane);
+        warp_sort_list<16>(src, dst, len, lane, key_order);
     } else if (len <= kWarpCap) {
-        warp_sort_list<32>(src, dst, len, lane);
+        warp_sort_list<32>(src, dst, len, lane, key_order);
     } else if (lane == 0) {
         atomicOr(&s_big, 1 << warp);
     }
@@ -278,12 +290,30 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tile
             for (int i = threadIdx.x; i < lp; i += kSortThreads) s_buf[i] = i < blen ? unsorted[boff + i] : INT_MAX;
             __syncthreads();
             cta_bitonic_sort(s_buf, lp);
-            for (int i = threadIdx.x; i < blen; i += kSortThreads) gid_sorted[boff + i] = s_buf[i];
+            for (int i = threadIdx.x; i < blen; i += kSortThreads) {
+                gid_sorted[boff + i] = key_order != nullptr ? key_order[s_buf[i]] : s_buf[i];
+            }
             __syncthreads();
         } else {
-            bitmap_sort(unsorted + boff, gid_sorted + boff, blen, n, s_buf, s_warp);
+            bitmap_sort(unsorted + boff, gid_sorted + boff, blen, n, s_buf, s_warp, key_order);
         }
     }
+}
+
+// Monotone map of a float to uint32 (-0.0 first made +0.0): ordering the keys as
+// unsigned integers orders the floats, -inf first and +inf last.
+__global__ void k_depth_keys(int n, const float* __restrict__ depth, uint32_t* __restrict__ keys,
+                             int32_t* __restrict__ vals) {
+    const int g = blockIdx.x * 256 + threadIdx.x;
+    if (g >= n) return;
+    const uint32_t u = __float_as_uint(depth[g] + 0.0f);
+    keys[g] = (u & 0x80000000u) != 0u ? ~u : (u | 0x80000000u);
+    vals[g] = g;
+}
+
+__global__ void k_rank_of(int n, const int32_t* __restrict__ order, int32_t* __restrict__ rank) {
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i < n) rank[order[i]] = i;
 }
 
 __global__ void k_empty_lists(int num_tiles, int32_t* __restrict__ tile_offsets, int32_t* __restrict__ overflow) {
@@ -296,8 +326,27 @@ __global__ void k_empty_lists(int num_tiles, int32_t* __restrict__ tile_offsets,
 
 int64_t tile_lists_scratch_bytes(int64_t capacity) { return arena_bytes(capacity, sizeof(int32_t)); }
 
+int64_t depth_order_scratch_bytes(int64_t n) {
+    return arena_bytes(n, sizeof(uint32_t)) + arena_bytes(n, sizeof(int32_t)) + radix_scratch_bytes(n, 0xffffffffu);
+}
+
+cudaError_t depth_order(int n, const float* depth, int32_t* order, int32_t* rank, void* scratch, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    Arena arena{static_cast<char*>(scratch), depth_order_scratch_bytes(n), 0};
+    uint32_t* keys = arena.take<uint32_t>(n);
+    int32_t* vals = arena.take<int32_t>(n);
+    void* radix_scratch = arena.base + arena.used;
+    const unsigned blocks = static_cast<unsigned>(div_up(n, 256));
+    k_depth_keys<<<blocks, 256, 0, stream>>>(n, depth, keys, vals);
+    cudaError_t err = radix_sort_pairs(keys, vals, n, 0xffffffffu, order, radix_scratch, stream);
+    if (err != cudaSuccess) return err;
+    k_rank_of<<<blocks, 256, 0, stream>>>(n, order, rank);
+    return cudaGetLastError();
+}
+
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
-                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity, int32_t* gid_sorted,
+                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
+                             const int32_t* sort_key, const int32_t* key_order, int32_t* gid_sorted,
                              int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream) {
     if (n == 0 || num_tiles == 0) {
         k_empty_lists<<<static_cast<unsigned>(div_up(static_cast<int64_t>(num_tiles) + 1, 256)), 256, 0, stream>>>(
@@ -307,11 +356,11 @@ cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb,
     int32_t* unsorted = static_cast<int32_t*>(scratch);
     k_scatter_pairs<<<static_cast<unsigned>(div_up(n, kScatterThreads)), kScatterThreads, 0, stream>>>(
         n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, tile_count, tile_offsets, total_pairs,
-        capacity, unsorted, overflow);
+        capacity, sort_key, unsorted, overflow);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     k_sort_tiles<<<static_cast<unsigned>(div_up(num_tiles, kSortWarps)), kSortThreads, 0, stream>>>(
-        n, num_tiles, tile_offsets, unsorted, gid_sorted);
+        n, num_tiles, tile_offsets, unsorted, key_order, gid_sorted);
     return cudaGetLastError();
 }
 

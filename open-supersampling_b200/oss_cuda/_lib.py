@@ -34,7 +34,18 @@ SIGNATURES = {
     "oss_render_prepare": (
         ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
-    "oss_bin_pairs": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64, _p]),
+    "oss_bin_pairs": (
+        ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_depth_order_scratch_bytes": (_i64, [_i64]),
+    "oss_depth_order": (ctypes.c_int, [_i64, _p, _p, _p, _p, _i64, _p]),
+    "oss_render_alpha_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_alpha_pair_grad_stride": (ctypes.c_int, [_i64]),
+    "oss_render_alpha_backward_scratch_bytes": (_i64, [_i64, _i64]),
+    "oss_render_alpha_backward": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+         _p, _i64, _p],
+    ),
     "oss_entry_record_floats": (ctypes.c_int, [_i64]),
     "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_render_backward_scratch_bytes": (_i64, [_i64, _i64, _i64]),

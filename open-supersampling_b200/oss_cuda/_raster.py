@@ -122,9 +122,24 @@ class Binned:
     tile_offsets: torch.Tensor  # (T+1,) int32
 
 
-def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: int, w: int, mode: int) -> Binned:
+def depth_order(depth: torch.Tensor):
+    """(order, rank) of the Gaussians sorted by (depth, gid): the alpha-blend list key."""
+    lib = _lib.lib()
+    n = int(depth.numel())
+    dev = depth.device
+    order = torch.empty((n,), device=dev, dtype=torch.int32)
+    rank = torch.empty((n,), device=dev, dtype=torch.int32)
+    scratch = torch.empty((max(1, lib.oss_depth_order_scratch_bytes(n)),), device=dev, dtype=torch.uint8)
+    _lib.check(lib.oss_depth_order(n, depth.data_ptr(), order.data_ptr(), rank.data_ptr(), scratch.data_ptr(),
+                                   scratch.numel(), stream_of(depth)), "oss_depth_order")
+    return order, rank
+
+
+def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: int, w: int, mode: int,
+                  depth: torch.Tensor | None = None) -> Binned:
     """Preprocess + deterministic tile binning.  One host sync (the pair total)
-    except in full mode, where the total N*T is known up front."""
+    except in full mode, where the total N*T is known up front.  With depth the
+    tile lists are ordered by (depth, gid) instead of gid (alpha blending)."""
     lib = _lib.lib()
     n = int(xy.size(0))
     _, _, num_tiles, _ = check_hw(h, w, _lib.TILE)
@@ -161,11 +176,15 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     overflow = torch.empty((1,), **i32)
     nbytes = lib.oss_bin_pairs_scratch_bytes(n, total_pairs, num_tiles)
     scratch2 = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
+    order = rank = None
+    if depth is not None and mode != _lib.OSS_BIN_FULL:
+        order, rank = depth_order(depth)
     # capacity == the exact total read above, so the device-side overflow check cannot fire
     _lib.check(
         lib.oss_bin_pairs(n, h, w, mode, aabb.data_ptr(), pair_offset.data_ptr(), tile_count.data_ptr(),
-                          total.data_ptr(), total_pairs, gid_sorted.data_ptr(), tile_offsets.data_ptr(),
-                          overflow.data_ptr(), scratch2.data_ptr(), scratch2.numel(), stream),
+                          total.data_ptr(), total_pairs, _lib.ptr(rank), _lib.ptr(order), gid_sorted.data_ptr(),
+                          tile_offsets.data_ptr(), overflow.data_ptr(), scratch2.data_ptr(), scratch2.numel(),
+                          stream),
         "oss_bin_pairs",
     )
     return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
@@ -222,5 +241,65 @@ def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
                                 _lib.ptr(d_opacity), d_scale.data_ptr(), d_rot.data_ptr(), scratch.data_ptr(),
                                 scratch.numel(), stream_of(feat)),
         "oss_render_backward",
+    )
+    return d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot
+
+
+def background_vector(background, f: int, device) -> torch.Tensor | None:
+    """None, a scalar or F values -> a device (F,) fp32 tensor (None stays None)."""
+    if background is None:
+        return None
+    bg = torch.as_tensor(background, dtype=torch.float32, device=device).reshape(-1)
+    if bg.numel() == 1:
+        bg = bg.expand(f)
+    if bg.numel() != f:
+        raise RuntimeError("background must be a scalar or have F values")
+    return bg.contiguous()
+
+
+def render_alpha_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
+                         background: torch.Tensor | None):
+    """(image (F,H,W), t_final (H,W), n_contrib (H,W) int32) of front-to-back compositing."""
+    lib = _lib.lib()
+    f = int(feat.size(1))
+    dev = feat.device
+    image = torch.empty((f, b.h, b.w), device=dev, dtype=torch.float32)
+    t_final = torch.empty((b.h, b.w), device=dev, dtype=torch.float32)
+    n_contrib = torch.empty((b.h, b.w), device=dev, dtype=torch.int32)
+    _lib.check(
+        lib.oss_render_alpha_forward(b.n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                                     _lib.ptr(background), b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(),
+                                     image.data_ptr(), t_final.data_ptr(), n_contrib.data_ptr(), stream_of(feat)),
+        "oss_render_alpha_forward",
+    )
+    return image, t_final, n_contrib
+
+
+def render_alpha_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
+                          background: torch.Tensor | None, scale: torch.Tensor, rot: torch.Tensor,
+                          t_final: torch.Tensor, n_contrib: torch.Tensor, grad_image: torch.Tensor):
+    """Deterministic (d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot) of the alpha blend."""
+    lib = _lib.lib()
+    dev = feat.device
+    n, f = b.n, int(feat.size(1))
+    f32 = dict(device=dev, dtype=torch.float32)
+    d_xy = torch.empty((n, 2), **f32)
+    d_conic = torch.empty((n, 3), **f32)
+    d_feat = torch.empty((n, f), **f32)
+    d_opacity = torch.empty((n,), **f32)
+    d_scale = torch.empty((n, 2), **f32)
+    d_rot = torch.empty((n,), **f32)
+    nbytes = lib.oss_render_alpha_backward_scratch_bytes(b.total_pairs, f)
+    scratch = torch.empty((max(16, nbytes),), device=dev, dtype=torch.uint8)
+    scale = aligned(scale, 8)
+    _lib.check(
+        lib.oss_render_alpha_backward(n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                                      _lib.ptr(background), scale.data_ptr(), rot.data_ptr(), b.aabb.data_ptr(),
+                                      b.pair_offset.data_ptr(), b.total_pairs, b.gid_sorted.data_ptr(),
+                                      b.tile_offsets.data_ptr(), t_final.data_ptr(), n_contrib.data_ptr(),
+                                      grad_image.data_ptr(), d_xy.data_ptr(), d_conic.data_ptr(), d_feat.data_ptr(),
+                                      d_opacity.data_ptr(), d_scale.data_ptr(), d_rot.data_ptr(), scratch.data_ptr(),
+                                      scratch.numel(), stream_of(feat)),
+        "oss_render_alpha_backward",
     )
     return d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot

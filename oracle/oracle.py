@@ -53,6 +53,8 @@ def lib():
         _lib.orc_render_forward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_render_backward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_conic_to_scale_rot_grad.argtypes = [i64, p, p, p, p, p]
+        _lib.orc_render_alpha_forward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
+        _lib.orc_render_alpha_backward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_tile_bin_counting_sort.argtypes = [i64, i64, p, p, p, p]
         _lib.orc_num_threads.restype = i32
         _lib.orc_set_num_threads.argtypes = [i32]
@@ -215,6 +217,74 @@ def render_grads(xy, scale, rot, feat, grad, h, w, mode=TIGHT, opacity=None):
     """(d_xy, d_scale, d_rot, d_feat, d_opacity, d_conic) through the oracle's own lists."""
     conic, _, _, gid, offs = lists(xy, scale, rot, h, w, mode)
     d_xy, d_conic, d_feat, d_op = render_backward(xy, conic, feat, gid, offs, grad, h, w, opacity)
+    d_scale, d_rot = conic_to_scale_rot_grad(scale, rot, d_conic)
+    return d_xy, d_scale, d_rot, d_feat, d_op, d_conic
+
+
+def depth_order_lists(gid, offs, depth):
+    """Re-sort every tile list by (depth, gid) ascending: the list order of the
+    alpha-blend mode (depth -0.0 counts as +0.0)."""
+    gid, offs = _i32(gid), _i32(offs)
+    d = _f32(depth) + np.float32(0.0)
+    out = gid.copy()
+    for t in range(offs.size - 1):
+        b, e = int(offs[t]), int(offs[t + 1])
+        if e - b > 1:
+            seg = gid[b:e]
+            out[b:e] = seg[np.lexsort((seg, d[seg]))]
+    return out
+
+
+def render_alpha_forward(xy, conic, feat, opacity, gid, offs, h, w, background=None, tile_range=None):
+    """(image (F,H,W), t_final (H,W), n_contrib (H,W) int32, ambiguous (H,W) bool) of
+    front-to-back compositing over the given lists (see oss_oracle.c)."""
+    xy, conic, feat, op = _f32(xy), _f32(conic), _f32(feat), _f32(opacity)
+    gid, offs = _i32(gid), _i32(offs)
+    bg = None if background is None else _f32(np.broadcast_to(np.asarray(background, np.float32), (feat.shape[1],)))
+    n, f = feat.shape
+    _, _, t = tiles(h, w)
+    lo, hi = (0, t) if tile_range is None else tile_range
+    out = np.zeros((f, h, w), np.float32)
+    tf = np.ones((h, w), np.float32)
+    nc = np.zeros((h, w), np.int32)
+    amb = np.zeros((h, w), np.uint8)
+    lib().orc_render_alpha_forward(n, f, h, w, _p(xy), _p(conic), _p(feat), _p(op), _p(bg), _p(gid), _p(offs),
+                                   _p(out), _p(tf), _p(nc), _p(amb), lo, hi)
+    return out, tf, nc, amb.astype(bool)
+
+
+def render_alpha_backward(xy, conic, feat, opacity, gid, offs, grad, h, w, background=None, tile_range=None):
+    """(d_xy, d_conic, d_feat, d_opacity) of render_alpha_forward, double sums."""
+    xy, conic, feat, op, grad = _f32(xy), _f32(conic), _f32(feat), _f32(opacity), _f32(grad)
+    gid, offs = _i32(gid), _i32(offs)
+    bg = None if background is None else _f32(np.broadcast_to(np.asarray(background, np.float32), (feat.shape[1],)))
+    n, f = feat.shape
+    _, _, t = tiles(h, w)
+    lo, hi = (0, t) if tile_range is None else tile_range
+    d_xy = np.empty((n, 2), np.float32)
+    d_conic = np.empty((n, 3), np.float32)
+    d_feat = np.empty((n, f), np.float32)
+    d_op = np.empty((n,), np.float32)
+    lib().orc_render_alpha_backward(n, f, h, w, _p(xy), _p(conic), _p(feat), _p(op), _p(bg), _p(gid), _p(offs),
+                                    _p(grad), _p(d_xy), _p(d_conic), _p(d_feat), _p(d_op), lo, hi)
+    return d_xy, d_conic, d_feat, d_op
+
+
+def alpha_lists(xy, scale, rot, depth, h, w, mode=TIGHT):
+    """(conic, gid_sorted by (tile, depth, gid), tile_offsets)."""
+    conic, _, _, gid, offs = lists(xy, scale, rot, h, w, mode)
+    return conic, (gid if depth is None else depth_order_lists(gid, offs, depth)), offs
+
+
+def render_alpha(xy, scale, rot, feat, opacity, h, w, depth=None, background=None, mode=TIGHT):
+    conic, gid, offs = alpha_lists(xy, scale, rot, depth, h, w, mode)
+    return render_alpha_forward(xy, conic, feat, opacity, gid, offs, h, w, background)
+
+
+def render_alpha_grads(xy, scale, rot, feat, opacity, grad, h, w, depth=None, background=None, mode=TIGHT):
+    """(d_xy, d_scale, d_rot, d_feat, d_opacity, d_conic) of the alpha-blend render."""
+    conic, gid, offs = alpha_lists(xy, scale, rot, depth, h, w, mode)
+    d_xy, d_conic, d_feat, d_op = render_alpha_backward(xy, conic, feat, opacity, gid, offs, grad, h, w, background)
     d_scale, d_rot = conic_to_scale_rot_grad(scale, rot, d_conic)
     return d_xy, d_scale, d_rot, d_feat, d_op, d_conic
 

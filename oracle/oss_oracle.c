@@ -289,6 +289,191 @@ void orc_render_backward(int64_t n, int f, int h, int w, const float* xy, const 
     free(pacc);
 }
 
+/*
+ * Front-to-back alpha compositing over per-tile lists: a build-defined mode (the
+ * reference rasterizer is additive only; its design notes name gsplat-style
+ * compositing, RESEARCH.md:114, without code).  The standard over operator, per
+ * pixel, in list order (lists sorted by (depth, gid)):
+ *   G_i = exp(-q_i/2) (0 for q < 0 or non-finite);  a_i = min(0.99, opacity_i G_i)
+ *   skip the entry when a_i < 1/255;
+ *   stop before the first entry whose T (1 - a_i) would fall below 1e-4;
+ *   C += feat_i a_i T;  T *= 1 - a_i;   out = C + T * background.
+ * C and T are carried in double.  t_final[p] = T, n_contrib[p] = 1 + the
+ * position in the tile list of the last composited entry (0 if none).
+ * ambiguous[p] (optional) = 1 when one of the pixel's skip / clamp / stop tests
+ * lies within a relative 2e-5 (1e-4 for the transmittance test) of its
+ * threshold: there, fp32 rounding of q, of exp or of the running transmittance
+ * (a few ulp per entry) may decide it either way.
+ */
+#define ORC_ALPHA_MAX 0.99
+#define ORC_ALPHA_MIN (1.0 / 255.0)
+#define ORC_T_MIN 1e-4
+
+static int near_rel(double v, double thr, double rel) { return fabs(v - thr) <= rel * thr; }
+
+void orc_render_alpha_forward(int64_t n, int f, int h, int w, const float* xy, const float* conic, const float* feat,
+                              const float* opacity, const float* background, const int32_t* gid_sorted,
+                              const int32_t* tile_offsets, float* out, float* t_final, int32_t* n_contrib,
+                              uint8_t* ambiguous, int64_t tile_lo, int64_t tile_hi) {
+    (void)n;
+    const int ntx = num_tiles_1d(w);
+    const int64_t plane = (int64_t)h * w;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t t = tile_lo; t < tile_hi; ++t) {
+        const int tx0 = (int)(t % ntx) * ORC_TILE, ty0 = (int)(t / ntx) * ORC_TILE;
+        const int beg = tile_offsets[t], end = tile_offsets[t + 1];
+        double acc[64];
+        for (int ly = 0; ly < ORC_TILE; ++ly) {
+            const int py = ty0 + ly;
+            if (py >= h) break;
+            for (int lx = 0; lx < ORC_TILE; ++lx) {
+                const int px = tx0 + lx;
+                if (px >= w) break;
+                for (int c = 0; c < f; ++c) acc[c] = 0.0;
+                double T = 1.0;
+                int last = 0;
+                int amb = 0;
+                for (int j = beg; j < end; ++j) {
+                    const int g = gid_sorted[j];
+                    const float dx = (float)px - xy[2 * g];
+                    const float dy = (float)py - xy[2 * g + 1];
+                    const float q = quad_of(conic + 3 * g, dx, dy);
+                    if (!isfinite(q) || q < 0.0f) continue;
+                    const double og = (double)opacity[g] * (double)expf(-0.5f * q);
+                    amb |= near_rel(og, ORC_ALPHA_MAX, 2e-5) | near_rel(og, ORC_ALPHA_MIN, 2e-5);
+                    const double a = og < ORC_ALPHA_MAX ? og : ORC_ALPHA_MAX;
+                    if (a < ORC_ALPHA_MIN) continue;
+                    const double tn = T * (1.0 - a);
+                    amb |= near_rel(tn, ORC_T_MIN, 1e-4);
+                    if (tn < ORC_T_MIN) break;
+                    for (int c = 0; c < f; ++c) acc[c] += (double)feat[(int64_t)g * f + c] * a * T;
+                    T = tn;
+                    last = j - beg + 1;
+                }
+                const int64_t pix = (int64_t)py * w + px;
+                for (int c = 0; c < f; ++c) {
+                    const double bg = background ? (double)background[c] : 0.0;
+                    out[c * plane + pix] = (float)(acc[c] + T * bg);
+                }
+                if (t_final) t_final[pix] = (float)T;
+                if (n_contrib) n_contrib[pix] = last;
+                if (ambiguous) ambiguous[pix] = (uint8_t)amb;
+            }
+        }
+    }
+}
+
+/*
+ * Backward of orc_render_alpha_forward.  Per pixel the forward is replayed in
+ * double (a_i, T_i, which entries composite), then entries are visited back to
+ * front with S = the normalised colour behind entry i (S starts at the
+ * background):
+ *   dL/da_i = T_i sum_c go_c (feat_ic - S_c);  d feat_ic += a_i T_i go_c;
+ *   S_c = feat_ic a_i + S_c (1 - a_i)
+ * then, where a_i = opacity_i G_i is not clamped at 0.99,
+ *   d opacity_i += G_i dL/da_i;  dL/dq = -0.5 G_i opacity_i dL/da_i
+ * and d_xy, d_conic follow from dL/dq exactly as in the additive backward.
+ * Per-entry sums in double, then per Gaussian over list entries in list order.
+ */
+void orc_render_alpha_backward(int64_t n, int f, int h, int w, const float* xy, const float* conic,
+                               const float* feat, const float* opacity, const float* background,
+                               const int32_t* gid_sorted, const int32_t* tile_offsets, const float* grad,
+                               float* d_xy, float* d_conic, float* d_feat, float* d_opacity, int64_t tile_lo,
+                               int64_t tile_hi) {
+    const int ntx = num_tiles_1d(w);
+    const int64_t plane = (int64_t)h * w;
+    const int stride = 6 + f;
+    const int64_t p_lo = tile_offsets[tile_lo], p_hi = tile_offsets[tile_hi];
+    double* pacc = (double*)calloc((size_t)((p_hi - p_lo) * stride + 1), sizeof(double));
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t t = tile_lo; t < tile_hi; ++t) {
+        const int tx0 = (int)(t % ntx) * ORC_TILE, ty0 = (int)(t / ntx) * ORC_TILE;
+        const int beg = tile_offsets[t], end = tile_offsets[t + 1];
+        const int len = end - beg;
+        if (len == 0) continue;
+        double* av = (double*)malloc(sizeof(double) * (size_t)len * 3);  /* a, T before, G */
+        uint8_t* on = (uint8_t*)malloc((size_t)len);
+        for (int ly = 0; ly < ORC_TILE; ++ly) {
+            const int py = ty0 + ly;
+            if (py >= h) break;
+            for (int lx = 0; lx < ORC_TILE; ++lx) {
+                const int px = tx0 + lx;
+                if (px >= w) break;
+                const int64_t pix = (int64_t)py * w + px;
+                double T = 1.0;
+                int last = 0;
+                for (int j = 0; j < len; ++j) {
+                    on[j] = 0;
+                    const int g = gid_sorted[beg + j];
+                    const float dx = (float)px - xy[2 * g];
+                    const float dy = (float)py - xy[2 * g + 1];
+                    const float q = quad_of(conic + 3 * g, dx, dy);
+                    if (!isfinite(q) || q < 0.0f) continue;
+                    const double G = (double)expf(-0.5f * q);
+                    const double og = (double)opacity[g] * G;
+                    const double a = og < ORC_ALPHA_MAX ? og : ORC_ALPHA_MAX;
+                    if (a < ORC_ALPHA_MIN) continue;
+                    const double tn = T * (1.0 - a);
+                    if (tn < ORC_T_MIN) break;
+                    av[3 * j] = a;
+                    av[3 * j + 1] = T;
+                    av[3 * j + 2] = G;
+                    on[j] = (uint8_t)(og < ORC_ALPHA_MAX ? 1 : 2);
+                    T = tn;
+                    last = j + 1;
+                }
+                double S[64];
+                for (int c = 0; c < f; ++c) S[c] = background ? (double)background[c] : 0.0;
+                for (int j = last - 1; j >= 0; --j) {
+                    if (!on[j]) continue;
+                    const int g = gid_sorted[beg + j];
+                    const double a = av[3 * j], Ti = av[3 * j + 1], G = av[3 * j + 2];
+                    double* acc = pacc + (int64_t)(beg + j - p_lo) * stride;
+                    double dlda = 0.0;
+                    for (int c = 0; c < f; ++c) {
+                        const double go = grad[c * plane + pix];
+                        const double fc = (double)feat[(int64_t)g * f + c];
+                        dlda += go * (fc - S[c]);
+                        acc[5 + c] += a * Ti * go;
+                        S[c] = fc * a + S[c] * (1.0 - a);
+                    }
+                    dlda *= Ti;
+                    if (on[j] != 1) continue;  /* clamped at 0.99: no gradient through G or opacity */
+                    acc[5 + f] += G * dlda;
+                    const float* k = conic + 3 * g;
+                    const double dx = (double)((float)px - xy[2 * g]);
+                    const double dy = (double)((float)py - xy[2 * g + 1]);
+                    const double dldq = -0.5 * G * (double)opacity[g] * dlda;
+                    acc[0] -= dldq * (2.0 * k[0] * dx + 2.0 * k[1] * dy);
+                    acc[1] -= dldq * (2.0 * k[1] * dx + 2.0 * k[2] * dy);
+                    acc[2] += dldq * dx * dx;
+                    acc[3] += dldq * 2.0 * dx * dy;
+                    acc[4] += dldq * dy * dy;
+                }
+            }
+        }
+        free(on);
+        free(av);
+    }
+    double* gacc = (double*)calloc((size_t)(n * stride + 1), sizeof(double));
+    for (int64_t j = p_lo; j < p_hi; ++j) {
+        const int g = gid_sorted[j];
+        for (int v = 0; v < stride; ++v) gacc[(int64_t)g * stride + v] += pacc[(j - p_lo) * stride + v];
+    }
+    for (int64_t g = 0; g < n; ++g) {
+        const double* a = gacc + g * stride;
+        d_xy[2 * g] = (float)a[0];
+        d_xy[2 * g + 1] = (float)a[1];
+        d_conic[3 * g] = (float)a[2];
+        d_conic[3 * g + 1] = (float)a[3];
+        d_conic[3 * g + 2] = (float)a[4];
+        for (int c = 0; c < f; ++c) d_feat[g * f + c] = (float)a[5 + c];
+        if (d_opacity) d_opacity[g] = (float)a[5 + f];
+    }
+    free(gacc);
+    free(pacc);
+}
+
 /* conic_to_scale_rot_grad, rasterizer_bwd.cu:128-153 */
 void orc_conic_to_scale_rot_grad(int64_t n, const float* scale, const float* rot, const float* d_conic,
                                  float* d_scale, float* d_rot) {

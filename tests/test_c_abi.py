@@ -44,7 +44,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_clean_error_state():
     lib = _lib.lib()
-    assert lib.oss_abi_version() == 4
+    assert lib.oss_abi_version() == 5
 
 
 def test_rejects_tile_size_other_than_16():
@@ -72,12 +72,13 @@ def test_rejects_bad_sizes_and_modes():
     assert "full-frame" in lib.oss_last_error().decode()
     assert lib.oss_tile_bin_counting_sort(4, 0, None, None, None, None, None, 0, None) == 1
     assert lib.oss_last_error().decode() == "num_tiles must be positive"
-    assert lib.oss_bin_pairs(1, 32, 32, 0, None, None, None, None, 1 << 32, None, None, None, None, 0, None) == 3
+    assert lib.oss_bin_pairs(1, 32, 32, 0, None, None, None, None, 1 << 32, None, None, None, None, None, None, 0,
+                             None) == 3
     assert lib.oss_last_error().decode() == "capacity exceeds int32 range"
-    assert lib.oss_bin_pairs(1, 32, 32, 0, None, None, None, None, 16, 8, 8, None, None, 0, None) == 1
+    assert lib.oss_bin_pairs(1, 32, 32, 0, None, None, None, None, 16, None, None, 8, 8, None, None, 0, None) == 1
     assert "overflow must be non-null" in lib.oss_last_error().decode()
     # full-frame lists need capacity >= N * tiles, checked on the host
-    assert lib.oss_bin_pairs(3, 32, 32, 2, None, None, None, None, 11, 8, 8, 8, None, 0, None) == 3
+    assert lib.oss_bin_pairs(3, 32, 32, 2, None, None, None, None, 11, None, None, 8, 8, 8, None, 0, None) == 3
     assert "capacity >= N * num_tiles" in lib.oss_last_error().decode()
 
 
@@ -91,8 +92,12 @@ def test_rejects_scratch_too_small():
     assert rc == 1 and "tile_count" in lib.oss_last_error().decode()
     assert lib.oss_tile_count_elems(100) >= 100
     bneed = lib.oss_bin_pairs_scratch_bytes(1000, 5000, 16)
-    rc = lib.oss_bin_pairs(1000, 64, 64, 0, 16, 8, 8, 8, 5000, 8, 8, 8, 8, bneed - 1, None)
+    rc = lib.oss_bin_pairs(1000, 64, 64, 0, 16, 8, 8, 8, 5000, None, None, 8, 8, 8, 8, bneed - 1, None)
     assert rc == 4 and "scratch" in lib.oss_last_error().decode()
+    assert lib.oss_bin_pairs(1000, 64, 64, 0, 16, 8, 8, 8, 5000, 8, None, 8, 8, 8, 8, bneed, None) == 1
+    assert "sort_key and key_order" in lib.oss_last_error().decode()
+    assert lib.oss_depth_order(10, 8, 8, 8, 8, lib.oss_depth_order_scratch_bytes(10) - 1, None) == 4
+    assert lib.oss_alpha_pair_grad_stride(3) == 12
 
 
 def test_scratch_sizes_are_monotone():

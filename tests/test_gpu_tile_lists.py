@@ -73,7 +73,7 @@ class Lists:
                                              self.prep_scratch.numel(), s), "prepare")
         self.chk(self.lib.oss_bin_pairs(self.n, self.h, self.w, self.mode, self.aabb.data_ptr(),
                                         self.pair_offset.data_ptr(), self.tile_count.data_ptr(),
-                                        self.total.data_ptr(), self.capacity, self.gid.data_ptr(),
+                                        self.total.data_ptr(), self.capacity, None, None, self.gid.data_ptr(),
                                         self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
                                         self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
 
