@@ -88,7 +88,8 @@ def make_inputs(h, w, n, ls_mean, ls_sd, seed):
     opacity = (1.0 / (1.0 + np.exp(-rng.standard_normal(n)))).astype(np.float32)
     rgb = rng.random((n, 3)).astype(np.float32)
     grad = rng.standard_normal((3, h, w)).astype(np.float32)
-    return dict(xy=xy, scale=scale, rot=rot, opacity=opacity, rgb=rgb, grad=grad)
+    depth = rng.random(n).astype(np.float32)  # drawn last: the other inputs do not depend on it
+    return dict(xy=xy, scale=scale, rot=rot, opacity=opacity, rgb=rgb, grad=grad, depth=depth)
 
 
 class ClockSampler:
@@ -303,6 +304,104 @@ class Pipeline:
         return int(np.sum(lens * rows * cols))
 
 
+class AlphaPipeline(Pipeline):
+    """The blend="alpha" path over the C ABI: depth order -> prepare -> lists
+    ordered by depth rank -> front-to-back forward -> back-to-front backward and
+    per-Gaussian reduce (background 0).  Sync-free after the first step, like
+    Pipeline; inputs additionally carry `depth`."""
+
+    def __init__(self, capacity_n, h, w, mode, device):
+        super().__init__(capacity_n, h, w, mode, device)
+        i32 = dict(device=device, dtype=torch.int32)
+        n = capacity_n
+        self.order = torch.empty((max(1, n),), **i32)
+        self.rank = torch.empty((max(1, n),), **i32)
+        self.depth_scratch = torch.empty((max(1, self.lib.oss_depth_order_scratch_bytes(n)),), device=device,
+                                         dtype=torch.uint8)
+        self.t_final = torch.empty((h, w), device=device, dtype=torch.float32)
+        self.n_contrib = torch.empty((h, w), **i32)
+
+    def _ensure(self, pairs):
+        super()._ensure(pairs)
+        need = self.lib.oss_render_alpha_backward_scratch_bytes(self.capacity, 3)
+        if need > self.scratch.numel():
+            self.scratch = torch.empty((need,), device=self.device, dtype=torch.uint8)
+
+    def step(self, d, backward=True, sync=False, timed=True):
+        lib, chk = self.lib, self._lib.check
+        s = torch.cuda.current_stream().cuda_stream
+        n, h, w = int(d["xy"].shape[0]), self.h, self.w
+        self._mark(0, timed)
+        chk(lib.oss_depth_order(n, d["depth"].data_ptr(), self.order.data_ptr(), self.rank.data_ptr(),
+                                self.depth_scratch.data_ptr(), self.depth_scratch.numel(), s), "depth_order")
+        chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
+                                   d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
+                                   self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
+                                   self.tile_count.data_ptr(), self.tile_offsets.data_ptr(),
+                                   self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
+        self._mark(1, timed)
+        if sync or self.capacity == 0:
+            self.pairs = int(self.total.item())
+            self._ensure(self.pairs)
+        self._mark(2, timed)
+        chk(lib.oss_bin_pairs(n, h, w, self.mode, self.aabb.data_ptr(), self.pair_offset.data_ptr(),
+                              self.tile_count.data_ptr(), self.total.data_ptr(), self.capacity,
+                              self.rank.data_ptr(), self.order.data_ptr(), self.gid_sorted.data_ptr(),
+                              self.tile_offsets.data_ptr(), self.overflow.data_ptr(), self.scratch.data_ptr(),
+                              self.scratch.numel(), s), "bin")
+        self._mark(3, timed)
+        chk(lib.oss_render_alpha_forward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
+                                         d["opacity"].data_ptr(), None, self.gid_sorted.data_ptr(),
+                                         self.tile_offsets.data_ptr(), self.image.data_ptr(), self.t_final.data_ptr(),
+                                         self.n_contrib.data_ptr(), s), "alpha_forward")
+        self._mark(4, timed)
+        if not backward:
+            return
+        g = self.grads
+        chk(lib.oss_render_alpha_backward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
+                                          d["opacity"].data_ptr(), None, d["scale"].data_ptr(), d["rot"].data_ptr(),
+                                          self.aabb.data_ptr(), self.pair_offset.data_ptr(), self.capacity,
+                                          self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
+                                          self.t_final.data_ptr(), self.n_contrib.data_ptr(), d["grad"].data_ptr(),
+                                          g["d_xy"].data_ptr(), g["d_conic"].data_ptr(), g["d_rgb"].data_ptr(),
+                                          g["d_opacity"].data_ptr(), g["d_scale"].data_ptr(), g["d_rot"].data_ptr(),
+                                          self.scratch.data_ptr(), self.scratch.numel(), s), "alpha_backward")
+        self._mark(5, timed)
+        self._mark(6, timed)
+
+    def launches_per_step(self, backward=True):
+        from_radix = 1 + 4 * (1 + 2 + 1) + 1  # depth keys, 4 x (upsweep, digit scan, downsweep), rank
+        return from_radix + 2 + 2 + 1 + (2 if backward else 0)
+
+
+def time_graphs(pipe, d, steps, flush, world):
+    """Per-step device ms of the fwd+bwd and fwd-only CUDA graphs (max over ranks)."""
+    graphs = {"fwdbwd": pipe.capture(d), "fwd": pipe.capture(d, backward=False)}
+    for g in graphs.values():
+        for _ in range(3):
+            flush.zero_()
+            g.replay()
+    torch.cuda.synchronize()
+    timed = {}
+    for name, g in graphs.items():
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record()
+            g.replay()
+            e1.record()
+        torch.cuda.synchronize()
+        timed[name] = sum(e0.elapsed_time(e1) for e0, e1 in ev) / steps
+    pipe.check_overflow()
+    del graphs
+    out = torch.tensor([timed["fwdbwd"], timed["fwd"]], device=flush.device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(out, op=dist.ReduceOp.MAX)
+    return float(out[0]), float(out[1])
+
+
 # ----------------------------------------------------------------------------- CPU baseline
 
 def cpu_sample(inp, h, w, mode_name, budget_s, threads=None):
@@ -494,9 +593,26 @@ def run_ours(args, rank, world, local):
         "clocks": clocks.summary(), "wall_s": wall,
     }
 
+    # blend="alpha" (opt-in mode; the headline above is the reference's additive sum)
+    apipe = AlphaPipeline(n, h, w, mode, device)
+    for _ in range(3):
+        apipe.step(dev_inp, sync=True)
+        flush.zero_()
+    torch.cuda.synchronize()
+    ka = max(3, min(K, 50))
+    a_ms, a_fwd_ms = time_graphs(apipe, dev_inp, ka, flush, world)
+    line["alpha_blend"] = {
+        "mpix_s": pixels / (a_ms * 1e-3) / 1e6, "fwdbwd_ms_per_frame": a_ms, "fwd_ms_per_frame": a_fwd_ms,
+        "fwd_mpix_s": pixels / (a_fwd_ms * 1e-3) / 1e6, "steps": ka,
+        "workload": f"{args.config} inputs, depth ~ U[0,1], front-to-back compositing (a<=0.99, skip a<1/255, "
+                    "stop at T<1e-4), background 0, fwd+bwd incl. the depth sort; CUDA-graph replay",
+        "gpu_launches_per_step": apipe.launches_per_step(),
+    }
+    del apipe
+
     # e2e: public autograd API, host buffers in and out
     if not args.no_e2e:
-        host = {k: torch.from_numpy(v).pin_memory() for k, v in inp.items()}
+        host = {k: torch.from_numpy(v).pin_memory() for k, v in inp.items() if k != "depth"}
         outs = {"image": torch.empty((3, h, w), dtype=torch.float32).pin_memory()}
         for k, s in (("xy", (n, 2)), ("scale", (n, 2)), ("rot", (n,)), ("rgb", (n, 3)), ("opacity", (n,))):
             outs["d_" + k] = torch.empty(s, dtype=torch.float32).pin_memory()
