@@ -128,6 +128,14 @@ OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
  * gid; key_order[k] = the gid with key k.  oss_depth_order makes them for the
  * alpha-blend mode (rank and order of the Gaussians by depth). */
 
+/* Host-side read of the pair total without a copy engine: a one-thread kernel
+ * on `stream` stores *total_pairs (device) into host_total, which must be
+ * pinned host memory (written through its device mapping).  Record an event
+ * after it and synchronise on the event to read host_total -- unlike a
+ * device-to-host copy, this does not queue behind large transfers other
+ * streams have in flight. */
+OSS_API int oss_publish_total(const int64_t* total_pairs, int64_t* host_total, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Stable depth order for the alpha-blend lists: order[i] = the gid at position
  * i of the Gaussians sorted by (depth, gid) ascending, rank[g] = its position

@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(kThreads) k_tile_keys(int n, int num_tiles, co
 
 __global__ void k_set_i32(int32_t* p, int32_t v) { *p = v; }
 
+__global__ void k_copy_i64(const int64_t* __restrict__ src, int64_t* dst) { *dst = *src; }
+
 }  // namespace
 
 cudaError_t launch_full_tile_pairs(int n, int num_tiles, int32_t* gid_sorted, int32_t* tile_offsets,
@@ -47,6 +49,11 @@ cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const
     if (n == 0) return cudaSuccess;
     k_tile_keys<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(n, num_tiles, tile_id, gid,
                                                                                      keys, vals, tile_count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_i64(const int64_t* src, int64_t* dst, cudaStream_t stream) {
+    k_copy_i64<<<1, 1, 0, stream>>>(src, dst);
     return cudaGetLastError();
 }
 

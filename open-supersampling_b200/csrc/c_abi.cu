@@ -181,6 +181,17 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
     return OSS_OK;
 }
 
+int oss_publish_total(const int64_t* total_pairs, int64_t* host_total, void* stream) {
+    OSS_CHECK(total_pairs != nullptr && host_total != nullptr, OSS_ERR_INVALID, "pointers must be non-null");
+    void* mapped = nullptr;
+    if (cudaHostGetDevicePointer(&mapped, host_total, 0) != cudaSuccess || mapped == nullptr) {
+        cudaGetLastError();  // clear the sticky-free error of the failed query
+        OSS_CHECK(false, OSS_ERR_INVALID, "host_total must be pinned host memory");
+    }
+    OSS_CUDA_TRY(oss::launch_copy_i64(total_pairs, static_cast<int64_t*>(mapped), as_stream(stream)));
+    return OSS_OK;
+}
+
 int64_t oss_depth_order_scratch_bytes(int64_t n) { return oss::depth_order_scratch_bytes(n < 0 ? 0 : n); }
 
 int oss_depth_order(int64_t n, const float* depth, int32_t* order, int32_t* rank, void* scratch,

@@ -67,6 +67,8 @@ cudaError_t launch_full_tile_pairs(int n, int num_tiles, int32_t* gid_sorted, in
 cudaError_t launch_tile_keys(int n, int num_tiles, const int32_t* tile_id, const int32_t* gid,
                              uint32_t* keys, int32_t* vals, int32_t* tile_count, cudaStream_t stream);
 cudaError_t launch_set_i32(int32_t* p, int32_t value, cudaStream_t stream);
+// One-thread copy of an int64 (dst may be mapped pinned host memory).
+cudaError_t launch_copy_i64(const int64_t* src, int64_t* dst, cudaStream_t stream);
 
 // ---- tile_lists.cu --------------------------------------------------------
 // Per-tile lists from the tile counts and offsets of render prepare (the

@@ -36,6 +36,7 @@ SIGNATURES = {
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_bin_pairs": (
         ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_publish_total": (ctypes.c_int, [_p, _p, _p]),
     "oss_depth_order_scratch_bytes": (_i64, [_i64]),
     "oss_depth_order": (ctypes.c_int, [_i64, _p, _p, _p, _p, _i64, _p]),
     "oss_render_alpha_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),

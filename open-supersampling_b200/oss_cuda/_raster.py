@@ -122,6 +122,25 @@ class Binned:
     tile_offsets: torch.Tensor  # (T+1,) int32
 
 
+_HOST_TOTAL = {}
+
+
+def read_total(total: torch.Tensor, stream: int) -> int:
+    """The device pair total on the host: a one-thread kernel stores it into
+    mapped pinned memory and the host waits on an event -- the path's one host
+    synchronisation, which so does not queue behind large copies in flight."""
+    key = (total.device.index, stream)
+    slot = _HOST_TOTAL.get(key)
+    if slot is None:
+        slot = (torch.empty((1,), dtype=torch.int64).pin_memory(), torch.cuda.Event())
+        _HOST_TOTAL[key] = slot
+    host, ev = slot
+    _lib.check(_lib.lib().oss_publish_total(total.data_ptr(), host.data_ptr(), stream), "oss_publish_total")
+    ev.record(torch.cuda.current_stream(total.device))
+    ev.synchronize()
+    return int(host[0])
+
+
 def depth_order(depth: torch.Tensor):
     """(order, rank) of the Gaussians sorted by (depth, gid): the alpha-blend list key."""
     lib = _lib.lib()
@@ -135,11 +154,38 @@ def depth_order(depth: torch.Tensor):
     return order, rank
 
 
+_STICKY_OVERFLOW = {}
+
+
+def sticky_overflow(device) -> torch.Tensor:
+    """Per-device int32 flag that capacity-mode binning ORs its overflow into."""
+    idx = torch.device(device).index
+    flag = _STICKY_OVERFLOW.get(idx)
+    if flag is None:
+        flag = torch.zeros((1,), device=torch.device("cuda", idx), dtype=torch.int32)
+        _STICKY_OVERFLOW[idx] = flag
+    return flag
+
+
+def pair_capacity_overflowed(device=None, reset: bool = True) -> bool:
+    """True if a capacity-mode call on `device` since the last check had more
+    pairs than its capacity (its lists were emptied: zero image and gradients).
+    A host synchronisation with the device."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flag = sticky_overflow(dev)
+    hit = bool(int(flag.item()))
+    if reset:
+        flag.zero_()
+    return hit
+
+
 def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: int, w: int, mode: int,
-                  depth: torch.Tensor | None = None) -> Binned:
+                  depth: torch.Tensor | None = None, capacity: int | None = None) -> Binned:
     """Preprocess + deterministic tile binning.  One host sync (the pair total)
-    except in full mode, where the total N*T is known up front.  With depth the
-    tile lists are ordered by (depth, gid) instead of gid (alpha blending)."""
+    except in full mode, where the total N*T is known up front, and in capacity
+    mode, where the lists are sized for `capacity` pairs, the device checks the
+    total and raises the sticky overflow flag instead (no host sync).  With depth
+    the tile lists are ordered by (depth, gid) instead of gid (alpha blending)."""
     lib = _lib.lib()
     n = int(xy.size(0))
     _, _, num_tiles, _ = check_hw(h, w, _lib.TILE)
@@ -168,8 +214,10 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     )
     if mode == _lib.OSS_BIN_FULL:
         total_pairs = n * num_tiles
+    elif capacity is not None:
+        total_pairs = int(capacity)
     else:
-        total_pairs = int(total.item())
+        total_pairs = read_total(total, stream)
     if total_pairs > INT32_MAX:
         raise RuntimeError("total pair count exceeds int32 range")
     gid_sorted = torch.empty((total_pairs,), **i32)
@@ -179,7 +227,7 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     order = rank = None
     if depth is not None and mode != _lib.OSS_BIN_FULL:
         order, rank = depth_order(depth)
-    # capacity == the exact total read above, so the device-side overflow check cannot fire
+    # without a capacity, total_pairs is the exact total read above and the check cannot fire
     _lib.check(
         lib.oss_bin_pairs(n, h, w, mode, aabb.data_ptr(), pair_offset.data_ptr(), tile_count.data_ptr(),
                           total.data_ptr(), total_pairs, _lib.ptr(rank), _lib.ptr(order), gid_sorted.data_ptr(),
@@ -187,6 +235,8 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
                           stream),
         "oss_bin_pairs",
     )
+    if capacity is not None and mode != _lib.OSS_BIN_FULL:
+        sticky_overflow(dev).bitwise_or_(overflow)
     return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
 
 

@@ -225,3 +225,36 @@ def test_sync_free_path_replays_in_cuda_graph(cuda_device):
         np.testing.assert_array_equal(host(L.gid)[:g_ref.size], g_ref)
         assert_close(host(img), orc.render_forward(xy, c_ref, f, g_ref, o_ref, h, w), what="graph image")
     del graph
+
+
+def test_public_api_pair_capacity_mode(cuda_device):
+    """rasterize_gaussians(pair_capacity=) launches without a host sync: same image
+    and gradients as the default call when the capacity suffices; above it the
+    lists are emptied (zero image) and the sticky flag reports it once."""
+    from oss_cuda import pair_capacity_overflowed, rasterize_gaussians
+
+    h, w, n = 80, 120, 2500
+    rng = np.random.default_rng(41)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    s = (rng.random((n, 2)) * 3.0 + 0.5).astype(np.float32)
+    rot = (rng.random(n) * 6.28).astype(np.float32)
+    feat = rng.random((n, 3)).astype(np.float32)
+    grad = dev(rng.standard_normal((3, h, w)))
+    total = int(orc.lists(xy, s, rot, h, w, orc.TIGHT)[3].size)
+    pair_capacity_overflowed()  # clear
+
+    def run(**kw):
+        leaves = [dev(a).requires_grad_(True) for a in (xy, s, rot, feat)]
+        img = rasterize_gaussians(*leaves, h, w, binning="tight3sigma", **kw)
+        return [host(img)] + [host(g) for g in torch.autograd.grad(img, leaves, grad)]
+
+    want = run()
+    got = run(pair_capacity=total + 100)
+    assert not pair_capacity_overflowed()
+    for a, b in zip(got, want):
+        np.testing.assert_array_equal(a, b)
+    short = run(pair_capacity=total - 1)
+    assert pair_capacity_overflowed()
+    assert not pair_capacity_overflowed()  # reset by the first read
+    for a in short:
+        assert not a.any()
