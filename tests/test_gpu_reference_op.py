@@ -13,19 +13,22 @@ test_rasterizer_backward_equivalence.py:71-95):
 * forward images 5e-3: the reference's forward feeds weights and features to
   bf16 tensor-core MMAs as hi/lo pairs, so it is itself only 5e-3-close to its
   fp32 definition (the product is held to 1e-5 against the fp32 oracle in
-  test_gpu_raster.py); the test also reports how much of the gap is the
-  reference's own error;
-* gradients 1e-4 (the reference accumulates them with float atomics).
+  test_gpu_raster.py, and to 1e-5 here between its culled and full-frame
+  lists);
+* gradients 1e-4 (the reference accumulates them with float atomics); where
+  the two ops differ by more, the product must be the one within the fp32 bar
+  of the float64-summed oracle.
 
 Inputs follow the reference tests: xy uniform over the frame, scale
 U(0.5, 5.5), rot U(0, 6.28), feat N(0, 1), seeded with 0xC0DA.
 """
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
-from conftest import ROOT
+from conftest import ROOT, assert_close_grad
 
 pytestmark = pytest.mark.gpu
 
@@ -148,18 +151,48 @@ BWD_GRID = [(n, h, w, f) for n in (1, 16, 256, 4096) for (h, w) in ((32, 32), (6
             for f in (1, 3, 12, 64) if n * h * w * f <= 270_000_000]
 
 
+def _check_grad(got, ref, truth, what):
+    """Within the reference's own 1e-4 bar of the reference op; where not, the
+    product must meet the fp32 parity bar against the float64-summed oracle
+    and be at least as close to it as the reference op is.  Both ops sum the
+    same fp32 terms in different orders (the reference with float atomics), so
+    elements whose terms cancel keep a summation noise of 1e-4 and more."""
+    g, r = got.detach().double().cpu(), ref.detach().double().cpu()
+    near = (g - r).abs() <= 1e-4 + 1e-4 * r.abs()
+    if bool(near.all()):
+        return
+    t = torch.as_tensor(np.asarray(truth(), np.float64))
+    assert_close_grad(g.numpy(), t.numpy(), what=what + " vs float64 oracle")
+    slack = 1e-6 * float(t.abs().max())
+    eg, er = (g - t).abs()[~near], (r - t).abs()[~near]
+    assert bool((eg <= er + slack).all()), (
+        f"{what}: {int((~near).sum())} elements differ from the reference op beyond 1e-4 and the product is "
+        f"further from the float64 sum there (max product err {float(eg.max()):.3e}, reference {float(er.max()):.3e})")
+
+
 @pytest.mark.parametrize("n,h,w,f", BWD_GRID)
 def test_backward_matches_reference_op(ref_op, our_op, cuda_device, n, h, w, f):
+    import oracle as orc
+
     xy, scale, rot, feat = _inputs(n, h, w, f, cuda_device)
     _, g_r, off_r, c_r = ref_op.rasterize_forward(xy, scale, rot, feat, h, w, 16, True)
     grad = torch.randn(f, h, w, device=cuda_device, generator=torch.Generator(device=cuda_device).manual_seed(7))
     dxy_r, dc_r, df_r = ref_op.rasterize_backward(xy, scale, rot, feat, c_r, g_r, off_r, grad, h, w, 16)
     ds_r, dr_r = ref_op.conic_to_scale_rot_grad(scale, rot, dc_r)
+    cpu = [t.cpu().numpy() for t in (xy, scale, rot, feat, grad)]
 
     # the product's backward over the reference's own lists and conic
     dxy_k, dc_k, df_k = our_op.rasterize_backward(xy, scale, rot, feat, c_r, g_r, off_r, grad, h, w, 16)
-    for name, got, ref in (("d_xy", dxy_k, dxy_r), ("d_conic", dc_k, dc_r), ("d_feat", df_k, df_r)):
-        _assert_close(got, ref, 1e-4, 1e-4, name + " (reference lists)")
+    on_ref_lists = {}
+
+    def truth_ref_lists(i):
+        if not on_ref_lists:
+            on_ref_lists["v"] = orc.render_backward(cpu[0], c_r.cpu().numpy(), cpu[3], g_r.cpu().numpy(),
+                                                    off_r.cpu().numpy(), cpu[4], h, w)
+        return on_ref_lists["v"][i]
+
+    for i, (name, got, ref) in enumerate((("d_xy", dxy_k, dxy_r), ("d_conic", dc_k, dc_r), ("d_feat", df_k, df_r))):
+        _check_grad(got, ref, lambda i=i: truth_ref_lists(i), name + " (reference lists)")
 
     # the product's autograd path with its own (exact) lists
     from oss_cuda import rasterize_gaussians
@@ -167,9 +200,16 @@ def test_backward_matches_reference_op(ref_op, our_op, cuda_device, n, h, w, f):
     leaves = [t.detach().clone().requires_grad_(True) for t in (xy, scale, rot, feat)]
     out = rasterize_gaussians(*leaves, h, w, tile_size=16, topk_norm=True)
     out.backward(grad)
-    for name, got, ref in (("d_xy", leaves[0].grad, dxy_r), ("d_scale", leaves[1].grad, ds_r),
-                           ("d_rot", leaves[2].grad, dr_r), ("d_feat", leaves[3].grad, df_r)):
-        _assert_close(got, ref, 1e-4, 1e-4, name + " (autograd)")
+    own = {}
+
+    def truth_own(i):
+        if not own:
+            own["v"] = orc.render_grads(cpu[0], cpu[1], cpu[2], cpu[3], cpu[4], h, w, mode=orc.EXACT)
+        return own["v"][i]
+
+    for name, got, ref, i in (("d_xy", leaves[0].grad, dxy_r, 0), ("d_scale", leaves[1].grad, ds_r, 1),
+                              ("d_rot", leaves[2].grad, dr_r, 2), ("d_feat", leaves[3].grad, df_r, 3)):
+        _check_grad(got, ref, lambda i=i: truth_own(i), name + " (autograd)")
 
 
 @pytest.mark.parametrize("n", [1, 1000, 200000])
