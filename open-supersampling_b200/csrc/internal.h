@@ -30,9 +30,14 @@ cudaError_t scan_exclusive_i32(const int32_t* in, int32_t* out, int64_t n, bool 
                                int64_t* total_out, void* scratch, cudaStream_t stream);
 
 // Preprocess tiling shared with the fused pair-count scan: each preprocess CTA
-// handles kPrepTile Gaussians and writes their count sum to block_sums.
+// handles kPrepTile Gaussians and writes their count sum to block_sums.  The
+// preprocess runs one Gaussian per thread (kPreprocThreads = kPrepTile: its
+// per-thread chain of loads, double cos/sin, divisions and counter reductions
+// is latency-bound, so it wants every Gaussian in flight at once); the scan
+// apply runs kPrepThreads threads of kPrepTile / kPrepThreads values.
 constexpr int kPrepThreads = 256;
 constexpr int kPrepTile = 1024;
+constexpr int kPreprocThreads = kPrepTile;
 int64_t scan_fused_scratch_bytes(int64_t n);
 // Second half of the fused scan: out[0..n) = exclusive scan, out[n] = total.
 // With tile_count non-null the same launch also scans the per-tile pair counts

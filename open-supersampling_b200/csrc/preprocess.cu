@@ -15,13 +15,13 @@ __device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, c
     rec[1] = make_float4(k.d * kNegHalfLog2e, k.a, k.b, k.d);
 }
 
-// One CTA per kPrepTile Gaussians (kPrepTile / kPrepThreads per thread, strided
-// for coalescing).  With block_sums non-null the CTA also writes the sum of its
-// pair counts: the reduce half of the gid-major pair-offset scan.  With
+// One CTA per kPrepTile Gaussians, one Gaussian per thread.  With block_sums
+// non-null the CTA also writes the sum of its pair counts: the reduce half of
+// the gid-major pair-offset scan.  With
 // tile_count non-null every Gaussian adds one to each tile of its rectangle
 // (fire-and-forget reductions into counters kTileCountStride ints apart): the
 // per-tile list lengths.
-__global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int nty, int mode,
+__global__ void __launch_bounds__(kPreprocThreads) k_preprocess(int n, int ntx, int nty, int mode,
                                                               const float2* __restrict__ xy,
                                                               const float2* __restrict__ scale,
                                                               const float* __restrict__ rot,
@@ -32,10 +32,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
                                                               long long* __restrict__ block_sums,
                                                               int32_t* __restrict__ tile_count) {
     long long local = 0;
-#pragma unroll
-    for (int it = 0; it < kPrepTile / kPrepThreads; ++it) {
-        const int g = blockIdx.x * kPrepTile + it * kPrepThreads + threadIdx.x;
-        if (g >= n) break;
+    const int g = blockIdx.x * kPrepTile + threadIdx.x;
+    if (g < n) {
         const float2 c = xy[g];
         const float2 s = scale[g];
         const Conic k = conic_from_scale_rot(s.x, s.y, rot[g]);
@@ -63,7 +61,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
         }
     }
     if (block_sums != nullptr) {
-        __shared__ long long s_part[kPrepThreads / 32];
+        __shared__ long long s_part[kPreprocThreads / 32];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
         if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = local;
@@ -71,7 +69,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_preprocess(int n, int ntx, int
         if (threadIdx.x == 0) {
             long long tot = 0;
 #pragma unroll
-            for (int w = 0; w < kPrepThreads / 32; ++w) tot += s_part[w];
+            for (int w = 0; w < kPreprocThreads / 32; ++w) tot += s_part[w];
             block_sums[blockIdx.x] = tot;
         }
     }
@@ -110,7 +108,7 @@ cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy
                               const float* rot, float* conic, int32_t* aabb, int32_t* count, float* geo,
                               long long* block_sums, int32_t* tile_count, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPrepThreads, 0, stream>>>(
+    k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
         conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count);
     return cudaGetLastError();

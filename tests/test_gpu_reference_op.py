@@ -151,13 +151,13 @@ BWD_GRID = [(n, h, w, f) for n in (1, 16, 256, 4096) for (h, w) in ((32, 32), (6
             for f in (1, 3, 12, 64) if n * h * w * f <= 270_000_000]
 
 
-def _check_grad(got, ref, truth, what):
+def _check_grad(got, ref, truth, what, bar=None):
     """Within the reference's own 1e-4 bar of the reference op.  Where not,
     the float64-summed oracle decides: each such element must be within the
-    fp32 parity bar of it, or no further from it than the reference op is.
-    Both ops sum the same fp32 terms in different orders (the reference with
-    float atomics), so elements whose terms cancel keep a summation noise of
-    1e-4 and more; d_scale/d_rot multiply the d_conic noise by up to 2/s^3."""
+    fp32 parity bar of it (`bar(t)` when given, per element), or no further
+    from it than the reference op is.  Both ops sum the same fp32 terms in
+    different orders (the reference with float atomics), so elements whose
+    terms cancel keep a summation noise of 1e-4 and more."""
     g, r = got.detach().double().cpu(), ref.detach().double().cpu()
     near = (g - r).abs() <= 1e-4 + 1e-4 * r.abs()
     if bool(near.all()):
@@ -165,7 +165,7 @@ def _check_grad(got, ref, truth, what):
     t = torch.as_tensor(np.asarray(truth(), np.float64))
     slack = 1e-6 * float(t.abs().max())
     eg, er = (g - t).abs(), (r - t).abs()
-    meets_bar = eg <= ATOL + slack + RTOL * t.abs()
+    meets_bar = eg <= (ATOL + slack + RTOL * t.abs() if bar is None else bar(t))
     no_worse = eg <= er + slack
     ok = near | meets_bar | no_worse
     if not bool(ok.all()):
@@ -175,6 +175,27 @@ def _check_grad(got, ref, truth, what):
             f"the fp32 bar of the float64 sum nor closer to it than the reference op; first at flat index {i}: "
             f"product {float(g.reshape(-1)[i])!r}, reference {float(r.reshape(-1)[i])!r}, "
             f"float64 {float(t.reshape(-1)[i])!r}")
+
+
+def _chain_rule_bars(scale, rot, d_conic):
+    """Per-element fp32 bars of d_scale (N,2) and d_rot (N,): the d_conic bar
+    (ATOL + 1e-6 max|d_conic| + RTOL |d_conic[g]|) carried through the chain
+    rule, d_s = -2/s^3 (c^2, cs, s^2)-combination of d_conic (coefficient sum
+    <= 1.5) and d_rot = (1/sx^2 - 1/sy^2) x a combination with coefficient
+    sum <= 3."""
+    dc = torch.as_tensor(np.asarray(d_conic, np.float64))
+    s = torch.as_tensor(np.asarray(scale, np.float64)).clamp_min(1e-6)
+    delta = ATOL + 1e-6 * float(dc.abs().max()) + RTOL * dc.abs().max(1).values
+    amp_s = 1.5 * 2.0 / s ** 3
+    diff = (1.0 / s[:, 0] ** 2 - 1.0 / s[:, 1] ** 2).abs()
+
+    def bar_scale(t):
+        return ATOL + RTOL * t.abs() + amp_s * delta[:, None]
+
+    def bar_rot(t):
+        return ATOL + RTOL * t.abs() + 3.0 * diff * delta
+
+    return bar_scale, bar_rot
 
 
 @pytest.mark.parametrize("n,h,w,f", BWD_GRID)
@@ -214,9 +235,19 @@ def test_backward_matches_reference_op(ref_op, our_op, cuda_device, n, h, w, f):
             own["v"] = orc.render_grads(cpu[0], cpu[1], cpu[2], cpu[3], cpu[4], h, w, mode=orc.EXACT)
         return own["v"][i]
 
-    for name, got, ref, i in (("d_xy", leaves[0].grad, dxy_r, 0), ("d_scale", leaves[1].grad, ds_r, 1),
-                              ("d_rot", leaves[2].grad, dr_r, 2), ("d_feat", leaves[3].grad, df_r, 3)):
+    for name, got, ref, i in (("d_xy", leaves[0].grad, dxy_r, 0), ("d_feat", leaves[3].grad, df_r, 3)):
         _check_grad(got, ref, lambda i=i: truth_own(i), name + " (autograd)")
+    # d_scale / d_rot carry the d_conic summation noise through the chain rule
+    # (up to 3/s^3): their fp32 bar is the d_conic bar propagated
+    bars = {}
+
+    def bar(i):
+        if not bars:
+            bars["v"] = _chain_rule_bars(cpu[1], cpu[2], truth_own(5))
+        return bars["v"][i - 1]
+
+    for name, got, ref, i in (("d_scale", leaves[1].grad, ds_r, 1), ("d_rot", leaves[2].grad, dr_r, 2)):
+        _check_grad(got, ref, lambda i=i: truth_own(i), name + " (autograd)", bar=lambda t, i=i: bar(i)(t))
 
 
 @pytest.mark.parametrize("n", [1, 1000, 200000])
