@@ -184,6 +184,7 @@ class Pipeline:
         self.aabb = torch.empty((n, 4), **i32)
         self.pair_offset = torch.empty((n + 1,), **i32)
         self.geo = torch.empty((n, 8), **f32)
+        self.prec = torch.empty((n, self.lib.oss_entry_record_floats(3)), **f32)
         self.total = torch.empty((1,), device=device, dtype=torch.int64)
         self.tile_count = torch.empty((max(1, self.lib.oss_tile_count_elems(self.tiles)),), **i32)
         self.overflow = torch.zeros((1,), **i32)
@@ -211,7 +212,6 @@ class Pipeline:
             self.pg_bytes = ((self.capacity * self.lib.oss_pair_grad_stride(3) * 4 + 255) // 256) * 256
             self.records = torch.empty((self.capacity, self.lib.oss_entry_record_floats(3)), device=dev,
                                        dtype=torch.float32)
-            self.slots = torch.empty((self.capacity,), device=dev, dtype=torch.int32)
 
     def _mark(self, i, timed):
         if timed:
@@ -225,9 +225,11 @@ class Pipeline:
         n, h, w = int(d["xy"].shape[0]), self.h, self.w
         self.n_step = n
         self._mark(0, timed)
+        # the preprocess also packs the forward records (x, y, A, B, D, rgb * opacity)
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
-                                   d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
-                                   self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
+                                   d["rot"].data_ptr(), 3, d["rgb"].data_ptr(), d["opacity"].data_ptr(),
+                                   self.conic.data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
+                                   self.geo.data_ptr(), self.prec.data_ptr(), self.total.data_ptr(),
                                    self.tile_count.data_ptr(), self.tile_offsets.data_ptr(),
                                    self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
         self._mark(1, timed)
@@ -240,17 +242,18 @@ class Pipeline:
                               self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
                               self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
         self._mark(3, timed)
-        rec = (self.records.data_ptr(), self.slots.data_ptr()) if backward else (None, None)
-        chk(lib.oss_render_forward(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(), d["opacity"].data_ptr(),
-                                   self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.image.data_ptr(),
-                                   self.aabb.data_ptr(), self.pair_offset.data_ptr(), rec[0], rec[1], s), "forward")
+        # entry records for the backward (which derives the pair slots itself)
+        rec = self.records.data_ptr() if backward else None
+        chk(lib.oss_render_forward(n, 3, h, w, None, None, None, self.prec.data_ptr(), self.gid_sorted.data_ptr(),
+                                   self.tile_offsets.data_ptr(), self.image.data_ptr(), None, None, rec, None, s),
+            "forward")
         self._mark(4, timed)
         if not backward:
             return
         chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
                                           self.capacity, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
-                                          rec[0], rec[1], d["grad"].data_ptr(), self.scratch.data_ptr(),
+                                          rec, None, d["grad"].data_ptr(), self.scratch.data_ptr(),
                                           self.scratch.data_ptr() + self.pg_bytes, self.scratch.numel() - self.pg_bytes,
                                           s), "backward_pairs")
         self._mark(5, timed)
@@ -335,8 +338,8 @@ class AlphaPipeline(Pipeline):
         chk(lib.oss_depth_order(n, d["depth"].data_ptr(), self.order.data_ptr(), self.rank.data_ptr(),
                                 self.depth_scratch.data_ptr(), self.depth_scratch.numel(), s), "depth_order")
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
-                                   d["rot"].data_ptr(), self.conic.data_ptr(), self.aabb.data_ptr(),
-                                   self.pair_offset.data_ptr(), self.geo.data_ptr(), self.total.data_ptr(),
+                                   d["rot"].data_ptr(), 0, None, None, self.conic.data_ptr(), self.aabb.data_ptr(),
+                                   self.pair_offset.data_ptr(), self.geo.data_ptr(), None, self.total.data_ptr(),
                                    self.tile_count.data_ptr(), self.tile_offsets.data_ptr(),
                                    self.prep_scratch.data_ptr(), self.prep_scratch.numel(), s), "prepare")
         self._mark(1, timed)
@@ -493,11 +496,15 @@ def run_ours(args, rank, world, local):
     if world > 1:
         import torch.distributed as dist
 
-    # per-stage breakdown: eager sync-free steps with an event between stages
+    # per-stage breakdown: eager sync-free steps with an event between stages.  A
+    # ~1 ms clock-bounded delay kernel queued ahead of each step lets the host
+    # enqueue the whole step before the GPU reaches it, so host launch gaps do not
+    # land in the stage times.
     ks = max(3, min(K, 20))
     stages = {k: 0.0 for k in pipe.stage_ms()}
     for _ in range(ks):
         flush.zero_()
+        torch.cuda._sleep(2_000_000)
         pipe.step(dev_inp)
         torch.cuda.synchronize()
         for k, v in pipe.stage_ms().items():

@@ -18,6 +18,8 @@
  *   aabb[n][4]       = (tx0, ty0, tx1, ty1) int32 tile rectangle, half-open
  *   image[f][h][w]   planar, pixel (px, py) evaluated at integer coordinates
  *   geo[n][8]        = (x, y, A, B, D, a, b, d) with (A, B, D) = (a, 2b, d) * (-0.5*log2 e)
+ *   prec[n][r]       = (x, y, A, B, D, feat'[0..f), zeros), r = oss_entry_record_floats(f),
+ *                      feat' = feat * opacity: the packed forward record of a Gaussian
  *   tile id          = ty * ceil(w/16) + tx, tiles are 16x16 pixels
  *
  * Binning modes (oss_bin_mode):
@@ -88,12 +90,17 @@ OSS_API int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, i
  * tile_count[oss_tile_count_elems(T)] (the per-tile list lengths in the
  * layout oss_bin_pairs reads; it consumes them).  In OSS_BIN_FULL mode
  * tile_count and tile_offsets are not written and may be NULL.
+ * prec (optional, 16-byte aligned; NULL skips it, and then f, feat and opacity
+ * are ignored): the packed forward records of the additive render, so that
+ * oss_render_forward gathers one record per list entry instead of geo, feat
+ * and opacity separately.  opacity may be NULL (1).
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_prepare_scratch_bytes(int64_t n);
 OSS_API int64_t oss_tile_count_elems(int64_t num_tiles);
 OSS_API int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode,
                        const float* xy, const float* scale, const float* rot,
-                       float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
+                       int64_t f, const float* feat, const float* opacity,
+                       float* conic, int32_t* aabb, int32_t* pair_offset, float* geo, float* prec,
                        int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets,
                        void* scratch, int64_t scratch_bytes, void* stream);
 
@@ -151,16 +158,21 @@ OSS_API int oss_depth_order(int64_t n, const float* depth, int32_t* order, int32
  * Replaces the rasterize_sum loop of _C.rasterize_forward
  * (rasterizer_fwd.cu:151-322, host loop :570-587).  Writes every pixel.
  *
- * Entry records (optional, both NULL or both set): for every list entry e in
- * list order, records[e][oss_entry_record_floats(f)] = (x, y, A, B, D,
- * feat'(f), zero padding) of its Gaussian and slots[e] = its gid-major pair
- * slot pair_offset[g] + local tile index (needs aabb and pair_offset).  The
- * backward reads them instead of gathering per-Gaussian data a second time.
- * records and slots hold capacity entries (any upper bound of the pair total).
+ * Per-Gaussian inputs: prec (oss_render_prepare's packed records for this f;
+ * geo, feat and opacity are then not read and may be NULL), or geo, feat and
+ * opacity.
+ *
+ * Entry records (optional): for every list entry e in list order,
+ * records[e][oss_entry_record_floats(f)] = (x, y, A, B, D, feat'(f), zero
+ * padding) of its Gaussian, and, if slots is non-NULL, slots[e] = its gid-major
+ * pair slot pair_offset[g] + local tile index (needs aabb and pair_offset).
+ * The backward reads them instead of gathering per-Gaussian data a second time
+ * (and derives the slots itself when it gets none).  records and slots hold
+ * capacity entries (any upper bound of the pair total).
  * ------------------------------------------------------------------------- */
 OSS_API int oss_entry_record_floats(int64_t f);
 OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
-                       const float* geo, const float* feat, const float* opacity,
+                       const float* geo, const float* feat, const float* opacity, const float* prec,
                        const int32_t* gid_sorted, const int32_t* tile_offsets,
                        float* image, const int32_t* aabb, const int32_t* pair_offset,
                        float* records, int32_t* slots, void* stream);
@@ -175,7 +187,8 @@ OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
  * may be NULL.  total_pairs may be the exact pair count or any upper bound of
  * it, such as the capacity given to oss_bin_pairs: the kernels take the list
  * lengths from tile_offsets and pair_offset on the device.  records/slots are
- * the forward's entry records (NULL: gathered through gid_sorted instead).
+ * the forward's entry records and slots (records NULL: gathered through
+ * gid_sorted instead; slots NULL: derived from gid_sorted, aabb, pair_offset).
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_backward_scratch_bytes(int64_t total_pairs, int64_t f, int64_t num_tiles);
 OSS_API int oss_render_backward(int64_t n, int64_t f, int64_t h, int64_t w,

@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 5; }
+int oss_abi_version(void) { return 6; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -93,7 +93,7 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
     OSS_CHECK(conic != nullptr && aabb != nullptr && pair_count != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
     OSS_CHECK(aligned(aabb, 16), OSS_ERR_INVALID, "aabb must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_count, nullptr,
-                                        nullptr, nullptr, as_stream(stream)));
+                                        nullptr, nullptr, 0, nullptr, nullptr, nullptr, as_stream(stream)));
     return OSS_OK;
 }
 
@@ -104,9 +104,10 @@ int64_t oss_tile_count_elems(int64_t num_tiles) {
 }
 
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
-                       const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                       int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets, void* scratch,
-                       int64_t scratch_bytes, void* stream) {
+                       const float* rot, int64_t f, const float* feat, const float* opacity, float* conic,
+                       int32_t* aabb, int32_t* pair_offset, float* geo, float* prec, int64_t* total_pairs,
+                       int32_t* tile_count, int32_t* tile_offsets, void* scratch, int64_t scratch_bytes,
+                       void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
@@ -120,6 +121,9 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
     if (g.n > 0) {
         OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
         OSS_CHECK(aligned(aabb, 16) && aligned(geo, 16), OSS_ERR_INVALID, "aabb and geo must be 16-byte aligned");
+        OSS_CHECK(prec == nullptr || (aligned(prec, 16) && f >= 0 && f <= OSS_MAX_CHANNELS &&
+                                      (f == 0 || feat != nullptr)),
+                  OSS_ERR_INVALID, "prec (16-byte aligned) needs F in [0, 64] and feat");
     }
     cudaStream_t s = as_stream(stream);
     long long* block_sums = static_cast<long long*>(scratch);
@@ -130,7 +134,8 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
         OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
     }
     OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
-                                        block_sums, counts, s));
+                                        block_sums, counts, static_cast<int>(prec != nullptr ? f : 0), feat, opacity,
+                                        prec, s));
     OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, counts,
                                                  oss::kTileCountStride, g.tiles, lists ? tile_offsets : nullptr, s));
     return OSS_OK;
@@ -276,9 +281,9 @@ int oss_entry_record_floats(int64_t f) {
 }
 
 int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
-                       const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
-                       const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
-                       void* stream) {
+                       const float* opacity, const float* prec, const int32_t* gid_sorted,
+                       const int32_t* tile_offsets, float* image, const int32_t* aabb, const int32_t* pair_offset,
+                       float* records, int32_t* slots, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
@@ -286,14 +291,15 @@ int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* 
     OSS_CHECK(f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be <= 64");
     if (g.tiles == 0 || f == 0) return OSS_OK;
     OSS_CHECK(tile_offsets != nullptr && image != nullptr, OSS_ERR_INVALID, "tile_offsets and image must be non-null");
-    OSS_CHECK(g.n == 0 || (geo != nullptr && feat != nullptr && aligned(geo, 16)), OSS_ERR_INVALID,
-              "geo (16-byte aligned) and feat must be non-null");
-    OSS_CHECK((records == nullptr) == (slots == nullptr), OSS_ERR_INVALID, "records and slots go together");
-    OSS_CHECK(records == nullptr || (aligned(records, 16) && aabb != nullptr && aligned(aabb, 16) &&
-                                     pair_offset != nullptr),
-              OSS_ERR_INVALID, "records (16-byte aligned) need aabb (16-byte aligned) and pair_offset");
+    OSS_CHECK(g.n == 0 || (prec != nullptr ? aligned(prec, 16)
+                                            : (geo != nullptr && feat != nullptr && aligned(geo, 16))),
+              OSS_ERR_INVALID, "prec (16-byte aligned), or geo (16-byte aligned) and feat, must be non-null");
+    OSS_CHECK(slots == nullptr || records != nullptr, OSS_ERR_INVALID, "slots are written with records");
+    OSS_CHECK(records == nullptr || aligned(records, 16), OSS_ERR_INVALID, "records must be 16-byte aligned");
+    OSS_CHECK(slots == nullptr || (aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr), OSS_ERR_INVALID,
+              "slots need aabb (16-byte aligned) and pair_offset");
     OSS_CUDA_TRY(oss::launch_render_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
-                                            tile_offsets, image, aabb, pair_offset, records, slots,
+                                            tile_offsets, image, aabb, pair_offset, records, slots, prec,
                                             as_stream(stream)));
     return OSS_OK;
 }
@@ -366,7 +372,7 @@ int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const 
     OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
     OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
               "lists and grad_image must be non-null");
-    OSS_CHECK((records == nullptr) == (slots == nullptr), OSS_ERR_INVALID, "records and slots go together");
+    OSS_CHECK(slots == nullptr || records != nullptr, OSS_ERR_INVALID, "slots come with records");
     OSS_CHECK(records == nullptr || aligned(records, 16), OSS_ERR_INVALID, "records must be 16-byte aligned");
     OSS_CUDA_TRY(oss::launch_render_backward_tiles(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, opacity,
                                                    gid_sorted, tile_offsets, grad_image, aabb, pair_offset, records,

@@ -58,9 +58,12 @@ cudaError_t radix_sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, uint32_t 
                              int32_t* vals_out, void* scratch, cudaStream_t stream);
 
 // ---- preprocess.cu ---------------------------------------------------------
+// With prec non-null also the packed forward records (entry_record_floats(f)
+// floats per Gaussian: x, y, A, B, D, feat * opacity, zero padding).
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count,
-                              float* geo, long long* block_sums, int32_t* tile_count, cudaStream_t stream);
+                              float* geo, long long* block_sums, int32_t* tile_count, int f, const float* feat,
+                              const float* opacity, float* prec, cudaStream_t stream);
 cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
 cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
                                            const float* d_conic, float* d_scale, float* d_rot,
@@ -106,11 +109,13 @@ cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, floa
 // ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
 // Entry records (forward -> backward): floats per record for f channels.
 int entry_record_floats(int f);
+// prec (optional): the packed records of launch_preprocess, read instead of
+// geo / feat / opacity.  slots (optional with records) needs aabb and pair_offset.
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat,
                                   const float* opacity, const int32_t* gid_sorted,
                                   const int32_t* tile_offsets, float* image, const int32_t* aabb,
                                   const int32_t* pair_offset, float* records, int32_t* slots,
-                                  cudaStream_t stream);
+                                  const float* prec, cudaStream_t stream);
 
 // Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows
 // (Sx, Sy, d_conic, dF) of pair_stride floats at pair_offset[g] + local tile

@@ -15,6 +15,26 @@ __device__ __forceinline__ void write_geo(float* geo, int g, float x, float y, c
     rec[1] = make_float4(k.d * kNegHalfLog2e, k.a, k.b, k.d);
 }
 
+// Packed forward record of Gaussian g: (x, y, A, B | D, feat'[0..F), zeros) in
+// prs floats (a multiple of 4), feat' = feat * opacity -- the entry record the
+// forward copies into list order, so its staging gathers one record per entry.
+__device__ __forceinline__ void write_prec(float* prec, int prs, int g, float x, float y, const Conic& k, int F,
+                                           const float* __restrict__ feat, const float* __restrict__ opacity) {
+    float4* rec = reinterpret_cast<float4*>(prec + static_cast<int64_t>(g) * prs);
+    rec[0] = make_float4(x, y, k.a * kNegHalfLog2e, (2.0f * k.b) * kNegHalfLog2e);
+    const float op = opacity != nullptr ? opacity[g] : 1.0f;
+    const float* fg = feat + static_cast<int64_t>(g) * F;
+    for (int v = 1; v < prs / 4; ++v) {
+        float e[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = 4 * v + u;  // record float i; feature c = i - 5
+            e[u] = i == 4 ? k.d * kNegHalfLog2e : (i - 5 < F ? fg[i - 5] * op : 0.0f);
+        }
+        rec[v] = make_float4(e[0], e[1], e[2], e[3]);
+    }
+}
+
 // One CTA per kPrepTile Gaussians, one Gaussian per thread.  With block_sums
 // non-null the CTA also writes the sum of its pair counts: the reduce half of
 // the gid-major pair-offset scan.  With
@@ -30,7 +50,10 @@ __global__ void __launch_bounds__(kPreprocThreads) k_preprocess(int n, int ntx, 
                                                               int32_t* __restrict__ count,
                                                               float* __restrict__ geo,
                                                               long long* __restrict__ block_sums,
-                                                              int32_t* __restrict__ tile_count) {
+                                                              int32_t* __restrict__ tile_count, int F, int prs,
+                                                              const float* __restrict__ feat,
+                                                              const float* __restrict__ opacity,
+                                                              float* __restrict__ prec) {
     long long local = 0;
     const int g = blockIdx.x * kPrepTile + threadIdx.x;
     if (g < n) {
@@ -52,6 +75,7 @@ __global__ void __launch_bounds__(kPreprocThreads) k_preprocess(int n, int ntx, 
         count[g] = cnt;
         local += cnt;
         if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
+        if (prec != nullptr) write_prec(prec, prs, g, c.x, c.y, k, F, feat, opacity);
         if (tile_count != nullptr && cnt > 0) {
             for (int ty = box.y; ty < box.w; ++ty) {
                 for (int tx = box.x; tx < box.z; ++tx) {
@@ -106,11 +130,13 @@ __global__ void __launch_bounds__(kThreads) k_conic_to_scale_rot_grad(int n, con
 
 cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
                               const float* rot, float* conic, int32_t* aabb, int32_t* count, float* geo,
-                              long long* block_sums, int32_t* tile_count, cudaStream_t stream) {
+                              long long* block_sums, int32_t* tile_count, int f, const float* feat,
+                              const float* opacity, float* prec, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
+    const int prs = prec != nullptr ? entry_record_floats(f) : 0;
     k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
-        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count);
+        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count, f, prs, feat, opacity, prec);
     return cudaGetLastError();
 }
 

@@ -14,7 +14,9 @@
 // d_conic = (-Sxx/2, -Sxy, -Syy/2) -- the reference's per-pixel terms
 // (rasterizer_bwd.cu:89-108) summed over the tile.  The entry's data comes from
 // the forward's entry records (one coalesced load) when the caller kept them,
-// else it is gathered through gid_sorted.
+// else it is gathered through gid_sorted.  The entry's pair slot comes from the
+// forward's slots when given, else from gid_sorted, aabb and pair_offset, read
+// after the sums so their latency overlaps the arithmetic.
 //
 // A tile's last item is usually partial.  With r < 32 entries it runs k lanes
 // per entry (k = 2, 4, 8 or 16, the largest with r*k <= 32), each lane taking
@@ -326,7 +328,11 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
             g1.x = rv[0];
 #pragma unroll
             for (int c = 0; c < FC; ++c) fv[c] = rv[1 + c];
-            slot = slots[first + e];
+            if (slots != nullptr) {
+                slot = slots[first + e];
+            } else {
+                g = gid_sorted[first + e];  // the slot is derived after the sums
+            }
         } else {
             g = gid_sorted[first + e];
             const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
     const float dcb = -Sxy;
     const float dcd = -0.5f * Syy;
     if (MODE != kAtomicGather) {
-        if (MODE == kDetGather) {
+        if (MODE == kDetGather || slots == nullptr) {
             const int4 box = aabb[g];
             slot = pair_offset[g] + (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
         }

@@ -16,8 +16,17 @@
 //
 // With `records` non-null the staging pass also writes, for every list entry in
 // list order, the record the backward reads instead of gathering it again:
-// [x, y, A, B | D, feat'(F) | zero padding] (entry_record_floats(F) floats), and
-// the entry's gid-major pair slot pair_offset[g] + (local tile index).
+// [x, y, A, B | D, feat'(F) | zero padding] (entry_record_floats(F) floats), and,
+// with `slots` non-null, the entry's gid-major pair slot pair_offset[g] +
+// (local tile index).
+//
+// Staging is a gather through gid_sorted, and scattered loads cost one L1
+// wavefront per distinct cache line per instruction: from geo, opacity, feat,
+// aabb and pair_offset that is eight per entry, which made the staging, not
+// the ex2 math, the larger part of the kernel.  With `prec` (the per-Gaussian
+// packed records the preprocess writes, already in the entry-record layout)
+// an entry costs one 32-byte line (two 16-byte loads at F <= 3), and the
+// backward derives the slots itself.
 //
 // The reference zeroes a weight when q is non-finite or negative
 // (rasterizer_fwd.cu:245).  A batch whose conics are all finite and
@@ -42,6 +51,13 @@ struct FwdCfg {
 __device__ __forceinline__ bool regular_conic(float x, float y, float a, float b, float d) {
     const bool finite = isfinite(x) && isfinite(y) && isfinite(a) && isfinite(b) && isfinite(d);
     return finite && a > 0.0f && d > 0.0f && (a * d - b * b) >= 1.0e-3f * (a * d);
+}
+
+// The same test on the scaled record (A, B, D) = (a, 2b, d) * (-log2(e) / 2):
+// the inequality scales by a positive factor, so only rounding (1e-7
+// relative, against the 1e-3 margin) separates the two.
+__device__ __forceinline__ bool regular_scaled(float x, float y, float A, float B, float D) {
+    return regular_conic(x, y, -A, -0.5f * B, -D);
 }
 
 template <int FC, bool CHECK>
@@ -85,7 +101,7 @@ __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__
                                              float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
     constexpr int NP = FwdCfg<FC>::PX / 2;
     constexpr int S = FwdCfg<FC>::S;
-#pragma unroll 2
+#pragma unroll 4
     for (int j = 0; j < cnt; ++j) {
         const float4 g0 = s_geo[j];
         const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
@@ -134,7 +150,8 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
                                                                 const int4* __restrict__ aabb,
                                                                 const int32_t* __restrict__ pair_offset,
                                                                 float* __restrict__ records,
-                                                                int32_t* __restrict__ slots) {
+                                                                int32_t* __restrict__ slots,
+                                                                const float* __restrict__ prec) {
     constexpr int PX = FwdCfg<FC>::PX;
     constexpr int NT = FwdCfg<FC>::NT;
     constexpr int S = FwdCfg<FC>::S;
@@ -177,26 +194,49 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
         bool regular = true;
         for (int j = threadIdx.x; j < cnt; j += NT) {
             const int g = gid_sorted[b + j];
-            const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-            const float4 g0 = rec[0];
-            const float4 g1 = rec[1];
-            s_geo[j] = g0;
-            regular = regular && regular_conic(g0.x, g0.y, g1.y, g1.z, g1.w);
-            const float op = opacity != nullptr ? opacity[g] : 1.0f;
-            float* df = s_df + j * S;
-            df[0] = g1.x;
-            const float* fg = feat + static_cast<int64_t>(g) * F;
+            const int e = b + j;
+            float4* sdf4 = reinterpret_cast<float4*>(s_df + j * S);
+            float4* rec = records != nullptr ? reinterpret_cast<float4*>(records + static_cast<int64_t>(e) * (4 + S))
+                                             : nullptr;
+            if (prec != nullptr) {
+                // one packed record per entry: a single gathered cache line
+                const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * (4 + S));
+                const float4 g0 = pr[0];
+                const float4 g1 = pr[1];
+                s_geo[j] = g0;
+                regular = regular && regular_scaled(g0.x, g0.y, g0.z, g0.w, g1.x);
+                sdf4[0] = g1;
+                if (rec != nullptr) {
+                    rec[0] = g0;
+                    rec[1] = g1;
+                }
 #pragma unroll
-            for (int c = 0; c < FC; ++c) df[1 + c] = c < F ? fg[c] * op : 0.0f;
+                for (int v = 1; v < S / 4; ++v) {
+                    const float4 t = pr[1 + v];
+                    sdf4[v] = t;
+                    if (rec != nullptr) rec[1 + v] = t;
+                }
+            } else {
+                const float4* gr = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
+                const float4 g0 = gr[0];
+                const float4 g1 = gr[1];
+                s_geo[j] = g0;
+                regular = regular && regular_conic(g0.x, g0.y, g1.y, g1.z, g1.w);
+                const float op = opacity != nullptr ? opacity[g] : 1.0f;
+                float* df = s_df + j * S;
+                df[0] = g1.x;
+                const float* fg = feat + static_cast<int64_t>(g) * F;
 #pragma unroll
-            for (int c = 1 + FC; c < S; ++c) df[c] = 0.0f;
-            if (records != nullptr) {
-                const int e = b + j;
-                float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(e) * (4 + S));
-                rec[0] = g0;
-                const float4* df4 = reinterpret_cast<const float4*>(df);
+                for (int c = 0; c < FC; ++c) df[1 + c] = c < F ? fg[c] * op : 0.0f;
 #pragma unroll
-                for (int v = 0; v < S / 4; ++v) rec[1 + v] = df4[v];
+                for (int c = 1 + FC; c < S; ++c) df[c] = 0.0f;
+                if (rec != nullptr) {
+                    rec[0] = g0;
+#pragma unroll
+                    for (int v = 0; v < S / 4; ++v) rec[1 + v] = sdf4[v];
+                }
+            }
+            if (slots != nullptr) {
                 const int4 box = aabb[g];
                 slots[e] = pair_offset[g] + (tile / ntx - box.y) * (box.z - box.x) + (tile % ntx - box.x);
             }
@@ -241,14 +281,235 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
     }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, software-pipelined variant for packed records (F <= 4).
+//
+// With one CTA per tile, the CTAs an SM holds start together, stage together
+// (the MUFU idle) and compute together, wave after wave.  Here a CTA walks the
+// tiles blockIdx.x, +gridDim.x, ... and, while it computes tile i, tile i+1's
+// records are already on their way into the other shared-memory buffer
+// (cp.async, 16-byte global -> shared copies that hold no registers).  The
+// gids of tile i+2 and the list offsets of tile i+3 are loaded into registers
+// a step earlier still, so no dependent global load waits in front of the
+// math.  Lists longer than PBATCH entries stage their later batches in place.
+// ---------------------------------------------------------------------------
+constexpr int kPipeBatch = 128;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+template <int FC>
+__global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H, int W, int ntx, int num_tiles,
+                                                                     const float* __restrict__ prec,
+                                                                     const int32_t* __restrict__ gid_sorted,
+                                                                     const int32_t* __restrict__ tile_offsets,
+                                                                     float* __restrict__ image,
+                                                                     float* __restrict__ records) {
+    constexpr int PX = FwdCfg<FC>::PX;
+    static_assert(PX % 2 == 0, "pipelined forward runs the packed pixel-pair path");
+    constexpr int NT = FwdCfg<FC>::NT;
+    constexpr int S = FwdCfg<FC>::S;
+    constexpr int RS = 4 + S;               // record floats
+    constexpr int PB = kPipeBatch;
+    constexpr int PER = PB / NT;             // entries per thread and batch
+    constexpr int ROWSTEP = kTile / PX;
+    constexpr int NP = PX / 2;
+    __shared__ float4 s_geo[2][PB];
+    __shared__ __align__(16) float s_df[2][PB * S];
+
+    const int G = gridDim.x;
+    const int lx = threadIdx.x & (kTile - 1);
+    const int ly = threadIdx.x >> 4;
+
+    // register pipeline: offsets of the current, next and next-but-one tile, gids of the next
+    int t = blockIdx.x;
+    int oc0 = 0, oc1 = 0, on0 = 0, on1 = 0, oq0 = 0, oq1 = 0;
+    if (t < num_tiles) { oc0 = tile_offsets[t]; oc1 = tile_offsets[t + 1]; }
+    if (t + G < num_tiles) { on0 = tile_offsets[t + G]; on1 = tile_offsets[t + G + 1]; }
+    if (t + 2 * G < num_tiles) { oq0 = tile_offsets[t + 2 * G]; oq1 = tile_offsets[t + 2 * G + 1]; }
+    int gn[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int j = threadIdx.x + k * NT;
+        gn[k] = j < min(PB, on1 - on0) ? gid_sorted[on0 + j] : 0;
+    }
+    // prologue: the first tile's first batch into buffer 0
+    {
+        const int cnt = min(PB, oc1 - oc0);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int j = threadIdx.x + k * NT;
+            if (j < cnt) {
+                const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(gid_sorted[oc0 + j]) * RS);
+                cp_async16(&s_geo[0][j], pr);
+#pragma unroll
+                for (int v = 0; v < S / 4; ++v) cp_async16(&s_df[0][j * S + 4 * v], pr + 1 + v);
+            }
+        }
+        cp_async_commit();
+    }
+
+    for (int it = 0; t < num_tiles; t += G, ++it) {
+        const int buf = it & 1;
+        // 1. next tile's first batch into the other buffer (its readers finished at the last barrier)
+        {
+            const int cnt = min(PB, on1 - on0);
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int j = threadIdx.x + k * NT;
+                if (t + G < num_tiles && j < cnt) {
+                    const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(gn[k]) * RS);
+                    cp_async16(&s_geo[buf ^ 1][j], pr);
+#pragma unroll
+                    for (int v = 0; v < S / 4; ++v) cp_async16(&s_df[buf ^ 1][j * S + 4 * v], pr + 1 + v);
+                }
+            }
+            cp_async_commit();
+        }
+        // 2. gids of the tile after next, offsets of the one after that
+        {
+            const int cnt = min(PB, oq1 - oq0);
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int j = threadIdx.x + k * NT;
+                gn[k] = (t + 2 * G < num_tiles && j < cnt) ? gid_sorted[oq0 + j] : 0;
+            }
+        }
+        const int cur0 = oc0, cur1 = oc1;
+        oc0 = on0; oc1 = on1; on0 = oq0; on1 = oq1;
+        if (t + 3 * G < num_tiles) {
+            oq0 = tile_offsets[t + 3 * G];
+            oq1 = tile_offsets[t + 3 * G + 1];
+        } else {
+            oq0 = 0;
+            oq1 = 0;
+        }
+
+        const int tx0 = (t % ntx) * kTile;
+        const int ty0 = (t / ntx) * kTile;
+        const float fpx = static_cast<float>(tx0 + lx);
+        float2 fpy2[NP];
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+            fpy2[q] = make_float2(static_cast<float>(ty0 + ly + 2 * q * ROWSTEP),
+                                  static_cast<float>(ty0 + ly + (2 * q + 1) * ROWSTEP));
+        }
+        float2 acc2[NP][FC];
+#pragma unroll
+        for (int q = 0; q < NP; ++q)
+#pragma unroll
+            for (int c = 0; c < FC; ++c) acc2[q][c] = make_float2(0.0f, 0.0f);
+
+        // 3. this tile's first batch: own copies done, entry records out, then everyone's visible
+        cp_async_wait_one();
+        const int n0 = min(PB, cur1 - cur0);
+        bool regular = true;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int j = threadIdx.x + k * NT;
+            if (j < n0) {
+                const float4 g0 = s_geo[buf][j];
+                const float4* d4 = reinterpret_cast<const float4*>(&s_df[buf][j * S]);
+                regular = regular && regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                if (records != nullptr) {
+                    float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(cur0 + j) * RS);
+                    rec[0] = g0;
+#pragma unroll
+                    for (int v = 0; v < S / 4; ++v) rec[1 + v] = d4[v];
+                }
+            }
+        }
+        bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
+        if (all_regular) {
+            fwd_batch_pk<FC, false>(n0, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
+        } else {
+            fwd_batch_pk<FC, true>(n0, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
+        }
+        // 4. later batches of a long list, staged in place
+        for (int b = cur0 + PB; b < cur1; b += PB) {
+            const int cnt = min(PB, cur1 - b);
+            __syncthreads();  // the previous batch has been consumed
+            bool reg = true;
+            for (int j = threadIdx.x; j < cnt; j += NT) {
+                const int e = b + j;
+                const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(gid_sorted[e]) * RS);
+                const float4 g0 = pr[0];
+                s_geo[buf][j] = g0;
+                float4* d4 = reinterpret_cast<float4*>(&s_df[buf][j * S]);
+#pragma unroll
+                for (int v = 0; v < S / 4; ++v) d4[v] = pr[1 + v];
+                reg = reg && regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                if (records != nullptr) {
+                    float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(e) * RS);
+                    rec[0] = g0;
+#pragma unroll
+                    for (int v = 0; v < S / 4; ++v) rec[1 + v] = d4[v];
+                }
+            }
+            all_regular = __syncthreads_and(reg ? 1 : 0) != 0;
+            if (all_regular) {
+                fwd_batch_pk<FC, false>(cnt, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
+            } else {
+                fwd_batch_pk<FC, true>(cnt, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
+            }
+        }
+        // 5. image
+        const int px = tx0 + lx;
+        if (px < W) {
+            const int64_t plane = static_cast<int64_t>(H) * W;
+#pragma unroll
+            for (int q = 0; q < NP; ++q) {
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const int py = ty0 + ly + (2 * q + h2) * ROWSTEP;
+                    if (py < H) {
+                        const int64_t pix = static_cast<int64_t>(py) * W + px;
+#pragma unroll
+                        for (int c = 0; c < FC; ++c) {
+                            if (c < F) image[c * plane + pix] = h2 == 0 ? acc2[q][c].x : acc2[q][c].y;
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();  // buffer `buf` is free for the prefetch two tiles on
+    }
+}
+
+// CTAs per SM the pipelined forward runs with (queried once per device).
+template <int FC>
+int pipe_grid(int num_tiles) {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_tiles;
+    if (cached[dev] == 0) {
+        int sms = 0, per = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC>, FwdCfg<FC>::NT, 0);
+        cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
+    }
+    return num_tiles < cached[dev] ? num_tiles : cached[dev];
+}
+
 template <int FC>
 cudaError_t launch_fwd_fc(int f, int h, int w, int ntx, int num_tiles, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
                           const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
-                          cudaStream_t stream) {
+                          const float* prec, cudaStream_t stream) {
+    if constexpr (FwdCfg<FC>::PX % 2 == 0) {
+        if (prec != nullptr && slots == nullptr) {
+            k_render_fwd_pipe<FC><<<static_cast<unsigned>(pipe_grid<FC>(num_tiles)), FwdCfg<FC>::NT, 0, stream>>>(
+                f, h, w, ntx, num_tiles, prec, gid_sorted, tile_offsets, image, records);
+            return cudaGetLastError();
+        }
+    }
     k_render_fwd<FC><<<static_cast<unsigned>(num_tiles), FwdCfg<FC>::NT, 0, stream>>>(
         f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, image, reinterpret_cast<const int4*>(aabb),
-        pair_offset, records, slots);
+        pair_offset, records, slots, prec);
     return cudaGetLastError();
 }
 
@@ -272,14 +533,14 @@ int entry_record_floats(int f) {
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat, const float* opacity,
                                   const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
                                   const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
-                                  cudaStream_t stream) {
+                                  const float* prec, cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
     if (num_tiles == 0 || f == 0) return cudaSuccess;
 #define OSS_FWD_CALL(FC)                                                                                           \
     launch_fwd_fc<FC>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, aabb,          \
-                      pair_offset, records, slots, stream)
+                      pair_offset, records, slots, prec, stream)
     if (f <= 1) return OSS_FWD_CALL(1);
     if (f <= 3) return OSS_FWD_CALL(3);
     if (f <= 4) return OSS_FWD_CALL(4);

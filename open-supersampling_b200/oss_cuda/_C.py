@@ -42,7 +42,7 @@ def rasterize_forward(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True, 
     check_hw(h, w, tile_size)
     mode = binning_mode(binning)
     with torch.cuda.device(xy.device):
-        b = bin_gaussians(xy, scale, rot, h, w, mode)
+        b = bin_gaussians(xy, scale, rot, h, w, mode, feat=feat)
         out = render_forward(b, aligned(feat, 4), None)
     return out, b.gid_sorted, b.tile_offsets, b.conic
 

@@ -32,7 +32,8 @@ SIGNATURES = {
     "oss_render_prepare_scratch_bytes": (_i64, [_i64]),
     "oss_tile_count_elems": (_i64, [_i64]),
     "oss_render_prepare": (
-        ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i32, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_bin_pairs": (
         ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p]),
@@ -48,7 +49,7 @@ SIGNATURES = {
          _p, _i64, _p],
     ),
     "oss_entry_record_floats": (ctypes.c_int, [_i64]),
-    "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_render_backward_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_render_backward": (
         ctypes.c_int,

@@ -120,6 +120,8 @@ class Binned:
     total_pairs: int
     gid_sorted: torch.Tensor   # (P,) int32
     tile_offsets: torch.Tensor  # (T+1,) int32
+    prec: torch.Tensor | None = None  # (N, entry_record_floats(prec_f)) packed forward records
+    prec_f: int = -1
 
 
 _HOST_TOTAL = {}
@@ -180,12 +182,15 @@ def pair_capacity_overflowed(device=None, reset: bool = True) -> bool:
 
 
 def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: int, w: int, mode: int,
-                  depth: torch.Tensor | None = None, capacity: int | None = None) -> Binned:
+                  depth: torch.Tensor | None = None, capacity: int | None = None, feat: torch.Tensor | None = None,
+                  opacity: torch.Tensor | None = None) -> Binned:
     """Preprocess + deterministic tile binning.  One host sync (the pair total)
     except in full mode, where the total N*T is known up front, and in capacity
     mode, where the lists are sized for `capacity` pairs, the device checks the
     total and raises the sticky overflow flag instead (no host sync).  With depth
-    the tile lists are ordered by (depth, gid) instead of gid (alpha blending)."""
+    the tile lists are ordered by (depth, gid) instead of gid (alpha blending).
+    With feat (and optionally opacity) the preprocess also packs the forward
+    records of the additive render (one gathered line per list entry)."""
     lib = _lib.lib()
     n = int(xy.size(0))
     _, _, num_tiles, _ = check_hw(h, w, _lib.TILE)
@@ -201,15 +206,21 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     aabb = torch.empty((n, 4), **i32)
     pair_offset = torch.empty((n + 1,), **i32)
     geo = torch.empty((n, 8), **f32)
+    prec, prec_f = None, -1
+    if feat is not None:
+        prec_f = int(feat.size(1))
+        feat = aligned(feat, 4)
+        prec = torch.empty((n, lib.oss_entry_record_floats(prec_f)), **f32)
     total = torch.empty((1,), device=dev, dtype=torch.int64)
     tile_count = torch.empty((max(1, lib.oss_tile_count_elems(num_tiles)),), **i32)
     tile_offsets = torch.empty((num_tiles + 1,), **i32)
     scratch = torch.empty((max(1, lib.oss_render_prepare_scratch_bytes(n)),), device=dev, dtype=torch.uint8)
     _lib.check(
-        lib.oss_render_prepare(n, h, w, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(), conic.data_ptr(),
-                               aabb.data_ptr(), pair_offset.data_ptr(), geo.data_ptr(), total.data_ptr(),
-                               tile_count.data_ptr(), tile_offsets.data_ptr(), scratch.data_ptr(), scratch.numel(),
-                               stream),
+        lib.oss_render_prepare(n, h, w, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(), max(prec_f, 0),
+                               _lib.ptr(feat), _lib.ptr(opacity if feat is not None else None), conic.data_ptr(),
+                               aabb.data_ptr(), pair_offset.data_ptr(), geo.data_ptr(), _lib.ptr(prec),
+                               total.data_ptr(), tile_count.data_ptr(), tile_offsets.data_ptr(), scratch.data_ptr(),
+                               scratch.numel(), stream),
         "oss_render_prepare",
     )
     if mode == _lib.OSS_BIN_FULL:
@@ -237,12 +248,14 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
     )
     if capacity is not None and mode != _lib.OSS_BIN_FULL:
         sticky_overflow(dev).bitwise_or_(overflow)
-    return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
+    return Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets, prec, prec_f)
 
 
 def render_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, records: bool = False):
-    """(F, H, W) image; with records=True also the per-entry records and pair
-    slots the backward reads (returns (image, records, slots))."""
+    """(F, H, W) image; with records=True also the per-entry records the
+    backward reads (returns (image, records, slots); slots is None: the backward
+    derives the pair slots from the lists).  Uses the packed records of
+    bin_gaussians(feat=...) when they were made for these features."""
     lib = _lib.lib()
     f = int(feat.size(1))
     dev = feat.device
@@ -250,12 +263,12 @@ def render_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, 
     rec = slots = None
     if records and b.mode != _lib.OSS_BIN_FULL and b.total_pairs > 0:
         rec = torch.empty((b.total_pairs, lib.oss_entry_record_floats(f)), device=dev, dtype=torch.float32)
-        slots = torch.empty((b.total_pairs,), device=dev, dtype=torch.int32)
+    prec = b.prec if b.prec is not None and b.prec_f == f else None
     _lib.check(
         lib.oss_render_forward(b.n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
-                               b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(), image.data_ptr(),
-                               b.aabb.data_ptr(), b.pair_offset.data_ptr(), _lib.ptr(rec), _lib.ptr(slots),
-                               stream_of(feat)),
+                               _lib.ptr(prec), b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(),
+                               image.data_ptr(), b.aabb.data_ptr(), b.pair_offset.data_ptr(), _lib.ptr(rec),
+                               _lib.ptr(slots), stream_of(feat)),
         "oss_render_forward",
     )
     if records:

@@ -56,7 +56,7 @@ class _RasterizeGaussians(Function):
             )
         del topk_norm
         with torch.cuda.device(xy.device):
-            b = _raster.bin_gaussians(xy, scale, rot, h, w, mode, capacity=capacity)
+            b = _raster.bin_gaussians(xy, scale, rot, h, w, mode, capacity=capacity, feat=feat, opacity=opacity)
             # the entry records the backward reads are written only when a gradient can follow
             if any(ctx.needs_input_grad[:5]):
                 out, records, slots = _raster.render_forward(b, _raster.aligned(feat, 4), opacity, records=True)

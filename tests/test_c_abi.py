@@ -44,7 +44,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_clean_error_state():
     lib = _lib.lib()
-    assert lib.oss_abi_version() == 5
+    assert lib.oss_abi_version() == 6
 
 
 def test_rejects_tile_size_other_than_16():
@@ -62,10 +62,10 @@ def test_rejects_bad_sizes_and_modes():
     assert lib.oss_last_error().decode() == "H exceeds int32 range"
     assert lib.oss_preprocess(1, 1 << 30, 1 << 30, 16, 0, None, None, None, None, None, None, None) == 3
     assert lib.oss_last_error().decode() == "number of tiles exceeds int32 range"
-    assert lib.oss_render_prepare(1, 32, 32, 7, None, None, None, None, None, None, None, None, None, None, None,
-                                  0, None) == 1
+    assert lib.oss_render_prepare(1, 32, 32, 7, None, None, None, 0, None, None, None, None, None, None, None, None,
+                                  None, None, None, 0, None) == 1
     assert "binning mode" in lib.oss_last_error().decode()
-    assert lib.oss_render_forward(1, 65, 32, 32, None, None, None, None, None, None, None, None, None, None,
+    assert lib.oss_render_forward(1, 65, 32, 32, None, None, None, None, None, None, None, None, None, None, None,
                                   None) == 1
     assert lib.oss_last_error().decode() == "F must be <= 64"
     assert lib.oss_full_tile_pairs(1 << 20, 1 << 12, None, None, None) == 3
@@ -86,10 +86,17 @@ def test_rejects_scratch_too_small():
     lib = _lib.lib()
     need = lib.oss_render_prepare_scratch_bytes(1000)
     assert need > 0
-    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 8, 16, 8, 16, 8, 8, 8, 8, need - 1, None)
+    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 0, None, None, 8, 16, 8, 16, None, 8, 8, 8, 8, need - 1,
+                                None)
     assert rc == 4 and "scratch" in lib.oss_last_error().decode()
-    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 8, 16, 8, 16, 8, None, 8, 8, need, None)
+    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 0, None, None, 8, 16, 8, 16, None, 8, None, 8, 8, need,
+                                None)
     assert rc == 1 and "tile_count" in lib.oss_last_error().decode()
+    # packed records need 16-byte alignment and the features
+    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 3, None, None, 16, 16, 8, 16, 32, 8, 8, 8, 8, need, None)
+    assert rc == 1 and "prec" in lib.oss_last_error().decode()
+    rc = lib.oss_render_prepare(1000, 64, 64, 0, 8, 8, 8, 3, 16, None, 16, 16, 8, 16, 40, 8, 8, 8, 8, need, None)
+    assert rc == 1 and "prec" in lib.oss_last_error().decode()
     assert lib.oss_tile_count_elems(100) >= 100
     bneed = lib.oss_bin_pairs_scratch_bytes(1000, 5000, 16)
     rc = lib.oss_bin_pairs(1000, 64, 64, 0, 16, 8, 8, 8, 5000, None, None, 8, 8, 8, 8, bneed - 1, None)

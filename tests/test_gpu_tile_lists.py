@@ -56,6 +56,13 @@ class Lists:
         self.overflow = torch.full((1,), -1, **i32)
         self.prep_scratch = torch.empty((max(1, self.lib.oss_render_prepare_scratch_bytes(n)),), device="cuda",
                                         dtype=torch.uint8)
+        self.pf, self.pfeat, self.popacity, self.prec = 0, None, None, None
+
+    def pack(self, feat, opacity=None):
+        """Have the preprocess also write the packed forward records."""
+        self.pf, self.pfeat, self.popacity = int(feat.size(1)), feat, opacity
+        self.prec = torch.empty((max(1, self.n), self.lib.oss_entry_record_floats(self.pf)), device="cuda",
+                                dtype=torch.float32)
 
     def set_capacity(self, capacity):
         self.capacity = capacity
@@ -64,11 +71,14 @@ class Lists:
         self.scratch = torch.empty((max(1, nb),), device="cuda", dtype=torch.uint8)
 
     def run(self):
+        from oss_cuda import _lib
+
         s = torch.cuda.current_stream().cuda_stream
         self.chk(self.lib.oss_render_prepare(self.n, self.h, self.w, self.mode, self.xy.data_ptr(),
-                                             self.scale.data_ptr(), self.rot.data_ptr(), self.conic.data_ptr(),
+                                             self.scale.data_ptr(), self.rot.data_ptr(), self.pf,
+                                             _lib.ptr(self.pfeat), _lib.ptr(self.popacity), self.conic.data_ptr(),
                                              self.aabb.data_ptr(), self.pair_offset.data_ptr(), self.geo.data_ptr(),
-                                             self.total.data_ptr(), self.tile_count.data_ptr(),
+                                             _lib.ptr(self.prec), self.total.data_ptr(), self.tile_count.data_ptr(),
                                              self.tile_offsets.data_ptr(), self.prep_scratch.data_ptr(),
                                              self.prep_scratch.numel(), s), "prepare")
         self.chk(self.lib.oss_bin_pairs(self.n, self.h, self.w, self.mode, self.aabb.data_ptr(),
@@ -154,7 +164,7 @@ def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
     # downstream stages stay in bounds and produce zeros
     lib, s_ = L.lib, torch.cuda.current_stream().cuda_stream
     img = torch.full((3, h, w), 5.0, device="cuda")
-    _lib.check(lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
+    _lib.check(lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, None, L.gid.data_ptr(),
                                       L.tile_offsets.data_ptr(), img.data_ptr(), None, None, None, None, s_),
                "forward")
     assert not host(img).any()
@@ -175,6 +185,65 @@ def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
     assert int(L.overflow.item()) == 0
     np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
     np.testing.assert_array_equal(host(L.gid), g_ref)
+
+
+@pytest.mark.parametrize("f,dense", [(1, False), (3, False), (3, True), (5, False), (12, False), (24, False)])
+def test_packed_records_and_derived_slots_bit_identical(cuda_device, f, dense):
+    """The forward reading the preprocess's packed records gives the same image
+    bits as the geo / feat / opacity gathers, and the backward deriving the
+    pair slots gives the same gradient bits as with the forward's slots."""
+    from oss_cuda import _lib
+
+    h, w, n = 112, 176, 2500
+    rng = np.random.default_rng(5 + f)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    # dense: lists of several hundred entries (later batches staged in place)
+    s = (rng.random((n, 2)) * (12.0 if dense else 3.0) + 0.5).astype(np.float32)
+    rot = (rng.random(n) * 6.28).astype(np.float32)
+    feat = dev(rng.standard_normal((n, f)))
+    opacity = dev(rng.random(n))
+    L = Lists(xy, s, rot, h, w, orc.TIGHT)
+    L.pack(feat, opacity)
+    L.set_capacity(int(orc.lists(xy, s, rot, h, w, orc.TIGHT)[3].size))
+    L.run()
+    assert int(L.overflow.item()) == 0
+    lib, s_ = L.lib, torch.cuda.current_stream().cuda_stream
+    rf = lib.oss_entry_record_floats(f)
+    imgs, recs, slots = [], [], []
+    # gathers with slots; packed records with slots; packed records without slots (the
+    # persistent pipelined kernel for F <= 16)
+    for packed, with_slots in ((False, True), (True, True), (True, False)):
+        img = torch.empty((f, h, w), device="cuda")
+        rec = torch.empty((L.capacity, rf), device="cuda")
+        sl = torch.full((L.capacity,), -1, device="cuda", dtype=torch.int32)
+        _lib.check(lib.oss_render_forward(n, f, h, w, L.geo.data_ptr(), feat.data_ptr(), opacity.data_ptr(),
+                                          L.prec.data_ptr() if packed else None, L.gid.data_ptr(),
+                                          L.tile_offsets.data_ptr(), img.data_ptr(), L.aabb.data_ptr(),
+                                          L.pair_offset.data_ptr(), rec.data_ptr(),
+                                          sl.data_ptr() if with_slots else None, s_), "forward")
+        imgs.append(img)
+        recs.append(rec)
+        slots.append(sl)
+    for k in (1, 2):
+        assert torch.equal(imgs[0], imgs[k])
+        assert torch.equal(recs[0][: L.total.item()], recs[k][: L.total.item()])
+    assert torch.equal(slots[0], slots[1])
+    grad = dev(rng.standard_normal((f, h, w)))
+    nb = lib.oss_render_backward_scratch_bytes(L.capacity, f, L.tiles)
+    grads = []
+    for use_slots in (True, False):
+        scratch = torch.empty((nb,), device="cuda", dtype=torch.uint8)
+        outs = [torch.empty(sh, device="cuda") for sh in ((n, 2), (n, 3), (n, f), (n,), (n, 2), (n,))]
+        _lib.check(lib.oss_render_backward(n, f, h, w, L.geo.data_ptr(), feat.data_ptr(), opacity.data_ptr(),
+                                           L.scale.data_ptr(), L.rot.data_ptr(), L.aabb.data_ptr(),
+                                           L.pair_offset.data_ptr(), L.capacity, L.gid.data_ptr(),
+                                           L.tile_offsets.data_ptr(), recs[1].data_ptr(),
+                                           slots[1].data_ptr() if use_slots else None, grad.data_ptr(),
+                                           *[o.data_ptr() for o in outs], scratch.data_ptr(), scratch.numel(), s_),
+                   "backward")
+        grads.append(outs)
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
 
 
 def test_sync_free_path_replays_in_cuda_graph(cuda_device):
@@ -199,9 +268,9 @@ def test_sync_free_path_replays_in_cuda_graph(cuda_device):
 
     def step():
         L.run()
-        _lib.check(L.lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, L.gid.data_ptr(),
-                                            L.tile_offsets.data_ptr(), img.data_ptr(), None, None, None, None,
-                                            torch.cuda.current_stream().cuda_stream), "forward")
+        _lib.check(L.lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, None,
+                                            L.gid.data_ptr(), L.tile_offsets.data_ptr(), img.data_ptr(), None, None,
+                                            None, None, torch.cuda.current_stream().cuda_stream), "forward")
 
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
