@@ -519,24 +519,50 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
     if (g >= n) return;
     const int beg = pair_offset[g];
     const int end = pair_offset[g + 1];
+    // per-Gaussian inputs of the epilogue, loaded ahead of the row sums so their
+    // latency overlaps them
+    const float4 k1 = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8)[1];
+    const float op = opacity != nullptr ? opacity[g] : 1.0f;
+    float2 sc = make_float2(0.0f, 0.0f);
+    float th = 0.0f;
+    if (d_scale != nullptr) {
+        sc = make_float2(scale[2 * g], scale[2 * g + 1]);
+        th = rot[g];
+    }
     float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
     float dF[FC];
 #pragma unroll
     for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
-    for (int p = beg; p < end; ++p) {
+    if (FC <= 3) {
+        // rows four at a time, all loads issued before the (in-order) sums
+        for (int p = beg; p < end; p += 4) {
+            float4 r0[4], r1[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (p + u < end) {
+                    const float4* row = reinterpret_cast<const float4*>(pairgrad + static_cast<int64_t>(p + u) * pstride);
+                    r0[u] = row[0];
+                    r1[u] = row[1];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (p + u < end) {
+                    s0 += r0[u].x;
+                    s1 += r0[u].y;
+                    s2 += r0[u].z;
+                    s3 += r0[u].w;
+                    s4 += r1[u].x;
+                    dF[0] += r1[u].y;
+                    if (FC > 1) dF[FC > 1 ? 1 : 0] += r1[u].z;
+                    if (FC > 2) dF[FC > 2 ? 2 : 0] += r1[u].w;
+                }
+            }
+        }
+    } else {
+      for (int p = beg; p < end; ++p) {
         const float* row = pairgrad + static_cast<int64_t>(p) * pstride;
-        if (FC <= 3) {
-            const float4 r0 = reinterpret_cast<const float4*>(row)[0];
-            const float4 r1 = reinterpret_cast<const float4*>(row)[1];
-            s0 += r0.x;
-            s1 += r0.y;
-            s2 += r0.z;
-            s3 += r0.w;
-            s4 += r1.x;
-            dF[0] += r1.y;
-            if (FC > 1) dF[FC > 1 ? 1 : 0] += r1.z;
-            if (FC > 2) dF[FC > 2 ? 2 : 0] += r1.w;
-        } else {
+        {
             s0 += row[0];
             s1 += row[1];
             s2 += row[2];
@@ -547,15 +573,14 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
                 if (c < F) dF[c] += row[5 + c];
             }
         }
+      }
     }
     // (s0, s1) = (sum Sx, sum Sy); the raw conic (a, b, d) is geo[g][5..7]
-    const float4 k1 = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8)[1];
     d_xy[2 * g + 0] = fmaf(k1.y, s0, k1.z * s1);
     d_xy[2 * g + 1] = fmaf(k1.z, s0, k1.w * s1);
     d_conic[3 * g + 0] = s2;
     d_conic[3 * g + 1] = s3;
     d_conic[3 * g + 2] = s4;
-    const float op = opacity != nullptr ? opacity[g] : 1.0f;
     float dop = 0.0f;
 #pragma unroll
     for (int c = 0; c < FC; ++c) {
@@ -568,7 +593,7 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
     if (d_opacity != nullptr) d_opacity[g] = dop;
     if (d_scale != nullptr) {
         float dsx, dsy, dr;
-        conic_grad_to_scale_rot(scale[2 * g], scale[2 * g + 1], rot[g], s2, s3, s4, dsx, dsy, dr);
+        conic_grad_to_scale_rot(sc.x, sc.y, th, s2, s3, s4, dsx, dsy, dr);
         d_scale[2 * g + 0] = dsx;
         d_scale[2 * g + 1] = dsy;
         d_rot[g] = dr;
