@@ -197,6 +197,7 @@ class Pipeline:
         self.tile_offsets = torch.empty((self.tiles + 1,), **i32)
         self.capacity = 0
         self.events = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        self.side = torch.cuda.Stream(device=device)  # the backward's item table, beside the forward
         self.device = device
         self.n = n
         self.pairs = 0
@@ -242,6 +243,15 @@ class Pipeline:
                               self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(), self.overflow.data_ptr(),
                               self.scratch.data_ptr(), self.scratch.numel(), s), "bin")
         self._mark(3, timed)
+        items = self.scratch.data_ptr() + self.pg_bytes
+        items_bytes = self.scratch.numel() - self.pg_bytes
+        if backward:
+            # the backward's work-item table needs only the list offsets: build it on a
+            # side stream while the forward runs
+            main = torch.cuda.current_stream()
+            self.side.wait_stream(main)
+            chk(lib.oss_backward_items(h, w, self.capacity, self.tile_offsets.data_ptr(), items, items_bytes,
+                                       self.side.cuda_stream), "items")
         # entry records for the backward (which derives the pair slots itself)
         rec = self.records.data_ptr() if backward else None
         chk(lib.oss_render_forward(n, 3, h, w, None, None, None, self.prec.data_ptr(), self.gid_sorted.data_ptr(),
@@ -250,11 +260,11 @@ class Pipeline:
         self._mark(4, timed)
         if not backward:
             return
-        chk(lib.oss_render_backward_pairs(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
+        torch.cuda.current_stream().wait_stream(self.side)
+        chk(lib.oss_render_backward_items(n, 3, h, w, self.geo.data_ptr(), d["rgb"].data_ptr(),
                                           d["opacity"].data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
                                           self.capacity, self.gid_sorted.data_ptr(), self.tile_offsets.data_ptr(),
-                                          rec, None, d["grad"].data_ptr(), self.scratch.data_ptr(),
-                                          self.scratch.data_ptr() + self.pg_bytes, self.scratch.numel() - self.pg_bytes,
+                                          rec, None, d["grad"].data_ptr(), self.scratch.data_ptr(), items, items_bytes,
                                           s), "backward_pairs")
         self._mark(5, timed)
         g = self.grads
@@ -294,7 +304,7 @@ class Pipeline:
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
         prepare = 2                                   # k_preprocess, k_prepare_scan (pair + tile offsets)
         binning = 2                                   # k_scatter_pairs, k_sort_tiles
-        bwd = 4                                       # k_item_block_sums, k_item_table, k_render_bwd, k_reduce_gaussian
+        bwd = 4                                       # k_item_block_sums, k_item_table (beside the forward), k_render_bwd, k_reduce_gaussian
         return prepare + binning + 1 + (bwd if backward else 0)
 
     def evaluations(self):

@@ -381,6 +381,50 @@ int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const 
     return OSS_OK;
 }
 
+int oss_backward_items(int64_t h, int64_t w, int64_t total_pairs, const int32_t* tile_offsets, void* items,
+                       int64_t items_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(0, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "backward item table too small");
+    if (total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && items != nullptr && aligned(items, 16), OSS_ERR_INVALID,
+              "tile_offsets and items (16-byte aligned) must be non-null");
+    OSS_CUDA_TRY(oss::launch_backward_items(g.h, g.w, total_pairs, tile_offsets, items, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                              const float* opacity, const int32_t* aabb, const int32_t* pair_offset,
+                              int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* records, const int32_t* slots, const float* grad_image, float* pairgrad,
+                              const void* items, int64_t items_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "backward item table too small");
+    if (g.n == 0 || total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
+              OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
+    OSS_CHECK(f == 0 || feat != nullptr, OSS_ERR_INVALID, "feat must be non-null");
+    OSS_CHECK(pairgrad != nullptr && aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CHECK(items != nullptr && aligned(items, 16), OSS_ERR_INVALID, "items must be 16-byte aligned");
+    OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
+              "lists and grad_image must be non-null");
+    OSS_CHECK(slots == nullptr || records != nullptr, OSS_ERR_INVALID, "slots come with records");
+    OSS_CHECK(records == nullptr || aligned(records, 16), OSS_ERR_INVALID, "records must be 16-byte aligned");
+    OSS_CUDA_TRY(oss::launch_render_backward_items(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, opacity,
+                                                   gid_sorted, tile_offsets, grad_image, aabb, pair_offset, records,
+                                                   slots, pairgrad, oss_pair_grad_stride(f), nullptr, nullptr, nullptr,
+                                                   items, as_stream(stream)));
+    return OSS_OK;
+}
+
 int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int32_t* pair_offset, const float* geo,
                           const float* feat, const float* opacity, const float* scale, const float* rot, float* d_xy,
                           float* d_conic, float* d_feat, float* d_opacity, float* d_scale, float* d_rot,

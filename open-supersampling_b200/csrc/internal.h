@@ -121,7 +121,17 @@ cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const f
 // (Sx, Sy, d_conic, dF) of pair_stride floats at pair_offset[g] + local tile
 // index, entries read from the forward's records/slots when records != null.
 // Atomic mode: adds into d_xy / d_conic / d_feat.  items_scratch holds the
-// work-item table (backward_items_scratch_bytes).
+// work-item table (backward_items_scratch_bytes): launch_render_backward_tiles
+// builds it and runs the backward; the two halves are also exposed so that the
+// table (which needs only tile_offsets) can be built beside the forward.
+cudaError_t launch_backward_items(int h, int w, int64_t total_pairs, const int32_t* tile_offsets, void* items_scratch,
+                                  cudaStream_t stream);
+cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pairs, const float* geo,
+                                         const float* feat, const float* opacity, const int32_t* gid_sorted,
+                                         const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
+                                         const int32_t* pair_offset, const float* records, const int32_t* slots,
+                                         float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
+                                         const void* items_scratch, cudaStream_t stream);
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo,
                                          const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image,

@@ -664,12 +664,8 @@ int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
 #define OSS_DISPATCH_FC(f, CALL) \
     ((f) <= 1 ? CALL(1) : (f) <= 3 ? CALL(3) : (f) <= 4 ? CALL(4) : (f) <= 8 ? CALL(8) : (f) <= 16 ? CALL(16) : (f) <= 32 ? CALL(32) : CALL(64))
 
-cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo, const float* feat,
-                                         const float* opacity, const int32_t* gid_sorted,
-                                         const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
-                                         const int32_t* pair_offset, const float* records, const int32_t* slots,
-                                         float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
-                                         void* items_scratch, cudaStream_t stream) {
+cudaError_t launch_backward_items(int h, int w, int64_t total_pairs, const int32_t* tile_offsets, void* items_scratch,
+                                  cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
@@ -684,13 +680,42 @@ cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pair
                                                                                          block_items);
     k_item_table<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(num_tiles, tile_offsets,
                                                                                     block_items, items, num_items);
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pairs, const float* geo,
+                                         const float* feat, const float* opacity, const int32_t* gid_sorted,
+                                         const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
+                                         const int32_t* pair_offset, const float* records, const int32_t* slots,
+                                         float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
+                                         const void* items_scratch, cudaStream_t stream) {
+    const int ntx = static_cast<int>(div_up(w, kTile));
+    const int nty = static_cast<int>(div_up(h, kTile));
+    const int num_tiles = ntx * nty;
+    if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
+    const int64_t max_items = backward_max_items(total_pairs, num_tiles);
+    Arena arena{static_cast<char*>(const_cast<void*>(items_scratch)), backward_items_scratch_bytes(total_pairs, num_tiles),
+                0};
+    const int4* items = arena.take<int4>(max_items);
+    const int32_t* num_items = arena.take<int32_t>(1);
 #define OSS_BWD_CALL(FC)                                                                                          \
     launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items, grad_image,     \
                       aabb, pair_offset, records, slots, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
     return OSS_DISPATCH_FC(f, OSS_BWD_CALL);
 #undef OSS_BWD_CALL
+}
+
+cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo, const float* feat,
+                                         const float* opacity, const int32_t* gid_sorted,
+                                         const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
+                                         const int32_t* pair_offset, const float* records, const int32_t* slots,
+                                         float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
+                                         void* items_scratch, cudaStream_t stream) {
+    cudaError_t err = launch_backward_items(h, w, total_pairs, tile_offsets, items_scratch, stream);
+    if (err != cudaSuccess) return err;
+    return launch_render_backward_items(f, h, w, total_pairs, geo, feat, opacity, gid_sorted, tile_offsets, grad_image,
+                                        aabb, pair_offset, records, slots, pairgrad, pair_stride, d_xy, d_conic, d_feat,
+                                        items_scratch, stream);
 }
 
 cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,

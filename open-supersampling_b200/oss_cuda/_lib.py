@@ -57,6 +57,9 @@ SIGNATURES = {
          _i64, _p],
     ),
     "oss_pair_grad_stride": (ctypes.c_int, [_i64]),
+    "oss_backward_items": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _i64, _p]),
+    "oss_render_backward_items": (
+        ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_render_backward_pairs_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_render_backward_pairs": (
         ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),

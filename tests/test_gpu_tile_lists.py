@@ -244,6 +244,29 @@ def test_packed_records_and_derived_slots_bit_identical(cuda_device, f, dense):
         grads.append(outs)
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+    # the item table built on its own (another stream) + the table-driven backward
+    # write the same per-pair rows as oss_render_backward_pairs
+    stride = lib.oss_pair_grad_stride(f)
+    ib = lib.oss_render_backward_pairs_scratch_bytes(L.capacity, L.tiles)
+    total = int(L.total.item())
+    rows = []
+    for split in (False, True):
+        pg = torch.zeros((L.capacity, stride), device="cuda")
+        items = torch.empty((ib,), device="cuda", dtype=torch.uint8)
+        args = (n, f, h, w, L.geo.data_ptr(), feat.data_ptr(), opacity.data_ptr(), L.aabb.data_ptr(),
+                L.pair_offset.data_ptr(), L.capacity, L.gid.data_ptr(), L.tile_offsets.data_ptr(), recs[1].data_ptr(),
+                None, grad.data_ptr(), pg.data_ptr(), items.data_ptr(), ib)
+        if split:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            _lib.check(lib.oss_backward_items(h, w, L.capacity, L.tile_offsets.data_ptr(), items.data_ptr(), ib,
+                                              side.cuda_stream), "items")
+            torch.cuda.current_stream().wait_stream(side)
+            _lib.check(lib.oss_render_backward_items(*args, s_), "backward_items")
+        else:
+            _lib.check(lib.oss_render_backward_pairs(*args, s_), "backward_pairs")
+        rows.append(pg[:total])
+    assert torch.equal(rows[0], rows[1])
 
 
 def test_sync_free_path_replays_in_cuda_graph(cuda_device):
