@@ -60,14 +60,47 @@ __device__ __forceinline__ bool regular_scaled(float x, float y, float A, float 
     return regular_conic(x, y, -A, -0.5f * B, -D);
 }
 
-template <int FC, bool CHECK>
+// True when the entry's weight is exactly 0 at every pixel of the tile whose
+// pixel centres span [tx0, tx0 + 15] x [ty0, ty0 + 15]: the largest q' over
+// that rectangle (a concave quadratic for a regular conic, so on a corner or at
+// an edge's vertex) lies below -127, and ex2.approx.ftz flushes every 2^q' below
+// 2^-126 to 0.  The 1.0 margin covers the fp32 rounding of q'.  Such entries
+// add exact zeros, so the forward skips them; this is what the q = 208 lists of
+// the exact binning mode carry in their outer tiles.
+// Entry skipping pays off on long lists (the outer tiles of exact-mode lists);
+// tiles with shorter lists do not test for it.
+constexpr int kSkipMinList = 128;
+
+__device__ __forceinline__ bool entry_zero_in_tile(float x, float y, float A, float B, float D, float tx0,
+                                                   float ty0) {
+    if (!(A < 0.0f && D < 0.0f)) return false;
+    const float X0 = tx0 - x, X1 = X0 + static_cast<float>(kTile - 1);
+    const float Y0 = ty0 - y, Y1 = Y0 + static_cast<float>(kTile - 1);
+    if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return false;  // the centre is inside
+    const float h2d = __fdividef(-0.5f, D), h2a = __fdividef(-0.5f, A);  // only moves the probe points
+    float best = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const float X = e == 0 ? X0 : X1;  // edge dx = X: dy* = -B X / (2 D)
+        const float dy = fminf(fmaxf(B * X * h2d, Y0), Y1);
+        best = fmaxf(best, fmaf(X, fmaf(A, X, B * dy), D * dy * dy));
+        const float Y = e == 0 ? Y0 : Y1;  // edge dy = Y: dx* = -B Y / (2 A)
+        const float dx = fminf(fmaxf(B * Y * h2a, X0), X1);
+        best = fmaxf(best, fmaf(dx, fmaf(A, dx, B * Y), D * Y * Y));
+    }
+    return best < -127.0f;
+}
+
+template <int FC, bool CHECK, bool SKIP>
 __device__ __forceinline__ void fwd_batch(int cnt, const float4* __restrict__ s_geo, const float* __restrict__ s_df,
+                                          const unsigned char* __restrict__ s_skip,
                                           float fpx, const float (&fpy)[FwdCfg<FC>::PX],
                                           float (&acc)[FwdCfg<FC>::PX][FC]) {
     constexpr int PX = FwdCfg<FC>::PX;
     constexpr int S = FwdCfg<FC>::S;
 #pragma unroll 2
     for (int j = 0; j < cnt; ++j) {
+        if (SKIP && s_skip[j]) continue;  // exact zero at every pixel of the tile (same for every thread)
         const float4 g0 = s_geo[j];
         const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
         float r[S];
@@ -94,15 +127,17 @@ __device__ __forceinline__ void fwd_batch(int cnt, const float4* __restrict__ s_
 }
 
 // fwd_batch on pixel pairs: acc2[p][c] holds pixels 2p and 2p+1.
-template <int FC, bool CHECK>
+template <int FC, bool CHECK, bool SKIP>
 __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__ s_geo,
-                                             const float* __restrict__ s_df, float fpx,
+                                             const float* __restrict__ s_df,
+                                             const unsigned char* __restrict__ s_skip, float fpx,
                                              const float2 (&fpy2)[FwdCfg<FC>::PX / 2],
                                              float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
     constexpr int NP = FwdCfg<FC>::PX / 2;
     constexpr int S = FwdCfg<FC>::S;
 #pragma unroll 4
     for (int j = 0; j < cnt; ++j) {
+        if (SKIP && s_skip[j]) continue;  // exact zero at every pixel of the tile (same for every thread)
         const float4 g0 = s_geo[j];
         const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
         float r[S];
@@ -139,6 +174,36 @@ __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__
     }
 }
 
+// Batch loop with its per-pixel sign test only where a conic is irregular and
+// its entry skip only where some entry of the batch is zero over the tile.
+template <int FC>
+__device__ __forceinline__ void fwd_batch_pk_sel(bool regular, bool skip, int cnt, const float4* s_geo,
+                                                 const float* s_df, const unsigned char* s_skip, float fpx,
+                                                 const float2 (&fpy2)[FwdCfg<FC>::PX / 2],
+                                                 float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
+    if (regular) {
+        if (skip) fwd_batch_pk<FC, false, true>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+        else fwd_batch_pk<FC, false, false>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+    } else {
+        if (skip) fwd_batch_pk<FC, true, true>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+        else fwd_batch_pk<FC, true, false>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+    }
+}
+
+template <int FC>
+__device__ __forceinline__ void fwd_batch_sel(bool regular, bool skip, int cnt, const float4* s_geo,
+                                              const float* s_df, const unsigned char* s_skip, float fpx,
+                                              const float (&fpy)[FwdCfg<FC>::PX],
+                                              float (&acc)[FwdCfg<FC>::PX][FC]) {
+    if (regular) {
+        if (skip) fwd_batch<FC, false, true>(cnt, s_geo, s_df, s_skip, fpx, fpy, acc);
+        else fwd_batch<FC, false, false>(cnt, s_geo, s_df, s_skip, fpx, fpy, acc);
+    } else {
+        if (skip) fwd_batch<FC, true, true>(cnt, s_geo, s_df, s_skip, fpx, fpy, acc);
+        else fwd_batch<FC, true, false>(cnt, s_geo, s_df, s_skip, fpx, fpy, acc);
+    }
+}
+
 template <int FC>
 __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int W, int ntx,
                                                                 const float* __restrict__ geo,
@@ -159,6 +224,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
     constexpr int ROWSTEP = kTile / PX;
     __shared__ float4 s_geo[BATCH];
     __shared__ __align__(16) float s_df[BATCH * S];
+    __shared__ unsigned char s_skip[BATCH];
 
     const int tile = blockIdx.x;
     const int tx0 = (tile % ntx) * kTile;
@@ -192,6 +258,8 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
         const int cnt = min(BATCH, end - b);
         __syncthreads();  // the previous batch has been consumed
         bool regular = true;
+        bool skip_any = false;
+        const bool try_skip = end - start > kSkipMinList;  // the same for the whole CTA
         for (int j = threadIdx.x; j < cnt; j += NT) {
             const int g = gid_sorted[b + j];
             const int e = b + j;
@@ -204,7 +272,13 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
                 const float4 g0 = pr[0];
                 const float4 g1 = pr[1];
                 s_geo[j] = g0;
-                regular = regular && regular_scaled(g0.x, g0.y, g0.z, g0.w, g1.x);
+                const bool reg = regular_scaled(g0.x, g0.y, g0.z, g0.w, g1.x);
+                regular = regular && reg;
+                const bool sk = try_skip && reg &&
+                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, g1.x, static_cast<float>(tx0),
+                                                   static_cast<float>(ty0));
+                s_skip[j] = sk;
+                skip_any = skip_any || sk;
                 sdf4[0] = g1;
                 if (rec != nullptr) {
                     rec[0] = g0;
@@ -221,7 +295,13 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
                 const float4 g0 = gr[0];
                 const float4 g1 = gr[1];
                 s_geo[j] = g0;
-                regular = regular && regular_conic(g0.x, g0.y, g1.y, g1.z, g1.w);
+                const bool reg = regular_conic(g0.x, g0.y, g1.y, g1.z, g1.w);
+                regular = regular && reg;
+                const bool sk = try_skip && reg &&
+                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, g1.x, static_cast<float>(tx0),
+                                                   static_cast<float>(ty0));
+                s_skip[j] = sk;
+                skip_any = skip_any || sk;
                 const float op = opacity != nullptr ? opacity[g] : 1.0f;
                 float* df = s_df + j * S;
                 df[0] = g1.x;
@@ -242,18 +322,11 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
             }
         }
         const bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
+        const bool any_skip = try_skip && __syncthreads_or(skip_any ? 1 : 0) != 0;
         if constexpr (PK) {
-            if (all_regular) {
-                fwd_batch_pk<FC, false>(cnt, s_geo, s_df, fpx, fpy2, acc2);
-            } else {
-                fwd_batch_pk<FC, true>(cnt, s_geo, s_df, fpx, fpy2, acc2);
-            }
+            fwd_batch_pk_sel<FC>(all_regular, any_skip, cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
         } else {
-            if (all_regular) {
-                fwd_batch<FC, false>(cnt, s_geo, s_df, fpx, fpy, acc);
-            } else {
-                fwd_batch<FC, true>(cnt, s_geo, s_df, fpx, fpy, acc);
-            }
+            fwd_batch_sel<FC>(all_regular, any_skip, cnt, s_geo, s_df, s_skip, fpx, fpy, acc);
         }
     }
     if constexpr (PK) {
@@ -320,6 +393,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
     constexpr int NP = PX / 2;
     __shared__ float4 s_geo[2][PB];
     __shared__ __align__(16) float s_df[2][PB * S];
+    __shared__ unsigned char s_skip[2][PB];
 
     const int G = gridDim.x;
     const int lx = threadIdx.x & (kTile - 1);
@@ -408,13 +482,21 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         cp_async_wait_one();
         const int n0 = min(PB, cur1 - cur0);
         bool regular = true;
+        bool skip_any = false;
+        const bool try_skip = cur1 - cur0 > kSkipMinList;  // the same for the whole CTA
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
             const int j = threadIdx.x + k * NT;
             if (j < n0) {
                 const float4 g0 = s_geo[buf][j];
                 const float4* d4 = reinterpret_cast<const float4*>(&s_df[buf][j * S]);
-                regular = regular && regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                const bool reg = regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                regular = regular && reg;
+                const bool sk = try_skip && reg &&
+                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
+                                                   static_cast<float>(ty0));
+                s_skip[buf][j] = sk;
+                skip_any = skip_any || sk;
                 if (records != nullptr) {
                     float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(cur0 + j) * RS);
                     rec[0] = g0;
@@ -424,16 +506,14 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
             }
         }
         bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
-        if (all_regular) {
-            fwd_batch_pk<FC, false>(n0, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
-        } else {
-            fwd_batch_pk<FC, true>(n0, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
-        }
+        bool any_skip = try_skip && __syncthreads_or(skip_any ? 1 : 0) != 0;
+        fwd_batch_pk_sel<FC>(all_regular, any_skip, n0, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2);
         // 4. later batches of a long list, staged in place
         for (int b = cur0 + PB; b < cur1; b += PB) {
             const int cnt = min(PB, cur1 - b);
             __syncthreads();  // the previous batch has been consumed
             bool reg = true;
+            bool skp = false;
             for (int j = threadIdx.x; j < cnt; j += NT) {
                 const int e = b + j;
                 const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(gid_sorted[e]) * RS);
@@ -442,7 +522,13 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 float4* d4 = reinterpret_cast<float4*>(&s_df[buf][j * S]);
 #pragma unroll
                 for (int v = 0; v < S / 4; ++v) d4[v] = pr[1 + v];
-                reg = reg && regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                const bool rg = regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
+                reg = reg && rg;
+                const bool sk = try_skip && rg &&
+                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
+                                                   static_cast<float>(ty0));
+                s_skip[buf][j] = sk;
+                skp = skp || sk;
                 if (records != nullptr) {
                     float4* rec = reinterpret_cast<float4*>(records + static_cast<int64_t>(e) * RS);
                     rec[0] = g0;
@@ -451,11 +537,8 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 }
             }
             all_regular = __syncthreads_and(reg ? 1 : 0) != 0;
-            if (all_regular) {
-                fwd_batch_pk<FC, false>(cnt, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
-            } else {
-                fwd_batch_pk<FC, true>(cnt, s_geo[buf], s_df[buf], fpx, fpy2, acc2);
-            }
+            any_skip = try_skip && __syncthreads_or(skp ? 1 : 0) != 0;
+            fwd_batch_pk_sel<FC>(all_regular, any_skip, cnt, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2);
         }
         // 5. image
         const int px = tx0 + lx;
