@@ -25,9 +25,11 @@
  * Binning modes (oss_bin_mode):
  *   OSS_BIN_TIGHT3SIGMA  tile AABB of the q = 9 ellipse (the reference's
  *                        pair_construction_only lists, rasterizer_fwd.cu:74-108)
- *   OSS_BIN_EXACT        tile AABB of the q = 208 ellipse: every pixel outside
- *                        the lists has exp(-q/2) == 0 in fp32, so images equal the
- *                        reference's full-tail sum (rasterizer.py:294-300)
+ *   OSS_BIN_EXACT        tile AABB of the q = 176 ellipse: every pixel outside
+ *                        the lists has exp(-q/2) below the smallest normal fp32 (0
+ *                        under flush-to-zero), so images equal the reference's
+ *                        full-tail sum (rasterizer.py:294-300) to within 1.2e-38
+ *                        per Gaussian
  *   OSS_BIN_FULL         every Gaussian in every tile (the reference forward's
  *                        build_full_tile_pairs, rasterizer_fwd.cu:135-149)
  */

@@ -12,9 +12,13 @@ constexpr int kTile = OSS_TILE;          // tile edge in pixels
 constexpr int kTilePixels = kTile * kTile;
 constexpr float kMinScale = 1.0e-6f;     // rasterizer_fwd.cu common.cuh:15
 constexpr float kTauTight = 9.0f;        // rasterizer_fwd.cu:92
-// exp(-q/2) rounds to 0 in IEEE fp32 for q > 2*150*ln2 = 207.94; 208 keeps a
-// 3e-4 relative margin over fp32 rounding of q and of the AABB radius.
-constexpr float kTauExact = 208.0f;
+// Exact-mode cutoff.  For q > 2*126*ln2 = 174.67, 2^(-q/2 log2 e) is below
+// 2^-126, the smallest normal fp32: the kernels' ex2.approx.ftz returns exactly
+// 0 there (as does any flush-to-zero evaluation, such as the reference CUDA
+// op's -ftz=true build), and an evaluation with subnormals gets at most
+// 1.2e-38 per Gaussian.  176 keeps a 0.8% margin over fp32 rounding of q and of
+// the AABB radius.
+constexpr float kTauExact = 176.0f;
 // -0.5*log2(e): folds exp(-q/2) = 2^(q * -0.5 log2 e) into the conic.
 constexpr float kNegHalfLog2e = -0.72134752044448170368f;
 
@@ -151,7 +155,7 @@ __host__ __device__ inline float mode_tau(int mode) { return mode == OSS_BIN_EXA
 // Fallback radius factor for degenerate conics: 3*max(s) for the 3-sigma lists
 // (rasterizer_fwd.cu:96), sqrt(tau)*max(s) for the exact lists.
 __host__ __device__ inline float mode_fallback(int mode) {
-    return mode == OSS_BIN_EXACT ? 14.422205101855956f : 3.0f;
+    return mode == OSS_BIN_EXACT ? 13.266499161421599f : 3.0f;
 }
 
 }  // namespace oss

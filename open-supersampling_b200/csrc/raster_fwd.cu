@@ -65,7 +65,7 @@ __device__ __forceinline__ bool regular_scaled(float x, float y, float A, float 
 // that rectangle (a concave quadratic for a regular conic, so on a corner or at
 // an edge's vertex) lies below -127, and ex2.approx.ftz flushes every 2^q' below
 // 2^-126 to 0.  The 1.0 margin covers the fp32 rounding of q'.  Such entries
-// add exact zeros, so the forward skips them; this is what the q = 208 lists of
+// add exact zeros, so the forward skips them; this is what the q = 176 lists of
 // the exact binning mode carry in their outer tiles.
 // Entry skipping pays off on long lists (the outer tiles of exact-mode lists);
 // tiles with shorter lists do not test for it.

@@ -26,7 +26,7 @@
 #define ORC_TILE 16
 #define ORC_MIN_SCALE 1.0e-6f
 #define ORC_TAU_TIGHT 9.0f
-#define ORC_TAU_EXACT 208.0f
+#define ORC_TAU_EXACT 176.0f
 
 enum { ORC_TIGHT = 0, ORC_EXACT = 1, ORC_FULL = 2 };
 
@@ -59,8 +59,9 @@ static void conic_of(float raw_sx, float raw_sy, float angle, float* a, float* b
 
 /*
  * preprocess_gaussians, rasterizer_fwd.cu:38-109.  mode ORC_TIGHT uses tau = 9
- * and the 3*max(scale) fallback (the reference); ORC_EXACT uses tau = 208
- * (exp(-q/2) == 0 in fp32 outside) and sqrt(208)*max(scale); ORC_FULL
+ * and the 3*max(scale) fallback (the reference); ORC_EXACT uses tau = 176
+ * (exp(-q/2) below the smallest normal fp32 outside) and sqrt(176)*max(scale);
+ * ORC_FULL
  * writes the full-frame rectangle for every Gaussian.
  */
 void orc_preprocess(int64_t n, int h, int w, int mode, const float* xy, const float* scale, const float* rot,
@@ -68,7 +69,7 @@ void orc_preprocess(int64_t n, int h, int w, int mode, const float* xy, const fl
     const int ntx = num_tiles_1d(w);
     const int nty = num_tiles_1d(h);
     const float tau = mode == ORC_EXACT ? ORC_TAU_EXACT : ORC_TAU_TIGHT;
-    const float fb = mode == ORC_EXACT ? 14.422205101855956f : 3.0f;
+    const float fb = mode == ORC_EXACT ? 13.266499161421599f : 3.0f;
 #pragma omp parallel for schedule(static)
     for (int64_t g = 0; g < n; ++g) {
         float a, b, d;
