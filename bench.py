@@ -555,7 +555,22 @@ def run_ours(args, rank, world, local):
     fwd_ms = float(total_ms[1]) / K
     pixels = h * w * world
     value = pixels / (step_ms * 1e-3) / 1e6
-    del graphs
+
+    # self-check: the timed graph computes the public API's results bit for bit
+    graphs["fwdbwd"].replay()
+    torch.cuda.synchronize()
+    leaves = [dev_inp[k].detach().clone().requires_grad_(True) for k in ("xy", "scale", "rot", "rgb", "opacity")]
+    api_img = rasterize_gaussians(leaves[0], leaves[1], leaves[2], leaves[3], h, w, binning=args.binning,
+                                  opacity=leaves[4])
+    api_grads = torch.autograd.grad(api_img, leaves, dev_inp["grad"])
+    g = pipe.grads
+    selfcheck = {
+        "image_bitwise_equal": bool(torch.equal(api_img.detach(), pipe.image)),
+        "grads_bitwise_equal": all(bool(torch.equal(a, b)) for a, b in zip(
+            api_grads, (g["d_xy"], g["d_scale"], g["d_rot"], g["d_rgb"], g["d_opacity"]))),
+        "against": "oss_cuda.rasterize_gaussians + torch.autograd.grad on the same device inputs",
+    }
+    del graphs, leaves, api_img, api_grads
 
     # roofline of the dominant kernel (FP32 SIMT; no tensor cores on this path)
     evals = pipe.evaluations()
@@ -605,7 +620,7 @@ def run_ours(args, rank, world, local):
         "fwd_mpix_s": pixels / (fwd_ms * 1e-3) / 1e6, "fwd_ms_per_frame": fwd_ms, "fwdbwd_ms_per_frame": step_ms,
         "timing": "CUDA-graph replay of the sync-free step (C ABI calls captured once); stages_ms from eager "
                   f"steps with an event between stages ({ks} steps)",
-        "stages_ms": stage_avg, "roofline": roofline, "hbm_stages": hbm,
+        "stages_ms": stage_avg, "roofline": roofline, "hbm_stages": hbm, "selfcheck": selfcheck,
         "gpu_launches": (pipe.launches_per_step() + pipe.launches_per_step(backward=False)) * K,
         "clocks": clocks.summary(), "wall_s": wall,
     }
