@@ -40,6 +40,7 @@ struct AlphaCfg {
     static constexpr int S = ((2 + FC + 3) / 4) * 4;              // [D, opacity, feat...] floats
     static constexpr int BATCH = S <= 8 ? 128 : (S <= 20 ? 64 : (S <= 36 ? 32 : 16));
     static constexpr int NV = 6 + FC;                             // Sx Sy Sxx Sxy Syy dOp dF[FC]
+    static_assert((2 + FC) % 4 != 0, "the record's last float must be padding (it holds the alpha cut)");
 };
 
 // Stage list entries [b, b + cnt) of a tile: geometry (x, y, A, B) and the
@@ -60,6 +61,10 @@ __device__ __forceinline__ void stage_alpha(int b, int cnt, int F, const float* 
         const float* fg = feat + static_cast<int64_t>(g) * F;
 #pragma unroll
         for (int c = 0; c < S - 2; ++c) r[2 + c] = c < F && c < FC ? fg[c] : 0.0f;
+        // r[S - 1] (always padding: 2 + FC is never a multiple of 4) = the q' below which
+        // alpha = opacity * 2^q' is clearly under 1/255, with a 1e-3 margin (0.07% in
+        // alpha): pixels below it are skipped before the exact test
+        r[S - 1] = -log2f(255.0f * r[1]) - 1.0e-3f;
         if (s_gid != nullptr) s_gid[j] = g;
     }
 }
@@ -121,10 +126,13 @@ __global__ void __launch_bounds__(AlphaCfg<FC>::NT) k_render_alpha_fwd(
             const float bdx = g0.w * dx;
             const float adx2 = (g0.z * dx) * dx;
 #pragma unroll
+            const float qmin = r[S - 1];
+#pragma unroll
             for (int k = 0; k < PX; ++k) {
                 if (!live[k]) continue;
                 const float dy = fpy[k] - g0.y;
                 const float q = fmaf(dy, fmaf(D, dy, bdx), adx2);
+                if (q < qmin) continue;      // alpha clearly below 1/255
                 if (!(q <= 0.0f)) continue;  // q' > 0 or NaN: weight 0
                 const float a = fminf(op * ex2_ftz(q), kAlphaMax);
                 if (a < kAlphaMin) continue;
@@ -266,6 +274,7 @@ __global__ void __launch_bounds__(AlphaCfg<FC>::NT) k_render_alpha_bwd(
                 if (j >= nc[k]) continue;
                 const float dy = fpy[k] - g0.y;
                 const float q = fmaf(dy, fmaf(D, dy, bdx), adx2);
+                if (q < r[S - 1]) continue;  // alpha clearly below 1/255
                 if (!(q <= 0.0f)) continue;
                 const float G = ex2_ftz(q);
                 const float og = op * G;
