@@ -125,7 +125,6 @@ __global__ void __launch_bounds__(AlphaCfg<FC>::NT) k_render_alpha_fwd(
             const float dx = fpx - g0.x;
             const float bdx = g0.w * dx;
             const float adx2 = (g0.z * dx) * dx;
-#pragma unroll
             const float qmin = r[S - 1];
 #pragma unroll
             for (int k = 0; k < PX; ++k) {
