@@ -13,13 +13,13 @@ oss/sr/v6/model.py:795-820 on the rasterized canvas.
 """
 from __future__ import annotations
 
-import math
 from typing import Tuple
 
 import torch
 import torch.nn as nn
 
 from oss_cuda import rasterize_gaussians
+from oss_cuda.overlap import cosine_ramp, phase_feather_mask, render_overlapped_with  # noqa: F401
 
 TILE_SIZE = 16
 _MIN_PIXEL_SCALE = 1.0e-3
@@ -32,43 +32,13 @@ def render(xy, scale, rot, feat, h, w, binning=None, opacity=None):
                                binning=binning, opacity=opacity)
 
 
-def cosine_ramp(t: torch.Tensor) -> torch.Tensor:
-    return 0.5 - 0.5 * torch.cos(t * math.pi)
-
-
-def phase_feather_mask(h: int, w: int, origin: Tuple[int, int], overlap: int, device) -> torch.Tensor:
-    """Weight of one phase-shifted render: a cosine ramp over the distance to the
-    nearest tile edge of that phase's grid (rasterizer.py:212-234)."""
-    if overlap <= 0:
-        return torch.ones((1, h, w), device=device, dtype=torch.float32)
-    tile = float(TILE_SIZE)
-    oy, ox = float(origin[0]), float(origin[1])
-    py = torch.remainder(torch.arange(h, device=device, dtype=torch.float32) + 0.5 - oy, tile)
-    px = torch.remainder(torch.arange(w, device=device, dtype=torch.float32) + 0.5 - ox, tile)
-    wy = cosine_ramp((torch.minimum(py, tile - py) / float(overlap)).clamp(0.0, 1.0))
-    wx = cosine_ramp((torch.minimum(px, tile - px) / float(overlap)).clamp(0.0, 1.0))
-    return (wy.view(1, h, 1) * wx.view(1, 1, w)).to(torch.float32)
-
-
 def render_overlapped(xy, scale, rot, feat, h, w, overlap, binning=None, opacity=None):
-    """Feathered overlapping-tile render (rasterizer.py:159-210): four renders whose
-    16-px tile grids are shifted by (0|-o, 0|-o), each cropped back to (h, w) and
-    blended by its feather mask, then normalised by the mask sum."""
-    device = xy.device
-    f = int(feat.shape[1])
-    accum = torch.zeros((f, h, w), device=device, dtype=torch.float32)
-    wsum = torch.zeros((1, h, w), device=device, dtype=torch.float32)
-    for oy, ox in ((0, 0), (-overlap, 0), (0, -overlap), (-overlap, -overlap)):
-        crop_h = -(-(h - min(oy, 0)) // TILE_SIZE) * TILE_SIZE
-        crop_w = -(-(w - min(ox, 0)) // TILE_SIZE) * TILE_SIZE
-        shift = torch.tensor([float(ox), float(oy)], device=device, dtype=xy.dtype)
-        img = render(xy - shift, scale, rot, feat, crop_h, crop_w, binning, opacity)
-        ys, xs = -min(oy, 0), -min(ox, 0)
-        img = img[:, ys:ys + h, xs:xs + w]
-        mask = phase_feather_mask(h, w, (oy, ox), overlap, device)
-        accum = accum + img * mask
-        wsum = wsum + mask
-    return accum / wsum.clamp_min(1.0e-6)
+    """Feathered overlapping-tile render (rasterizer.py:159-210) through `render`:
+    four renders whose 16-px tile grids are shifted by (0|-o, 0|-o), each cropped
+    back to (h, w) and blended by its feather mask, then normalised by the mask
+    sum (oss_cuda.overlap)."""
+    return render_overlapped_with(lambda x, s, r, f, hh, ww: render(x, s, r, f, hh, ww, binning, opacity),
+                                  xy, scale, rot, feat, h, w, overlap)
 
 
 class V6Rasterizer(nn.Module):

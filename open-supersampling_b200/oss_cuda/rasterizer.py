@@ -117,13 +117,36 @@ class _RasterizeGaussiansAlpha(Function):
 
 
 def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True, *, binning=None, opacity=None,
-                        blend="sum", depth=None, background=None, pair_capacity=None):
+                        blend="sum", depth=None, background=None, pair_capacity=None, overlap=0,
+                        phase_offset=(0, 0)):
     """Render (F, H, W) on the GPU, differentiably: sum_g feat[g] * exp(-q_g / 2)
     (blend="sum", the reference op) or front-to-back compositing (blend="alpha").
 
-    Reference: oss/cuda/oss_cuda/rasterizer.py:68-70.
+    Reference: oss/cuda/oss_cuda/rasterizer.py:68-70.  The keywords add the
+    build's options; left at their defaults they do not change the result:
+    binning (tile lists), opacity (folded in the kernel), blend / depth /
+    background (alpha compositing), pair_capacity (no host sync), overlap (the
+    4-phase feathered overlapping-tile render of oss/sr/v6/rasterizer.py:159-242,
+    blend="sum") and phase_offset = (dx, dy) integer pixels added to every mean
+    before rendering (the per-frame spawner offset, oss/sr/v6/model.py:795-820).
     """
     h, w, tile_size = int(h), int(w), int(tile_size)
+    dx, dy = (int(v) for v in phase_offset)
+    if dx or dy:
+        xy = xy + torch.tensor([float(dx), float(dy)], device=xy.device, dtype=xy.dtype)
+    overlap = int(overlap)
+    if overlap < 0:
+        raise ValueError(f"overlap must be >= 0; got {overlap}")
+    if overlap > 0:
+        if blend != "sum":
+            raise ValueError("overlap applies to blend='sum' only")
+        from .overlap import render_overlapped_with
+
+        def one(x, s, r, f, hh, ww):
+            return rasterize_gaussians(x, s, r, f, hh, ww, tile_size, topk_norm, binning=binning, opacity=opacity,
+                                       pair_capacity=pair_capacity)
+
+        return render_overlapped_with(one, xy, scale, rot, feat, h, w, overlap)
     _raster.check_gaussians(xy, scale, rot, feat)
     _raster.check_hw(h, w, tile_size)
     if opacity is not None:
@@ -148,3 +171,25 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
             raise RuntimeError("depth must be (N,)")
     return _RasterizeGaussiansAlpha.apply(xy, scale, rot, feat, opacity, depth, background, h, w, mode,
                                           pair_capacity)
+
+
+def rasterize_gaussians_batched(xy, scale, rot, feat, offsets, h, w, tile_size=16, topk_norm=True, **kwargs):
+    """B frames in one call, frame b drawn from Gaussians [offsets[b], offsets[b+1])
+    of the concatenated inputs: (B, F, H, W), differentiable like
+    rasterize_gaussians (keywords as there; opacity and depth are per Gaussian of
+    the concatenation).  offsets is a host sequence or CPU tensor of B+1
+    non-decreasing ints from 0 to N."""
+    offs = [int(v) for v in (offsets.tolist() if torch.is_tensor(offsets) else offsets)]
+    n = int(xy.size(0))
+    if len(offs) < 1 or offs[0] != 0 or offs[-1] != n or any(b < a for a, b in zip(offs, offs[1:])):
+        raise ValueError("offsets must be non-decreasing from 0 to N")
+    per_g = {k: kwargs.pop(k) for k in ("opacity", "depth") if kwargs.get(k) is not None}
+    frames = []
+    for a, b in zip(offs, offs[1:]):
+        kw = dict(kwargs)
+        kw.update({k: v[a:b] for k, v in per_g.items()})
+        frames.append(rasterize_gaussians(xy[a:b], scale[a:b], rot[a:b], feat[a:b], h, w, tile_size, topk_norm,
+                                          **kw))
+    if not frames:
+        return torch.zeros((0, int(feat.size(1)), int(h), int(w)), device=xy.device, dtype=torch.float32)
+    return torch.stack(frames, 0)

@@ -1,0 +1,119 @@
+"""The build-added surface of the drop-in package: rasterize_gaussians'
+overlap / phase_offset keywords, rasterize_gaussians_batched and
+warp_canvas_cuda, each checked bit for bit against the composition it stands
+for (whose parity the other GPU tests pin against the oracle)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _gaussians(n, h, w, f, seed):
+    rng = np.random.default_rng(seed)
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    scale = np.exp(rng.standard_normal((n, 2)) * 0.3 + math.log(2.0)).astype(np.float32)
+    rot = (rng.random(n) * math.pi).astype(np.float32)
+    feat = rng.random((n, f)).astype(np.float32)
+    opacity = (1.0 / (1.0 + np.exp(-rng.standard_normal(n)))).astype(np.float32)
+    return [torch.from_numpy(a).cuda() for a in (xy, scale, rot, feat, opacity)]
+
+
+def _leaves(ts):
+    return [t.detach().clone().requires_grad_(True) for t in ts]
+
+
+@pytest.mark.parametrize("binning", ["tight3sigma", "exact"])
+def test_batched_equals_per_frame_calls(cuda_device, binning):
+    from oss_cuda import rasterize_gaussians, rasterize_gaussians_batched
+
+    h, w = 80, 112
+    sizes = [300, 0, 517, 64]
+    offs = [0]
+    for s in sizes:
+        offs.append(offs[-1] + s)
+    xy, scale, rot, feat, op = _gaussians(offs[-1], h, w, 3, 3)
+    grad = torch.randn((len(sizes), 3, h, w), device="cuda")
+    a = _leaves((xy, scale, rot, feat, op))
+    img = rasterize_gaussians_batched(a[0], a[1], a[2], a[3], offs, h, w, binning=binning, opacity=a[4])
+    assert img.shape == (len(sizes), 3, h, w)
+    img.backward(grad)
+    b = _leaves((xy, scale, rot, feat, op))
+    for i, (lo, hi) in enumerate(zip(offs, offs[1:])):
+        one = rasterize_gaussians(b[0][lo:hi], b[1][lo:hi], b[2][lo:hi], b[3][lo:hi], h, w, binning=binning,
+                                  opacity=b[4][lo:hi])
+        assert torch.equal(one.detach(), img[i].detach())
+        one.backward(grad[i])
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)
+
+
+def test_batched_rejects_bad_offsets(cuda_device):
+    from oss_cuda import rasterize_gaussians_batched
+
+    xy, scale, rot, feat, _ = _gaussians(10, 32, 32, 3, 1)
+    for offs in ([0, 5], [1, 10], [0, 6, 4, 10]):
+        with pytest.raises(ValueError):
+            rasterize_gaussians_batched(xy, scale, rot, feat, offs, 32, 32)
+
+
+def test_phase_offset_is_a_shift_of_the_means(cuda_device):
+    from oss_cuda import rasterize_gaussians
+
+    h, w = 64, 96
+    xy, scale, rot, feat, op = _gaussians(700, h, w, 3, 5)
+    a = _leaves((xy, scale, rot, feat))
+    img = rasterize_gaussians(*a, h, w, binning="tight3sigma", phase_offset=(5, -3))
+    img.sum().backward()
+    b = _leaves((xy, scale, rot, feat))
+    ref = rasterize_gaussians(b[0] + torch.tensor([5.0, -3.0], device="cuda"), b[1], b[2], b[3], h, w,
+                              binning="tight3sigma")
+    ref.sum().backward()
+    assert torch.equal(img.detach(), ref.detach())
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)
+
+
+def test_overlap_keyword_is_the_feathered_render(cuda_device):
+    from oss_b200 import render_overlapped
+    from oss_cuda import rasterize_gaussians
+
+    h, w = 70, 90
+    xy, scale, rot, feat, op = _gaussians(600, h, w, 4, 7)
+    a = _leaves((xy, scale, rot, feat))
+    img = rasterize_gaussians(*a, h, w, binning="tight3sigma", overlap=4)
+    img.sum().backward()
+    b = _leaves((xy, scale, rot, feat))
+    ref = render_overlapped(*b, h, w, 4, "tight3sigma")  # scales are far above its 1e-3 floor
+    ref.sum().backward()
+    assert torch.equal(img.detach(), ref.detach())
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)
+    with pytest.raises(ValueError):
+        rasterize_gaussians(*a, h, w, overlap=-1)
+    with pytest.raises(ValueError):
+        rasterize_gaussians(*a, h, w, overlap=4, blend="alpha", opacity=op)
+
+
+def test_warp_canvas_cuda_is_the_canvas_warp(cuda_device):
+    from oss_b200 import CanvasState, warp_canvas
+    from oss_cuda import warp_canvas_cuda
+
+    n, h, w = 500, 96, 128
+    g = torch.Generator(device="cuda").manual_seed(9)
+    canvas = CanvasState(torch.rand((n, 2), device="cuda", generator=g) * torch.tensor([w, h], device="cuda"),
+                         torch.rand((n, 2), device="cuda", generator=g) + 0.5,
+                         torch.rand((n,), device="cuda", generator=g) * 3.0,
+                         torch.rand((n,), device="cuda", generator=g),
+                         torch.rand((n, 3), device="cuda", generator=g), count=n)
+    motion = (torch.rand((1, 2, h // 2, w // 2), device="cuda", generator=g) - 0.5) * 8.0
+    a = warp_canvas_cuda(canvas, motion, (h, w), sigma_recon=0.5, alpha=0.5)
+    b = warp_canvas(canvas, motion, (h, w), sigma_recon=0.5, alpha=0.5)
+    assert a.count == b.count
+    for x, y in zip((a.positions, a.scales, a.rotations, a.opacities, a.colors),
+                    (b.positions, b.scales, b.rotations, b.opacities, b.colors)):
+        assert torch.equal(x, y)
