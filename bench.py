@@ -896,16 +896,26 @@ def run_config5(args, rank, world):
     ar_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     sl = slice(n_own, n_own + n_shared)
 
+    # size the pair capacity over every frame (host reads of the totals), then capture one
+    # sync-free CUDA graph per frame; a step replays them, accumulating the shared canvas's
+    # gradients, and all-reduces those once
+    for d in per_frame:
+        pipe.step(d, sync=True, timed=False)
+    torch.cuda.synchronize()
+    graphs = [pipe.capture(d) for d in per_frame]
+
     def step():
         d_shared.zero_()
-        for d in per_frame:
-            pipe.step(d, sync=True)
+        for g in graphs:
+            g.replay()
             d_shared.add_(pack_shared_grads(pipe.grads, sl))
         ar_events[0].record()
         reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
         ar_events[1].record()
 
     ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    pipe.check_overflow()
+    del graphs
     allreduce = None
     if world > 1:
         torch.cuda.synchronize()
