@@ -224,7 +224,9 @@ OSS_API int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w
  * oss_render_backward_pairs_scratch_bytes(total_pairs, num_tiles) bytes).  It
  * reads only tile_offsets, so it can be built on another stream while the
  * forward runs; oss_render_backward_items then runs the per-pair backward over
- * that table (oss_render_backward_pairs = both, in order). */
+ * that table (oss_render_backward_pairs = both, in order).  The table holds the
+ * backward's work counter: the backward takes items through it and leaves it
+ * cleared, so a table serves any number of backward launches, one at a time. */
 OSS_API int oss_backward_items(int64_t h, int64_t w, int64_t total_pairs, const int32_t* tile_offsets,
                        void* items, int64_t items_bytes, void* stream);
 OSS_API int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w,
@@ -233,7 +235,7 @@ OSS_API int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w
                               const int32_t* gid_sorted, const int32_t* tile_offsets,
                               const float* records, const int32_t* slots,
                               const float* grad_image, float* pairgrad,
-                              const void* items, int64_t items_bytes, void* stream);
+                              void* items, int64_t items_bytes, void* stream);
 OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
                           const int32_t* pair_offset, const float* geo,
                           const float* feat, const float* opacity,

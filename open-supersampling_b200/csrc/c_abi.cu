@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 6; }
+int oss_abi_version(void) { return 7; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -400,7 +400,7 @@ int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w, const 
                               const float* opacity, const int32_t* aabb, const int32_t* pair_offset,
                               int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
                               const float* records, const int32_t* slots, const float* grad_image, float* pairgrad,
-                              const void* items, int64_t items_bytes, void* stream) {
+                              void* items, int64_t items_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;

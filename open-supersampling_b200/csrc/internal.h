@@ -131,7 +131,7 @@ cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pair
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
                                          const int32_t* pair_offset, const float* records, const int32_t* slots,
                                          float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
-                                         const void* items_scratch, cudaStream_t stream);
+                                         void* items_scratch, cudaStream_t stream);
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo,
                                          const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image,

@@ -1,12 +1,13 @@
 // Backward of the additive tile render (the reference's rasterize_backward,
 // rasterizer_bwd.cu:32-113), re-organised so that no per-pixel atomics remain.
 //
-// Work is cut into items: up to 32 list entries of one tile, listed in an item
-// table (tile, first entry, count) built by one small kernel.  One warp runs one
-// item.  It stages the tile's dL/dimage block into its own shared-memory slot
-// (rows padded so that lanes on different rows hit different banks), then each
-// lane owns one list entry and walks the tile's pixels, keeping the per-pair
-// sums in registers:
+// Work is cut into items: up to 32 list entries of one tile, listed longest
+// first in an item table (tile, first entry, count) built by two small kernels.
+// The kernel's warps are persistent and take items one at a time through a
+// counter.  For each item a warp stages the tile's dL/dimage block into its own
+// shared-memory slot (rows padded so that lanes on different rows hit different
+// banks), then each lane owns one list entry and walks the tile's pixels,
+// keeping the per-pair sums in registers:
 //   g = w * sum_c go_c f'_c      (w = exp(-q/2), dL/dq = -g/2)
 //   Sx = sum g dx, Sy = sum g dy, Sxx = sum g dx^2, Sxy = sum g dx dy,
 //   Syy = sum g dy^2, dF_c = sum w go_c
@@ -235,205 +236,238 @@ __device__ __forceinline__ float group_sum(float v, int k) {
 // Entry sources and pair-gradient sinks of the backward kernel.
 enum BwdMode { kAtomicGather = 0, kDetGather = 1, kDetRecords = 2 };
 
+// Persistent warps: warp i of the grid runs item i first, then takes further
+// items (from index warps-in-grid on) through a shared counter, so a warp that
+// finishes a short item starts the next one at once instead of idling until the
+// other warps of its CTA are done, and the table's longest-first order leaves
+// only short items for the end of the launch.  A warp whose first item exists
+// takes one index past the end before it leaves, so a launch increments the
+// counter exactly num_items times, and atomicInc's wrap limit (num_items - 1)
+// puts it back to 0 for the next launch.
+__device__ __forceinline__ int take_item(uint32_t* work, uint32_t limit, int base, int lane) {
+    uint32_t v = 0;
+    if (lane == 0) v = atomicInc(work, limit);
+    return base + static_cast<int>(__shfl_sync(0xffffffffu, v, 0));
+}
+
 template <int FC, int MODE>
 __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
     const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted, const int4* __restrict__ items,
-    const int32_t* __restrict__ num_items, const float* __restrict__ grad_image, const int4* __restrict__ aabb,
-    const int32_t* __restrict__ pair_offset, const float* __restrict__ records, const int32_t* __restrict__ slots,
-    float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy, float* __restrict__ d_conic,
-    float* __restrict__ d_feat) {
+    const int32_t* __restrict__ num_items, uint32_t* __restrict__ work, const float* __restrict__ grad_image,
+    const int4* __restrict__ aabb, const int32_t* __restrict__ pair_offset, const float* __restrict__ records,
+    const int32_t* __restrict__ slots, float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy,
+    float* __restrict__ d_conic, float* __restrict__ d_feat) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int RS = 4 + ((1 + FC + 3) / 4) * 4;  // entry record floats (the forward's layout)
     extern __shared__ float4 s_mem4[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x * BwdCfg<FC>::WARPS + warp;
-    if (item >= *num_items) return;  // uniform per warp
     float* s_go = reinterpret_cast<float*>(s_mem4) + warp * BwdCfg<FC>::SLOT;
+    const int n_items = *num_items;
+    const uint32_t limit = static_cast<uint32_t>(n_items) - 1u;
+    const int grid_warps = static_cast<int>(gridDim.x) * BwdCfg<FC>::WARPS;
+    int item = static_cast<int>(blockIdx.x) * BwdCfg<FC>::WARPS + warp;
+    while (item < n_items) {
+        __syncwarp();  // the previous item's reads of s_go are done
+        const int4 it = items[item];
+        const int tile = it.x;
+        const int first = it.y;
+        const int r = it.z;
+        const int tile_x = tile % ntx;
+        const int tile_y = tile / ntx;
+        const int tx0 = tile_x * kTile;
+        const int ty0 = tile_y * kTile;
+        const int nrow = min(kTile, H - ty0);
+        const int ncol = min(kTile, W - tx0);
 
-    const int4 it = items[item];
-    const int tile = it.x;
-    const int first = it.y;
-    const int r = it.z;
-    const int tile_x = tile % ntx;
-    const int tile_y = tile / ntx;
-    const int tx0 = tile_x * kTile;
-    const int ty0 = tile_y * kTile;
-    const int nrow = min(kTile, H - ty0);
-    const int ncol = min(kTile, W - tx0);
-
-    // stage this tile's dL/dimage (zero outside the image): all of a lane's
-    // loads are issued before any store, so staging costs one L2 round trip
-    const int64_t plane = static_cast<int64_t>(H) * W;
-    {
-        constexpr int kPerLane = kTilePixels / 32;  // 8 pixels per lane and channel
-        const float* gbase = grad_image + static_cast<int64_t>(ty0) * W + tx0;
+        // stage this tile's dL/dimage (zero outside the image): all of a lane's
+        // loads are issued before any store, so staging costs one L2 round trip
+        const int64_t plane = static_cast<int64_t>(H) * W;
+        {
+            constexpr int kPerLane = kTilePixels / 32;  // 8 pixels per lane and channel
+            const float* gbase = grad_image + static_cast<int64_t>(ty0) * W + tx0;
 #pragma unroll 1
-        for (int c0 = 0; c0 < SG; c0 += 4) {  // groups of 4 channels: 32 loads in flight per lane
-            float v[4][kPerLane];
+            for (int c0 = 0; c0 < SG; c0 += 4) {  // groups of 4 channels: 32 loads in flight per lane
+                float v[4][kPerLane];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+                for (int cc = 0; cc < 4; ++cc) {
 #pragma unroll
-                for (int i = 0; i < kPerLane; ++i) {
-                    const int p = i * 32 + lane;
-                    const int ly = p >> 4, lx = p & (kTile - 1);
-                    const int c = c0 + cc;
-                    v[cc][i] = (c < F && ly < nrow && lx < ncol)
-                                   ? __ldg(gbase + c * plane + static_cast<int64_t>(ly) * W + lx)
-                                   : 0.0f;
+                    for (int i = 0; i < kPerLane; ++i) {
+                        const int p = i * 32 + lane;
+                        const int ly = p >> 4, lx = p & (kTile - 1);
+                        const int c = c0 + cc;
+                        v[cc][i] = (c < F && ly < nrow && lx < ncol)
+                                       ? __ldg(gbase + c * plane + static_cast<int64_t>(ly) * W + lx)
+                                       : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+                    for (int i = 0; i < kPerLane; ++i) {
+                        const int p = i * 32 + lane;
+                        s_go[go_index<FC>(p >> 4, p & (kTile - 1), c0 + cc)] = v[cc][i];
+                    }
                 }
             }
+        }
+        __syncwarp();
+
+        // lanes per entry (k) and this lane's entry and row band
+        const int k = r > 16 ? 1 : (r > 8 ? 2 : (r > 4 ? 4 : (r > 2 ? 8 : 16)));
+        const int e = lane / k;
+        const int band = lane - e * k;
+        const int rows_per = kTile / k;
+        const int r0 = band * rows_per;
+        const int r1 = min(r0 + rows_per, nrow);
+        const bool active = e < r;
+
+        int g = 0;
+        int slot = 0;
+        float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float fv[FC];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+        for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
+        if (active) {  // idle lanes run on a neutral entry so the warp stays converged
+            if (MODE == kDetRecords) {
+                const float4* rec = reinterpret_cast<const float4*>(records + static_cast<int64_t>(first + e) * RS);
+                g0 = rec[0];
+                float rv[RS - 4];
 #pragma unroll
-                for (int i = 0; i < kPerLane; ++i) {
-                    const int p = i * 32 + lane;
-                    s_go[go_index<FC>(p >> 4, p & (kTile - 1), c0 + cc)] = v[cc][i];
+                for (int v = 0; v < (RS - 4) / 4; ++v) {
+                    const float4 t = rec[1 + v];
+                    rv[4 * v + 0] = t.x;
+                    rv[4 * v + 1] = t.y;
+                    rv[4 * v + 2] = t.z;
+                    rv[4 * v + 3] = t.w;
+                }
+                g1.x = rv[0];
+#pragma unroll
+                for (int c = 0; c < FC; ++c) fv[c] = rv[1 + c];
+                if (slots != nullptr) {
+                    slot = slots[first + e];
+                } else {
+                    g = gid_sorted[first + e];  // the slot is derived after the sums
+                }
+            } else {
+                g = gid_sorted[first + e];
+                const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
+                g0 = rec[0];
+                g1 = rec[1];
+                const float op = opacity != nullptr ? opacity[g] : 1.0f;
+                const float* fg = feat + static_cast<int64_t>(g) * F;
+#pragma unroll
+                for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
+            }
+        }
+        // the same test on (-A, -B/2, -D) = k (a, b, d) with k = 0.5 log2(e) > 0 (records carry no raw conic)
+        const bool regular = !active || regular_conic_bwd(g0.x, g0.y, -g0.z, -0.5f * g0.w, -g1.x);
+        const bool warp_regular = __all_sync(0xffffffffu, regular);
+
+        float dF[FC];
+#pragma unroll
+        for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
+        float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f;
+        const float A = g0.z, B = g0.w, D = g1.x;
+        if (ncol == kTile) {
+            const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
+            if (warp_regular) {
+                if constexpr (BwdCfg<FC>::PAIRED) {
+                    bwd_rows_full_pk<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                                Syy);
+                } else {
+                    bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+                }
+            } else {
+                if constexpr (BwdCfg<FC>::PAIRED) {
+                    bwd_rows_full_pk<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                               Syy);
+                } else {
+                    bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+                }
+            }
+        } else {
+            bwd_rows_edge<FC>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+        }
+        if (k > 1) {  // combine the k row bands of each entry (all lanes take part)
+            Sx = group_sum(Sx, k);
+            Sy = group_sum(Sy, k);
+            Sxx = group_sum(Sxx, k);
+            Sxy = group_sum(Sxy, k);
+            Syy = group_sum(Syy, k);
+#pragma unroll
+            for (int c = 0; c < FC; ++c) dF[c] = group_sum(dF[c], k);
+        }
+        // the next item's index; its latency overlaps the epilogue's loads
+        const int next = take_item(work, limit, grid_warps, lane);
+        if (active && band == 0) {
+            const float dca = -0.5f * Sxx;
+            const float dcb = -Sxy;
+            const float dcd = -0.5f * Syy;
+            if (MODE != kAtomicGather) {
+                if (MODE == kDetGather || slots == nullptr) {
+                    const int4 box = aabb[g];
+                    slot = pair_offset[g] + (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
+                }
+                float* row = pairgrad + static_cast<int64_t>(slot) * pstride;
+                if (FC <= 3) {
+                    float4* row4 = reinterpret_cast<float4*>(row);
+                    row4[0] = make_float4(Sx, Sy, dca, dcb);
+                    row4[1] = make_float4(dcd, dF[0], FC > 1 ? dF[FC > 1 ? 1 : 0] : 0.0f,
+                                          FC > 2 ? dF[FC > 2 ? 2 : 0] : 0.0f);
+                } else {
+                    row[0] = Sx;
+                    row[1] = Sy;
+                    row[2] = dca;
+                    row[3] = dcb;
+                    row[4] = dcd;
+#pragma unroll
+                    for (int c = 0; c < FC; ++c) {
+                        if (c < F) row[5 + c] = dF[c];
+                    }
+                }
+            } else {
+                // raw conic (a, b, d) sits in g1.yzw
+                atomicAdd(&d_xy[2 * g + 0], fmaf(g1.y, Sx, g1.z * Sy));
+                atomicAdd(&d_xy[2 * g + 1], fmaf(g1.z, Sx, g1.w * Sy));
+                atomicAdd(&d_conic[3 * g + 0], dca);
+                atomicAdd(&d_conic[3 * g + 1], dcb);
+                atomicAdd(&d_conic[3 * g + 2], dcd);
+#pragma unroll
+                for (int c = 0; c < FC; ++c) {
+                    if (c < F) atomicAdd(&d_feat[static_cast<int64_t>(g) * F + c], dF[c]);
                 }
             }
         }
-    }
-    __syncwarp();
-
-    // lanes per entry (k) and this lane's entry and row band
-    const int k = r > 16 ? 1 : (r > 8 ? 2 : (r > 4 ? 4 : (r > 2 ? 8 : 16)));
-    const int e = lane / k;
-    const int band = lane - e * k;
-    const int rows_per = kTile / k;
-    const int r0 = band * rows_per;
-    const int r1 = min(r0 + rows_per, nrow);
-    const bool active = e < r;
-
-    int g = 0;
-    int slot = 0;
-    float4 g0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float4 g1 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float fv[FC];
-#pragma unroll
-    for (int c = 0; c < FC; ++c) fv[c] = 0.0f;
-    if (active) {  // idle lanes run on a neutral entry so the warp stays converged
-        if (MODE == kDetRecords) {
-            const float4* rec = reinterpret_cast<const float4*>(records + static_cast<int64_t>(first + e) * RS);
-            g0 = rec[0];
-            float rv[RS - 4];
-#pragma unroll
-            for (int v = 0; v < (RS - 4) / 4; ++v) {
-                const float4 t = rec[1 + v];
-                rv[4 * v + 0] = t.x;
-                rv[4 * v + 1] = t.y;
-                rv[4 * v + 2] = t.z;
-                rv[4 * v + 3] = t.w;
-            }
-            g1.x = rv[0];
-#pragma unroll
-            for (int c = 0; c < FC; ++c) fv[c] = rv[1 + c];
-            if (slots != nullptr) {
-                slot = slots[first + e];
-            } else {
-                g = gid_sorted[first + e];  // the slot is derived after the sums
-            }
-        } else {
-            g = gid_sorted[first + e];
-            const float4* rec = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8);
-            g0 = rec[0];
-            g1 = rec[1];
-            const float op = opacity != nullptr ? opacity[g] : 1.0f;
-            const float* fg = feat + static_cast<int64_t>(g) * F;
-#pragma unroll
-            for (int c = 0; c < FC; ++c) fv[c] = c < F ? fg[c] * op : 0.0f;
-        }
-    }
-    // the same test on (-A, -B/2, -D) = k (a, b, d) with k = 0.5 log2(e) > 0 (records carry no raw conic)
-    const bool regular = !active || regular_conic_bwd(g0.x, g0.y, -g0.z, -0.5f * g0.w, -g1.x);
-    const bool warp_regular = __all_sync(0xffffffffu, regular);
-
-    float dF[FC];
-#pragma unroll
-    for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
-    float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f;
-    const float A = g0.z, B = g0.w, D = g1.x;
-    if (ncol == kTile) {
-        const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
-        if (warp_regular) {
-            if constexpr (BwdCfg<FC>::PAIRED) {
-                bwd_rows_full_pk<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
-                                            Syy);
-            } else {
-                bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
-            }
-        } else {
-            if constexpr (BwdCfg<FC>::PAIRED) {
-                bwd_rows_full_pk<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
-                                           Syy);
-            } else {
-                bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
-            }
-        }
-    } else {
-        bwd_rows_edge<FC>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
-    }
-    if (k > 1) {  // combine the k row bands of each entry (all lanes take part)
-        Sx = group_sum(Sx, k);
-        Sy = group_sum(Sy, k);
-        Sxx = group_sum(Sxx, k);
-        Sxy = group_sum(Sxy, k);
-        Syy = group_sum(Syy, k);
-#pragma unroll
-        for (int c = 0; c < FC; ++c) dF[c] = group_sum(dF[c], k);
-    }
-    if (!active || band != 0) return;
-
-    const float dca = -0.5f * Sxx;
-    const float dcb = -Sxy;
-    const float dcd = -0.5f * Syy;
-    if (MODE != kAtomicGather) {
-        if (MODE == kDetGather || slots == nullptr) {
-            const int4 box = aabb[g];
-            slot = pair_offset[g] + (tile_y - box.y) * (box.z - box.x) + (tile_x - box.x);
-        }
-        float* row = pairgrad + static_cast<int64_t>(slot) * pstride;
-        if (FC <= 3) {
-            float4* row4 = reinterpret_cast<float4*>(row);
-            row4[0] = make_float4(Sx, Sy, dca, dcb);
-            row4[1] = make_float4(dcd, dF[0], FC > 1 ? dF[FC > 1 ? 1 : 0] : 0.0f,
-                                  FC > 2 ? dF[FC > 2 ? 2 : 0] : 0.0f);
-        } else {
-            row[0] = Sx;
-            row[1] = Sy;
-            row[2] = dca;
-            row[3] = dcb;
-            row[4] = dcd;
-#pragma unroll
-            for (int c = 0; c < FC; ++c) {
-                if (c < F) row[5 + c] = dF[c];
-            }
-        }
-    } else {
-        // raw conic (a, b, d) sits in g1.yzw
-        atomicAdd(&d_xy[2 * g + 0], fmaf(g1.y, Sx, g1.z * Sy));
-        atomicAdd(&d_xy[2 * g + 1], fmaf(g1.z, Sx, g1.w * Sy));
-        atomicAdd(&d_conic[3 * g + 0], dca);
-        atomicAdd(&d_conic[3 * g + 1], dcb);
-        atomicAdd(&d_conic[3 * g + 2], dcd);
-#pragma unroll
-        for (int c = 0; c < FC; ++c) {
-            if (c < F) atomicAdd(&d_feat[static_cast<int64_t>(g) * F + c], dF[c]);
-        }
+        item = next;
     }
 }
 
 // Work items of the backward: every tile has ceil(L / 32) items of up to 32
-// consecutive list entries, item k of tile t = (t, first entry, count).  Two
-// parallel launches build the table: per block of kItemSpan tiles the item
-// total, then per block the prefix of the earlier totals, a block scan and the
-// writes; the last block also stores the item count.
+// consecutive list entries, item = (tile, first entry, count).  The table lists
+// them longest first, in three duration classes: items of 17..32 entries (one
+// lane per entry over all 16 rows), of 9..16 (two lanes per entry, 8 rows
+// each) and of 1..8 (4 rows or fewer); tile order within a class.  Two parallel
+// launches build it: per block of kItemSpan tiles the item count of each class,
+// then per block the prefix of the earlier blocks' counts, a block scan and the
+// writes.  The last block also stores the item count and clears the backward's
+// work counter.
 constexpr int kItemThreads = 256;
 constexpr int kItemTilesPerThread = 4;
 constexpr int kItemSpan = kItemThreads * kItemTilesPerThread;
+constexpr int kItemClasses = 3;
 
-__device__ __forceinline__ int tile_items(const int32_t* __restrict__ tile_offsets, int t) {
-    return (tile_offsets[t + 1] - tile_offsets[t] + kItemEntries - 1) / kItemEntries;
+__device__ __forceinline__ int item_class(int count) { return count > 16 ? 0 : (count > 8 ? 1 : 2); }
+
+// Items of each class for a list of len entries.
+__device__ __forceinline__ void tile_item_counts(int len, int (&cnt)[kItemClasses]) {
+    cnt[0] = len / kItemEntries;
+    cnt[1] = 0;
+    cnt[2] = 0;
+    const int rest = len % kItemEntries;
+    if (rest > 0) cnt[item_class(rest)] += 1;
 }
 
 // Exclusive block scan of one int per thread; `total` receives the block sum.
@@ -465,44 +499,85 @@ __global__ void __launch_bounds__(kItemThreads) k_item_block_sums(int num_tiles,
                                                                    int32_t* __restrict__ block_items) {
     __shared__ int s_warp[kItemThreads / 32];
     const int t0 = blockIdx.x * kItemSpan + threadIdx.x * kItemTilesPerThread;
-    int local = 0;
+    int local[kItemClasses] = {0, 0, 0};
 #pragma unroll
-    for (int k = 0; k < kItemTilesPerThread; ++k) local += t0 + k < num_tiles ? tile_items(tile_offsets, t0 + k) : 0;
-    int total;
-    item_block_scan(local, s_warp, total);
-    if (threadIdx.x == 0) block_items[blockIdx.x] = total;
+    for (int k = 0; k < kItemTilesPerThread; ++k) {
+        if (t0 + k < num_tiles) {
+            int cnt[kItemClasses];
+            tile_item_counts(tile_offsets[t0 + k + 1] - tile_offsets[t0 + k], cnt);
+#pragma unroll
+            for (int c = 0; c < kItemClasses; ++c) local[c] += cnt[c];
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < kItemClasses; ++c) {
+        int total;
+        item_block_scan(local[c], s_warp, total);
+        if (threadIdx.x == 0) block_items[blockIdx.x * kItemClasses + c] = total;
+    }
 }
 
 __global__ void __launch_bounds__(kItemThreads) k_item_table(int num_tiles, const int32_t* __restrict__ tile_offsets,
                                                               const int32_t* __restrict__ block_items,
-                                                              int4* __restrict__ items, int32_t* __restrict__ num_items) {
+                                                              int4* __restrict__ items, int32_t* __restrict__ num_items,
+                                                              uint32_t* __restrict__ work) {
     __shared__ int s_warp[kItemThreads / 32];
-    int part = 0;
-    for (int b = threadIdx.x; b < static_cast<int>(blockIdx.x); b += kItemThreads) part += block_items[b];
-    int prefix;
-    item_block_scan(part, s_warp, prefix);
+    // start of this block's run in each class: all items of the earlier classes,
+    // then the earlier blocks' items of the class
+    int before[kItemClasses] = {0, 0, 0}, all[kItemClasses] = {0, 0, 0};
+    for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kItemThreads) {
+#pragma unroll
+        for (int c = 0; c < kItemClasses; ++c) {
+            const int v = block_items[b * kItemClasses + c];
+            all[c] += v;
+            before[c] += b < static_cast<int>(blockIdx.x) ? v : 0;
+        }
+    }
+    int run[kItemClasses];
+    int class_base = 0;
+#pragma unroll
+    for (int c = 0; c < kItemClasses; ++c) {
+        int earlier, total;
+        item_block_scan(before[c], s_warp, earlier);
+        item_block_scan(all[c], s_warp, total);
+        run[c] = class_base + earlier;
+        class_base += total;
+    }
     const int t0 = blockIdx.x * kItemSpan + threadIdx.x * kItemTilesPerThread;
     int beg[kItemTilesPerThread + 1];
 #pragma unroll
     for (int k = 0; k <= kItemTilesPerThread; ++k) beg[k] = t0 + k <= num_tiles ? tile_offsets[t0 + k] : 0;
-    int cnt[kItemTilesPerThread];
-    int local = 0;
+    int local[kItemClasses] = {0, 0, 0};
 #pragma unroll
     for (int k = 0; k < kItemTilesPerThread; ++k) {
-        cnt[k] = t0 + k < num_tiles ? (beg[k + 1] - beg[k] + kItemEntries - 1) / kItemEntries : 0;
-        local += cnt[k];
-    }
-    int total;
-    int run = prefix + item_block_scan(local, s_warp, total);
+        if (t0 + k < num_tiles) {
+            int cnt[kItemClasses];
+            tile_item_counts(beg[k + 1] - beg[k], cnt);
 #pragma unroll
-    for (int k = 0; k < kItemTilesPerThread; ++k) {
-        const int len = beg[k + 1] - beg[k];
-        for (int i = 0; i < cnt[k]; ++i) {
-            items[run + i] = make_int4(t0 + k, beg[k] + i * kItemEntries, min(kItemEntries, len - i * kItemEntries), 0);
+            for (int c = 0; c < kItemClasses; ++c) local[c] += cnt[c];
         }
-        run += cnt[k];
     }
-    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) *num_items = prefix + total;
+#pragma unroll
+    for (int c = 0; c < kItemClasses; ++c) {
+        int total;
+        run[c] += item_block_scan(local[c], s_warp, total);
+    }
+#pragma unroll
+    for (int k = 0; k < kItemTilesPerThread; ++k) {
+        if (t0 + k >= num_tiles) continue;
+        const int len = beg[k + 1] - beg[k];
+        const int full = len / kItemEntries;
+        for (int i = 0; i < full; ++i) items[run[0]++] = make_int4(t0 + k, beg[k] + i * kItemEntries, kItemEntries, 0);
+        const int rest = len - full * kItemEntries;
+        if (rest > 0) {
+            const int c = item_class(rest);
+            items[run[c]++] = make_int4(t0 + k, beg[k] + full * kItemEntries, rest, 0);
+        }
+    }
+    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+        *num_items = class_base;
+        *work = 0u;
+    }
 }
 
 template <int FC>
@@ -600,18 +675,35 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
     }
 }
 
+// Persistent grid of the backward: as many CTAs as fit on the device at once
+// (cached per device), never more than the table's largest item count needs.
+template <int FC, int MODE>
+int bwd_grid(int64_t max_items, int smem) {
+    static int cached[64] = {0};
+    const int64_t need = div_up(max_items, BwdCfg<FC>::WARPS);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return static_cast<int>(need);
+    if (cached[dev] == 0) {
+        int sms = 0, per = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE>, BwdCfg<FC>::THREADS, smem);
+        cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
+    }
+    return static_cast<int>(need < cached[dev] ? need : cached[dev]);
+}
+
 template <int FC, int MODE>
 cudaError_t launch_bwd_mode(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
                             const float* opacity, const int32_t* gid_sorted, const int4* items,
-                            const int32_t* num_items, const float* grad_image, const int32_t* aabb,
+                            const int32_t* num_items, uint32_t* work, const float* grad_image, const int32_t* aabb,
                             const int32_t* pair_offset, const float* records, const int32_t* slots, float* pairgrad,
                             int pstride, float* d_xy, float* d_conic, float* d_feat, cudaStream_t stream) {
     const int smem = BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT * static_cast<int>(sizeof(float));
-    const unsigned blocks = static_cast<unsigned>(div_up(max_items, BwdCfg<FC>::WARPS));
     auto kern = k_render_bwd<FC, MODE>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const unsigned blocks = static_cast<unsigned>(bwd_grid<FC, MODE>(max_items, smem));
     kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
-        f, h, w, ntx, geo, feat, opacity, gid_sorted, items, num_items, grad_image,
+        f, h, w, ntx, geo, feat, opacity, gid_sorted, items, num_items, work, grad_image,
         reinterpret_cast<const int4*>(aabb), pair_offset, records, slots, pairgrad, pstride, d_xy, d_conic, d_feat);
     return cudaGetLastError();
 }
@@ -619,21 +711,22 @@ cudaError_t launch_bwd_mode(int f, int h, int w, int ntx, int64_t max_items, con
 template <int FC>
 cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int4* items, const int32_t* num_items,
+                          uint32_t* work,
                           const float* grad_image, const int32_t* aabb, const int32_t* pair_offset,
                           const float* records, const int32_t* slots, float* pairgrad, int pstride, float* d_xy,
                           float* d_conic, float* d_feat, cudaStream_t stream) {
     if (pairgrad == nullptr) {
         return launch_bwd_mode<FC, kAtomicGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
-                                                  num_items, grad_image, aabb, pair_offset, records, slots, pairgrad,
+                                                  num_items, work, grad_image, aabb, pair_offset, records, slots, pairgrad,
                                                   pstride, d_xy, d_conic, d_feat, stream);
     }
     if (records != nullptr) {
         return launch_bwd_mode<FC, kDetRecords>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
-                                                num_items, grad_image, aabb, pair_offset, records, slots, pairgrad,
+                                                num_items, work, grad_image, aabb, pair_offset, records, slots, pairgrad,
                                                 pstride, d_xy, d_conic, d_feat, stream);
     }
     return launch_bwd_mode<FC, kDetGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items,
-                                           grad_image, aabb, pair_offset, records, slots, pairgrad, pstride, d_xy,
+                                           work, grad_image, aabb, pair_offset, records, slots, pairgrad, pstride, d_xy,
                                            d_conic, d_feat, stream);
 }
 
@@ -657,8 +750,8 @@ int64_t backward_max_items(int64_t total_pairs, int64_t num_tiles) {
 }
 
 int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
-    return arena_bytes(backward_max_items(total_pairs, num_tiles), sizeof(int4)) + arena_bytes(1, sizeof(int32_t)) +
-           arena_bytes(div_up(num_tiles, kItemSpan), sizeof(int32_t));
+    return arena_bytes(backward_max_items(total_pairs, num_tiles), sizeof(int4)) + arena_bytes(2, sizeof(int32_t)) +
+           arena_bytes(div_up(num_tiles, kItemSpan) * kItemClasses, sizeof(int32_t));
 }
 
 #define OSS_DISPATCH_FC(f, CALL) \
@@ -673,13 +766,13 @@ cudaError_t launch_backward_items(int h, int w, int64_t total_pairs, const int32
     const int64_t max_items = backward_max_items(total_pairs, num_tiles);
     Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
     int4* items = arena.take<int4>(max_items);
-    int32_t* num_items = arena.take<int32_t>(1);
+    int32_t* counters = arena.take<int32_t>(2);  // item count, the backward's work counter
     const int item_blocks = static_cast<int>(div_up(num_tiles, kItemSpan));
-    int32_t* block_items = arena.take<int32_t>(item_blocks);
+    int32_t* block_items = arena.take<int32_t>(static_cast<int64_t>(item_blocks) * kItemClasses);
     k_item_block_sums<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(num_tiles, tile_offsets,
                                                                                          block_items);
-    k_item_table<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(num_tiles, tile_offsets,
-                                                                                    block_items, items, num_items);
+    k_item_table<<<static_cast<unsigned>(item_blocks), kItemThreads, 0, stream>>>(
+        num_tiles, tile_offsets, block_items, items, counters, reinterpret_cast<uint32_t*>(counters + 1));
     return cudaGetLastError();
 }
 
@@ -688,18 +781,19 @@ cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pair
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
                                          const int32_t* pair_offset, const float* records, const int32_t* slots,
                                          float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
-                                         const void* items_scratch, cudaStream_t stream) {
+                                         void* items_scratch, cudaStream_t stream) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
     const int num_tiles = ntx * nty;
     if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
     const int64_t max_items = backward_max_items(total_pairs, num_tiles);
-    Arena arena{static_cast<char*>(const_cast<void*>(items_scratch)), backward_items_scratch_bytes(total_pairs, num_tiles),
-                0};
+    Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
     const int4* items = arena.take<int4>(max_items);
-    const int32_t* num_items = arena.take<int32_t>(1);
+    int32_t* counters = arena.take<int32_t>(2);
+    const int32_t* num_items = counters;
+    uint32_t* work = reinterpret_cast<uint32_t*>(counters + 1);
 #define OSS_BWD_CALL(FC)                                                                                          \
-    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items, grad_image,     \
+    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items, work, grad_image, \
                       aabb, pair_offset, records, slots, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
     return OSS_DISPATCH_FC(f, OSS_BWD_CALL);
 #undef OSS_BWD_CALL

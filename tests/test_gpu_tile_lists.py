@@ -263,6 +263,12 @@ def test_packed_records_and_derived_slots_bit_identical(cuda_device, f, dense):
                                               side.cuda_stream), "items")
             torch.cuda.current_stream().wait_stream(side)
             _lib.check(lib.oss_render_backward_items(*args, s_), "backward_items")
+            # the table's work counter is back at zero after a launch: a second
+            # backward over the same table writes every row again, identically
+            first = pg[:total].clone()
+            pg.zero_()
+            _lib.check(lib.oss_render_backward_items(*args, s_), "backward_items again")
+            assert torch.equal(first, pg[:total])
         else:
             _lib.check(lib.oss_render_backward_pairs(*args, s_), "backward_pairs")
         rows.append(pg[:total])
@@ -350,3 +356,42 @@ def test_public_api_pair_capacity_mode(cuda_device):
     assert not pair_capacity_overflowed()  # reset by the first read
     for a in short:
         assert not a.any()
+
+
+def test_item_table_lists_every_item_once_longest_first(cuda_device):
+    """The backward's work-item table: every list cut into items of <= 32 entries,
+    ordered by duration class (17..32 entries, 9..16, 1..8), tile order within a
+    class; the item count follows the table and the work counter is cleared."""
+    from oss_cuda import _lib
+
+    lib = _lib.lib()
+    ntx, nty = 8, 5
+    h, w = 16 * nty - 3, 16 * ntx - 5  # ragged border tiles
+    lens = [0, 1, 8, 9, 16, 17, 31, 32, 33, 40, 48, 49, 64, 65, 100, 255, 256, 257, 3, 0,
+            12, 24, 7, 1000, 2, 5, 96, 97, 31, 18, 0, 0, 1, 9, 17, 33, 64, 11, 70, 5]
+    assert len(lens) == ntx * nty
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    total = int(offs[-1])
+    ib = lib.oss_render_backward_pairs_scratch_bytes(total, ntx * nty)
+    items = torch.full((ib,), 0x5A, device="cuda", dtype=torch.uint8)
+    s = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.oss_backward_items(h, w, total, dev(offs, torch.int32).data_ptr(), items.data_ptr(), ib, s),
+               "items")
+    torch.cuda.synchronize()
+    raw = host(items)
+    max_items = ntx * nty + (total + 31) // 32
+    off = ((max_items * 16 + 255) // 256) * 256
+    count, counter = raw[off:off + 8].view(np.int32)
+    table = raw[:max_items * 16].view(np.int32).reshape(max_items, 4)[:count]
+
+    want = {0: [], 1: [], 2: []}
+    for t, n in enumerate(lens):
+        for i in range(n // 32):
+            want[0].append((t, int(offs[t]) + 32 * i, 32))
+        rest = n % 32
+        if rest:
+            want[0 if rest > 16 else (1 if rest > 8 else 2)].append((t, int(offs[t]) + n - rest, rest))
+    expect = want[0] + want[1] + want[2]
+    assert count == len(expect)
+    assert counter == 0
+    assert [tuple(map(int, r[:3])) for r in table] == expect
