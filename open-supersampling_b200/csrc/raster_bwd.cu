@@ -46,7 +46,7 @@ struct BwdCfg {
     static constexpr int SLOT = kTile * ROW;              // floats per warp slot
     static constexpr int WARPS = SLOT * 4 * 4 <= 200 * 1024 ? 4 : 2;  // warps (slots) per CTA
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int MIN_CTAS = FC <= 4 ? 6 : 1;  // 6 x 4 warps per SM (<= 80 registers) for F <= 4
+    static constexpr int MIN_CTAS = FC <= 4 ? 5 : 1;  // 5 x 4 warps per SM (<= 96 registers) for F <= 4
     // F <= 4 runs the packed f32x2 path: the staged block is interleaved by
     // column pairs, [go_k(c), go_k(c+1)] for k = 0..SG-1 per pair of columns.
     static constexpr bool PAIRED = FC <= 4;
@@ -68,6 +68,8 @@ __device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, flo
 // Packed-f32x2 version of the full-row sums for F <= 4: every FP32 operation
 // works on two adjacent columns at once (__ffma2_rn / __fmul2_rn / __fadd2_rn),
 // halving the FP32 instructions per pixel; exp2 stays one MUFU op per pixel.
+// The column offsets dx and their squares are held in registers, so the
+// moments take g dx and g dx^2 as one FFMA2 each.
 template <int FC, bool CHECK>
 __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go, int r0, int r1, float fx0, float fy0,
                                                  float gx, float gy, float A, float B, float D, const float (&fv)[FC],
@@ -75,10 +77,11 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
                                                  float& Syy) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int ROW = BwdCfg<FC>::ROW;
-    float2 dx2[kTile / 2];
+    float2 dx2[kTile / 2], dxsq2[kTile / 2];
 #pragma unroll
     for (int j = 0; j < kTile / 2; ++j) {
         dx2[j] = make_float2((fx0 + static_cast<float>(2 * j)) - gx, (fx0 + static_cast<float>(2 * j + 1)) - gx);
+        dxsq2[j] = __fmul2_rn(dx2[j], dx2[j]);
     }
     const float2 A2 = make_float2(A, A);
     float2 f2[FC], dF2[FC];
@@ -118,9 +121,8 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
 #pragma unroll
             for (int k = 0; k < FC; ++k) dF2[k] = __ffma2_rn(w, go2[k], dF2[k]);
             const float2 gw = __fmul2_rn(w, dLdw);
-            const float2 gdx = __fmul2_rn(gw, dx);
-            rowGx2 = __fadd2_rn(rowGx2, gdx);
-            Sxx2 = __ffma2_rn(gdx, dx, Sxx2);
+            rowGx2 = __ffma2_rn(gw, dx, rowGx2);
+            Sxx2 = __ffma2_rn(gw, dxsq2[j], Sxx2);
             rowG2 = __fadd2_rn(rowG2, gw);
         }
         const float rowGx = rowGx2.x + rowGx2.y;
