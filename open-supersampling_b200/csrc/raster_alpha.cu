@@ -279,7 +279,9 @@ __global__ void __launch_bounds__(AlphaCfg<FC>::NT) k_render_alpha_bwd(
                 const float og = op * G;
                 const float a = fminf(og, kAlphaMax);
                 if (a < kAlphaMin) continue;
-                T[k] = __fdiv_rn(T[k], 1.0f - a);  // transmittance in front of this entry
+                // transmittance in front of this entry; 1 - a lies in [0.01, 1), where the
+                // fast division is within 2 ulp (a correctly rounded one cost 4% of the step)
+                T[k] = __fdividef(T[k], 1.0f - a);
                 const float wgt = a * T[k];
                 float dlda = 0.0f;
 #pragma unroll
