@@ -163,3 +163,32 @@ class V6Rasterizer(nn.Module):
         if colors.shape[-1] > f:
             return colors[..., :f]
         return torch.nn.functional.pad(colors, (0, f - colors.shape[-1]))
+
+
+def render_canvas_at_lr(rasterizer: V6Rasterizer, warped_canvas, active_mask, batch_size: int, h_lr: int,
+                        w_lr: int, scale: float, device, dtype):
+    """(G, m) for ConcatFusion (oss/sr/v6/model.py:628-678, ``_rasterize_canvas_at_lr``):
+    the warped canvas, whose positions and scales live in HR pixels, divided by
+    the upscale factor and rendered at LR resolution with the weight-sum channel.
+    G is (B, latent_rank, h_lr, w_lr), m is (B, 1, h_lr, w_lr); both are zeros
+    without a canvas.  ``active_mask`` None means every one of the canvas's
+    ``count`` Gaussians."""
+    from .canvas import CanvasState
+
+    r = int(rasterizer.latent_rank)
+    if warped_canvas is None or warped_canvas.count == 0:
+        return (torch.zeros((batch_size, r, h_lr, w_lr), device=device, dtype=dtype),
+                torch.zeros((batch_size, 1, h_lr, w_lr), device=device, dtype=dtype))
+    scaled = CanvasState(positions=warped_canvas.positions / float(scale),
+                         scales=warped_canvas.scales / float(scale), rotations=warped_canvas.rotations,
+                         opacities=warped_canvas.opacities, colors=warped_canvas.colors, count=warped_canvas.count)
+    mask = active_mask if active_mask is not None else torch.ones(int(warped_canvas.count), device=device,
+                                                                  dtype=torch.bool)
+    out = rasterizer(scaled, mask.unsqueeze(0).expand(batch_size, -1) if mask.ndim == 1 else mask,
+                     output_hw=(h_lr, w_lr), return_weight_sum=True)
+    if isinstance(out, tuple):
+        g, m = out
+    else:
+        g = out
+        m = torch.zeros((batch_size, 1, h_lr, w_lr), device=device, dtype=dtype)
+    return g.to(dtype=dtype), m.to(dtype=dtype)

@@ -117,3 +117,30 @@ def test_warp_canvas_cuda_is_the_canvas_warp(cuda_device):
     for x, y in zip((a.positions, a.scales, a.rotations, a.opacities, a.colors),
                     (b.positions, b.scales, b.rotations, b.opacities, b.colors)):
         assert torch.equal(x, y)
+
+
+def test_render_canvas_at_lr_is_the_scaled_weight_sum_render(cuda_device):
+    """The LR render for ConcatFusion (oss/sr/v6/model.py:628-678): the canvas
+    divided by the upscale factor through V6Rasterizer with the weight-sum
+    channel, expanded over the batch; zeros without a canvas."""
+    from oss_b200 import CanvasState, V6Rasterizer, render_canvas_at_lr
+
+    n, h_lr, w_lr, s = 800, 48, 80, 2.0
+    g = torch.Generator(device="cuda").manual_seed(4)
+    canvas = CanvasState(torch.rand((n, 2), device="cuda", generator=g) * torch.tensor([w_lr * s, h_lr * s],
+                                                                                       device="cuda"),
+                         torch.rand((n, 2), device="cuda", generator=g) * 3.0 + 1.0,
+                         torch.rand((n,), device="cuda", generator=g) * 3.0,
+                         torch.rand((n,), device="cuda", generator=g),
+                         torch.rand((n, 8), device="cuda", generator=g), count=n)
+    ras = V6Rasterizer(token_dim=32, latent_rank=8)
+    mask = torch.rand((n,), device="cuda", generator=g) > 0.3
+    G, m = render_canvas_at_lr(ras, canvas, mask, 2, h_lr, w_lr, s, torch.device("cuda"), torch.float32)
+    assert G.shape == (2, 8, h_lr, w_lr) and m.shape == (2, 1, h_lr, w_lr)
+    scaled = CanvasState(canvas.positions / s, canvas.scales / s, canvas.rotations, canvas.opacities,
+                         canvas.colors, count=n)
+    G2, m2 = ras(scaled, mask.unsqueeze(0).expand(2, -1), output_hw=(h_lr, w_lr), return_weight_sum=True)
+    assert torch.equal(G, G2) and torch.equal(m, m2)
+    assert float(m.max()) > 0.0
+    Gz, mz = render_canvas_at_lr(ras, None, None, 3, h_lr, w_lr, s, torch.device("cuda"), torch.float32)
+    assert Gz.shape == (3, 8, h_lr, w_lr) and not Gz.any() and not mz.any()
