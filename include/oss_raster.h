@@ -373,6 +373,53 @@ OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, in
 OSS_API int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, float alpha,
                                const float* xy, float* out_xy, uint8_t* in_frame, void* stream);
 
+/* ---- Persistent-canvas lifecycle (oss/gaussian/canvas/canvas.py:191-295) ----
+ * The steps around the render in PersistentCanvas.update, all on the device.
+ * Masks are uint8 (0 / 1), ages int64, everything else fp32. */
+
+/* Per-tile mean squared error (error_detection.py:26-63, per_tile_mse): tile_err[ty * (w / ts) + tx]
+ * = mean over the tile's ts x ts pixels of the channel mean of (rendered - target)^2.  rendered is
+ * (f, h, w); h and w must be multiples of ts.  target is (f, target_h, target_w): at (h, w) it is used
+ * as is, otherwise it is the LR frame and is upsampled on the fly as F.interpolate(bilinear,
+ * align_corners=False) would (canvas.py:256-263). */
+OSS_API int oss_tile_mse(int64_t f, int64_t h, int64_t w, int64_t ts, const float* rendered, int64_t target_h,
+                         int64_t target_w, const float* target, float* tile_err, void* stream);
+/* Per-slot error (error_detection.py:66-113, gaussians_error_from_tiles): g_error[i] = the error of the
+ * tile holding xy[i], +inf outside [0, w) x [0, h) or, when in_frame is given, where in_frame[i] == 0
+ * (canvas.py:266-269).  With alive given: error[i] = alive[i] ? g_error[i] : 0 and
+ * age[i] = alive[i] ? age[i] + 1 : 0 (canvas.py:246-249, 270).  Any output may be NULL. */
+OSS_API int oss_canvas_error(int64_t n, int64_t h, int64_t w, int64_t ts, const float* xy, const uint8_t* in_frame,
+                             const float* tile_err, const uint8_t* alive, int64_t* age, float* g_error,
+                             float* error, void* stream);
+/* Prune decision tree (prune_spawn.py:72-157, select_for_pruning) with its policy fields
+ * (prune_spawn.py:36-62).  prune_idx (n int64) receives *prune_count slot indices: in slot order when
+ * the selection fits max(1, floor(max_prune_frac * capacity)), else that many in descending order of
+ * priority * 1e6 + error (ties in slot order).  quantiles (2 floats) receive the R2 and R3 thresholds. */
+OSS_API int64_t oss_prune_scratch_bytes(int64_t n);
+OSS_API int oss_select_for_pruning(int64_t n, const uint8_t* alive, const uint8_t* in_frame, const int64_t* age,
+                                   const float* g_error, int64_t capacity, int64_t age_max, double age_low_error_pct,
+                                   double tile_error_pct, int64_t min_age_before_prune, double max_prune_frac,
+                                   int64_t* prune_idx, int64_t* prune_count, float* quantiles, void* scratch,
+                                   int64_t scratch_bytes, void* stream);
+/* Spawn tiles (prune_spawn.py:165-208, select_spawn_tiles): the (ty, tx) of the largest tile errors
+ * (classifier_mask, nullable, sends masked tiles to -inf; ties in tile order), *take = min(n_tiles,
+ * finite eligible tiles) rows of tiles_yx (th * tw x 2 int64). */
+OSS_API int64_t oss_spawn_tiles_scratch_bytes(int64_t num_tiles);
+OSS_API int oss_select_spawn_tiles(int64_t th, int64_t tw, const float* tile_err, const uint8_t* classifier_mask,
+                                   int64_t n_tiles, int64_t* tiles_yx, int64_t* take, void* scratch,
+                                   int64_t scratch_bytes, void* stream);
+/* Prune/spawn slot update (prune_spawn.py:216-255, apply_prune_spawn): the first *prune_count entries
+ * of prune_idx (at most max_prune) die with age and error reset, then the r-th dead slot in slot order
+ * takes new Gaussian r for r < num_new (positions, scales, rotation, the first min(f, f_new) colour
+ * channels; alive, age 0, error 0).  *n_spawned receives the number written.  num_new may be 0. */
+OSS_API int64_t oss_prune_spawn_scratch_bytes(int64_t n);
+OSS_API int oss_apply_prune_spawn(int64_t n, int64_t f, const int64_t* prune_idx, const int64_t* prune_count,
+                                  int64_t max_prune, int64_t num_new, int64_t f_new, const float* new_xy,
+                                  const float* new_scale, const float* new_rot, const float* new_feat,
+                                  float* positions, float* scales, float* rotations, float* colors, uint8_t* alive,
+                                  int64_t* age, float* error, int64_t* n_spawned, void* scratch,
+                                  int64_t scratch_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -571,6 +571,111 @@ int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, flo
     return OSS_OK;
 }
 
+int oss_tile_mse(int64_t f, int64_t h, int64_t w, int64_t ts, const float* rendered, int64_t target_h,
+                 int64_t target_w, const float* target, float* tile_err, void* stream) {
+    OSS_CHECK(f > 0 && f <= INT_MAX, OSS_ERR_INVALID, "F must be positive");
+    OSS_CHECK(ts > 0 && ts <= 1024, OSS_ERR_INVALID, "tile_size must be in [1, 1024]");
+    OSS_CHECK(h > 0 && w > 0 && h <= INT_MAX && w <= INT_MAX, OSS_ERR_INVALID, "H and W must be positive");
+    OSS_CHECK(h % ts == 0 && w % ts == 0, OSS_ERR_INVALID, "H and W must both be multiples of tile_size");
+    OSS_CHECK(target_h > 0 && target_w > 0 && target_h <= INT_MAX && target_w <= INT_MAX, OSS_ERR_INVALID,
+              "target H and W must be positive");
+    OSS_CHECK(f * h * w <= INT64_MAX / 4, OSS_ERR_RANGE, "rendered is too large");
+    OSS_CHECK(rendered != nullptr && target != nullptr && tile_err != nullptr, OSS_ERR_INVALID,
+              "pointers must be non-null");
+    OSS_CUDA_TRY(oss::launch_tile_mse(static_cast<int>(f), static_cast<int>(h), static_cast<int>(w),
+                                      static_cast<int>(ts), rendered, static_cast<int>(target_h),
+                                      static_cast<int>(target_w), target, tile_err, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_canvas_error(int64_t n, int64_t h, int64_t w, int64_t ts, const float* xy, const uint8_t* in_frame,
+                     const float* tile_err, const uint8_t* alive, int64_t* age, float* g_error, float* error,
+                     void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N must be in [0, INT_MAX]");
+    OSS_CHECK(ts > 0 && ts <= 1024, OSS_ERR_INVALID, "tile_size must be in [1, 1024]");
+    OSS_CHECK(h > 0 && w > 0 && h <= INT_MAX && w <= INT_MAX, OSS_ERR_INVALID, "H and W must be positive");
+    OSS_CHECK(h % ts == 0 && w % ts == 0, OSS_ERR_INVALID, "H and W must both be multiples of tile_size");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(xy != nullptr && tile_err != nullptr && aligned(xy, 8), OSS_ERR_INVALID,
+              "xy (8-byte aligned) and tile_err must be non-null");
+    OSS_CUDA_TRY(oss::launch_canvas_error(static_cast<int>(n), static_cast<int>(h), static_cast<int>(w),
+                                          static_cast<int>(ts), xy, in_frame, tile_err, alive, age, g_error, error,
+                                          as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_prune_scratch_bytes(int64_t n) { return oss::prune_scratch_bytes(n < 0 ? 0 : n); }
+
+int oss_select_for_pruning(int64_t n, const uint8_t* alive, const uint8_t* in_frame, const int64_t* age,
+                           const float* g_error, int64_t capacity, int64_t age_max, double age_low_error_pct,
+                           double tile_error_pct, int64_t min_age_before_prune, double max_prune_frac,
+                           int64_t* prune_idx, int64_t* prune_count, float* quantiles, void* scratch,
+                           int64_t scratch_bytes, void* stream) {
+    OSS_CHECK(n >= 0 && n < INT_MAX, OSS_ERR_RANGE, "N must be in [0, INT_MAX)");
+    OSS_CHECK(prune_count != nullptr && quantiles != nullptr && scratch != nullptr, OSS_ERR_INVALID,
+              "prune_count, quantiles and scratch must be non-null");
+    OSS_CHECK(scratch_bytes >= oss::prune_scratch_bytes(n), OSS_ERR_SCRATCH, "scratch too small");
+    OSS_CHECK(n == 0 || (alive != nullptr && in_frame != nullptr && age != nullptr && g_error != nullptr &&
+                         prune_idx != nullptr),
+              OSS_ERR_INVALID, "alive, in_frame, age, g_error and prune_idx must be non-null");
+    // max(1, int(frac * capacity)) in double, as the policy's Python arithmetic
+    const double prod = max_prune_frac * static_cast<double>(capacity);
+    long long cap = prod >= 9.0e18 ? static_cast<long long>(9e18) : static_cast<long long>(prod);
+    if (cap < 1) cap = 1;
+    OSS_CUDA_TRY(oss::launch_select_for_pruning(static_cast<int>(n), alive, in_frame, age, g_error, cap, age_max,
+                                                static_cast<float>(age_low_error_pct),
+                                                static_cast<float>(tile_error_pct), min_age_before_prune, prune_idx,
+                                                prune_count, quantiles, scratch, as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_spawn_tiles_scratch_bytes(int64_t num_tiles) {
+    return oss::spawn_tiles_scratch_bytes(num_tiles < 0 ? 0 : num_tiles);
+}
+
+int oss_select_spawn_tiles(int64_t th, int64_t tw, const float* tile_err, const uint8_t* classifier_mask,
+                           int64_t n_tiles, int64_t* tiles_yx, int64_t* take, void* scratch, int64_t scratch_bytes,
+                           void* stream) {
+    OSS_CHECK(th >= 0 && tw >= 0 && th * tw <= INT_MAX, OSS_ERR_RANGE, "tile grid must be in int32 range");
+    OSS_CHECK(take != nullptr && scratch != nullptr, OSS_ERR_INVALID, "take and scratch must be non-null");
+    OSS_CHECK(scratch_bytes >= oss::spawn_tiles_scratch_bytes(th * tw), OSS_ERR_SCRATCH, "scratch too small");
+    OSS_CHECK(th * tw == 0 || (tile_err != nullptr && tiles_yx != nullptr), OSS_ERR_INVALID,
+              "tile_err and tiles_yx must be non-null");
+    OSS_CUDA_TRY(oss::launch_select_spawn_tiles(static_cast<int>(th), static_cast<int>(tw), tile_err,
+                                                classifier_mask, n_tiles, tiles_yx, take, scratch,
+                                                as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_prune_spawn_scratch_bytes(int64_t n) { return oss::prune_spawn_scratch_bytes(n < 0 ? 0 : n); }
+
+int oss_apply_prune_spawn(int64_t n, int64_t f, const int64_t* prune_idx, const int64_t* prune_count,
+                          int64_t max_prune, int64_t num_new, int64_t f_new, const float* new_xy,
+                          const float* new_scale, const float* new_rot, const float* new_feat, float* positions,
+                          float* scales, float* rotations, float* colors, uint8_t* alive, int64_t* age,
+                          float* error, int64_t* n_spawned, void* scratch, int64_t scratch_bytes, void* stream) {
+    OSS_CHECK(n >= 0 && n < INT_MAX, OSS_ERR_RANGE, "N must be in [0, INT_MAX)");
+    OSS_CHECK(f > 0 && f <= INT_MAX && f_new >= 0 && f_new <= INT_MAX, OSS_ERR_INVALID,
+              "F must be positive and F_new non-negative");
+    OSS_CHECK(num_new >= 0 && num_new <= INT_MAX && max_prune >= 0, OSS_ERR_INVALID,
+              "num_new and max_prune must be non-negative");
+    OSS_CHECK(n_spawned != nullptr && scratch != nullptr, OSS_ERR_INVALID, "n_spawned and scratch must be non-null");
+    OSS_CHECK(scratch_bytes >= oss::prune_spawn_scratch_bytes(n), OSS_ERR_SCRATCH, "scratch too small");
+    OSS_CHECK(max_prune == 0 || (prune_idx != nullptr && prune_count != nullptr), OSS_ERR_INVALID,
+              "prune_idx and prune_count must be non-null");
+    OSS_CHECK(n == 0 || (positions != nullptr && scales != nullptr && rotations != nullptr && colors != nullptr &&
+                         alive != nullptr && age != nullptr && error != nullptr),
+              OSS_ERR_INVALID, "canvas arrays must be non-null");
+    OSS_CHECK(num_new == 0 || (new_xy != nullptr && new_scale != nullptr && new_rot != nullptr &&
+                               (f_new == 0 || new_feat != nullptr)),
+              OSS_ERR_INVALID, "new Gaussian arrays must be non-null");
+    OSS_CUDA_TRY(oss::launch_apply_prune_spawn(static_cast<int>(n), static_cast<int>(f), prune_idx, prune_count,
+                                               max_prune, static_cast<int>(num_new), static_cast<int>(f_new), new_xy,
+                                               new_scale, new_rot, new_feat, positions, scales, rotations, colors,
+                                               alive, age, error, n_spawned, scratch, as_stream(stream)));
+    return OSS_OK;
+}
+
 int64_t oss_tile_bin_counting_sort_scratch_bytes(int64_t n, int64_t num_tiles) {
     if (n < 0) n = 0;
     if (num_tiles < 0) num_tiles = 0;

@@ -96,6 +96,30 @@ int64_t depth_order_scratch_bytes(int64_t n);
 cudaError_t depth_order(int n, const float* depth, int32_t* order, int32_t* rank, void* scratch,
                         cudaStream_t stream);
 
+// ---- canvas_life.cu -----------------------------------------------------------
+// Persistent-canvas lifecycle: tile error against the (upsampled) LR frame,
+// per-slot error and age, the prune decision tree, spawn-tile ranking and the
+// prune/spawn slot update.  Counts and lists stay on the device.
+cudaError_t launch_tile_mse(int f, int h, int w, int ts, const float* rendered, int hl, int wl, const float* target,
+                            float* tile_err, cudaStream_t stream);
+cudaError_t launch_canvas_error(int n, int h, int w, int ts, const float* xy, const uint8_t* in_frame,
+                                const float* tile_err, const uint8_t* alive, int64_t* age, float* g_error,
+                                float* error, cudaStream_t stream);
+int64_t prune_scratch_bytes(int64_t n);
+cudaError_t launch_select_for_pruning(int n, const uint8_t* alive, const uint8_t* in_frame, const int64_t* age,
+                                      const float* err, long long cap, long long age_max, float q_age, float q_tile,
+                                      long long min_age, int64_t* prune_idx, int64_t* prune_count, float* quant,
+                                      void* scratch, cudaStream_t stream);
+int64_t spawn_tiles_scratch_bytes(int64_t num_tiles);
+cudaError_t launch_select_spawn_tiles(int th, int tw, const float* tile_err, const uint8_t* cls, long long n_tiles,
+                                      int64_t* tiles_yx, int64_t* take, void* scratch, cudaStream_t stream);
+int64_t prune_spawn_scratch_bytes(int64_t n);
+cudaError_t launch_apply_prune_spawn(int n, int f, const int64_t* prune_idx, const int64_t* prune_count,
+                                     int64_t max_prune, int num_new, int f_new, const float* nxy,
+                                     const float* nscale, const float* nrot, const float* nfeat, float* positions,
+                                     float* scales, float* rotations, float* colors, uint8_t* alive, int64_t* age,
+                                     float* error, int64_t* n_spawned, void* scratch, cudaStream_t stream);
+
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);
 cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,

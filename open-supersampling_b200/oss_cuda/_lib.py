@@ -79,6 +79,19 @@ SIGNATURES = {
          _p, _i64, _p],
     ),
     "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
+    "oss_tile_mse": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p]),
+    "oss_canvas_error": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_prune_scratch_bytes": (_i64, [_i64]),
+    "oss_select_for_pruning": (
+        ctypes.c_int,
+        [_i64, _p, _p, _p, _p, _i64, _i64, ctypes.c_double, ctypes.c_double, _i64, ctypes.c_double, _p, _p, _p, _p,
+         _i64, _p]),
+    "oss_spawn_tiles_scratch_bytes": (_i64, [_i64]),
+    "oss_select_spawn_tiles": (ctypes.c_int, [_i64, _i64, _p, _p, _i64, _p, _p, _p, _i64, _p]),
+    "oss_prune_spawn_scratch_bytes": (_i64, [_i64]),
+    "oss_apply_prune_spawn": (
+        ctypes.c_int,
+        [_i64, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_tile_bin_counting_sort_noalloc": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p]),
     "oss_tile_bin_counting_sort_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_tile_bin_counting_sort": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),
