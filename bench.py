@@ -54,7 +54,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5"], default="config2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5", "canvas"],
+                    default="config2")
     ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -927,14 +928,92 @@ def run_config5(args, rank, world):
                      allreduce_ms_last_step=allreduce, frames_per_rank=len(frames))
 
 
+def run_canvas(args, rank, world):
+    """Persistent-canvas lifecycle (oss/gaussian/canvas/canvas.py:191-295), one
+    canvas per rank: 200k slots seeded with config-2 Gaussians, rendered at
+    1088x1920 (the canvas needs sizes that are multiples of the 16-px tile); per
+    frame a smooth motion field at the output size, an LR frame at half size
+    and 5,000 replacement Gaussians.  A step is one PersistentCanvas.update:
+    warp, age, render, tile error against the upsampled LR frame, per-slot
+    error, decision tree, spawn-tile ranking and slot update, statistics read
+    back.  The tile-error kernel and the decision tree are also timed alone."""
+    from oss_b200 import GaussianBatch, PersistentCanvas, per_tile_mse_lr
+
+    h, w, n = 1088, 1920, 200_000
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = make_inputs(h, w, n, math.log(2.0), 0.3, seed=2024 + rank)
+    canvas = PersistentCanvas(capacity=n, feat_dim=3, output_hw=(h, w), device=device)
+    t = {k: torch.from_numpy(v).to(device) for k, v in inp.items()}
+    canvas.initialize_from_batch(GaussianBatch(t["xy"], t["scale"], t["rot"], t["rgb"]))
+    canvas.age = torch.from_numpy(np.random.default_rng(3).integers(0, 90, n)).to(device)
+    frames = 4
+    motions = [torch.from_numpy(smooth_motion(h, w, 900 + f, max_mag=4.0)).to(device) for f in range(frames)]
+    lrs = [torch.rand((3, h // 2, w // 2), device=device, generator=torch.Generator(device=device).manual_seed(f))
+           for f in range(frames)]
+    news = []
+    for f in range(frames):
+        b = make_inputs(h, w, 5000, math.log(2.0), 0.3, seed=7000 + f)
+        news.append(GaussianBatch(*(torch.from_numpy(b[k]).to(device) for k in ("xy", "scale", "rot", "rgb"))))
+    state = {"i": 0, "pruned": 0}
+
+    def step():
+        i = state["i"] % frames
+        st = canvas.update(motions[i], lrs[i], new_gaussians=news[i])
+        state["i"] += 1
+        state["pruned"] += st.n_pruned
+
+    ms, clocks = timed(step, args.steps, args.warmup, device, world)
+
+    # device time of the tile-error kernel and of the decision tree alone: a ~1 ms
+    # clock-bounded delay kernel queued ahead of each call lets the host enqueue
+    # the call before the GPU reaches it, so host overhead stays out
+    from oss_b200.persistent_canvas import _prune_device
+
+    def device_ms(fn, reps=max(3, min(args.steps, 20))):
+        flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fn()
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            torch.cuda._sleep(2_000_000)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        return total / reps
+
+    rendered = canvas.render()
+    lr = lrs[0]
+    ms_mse = device_ms(lambda: per_tile_mse_lr(rendered, lr, 16))
+    alive_u8 = canvas.alive.view(torch.uint8)
+    frame_u8 = torch.ones_like(alive_u8)
+    ms_prune = device_ms(lambda: _prune_device(alive_u8, frame_u8, canvas.age, canvas.error, n, canvas.policy))
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    mse_bytes = 3 * h * w * 4 + 3 * (h // 2) * (w // 2) * 4 + (h // 16) * (w // 16) * 4
+    value = h * w / (ms * 1e-3) / 1e6
+    return base_line(args, world, value, ms, f"canvas: PersistentCanvas.update, {n} slots at {w}x{h}, F=3, LR "
+                     f"{w // 2}x{h // 2}, 5000 replacements per frame, one canvas per rank", "weak", clocks,
+                     ms_per_update=ms, pruned_per_update=state["pruned"] / max(1, state["i"]),
+                     tile_mse={"ms": ms_mse, "bytes": mse_bytes,
+                               "roofline": {"bound": "hbm", "achieved": mse_bytes / (ms_mse * 1e-3) / 1e9,
+                                            "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                                            "frac": (mse_bytes / (ms_mse * 1e-3) / 1e9) / peaks["hbm_gbs"]
+                                            if peaks.get("hbm_gbs") else None}},
+                     select_for_pruning_ms=ms_prune)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.config in ("config3", "config4", "config5"):
-            line = {"config3": run_config3, "config4": run_config4, "config5": run_config5}[args.config](
+        elif args.config in ("config3", "config4", "config5", "canvas"):
+            line = {"config3": run_config3, "config4": run_config4, "config5": run_config5,
+                    "canvas": run_canvas}[args.config](
                 args, rank, world)
             if rank == 0:
                 print(json.dumps(line), flush=True)

@@ -39,25 +39,42 @@ struct LrFrame {
     int same;      // already at the HR size: read it directly
 };
 
-__device__ __forceinline__ float lr_tap(const LrFrame& f, int c, int y, int x) {
-    return __ldg(f.p + (static_cast<int64_t>(c) * f.hl + y) * f.wl + x);
-}
+// Bilinear taps of HR texel (i, j) in F.interpolate(frame, (h, w), bilinear,
+// align_corners=False): LR offsets of the four neighbours and their weights.
+struct Taps {
+    int o00, o01, o10, o11;
+    float lx0, lx1, ly0, ly1;
+};
 
-// Texel (i, j) of F.interpolate(frame, (h, w), bilinear, align_corners=False).
-__device__ float target_at(const LrFrame& f, int c, int i, int j) {
-    if (f.same) return lr_tap(f, c, i, j);
+__device__ __forceinline__ Taps taps_at(const LrFrame& f, int i, int j) {
+    Taps t;
+    if (f.same) {
+        t.o00 = t.o01 = t.o10 = t.o11 = i * f.wl + j;
+        t.lx0 = t.ly0 = 1.0f;
+        t.lx1 = t.ly1 = 0.0f;
+        return t;
+    }
     float sy = __fsub_rn(__fmul_rn(f.sy, __fadd_rn(static_cast<float>(i), 0.5f)), 0.5f);
     if (sy < 0.0f) sy = 0.0f;
     float sx = __fsub_rn(__fmul_rn(f.sx, __fadd_rn(static_cast<float>(j), 0.5f)), 0.5f);
     if (sx < 0.0f) sx = 0.0f;
     const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
     const int y1 = y0 + (y0 < f.hl - 1 ? 1 : 0), x1 = x0 + (x0 < f.wl - 1 ? 1 : 0);
-    const float ly1 = __fsub_rn(sy, static_cast<float>(y0));
-    const float lx1 = __fsub_rn(sx, static_cast<float>(x0));
-    const float ly0 = __fsub_rn(1.0f, ly1), lx0 = __fsub_rn(1.0f, lx1);
-    const float top = __fadd_rn(__fmul_rn(lx0, lr_tap(f, c, y0, x0)), __fmul_rn(lx1, lr_tap(f, c, y0, x1)));
-    const float bot = __fadd_rn(__fmul_rn(lx0, lr_tap(f, c, y1, x0)), __fmul_rn(lx1, lr_tap(f, c, y1, x1)));
-    return __fadd_rn(__fmul_rn(ly0, top), __fmul_rn(ly1, bot));
+    t.ly1 = __fsub_rn(sy, static_cast<float>(y0));
+    t.lx1 = __fsub_rn(sx, static_cast<float>(x0));
+    t.ly0 = __fsub_rn(1.0f, t.ly1);
+    t.lx0 = __fsub_rn(1.0f, t.lx1);
+    t.o00 = y0 * f.wl + x0;
+    t.o01 = y0 * f.wl + x1;
+    t.o10 = y1 * f.wl + x0;
+    t.o11 = y1 * f.wl + x1;
+    return t;
+}
+
+__device__ __forceinline__ float bilerp(const Taps& t, float v00, float v01, float v10, float v11) {
+    const float top = __fadd_rn(__fmul_rn(t.lx0, v00), __fmul_rn(t.lx1, v01));
+    const float bot = __fadd_rn(__fmul_rn(t.lx0, v10), __fmul_rn(t.lx1, v11));
+    return __fadd_rn(__fmul_rn(t.ly0, top), __fmul_rn(t.ly1, bot));
 }
 
 // Fixed-order block sum (warp trees, then the warp totals in warp order).
@@ -72,6 +89,37 @@ __device__ float block_sum(float v, float* s_warp) {
     return t;
 }
 
+// Squared difference of pixel (y, x) summed over channels [c0, c0 + NC): every
+// load of the NC channels is issued before the first is used.
+template <int NC>
+__device__ __forceinline__ float pixel_sq(const float* __restrict__ rendered, int64_t plane, int64_t pix,
+                                          const LrFrame& f, const Taps& t, int c0, int F, float s) {
+    const int64_t lplane = static_cast<int64_t>(f.hl) * f.wl;
+    float r[NC], v[NC][4];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = c0 + k < F ? c0 + k : F - 1;
+        const float* lp = f.p + c * lplane;
+        r[k] = __ldg(rendered + c * plane + pix);
+        v[k][0] = __ldg(lp + t.o00);
+        v[k][1] = __ldg(lp + t.o01);
+        v[k][2] = __ldg(lp + t.o10);
+        v[k][3] = __ldg(lp + t.o11);
+    }
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        if (c0 + k < F) {
+            const float d = __fsub_rn(r[k], f.same ? v[k][0] : bilerp(t, v[k][0], v[k][1], v[k][2], v[k][3]));
+            s = __fadd_rn(s, __fmul_rn(d, d));
+        }
+    }
+    return s;
+}
+
+// One CTA per tile.  Per pixel the channel mean of the squared difference to the
+// target texel, then the tile mean; channels run in groups of NC (F itself up to
+// 4) whose loads are all in flight together.
+template <int NC>
 __global__ void __launch_bounds__(kThreads) k_tile_mse(int F, int H, int W, int ts, int ntx,
                                                        const float* __restrict__ rendered, LrFrame tgt,
                                                        float* __restrict__ tile_err) {
@@ -84,15 +132,114 @@ __global__ void __launch_bounds__(kThreads) k_tile_mse(int F, int H, int W, int 
     for (int p = threadIdx.x; p < ts * ts; p += kThreads) {
         const int y = ty * ts + p / ts, x = tx * ts + p % ts;
         const int64_t pix = static_cast<int64_t>(y) * W + x;
+        const Taps t = taps_at(tgt, y, x);
         float s = 0.0f;
-        for (int c = 0; c < F; ++c) {
-            const float d = __fsub_rn(__ldg(rendered + c * plane + pix), target_at(tgt, c, y, x));
-            s = __fadd_rn(s, __fmul_rn(d, d));
-        }
+        for (int c0 = 0; c0 < F; c0 += NC) s = pixel_sq<NC>(rendered, plane, pix, tgt, t, c0, F, s);
         acc += __fdiv_rn(s, ff);
     }
     const float total = block_sum(acc, s_warp);
     if (threadIdx.x == 0) tile_err[tile] = __fdiv_rn(total, static_cast<float>(ts * ts));
+}
+
+// The 16x16-tile path for an LR frame at most the render's size (or the same
+// size): a CTA of 64 threads per tile, each thread four adjacent pixels of one
+// row read as a float4 per channel, and the LR texels the tile's taps touch
+// (at most 18 x 18 per channel when upsampling) staged in shared memory once.
+constexpr int kMseThreads = 64;
+constexpr int kPatch = 18;
+
+__device__ __forceinline__ float src_coord(float scale, int i) {
+    const float v = __fsub_rn(__fmul_rn(scale, __fadd_rn(static_cast<float>(i), 0.5f)), 0.5f);
+    return v < 0.0f ? 0.0f : v;
+}
+
+template <int NC, bool SAME>
+__global__ void __launch_bounds__(kMseThreads) k_tile_mse16(int F, int H, int W, int ntx,
+                                                            const float* __restrict__ rendered, LrFrame tgt,
+                                                            float* __restrict__ tile_err) {
+    __shared__ float s_lr[NC][kPatch][kPatch];
+    __shared__ float s_warp[kMseThreads / 32];
+    const int tile = blockIdx.x;
+    const int ty = tile / ntx, tx = tile - (tile / ntx) * ntx;
+    const int y = ty * 16 + (threadIdx.x >> 2);
+    const int xq = tx * 16 + (threadIdx.x & 3) * 4;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    const int64_t pix = static_cast<int64_t>(y) * W + xq;
+    // this thread's row taps and the patch origin (the tile's first source texel)
+    int py0 = 0, py1 = 0;
+    float wy0 = 1.0f, wy1 = 0.0f;
+    int oy = 0, ox = 0;
+    if (!SAME) {
+        oy = static_cast<int>(src_coord(tgt.sy, ty * 16));
+        ox = static_cast<int>(src_coord(tgt.sx, tx * 16));
+        const float sy = src_coord(tgt.sy, y);
+        const int y0 = static_cast<int>(sy);
+        const int y1 = y0 + (y0 < tgt.hl - 1 ? 1 : 0);
+        wy1 = __fsub_rn(sy, static_cast<float>(y0));
+        wy0 = __fsub_rn(1.0f, wy1);
+        py0 = y0 - oy;
+        py1 = y1 - oy;
+    }
+    const int64_t lplane = static_cast<int64_t>(tgt.hl) * tgt.wl;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c0 = 0; c0 < F; c0 += NC) {
+        float4 r[NC], t4[NC];
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = c0 + k < F ? c0 + k : F - 1;
+            r[k] = __ldg(reinterpret_cast<const float4*>(rendered + c * plane + pix));
+            if (SAME) t4[k] = __ldg(reinterpret_cast<const float4*>(tgt.p + c * plane + pix));
+        }
+        if (!SAME) {
+            __syncthreads();  // the previous group's patch is no longer read
+            for (int e = threadIdx.x; e < NC * kPatch * kPatch; e += kMseThreads) {
+                const int k = e / (kPatch * kPatch), rem = e - k * kPatch * kPatch;
+                const int i = rem / kPatch, j = rem - (rem / kPatch) * kPatch;
+                const int c = c0 + k < F ? c0 + k : F - 1;
+                const int yy = min(oy + i, tgt.hl - 1), xx = min(ox + j, tgt.wl - 1);
+                s_lr[k][i][j] = __ldg(tgt.p + c * lplane + static_cast<int64_t>(yy) * tgt.wl + xx);
+            }
+            __syncthreads();
+#pragma unroll 1
+            for (int k = 0; k < NC; ++k) {
+                if (c0 + k >= F) continue;
+                float4 rk = r[0];  // r[k] by selects, so r stays in registers in the rolled loop
+#pragma unroll
+                for (int u = 1; u < NC; ++u) rk = k == u ? r[u] : rk;
+                const float rv[4] = {rk.x, rk.y, rk.z, rk.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float sx = src_coord(tgt.sx, xq + q);
+                    const int x0 = static_cast<int>(sx);
+                    const int x1 = x0 + (x0 < tgt.wl - 1 ? 1 : 0);
+                    const float wx1 = __fsub_rn(sx, static_cast<float>(x0));
+                    const float wx0 = __fsub_rn(1.0f, wx1);
+                    const int j0 = x0 - ox, j1 = x1 - ox;
+                    const float top = __fadd_rn(__fmul_rn(wx0, s_lr[k][py0][j0]), __fmul_rn(wx1, s_lr[k][py0][j1]));
+                    const float bot = __fadd_rn(__fmul_rn(wx0, s_lr[k][py1][j0]), __fmul_rn(wx1, s_lr[k][py1][j1]));
+                    const float d = __fsub_rn(rv[q], __fadd_rn(__fmul_rn(wy0, top), __fmul_rn(wy1, bot)));
+                    s[q] = __fadd_rn(s[q], __fmul_rn(d, d));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                if (c0 + k >= F) continue;
+                const float d0 = __fsub_rn(r[k].x, t4[k].x), d1 = __fsub_rn(r[k].y, t4[k].y);
+                const float d2 = __fsub_rn(r[k].z, t4[k].z), d3 = __fsub_rn(r[k].w, t4[k].w);
+                s[0] = __fadd_rn(s[0], __fmul_rn(d0, d0));
+                s[1] = __fadd_rn(s[1], __fmul_rn(d1, d1));
+                s[2] = __fadd_rn(s[2], __fmul_rn(d2, d2));
+                s[3] = __fadd_rn(s[3], __fmul_rn(d3, d3));
+            }
+        }
+    }
+    const float ff = static_cast<float>(F);
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc += __fdiv_rn(s[q], ff);
+    const float total = block_sum(acc, s_warp);
+    if (threadIdx.x == 0) tile_err[tile] = __fdiv_rn(total, 256.0f);
 }
 
 // Per slot: the error of the tile holding its centre (+inf outside the frame or
@@ -308,7 +455,25 @@ cudaError_t launch_tile_mse(int f, int h, int w, int ts, const float* rendered, 
     if (ntx == 0 || nty == 0) return cudaSuccess;
     LrFrame t{target, hl, wl, h, w, static_cast<float>(hl) / static_cast<float>(h),
               static_cast<float>(wl) / static_cast<float>(w), hl == h && wl == w ? 1 : 0};
-    k_tile_mse<<<static_cast<unsigned>(ntx * nty), kThreads, 0, stream>>>(f, h, w, ts, ntx, rendered, t, tile_err);
+    const unsigned grid = static_cast<unsigned>(ntx * nty);
+    // 16-px tiles over float4-aligned rows, with an LR frame no larger than the render
+    const bool vec = ts == 16 && w % 4 == 0 && (reinterpret_cast<uintptr_t>(rendered) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(target) & 15) == 0 && hl <= h && wl <= w;
+    if (vec) {
+#define OSS_MSE16(NC)                                                                                 \
+    (t.same ? k_tile_mse16<NC, true><<<grid, kMseThreads, 0, stream>>>(f, h, w, ntx, rendered, t, tile_err) \
+            : k_tile_mse16<NC, false><<<grid, kMseThreads, 0, stream>>>(f, h, w, ntx, rendered, t, tile_err))
+        if (f == 1) OSS_MSE16(1);
+        else if (f == 2) OSS_MSE16(2);
+        else if (f == 3) OSS_MSE16(3);
+        else OSS_MSE16(4);
+#undef OSS_MSE16
+        return cudaGetLastError();
+    }
+    if (f == 1) k_tile_mse<1><<<grid, kThreads, 0, stream>>>(f, h, w, ts, ntx, rendered, t, tile_err);
+    else if (f == 2) k_tile_mse<2><<<grid, kThreads, 0, stream>>>(f, h, w, ts, ntx, rendered, t, tile_err);
+    else if (f == 3) k_tile_mse<3><<<grid, kThreads, 0, stream>>>(f, h, w, ts, ntx, rendered, t, tile_err);
+    else k_tile_mse<4><<<grid, kThreads, 0, stream>>>(f, h, w, ts, ntx, rendered, t, tile_err);
     return cudaGetLastError();
 }
 

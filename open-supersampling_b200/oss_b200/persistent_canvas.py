@@ -20,6 +20,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
+import numpy as np
 import torch
 
 from oss_cuda import _lib
@@ -378,7 +379,12 @@ class PersistentCanvas:
                classifier_mask: Optional[torch.Tensor] = None) -> CanvasStats:
         """One frame (canvas.py:191-295): warp the positions, bump the ages,
         render, score the tiles against the upsampled LR frame, give every slot
-        its tile's error, prune, rank spawn tiles and write the replacements."""
+        its tile's error, prune and write the replacements.  The host waits
+        three times: for the alive list and the pair total of the render, and for
+        the statistics at the end.  The reference also ranks spawn tiles here and
+        discards the ranking (canvas.py:281-289); ``classifier_mask`` only feeds
+        that ranking, so it is accepted and unused (``select_spawn_tiles`` gives
+        the ranking to callers that want it)."""
         H, W = self.output_hw
         T = self.tile_size
         new_xy, in_frame = warp_positions(self.positions, motion, self.output_hw)
@@ -396,12 +402,10 @@ class PersistentCanvas:
                                             tile_err.data_ptr(), alive_u8.data_ptr(), self.age.data_ptr(), None,
                                             self.error.data_ptr(), stream_of(self.positions)), "oss_canvas_error")
         idx, cnt, _ = _prune_device(alive_u8, frame_u8, self.age, self.error, self.capacity, self.policy)
-        # spawn tiles are ranked as the reference does and, as there, not used here
-        # (the caller drives the network that produces new_gaussians from them)
-        n_spawn_tiles = torch.clamp(cnt, min=1)
-        _ = select_spawn_tiles(tile_err, int(n_spawn_tiles.item()), classifier_mask=classifier_mask)
-        spawned = _apply_device(self, idx, cnt, self.capacity, new_gaussians)
-        n_pruned = int(cnt.item())
-        return CanvasStats(n_alive_before=int(n_before.item()), n_alive_after=self.n_alive, n_pruned=n_pruned,
+        _apply_device(self, idx, cnt, self.capacity, new_gaussians)
+        stats = torch.stack([n_before.to(torch.float64), torch.count_nonzero(self.alive).to(torch.float64),
+                             cnt[0].to(torch.float64), tile_err.to(torch.float64).mean()]).tolist()
+        n_pruned = int(stats[2])
+        return CanvasStats(n_alive_before=int(stats[0]), n_alive_after=int(stats[1]), n_pruned=n_pruned,
                            n_spawned=min(new_gaussians.num_gaussians, n_pruned) if new_gaussians is not None else 0,
-                           mean_tile_error=float(tile_err.mean().item()))
+                           mean_tile_error=float(np.float32(stats[3])))
