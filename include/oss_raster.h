@@ -373,6 +373,29 @@ OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, in
 OSS_API int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, float alpha,
                                const float* xy, float* out_xy, uint8_t* in_frame, void* stream);
 
+/* ---- v7 N-D time-slice splat (oss/sr/v7/nd_rasterizer.py:107-165) ----
+ * After the time conditioning every Gaussian is a 2D Gaussian: mean xy (n x 2), inverse covariance
+ * conic (n x 3: a, b, d with q = a dx^2 + 2 b dx dy + d dy^2), amplitude amp (n), features feat
+ * (n x f, f <= 32) and a cull box (n x 4 int32: x0, y0, x1, y1 in pixels).  out[c](i, j) = sum over
+ * Gaussians whose box holds (j, i) of feat[c] * amp * exp(-q / 2) at dx = j + 0.5 - x, dy = i + 0.5 - y.
+ *
+ * oss_nd_prepare is oss_render_prepare for these inputs (tiles = those the box overlaps; prec holds
+ * oss_nd_record_floats(f) floats per Gaussian); bin with oss_bin_pairs(mode OSS_BIN_TIGHT3SIGMA), then
+ * oss_nd_forward.  oss_nd_backward_pairs writes the per-pair rows of oss_render_backward_pairs
+ * (pair_stride = oss_pair_grad_stride(f)); oss_reduce_pair_grads with opacity = amp and no scale / rot
+ * turns them into d_xy, d_conic, d_feat and d_amp (its d_opacity). */
+OSS_API int64_t oss_nd_record_floats(int64_t f);
+OSS_API int oss_nd_prepare(int64_t n, int64_t h, int64_t w, const float* xy, const float* conic, const int32_t* box,
+                           int64_t f, const float* feat, const float* amp, int32_t* aabb, int32_t* pair_offset,
+                           float* geo, float* prec, int64_t* total_pairs, int32_t* tile_count,
+                           int32_t* tile_offsets, void* scratch, int64_t scratch_bytes, void* stream);
+OSS_API int oss_nd_forward(int64_t f, int64_t h, int64_t w, const float* prec, const int32_t* box,
+                           const int32_t* gid_sorted, const int32_t* tile_offsets, float* image, void* stream);
+OSS_API int oss_nd_backward_pairs(int64_t f, int64_t h, int64_t w, const float* prec, const int32_t* box,
+                                  const int32_t* gid_sorted, const int32_t* tile_offsets, const int32_t* aabb,
+                                  const int32_t* pair_offset, const float* grad_image, float* pairgrad,
+                                  void* stream);
+
 /* ---- Persistent-canvas lifecycle (oss/gaussian/canvas/canvas.py:191-295) ----
  * The steps around the render in PersistentCanvas.update, all on the device.
  * Masks are uint8 (0 / 1), ages int64, everything else fp32. */

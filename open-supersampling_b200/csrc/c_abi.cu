@@ -571,6 +571,79 @@ int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, flo
     return OSS_OK;
 }
 
+int64_t oss_nd_record_floats(int64_t f) { return f < 1 || f > 32 ? 0 : oss::nd_record_floats(static_cast<int>(f)); }
+
+int oss_nd_prepare(int64_t n, int64_t h, int64_t w, const float* xy, const float* conic, const int32_t* box,
+                   int64_t f, const float* feat, const float* amp, int32_t* aabb, int32_t* pair_offset, float* geo,
+                   float* prec, int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets, void* scratch,
+                   int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 1 && f <= 32, OSS_ERR_INVALID, "F must be in [1, 32]");
+    OSS_CHECK(pair_offset != nullptr && total_pairs != nullptr, OSS_ERR_INVALID,
+              "pair_offset and total_pairs must be non-null");
+    OSS_CHECK(g.tiles == 0 || (tile_count != nullptr && tile_offsets != nullptr), OSS_ERR_INVALID,
+              "tile_count and tile_offsets must be non-null");
+    OSS_CHECK(scratch_bytes >= oss_render_prepare_scratch_bytes(n), OSS_ERR_SCRATCH, "nd_prepare scratch too small");
+    if (g.n > 0) {
+        OSS_CHECK(xy != nullptr && conic != nullptr && box != nullptr && feat != nullptr && amp != nullptr &&
+                      aabb != nullptr && geo != nullptr && prec != nullptr,
+                  OSS_ERR_INVALID, "inputs and outputs must be non-null");
+        OSS_CHECK(aligned(xy, 8) && aligned(box, 16) && aligned(aabb, 16) && aligned(geo, 16) && aligned(prec, 16),
+                  OSS_ERR_INVALID, "xy (8), box, aabb, geo and prec (16) must be aligned");
+    }
+    cudaStream_t s = as_stream(stream);
+    long long* block_sums = static_cast<long long*>(scratch);
+    OSS_CHECK(g.n == 0 || (block_sums != nullptr && aligned(block_sums, 8)), OSS_ERR_INVALID,
+              "scratch must be 8-byte aligned");
+    int32_t* counts = g.tiles > 0 ? tile_count : nullptr;
+    if (counts != nullptr) {
+        OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
+    }
+    if (g.n > 0) {
+        OSS_CUDA_TRY(oss::launch_nd_preprocess(g.n, g.ntx, g.nty, xy, conic, box, static_cast<int>(f), feat, amp,
+                                               aabb, pair_offset, geo, prec, block_sums, counts, s));
+    }
+    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, counts,
+                                                 oss::kTileCountStride, g.tiles, counts != nullptr ? tile_offsets : nullptr,
+                                                 s));
+    return OSS_OK;
+}
+
+int oss_nd_forward(int64_t f, int64_t h, int64_t w, const float* prec, const int32_t* box, const int32_t* gid_sorted,
+                   const int32_t* tile_offsets, float* image, void* stream) {
+    Grid g;
+    int rc = check_grid(0, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 1 && f <= 32, OSS_ERR_INVALID, "F must be in [1, 32]");
+    if (g.tiles == 0) return OSS_OK;
+    OSS_CHECK(prec != nullptr && box != nullptr && gid_sorted != nullptr && tile_offsets != nullptr &&
+                  image != nullptr && aligned(prec, 16) && aligned(box, 16),
+              OSS_ERR_INVALID, "pointers must be non-null (prec and box 16-byte aligned)");
+    OSS_CUDA_TRY(oss::launch_nd_forward(static_cast<int>(f), g.h, g.w, prec, box, gid_sorted, tile_offsets, image,
+                                        as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_nd_backward_pairs(int64_t f, int64_t h, int64_t w, const float* prec, const int32_t* box,
+                          const int32_t* gid_sorted, const int32_t* tile_offsets, const int32_t* aabb,
+                          const int32_t* pair_offset, const float* grad_image, float* pairgrad, void* stream) {
+    Grid g;
+    int rc = check_grid(0, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 1 && f <= 32, OSS_ERR_INVALID, "F must be in [1, 32]");
+    if (g.tiles == 0) return OSS_OK;
+    OSS_CHECK(prec != nullptr && box != nullptr && gid_sorted != nullptr && tile_offsets != nullptr && aabb != nullptr &&
+                  pair_offset != nullptr && grad_image != nullptr && pairgrad != nullptr && aligned(prec, 16) &&
+                  aligned(box, 16) && aligned(aabb, 16),
+              OSS_ERR_INVALID, "pointers must be non-null (prec, box and aabb 16-byte aligned)");
+    OSS_CUDA_TRY(oss::launch_nd_backward_pairs(static_cast<int>(f), g.h, g.w, prec, box, gid_sorted, tile_offsets,
+                                               aabb, pair_offset, grad_image, pairgrad,
+                                               oss::backward_pair_stride(static_cast<int>(f)), as_stream(stream)));
+    return OSS_OK;
+}
+
 int oss_tile_mse(int64_t f, int64_t h, int64_t w, int64_t ts, const float* rendered, int64_t target_h,
                  int64_t target_w, const float* target, float* tile_err, void* stream) {
     OSS_CHECK(f > 0 && f <= INT_MAX, OSS_ERR_INVALID, "F must be positive");

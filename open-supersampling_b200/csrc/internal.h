@@ -120,6 +120,24 @@ cudaError_t launch_apply_prune_spawn(int n, int f, const int64_t* prune_idx, con
                                      float* scales, float* rotations, float* colors, uint8_t* alive, int64_t* age,
                                      float* error, int64_t* n_spawned, void* scratch, cudaStream_t stream);
 
+// ---- nd.cu -------------------------------------------------------------------
+// Splat of the v7 time-slice rasterizer: 2D Gaussians given by mean, inverse
+// covariance (a, b, d), amplitude, features and a pixel cull box, evaluated at
+// pixel centres inside the box.  The preprocess feeds the additive path's scan
+// and binning; the backward writes its per-pair rows (reduced by
+// launch_reduce_gaussian_grads with the amplitude as opacity).
+int nd_record_floats(int f);
+cudaError_t launch_nd_preprocess(int n, int ntx, int nty, const float* xy, const float* conic, const int32_t* box,
+                                 int f, const float* feat, const float* amp, int32_t* aabb, int32_t* count,
+                                 float* geo, float* prec, long long* block_sums, int32_t* tile_count,
+                                 cudaStream_t stream);
+cudaError_t launch_nd_forward(int f, int h, int w, const float* prec, const int32_t* box, const int32_t* gid_sorted,
+                              const int32_t* tile_offsets, float* image, cudaStream_t stream);
+cudaError_t launch_nd_backward_pairs(int f, int h, int w, const float* prec, const int32_t* box,
+                                     const int32_t* gid_sorted, const int32_t* tile_offsets, const int32_t* aabb,
+                                     const int32_t* pair_offset, const float* grad_image, float* pairgrad,
+                                     int pair_stride, cudaStream_t stream);
+
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);
 cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,

@@ -1,0 +1,272 @@
+// Splat of the v7 N-D time-slice rasterizer (oss/sr/v7/nd_rasterizer.py:107-165,
+// _evaluate_2d_gaussian_at_pixels): after the time conditioning, each Gaussian is
+// a 2D Gaussian with a mean, an inverse covariance (a, b, d), an amplitude
+// (opacity x time weight x Mip factors) and R features, evaluated at pixel
+// centres (j + 0.5, i + 0.5) inside its own cull box [x0, x1) x [y0, y1) --
+// 3 sqrt(largest eigenvalue) around the mean, the reference's loop bound -- and
+// zero outside it.  Its sum is
+//   out[c](i, j) = sum_g feat[g][c] * amp[g] * exp(-q_g / 2), (i, j) in box_g.
+//
+// The lists come from the same tile binning as the additive render: a Gaussian
+// covers the tiles its box overlaps.  The preprocess here writes the packed
+// record (x - 0.5, y - 0.5, A, B | D, feat * amp) of the additive forward, so
+// dx = j - (x - 0.5) equals the reference's (j + 0.5) - x exactly, and q' =
+// dx (A dx + B dy) + D dy^2 with (A, B, D) = (a, 2b, d) * (-log2(e) / 2); the
+// per-pixel test against the box is the only difference from the additive
+// kernels.  The backward writes the additive backward's per-pair rows (Sx, Sy,
+// d_conic, dF) over the box's pixels of each tile, so the per-Gaussian reduce of
+// the additive path turns them into d_xy, d_conic, d_feat and d_amp.
+#include "internal.h"
+#include "oss_common.cuh"
+
+namespace oss {
+namespace {
+
+constexpr int kNdThreads = 256;  // one pixel per thread, one CTA per tile
+constexpr int kNdBatch = 64;     // list entries staged per batch
+
+template <int FC>
+struct NdCfg {
+    static constexpr int S = ((1 + FC + 3) / 4) * 4;  // [D, feat * amp] floats, the additive record's tail
+    static constexpr int RS = 4 + S;                  // record floats
+};
+
+__global__ void __launch_bounds__(kPreprocThreads) k_nd_preprocess(
+    int n, int ntx, int nty, const float2* __restrict__ xy, const float* __restrict__ conic,
+    const int4* __restrict__ box, int F, int prs, const float* __restrict__ feat, const float* __restrict__ amp,
+    int4* __restrict__ aabb, int32_t* __restrict__ count, float* __restrict__ geo, float* __restrict__ prec,
+    long long* __restrict__ block_sums, int32_t* __restrict__ tile_count) {
+    long long local = 0;
+    const int g = blockIdx.x * kPrepTile + threadIdx.x;
+    if (g < n) {
+        const float2 c = xy[g];
+        const float x = __fsub_rn(c.x, 0.5f), y = __fsub_rn(c.y, 0.5f);
+        const float a = conic[3 * g + 0], b = conic[3 * g + 1], d = conic[3 * g + 2];
+        const int4 bx = box[g];  // (x0, y0, x1, y1) in pixels
+        int4 t = make_int4(0, 0, 0, 0);
+        int cnt = 0;
+        if (bx.z > bx.x && bx.w > bx.y) {
+            t = make_int4(bx.x / kTile, bx.y / kTile, min(ntx, (bx.z + kTile - 1) / kTile),
+                          min(nty, (bx.w + kTile - 1) / kTile));
+            cnt = (t.z - t.x) * (t.w - t.y);
+        }
+        aabb[g] = t;
+        count[g] = cnt;
+        local = cnt;
+        const float A = a * kNegHalfLog2e, B = (2.0f * b) * kNegHalfLog2e, D = d * kNegHalfLog2e;
+        float4* gr = reinterpret_cast<float4*>(geo + static_cast<int64_t>(g) * 8);
+        gr[0] = make_float4(x, y, A, B);
+        gr[1] = make_float4(D, a, b, d);
+        float4* rec = reinterpret_cast<float4*>(prec + static_cast<int64_t>(g) * prs);
+        rec[0] = make_float4(x, y, A, B);
+        const float op = amp[g];
+        for (int v = 1; v < prs / 4; ++v) {
+            float e[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = 4 * v + u;
+                e[u] = i == 4 ? D : (i - 5 < F ? feat[static_cast<int64_t>(g) * F + (i - 5)] * op : 0.0f);
+            }
+            rec[v] = make_float4(e[0], e[1], e[2], e[3]);
+        }
+        for (int ty = t.y; ty < t.w; ++ty) {
+            for (int tx = t.x; tx < t.z; ++tx) {
+                atomicAdd(&tile_count[static_cast<int64_t>(ty * ntx + tx) * kTileCountStride], 1);
+            }
+        }
+    }
+    __shared__ long long s_part[kPreprocThreads / 32];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long tot = 0;
+#pragma unroll
+        for (int w = 0; w < kPreprocThreads / 32; ++w) tot += s_part[w];
+        block_sums[blockIdx.x] = tot;
+    }
+}
+
+template <int FC>
+__global__ void __launch_bounds__(kNdThreads) k_nd_fwd(int F, int H, int W, int ntx, const float* __restrict__ prec,
+                                                        const int4* __restrict__ box,
+                                                        const int32_t* __restrict__ gid_sorted,
+                                                        const int32_t* __restrict__ tile_offsets,
+                                                        float* __restrict__ image) {
+    constexpr int RS = NdCfg<FC>::RS;
+    __shared__ float4 s_rec[kNdBatch][RS / 4];
+    __shared__ int4 s_box[kNdBatch];
+    const int tile = blockIdx.x;
+    const int tx0 = (tile % ntx) * kTile, ty0 = (tile / ntx) * kTile;
+    const int px = tx0 + (threadIdx.x & (kTile - 1)), py = ty0 + (threadIdx.x >> 4);
+    const float fpx = static_cast<float>(px), fpy = static_cast<float>(py);
+    float acc[FC];
+#pragma unroll
+    for (int c = 0; c < FC; ++c) acc[c] = 0.0f;
+    const int beg = tile_offsets[tile], end = tile_offsets[tile + 1];
+    for (int b = beg; b < end; b += kNdBatch) {
+        const int cnt = min(kNdBatch, end - b);
+        __syncthreads();
+        for (int e = threadIdx.x; e < cnt * (RS / 4); e += kNdThreads) {
+            const int j = e / (RS / 4), v = e - j * (RS / 4);
+            const int g = gid_sorted[b + j];
+            s_rec[j][v] = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * RS)[v];
+            if (v == 0) s_box[j] = box[g];
+        }
+        __syncthreads();
+        for (int j = 0; j < cnt; ++j) {
+            const int4 bx = s_box[j];
+            if (px < bx.x || px >= bx.z || py < bx.y || py >= bx.w) continue;
+            const float4 g0 = s_rec[j][0];
+            const float* r = reinterpret_cast<const float*>(&s_rec[j][1]);
+            const float dx = fpx - g0.x, dy = fpy - g0.y;
+            const float q = fmaf(dx, fmaf(g0.z, dx, g0.w * dy), (r[0] * dy) * dy);
+            const float wgt = ex2_ftz(q);
+#pragma unroll
+            for (int c = 0; c < FC; ++c) acc[c] = fmaf(wgt, r[1 + c], acc[c]);
+        }
+    }
+    if (px >= W || py >= H) return;
+    const int64_t plane = static_cast<int64_t>(H) * W, pix = static_cast<int64_t>(py) * W + px;
+#pragma unroll
+    for (int c = 0; c < FC; ++c) {
+        if (c < F) image[c * plane + pix] = acc[c];
+    }
+}
+
+// Per-pair sums over the pixels of tile t inside the entry's box: one thread per
+// list entry, the tile's dL/dimage staged in shared memory.  Rows (Sx, Sy,
+// d_conic, dF) land at the entry's gid-major pair slot, as in the additive
+// backward, so k_reduce_gaussian finishes the per-Gaussian gradients.
+template <int FC>
+__global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int ntx, const float* __restrict__ prec,
+                                                        const int4* __restrict__ box,
+                                                        const int32_t* __restrict__ gid_sorted,
+                                                        const int32_t* __restrict__ tile_offsets,
+                                                        const int4* __restrict__ aabb,
+                                                        const int32_t* __restrict__ pair_offset,
+                                                        const float* __restrict__ grad_image,
+                                                        float* __restrict__ pairgrad, int pstride) {
+    constexpr int RS = NdCfg<FC>::RS;
+    __shared__ float s_go[FC][kTilePixels];
+    const int tile = blockIdx.x;
+    const int tile_x = tile % ntx, tile_y = tile / ntx;
+    const int tx0 = tile_x * kTile, ty0 = tile_y * kTile;
+    const int64_t plane = static_cast<int64_t>(H) * W;
+    {
+        const int px = tx0 + (threadIdx.x & (kTile - 1)), py = ty0 + (threadIdx.x >> 4);
+        const bool in = px < W && py < H;
+#pragma unroll
+        for (int c = 0; c < FC; ++c) {
+            s_go[c][threadIdx.x] = in && c < F ? grad_image[c * plane + static_cast<int64_t>(py) * W + px] : 0.0f;
+        }
+    }
+    __syncthreads();
+    const int beg = tile_offsets[tile], end = tile_offsets[tile + 1];
+    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kNdThreads) {
+        const int g = gid_sorted[e];
+        const int4 bx = box[g];
+        const float4* rec = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * RS);
+        const float4 g0 = rec[0];
+        float r[RS - 4];
+#pragma unroll
+        for (int v = 0; v < (RS - 4) / 4; ++v) {
+            const float4 t = rec[1 + v];
+            r[4 * v + 0] = t.x;
+            r[4 * v + 1] = t.y;
+            r[4 * v + 2] = t.z;
+            r[4 * v + 3] = t.w;
+        }
+        const int x_lo = max(bx.x, tx0) - tx0, x_hi = min(min(bx.z, tx0 + kTile), W) - tx0;
+        const int y_lo = max(bx.y, ty0) - ty0, y_hi = min(min(bx.w, ty0 + kTile), H) - ty0;
+        float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f, dF[FC];
+#pragma unroll
+        for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
+        for (int ly = y_lo; ly < y_hi; ++ly) {
+            const float dy = static_cast<float>(ty0 + ly) - g0.y;
+            for (int lx = x_lo; lx < x_hi; ++lx) {
+                const float dx = static_cast<float>(tx0 + lx) - g0.x;
+                const float q = fmaf(dx, fmaf(g0.z, dx, g0.w * dy), (r[0] * dy) * dy);
+                const float wgt = ex2_ftz(q);
+                const int p = ly * kTile + lx;
+                float dLdw = 0.0f;
+#pragma unroll
+                for (int c = 0; c < FC; ++c) {
+                    const float go = s_go[c][p];
+                    dLdw = fmaf(go, r[1 + c], dLdw);
+                    dF[c] = fmaf(wgt, go, dF[c]);
+                }
+                const float gw = wgt * dLdw;
+                Sx = fmaf(gw, dx, Sx);
+                Sy = fmaf(gw, dy, Sy);
+                Sxx = fmaf(gw * dx, dx, Sxx);
+                Sxy = fmaf(gw * dx, dy, Sxy);
+                Syy = fmaf(gw * dy, dy, Syy);
+            }
+        }
+        const int4 tb = aabb[g];
+        const int slot = pair_offset[g] + (tile_y - tb.y) * (tb.z - tb.x) + (tile_x - tb.x);
+        float* row = pairgrad + static_cast<int64_t>(slot) * pstride;
+        row[0] = Sx;
+        row[1] = Sy;
+        row[2] = -0.5f * Sxx;
+        row[3] = -Sxy;
+        row[4] = -0.5f * Syy;
+#pragma unroll
+        for (int c = 0; c < FC; ++c) {
+            if (c < F) row[5 + c] = dF[c];
+        }
+    }
+}
+
+#define OSS_ND_DISPATCH(f, CALL) \
+    ((f) <= 1 ? CALL(1) : (f) <= 3 ? CALL(3) : (f) <= 4 ? CALL(4) : (f) <= 8 ? CALL(8) : (f) <= 16 ? CALL(16) : CALL(32))
+
+}  // namespace
+
+int nd_record_floats(int f) {
+#define OSS_ND_RS(FC) NdCfg<FC>::RS
+    return OSS_ND_DISPATCH(f, OSS_ND_RS);
+#undef OSS_ND_RS
+}
+
+cudaError_t launch_nd_preprocess(int n, int ntx, int nty, const float* xy, const float* conic, const int32_t* box,
+                                 int f, const float* feat, const float* amp, int32_t* aabb, int32_t* count,
+                                 float* geo, float* prec, long long* block_sums, int32_t* tile_count,
+                                 cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_nd_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
+        n, ntx, nty, reinterpret_cast<const float2*>(xy), conic, reinterpret_cast<const int4*>(box), f,
+        nd_record_floats(f), feat, amp, reinterpret_cast<int4*>(aabb), count, geo, prec, block_sums, tile_count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_nd_forward(int f, int h, int w, const float* prec, const int32_t* box, const int32_t* gid_sorted,
+                              const int32_t* tile_offsets, float* image, cudaStream_t stream) {
+    const int ntx = static_cast<int>(div_up(w, kTile)), nty = static_cast<int>(div_up(h, kTile));
+    if (ntx * nty == 0 || f == 0) return cudaSuccess;
+#define OSS_ND_FWD(FC)                                                                                         \
+    (k_nd_fwd<FC><<<static_cast<unsigned>(ntx * nty), kNdThreads, 0, stream>>>(                              \
+         f, h, w, ntx, prec, reinterpret_cast<const int4*>(box), gid_sorted, tile_offsets, image),            \
+     cudaGetLastError())
+    return OSS_ND_DISPATCH(f, OSS_ND_FWD);
+#undef OSS_ND_FWD
+}
+
+cudaError_t launch_nd_backward_pairs(int f, int h, int w, const float* prec, const int32_t* box,
+                                     const int32_t* gid_sorted, const int32_t* tile_offsets, const int32_t* aabb,
+                                     const int32_t* pair_offset, const float* grad_image, float* pairgrad,
+                                     int pair_stride, cudaStream_t stream) {
+    const int ntx = static_cast<int>(div_up(w, kTile)), nty = static_cast<int>(div_up(h, kTile));
+    if (ntx * nty == 0 || f == 0) return cudaSuccess;
+#define OSS_ND_BWD(FC)                                                                                         \
+    (k_nd_bwd<FC><<<static_cast<unsigned>(ntx * nty), kNdThreads, 0, stream>>>(                              \
+         f, h, w, ntx, prec, reinterpret_cast<const int4*>(box), gid_sorted, tile_offsets,                     \
+         reinterpret_cast<const int4*>(aabb), pair_offset, grad_image, pairgrad, pair_stride),                 \
+     cudaGetLastError())
+    return OSS_ND_DISPATCH(f, OSS_ND_BWD);
+#undef OSS_ND_BWD
+}
+
+}  // namespace oss

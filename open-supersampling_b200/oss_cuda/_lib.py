@@ -79,6 +79,11 @@ SIGNATURES = {
          _p, _i64, _p],
     ),
     "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
+    "oss_nd_record_floats": (_i64, [_i64]),
+    "oss_nd_prepare": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+                                      _p]),
+    "oss_nd_forward": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p]),
+    "oss_nd_backward_pairs": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_tile_mse": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p]),
     "oss_canvas_error": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_prune_scratch_bytes": (_i64, [_i64]),
