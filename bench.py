@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5", "canvas"],
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5", "canvas", "nd"],
                     default="config2")
     ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -1005,15 +1005,53 @@ def run_canvas(args, rank, world):
                      select_for_pruning_ms=ms_prune)
 
 
+def run_nd(args, rank, world):
+    """v7 N-D time-slice render (oss/sr/v7/nd_rasterizer.py:242-281), one frame per
+    rank: 200k (x, y, t) Gaussians at 1080p with config-2 spatial sizes and time
+    extents, R = 8 latent features, t_query = 0.5, default Mip filters; a step is
+    the forward and the backward of all four inputs through the public call."""
+    from oss_b200 import render_nd_time_slice
+
+    h, w, n, r = 1080, 1920, 200_000, 8
+    device = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(99 + rank)
+    means = np.concatenate([rng.random((n, 2)) * np.array([w, h]), rng.random((n, 1))], axis=1).astype(np.float32)
+    s = np.exp(rng.standard_normal((n, 2)) * 0.3 + math.log(2.0))
+    th = rng.random(n) * math.pi
+    cov = np.zeros((n, 3, 3))
+    c, sn = np.cos(th), np.sin(th)
+    cov[:, 0, 0] = (c * s[:, 0]) ** 2 + (sn * s[:, 1]) ** 2
+    cov[:, 1, 1] = (sn * s[:, 0]) ** 2 + (c * s[:, 1]) ** 2
+    cov[:, 0, 1] = cov[:, 1, 0] = c * sn * (s[:, 0] ** 2 - s[:, 1] ** 2)
+    cov[:, 2, 2] = 0.05 + 0.1 * rng.random(n)
+    cov[:, 0, 2] = cov[:, 2, 0] = 0.3 * rng.standard_normal(n) * np.sqrt(cov[:, 0, 0] * cov[:, 2, 2]) * 0.5
+    cov[:, 1, 2] = cov[:, 2, 1] = 0.3 * rng.standard_normal(n) * np.sqrt(cov[:, 1, 1] * cov[:, 2, 2]) * 0.5
+    t = {"means": torch.from_numpy(means).to(device), "covs": torch.from_numpy(cov.astype(np.float32)).to(device),
+         "feats": torch.from_numpy(rng.random((n, r)).astype(np.float32)).to(device),
+         "opac": torch.from_numpy((1.0 / (1.0 + np.exp(-rng.standard_normal(n)))).astype(np.float32)).to(device)}
+    up = torch.from_numpy(rng.standard_normal((r, h, w)).astype(np.float32)).to(device)
+
+    def step():
+        leaves = [t[k].detach().requires_grad_(True) for k in ("means", "covs", "feats", "opac")]
+        img = render_nd_time_slice(leaves[0], leaves[1], leaves[2], leaves[3], 0.5, (h, w))
+        torch.autograd.grad(img, leaves, up)
+
+    ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    value = h * w / (ms * 1e-3) / 1e6
+    return base_line(args, world, value, ms, f"nd: v7 time-slice render {w}x{h}, N={n} (x, y, t) Gaussians, R={r}, "
+                     "t_query 0.5, Mip 3D 0.2 / 2D 0.1, fwd+bwd of means, covs, features, opacities, "
+                     "one frame per rank", "weak", clocks, ms_per_frame=ms)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.config in ("config3", "config4", "config5", "canvas"):
+        elif args.config in ("config3", "config4", "config5", "canvas", "nd"):
             line = {"config3": run_config3, "config4": run_config4, "config5": run_config5,
-                    "canvas": run_canvas}[args.config](
+                    "canvas": run_canvas, "nd": run_nd}[args.config](
                 args, rank, world)
             if rank == 0:
                 print(json.dumps(line), flush=True)

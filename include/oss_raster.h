@@ -385,6 +385,18 @@ OSS_API int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* mot
  * (pair_stride = oss_pair_grad_stride(f)); oss_reduce_pair_grads with opacity = amp and no scale / rot
  * turns them into d_xy, d_conic, d_feat and d_amp (its d_opacity). */
 OSS_API int64_t oss_nd_record_floats(int64_t f);
+/* The time conditioning that feeds the splat (nd_rasterizer.py:53-104, 168-239, 242-281): per
+ * Gaussian, means (n x 3: x, y, t), covariances (n x 9, row-major 3x3) and opacities (n) ->
+ * xy (n x 2), conic (n x 3), amp (n) and box (n x 4 int32), for t_query, the time falloff flag and
+ * the Mip 3D / 2D variances (<= 0 turns a filter off).  The backward takes the gradients of xy,
+ * conic and amp and writes those of the means, covariances and opacities. */
+OSS_API int oss_nd_condition(int64_t n, int64_t h, int64_t w, const float* means, const float* covs,
+                             const float* opac, float t_query, int32_t time_falloff, float mip3, float mip2,
+                             float* xy, float* conic, float* amp, int32_t* box, void* stream);
+OSS_API int oss_nd_condition_backward(int64_t n, const float* means, const float* covs, const float* opac,
+                                      float t_query, int32_t time_falloff, float mip3, float mip2,
+                                      const float* d_xy, const float* d_conic, const float* d_amp,
+                                      float* d_means, float* d_covs, float* d_opac, void* stream);
 OSS_API int oss_nd_prepare(int64_t n, int64_t h, int64_t w, const float* xy, const float* conic, const int32_t* box,
                            int64_t f, const float* feat, const float* amp, int32_t* aabb, int32_t* pair_offset,
                            float* geo, float* prec, int64_t* total_pairs, int32_t* tile_count,

@@ -573,6 +573,34 @@ int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, flo
 
 int64_t oss_nd_record_floats(int64_t f) { return f < 1 || f > 32 ? 0 : oss::nd_record_floats(static_cast<int>(f)); }
 
+int oss_nd_condition(int64_t n, int64_t h, int64_t w, const float* means, const float* covs, const float* opac,
+                     float t_query, int32_t time_falloff, float mip3, float mip2, float* xy, float* conic, float* amp,
+                     int32_t* box, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(means != nullptr && covs != nullptr && opac != nullptr && xy != nullptr && conic != nullptr &&
+                  amp != nullptr && box != nullptr && aligned(box, 16),
+              OSS_ERR_INVALID, "pointers must be non-null (box 16-byte aligned)");
+    OSS_CUDA_TRY(oss::launch_nd_prep_forward(g.n, g.h, g.w, means, covs, opac, t_query, time_falloff, mip3, mip2, xy,
+                                             conic, amp, box, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_nd_condition_backward(int64_t n, const float* means, const float* covs, const float* opac, float t_query,
+                              int32_t time_falloff, float mip3, float mip2, const float* d_xy, const float* d_conic,
+                              const float* d_amp, float* d_means, float* d_covs, float* d_opac, void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N must be in [0, INT_MAX]");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(means != nullptr && covs != nullptr && opac != nullptr && d_xy != nullptr && d_conic != nullptr &&
+                  d_amp != nullptr && d_means != nullptr && d_covs != nullptr && d_opac != nullptr,
+              OSS_ERR_INVALID, "pointers must be non-null");
+    OSS_CUDA_TRY(oss::launch_nd_prep_backward(static_cast<int>(n), means, covs, opac, t_query, time_falloff, mip3, mip2,
+                                              d_xy, d_conic, d_amp, d_means, d_covs, d_opac, as_stream(stream)));
+    return OSS_OK;
+}
+
 int oss_nd_prepare(int64_t n, int64_t h, int64_t w, const float* xy, const float* conic, const int32_t* box,
                    int64_t f, const float* feat, const float* amp, int32_t* aabb, int32_t* pair_offset, float* geo,
                    float* prec, int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets, void* scratch,

@@ -127,6 +127,16 @@ cudaError_t launch_apply_prune_spawn(int n, int f, const int64_t* prune_idx, con
 // and binning; the backward writes its per-pair rows (reduced by
 // launch_reduce_gaussian_grads with the amplitude as opacity).
 int nd_record_floats(int f);
+// Per-Gaussian time conditioning: (x, y, t) means, 3x3 covariances and
+// opacities -> conditional mean, inverse covariance (a, b, d), amplitude and cull
+// box; the backward maps their gradients onto means, covariances and opacities.
+cudaError_t launch_nd_prep_forward(int n, int h, int w, const float* means, const float* covs, const float* opac,
+                                   float tq, int falloff, float v3, float v2, float* xy, float* conic, float* amp,
+                                   int32_t* box, cudaStream_t stream);
+cudaError_t launch_nd_prep_backward(int n, const float* means, const float* covs, const float* opac, float tq,
+                                    int falloff, float v3, float v2, const float* g_xy, const float* g_conic,
+                                    const float* g_amp, float* g_means, float* g_covs, float* g_opac,
+                                    cudaStream_t stream);
 cudaError_t launch_nd_preprocess(int n, int ntx, int nty, const float* xy, const float* conic, const int32_t* box,
                                  int f, const float* feat, const float* amp, int32_t* aabb, int32_t* count,
                                  float* geo, float* prec, long long* block_sums, int32_t* tile_count,

@@ -220,10 +220,231 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
     }
 }
 
+// ---- per-Gaussian time conditioning (nd_rasterizer.py:53-239) -------------
+// One thread per Gaussian: Mip 3D smoothing, conditioning on t = t_query (mean
+// shift, Schur complement, marginal density of t_query), Mip 2D filter, then the
+// splat inputs: mean, inverse covariance (a, b, d), amplitude and the cull box.
+// The backward recomputes these steps and applies their chain rule by hand.
+struct NdPrep {
+    float S[9];              // smoothed 3x3 covariance
+    float f3, opf;           // opacity factor, smoothed opacity
+    float vtt, k, dt;        // clamped V_tt, dt / V_tt, t_query - mean_t
+    float c[4];              // conditional 2x2 covariance
+    float wt, W;             // density of t_query, weight before the 2D filter
+    float P[4], f2, W2;      // filtered 2x2 covariance, its factor, weight after it
+    float D;                 // det P
+    float mx, my;            // conditional mean
+};
+
+__device__ __forceinline__ float det3(const float* M) {
+    const float c0 = __fsub_rn(__fmul_rn(M[4], M[8]), __fmul_rn(M[5], M[7]));
+    const float c1 = __fsub_rn(__fmul_rn(M[3], M[8]), __fmul_rn(M[5], M[6]));
+    const float c2 = __fsub_rn(__fmul_rn(M[3], M[7]), __fmul_rn(M[4], M[6]));
+    return __fadd_rn(__fsub_rn(__fmul_rn(M[0], c0), __fmul_rn(M[1], c1)), __fmul_rn(M[2], c2));
+}
+
+// cofactor matrix (d det / d M)
+__device__ __forceinline__ void cof3(const float* M, float* out) {
+    out[0] = M[4] * M[8] - M[5] * M[7];
+    out[1] = -(M[3] * M[8] - M[5] * M[6]);
+    out[2] = M[3] * M[7] - M[4] * M[6];
+    out[3] = -(M[1] * M[8] - M[2] * M[7]);
+    out[4] = M[0] * M[8] - M[2] * M[6];
+    out[5] = -(M[0] * M[7] - M[1] * M[6]);
+    out[6] = M[1] * M[5] - M[2] * M[4];
+    out[7] = -(M[0] * M[5] - M[2] * M[3]);
+    out[8] = M[0] * M[4] - M[1] * M[3];
+}
+
+__device__ NdPrep nd_prep(const float* m, const float* C, float op, float tq, bool falloff, float v3, float v2) {
+    NdPrep p;
+#pragma unroll
+    for (int i = 0; i < 9; ++i) p.S[i] = C[i];
+    p.f3 = 1.0f;
+    p.opf = op;
+    if (v3 > 0.0f) {
+        p.S[0] = __fadd_rn(C[0], v3);
+        p.S[4] = __fadd_rn(C[4], v3);
+        p.S[8] = __fadd_rn(C[8], v3);
+        const float dc = fmaxf(det3(C), 1.0e-12f), ds = fmaxf(det3(p.S), 1.0e-12f);
+        p.f3 = __fsqrt_rn(__fdiv_rn(dc, ds));
+        p.opf = __fmul_rn(op, p.f3);
+    }
+    p.vtt = fmaxf(p.S[8], 1.0e-12f);
+    p.dt = __fsub_rn(tq, m[2]);
+    p.k = __fdiv_rn(p.dt, p.vtt);
+    p.mx = __fadd_rn(m[0], __fmul_rn(p.S[2], p.k));
+    p.my = __fadd_rn(m[1], __fmul_rn(p.S[5], p.k));
+    p.c[0] = __fsub_rn(p.S[0], __fdiv_rn(__fmul_rn(p.S[2], p.S[2]), p.vtt));
+    p.c[1] = __fsub_rn(p.S[1], __fdiv_rn(__fmul_rn(p.S[2], p.S[5]), p.vtt));
+    p.c[2] = __fsub_rn(p.S[3], __fdiv_rn(__fmul_rn(p.S[5], p.S[2]), p.vtt));
+    p.c[3] = __fsub_rn(p.S[4], __fdiv_rn(__fmul_rn(p.S[5], p.S[5]), p.vtt));
+    const float lw = __fsub_rn(__fdiv_rn(__fmul_rn(__fmul_rn(-0.5f, p.dt), p.dt), p.vtt),
+                               __fmul_rn(0.5f, __fadd_rn(1.8378770664093453f, logf(p.vtt))));
+    p.wt = expf(lw);
+    p.W = falloff ? p.wt : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p.P[i] = p.c[i];
+    p.f2 = 1.0f;
+    p.W2 = p.W;
+    if (v2 > 0.0f) {
+        p.P[0] = __fadd_rn(p.c[0], v2);
+        p.P[3] = __fadd_rn(p.c[3], v2);
+        const float dc = fmaxf(__fsub_rn(__fmul_rn(p.c[0], p.c[3]), __fmul_rn(p.c[1], p.c[2])), 1.0e-12f);
+        const float dp = fmaxf(__fsub_rn(__fmul_rn(p.P[0], p.P[3]), __fmul_rn(p.P[1], p.P[2])), 1.0e-12f);
+        p.f2 = __fsqrt_rn(__fdiv_rn(dc, dp));
+        p.W2 = __fmul_rn(p.W, p.f2);
+    }
+    p.D = __fsub_rn(__fmul_rn(p.P[0], p.P[3]), __fmul_rn(p.P[1], p.P[2]));
+    return p;
+}
+
+__global__ void __launch_bounds__(256) k_nd_prep_fwd(int n, int H, int W, const float* __restrict__ means,
+                                                      const float* __restrict__ covs, const float* __restrict__ opac,
+                                                      float tq, int falloff, float v3, float v2,
+                                                      float* __restrict__ xy, float* __restrict__ conic,
+                                                      float* __restrict__ amp, int4* __restrict__ box) {
+    const int g = blockIdx.x * 256 + threadIdx.x;
+    if (g >= n) return;
+    float m[3], C[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) m[i] = means[3 * static_cast<int64_t>(g) + i];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) C[i] = covs[9 * static_cast<int64_t>(g) + i];
+    const NdPrep p = nd_prep(m, C, opac[g], tq, falloff != 0, v3, v2);
+    xy[2 * g + 0] = p.mx;
+    xy[2 * g + 1] = p.my;
+    conic[3 * g + 0] = __fdiv_rn(p.P[3], p.D);
+    conic[3 * g + 1] = __fdiv_rn(-p.P[1], p.D);
+    conic[3 * g + 2] = __fdiv_rn(p.P[0], p.D);
+    amp[g] = __fmul_rn(p.opf, p.W2);
+    // cull box: 3 sqrt(largest eigenvalue, at least 1e-6) around the mean, fp64 floor / ceil
+    const float a = p.P[0], d = p.P[3], b = __fmul_rn(0.5f, __fadd_rn(p.P[1], p.P[2]));
+    const float half = __fmul_rn(0.5f, __fsub_rn(a, d));
+    float lam = __fadd_rn(__fmul_rn(0.5f, __fadd_rn(a, d)), __fsqrt_rn(__fadd_rn(__fmul_rn(half, half), __fmul_rn(b, b))));
+    lam = fmaxf(lam, 1.0e-6f);
+    const double r = 3.0 * static_cast<double>(__fsqrt_rn(lam));
+    const double x0 = fmax(floor(static_cast<double>(p.mx) - r), 0.0);
+    const double x1 = fmin(ceil(static_cast<double>(p.mx) + r), static_cast<double>(W));
+    const double y0 = fmax(floor(static_cast<double>(p.my) - r), 0.0);
+    const double y1 = fmin(ceil(static_cast<double>(p.my) + r), static_cast<double>(H));
+    int4 bx = make_int4(0, 0, 0, 0);
+    if (isfinite(x0) && isfinite(x1) && isfinite(y0) && isfinite(y1)) {
+        bx = make_int4(static_cast<int>(x0), static_cast<int>(y0), static_cast<int>(x1), static_cast<int>(y1));
+    }
+    box[g] = bx;
+}
+
+__global__ void __launch_bounds__(256) k_nd_prep_bwd(int n, const float* __restrict__ means,
+                                                      const float* __restrict__ covs, const float* __restrict__ opac,
+                                                      float tq, int falloff, float v3, float v2,
+                                                      const float* __restrict__ g_xy, const float* __restrict__ g_conic,
+                                                      const float* __restrict__ g_amp, float* __restrict__ g_means,
+                                                      float* __restrict__ g_covs, float* __restrict__ g_opac) {
+    const int g = blockIdx.x * 256 + threadIdx.x;
+    if (g >= n) return;
+    float m[3], C[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) m[i] = means[3 * static_cast<int64_t>(g) + i];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) C[i] = covs[9 * static_cast<int64_t>(g) + i];
+    const float op = opac[g];
+    const NdPrep p = nd_prep(m, C, op, tq, falloff != 0, v3, v2);
+    const float gx = g_xy[2 * g], gy = g_xy[2 * g + 1];
+    const float ga = g_conic[3 * g], gb = g_conic[3 * g + 1], gd = g_conic[3 * g + 2];
+    const float gamp = g_amp[g];
+    // amp = opf * W2
+    const float g_opf = gamp * p.W2;
+    const float g_W2 = gamp * p.opf;
+    // conic (a, b, d) = (P11, -P01, P00) / D
+    const float a = p.P[3] / p.D, b = -p.P[1] / p.D, d = p.P[0] / p.D;
+    const float sd = (ga * a + gb * b + gd * d) / p.D;
+    float gP[4];
+    gP[0] = gd / p.D - sd * p.P[3];
+    gP[3] = ga / p.D - sd * p.P[0];
+    gP[1] = -gb / p.D + sd * p.P[2];
+    gP[2] = sd * p.P[1];
+    // Mip 2D: P = c + v2 I, W2 = W * sqrt(det c / det P)
+    float gc[4] = {gP[0], gP[1], gP[2], gP[3]};
+    float g_W = g_W2;
+    if (v2 > 0.0f) {
+        g_W = g_W2 * p.f2;
+        const float g_f2 = g_W2 * p.W;
+        const float dc = p.c[0] * p.c[3] - p.c[1] * p.c[2];
+        const float dp = p.P[0] * p.P[3] - p.P[1] * p.P[2];
+        const float g_dc = dc >= 1.0e-12f ? g_f2 * p.f2 / (2.0f * dc) : 0.0f;
+        const float g_dp = dp >= 1.0e-12f ? -g_f2 * p.f2 / (2.0f * dp) : 0.0f;
+        gc[0] += g_dc * p.c[3] + g_dp * p.P[3];
+        gc[3] += g_dc * p.c[0] + g_dp * p.P[0];
+        gc[1] += -g_dc * p.c[2] - g_dp * p.P[2];
+        gc[2] += -g_dc * p.c[1] - g_dp * p.P[1];
+    }
+    // W = wt (time falloff) or 1; wt = exp(lw), lw = -dt^2 / (2 vtt) - (log 2 pi + log vtt) / 2
+    const float g_lw = falloff ? g_W * p.wt : 0.0f;
+    float g_dt = g_lw * (-p.dt / p.vtt);
+    float g_vtt = g_lw * (0.5f * p.dt * p.dt / (p.vtt * p.vtt) - 0.5f / p.vtt);
+    // conditional mean: m01 + vxt * k, k = dt / vtt
+    const float vx0 = p.S[2], vx1 = p.S[5];
+    float g_v0 = gx * p.k, g_v1 = gy * p.k;
+    const float g_k = gx * vx0 + gy * vx1;
+    g_dt += g_k / p.vtt;
+    g_vtt += -g_k * p.dt / (p.vtt * p.vtt);
+    // Schur complement: c_ij = S_ij - v_i v_j / vtt (i, j in {0, 1})
+    float gS[9] = {gc[0], gc[1], 0.0f, gc[2], gc[3], 0.0f, 0.0f, 0.0f, 0.0f};
+    g_v0 += -(2.0f * gc[0] * vx0 + (gc[1] + gc[2]) * vx1) / p.vtt;
+    g_v1 += -(2.0f * gc[3] * vx1 + (gc[1] + gc[2]) * vx0) / p.vtt;
+    g_vtt += (gc[0] * vx0 * vx0 + (gc[1] + gc[2]) * vx0 * vx1 + gc[3] * vx1 * vx1) / (p.vtt * p.vtt);
+    gS[2] += g_v0;
+    gS[5] += g_v1;
+    gS[8] += p.S[8] >= 1.0e-12f ? g_vtt : 0.0f;
+    // Mip 3D: S = C + v3 I, opf = op * sqrt(det C / det S)
+    float gC[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) gC[i] = gS[i];
+    float g_op = g_opf;
+    if (v3 > 0.0f) {
+        g_op = g_opf * p.f3;
+        const float g_f3 = g_opf * op;
+        const float dc = det3(C), ds = det3(p.S);
+        const float g_dc = dc >= 1.0e-12f ? g_f3 * p.f3 / (2.0f * dc) : 0.0f;
+        const float g_ds = ds >= 1.0e-12f ? -g_f3 * p.f3 / (2.0f * ds) : 0.0f;
+        float cc[9], cs[9];
+        cof3(C, cc);
+        cof3(p.S, cs);
+#pragma unroll
+        for (int i = 0; i < 9; ++i) gC[i] += g_dc * cc[i] + g_ds * cs[i];
+    }
+    g_means[3 * static_cast<int64_t>(g) + 0] = gx;
+    g_means[3 * static_cast<int64_t>(g) + 1] = gy;
+    g_means[3 * static_cast<int64_t>(g) + 2] = -g_dt;
+#pragma unroll
+    for (int i = 0; i < 9; ++i) g_covs[9 * static_cast<int64_t>(g) + i] = gC[i];
+    g_opac[g] = g_op;
+}
+
 #define OSS_ND_DISPATCH(f, CALL) \
     ((f) <= 1 ? CALL(1) : (f) <= 3 ? CALL(3) : (f) <= 4 ? CALL(4) : (f) <= 8 ? CALL(8) : (f) <= 16 ? CALL(16) : CALL(32))
 
 }  // namespace
+
+cudaError_t launch_nd_prep_forward(int n, int h, int w, const float* means, const float* covs, const float* opac,
+                                   float tq, int falloff, float v3, float v2, float* xy, float* conic, float* amp,
+                                   int32_t* box, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_nd_prep_fwd<<<static_cast<unsigned>(div_up(n, 256)), 256, 0, stream>>>(
+        n, h, w, means, covs, opac, tq, falloff, v3, v2, xy, conic, amp, reinterpret_cast<int4*>(box));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_nd_prep_backward(int n, const float* means, const float* covs, const float* opac, float tq,
+                                    int falloff, float v3, float v2, const float* g_xy, const float* g_conic,
+                                    const float* g_amp, float* g_means, float* g_covs, float* g_opac,
+                                    cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    k_nd_prep_bwd<<<static_cast<unsigned>(div_up(n, 256)), 256, 0, stream>>>(
+        n, means, covs, opac, tq, falloff, v3, v2, g_xy, g_conic, g_amp, g_means, g_covs, g_opac);
+    return cudaGetLastError();
+}
 
 int nd_record_floats(int f) {
 #define OSS_ND_RS(FC) NdCfg<FC>::RS

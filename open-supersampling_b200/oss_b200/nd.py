@@ -1,20 +1,21 @@
 """v7 N-D Gaussian time-slice rasterizer on the B200 kernels.
 
 Drop-in for oss/sr/v7/nd_rasterizer.py (``render_nd_time_slice``,
-``time_marginal``, ``NDGaussian``): the same signatures and math.  Per
-Gaussian, on the device with PyTorch ops (differentiable):
-  * Mip-Splatting 3D smoothing: cov + v3 I, opacity * sqrt(det cov / det(cov + v3 I));
-  * conditioning on t = t_query: mean_xy + cov_xt (t_query - mean_t) / cov_tt, the
-    Schur complement cov_xy - cov_xt cov_xt^T / cov_tt and the marginal density
-    of t_query (cov_tt clamped at 1e-12);
-  * Mip 2D filter: cov_2d + v2 I, weight * sqrt(det cov_2d / det(cov_2d + v2 I)).
-The splat -- the part that touches every pixel -- runs in liboss_b200.so
-(csrc/nd.cu) through tile lists: each Gaussian adds feat * opacity * weight *
-exp(-q/2) at pixel centres (j + 0.5, i + 0.5) inside its cull box of 3 sqrt(largest
-eigenvalue) around the conditioned mean, as the reference's loop bounds
-(nd_rasterizer.py:107-165).  Its backward comes from the per-pair kernel and the
-per-Gaussian reduce of the additive path; PyTorch's autograd carries the
-gradients back through the per-Gaussian steps above.
+``time_marginal``, ``NDGaussian``): the same signatures and math, in two
+autograd steps that both run in liboss_b200.so (csrc/nd.cu):
+  * per Gaussian, one kernel: Mip-Splatting 3D smoothing (cov + v3 I, opacity *
+    sqrt(det cov / det(cov + v3 I))), conditioning on t = t_query (mean_xy +
+    cov_xt (t_query - mean_t) / cov_tt, the Schur complement cov_xy - cov_xt
+    cov_xt^T / cov_tt and the marginal density of t_query, cov_tt clamped at
+    1e-12), the Mip 2D filter (cov_2d + v2 I, weight * sqrt(det cov_2d /
+    det(cov_2d + v2 I))), the inverse covariance and the cull box of 3 sqrt(largest
+    eigenvalue) around the conditioned mean (nd_rasterizer.py:117-124); its
+    backward is the chain rule of these steps written out;
+  * the splat through tile lists: each Gaussian adds feat * opacity * weight *
+    exp(-q/2) at pixel centres (j + 0.5, i + 0.5) inside its cull box
+    (nd_rasterizer.py:107-165); its backward is the per-pair kernel and the
+    per-Gaussian reduce of the additive path.
+``time_marginal`` is also given as PyTorch ops for callers that use it alone.
 """
 from __future__ import annotations
 
@@ -54,55 +55,49 @@ def time_marginal(mean: torch.Tensor, cov: torch.Tensor, t_query: float):
     return mean_c, cov_c, log_w.exp()
 
 
-def _det3(c: torch.Tensor) -> torch.Tensor:
-    return (c[..., 0, 0] * (c[..., 1, 1] * c[..., 2, 2] - c[..., 1, 2] * c[..., 2, 1])
-            - c[..., 0, 1] * (c[..., 1, 0] * c[..., 2, 2] - c[..., 1, 2] * c[..., 2, 0])
-            + c[..., 0, 2] * (c[..., 1, 0] * c[..., 2, 1] - c[..., 1, 1] * c[..., 2, 0]))
+class _NDCondition(torch.autograd.Function):
+    """(means, covs, opacities) -> (xy, conic, amp, box) in one kernel per
+    direction (csrc/nd.cu): the Mip 3D filter, the conditioning on t_query and
+    the Mip 2D filter of the functions above, with their chain rule by hand."""
 
+    @staticmethod
+    def forward(ctx, means, covs, opac, t_query, falloff, v3, v2, h, w):
+        lib = _lib.lib()
+        n = int(means.shape[0])
+        dev = means.device
+        m = means.detach().to(torch.float32).contiguous()
+        c = covs.detach().to(torch.float32).reshape(n, 9).contiguous()
+        o = opac.detach().to(torch.float32).contiguous()
+        xy = torch.empty((n, 2), device=dev, dtype=torch.float32)
+        conic = torch.empty((n, 3), device=dev, dtype=torch.float32)
+        amp = torch.empty((n,), device=dev, dtype=torch.float32)
+        box = torch.empty((n, 4), device=dev, dtype=torch.int32)
+        _lib.check(lib.oss_nd_condition(n, h, w, m.data_ptr(), c.data_ptr(), o.data_ptr(), float(t_query),
+                                        int(bool(falloff)), float(v3), float(v2), xy.data_ptr(), conic.data_ptr(),
+                                        amp.data_ptr(), box.data_ptr(), stream_of(m)), "oss_nd_condition")
+        ctx.save_for_backward(m, c, o)
+        ctx.params = (float(t_query), int(bool(falloff)), float(v3), float(v2))
+        ctx.dtypes = (means.dtype, covs.dtype, opac.dtype)
+        ctx.mark_non_differentiable(box)
+        return xy, conic, amp, box
 
-def _det2(c: torch.Tensor) -> torch.Tensor:
-    return c[..., 0, 0] * c[..., 1, 1] - c[..., 0, 1] * c[..., 1, 0]
-
-
-def _smooth3(covs: torch.Tensor, opacities: torch.Tensor, variance: float):
-    """Mip-Splatting 3D smoothing (nd_rasterizer.py:168-209), in fp32."""
-    if variance <= 0:
-        return covs, opacities
-    c = covs.float()
-    s = c + variance * torch.eye(3, device=c.device, dtype=torch.float32)
-    factor = torch.sqrt(_det3(c).clamp(min=1e-12) / _det3(s).clamp(min=1e-12))
-    return s.to(covs.dtype), opacities * factor.to(opacities.dtype)
-
-
-def _mip2(cov2: torch.Tensor, weights: torch.Tensor, variance: float):
-    """Mip-Splatting 2D filter (nd_rasterizer.py:212-239), in fp32."""
-    if variance <= 0:
-        return cov2, weights
-    c = cov2.float()
-    s = c + variance * torch.eye(2, device=c.device, dtype=torch.float32)
-    factor = torch.sqrt(_det2(c).clamp(min=1e-12) / _det2(s).clamp(min=1e-12))
-    return s.to(cov2.dtype), weights * factor.to(weights.dtype)
-
-
-def _cull_boxes(mean_xy: torch.Tensor, cov2: torch.Tensor, h: int, w: int) -> torch.Tensor:
-    """(N, 4) int32 boxes [x0, x1) x [y0, y1) of 3 sqrt(largest eigenvalue, at least
-    1e-6) around the mean, clipped to the frame (nd_rasterizer.py:117-124); the
-    bounds come from the fp32 eigenvalue and fp64 floor / ceil, as the
-    reference's Python arithmetic on .item() values."""
-    with torch.no_grad():
-        c = cov2.float()
-        a, b, d = c[:, 0, 0], 0.5 * (c[:, 0, 1] + c[:, 1, 0]), c[:, 1, 1]
-        half = 0.5 * (a - d)
-        lam = (0.5 * (a + d) + torch.sqrt(half * half + b * b)).clamp(min=1e-6)
-        r = 3.0 * torch.sqrt(lam).double()
-        m = mean_xy.detach().double()
-        x0 = torch.floor(m[:, 0] - r).clamp(min=0)
-        x1 = torch.minimum(torch.ceil(m[:, 0] + r), torch.full_like(r, float(w)))
-        y0 = torch.floor(m[:, 1] - r).clamp(min=0)
-        y1 = torch.minimum(torch.ceil(m[:, 1] + r), torch.full_like(r, float(h)))
-        box = torch.stack([x0, y0, x1, y1], dim=-1)
-        box = torch.nan_to_num(box, nan=0.0, posinf=0.0, neginf=0.0).clamp(-2**30, 2**30)
-        return box.to(torch.int32).contiguous()
+    @staticmethod
+    def backward(ctx, g_xy, g_conic, g_amp, _g_box):
+        lib = _lib.lib()
+        m, c, o = ctx.saved_tensors
+        n = int(m.shape[0])
+        tq, falloff, v3, v2 = ctx.params
+        z = lambda g, shape: (g if g is not None else torch.zeros(shape, device=m.device)).to(torch.float32).contiguous()
+        gx, gc, ga = z(g_xy, (n, 2)), z(g_conic, (n, 3)), z(g_amp, (n,))
+        d_m = torch.empty_like(m)
+        d_c = torch.empty_like(c)
+        d_o = torch.empty_like(o)
+        _lib.check(lib.oss_nd_condition_backward(n, m.data_ptr(), c.data_ptr(), o.data_ptr(), tq, falloff, v3, v2,
+                                                 gx.data_ptr(), gc.data_ptr(), ga.data_ptr(), d_m.data_ptr(),
+                                                 d_c.data_ptr(), d_o.data_ptr(), stream_of(m)),
+                   "oss_nd_condition_backward")
+        dm, dc, do = ctx.dtypes
+        return d_m.to(dm), d_c.reshape(n, 3, 3).to(dc), d_o.to(do), None, None, None, None, None, None
 
 
 class _NDSplat(torch.autograd.Function):
@@ -187,20 +182,12 @@ def render_nd_time_slice(means: torch.Tensor, covs: torch.Tensor, features: torc
         raise RuntimeError("render_nd_time_slice runs on liboss_b200.so and needs CUDA tensors")
     h, w = int(image_hw[0]), int(image_hw[1])
     dtype = features.dtype
-    covs_f, op_f = _smooth3(covs, opacities, mip_3d_variance)
-    mean_c, cov_c, weight_t = time_marginal(means, covs_f, t_query)
-    weights = weight_t if time_falloff else torch.ones_like(weight_t)
-    cov_c, weights = _mip2(cov_c, weights, mip_2d_variance)
     n = means.shape[0]
     r = features.shape[1]
     if n == 0 or r == 0:
         return torch.zeros((r, h, w), device=means.device, dtype=dtype)
-    c = cov_c.float()
-    det = c[:, 0, 0] * c[:, 1, 1] - c[:, 0, 1] * c[:, 1, 0]
-    conic = torch.stack([c[:, 1, 1] / det, -c[:, 0, 1] / det, c[:, 0, 0] / det], dim=-1)
-    amp = (op_f.float() * weights.float())
-    box = _cull_boxes(mean_c, c, h, w)
-    xy = mean_c.float()
+    xy, conic, amp, box = _NDCondition.apply(means, covs, opacities, float(t_query), bool(time_falloff),
+                                             float(mip_3d_variance), float(mip_2d_variance), h, w)
     feat = features.float()
     parts = [_NDSplat.apply(xy, conic, amp, feat[:, k:k + _MAX_F], box, h, w) for k in range(0, r, _MAX_F)]
     return (parts[0] if len(parts) == 1 else torch.cat(parts, dim=0)).to(dtype)

@@ -80,6 +80,10 @@ SIGNATURES = {
     ),
     "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
     "oss_nd_record_floats": (_i64, [_i64]),
+    "oss_nd_condition": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, ctypes.c_float, _i32, ctypes.c_float,
+                                        ctypes.c_float, _p, _p, _p, _p, _p]),
+    "oss_nd_condition_backward": (ctypes.c_int, [_i64, _p, _p, _p, ctypes.c_float, _i32, ctypes.c_float,
+                                                 ctypes.c_float, _p, _p, _p, _p, _p, _p, _p]),
     "oss_nd_prepare": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                                       _p]),
     "oss_nd_forward": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, _p, _p, _p]),
