@@ -373,6 +373,20 @@ OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, in
 OSS_API int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, float alpha,
                                const float* xy, float* out_xy, uint8_t* in_frame, void* stream);
 
+/* ---- Analytic-Splatting pixel integral (oss/sr/v6/aa_analytic_splat.py:46-202) ----
+ * Elementwise over n elements: the integral of an un-normalised 2D Gaussian with inverse covariance
+ * [[s00, s01], [s10, s11]] over the unit pixel square at offset (dx, dy), with the conditioned logistic
+ * CDF S(x) = 1 / (1 + exp(-1.6 x - 0.07 x^3)); the backward maps the gradient of the values onto the
+ * six inputs.  oss_logistic_cdf writes S(x) (g NULL) or g * S'(x). */
+OSS_API int oss_analytic_pixel_integral(int64_t n, const float* dx, const float* dy, const float* s00,
+                                        const float* s01, const float* s10, const float* s11, float* out,
+                                        void* stream);
+OSS_API int oss_analytic_pixel_integral_backward(int64_t n, const float* dx, const float* dy, const float* s00,
+                                                 const float* s01, const float* s10, const float* s11,
+                                                 const float* g, float* g_dx, float* g_dy, float* g_s00,
+                                                 float* g_s01, float* g_s10, float* g_s11, void* stream);
+OSS_API int oss_logistic_cdf(int64_t n, const float* x, const float* g, float* out, void* stream);
+
 /* ---- v7 N-D time-slice splat (oss/sr/v7/nd_rasterizer.py:107-165) ----
  * After the time conditioning every Gaussian is a 2D Gaussian: mean xy (n x 2), inverse covariance
  * conic (n x 3: a, b, d with q = a dx^2 + 2 b dx dy + d dy^2), amplitude amp (n), features feat

@@ -571,6 +571,40 @@ int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, flo
     return OSS_OK;
 }
 
+int oss_analytic_pixel_integral(int64_t n, const float* dx, const float* dy, const float* s00, const float* s01,
+                                const float* s10, const float* s11, float* out, void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "n must be non-negative");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(dx != nullptr && dy != nullptr && s00 != nullptr && s01 != nullptr && s10 != nullptr &&
+                  s11 != nullptr && out != nullptr,
+              OSS_ERR_INVALID, "pointers must be non-null");
+    OSS_CUDA_TRY(oss::launch_analytic_forward(n, dx, dy, s00, s01, s10, s11, out, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_analytic_pixel_integral_backward(int64_t n, const float* dx, const float* dy, const float* s00,
+                                         const float* s01, const float* s10, const float* s11, const float* g,
+                                         float* g_dx, float* g_dy, float* g_s00, float* g_s01, float* g_s10,
+                                         float* g_s11, void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "n must be non-negative");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(dx != nullptr && dy != nullptr && s00 != nullptr && s01 != nullptr && s10 != nullptr &&
+                  s11 != nullptr && g != nullptr && g_dx != nullptr && g_dy != nullptr && g_s00 != nullptr &&
+                  g_s01 != nullptr && g_s10 != nullptr && g_s11 != nullptr,
+              OSS_ERR_INVALID, "pointers must be non-null");
+    OSS_CUDA_TRY(oss::launch_analytic_backward(n, dx, dy, s00, s01, s10, s11, g, g_dx, g_dy, g_s00, g_s01, g_s10,
+                                               g_s11, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_logistic_cdf(int64_t n, const float* x, const float* g, float* out, void* stream) {
+    OSS_CHECK(n >= 0, OSS_ERR_INVALID, "n must be non-negative");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(x != nullptr && out != nullptr, OSS_ERR_INVALID, "x and out must be non-null");
+    OSS_CUDA_TRY(oss::launch_logistic_cdf(n, x, g, out, as_stream(stream)));
+    return OSS_OK;
+}
+
 int64_t oss_nd_record_floats(int64_t f) { return f < 1 || f > 32 ? 0 : oss::nd_record_floats(static_cast<int>(f)); }
 
 int oss_nd_condition(int64_t n, int64_t h, int64_t w, const float* means, const float* covs, const float* opac,

@@ -148,6 +148,17 @@ cudaError_t launch_nd_backward_pairs(int f, int h, int w, const float* prec, con
                                      const int32_t* pair_offset, const float* grad_image, float* pairgrad,
                                      int pair_stride, cudaStream_t stream);
 
+// ---- analytic.cu -------------------------------------------------------------
+// Analytic-Splatting pixel integral per element (offset dx, dy and inverse
+// covariance s00, s01, s10, s11, all of n elements), its backward, and the
+// conditioned logistic CDF (g null: values; else g * slope).
+cudaError_t launch_analytic_forward(int64_t n, const float* dx, const float* dy, const float* s00, const float* s01,
+                                    const float* s10, const float* s11, float* out, cudaStream_t stream);
+cudaError_t launch_analytic_backward(int64_t n, const float* dx, const float* dy, const float* s00, const float* s01,
+                                     const float* s10, const float* s11, const float* g, float* g_dx, float* g_dy,
+                                     float* g_s00, float* g_s01, float* g_s10, float* g_s11, cudaStream_t stream);
+cudaError_t launch_logistic_cdf(int64_t n, const float* x, const float* g, float* out, cudaStream_t stream);
+
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);
 cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,

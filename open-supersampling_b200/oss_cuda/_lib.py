@@ -79,6 +79,10 @@ SIGNATURES = {
          _p, _i64, _p],
     ),
     "oss_warp_positions": (ctypes.c_int, [_i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p]),
+    "oss_analytic_pixel_integral": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_analytic_pixel_integral_backward": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                                            _p, _p]),
+    "oss_logistic_cdf": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
     "oss_nd_record_floats": (_i64, [_i64]),
     "oss_nd_condition": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, ctypes.c_float, _i32, ctypes.c_float,
                                         ctypes.c_float, _p, _p, _p, _p, _p]),
