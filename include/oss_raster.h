@@ -387,6 +387,23 @@ OSS_API int oss_analytic_pixel_integral_backward(int64_t n, const float* dx, con
                                                  float* g_s01, float* g_s10, float* g_s11, void* stream);
 OSS_API int oss_logistic_cdf(int64_t n, const float* x, const float* g, float* out, void* stream);
 
+/* The additive render with this integral as the weight of every list entry (instead of exp(-q/2)),
+ * at integer pixel centres, over the lists and geo of oss_render_prepare / oss_bin_pairs (use exact
+ * lists: the logistic tails are zero in fp32 beyond them); f <= 32.  The backward writes d_xy, d_conic
+ * (of the conic entries a, b, d), d_feat, d_opacity (opacity may be NULL) and, with scale / rot given,
+ * d_scale / d_rot; scratch holds the per-pair rows. */
+OSS_API int oss_render_analytic_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo,
+                                        const float* feat, const float* opacity, const int32_t* gid_sorted,
+                                        const int32_t* tile_offsets, float* image, void* stream);
+OSS_API int64_t oss_render_analytic_backward_scratch_bytes(int64_t total_pairs, int64_t f);
+OSS_API int oss_render_analytic_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo,
+                                         const float* feat, const float* opacity, const float* scale,
+                                         const float* rot, const int32_t* aabb, const int32_t* pair_offset,
+                                         int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                         const float* grad_image, float* d_xy, float* d_conic, float* d_feat,
+                                         float* d_opacity, float* d_scale, float* d_rot, void* scratch,
+                                         int64_t scratch_bytes, void* stream);
+
 /* ---- v7 N-D time-slice splat (oss/sr/v7/nd_rasterizer.py:107-165) ----
  * After the time conditioning every Gaussian is a 2D Gaussian: mean xy (n x 2), inverse covariance
  * conic (n x 3: a, b, d with q = a dx^2 + 2 b dx dy + d dy^2), amplitude amp (n), features feat

@@ -605,6 +605,61 @@ int oss_logistic_cdf(int64_t n, const float* x, const float* g, float* out, void
     return OSS_OK;
 }
 
+int oss_render_analytic_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                                const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                float* image, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 1 && f <= 32, OSS_ERR_INVALID, "F must be in [1, 32]");
+    if (g.tiles == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && image != nullptr, OSS_ERR_INVALID, "tile_offsets and image must be non-null");
+    OSS_CHECK(g.n == 0 || (geo != nullptr && aligned(geo, 16) && feat != nullptr && gid_sorted != nullptr),
+              OSS_ERR_INVALID, "geo (16-byte aligned), feat and gid_sorted must be non-null");
+    OSS_CUDA_TRY(oss::launch_render_analytic_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
+                                                     tile_offsets, image, as_stream(stream)));
+    return OSS_OK;
+}
+
+int64_t oss_render_analytic_backward_scratch_bytes(int64_t total_pairs, int64_t f) {
+    if (total_pairs < 0) total_pairs = 0;
+    return oss::arena_bytes(total_pairs, sizeof(float) * oss::backward_pair_stride(static_cast<int>(f < 1 ? 1 : f)));
+}
+
+int oss_render_analytic_backward(int64_t n, int64_t f, int64_t h, int64_t w, const float* geo, const float* feat,
+                                 const float* opacity, const float* scale, const float* rot, const int32_t* aabb,
+                                 const int32_t* pair_offset, int64_t total_pairs, const int32_t* gid_sorted,
+                                 const int32_t* tile_offsets, const float* grad_image, float* d_xy, float* d_conic,
+                                 float* d_feat, float* d_opacity, float* d_scale, float* d_rot, void* scratch,
+                                 int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    OSS_CHECK(f >= 1 && f <= 32, OSS_ERR_INVALID, "F must be in [1, 32]");
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(scratch_bytes >= oss_render_analytic_backward_scratch_bytes(total_pairs, f), OSS_ERR_SCRATCH,
+              "render_analytic_backward scratch too small");
+    if (g.n == 0) return OSS_OK;
+    OSS_CHECK(geo != nullptr && aligned(geo, 16) && feat != nullptr && aabb != nullptr && aligned(aabb, 16) &&
+                  pair_offset != nullptr && tile_offsets != nullptr && grad_image != nullptr && d_xy != nullptr &&
+                  d_conic != nullptr && d_feat != nullptr && (total_pairs == 0 || gid_sorted != nullptr),
+              OSS_ERR_INVALID, "pointers must be non-null (geo and aabb 16-byte aligned)");
+    OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
+              "d_scale needs scale, rot and d_rot");
+    cudaStream_t s = as_stream(stream);
+    float* pairgrad = static_cast<float*>(scratch);
+    const int stride = oss::backward_pair_stride(static_cast<int>(f));
+    if (total_pairs > 0 && g.tiles > 0) {
+        OSS_CUDA_TRY(oss::launch_render_analytic_backward_pairs(static_cast<int>(f), g.h, g.w, geo, feat, opacity,
+                                                                gid_sorted, tile_offsets, aabb, pair_offset, grad_image,
+                                                                pairgrad, stride, s));
+    }
+    OSS_CUDA_TRY(oss::launch_reduce_gaussian_grads(g.n, static_cast<int>(f), pairgrad, stride, pair_offset, geo, feat,
+                                                   opacity, scale, rot, d_xy, d_conic, d_feat, d_opacity, d_scale,
+                                                   d_rot, s, true));
+    return OSS_OK;
+}
+
 int64_t oss_nd_record_floats(int64_t f) { return f < 1 || f > 32 ? 0 : oss::nd_record_floats(static_cast<int>(f)); }
 
 int oss_nd_condition(int64_t n, int64_t h, int64_t w, const float* means, const float* covs, const float* opac,

@@ -159,6 +159,19 @@ cudaError_t launch_analytic_backward(int64_t n, const float* dx, const float* dy
                                      float* g_s00, float* g_s01, float* g_s10, float* g_s11, cudaStream_t stream);
 cudaError_t launch_logistic_cdf(int64_t n, const float* x, const float* g, float* out, cudaStream_t stream);
 
+// ---- raster_analytic.cu ------------------------------------------------------
+// The additive render with the Analytic-Splatting pixel integral as weight (raw
+// conic from geo[5..7]) and its per-pair backward rows, which hold d_xy itself
+// (reduce with rows_dxy = true).
+cudaError_t launch_render_analytic_forward(int f, int h, int w, const float* geo, const float* feat,
+                                           const float* opacity, const int32_t* gid_sorted,
+                                           const int32_t* tile_offsets, float* image, cudaStream_t stream);
+cudaError_t launch_render_analytic_backward_pairs(int f, int h, int w, const float* geo, const float* feat,
+                                                  const float* opacity, const int32_t* gid_sorted,
+                                                  const int32_t* tile_offsets, const int32_t* aabb,
+                                                  const int32_t* pair_offset, const float* grad_image,
+                                                  float* pairgrad, int pair_stride, cudaStream_t stream);
+
 // ---- warp.cu ---------------------------------------------------------------
 int64_t warp_scratch_bytes(int64_t n);
 cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
@@ -210,7 +223,7 @@ cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, in
                                          const float* opacity, const float* scale, const float* rot,
                                          float* d_xy, float* d_conic, float* d_feat,
                                          float* d_opacity, float* d_scale, float* d_rot,
-                                         cudaStream_t stream);
+                                         cudaStream_t stream, bool rows_dxy = false);
 
 // ---- raster_alpha.cu -------------------------------------------------------
 // Front-to-back alpha compositing over (depth, gid)-ordered lists, its

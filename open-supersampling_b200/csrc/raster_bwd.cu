@@ -591,7 +591,8 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
                                                          const float* __restrict__ scale, const float* __restrict__ rot,
                                                          float* __restrict__ d_xy, float* __restrict__ d_conic,
                                                          float* __restrict__ d_feat, float* __restrict__ d_opacity,
-                                                         float* __restrict__ d_scale, float* __restrict__ d_rot) {
+                                                         float* __restrict__ d_scale, float* __restrict__ d_rot,
+                                                         int rows_dxy) {
     const int g = blockIdx.x * 256 + threadIdx.x;
     if (g >= n) return;
     const int beg = pair_offset[g];
@@ -652,9 +653,10 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
         }
       }
     }
-    // (s0, s1) = (sum Sx, sum Sy); the raw conic (a, b, d) is geo[g][5..7]
-    d_xy[2 * g + 0] = fmaf(k1.y, s0, k1.z * s1);
-    d_xy[2 * g + 1] = fmaf(k1.z, s0, k1.w * s1);
+    // (s0, s1) = (sum Sx, sum Sy); the raw conic (a, b, d) is geo[g][5..7].  Rows of
+    // weights other than exp(-q/2) hold d_xy itself (rows_dxy).
+    d_xy[2 * g + 0] = rows_dxy ? s0 : fmaf(k1.y, s0, k1.z * s1);
+    d_xy[2 * g + 1] = rows_dxy ? s1 : fmaf(k1.z, s0, k1.w * s1);
     d_conic[3 * g + 0] = s2;
     d_conic[3 * g + 1] = s3;
     d_conic[3 * g + 2] = s4;
@@ -736,10 +738,10 @@ template <int FC>
 cudaError_t launch_reduce_fc(int n, int f, const float* pairgrad, int pstride, const int32_t* pair_offset,
                              const float* geo, const float* feat, const float* opacity, const float* scale,
                              const float* rot, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
-                             float* d_scale, float* d_rot, cudaStream_t stream) {
+                             float* d_scale, float* d_rot, bool rows_dxy, cudaStream_t stream) {
     k_reduce_gaussian<FC><<<static_cast<unsigned>(div_up(n, 256)), 256, 0, stream>>>(
         n, f, pairgrad, pstride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, d_feat, d_opacity,
-        d_scale, d_rot);
+        d_scale, d_rot, rows_dxy ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -818,11 +820,11 @@ cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, in
                                          const int32_t* pair_offset, const float* geo, const float* feat,
                                          const float* opacity, const float* scale, const float* rot, float* d_xy,
                                          float* d_conic, float* d_feat, float* d_opacity, float* d_scale,
-                                         float* d_rot, cudaStream_t stream) {
+                                         float* d_rot, cudaStream_t stream, bool rows_dxy) {
     if (n == 0) return cudaSuccess;
 #define OSS_RED_CALL(FC)                                                                                          \
     launch_reduce_fc<FC>(n, f, pairgrad, pair_stride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, \
-                         d_feat, d_opacity, d_scale, d_rot, stream)
+                         d_feat, d_opacity, d_scale, d_rot, rows_dxy, stream)
     return OSS_DISPATCH_FC(f, OSS_RED_CALL);
 #undef OSS_RED_CALL
 }

@@ -83,6 +83,10 @@ SIGNATURES = {
     "oss_analytic_pixel_integral_backward": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                                             _p, _p]),
     "oss_logistic_cdf": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
+    "oss_render_analytic_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_analytic_backward_scratch_bytes": (_i64, [_i64, _i64]),
+    "oss_render_analytic_backward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p,
+                                                    _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_nd_record_floats": (_i64, [_i64]),
     "oss_nd_condition": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _p, ctypes.c_float, _i32, ctypes.c_float,
                                         ctypes.c_float, _p, _p, _p, _p, _p]),

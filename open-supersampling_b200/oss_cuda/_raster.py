@@ -308,6 +308,40 @@ def render_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None,
     return d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot
 
 
+def render_analytic_forward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None) -> torch.Tensor:
+    """(F, H, W) with the Analytic-Splatting pixel integral as the weight (F <= 32)."""
+    lib = _lib.lib()
+    f = int(feat.size(1))
+    image = torch.empty((f, b.h, b.w), device=feat.device, dtype=torch.float32)
+    _lib.check(lib.oss_render_analytic_forward(b.n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                                               b.gid_sorted.data_ptr(), b.tile_offsets.data_ptr(), image.data_ptr(),
+                                               stream_of(feat)), "oss_render_analytic_forward")
+    return image
+
+
+def render_analytic_backward(b: Binned, feat: torch.Tensor, opacity: torch.Tensor | None, scale: torch.Tensor,
+                             rot: torch.Tensor, grad_image: torch.Tensor):
+    """(d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot) of the analytic-weight render."""
+    lib = _lib.lib()
+    dev = feat.device
+    n, f = b.n, int(feat.size(1))
+    f32 = dict(device=dev, dtype=torch.float32)
+    d_xy, d_conic, d_feat = torch.empty((n, 2), **f32), torch.empty((n, 3), **f32), torch.empty((n, f), **f32)
+    d_opacity = torch.empty((n,), **f32) if opacity is not None else None
+    d_scale, d_rot = torch.empty((n, 2), **f32), torch.empty((n,), **f32)
+    nbytes = lib.oss_render_analytic_backward_scratch_bytes(b.total_pairs, f)
+    scratch = torch.empty((max(1, nbytes),), device=dev, dtype=torch.uint8)
+    scale = aligned(scale, 8)
+    _lib.check(lib.oss_render_analytic_backward(n, f, b.h, b.w, b.geo.data_ptr(), feat.data_ptr(), _lib.ptr(opacity),
+                                                scale.data_ptr(), rot.data_ptr(), b.aabb.data_ptr(),
+                                                b.pair_offset.data_ptr(), b.total_pairs, b.gid_sorted.data_ptr(),
+                                                b.tile_offsets.data_ptr(), grad_image.data_ptr(), d_xy.data_ptr(),
+                                                d_conic.data_ptr(), d_feat.data_ptr(), _lib.ptr(d_opacity),
+                                                d_scale.data_ptr(), d_rot.data_ptr(), scratch.data_ptr(),
+                                                scratch.numel(), stream_of(feat)), "oss_render_analytic_backward")
+    return d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot
+
+
 def background_vector(background, f: int, device) -> torch.Tensor | None:
     """None, a scalar or F values -> a device (F,) fp32 tensor (None stays None)."""
     if background is None:

@@ -18,6 +18,8 @@ Keyword-only additions (defaults keep the reference call's results):
   depth       (N,) tensor ordering each tile's list front to back (alpha only;
               None keeps gid order)
   background  scalar or F values composited behind (alpha only; default 0)
+  weight      "gaussian" (default, exp(-q/2)) | "analytic" (the Analytic-Splatting
+              pixel integral of oss/sr/v6/aa_analytic_splat.py, blend="sum")
   pair_capacity
               opt-in launch without any host synchronisation: the tile lists are
               sized for this many (Gaussian, tile) pairs and the device checks the
@@ -116,9 +118,38 @@ class _RasterizeGaussiansAlpha(Function):
                 None, None)
 
 
+class _RasterizeGaussiansAnalytic(Function):
+    """The additive render with the Analytic-Splatting pixel integral as weight."""
+
+    @staticmethod
+    def forward(ctx, xy, scale, rot, feat, opacity, h, w, mode):
+        if not _COMPILED:
+            raise RuntimeError(
+                "oss_cuda extension not compiled. Run: python open-supersampling_b200/build.py"
+            )
+        with torch.cuda.device(xy.device):
+            b = _raster.bin_gaussians(xy, scale, rot, h, w, mode)
+            out = _raster.render_analytic_forward(b, _raster.aligned(feat, 4), opacity)
+        ctx.save_for_backward(xy, scale, rot, feat, opacity, b.conic, b.aabb, b.pair_offset, b.geo, b.gid_sorted,
+                              b.tile_offsets)
+        ctx.meta = (b.n, b.h, b.w, b.mode, b.total_pairs)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, gid_sorted, tile_offsets = ctx.saved_tensors
+        n, h, w, mode, total_pairs = ctx.meta
+        b = _raster.Binned(n, h, w, mode, conic, aabb, pair_offset, geo, total_pairs, gid_sorted, tile_offsets)
+        grad = grad_out.contiguous().float()
+        with torch.cuda.device(xy.device):
+            d_xy, _d_conic, d_feat, d_opacity, d_scale, d_rot = _raster.render_analytic_backward(
+                b, _raster.aligned(feat, 4), opacity, scale, rot, grad)
+        return d_xy, d_scale, d_rot, d_feat, d_opacity, None, None, None
+
+
 def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True, *, binning=None, opacity=None,
                         blend="sum", depth=None, background=None, pair_capacity=None, overlap=0,
-                        phase_offset=(0, 0)):
+                        phase_offset=(0, 0), weight="gaussian"):
     """Render (F, H, W) on the GPU, differentiably: sum_g feat[g] * exp(-q_g / 2)
     (blend="sum", the reference op) or front-to-back compositing (blend="alpha").
 
@@ -127,8 +158,10 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
     binning (tile lists), opacity (folded in the kernel), blend / depth /
     background (alpha compositing), pair_capacity (no host sync), overlap (the
     4-phase feathered overlapping-tile render of oss/sr/v6/rasterizer.py:159-242,
-    blend="sum") and phase_offset = (dx, dy) integer pixels added to every mean
-    before rendering (the per-frame spawner offset, oss/sr/v6/model.py:795-820).
+    blend="sum"), phase_offset = (dx, dy) integer pixels added to every mean
+    before rendering (the per-frame spawner offset, oss/sr/v6/model.py:795-820)
+    and weight="analytic", the Analytic-Splatting pixel integral of
+    oss/sr/v6/aa_analytic_splat.py in place of exp(-q/2) (blend="sum", F <= 32).
     """
     h, w, tile_size = int(h), int(w), int(tile_size)
     dx, dy = (int(v) for v in phase_offset)
@@ -158,6 +191,14 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
         pair_capacity = int(pair_capacity)
         if pair_capacity < 0 or pair_capacity > _raster.INT32_MAX:
             raise ValueError("pair_capacity must be in [0, 2**31 - 1]")
+    if weight not in ("gaussian", "analytic"):
+        raise ValueError(f"weight must be 'gaussian' or 'analytic', got {weight!r}")
+    if weight == "analytic":
+        if blend != "sum" or pair_capacity is not None:
+            raise ValueError("weight='analytic' applies to blend='sum' without pair_capacity")
+        if int(feat.size(1)) > 32:
+            raise ValueError("weight='analytic' renders at most 32 channels per call")
+        return _RasterizeGaussiansAnalytic.apply(xy, scale, rot, feat, opacity, h, w, mode)
     if blend == "sum":
         if depth is not None or background is not None:
             raise ValueError("depth and background apply to blend='alpha' only")

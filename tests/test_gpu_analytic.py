@@ -68,3 +68,63 @@ def test_pixel_integral_shape_errors(cuda_device):
     with pytest.raises(ValueError, match=r"sigma_2d_inv must be \(\.\.\., 2, 2\)"):
         analytic_pixel_integral(torch.zeros(3, device="cuda"), torch.zeros(3, device="cuda"),
                                 torch.zeros(3, 3, device="cuda"))
+
+
+def _analytic_composition(xy, conic, feat, opacity, h, w):
+    """sum_g feat_g * opacity_g * w_g(p - xy_g) over every pixel, through the
+    elementwise integral above (pinned to the reference): the contract of
+    rasterize_gaussians(weight="analytic") with full-tail sums."""
+    from oss_b200 import analytic_pixel_integral
+
+    ys, xs = torch.meshgrid(torch.arange(h, device="cuda", dtype=torch.float32),
+                            torch.arange(w, device="cuda", dtype=torch.float32), indexing="ij")
+    dx = xs[None] - xy[:, 0, None, None]
+    dy = ys[None] - xy[:, 1, None, None]
+    inv = torch.stack([torch.stack([conic[:, 0], conic[:, 1]], -1), torch.stack([conic[:, 1], conic[:, 2]], -1)], -2)
+    wgt = analytic_pixel_integral(dx, dy, inv)
+    return torch.einsum("nf,nhw->fhw", feat * opacity[:, None], wgt)
+
+
+@pytest.mark.parametrize("binning", ["exact", "full"])
+def test_analytic_weight_render_matches_composition(cuda_device, binning):
+    """rasterize_gaussians(weight="analytic"): image and the gradients of xy,
+    features and opacity against the full-frame composition of the pinned
+    elementwise integral, and those of scale and rotation through the conic
+    chain rule of the additive path."""
+    from oss_cuda import _C, rasterize_gaussians
+
+    rng = np.random.default_rng(31)
+    n, h, w, f = 120, 40, 56, 3
+    xy = dev((rng.random((n, 2)) * np.array([w, h])).astype(np.float32))
+    scale = dev(np.exp(rng.standard_normal((n, 2)) * 0.3 + np.log(1.6)).astype(np.float32))
+    rot = dev((rng.random(n) * np.pi).astype(np.float32))
+    feat = dev(rng.random((n, f)).astype(np.float32))
+    op = dev((1 / (1 + np.exp(-rng.standard_normal(n)))).astype(np.float32))
+    up = dev(rng.standard_normal((f, h, w)).astype(np.float32))
+    leaves = [t.clone().requires_grad_(True) for t in (xy, scale, rot, feat, op)]
+    img = rasterize_gaussians(leaves[0], leaves[1], leaves[2], leaves[3], h, w, binning=binning, opacity=leaves[4],
+                              weight="analytic")
+    (img * up).sum().backward()
+    conic = _C.preprocess_only(xy, scale, rot, h, w)[0]
+    ref_leaves = [t.clone().requires_grad_(True) for t in (xy, conic, feat, op)]
+    ref = _analytic_composition(*ref_leaves, h, w)
+    assert_close(img.detach().cpu().numpy(), ref.detach().cpu().numpy(), what="image")
+    (ref * up).sum().backward()
+    assert_close_grad(leaves[0].grad.cpu().numpy(), ref_leaves[0].grad.cpu().numpy(), what="d_xy")
+    assert_close_grad(leaves[3].grad.cpu().numpy(), ref_leaves[2].grad.cpu().numpy(), what="d_feat")
+    assert_close_grad(leaves[4].grad.cpu().numpy(), ref_leaves[3].grad.cpu().numpy(), what="d_opacity")
+    d_scale, d_rot = _C.conic_to_scale_rot_grad(scale, rot, ref_leaves[1].grad.contiguous())
+    assert_close_grad(leaves[1].grad.cpu().numpy(), d_scale.cpu().numpy(), what="d_scale")
+    assert_close_grad(leaves[2].grad.cpu().numpy(), d_rot.cpu().numpy(), what="d_rot")
+
+
+def test_analytic_weight_argument_checks(cuda_device):
+    from oss_cuda import rasterize_gaussians
+
+    z = torch.zeros((4, 2), device="cuda")
+    r = torch.zeros((4,), device="cuda")
+    with pytest.raises(ValueError, match="weight must be"):
+        rasterize_gaussians(z, z + 1, r, z, 16, 16, weight="box")
+    with pytest.raises(ValueError, match="blend='sum'"):
+        rasterize_gaussians(z, z + 1, r, z, 16, 16, weight="analytic", blend="alpha",
+                            opacity=torch.ones(4, device="cuda"))
