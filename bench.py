@@ -54,8 +54,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5", "canvas", "nd"],
-                    default="config2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["config3", "config4", "config5", "canvas", "nd",
+                                                            "analytic"], default="config2")
     ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1043,15 +1043,38 @@ def run_nd(args, rank, world):
                      "one frame per rank", "weak", clocks, ms_per_frame=ms)
 
 
+def run_analytic(args, rank, world):
+    """Config-2 inputs rendered with the Analytic-Splatting pixel integral as the
+    weight (rasterize_gaussians(weight="analytic"), exact lists), fwd+bwd of xy,
+    scale, rot, rgb and opacity through the public call, one frame per rank."""
+    from oss_cuda import rasterize_gaussians
+
+    h, w, n, lsm, lss = CONFIGS["config2"]
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = {k: torch.from_numpy(v).to(device) for k, v in make_inputs(h, w, n, lsm, lss, seed=1234 + rank).items()}
+
+    def step():
+        leaves = [inp[k].detach().requires_grad_(True) for k in ("xy", "scale", "rot", "rgb", "opacity")]
+        img = rasterize_gaussians(leaves[0], leaves[1], leaves[2], leaves[3], h, w, binning="exact",
+                                  opacity=leaves[4], weight="analytic")
+        torch.autograd.grad(img, leaves, inp["grad"])
+
+    ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    value = h * w / (ms * 1e-3) / 1e6
+    return base_line(args, world, value, ms, f"analytic: config2 ({w}x{h}, N={n}, F=3) with the Analytic-Splatting "
+                     "pixel integral as weight, exact lists, fwd+bwd through rasterize_gaussians, one frame per rank",
+                     "weak", clocks, ms_per_frame=ms)
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.config in ("config3", "config4", "config5", "canvas", "nd"):
+        elif args.config in ("config3", "config4", "config5", "canvas", "nd", "analytic"):
             line = {"config3": run_config3, "config4": run_config4, "config5": run_config5,
-                    "canvas": run_canvas, "nd": run_nd}[args.config](
+                    "canvas": run_canvas, "nd": run_nd, "analytic": run_analytic}[args.config](
                 args, rank, world)
             if rank == 0:
                 print(json.dumps(line), flush=True)

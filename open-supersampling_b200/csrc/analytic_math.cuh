@@ -31,10 +31,12 @@ __device__ __forceinline__ AxisTerm axis_term(float u, float sigma, bool grads) 
     const float inv = 1.0f / sigma;
     const float xp = (u + 0.5f) * inv, xm = (u - 0.5f) * inv;
     AxisTerm t;
-    t.v = logistic(xp) - logistic(xm);
+    const float lp = logistic(xp), lm = logistic(xm);
+    t.v = lp - lm;
     t.du = t.dsigma = 0.0f;
-    if (grads) {
-        const float sp = logistic_slope(xp), sm = logistic_slope(xm);
+    if (grads) {  // slopes from the values above: S' = S (1 - S) (1.6 + 0.21 x^2)
+        const float sp = lp * (1.0f - lp) * fmaf(0.21f * xp, xp, 1.6f);
+        const float sm = lm * (1.0f - lm) * fmaf(0.21f * xm, xm, 1.6f);
         t.du = (sp - sm) * inv;
         t.dsigma = -(sp * xp - sm * xm) * inv;
     }
@@ -67,6 +69,24 @@ __device__ __forceinline__ Frame frame_of(float s00, float s01, float s10, float
     if (!f.iso) th = 0.5f * atan2f(2.0f * f.b, f.a - f.c);
     sincosf(th, &f.st, &f.ct);
     return f;
+}
+
+// True when every pixel centre of the rectangle [X0, X1] x [Y0, Y1] of offsets lies
+// at least 9 sigma (less the half pixel) from the centre along one of the frame's
+// axes (cos, sin; inverse sigmas ish, isl): the logistic slope there is below
+// 1e-27, so each pixel's weight 2 pi sigma_h sigma_l I_h I_l is below 1e-27 and the
+// entry's share of the tile is negligible next to the fp32 sums it joins.
+__device__ __forceinline__ float axis_gap(float c, float s, float X0, float X1, float Y0, float Y1) {
+    const float u0 = c * X0 + s * Y0, u1 = c * X1 + s * Y0, u2 = c * X0 + s * Y1, u3 = c * X1 + s * Y1;
+    const float lo = fminf(fminf(u0, u1), fminf(u2, u3)), hi = fmaxf(fmaxf(u0, u1), fmaxf(u2, u3));
+    return lo > 0.0f ? lo : (hi < 0.0f ? -hi : 0.0f);
+}
+
+__device__ __forceinline__ bool far_from_tile(float ct, float st, float ish, float isl, float X0, float X1, float Y0,
+                                              float Y1) {
+    const float gh = (axis_gap(ct, st, X0, X1, Y0, Y1) - 0.5f) * ish;
+    const float gl = (axis_gap(-st, ct, X0, X1, Y0, Y1) - 0.5f) * isl;
+    return gh >= 9.0f || gl >= 9.0f;
 }
 
 // d/d(a, b, c) of the frame from the sums of dL/d(sigma_h, sigma_l, theta) (or, for an

@@ -8,7 +8,10 @@
 //
 // Per list entry the eigen-frame (rotation, per-axis 1 / sigma, 2 pi sigma_h
 // sigma_l; the shared sigma and no rotation below the 1e-5 eigengap) is computed
-// once, at staging in the forward and per entry in the backward.  The backward
+// once, at staging in the forward and per entry in the backward.  An entry whose
+// every pixel of the tile lies 9 sigma or more from its centre along one axis
+// adds less than 1e-27 per pixel and is skipped (a zero row in the backward):
+// the outer ring of the exact lists, about half of their entries.  The backward
 // runs one thread per list entry over the tile's pixels with the tile's
 // dL/dimage in shared memory, sums dL/d(dx, dy, sigma_h, sigma_l, theta) and dF,
 // and turns them into d_xy and d_conic in the epilogue; the rows feed the
@@ -34,7 +37,7 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_fwd(int F, int H
                                                                      const int32_t* __restrict__ tile_offsets,
                                                                      float* __restrict__ image) {
     __shared__ float4 s_a[kAnBatch];  // x, y, cos, sin
-    __shared__ float4 s_b[kAnBatch];  // 1 / sigma_h, 1 / sigma_l, 2 pi sigma_h sigma_l, -
+    __shared__ float4 s_b[kAnBatch];  // 1 / sigma_h, 1 / sigma_l, 2 pi sigma_h sigma_l, far flag
     __shared__ float s_f[kAnBatch][FC];
     const int tile = blockIdx.x;
     const int tx0 = (tile % ntx) * kTile, ty0 = (tile / ntx) * kTile;
@@ -54,8 +57,12 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_fwd(int F, int H
             const float4 g0 = gr[0], g1 = gr[1];  // (x, y, A, B), (D, a, b, d)
             const Frame f = frame_of(g1.y, g1.z, g1.z, g1.w);
             const float sh = f.iso ? f.s : f.sh, sl = f.iso ? f.s : f.sl;
-            s_a[j] = make_float4(g0.x, g0.y, f.iso ? 1.0f : f.ct, f.iso ? 0.0f : f.st);
-            s_b[j] = make_float4(1.0f / sh, 1.0f / sl, kTwoPi * sh * sl, 0.0f);
+            const float ct = f.iso ? 1.0f : f.ct, st = f.iso ? 0.0f : f.st, ish = 1.0f / sh, isl = 1.0f / sl;
+            const float X0 = static_cast<float>(tx0) - g0.x, Y0 = static_cast<float>(ty0) - g0.y;
+            const bool far = far_from_tile(ct, st, ish, isl, X0, X0 + static_cast<float>(kTile - 1), Y0,
+                                           Y0 + static_cast<float>(kTile - 1));
+            s_a[j] = make_float4(g0.x, g0.y, ct, st);
+            s_b[j] = make_float4(ish, isl, kTwoPi * sh * sl, far ? 1.0f : 0.0f);
             const float op = opacity != nullptr ? opacity[g] : 1.0f;
 #pragma unroll
             for (int c = 0; c < FC; ++c) s_f[j][c] = c < F ? feat[static_cast<int64_t>(g) * F + c] * op : 0.0f;
@@ -63,6 +70,7 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_fwd(int F, int H
         __syncthreads();
         for (int j = 0; j < cnt; ++j) {
             const float4 a = s_a[j], q = s_b[j];
+            if (q.w != 0.0f) continue;  // below 1e-27 at every pixel of the tile (same for all threads)
             const float dx = fpx - a.x, dy = fpy - a.y;
             const float uh = a.z * dx + a.w * dy, ul = -a.w * dx + a.z * dy;
             const float ih = logistic((uh + 0.5f) * q.x) - logistic((uh - 0.5f) * q.x);
@@ -118,7 +126,10 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_bwd(
             dF[c] = 0.0f;
         }
         float Gx = 0.0f, Gy = 0.0f, Gt = 0.0f, Gh = 0.0f, Gl = 0.0f;
-        for (int ly = 0; ly < nrow; ++ly) {
+        const float X0 = static_cast<float>(tx0) - g0.x, Y0 = static_cast<float>(ty0) - g0.y;
+        const bool far = far_from_tile(ct, st, 1.0f / sh, 1.0f / sl, X0, X0 + static_cast<float>(kTile - 1), Y0,
+                                       Y0 + static_cast<float>(kTile - 1));
+        for (int ly = 0; ly < (far ? 0 : nrow); ++ly) {
             const float dy = static_cast<float>(ty0 + ly) - g0.y;
             for (int lx = 0; lx < ncol; ++lx) {
                 const float dx = static_cast<float>(tx0 + lx) - g0.x;
