@@ -12,7 +12,7 @@ constexpr float kTwoPi = 6.283185307179586f;
 
 __device__ __forceinline__ float logistic(float x) {
     const float z = fmaf(0.07f * x, x * x, 1.6f * x);
-    return 1.0f / (1.0f + expf(-z));
+    return __frcp_rn(1.0f + expf(-z));  // the correctly rounded 1 / (1 + e^-z)
 }
 
 // dS/dx = S (1 - S) (1.6 + 0.21 x^2)
@@ -27,8 +27,8 @@ struct AxisTerm {
     float dsigma;   // dI / dsigma
 };
 
-__device__ __forceinline__ AxisTerm axis_term(float u, float sigma, bool grads) {
-    const float inv = 1.0f / sigma;
+// I(u) and its derivatives from 1 / sigma.
+__device__ __forceinline__ AxisTerm axis_term_inv(float u, float inv, bool grads) {
     const float xp = (u + 0.5f) * inv, xm = (u - 0.5f) * inv;
     AxisTerm t;
     const float lp = logistic(xp), lm = logistic(xm);
@@ -41,6 +41,10 @@ __device__ __forceinline__ AxisTerm axis_term(float u, float sigma, bool grads) 
         t.dsigma = -(sp * xp - sm * xm) * inv;
     }
     return t;
+}
+
+__device__ __forceinline__ AxisTerm axis_term(float u, float sigma, bool grads) {
+    return axis_term_inv(u, 1.0f / sigma, grads);
 }
 
 struct Frame {
@@ -69,24 +73,6 @@ __device__ __forceinline__ Frame frame_of(float s00, float s01, float s10, float
     if (!f.iso) th = 0.5f * atan2f(2.0f * f.b, f.a - f.c);
     sincosf(th, &f.st, &f.ct);
     return f;
-}
-
-// True when every pixel centre of the rectangle [X0, X1] x [Y0, Y1] of offsets lies
-// at least 9 sigma (less the half pixel) from the centre along one of the frame's
-// axes (cos, sin; inverse sigmas ish, isl): the logistic slope there is below
-// 1e-27, so each pixel's weight 2 pi sigma_h sigma_l I_h I_l is below 1e-27 and the
-// entry's share of the tile is negligible next to the fp32 sums it joins.
-__device__ __forceinline__ float axis_gap(float c, float s, float X0, float X1, float Y0, float Y1) {
-    const float u0 = c * X0 + s * Y0, u1 = c * X1 + s * Y0, u2 = c * X0 + s * Y1, u3 = c * X1 + s * Y1;
-    const float lo = fminf(fminf(u0, u1), fminf(u2, u3)), hi = fmaxf(fmaxf(u0, u1), fmaxf(u2, u3));
-    return lo > 0.0f ? lo : (hi < 0.0f ? -hi : 0.0f);
-}
-
-__device__ __forceinline__ bool far_from_tile(float ct, float st, float ish, float isl, float X0, float X1, float Y0,
-                                              float Y1) {
-    const float gh = (axis_gap(ct, st, X0, X1, Y0, Y1) - 0.5f) * ish;
-    const float gl = (axis_gap(-st, ct, X0, X1, Y0, Y1) - 0.5f) * isl;
-    return gh >= 9.0f || gl >= 9.0f;
 }
 
 // d/d(a, b, c) of the frame from the sums of dL/d(sigma_h, sigma_l, theta) (or, for an

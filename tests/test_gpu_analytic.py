@@ -85,8 +85,15 @@ def _analytic_composition(xy, conic, feat, opacity, h, w):
     return torch.einsum("nf,nhw->fhw", feat * opacity[:, None], wgt)
 
 
+# (Gaussians, H, W, log-scale mean, log-scale sd): small round splats, and wide
+# elongated ones whose lists span many tiles of a ragged frame, so that entries
+# reach some 8x4 patches of a tile and not others.
+RENDER_CASES = {"small": (120, 40, 56, np.log(1.6), 0.3), "wide": (40, 72, 88, np.log(3.5), 0.6)}
+
+
+@pytest.mark.parametrize("case", sorted(RENDER_CASES))
 @pytest.mark.parametrize("binning", ["exact", "full"])
-def test_analytic_weight_render_matches_composition(cuda_device, binning):
+def test_analytic_weight_render_matches_composition(cuda_device, binning, case):
     """rasterize_gaussians(weight="analytic"): image and the gradients of xy,
     features and opacity against the full-frame composition of the pinned
     elementwise integral, and those of scale and rotation through the conic
@@ -94,9 +101,10 @@ def test_analytic_weight_render_matches_composition(cuda_device, binning):
     from oss_cuda import _C, rasterize_gaussians
 
     rng = np.random.default_rng(31)
-    n, h, w, f = 120, 40, 56, 3
+    n, h, w, lsm, lss = RENDER_CASES[case]
+    f = 3
     xy = dev((rng.random((n, 2)) * np.array([w, h])).astype(np.float32))
-    scale = dev(np.exp(rng.standard_normal((n, 2)) * 0.3 + np.log(1.6)).astype(np.float32))
+    scale = dev(np.exp(rng.standard_normal((n, 2)) * lss + lsm).astype(np.float32))
     rot = dev((rng.random(n) * np.pi).astype(np.float32))
     feat = dev(rng.random((n, f)).astype(np.float32))
     op = dev((1 / (1 + np.exp(-rng.standard_normal(n)))).astype(np.float32))
