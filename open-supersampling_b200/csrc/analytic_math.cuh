@@ -15,6 +15,23 @@ __device__ __forceinline__ float logistic(float x) {
     return __frcp_rn(1.0f + expf(-z));  // the correctly rounded 1 / (1 + e^-z)
 }
 
+// The render kernels' logistic: e^-z from the hardware base-2 exponential
+// (__expf) and 1 / (1 + e) from the approximate reciprocal (__fdividef), a
+// fraction of the instructions of the form above.  The absolute error of S stays
+// near one ulp of S: __expf's relative error grows with |z| (the rounding of
+// z log2 e, about |z| 2^-24), but it reaches S through dS/d(ln e) = -S (1 - S),
+// and S (1 - S) |z| 2^-24 stays below 2e-8 for every z; the reciprocal adds at
+// most about one ulp.  The elementwise kernels keep the accurate form.
+__device__ __forceinline__ float logistic_fast(float x) {
+    const float z = fmaf(0.07f * x, x * x, 1.6f * x);
+    return __fdividef(1.0f, 1.0f + __expf(-z));
+}
+
+template <bool FAST>
+__device__ __forceinline__ float logistic_t(float x) {
+    return FAST ? logistic_fast(x) : logistic(x);
+}
+
 // dS/dx = S (1 - S) (1.6 + 0.21 x^2)
 __device__ __forceinline__ float logistic_slope(float x) {
     const float s = logistic(x);
@@ -27,11 +44,12 @@ struct AxisTerm {
     float dsigma;   // dI / dsigma
 };
 
-// I(u) and its derivatives from 1 / sigma.
+// I(u) and its derivatives from 1 / sigma (FAST: with logistic_fast).
+template <bool FAST = false>
 __device__ __forceinline__ AxisTerm axis_term_inv(float u, float inv, bool grads) {
     const float xp = (u + 0.5f) * inv, xm = (u - 0.5f) * inv;
     AxisTerm t;
-    const float lp = logistic(xp), lm = logistic(xm);
+    const float lp = logistic_t<FAST>(xp), lm = logistic_t<FAST>(xm);
     t.v = lp - lm;
     t.du = t.dsigma = 0.0f;
     if (grads) {  // slopes from the values above: S' = S (1 - S) (1.6 + 0.21 x^2)

@@ -164,32 +164,6 @@ __global__ void __launch_bounds__(AlphaCfg<FC>::NT) k_render_alpha_fwd(
     }
 }
 
-// Sums of K values across the warp with K - 1 + log2(32 / K) shuffles instead of
-// 5 K (K a power of two <= 32): at each of the first log2(K) xor levels a lane
-// keeps half of its values and adds its partner's copy of that half, so after
-// them lane l holds value (l >> (5 - log2 K)) summed over the K lanes those
-// levels joined; the remaining butterfly levels finish the sum.  Returns that
-// lane's total; the summation order is fixed, so results are reproducible.
-template <int K>
-__device__ __forceinline__ float warp_reduce_scatter(float (&x)[K]) {
-    static_assert(K >= 1 && K <= 32 && (K & (K - 1)) == 0, "K must be a power of two <= 32");
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int k = K, off = 16; k > 1; k >>= 1, off >>= 1) {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int i = 0; i < k / 2; ++i) {
-            const float send = upper ? x[i] : x[i + k / 2];
-            const float keep = upper ? x[i + k / 2] : x[i];
-            x[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-    }
-    float v = x[0];
-#pragma unroll
-    for (int off = 16 / K; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    return v;
-}
-
 __host__ __device__ constexpr int pow2_ceil32(int v) { return v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : v <= 8 ? 8 : v <= 16 ? 16 : 32; }
 __host__ __device__ constexpr int log2_32(int v) { return v >= 32 ? 5 : v >= 16 ? 4 : v >= 8 ? 3 : v >= 4 ? 2 : v >= 2 ? 1 : 0; }
 

@@ -18,13 +18,17 @@
 // reaches about half of the tile's patches, so the masks remove three quarters
 // of the pixel evaluations.
 //
+// The logistic is the fast form (logistic_fast: __expf and the approximate
+// reciprocal, within about one ulp of S); the elementwise integral keeps the
+// accurate one.
+//
 // Forward: each warp walks the batch's entries that reach its patch (ballots of
 // the mask bits, so the walk is warp-uniform) and accumulates its 32 pixels.
 // Backward: the tile's dL/dimage sits in shared memory in patch order; warps take
 // entries one at a time from a shared counter, each lane evaluating its pixel of
 // every patch the entry reaches and summing dL/d(u_h, u_l) (in the entry's
-// frame), dL/d(theta), dL/d(sigma_h), dL/d(sigma_l) and dF; one butterfly
-// reduction per entry gives the warp's totals, and after the batch one thread
+// frame), dL/d(theta), dL/d(sigma_h), dL/d(sigma_l) and dF; one reduce-scatter
+// per entry (a plain butterfly above 32 sums) gives the warp's totals, and after the batch one thread
 // per entry turns them into d_xy and d_conic (frame_grad) and writes the pair
 // row.  The rows feed the per-Gaussian reduce of the additive path with
 // rows_dxy set.
@@ -131,8 +135,8 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_fwd(int F, int H
                 const float4 a = s_a[j], q = s_b[j];
                 const float dx = fpx - a.x, dy = fpy - a.y;
                 const float uh = a.z * dx + a.w * dy, ul = -a.w * dx + a.z * dy;
-                const float ih = logistic((uh + 0.5f) * q.x) - logistic((uh - 0.5f) * q.x);
-                const float il = logistic((ul + 0.5f) * q.y) - logistic((ul - 0.5f) * q.y);
+                const float ih = logistic_fast((uh + 0.5f) * q.x) - logistic_fast((uh - 0.5f) * q.x);
+                const float il = logistic_fast((ul + 0.5f) * q.y) - logistic_fast((ul - 0.5f) * q.y);
                 const float wgt = q.z * ih * il;
 #pragma unroll
                 for (int c = 0; c < FC; ++c) acc[c] = fmaf(wgt, s_f[j][c], acc[c]);
@@ -152,6 +156,13 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+
+// Power-of-two width holding the 5 + FC per-entry sums; 0 above a warp's 32.
+template <int FC>
+struct SumWidth {
+    static constexpr int n = 5 + FC;
+    static constexpr int value = n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 0;
+};
 
 template <int FC>
 __global__ void __launch_bounds__(kAnThreads) k_render_analytic_bwd(
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_bwd(
                 const float fpy = static_cast<float>(ty0 + patch_y0(p) + (lane >> 3));
                 const float dx = fpx - a.x, dy = fpy - a.y;
                 const float uh = a.z * dx + a.w * dy, ul = -a.w * dx + a.z * dy;
-                const AxisTerm ih = axis_term_inv(uh, q.x, true), il = axis_term_inv(ul, q.y, true);
+                const AxisTerm ih = axis_term_inv<true>(uh, q.x, true), il = axis_term_inv<true>(ul, q.y, true);
                 const float wgt = q.z * ih.v * il.v;
                 float dLdw = 0.0f;
 #pragma unroll
@@ -239,21 +250,37 @@ __global__ void __launch_bounds__(kAnThreads) k_render_analytic_bwd(
                 Gh = fmaf(gk, il.v * fmaf(ih.v, q.x, ih.dsigma), Gh);  // d(2 pi s_h s_l I_h I_l)/ds_h
                 Gl = fmaf(gk, ih.v * fmaf(il.v, q.y, il.dsigma), Gl);
             }
-            Sa = warp_sum(Sa);
-            Sb = warp_sum(Sb);
-            Gt = warp_sum(Gt);
-            Gh = warp_sum(Gh);
-            Gl = warp_sum(Gl);
+            constexpr int V = SumWidth<FC>::value;
+            if constexpr (V > 0) {
+                float v[V];
+                v[0] = Sa;
+                v[1] = Sb;
+                v[2] = Gt;
+                v[3] = Gh;
+                v[4] = Gl;
 #pragma unroll
-            for (int c = 0; c < FC; ++c) dF[c] = warp_sum(dF[c]);
-            if (lane == 0) {
-                s_sum[j][0] = Sa;
-                s_sum[j][1] = Sb;
-                s_sum[j][2] = Gt;
-                s_sum[j][3] = Gh;
-                s_sum[j][4] = Gl;
+                for (int i = 5; i < V; ++i) v[i] = i - 5 < FC ? dF[i - 5] : 0.0f;
+                const float t = warp_reduce_scatter<V>(v);  // lane l: total of v[l >> kShift]
+                constexpr int kShift = V == 8 ? 2 : V == 16 ? 1 : 0;
+                const int idx = lane >> kShift;
+                if ((lane & ((1 << kShift) - 1)) == 0 && idx < 5 + FC) s_sum[j][idx] = t;
+            } else {
+                Sa = warp_sum(Sa);
+                Sb = warp_sum(Sb);
+                Gt = warp_sum(Gt);
+                Gh = warp_sum(Gh);
+                Gl = warp_sum(Gl);
 #pragma unroll
-                for (int c = 0; c < FC; ++c) s_sum[j][5 + c] = dF[c];
+                for (int c = 0; c < FC; ++c) dF[c] = warp_sum(dF[c]);
+                if (lane == 0) {
+                    s_sum[j][0] = Sa;
+                    s_sum[j][1] = Sb;
+                    s_sum[j][2] = Gt;
+                    s_sum[j][3] = Gh;
+                    s_sum[j][4] = Gl;
+#pragma unroll
+                    for (int c = 0; c < FC; ++c) s_sum[j][5 + c] = dF[c];
+                }
             }
         }
         __syncthreads();
