@@ -135,10 +135,21 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_fwd(int F, int H, int W, int 
     }
 }
 
-// Per-pair sums over the pixels of tile t inside the entry's box: one thread per
-// list entry, the tile's dL/dimage staged in shared memory.  Rows (Sx, Sy,
-// d_conic, dF) land at the entry's gid-major pair slot, as in the additive
-// backward, so k_reduce_gaussian finishes the per-Gaussian gradients.
+// Per-pair sums over the pixels of tile t inside the entry's box.  The tile's
+// dL/dimage sits in shared memory; the CTA's warps take list entries from a
+// shared counter, and a warp's lanes share out the pixels of the entry's box
+// clipped to the tile and the image (w x h of them, lane k taking pixels k,
+// k + 32, ... in row order), so small boxes keep most lanes busy.  One warp
+// reduce-scatter per entry leaves the 5 + F sums in the lanes that write them,
+// and a tile with few entries still keeps every warp busy.  Rows (Sx, Sy,
+// d_conic, dF) land at the entry's gid-major pair slot, as in the additive backward, so
+// k_reduce_gaussian finishes the per-Gaussian gradients.
+template <int FC>
+struct NdSumWidth {  // power-of-two width holding the 5 + FC sums; 0 above a warp's 32
+    static constexpr int n = 5 + FC;
+    static constexpr int value = n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : 0;
+};
+
 template <int FC>
 __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int ntx, const float* __restrict__ prec,
                                                         const int4* __restrict__ box,
@@ -149,47 +160,61 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
                                                         const float* __restrict__ grad_image,
                                                         float* __restrict__ pairgrad, int pstride) {
     constexpr int RS = NdCfg<FC>::RS;
+    static_assert(kNdThreads == kTilePixels, "one thread per pixel for staging");
     __shared__ float s_go[FC][kTilePixels];
+    __shared__ int s_next;
+    const int lane = static_cast<int>(threadIdx.x) & 31;
     const int tile = blockIdx.x;
     const int tile_x = tile % ntx, tile_y = tile / ntx;
     const int tx0 = tile_x * kTile, ty0 = tile_y * kTile;
     const int64_t plane = static_cast<int64_t>(H) * W;
     {
-        const int px = tx0 + (threadIdx.x & (kTile - 1)), py = ty0 + (threadIdx.x >> 4);
+        const int px = tx0 + (static_cast<int>(threadIdx.x) & (kTile - 1)), py = ty0 + (static_cast<int>(threadIdx.x) >> 4);
         const bool in = px < W && py < H;
 #pragma unroll
         for (int c = 0; c < FC; ++c) {
             s_go[c][threadIdx.x] = in && c < F ? grad_image[c * plane + static_cast<int64_t>(py) * W + px] : 0.0f;
         }
     }
+    if (threadIdx.x == 0) s_next = 0;
     __syncthreads();
-    const int beg = tile_offsets[tile], end = tile_offsets[tile + 1];
-    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kNdThreads) {
-        const int g = gid_sorted[e];
+    const int beg = tile_offsets[tile], cnt = tile_offsets[tile + 1] - beg;
+    for (;;) {
+        int j = 0;
+        if (lane == 0) j = atomicAdd(&s_next, 1);
+        j = __shfl_sync(0xffffffffu, j, 0);
+        if (j >= cnt) break;
+        const int g = gid_sorted[beg + j];
         const int4 bx = box[g];
-        const float4* rec = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * RS);
-        const float4 g0 = rec[0];
-        float r[RS - 4];
-#pragma unroll
-        for (int v = 0; v < (RS - 4) / 4; ++v) {
-            const float4 t = rec[1 + v];
-            r[4 * v + 0] = t.x;
-            r[4 * v + 1] = t.y;
-            r[4 * v + 2] = t.z;
-            r[4 * v + 3] = t.w;
-        }
         const int x_lo = max(bx.x, tx0) - tx0, x_hi = min(min(bx.z, tx0 + kTile), W) - tx0;
         const int y_lo = max(bx.y, ty0) - ty0, y_hi = min(min(bx.w, ty0 + kTile), H) - ty0;
+        const int bw = x_hi - x_lo, npix = bw > 0 && y_hi > y_lo ? bw * (y_hi - y_lo) : 0;
         float Sx = 0.0f, Sy = 0.0f, Sxx = 0.0f, Sxy = 0.0f, Syy = 0.0f, dF[FC];
 #pragma unroll
         for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
-        for (int ly = y_lo; ly < y_hi; ++ly) {
-            const float dy = static_cast<float>(ty0 + ly) - g0.y;
-            for (int lx = x_lo; lx < x_hi; ++lx) {
+        if (npix > 0) {
+            const float4* rec = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * RS);
+            const float4 g0 = rec[0];
+            float r[RS - 4];
+#pragma unroll
+            for (int v = 0; v < (RS - 4) / 4; ++v) {
+                const float4 t = rec[1 + v];
+                r[4 * v + 0] = t.x;
+                r[4 * v + 1] = t.y;
+                r[4 * v + 2] = t.z;
+                r[4 * v + 3] = t.w;
+            }
+            // row of pixel i of the box: floor((i + 1/2) / w) is exact in fp32 here (i < 256,
+            // w <= 16: the quotient stays at least 1 / 32 from an integer, the rounding below 1e-4)
+            const float inv_w = 1.0f / static_cast<float>(bw);
+            for (int i = lane; i < npix; i += 32) {
+                const int iy = static_cast<int>((static_cast<float>(i) + 0.5f) * inv_w);
+                const int lx = x_lo + (i - iy * bw), ly = y_lo + iy;
+                const int p = ly * kTile + lx;
                 const float dx = static_cast<float>(tx0 + lx) - g0.x;
+                const float dy = static_cast<float>(ty0 + ly) - g0.y;
                 const float q = fmaf(dx, fmaf(g0.z, dx, g0.w * dy), (r[0] * dy) * dy);
                 const float wgt = ex2_ftz(q);
-                const int p = ly * kTile + lx;
                 float dLdw = 0.0f;
 #pragma unroll
                 for (int c = 0; c < FC; ++c) {
@@ -208,14 +233,44 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
         const int4 tb = aabb[g];
         const int slot = pair_offset[g] + (tile_y - tb.y) * (tb.z - tb.x) + (tile_x - tb.x);
         float* row = pairgrad + static_cast<int64_t>(slot) * pstride;
-        row[0] = Sx;
-        row[1] = Sy;
-        row[2] = -0.5f * Sxx;
-        row[3] = -Sxy;
-        row[4] = -0.5f * Syy;
+        // row = (Sx, Sy, -Sxx / 2, -Sxy, -Syy / 2, dF): the scalings are exact, so they
+        // go in before the sums
+        constexpr int V = NdSumWidth<FC>::value;
+        if constexpr (V > 0) {
+            float v[V];
+            v[0] = Sx;
+            v[1] = Sy;
+            v[2] = -0.5f * Sxx;
+            v[3] = -Sxy;
+            v[4] = -0.5f * Syy;
 #pragma unroll
-        for (int c = 0; c < FC; ++c) {
-            if (c < F) row[5 + c] = dF[c];
+            for (int i = 5; i < V; ++i) v[i] = i - 5 < FC ? dF[i - 5] : 0.0f;
+            const float t = warp_reduce_scatter<V>(v);  // lane l: the total of v[l >> kShift]
+            constexpr int kShift = V == 8 ? 2 : V == 16 ? 1 : 0;
+            const int idx = lane >> kShift;
+            if ((lane & ((1 << kShift) - 1)) == 0 && idx < 5 + F) row[idx] = t;
+        } else {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                Sx += __shfl_xor_sync(0xffffffffu, Sx, o);
+                Sy += __shfl_xor_sync(0xffffffffu, Sy, o);
+                Sxx += __shfl_xor_sync(0xffffffffu, Sxx, o);
+                Sxy += __shfl_xor_sync(0xffffffffu, Sxy, o);
+                Syy += __shfl_xor_sync(0xffffffffu, Syy, o);
+#pragma unroll
+                for (int c = 0; c < FC; ++c) dF[c] += __shfl_xor_sync(0xffffffffu, dF[c], o);
+            }
+            if (lane == 0) {
+                row[0] = Sx;
+                row[1] = Sy;
+                row[2] = -0.5f * Sxx;
+                row[3] = -Sxy;
+                row[4] = -0.5f * Syy;
+#pragma unroll
+                for (int c = 0; c < FC; ++c) {
+                    if (c < F) row[5 + c] = dF[c];
+                }
+            }
         }
     }
 }
