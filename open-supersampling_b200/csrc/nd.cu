@@ -161,6 +161,8 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
                                                         float* __restrict__ pairgrad, int pstride) {
     constexpr int RS = NdCfg<FC>::RS;
     static_assert(kNdThreads == kTilePixels, "one thread per pixel for staging");
+    // dL/dimage of the tile, row-major with column bit 3 flipped on rows 2 and 3 (mod 4):
+    // rows two apart otherwise share banks, and a warp's lanes span several box rows
     __shared__ float s_go[FC][kTilePixels];
     __shared__ int s_next;
     const int lane = static_cast<int>(threadIdx.x) & 31;
@@ -171,9 +173,11 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
     {
         const int px = tx0 + (static_cast<int>(threadIdx.x) & (kTile - 1)), py = ty0 + (static_cast<int>(threadIdx.x) >> 4);
         const bool in = px < W && py < H;
+        const int ly = static_cast<int>(threadIdx.x) >> 4, lx = static_cast<int>(threadIdx.x) & (kTile - 1);
+        const int at = ly * kTile + (lx ^ ((ly & 2) << 2));
 #pragma unroll
         for (int c = 0; c < FC; ++c) {
-            s_go[c][threadIdx.x] = in && c < F ? grad_image[c * plane + static_cast<int64_t>(py) * W + px] : 0.0f;
+            s_go[c][at] = in && c < F ? grad_image[c * plane + static_cast<int64_t>(py) * W + px] : 0.0f;
         }
     }
     if (threadIdx.x == 0) s_next = 0;
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(kNdThreads) k_nd_bwd(int F, int H, int W, int 
             for (int i = lane; i < npix; i += 32) {
                 const int iy = static_cast<int>((static_cast<float>(i) + 0.5f) * inv_w);
                 const int lx = x_lo + (i - iy * bw), ly = y_lo + iy;
-                const int p = ly * kTile + lx;
+                const int p = ly * kTile + (lx ^ ((ly & 2) << 2));
                 const float dx = static_cast<float>(tx0 + lx) - g0.x;
                 const float dy = static_cast<float>(ty0 + ly) - g0.y;
                 const float q = fmaf(dx, fmaf(g0.z, dx, g0.w * dy), (r[0] * dy) * dy);
