@@ -44,8 +44,8 @@ CONFIGS = {
     "config2": (1080, 1920, 200_000, math.log(2.0), 0.3),
     "config1": (540, 960, 16_384, math.log(1.5), 0.3),
 }
-SURVEY_FLOPS_FWD = 15.0  # FP32 flops per pixel-Gaussian evaluation, forward (+1 exp)
-SURVEY_FLOPS_BWD = 40.0  # backward (+1 exp)
+FLOPS_PER_EVAL_FWD = 15.0  # FP32 flops per pixel-Gaussian evaluation, forward (+1 exp)
+FLOPS_PER_EVAL_BWD = 40.0  # backward (+1 exp)
 
 
 def parse_args():
@@ -59,6 +59,7 @@ def parse_args():
     ap.add_argument("--binning", default="tight3sigma", choices=["tight3sigma", "exact"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config5/config3 objects of the default line")
     return ap.parse_args()
 
 
@@ -219,9 +220,10 @@ class Pipeline:
         if timed:
             self.events[i].record()
 
-    def step(self, d, backward=True, sync=False, timed=True):
+    def step(self, d, backward=True, sync=False, timed=True, reduce=True):
         """One pass of the hot path.  sync=True reads the pair total on the host
-        (and grows the capacity); the first step always does."""
+        (and grows the capacity); the first step always does.  reduce=False stops
+        after the backward's pair rows (the caller runs reduce_range)."""
         lib, chk = self.lib, self._lib.check
         s = torch.cuda.current_stream().cuda_stream
         n, h, w = int(d["xy"].shape[0]), self.h, self.w
@@ -268,30 +270,42 @@ class Pipeline:
                                           rec, None, d["grad"].data_ptr(), self.scratch.data_ptr(), items, items_bytes,
                                           s), "backward_pairs")
         self._mark(5, timed)
-        g = self.grads
-        chk(lib.oss_reduce_pair_grads(n, 3, self.scratch.data_ptr(), self.pair_offset.data_ptr(), self.geo.data_ptr(),
-                                      d["rgb"].data_ptr(),
-                                      d["opacity"].data_ptr(), d["scale"].data_ptr(), d["rot"].data_ptr(),
-                                      g["d_xy"].data_ptr(), g["d_conic"].data_ptr(), g["d_rgb"].data_ptr(),
-                                      g["d_opacity"].data_ptr(), g["d_scale"].data_ptr(), g["d_rot"].data_ptr(), s),
-            "reduce")
+        if reduce:
+            self.reduce_range(d, 0, n)
         self._mark(6, timed)
+
+    def reduce_range(self, d, a, b):
+        """Per-Gaussian gradients of Gaussians [a, b) from the last backward's pair
+        rows (rows are addressed through the absolute pair offsets, so a range is
+        the same launch on offset pointers)."""
+        if b <= a:
+            return
+        g, f4 = self.grads, 4
+        s = torch.cuda.current_stream().cuda_stream
+
+        def at(t, width):
+            return t.data_ptr() + a * width * f4
+
+        self._lib.check(self.lib.oss_reduce_pair_grads(
+            b - a, 3, self.scratch.data_ptr(), at(self.pair_offset, 1), at(self.geo, 8), at(d["rgb"], 3),
+            at(d["opacity"], 1), at(d["scale"], 2), at(d["rot"], 1), at(g["d_xy"], 2), at(g["d_conic"], 3),
+            at(g["d_rgb"], 3), at(g["d_opacity"], 1), at(g["d_scale"], 2), at(g["d_rot"], 1), s), "reduce")
 
     def check_overflow(self):
         """Host read of the overflow flag of the last step (a synchronisation)."""
         if int(self.overflow.item()) != 0:
             raise RuntimeError(f"pair capacity {self.capacity} exceeded ({int(self.total.item())} pairs)")
 
-    def capture(self, d, backward=True):
+    def capture(self, d, backward=True, reduce=True):
         """CUDA graph of one sync-free step (capacity must already be sized)."""
         graph = torch.cuda.CUDAGraph()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            self.step(d, backward=backward, timed=False)  # warm the capture stream
+            self.step(d, backward=backward, timed=False, reduce=reduce)  # warm the capture stream
         torch.cuda.current_stream().wait_stream(side)
         with torch.cuda.graph(graph):
-            self.step(d, backward=backward, timed=False)
+            self.step(d, backward=backward, timed=False, reduce=reduce)
         return graph
 
     def stage_ms(self):
@@ -341,7 +355,7 @@ class AlphaPipeline(Pipeline):
         if need > self.scratch.numel():
             self.scratch = torch.empty((need,), device=self.device, dtype=torch.uint8)
 
-    def step(self, d, backward=True, sync=False, timed=True):
+    def step(self, d, backward=True, sync=False, timed=True, reduce=True):
         lib, chk = self.lib, self._lib.check
         s = torch.cuda.current_stream().cuda_stream
         n, h, w = int(d["xy"].shape[0]), self.h, self.w
@@ -483,7 +497,56 @@ def run_reference(args, rank, world):
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     line["cpu_baseline"]["value"] = value
+    line["reference_cuda_op"] = reference_cuda_op(inp, h, w)
     print(json.dumps(line), flush=True)
+
+
+def reference_cuda_op(inp, h, w, iters=2):
+    """The reference's own CUDA op (its four op sources compiled unmodified for
+    sm_100a into oracle/_ref/_C.so) timed on this box's GPU beside the CPU line,
+    inputs resident, 256 MiB L2 flush before each timed call, CUDA events, median
+    of `iters` after one warm-up.  `public_fwd` is its public forward as it ships
+    (every Gaussian in every tile, rasterizer_fwd.cu:547-564); `tight_bwd` its
+    backward kernel fed its own 3-sigma lists from pair_construction_only.  None
+    when the build or a GPU is missing."""
+    so = ROOT / "oracle" / "_ref" / "_C.so"
+    if not so.exists() or not torch.cuda.is_available():
+        return {"unavailable": "oracle/_ref/_C.so not built" if not so.exists() else "no CUDA device"}
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import build_ref
+
+    ref = build_ref.load_built()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    feat = inp["rgb"] * inp["opacity"][:, None]
+    xy, scale, rot, feat, grad = (torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+                                  for a in (inp["xy"], inp["scale"], inp["rot"], feat, inp["grad"]))
+    flush = torch.empty((256 << 20,), device=dev, dtype=torch.uint8)
+
+    def med_ms(fn):
+        fn()
+        torch.cuda.synchronize()
+        out = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            out.append(e0.elapsed_time(e1))
+        return float(statistics.median(out))
+
+    fwd_ms = med_ms(lambda: ref.rasterize_forward(xy, scale, rot, feat, h, w, 16, True))
+    g_t, off_t, conic_t, tot_t = ref.pair_construction_only(xy, scale, rot, h, w, 16)
+    bin_ms = med_ms(lambda: ref.pair_construction_only(xy, scale, rot, h, w, 16))
+    bwd_ms = med_ms(lambda: ref.rasterize_backward(xy, scale, rot, feat, conic_t, g_t, off_t, grad, h, w, 16))
+    return {"public_fwd_ms": fwd_ms, "public_fwd_mpix_s": h * w / (fwd_ms * 1e-3) / 1e6,
+            "tight_binning_ms": bin_ms, "tight_bwd_ms": bwd_ms, "tight_pairs": int(tot_t),
+            "what": "oss/cuda/src/{bindings.cpp,rasterizer_fwd.cu,rasterizer_bwd.cu,tile_bin_counting_sort.cu} "
+                    "compiled unmodified for sm_100a; public_fwd = _C.rasterize_forward (full-frame lists, "
+                    "bf16-split wmma); tight_bwd = _C.rasterize_backward on pair_construction_only's 3-sigma "
+                    "lists (per-pixel float atomics); inputs resident, L2 flushed, median of "
+                    f"{iters} after a warm-up"}
 
 
 def run_ours(args, rank, world, local):
@@ -582,19 +645,14 @@ def run_ours(args, rank, world, local):
     fp32_peak = sms * 128 * 2 * sm_max * 1e6 / 1e12  # TFLOP/s, FMA = 2 flops
     mufu_peak = sms * 16 * sm_max * 1e6  # exp2 per second
     if stage_avg["backward_pairs"] >= stage_avg["forward"]:
-        kname, kms, fpe = "k_render_bwd (backward per-pair partials)", stage_avg["backward_pairs"], SURVEY_FLOPS_BWD
+        kname, kms, fpe = "k_render_bwd (backward per-pair partials)", stage_avg["backward_pairs"], FLOPS_PER_EVAL_BWD
     else:
-        kname, kms, fpe = "k_render_fwd (forward render)", stage_avg["forward"], SURVEY_FLOPS_FWD
+        kname, kms, fpe = "k_render_fwd (forward render)", stage_avg["forward"], FLOPS_PER_EVAL_FWD
     achieved = evals * fpe / (kms * 1e-3) / 1e12
-    traffic = None
-    tfile = ROOT / "profiles" / "dram_traffic_config2.txt"
-    if tfile.exists() and args.config == "config2" and args.binning == "tight3sigma":
-        for line in tfile.read_text().splitlines():
-            if line.startswith(kname.split()[0] + " "):
-                traffic = float(line.split()[1])
     roofline = {
         "bound": "fp32", "kernel": kname, "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-        "frac": achieved / fp32_peak, "traffic": traffic,
+        "frac": achieved / fp32_peak, "traffic": None,
+        "traffic_note": "DRAM bytes per launch come from ncu, not from this run: profiles/k_render_fwd_bwd_config2.md",
         "peak_note": f"FP32 FMA peak {sms} SMs x 128 lanes x 2 x {sm_max:.0f} MHz (max SM clock of "
                      "MEASURED_PEAKS.json); MEASURED_PEAKS.json holds no FP32 figure",
         "evaluations": evals, "flops_per_evaluation": fpe,
@@ -642,6 +700,12 @@ def run_ours(args, rank, world, local):
         "gpu_launches_per_step": apipe.launches_per_step(),
     }
     del apipe
+
+    # the drop-in default: binning="exact" (lists of the q = 176 ellipse box, whose image
+    # is the reference's full-tail sum), graph-replayed like the headline, plus the
+    # latency of the reference-signature calls, which read the pair total on the host
+    if args.binning != "exact":
+        line["exact"] = exact_line(dev_inp, h, w, n, pixels, flush, world, max(3, min(K, 50)))
 
     # e2e: public autograd API, host buffers in and out.  Steps are pipelined over
     # three streams with two buffer slots: step k+1's inputs upload while step k
@@ -727,25 +791,111 @@ def run_ours(args, rank, world, local):
         run(ke)
         e1.record(s_out)
         torch.cuda.synchronize()
-        e2e_ms = torch.tensor([e0.elapsed_time(e1) / ke], device=device, dtype=torch.float64)
+        e2e_ms_rank = e0.elapsed_time(e1) / ke
+        e2e_ms = torch.tensor([e2e_ms_rank], device=device, dtype=torch.float64)
         if pair_capacity_overflowed(device):
             raise RuntimeError("e2e pair capacity exceeded")
         if world > 1:
             dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
         h2d = slots[0]["hin"].numel() * 4
         d2h = (slots[0]["h_img"].numel() + slots[0]["h_grad"].numel()) * 4
+        # serial latency: one step at a time, upload -> compute -> download, waited for
+        lat_ms = []
+        for _ in range(min(ke, 10)):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            run(1)
+            torch.cuda.synchronize()
+            lat_ms.append((time.perf_counter() - t0) * 1e3)
+        lat = torch.tensor([statistics.median(lat_ms)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(lat, op=dist.ReduceOp.MAX)
         line["e2e"] = {"value": pixels / (float(e2e_ms[0]) * 1e-3) / 1e6, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                       "latency_ms": float(lat[0]),
+                       "rank_ms_per_step": rank_list(float(e2e_ms_rank), world),
                        "d2h_bytes_per_step": d2h, "ms_per_step": float(e2e_ms[0]), "steps": ke,
                        "api": "oss_cuda.rasterize_gaussians(pair_capacity=) + torch.autograd.grad",
                        "copies": "one pinned input block per step in; image (after the forward) and the packed "
                                  "gradients out; upload, compute and download on three streams, two slots; "
                                  "sync-free calls, overflow flag checked after the timed steps"}
 
+    # the batched configs at this N (the driver's scaling run records them beside the headline)
+    if not args.no_batched and args.binning == "tight3sigma":
+        kb = max(3, min(K, 10))
+        del pipe
+        torch.cuda.empty_cache()
+        line["config5"] = config5_object(rank, world, kb, 3)
+        torch.cuda.empty_cache()
+        line["config3"] = config3_object(rank, world, kb, 3)
+        torch.cuda.empty_cache()
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(inp, h, w, args.binning, budget_s=8.0).items()
                                 if k != "ms_per_frame"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def rank_list(v, world):
+    """Every rank's value of v, gathered to all ranks (one all_gather)."""
+    if world == 1:
+        return [v]
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device=torch.device("cuda", torch.cuda.current_device()), dtype=torch.float64)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x) for x in out]
+
+
+def exact_line(d, h, w, n, pixels, flush, world, steps):
+    from oss_cuda import _C, _lib, rasterize_gaussians
+
+    device = d["xy"].device
+    epipe = Pipeline(n, h, w, _lib.BINNING_MODES["exact"], device)
+    for _ in range(3):
+        epipe.step(d, sync=True)
+        flush.zero_()
+    torch.cuda.synchronize()
+    e_ms, e_fwd_ms = time_graphs(epipe, d, steps, flush, world)
+    pairs = epipe.pairs
+    del epipe
+    feat = (d["rgb"] * d["opacity"][:, None]).contiguous()
+
+    def api_fwd():
+        _C.rasterize_forward(d["xy"], d["scale"], d["rot"], feat, h, w, 16, True)
+
+    def api_fwdbwd():
+        leaves = [d[k].detach().requires_grad_(True) for k in ("xy", "scale", "rot", "rgb", "opacity")]
+        img = rasterize_gaussians(leaves[0], leaves[1], leaves[2], leaves[3], h, w, opacity=leaves[4])
+        torch.autograd.grad(img, leaves, d["grad"])
+
+    lat = {}
+    for name, fn in (("reference_signature_fwd_ms", api_fwd), ("autograd_api_fwdbwd_ms", api_fwdbwd)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            total += time.perf_counter() - t0
+        lat[name] = total / steps * 1e3
+    out = torch.tensor([e_ms, e_fwd_ms, lat["reference_signature_fwd_ms"], lat["autograd_api_fwdbwd_ms"]],
+                       device=device, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(out, op=dist.ReduceOp.MAX)
+    return {"fwdbwd_ms_per_frame": float(out[0]), "fwd_ms_per_frame": float(out[1]),
+            "mpix_s": pixels / (float(out[0]) * 1e-3) / 1e6, "pairs": pairs, "steps": steps,
+            "reference_signature_fwd_ms": float(out[2]), "autograd_api_fwdbwd_ms": float(out[3]),
+            "workload": "config inputs with binning='exact' (the default of the reference-signature call): "
+                        "sync-free step replayed from a CUDA graph; the two *_api_* latencies are host wall "
+                        "clock per call with a device sync, each call reading its pair total on the host"}
 
 
 # ----------------------------------------------------------------------------- configs 3-5
@@ -810,7 +960,7 @@ def base_line(args, world, value, ms, workload, scaling, clocks, **extra):
     return line
 
 
-def run_config3(args, rank, world):
+def config3_object(rank, world, steps, warmup, binning="tight3sigma"):
     """Config 3: canvas warp + render at alpha in {1.0, 0.5}; 1080p, N=200k, LR motion
     540x960 (smooth random flow, |m| <= 16 px), batch 8 frames split across ranks."""
     from oss_b200 import CanvasState, warp_canvas
@@ -822,7 +972,7 @@ def run_config3(args, rank, world):
     canvas = CanvasState(inp["xy"], inp["scale"], inp["rot"], inp["opacity"], inp["rgb"], n)
     frames = rank_frames(8, rank, world)
     motions = [torch.from_numpy(smooth_motion(540, 960, 300 + f)[None]).to(device) for f in frames]
-    pipe = Pipeline(n, h, w, _lib.BINNING_MODES[args.binning], device)
+    pipe = Pipeline(n, h, w, _lib.BINNING_MODES[binning], device)
 
     def step_at(alpha):
         def step():
@@ -833,13 +983,23 @@ def run_config3(args, rank, world):
                                "rgb": c.colors}, backward=False, sync=True)
         return step
 
-    ms1, clocks = timed(step_at(1.0), args.steps, args.warmup, device, world)
-    ms05, _ = timed(step_at(0.5), args.steps, args.warmup, device, world)
-    value = 8 * h * w / (ms1 * 1e-3) / 1e6
-    return base_line(args, world, value, ms1, f"config3: warp (GS-STVSR, LR 540x960 -> {w}x{h}) + forward render, "
-                     f"N={n}, alpha=1.0, batch 8 frames split over {world} rank(s), {args.binning} lists",
-                     "strong", clocks, alpha_0p5={"value": 8 * h * w / (ms05 * 1e-3) / 1e6, "ms_per_step": ms05},
-                     ms_per_frame=ms1 / max(1, len(frames)))
+    ms1, clocks = timed(step_at(1.0), steps, warmup, device, world)
+    ms05, _ = timed(step_at(0.5), steps, warmup, device, world)
+    return {"value": 8 * h * w / (ms1 * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms1, "steps": steps,
+            "frames_per_rank": len(frames), "ms_per_frame": ms1 / max(1, len(frames)),
+            "alpha_0p5": {"value": 8 * h * w / (ms05 * 1e-3) / 1e6, "ms_per_step": ms05},
+            "scaling": "strong", "clocks": clocks,
+            "workload": f"config3: warp (GS-STVSR, LR 540x960 -> {w}x{h}) + forward render, N={n}, alpha=1.0 "
+                        f"(alpha_0p5: 0.5), batch 8 frames split over {world} rank(s), {binning} lists"}
+
+
+def run_config3(args, rank, world):
+    obj = config3_object(rank, world, args.steps, args.warmup, args.binning)
+    clocks, workload = obj.pop("clocks"), obj.pop("workload")
+    value, ms = obj.pop("value"), obj.pop("ms_per_step")
+    for k in ("unit", "steps", "scaling"):
+        obj.pop(k)
+    return base_line(args, world, value, ms, workload, "strong", clocks, **obj)
 
 
 def run_config4(args, rank, world):
@@ -873,11 +1033,14 @@ def run_config4(args, rank, world):
                      "strong", clocks, ms_per_frame=ms / max(1, len(frames)))
 
 
-def run_config5(args, rank, world):
+def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
     """Config 5: 64 frames at 1080p split across ranks; each frame renders its own 200k
     canvas plus a shared 50k canvas (fwd+bwd); the shared canvas's per-Gaussian
     gradients (xy 2, scale 2, rot 1, opacity 1, rgb 3) are summed over the rank's
-    frames and all-reduced over NCCL once per step."""
+    frames and all-reduced over NCCL once per step.  The all-reduce runs on a side
+    stream: the last frame reduces its shared Gaussians' gradients first, the
+    all-reduce starts, and the own canvas's reduce of that frame runs beside it."""
+    from oss_b200.distributed import pack_shared_grads, reduce_shared_grads
     from oss_cuda import _lib
 
     h, w, lsm, lss = 1080, 1920, math.log(2.0), 0.3
@@ -890,42 +1053,64 @@ def run_config5(args, rank, world):
         own = make_inputs(h, w, n_own, lsm, lss, seed=10_000 + f)
         per_frame.append({k: torch.from_numpy(np.concatenate([own[k], shared[k]]) if k != "grad" else own[k]).to(device)
                           for k in own})
-    pipe = Pipeline(n_own + n_shared, h, w, _lib.BINNING_MODES[args.binning], device)
-    from oss_b200.distributed import pack_shared_grads, reduce_shared_grads
-
+    pipe = Pipeline(n_own + n_shared, h, w, _lib.BINNING_MODES[binning], device)
     d_shared = torch.zeros((n_shared, 9), device=device, dtype=torch.float32)
+    comm = torch.cuda.Stream()
+    ev_ready, ev_done = torch.cuda.Event(), torch.cuda.Event()
     ar_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     sl = slice(n_own, n_own + n_shared)
 
     # size the pair capacity over every frame (host reads of the totals), then capture one
-    # sync-free CUDA graph per frame; a step replays them, accumulating the shared canvas's
-    # gradients, and all-reduces those once
+    # sync-free CUDA graph per frame (the last without its per-Gaussian reduce)
     for d in per_frame:
         pipe.step(d, sync=True, timed=False)
     torch.cuda.synchronize()
-    graphs = [pipe.capture(d) for d in per_frame]
+    graphs = [pipe.capture(d, reduce=(i + 1 < len(per_frame))) for i, d in enumerate(per_frame)]
 
     def step():
+        main = torch.cuda.current_stream()
         d_shared.zero_()
-        for g in graphs:
+        for i, g in enumerate(graphs):
             g.replay()
+            if i + 1 == len(graphs):
+                last = per_frame[i]
+                pipe.reduce_range(last, n_own, n_own + n_shared)
             d_shared.add_(pack_shared_grads(pipe.grads, sl))
-        ar_events[0].record()
-        reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
-        ar_events[1].record()
+        ev_ready.record(main)
+        with torch.cuda.stream(comm):
+            comm.wait_event(ev_ready)
+            ar_events[0].record(comm)
+            reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
+            ar_events[1].record(comm)
+            ev_done.record(comm)
+        if graphs:
+            pipe.reduce_range(per_frame[-1], 0, n_own)  # the last frame's own canvas, beside the all-reduce
+        main.wait_event(ev_done)
 
-    ms, clocks = timed(step, args.steps, args.warmup, device, world)
+    ms, clocks = timed(step, steps, warmup, device, world)
     pipe.check_overflow()
     del graphs
-    allreduce = None
-    if world > 1:
-        torch.cuda.synchronize()
-        allreduce = ar_events[0].elapsed_time(ar_events[1])
-    value = 64 * h * w / (ms * 1e-3) / 1e6
-    return base_line(args, world, value, ms, f"config5: 64 frames {w}x{h} split over {world} rank(s), each own "
-                     f"N={n_own} + shared N={n_shared}, fwd+bwd, NCCL all-reduce of the shared canvas gradients "
-                     f"({n_shared}x9 fp32), {args.binning} lists", "strong", clocks,
-                     allreduce_ms_last_step=allreduce, frames_per_rank=len(frames))
+    torch.cuda.synchronize()
+    allreduce = ar_events[0].elapsed_time(ar_events[1])
+    ar = rank_list(allreduce, world)
+    return {"value": 64 * h * w / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "frames_per_rank": len(frames), "ms_per_frame": ms / max(1, len(frames)),
+            "allreduce_ms": max(ar), "allreduce_ms_per_rank": ar, "allreduce_bytes": n_shared * 9 * 4,
+            "scaling": "strong", "clocks": clocks,
+            "workload": f"config5: 64 frames {w}x{h} split over {world} rank(s), each own N={n_own} + shared "
+                        f"N={n_shared}, fwd+bwd, NCCL all-reduce (sum) of the shared canvas gradients "
+                        f"({n_shared}x9 fp32) on a side stream beside the last frame's own-canvas reduce, "
+                        f"{binning} lists; allreduce_ms from the last timed step"}
+
+
+def run_config5(args, rank, world):
+    obj = config5_object(rank, world, args.steps, args.warmup, args.binning)
+    clocks = obj.pop("clocks")
+    workload = obj.pop("workload")
+    value, ms = obj.pop("value"), obj.pop("ms_per_step")
+    for k in ("unit", "steps", "scaling"):
+        obj.pop(k)
+    return base_line(args, world, value, ms, workload, "strong", clocks, **obj)
 
 
 def run_canvas(args, rank, world):

@@ -333,9 +333,11 @@ OSS_API int oss_tile_bin_counting_sort(int64_t n, int64_t num_tiles,
  * library's device image (held by every GPU that loads the library until
  * process exit).  Limits: n <= 262144 entries and num_tiles <= 65536; larger
  * calls fail with OSS_ERR_RANGE.  Calls no cudaMalloc/cudaFree.
- * The first call on each device looks up that device's address of the array
- * (cudaGetSymbolAddress, with the device current); make that first call before
- * any stream capture.  All calls share the one array: calls whose GPU work
+ * Every call looks up the array's address in the calling thread's current
+ * context (cudaGetSymbolAddress), so a device reset or a context the caller made
+ * current itself is picked up; the first call in a context also loads the
+ * library's device code there, so make that first call before any stream
+ * capture.  All calls share the one array: calls whose GPU work
  * overlaps (e.g. on two streams at once) race and must be serialised by the
  * caller.  Each call clears what must start at zero.
  * ------------------------------------------------------------------------- */

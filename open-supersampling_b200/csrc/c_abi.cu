@@ -926,24 +926,19 @@ constexpr int64_t kNoAllocScratchBytes = 5242880;  // 5 MiB >= scratch need at b
 
 static __device__ __align__(256) unsigned char g_tile_bin_scratch[kNoAllocScratchBytes];
 
-constexpr int kNoAllocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
-
-// Device address of g_tile_bin_scratch on the current device.  In host code
-// the array's name only stands in for the symbol, so its address is looked up
-// once per device (with that device current) and cached.
+// Device address of g_tile_bin_scratch in the calling thread's current
+// context.  In host code the array's name only stands in for the symbol, so
+// its address has to be looked up with the device current.  The lookup runs
+// on every call rather than once per device index: a cached address would go
+// stale after cudaDeviceReset, or when an embedding host makes a context of
+// its own current, and a kernel handed that address faults.  Once the
+// library's device code is loaded in a context the lookup is a table read;
+// the first call in a context loads that code (the set-up step).
 int noalloc_scratch(void** out) {
-    int dev = -1;
-    OSS_CUDA_TRY(cudaGetDevice(&dev));
-    OSS_CHECK(dev >= 0 && dev < kNoAllocMaxDevices, OSS_ERR_INVALID, "device index out of range for the no-alloc scratch");
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        OSS_CUDA_TRY(cudaGetSymbolAddress(&p, g_tile_bin_scratch));
-        g_noalloc_ptr[dev] = p;
-    }
-    *out = g_noalloc_ptr[dev];
+    void* p = nullptr;
+    OSS_CUDA_TRY(cudaGetSymbolAddress(&p, g_tile_bin_scratch));
+    OSS_CHECK(p != nullptr, OSS_ERR_CUDA, "cudaGetSymbolAddress returned no address for the no-alloc scratch");
+    *out = p;
     return OSS_OK;
 }
 

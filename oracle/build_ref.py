@@ -80,7 +80,10 @@ def load_built():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("OSS_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("OSS_REFERENCE_DIR"),
+                    help="the reference checkout (default: $OSS_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or OSS_REFERENCE_DIR")
     print(build(Path(args.reference)))
     sys.exit(0)

@@ -58,3 +58,34 @@ def test_noalloc_rejects_sizes_beyond_its_maximum(cuda_device):
     assert "no-alloc maximum" in lib.oss_last_error().decode()
     assert lib.oss_tile_bin_counting_sort_noalloc(16, MAX_TILES + 1, None, None, None, None, stream) == 3
     assert "no-alloc maximum" in lib.oss_last_error().decode()
+
+
+def test_noalloc_leaves_device_memory_untouched(cuda_device):
+    """After the first call in this context (which may load the library's device
+    code), further calls change neither the device's free memory nor torch's
+    allocator: the scratch really is the fixed array."""
+    from oss_cuda import _lib
+
+    lib = _lib.lib()
+    n, num_tiles = 100_000, 8160
+    rng = np.random.default_rng(13)
+    tile_id = torch.from_numpy(rng.integers(0, num_tiles, size=n).astype(np.int32)).to(cuda_device)
+    gid = torch.arange(n, device=cuda_device, dtype=torch.int32)
+    sorted_gid = torch.empty((n,), device=cuda_device, dtype=torch.int32)
+    offsets = torch.empty((num_tiles + 1,), device=cuda_device, dtype=torch.int32)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        rc = lib.oss_tile_bin_counting_sort_noalloc(n, num_tiles, tile_id.data_ptr(), gid.data_ptr(),
+                                                    sorted_gid.data_ptr(), offsets.data_ptr(), stream)
+        _lib.check(rc, "oss_tile_bin_counting_sort_noalloc")
+
+    call()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(cuda_device)[0]
+    torch_bytes0 = torch.cuda.memory_allocated(cuda_device)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda_device)[0] == free0
+    assert torch.cuda.memory_allocated(cuda_device) == torch_bytes0
