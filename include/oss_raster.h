@@ -244,6 +244,47 @@ OSS_API int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad,
                           float* d_scale, float* d_rot, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * One-pass feathered overlapping-tile render: replaces the four phase-shifted
+ * renders and the blend of oss/sr/v6/rasterizer.py:159-242
+ * (V6Rasterizer._render_overlapped, _phase_feather_mask, _cosine_ramp), reached
+ * through rasterize_gaussians(..., overlap=o).  Each Gaussian becomes up to four
+ * virtual Gaussians 4 g + k (a second centre per axis only where the reference's
+ * shifted mean x + o rounds in fp32); each carries its tile hull (vaabb, 4 ints),
+ * its packed forward record (vprec, oss_entry_record_floats(f) floats, centre of
+ * its phases) and its window (vwin, 4 ints: packed int16 [lo, hi) phase tile
+ * ranges).  The image is the reference's sum over phases of mask * render /
+ * sum of masks, evaluated once per pixel and list entry with the separable
+ * feather window in the exponent.  Pipeline: prepare_feathered -> oss_bin_pairs
+ * over the 4N virtual Gaussians (mode tight3sigma: the lists follow vaabb) ->
+ * forward_feathered (records + entry_pat when a backward follows) ->
+ * oss_backward_items + backward_feathered -> reduce_pair_grads_feathered (sums
+ * the four variants' rows of each Gaussian).  F <= 16, overlap > 0, at most
+ * 32767 tiles per axis; oss_feather_supported says whether a call qualifies. */
+OSS_API int oss_feather_supported(int32_t overlap, int64_t f, int64_t h, int64_t w);
+OSS_API int64_t oss_feather_virtual_count(int64_t n);
+OSS_API int64_t oss_render_prepare_feathered_scratch_bytes(int64_t n);
+OSS_API int oss_render_prepare_feathered(int64_t n, int64_t h, int64_t w, int32_t mode, int32_t overlap,
+                                         const float* xy, const float* scale, const float* rot, int64_t f,
+                                         const float* feat, const float* opacity, float* conic, float* geo,
+                                         int32_t* vaabb, int32_t* vpair_offset, float* vprec, int32_t* vwin,
+                                         int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets,
+                                         void* scratch, int64_t scratch_bytes, void* stream);
+OSS_API int oss_render_forward_feathered(int64_t n, int64_t f, int64_t h, int64_t w, int32_t overlap,
+                                         const float* vprec, const int32_t* vwin, const int32_t* gid_sorted,
+                                         const int32_t* tile_offsets, float* image, float* records,
+                                         uint16_t* entry_pat, void* stream);
+OSS_API int oss_render_backward_feathered(int64_t n, int64_t f, int64_t h, int64_t w, int32_t overlap,
+                                          const int32_t* vaabb, const int32_t* vpair_offset, int64_t total_pairs,
+                                          const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                          const float* records, const uint16_t* entry_pat, const float* grad_image,
+                                          float* pairgrad, void* items, int64_t items_bytes, void* stream);
+OSS_API int oss_reduce_pair_grads_feathered(int64_t n, int64_t f, const float* pairgrad, const int32_t* vpair_offset,
+                                            const float* geo, const float* feat, const float* opacity,
+                                            const float* scale, const float* rot, float* d_xy, float* d_conic,
+                                            float* d_feat, float* d_opacity, float* d_scale, float* d_rot,
+                                            void* stream);
+
+/* ---------------------------------------------------------------------------
  * Alpha-blend mode (blend="alpha"; no reference counterpart -- the reference
  * rasterizer is additive only).  Over lists ordered by (depth, gid) (sort_key
  * = rank from oss_depth_order), per pixel front to back:

@@ -78,7 +78,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 7; }
+int oss_abi_version(void) { return 8; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -443,6 +443,145 @@ int oss_reduce_pair_grads(int64_t n, int64_t f, const float* pairgrad, const int
                                                    oss_pair_grad_stride(f), pair_offset, geo, feat, opacity, scale, rot,
                                                    d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot,
                                                    as_stream(stream)));
+    return OSS_OK;
+}
+
+// ---- one-pass feathered overlapping-tile render -------------------------------
+
+namespace {
+
+int check_feather(int32_t overlap, int64_t f, const Grid& g, oss::FeatherTable* tab) {
+    OSS_CHECK(overlap > 0, OSS_ERR_INVALID, "overlap must be positive");
+    OSS_CHECK(f >= 0 && f <= 16, OSS_ERR_INVALID, "the feathered render takes F in [0, 16]");
+    OSS_CHECK((static_cast<int64_t>(g.w) + overlap + oss::kTile - 1) / oss::kTile <= oss::kFeatherMaxTiles &&
+                  (static_cast<int64_t>(g.h) + overlap + oss::kTile - 1) / oss::kTile <= oss::kFeatherMaxTiles,
+              OSS_ERR_RANGE, "the feathered render takes at most 32767 tiles per axis");
+    OSS_CHECK(oss::feather_table(overlap, tab) != 0, OSS_ERR_RANGE,
+              "overlap too wide for the one-pass feathered render (its weight sum could reach the 1e-6 clamp)");
+    return OSS_OK;
+}
+
+}  // namespace
+
+int oss_feather_supported(int32_t overlap, int64_t f, int64_t h, int64_t w) {
+    Grid g;
+    if (check_grid(0, h, w, g) != OSS_OK) return 0;
+    oss::FeatherTable tab;
+    return check_feather(overlap, f, g, &tab) == OSS_OK ? 1 : 0;
+}
+
+int64_t oss_feather_virtual_count(int64_t n) { return (n < 0 ? 0 : n) * oss::kFeatherVariants; }
+
+int64_t oss_render_prepare_feathered_scratch_bytes(int64_t n) {
+    return oss::scan_fused_scratch_bytes(oss_feather_virtual_count(n));
+}
+
+int oss_render_prepare_feathered(int64_t n, int64_t h, int64_t w, int32_t mode, int32_t overlap, const float* xy,
+                                 const float* scale, const float* rot, int64_t f, const float* feat,
+                                 const float* opacity, float* conic, float* geo, int32_t* vaabb, int32_t* vpair_offset,
+                                 float* vprec, int32_t* vwin, int64_t* total_pairs, int32_t* tile_count,
+                                 int32_t* tile_offsets, void* scratch, int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    if ((rc = check_mode(mode)) != OSS_OK) return rc;
+    if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
+    oss::FeatherTable tab;
+    if ((rc = check_feather(overlap, f, g, &tab)) != OSS_OK) return rc;
+    const int64_t nv = oss_feather_virtual_count(n);
+    OSS_CHECK(nv <= INT_MAX, OSS_ERR_RANGE, "4 N exceeds int32 range");
+    OSS_CHECK(vpair_offset != nullptr && total_pairs != nullptr, OSS_ERR_INVALID,
+              "vpair_offset and total_pairs must be non-null");
+    OSS_CHECK(g.tiles == 0 || (tile_count != nullptr && tile_offsets != nullptr), OSS_ERR_INVALID,
+              "tile_count and tile_offsets must be non-null");
+    OSS_CHECK(scratch_bytes >= oss_render_prepare_feathered_scratch_bytes(n), OSS_ERR_SCRATCH,
+              "render_prepare_feathered scratch too small");
+    if (g.n > 0) {
+        OSS_CHECK(conic != nullptr && geo != nullptr && vaabb != nullptr && vprec != nullptr && vwin != nullptr,
+                  OSS_ERR_INVALID, "outputs must be non-null");
+        OSS_CHECK(aligned(geo, 16) && aligned(vaabb, 16) && aligned(vprec, 16) && aligned(vwin, 16), OSS_ERR_INVALID,
+                  "geo, vaabb, vprec and vwin must be 16-byte aligned");
+        OSS_CHECK(f == 0 || feat != nullptr, OSS_ERR_INVALID, "feat must be non-null");
+        OSS_CHECK(scratch != nullptr && aligned(scratch, 8), OSS_ERR_INVALID, "scratch must be 8-byte aligned");
+    }
+    cudaStream_t s = as_stream(stream);
+    if (g.tiles > 0) OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
+    long long* block_sums = static_cast<long long*>(scratch);
+    OSS_CUDA_TRY(oss::launch_prepare_feathered(g.n, g.h, g.w, mode, overlap, xy, scale, rot, static_cast<int>(f), feat,
+                                               opacity, conic, geo, vaabb, vpair_offset, vprec, vwin, block_sums,
+                                               g.tiles > 0 ? tile_count : nullptr, s));
+    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(vpair_offset, vpair_offset, nv, block_sums, total_pairs,
+                                                 g.tiles > 0 ? tile_count : nullptr, oss::kTileCountStride, g.tiles,
+                                                 g.tiles > 0 ? tile_offsets : nullptr, s));
+    return OSS_OK;
+}
+
+int oss_render_forward_feathered(int64_t n, int64_t f, int64_t h, int64_t w, int32_t overlap, const float* vprec,
+                                 const int32_t* vwin, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                 float* image, float* records, uint16_t* entry_pat, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    oss::FeatherTable tab;
+    if ((rc = check_feather(overlap, f, g, &tab)) != OSS_OK) return rc;
+    if (g.tiles == 0 || f == 0) return OSS_OK;
+    OSS_CHECK(tile_offsets != nullptr && image != nullptr, OSS_ERR_INVALID, "tile_offsets and image must be non-null");
+    OSS_CHECK(g.n == 0 || (vprec != nullptr && aligned(vprec, 16) && vwin != nullptr && aligned(vwin, 16)),
+              OSS_ERR_INVALID, "vprec and vwin (16-byte aligned) must be non-null");
+    OSS_CHECK((records == nullptr) == (entry_pat == nullptr), OSS_ERR_INVALID, "records and entry_pat go together");
+    OSS_CHECK(records == nullptr || aligned(records, 16), OSS_ERR_INVALID, "records must be 16-byte aligned");
+    OSS_CUDA_TRY(oss::launch_render_forward_feathered(static_cast<int>(f), g.h, g.w, tab, vprec, vwin, gid_sorted,
+                                                      tile_offsets, image, records, entry_pat, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_render_backward_feathered(int64_t n, int64_t f, int64_t h, int64_t w, int32_t overlap, const int32_t* vaabb,
+                                  const int32_t* vpair_offset, int64_t total_pairs, const int32_t* gid_sorted,
+                                  const int32_t* tile_offsets, const float* records, const uint16_t* entry_pat,
+                                  const float* grad_image, float* pairgrad, void* items, int64_t items_bytes,
+                                  void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    oss::FeatherTable tab;
+    if ((rc = check_feather(overlap, f, g, &tab)) != OSS_OK) return rc;
+    OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
+    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+              "backward item table too small");
+    if (g.n == 0 || total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    OSS_CHECK(vaabb != nullptr && aligned(vaabb, 16) && vpair_offset != nullptr, OSS_ERR_INVALID,
+              "vaabb (16-byte aligned) and vpair_offset must be non-null");
+    OSS_CHECK(records != nullptr && aligned(records, 16) && entry_pat != nullptr, OSS_ERR_INVALID,
+              "the forward's records (16-byte aligned) and entry_pat must be non-null");
+    OSS_CHECK(pairgrad != nullptr && aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CHECK(items != nullptr && aligned(items, 16), OSS_ERR_INVALID, "items must be 16-byte aligned");
+    OSS_CHECK(gid_sorted != nullptr && tile_offsets != nullptr && grad_image != nullptr, OSS_ERR_INVALID,
+              "lists and grad_image must be non-null");
+    OSS_CUDA_TRY(oss::launch_render_backward_feathered(static_cast<int>(f), g.h, g.w, total_pairs, tab, gid_sorted,
+                                                       tile_offsets, grad_image, vaabb, vpair_offset, records,
+                                                       entry_pat, pairgrad, oss_pair_grad_stride(f), items,
+                                                       as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_reduce_pair_grads_feathered(int64_t n, int64_t f, const float* pairgrad, const int32_t* vpair_offset,
+                                    const float* geo, const float* feat, const float* opacity, const float* scale,
+                                    const float* rot, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                                    float* d_scale, float* d_rot, void* stream) {
+    OSS_CHECK(n >= 0 && oss_feather_virtual_count(n) <= INT_MAX, OSS_ERR_RANGE, "4 N exceeds int32 range");
+    OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(vpair_offset != nullptr && d_xy != nullptr && d_conic != nullptr, OSS_ERR_INVALID,
+              "vpair_offset, d_xy and d_conic must be non-null");
+    OSS_CHECK(geo != nullptr && aligned(geo, 16), OSS_ERR_INVALID, "geo must be 16-byte aligned");
+    OSS_CHECK(f == 0 || (feat != nullptr && d_feat != nullptr), OSS_ERR_INVALID, "feat and d_feat must be non-null");
+    OSS_CHECK(d_scale == nullptr || (scale != nullptr && rot != nullptr && d_rot != nullptr), OSS_ERR_INVALID,
+              "d_scale needs scale, rot and d_rot");
+    OSS_CHECK(pairgrad == nullptr || aligned(pairgrad, 16), OSS_ERR_INVALID, "pairgrad must be 16-byte aligned");
+    OSS_CUDA_TRY(oss::launch_reduce_gaussian_grads(static_cast<int>(n), static_cast<int>(f), pairgrad,
+                                                   oss_pair_grad_stride(f), vpair_offset, geo, feat, opacity, scale,
+                                                   rot, d_xy, d_conic, d_feat, d_opacity, d_scale, d_rot,
+                                                   as_stream(stream), false, oss::kFeatherVariants));
     return OSS_OK;
 }
 

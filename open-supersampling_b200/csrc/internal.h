@@ -182,6 +182,39 @@ cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const
 cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, float alpha, const float* xy,
                                   float* out_xy, uint8_t* in_frame, cudaStream_t stream);
 
+// ---- feather.cu --------------------------------------------------------------
+// One-pass feathered overlapping-tile render.  Gaussian g becomes up to
+// kFeatherVariants virtual Gaussians 4 g + k; each carries its packed forward
+// record (centre of its phases), its tile hull in vaabb / vcount, and its window
+// in vwin: four packed [lo, hi) tile ranges (phase 0 and phase 1 along x, then
+// along y; phase-1 ranges in phase-0 tile units).  Ranges are int16.
+constexpr int kFeatherVariants = 4;
+constexpr int kFeatherMaxTiles = 32767;
+// log2 of the normalised feather weight of an entry at tile column (or row) c
+// for the phase-bit pattern p = [phase 0 covers the tile] | [phase 1 covers the
+// column's phase-1 tile, left part] << 1 | [... right part] << 2; -inf where 0.
+struct FeatherTable {
+    float lw[8][16];
+};
+// Fills the table; returns 0 when the reference's clamp of the weight sum at
+// 1e-6 could be active (very wide overlaps), where the separable form fails.
+int feather_table(int overlap, FeatherTable* tab);
+__host__ __device__ inline int pack_range(int lo, int hi) {
+    return static_cast<int>((static_cast<uint32_t>(lo) & 0xffffu) | (static_cast<uint32_t>(hi) << 16));
+}
+__host__ __device__ inline int range_lo(int v) { return static_cast<int16_t>(v & 0xffff); }
+__host__ __device__ inline int range_hi(int v) { return v >> 16; }
+// Phase-bit pattern of tile index t for the packed phase-0 range r0 and
+// phase-1 range r1 (see FeatherTable).
+__host__ __device__ inline int feather_pattern(int r0, int r1, int t) {
+    const int lo0 = range_lo(r0), hi0 = range_hi(r0), lo1 = range_lo(r1), hi1 = range_hi(r1);
+    return (lo0 <= t && t < hi0 ? 1 : 0) | (lo1 <= t && t < hi1 ? 2 : 0) | (lo1 <= t + 1 && t + 1 < hi1 ? 4 : 0);
+}
+cudaError_t launch_prepare_feathered(int n, int h, int w, int mode, int overlap, const float* xy, const float* scale,
+                                     const float* rot, int f, const float* feat, const float* opacity, float* conic,
+                                     float* geo, int32_t* vaabb, int32_t* vcount, float* vprec, int32_t* vwin,
+                                     long long* block_sums, int32_t* tile_count, cudaStream_t stream);
+
 // ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
 // Entry records (forward -> backward): floats per record for f channels.
 int entry_record_floats(int f);
@@ -192,6 +225,13 @@ cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const f
                                   const int32_t* tile_offsets, float* image, const int32_t* aabb,
                                   const int32_t* pair_offset, float* records, int32_t* slots,
                                   const float* prec, cudaStream_t stream);
+
+// The windowed forward of the one-pass feathered render over virtual Gaussians
+// (launch_prepare_feathered): f <= 16.  With records, entry_pat receives each
+// list entry's phase-bit patterns (x | y << 8) for the backward.
+cudaError_t launch_render_forward_feathered(int f, int h, int w, const FeatherTable& tab, const float* vprec,
+                                           const int32_t* vwin, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                           float* image, float* records, uint16_t* entry_pat, cudaStream_t stream);
 
 // Per-pair partial gradients.  Deterministic mode (pairgrad != null): rows
 // (Sx, Sy, d_conic, dF) of pair_stride floats at pair_offset[g] + local tile
@@ -216,6 +256,14 @@ cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pair
                                          float* pairgrad, int pair_stride,
                                          float* d_xy, float* d_conic, float* d_feat, void* items_scratch,
                                          cudaStream_t stream);
+// The backward of the windowed feathered forward (records and entry_pat of
+// launch_render_forward_feathered, items of launch_backward_items), per-pair
+// rows at the virtual Gaussians' gid-major slots; f <= 16.
+cudaError_t launch_render_backward_feathered(int f, int h, int w, int64_t total_pairs, const FeatherTable& tab,
+                                            const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                            const float* grad_image, const int32_t* vaabb, const int32_t* vpair_offset,
+                                            const float* records, const uint16_t* entry_pat, float* pairgrad,
+                                            int pair_stride, void* items_scratch, cudaStream_t stream);
 int backward_pair_stride(int f);
 int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles);
 cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, int pair_stride,
@@ -223,7 +271,7 @@ cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, in
                                          const float* opacity, const float* scale, const float* rot,
                                          float* d_xy, float* d_conic, float* d_feat,
                                          float* d_opacity, float* d_scale, float* d_rot,
-                                         cudaStream_t stream, bool rows_dxy = false);
+                                         cudaStream_t stream, bool rows_dxy = false, int vstride = 1);
 
 // ---- raster_alpha.cu -------------------------------------------------------
 // Front-to-back alpha compositing over (depth, gid)-ordered lists, its

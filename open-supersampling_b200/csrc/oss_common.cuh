@@ -176,6 +176,28 @@ __device__ __forceinline__ void conic_grad_to_scale_rot(float raw_sx, float raw_
     d_rot = __fadd_rn(__fadd_rn(t0, t1), t2);
 }
 
+// The same chain rule in double, for gradients summed in double: a thin
+// Gaussian's d_scale and d_rot are small differences of d_conic terms, which
+// the fp32 form rounds before they cancel.
+__device__ __forceinline__ void conic_grad_to_scale_rot_f64(float raw_sx, float raw_sy, float theta, double dca,
+                                                            double dcb, double dcd, float& d_sx, float& d_sy,
+                                                            float& d_rot) {
+    const double sx = fmax(static_cast<double>(raw_sx), static_cast<double>(kMinScale));
+    const double sy = fmax(static_cast<double>(raw_sy), static_cast<double>(kMinScale));
+    const double inv_sx2 = 1.0 / (sx * sx);
+    const double inv_sy2 = 1.0 / (sy * sy);
+    const double diff = inv_sx2 - inv_sy2;
+    double s, c;
+    sincos(static_cast<double>(theta), &s, &c);
+    const double cc = c * c, ss = s * s, cs = c * s;
+    const double d_inv_sx2 = cc * dca + cs * dcb + ss * dcd;
+    const double d_inv_sy2 = ss * dca - cs * dcb + cc * dcd;
+    const double rx = raw_sx, ry = raw_sy;
+    d_sx = raw_sx > kMinScale ? static_cast<float>(d_inv_sx2 * (-2.0 / (rx * rx * rx))) : 0.0f;
+    d_sy = raw_sy > kMinScale ? static_cast<float>(d_inv_sy2 * (-2.0 / (ry * ry * ry))) : 0.0f;
+    d_rot = static_cast<float>(dca * (-2.0 * cs * diff) + dcb * diff * (cc - ss) + dcd * (2.0 * cs * diff));
+}
+
 // Per-mode AABB parameters.
 __host__ __device__ inline float mode_tau(int mode) { return mode == OSS_BIN_EXACT ? kTauExact : kTauTight; }
 // Fallback radius factor for degenerate conics: 3*max(s) for the 3-sigma lists

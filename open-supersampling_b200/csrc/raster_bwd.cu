@@ -70,27 +70,32 @@ __device__ __forceinline__ bool regular_conic_bwd(float x, float y, float a, flo
 // halving the FP32 instructions per pixel; exp2 stays one MUFU op per pixel.
 // The column offsets dx and their squares are held in registers, so the
 // moments take g dx and g dx^2 as one FFMA2 each.
-template <int FC, bool CHECK>
+// With WIN (the one-pass feathered render) the entry's log2 window weights by
+// column (lwx) and row (lwy) enter the exponent: the column's folded into a
+// per-column constant A dx^2 + lwx, the row's into D dy^2.
+template <int FC, bool CHECK, bool WIN = false>
 __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go, int r0, int r1, float fx0, float fy0,
                                                  float gx, float gy, float A, float B, float D, const float (&fv)[FC],
                                                  float (&dF)[FC], float& Sx, float& Sy, float& Sxx, float& Sxy,
-                                                 float& Syy) {
+                                                 float& Syy, const float* __restrict__ lwx = nullptr,
+                                                 const float* __restrict__ lwy = nullptr) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int ROW = BwdCfg<FC>::ROW;
     float2 dx2[kTile / 2], dxsq2[kTile / 2];
+    float2 cx2[WIN ? kTile / 2 : 1];
+    const float2 A2 = make_float2(A, A);
 #pragma unroll
     for (int j = 0; j < kTile / 2; ++j) {
         dx2[j] = make_float2((fx0 + static_cast<float>(2 * j)) - gx, (fx0 + static_cast<float>(2 * j + 1)) - gx);
         dxsq2[j] = __fmul2_rn(dx2[j], dx2[j]);
+        if constexpr (WIN) cx2[j] = __ffma2_rn(A2, dxsq2[j], make_float2(lwx[2 * j], lwx[2 * j + 1]));
     }
-    const float2 A2 = make_float2(A, A);
     float2 f2[FC], dF2[FC];
 #pragma unroll
     for (int k = 0; k < FC; ++k) {
         f2[k] = make_float2(fv[k], fv[k]);
         dF2[k] = make_float2(0.0f, 0.0f);
     }
-    float2 Sxx2 = make_float2(0.0f, 0.0f);
 #pragma unroll 1
     for (int r = r0; r < r1; ++r) {
         const float dy = (fy0 + static_cast<float>(r)) - gy;
@@ -98,15 +103,32 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
         const float ddy = (D * dy) * dy;
         const float2 bdy2 = make_float2(bdy, bdy);
         const float2 ddy2 = make_float2(ddy, ddy);
-        float2 rowG2 = make_float2(0.0f, 0.0f), rowGx2 = make_float2(0.0f, 0.0f);
+        float2 ddyw2 = ddy2;
+        if constexpr (WIN) {
+            const float t = ddy + lwy[r];
+            ddyw2 = make_float2(t, t);
+        }
+        float2 rowG2 = make_float2(0.0f, 0.0f), rowGx2 = make_float2(0.0f, 0.0f), rowGxx2 = make_float2(0.0f, 0.0f);
         const float* go_row = s_go + r * ROW;
 #pragma unroll
         for (int j = 0; j < kTile / 2; ++j) {
             const float2 dx = dx2[j];
-            const float2 q = __ffma2_rn(dx, __ffma2_rn(A2, dx, bdy2), ddy2);
             float2 w;
-            w.x = CHECK ? (q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f) : ex2_ftz(q.x);
-            w.y = CHECK ? (q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f) : ex2_ftz(q.y);
+            if constexpr (WIN) {
+                const float2 q = __ffma2_rn(dx, bdy2, __fadd2_rn(cx2[j], ddyw2));
+                if (CHECK) {
+                    const float2 q0 = __ffma2_rn(dx, __ffma2_rn(A2, dx, bdy2), ddy2);  // the q >= 0 test, unwindowed
+                    w.x = q0.x <= 0.0f ? ex2_ftz(q.x) : 0.0f;
+                    w.y = q0.y <= 0.0f ? ex2_ftz(q.y) : 0.0f;
+                } else {
+                    w.x = ex2_ftz(q.x);
+                    w.y = ex2_ftz(q.y);
+                }
+            } else {
+                const float2 q = __ffma2_rn(dx, __ffma2_rn(A2, dx, bdy2), ddy2);
+                w.x = CHECK ? (q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f) : ex2_ftz(q.x);
+                w.y = CHECK ? (q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f) : ex2_ftz(q.y);
+            }
             const float4* go4 = reinterpret_cast<const float4*>(go_row + j * 2 * SG);
             float2 go2[SG];
 #pragma unroll
@@ -122,17 +144,18 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
             for (int k = 0; k < FC; ++k) dF2[k] = __ffma2_rn(w, go2[k], dF2[k]);
             const float2 gw = __fmul2_rn(w, dLdw);
             rowGx2 = __ffma2_rn(gw, dx, rowGx2);
-            Sxx2 = __ffma2_rn(gw, dxsq2[j], Sxx2);
+            rowGxx2 = __ffma2_rn(gw, dxsq2[j], rowGxx2);
             rowG2 = __fadd2_rn(rowG2, gw);
         }
         const float rowGx = rowGx2.x + rowGx2.y;
         const float rowG = rowG2.x + rowG2.y;
+        // every moment is summed per row first (16 terms), then over the rows
+        Sxx += rowGxx2.x + rowGxx2.y;
         Sx += rowGx;
         Sxy = fmaf(rowGx, dy, Sxy);
         Sy = fmaf(rowG, dy, Sy);
         Syy = fmaf(rowG * dy, dy, Syy);
     }
-    Sxx += Sxx2.x + Sxx2.y;
 #pragma unroll
     for (int k = 0; k < FC; ++k) dF[k] += dF2[k].x + dF2[k].y;
 }
@@ -141,28 +164,41 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
 // column offsets dx are hoisted into registers, each row hoists B*dy and
 // D*dy*dy, and the column loop is fully unrolled.  CHECK keeps the reference's
 // q >= 0 test per pixel.
-template <int FC, bool CHECK>
+template <int FC, bool CHECK, bool WIN = false>
 __device__ __forceinline__ void bwd_rows_full(const float* __restrict__ s_go, int r0, int r1, float fx0, float fy0,
                                               float gx, float gy, float A, float B, float D, const float (&fv)[FC],
                                               float (&dF)[FC], float& Sx, float& Sy, float& Sxx, float& Sxy,
-                                              float& Syy) {
+                                              float& Syy, const float* __restrict__ lwx = nullptr,
+                                              const float* __restrict__ lwy = nullptr) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int ROW = BwdCfg<FC>::ROW;
     float dxs[kTile];
 #pragma unroll
     for (int c = 0; c < kTile; ++c) dxs[c] = (fx0 + static_cast<float>(c)) - gx;
+    // rows are summed in fp32, the rows' sums in double: five double adds per row
+    // against 16 pixels of F + 12 fp32 operations, and a thin Gaussian's moments
+    // cancel across rows
+    double dSx = 0.0, dSy = 0.0, dSxx = 0.0, dSxy = 0.0, dSyy = 0.0;
 #pragma unroll 1
     for (int r = r0; r < r1; ++r) {
         const float dy = (fy0 + static_cast<float>(r)) - gy;
         const float bdy = B * dy;
         const float ddy2 = (D * dy) * dy;
-        float rowG = 0.0f, rowGx = 0.0f;
+        const float lwr = WIN ? lwy[r] : 0.0f;
+        // four interleaved partial sums per moment (columns c mod 4), added pairwise
+        float pG[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pGx[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pGxx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         const float* go_row = s_go + r * ROW;
 #pragma unroll
         for (int c = 0; c < kTile; ++c) {
             const float dx = dxs[c];
             const float q = fmaf(dx, fmaf(A, dx, bdy), ddy2);
-            const float w = CHECK ? (q <= 0.0f ? ex2_ftz(q) : 0.0f) : ex2_ftz(q);
+            float w;
+            if constexpr (WIN) {
+                const float qw = q + (lwx[c] + lwr);
+                w = CHECK ? (q <= 0.0f ? ex2_ftz(qw) : 0.0f) : ex2_ftz(qw);
+            } else {
+                w = CHECK ? (q <= 0.0f ? ex2_ftz(q) : 0.0f) : ex2_ftz(q);
+            }
             const float4* go4 = reinterpret_cast<const float4*>(go_row + c * SG);
             float go[SG];
 #pragma unroll
@@ -181,32 +217,47 @@ __device__ __forceinline__ void bwd_rows_full(const float* __restrict__ s_go, in
             }
             const float gw = w * dLdw;
             const float gdx = gw * dx;
-            rowGx += gdx;
-            Sxx = fmaf(gdx, dx, Sxx);
-            rowG += gw;
+            pGx[c & 3] += gdx;
+            pGxx[c & 3] = fmaf(gdx, dx, pGxx[c & 3]);
+            pG[c & 3] += gw;
         }
-        Sx += rowGx;
-        Sxy = fmaf(rowGx, dy, Sxy);
-        Sy = fmaf(rowG, dy, Sy);
-        Syy = fmaf(rowG * dy, dy, Syy);
+        const float rowGx = (pGx[0] + pGx[1]) + (pGx[2] + pGx[3]);
+        const float rowGxx = (pGxx[0] + pGxx[1]) + (pGxx[2] + pGxx[3]);
+        const float rowG = (pG[0] + pG[1]) + (pG[2] + pG[3]);
+        const double ddy = dy;
+        dSxx += rowGxx;
+        dSx += rowGx;
+        dSxy += static_cast<double>(rowGx) * ddy;
+        dSy += static_cast<double>(rowG) * ddy;
+        dSyy += static_cast<double>(rowG) * ddy * ddy;
     }
+    Sx += static_cast<float>(dSx);
+    Sy += static_cast<float>(dSy);
+    Sxx += static_cast<float>(dSxx);
+    Sxy += static_cast<float>(dSxy);
+    Syy += static_cast<float>(dSyy);
 }
 
 // Same sums for a tile cut by the image border (ncol < 16 or rows beyond H).
-template <int FC>
+template <int FC, bool WIN = false>
 __device__ __forceinline__ void bwd_rows_edge(const float* __restrict__ s_go, int r0, int r1, int ncol, int tx0,
                                               int ty0, float gx, float gy, float A, float B, float D,
                                               const float (&fv)[FC], float (&dF)[FC], float& Sx, float& Sy,
-                                              float& Sxx, float& Sxy, float& Syy) {
+                                              float& Sxx, float& Sxy, float& Syy, const float* __restrict__ lwx = nullptr,
+                                              const float* __restrict__ lwy = nullptr) {
     constexpr int ROW = BwdCfg<FC>::ROW;
+    double dSx = 0.0, dSy = 0.0, dSxx = 0.0, dSxy = 0.0, dSyy = 0.0;  // as bwd_rows_full
     for (int r = r0; r < r1; ++r) {
+        const float lwr = WIN ? lwy[r] : 0.0f;
         const float dy = static_cast<float>(ty0 + r) - gy;
-        float rowG = 0.0f, rowGx = 0.0f;
+        float pG[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pGx[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pGxx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         const float* go_row = s_go + r * ROW;
-        for (int c = 0; c < ncol; ++c) {
+#pragma unroll
+        for (int c = 0; c < kTile; ++c) {  // unrolled, so the partials stay in registers
+            if (c >= ncol) break;
             const float dx = static_cast<float>(tx0 + c) - gx;
             const float q = q_scaled(A, B, D, dx, dy);
-            const float w = q <= 0.0f ? ex2_ftz(q) : 0.0f;
+            const float w = q <= 0.0f ? ex2_ftz(WIN ? q + (lwx[c] + lwr) : q) : 0.0f;
             float go[FC];
 #pragma unroll
             for (int k = 0; k < FC; ++k) go[k] = s_go[go_index<FC>(r, c, k)];
@@ -219,15 +270,25 @@ __device__ __forceinline__ void bwd_rows_edge(const float* __restrict__ s_go, in
             }
             const float gw = w * dLdw;
             const float gdx = gw * dx;
-            rowGx += gdx;
-            Sxx = fmaf(gdx, dx, Sxx);
-            rowG += gw;
+            pGx[c & 3] += gdx;
+            pGxx[c & 3] = fmaf(gdx, dx, pGxx[c & 3]);
+            pG[c & 3] += gw;
         }
-        Sx += rowGx;
-        Sxy = fmaf(rowGx, dy, Sxy);
-        Sy = fmaf(rowG, dy, Sy);
-        Syy = fmaf(rowG * dy, dy, Syy);
+        const float rowGx = (pGx[0] + pGx[1]) + (pGx[2] + pGx[3]);
+        const float rowGxx = (pGxx[0] + pGxx[1]) + (pGxx[2] + pGxx[3]);
+        const float rowG = (pG[0] + pG[1]) + (pG[2] + pG[3]);
+        const double ddy = dy;
+        dSxx += rowGxx;
+        dSx += rowGx;
+        dSxy += static_cast<double>(rowGx) * ddy;
+        dSy += static_cast<double>(rowG) * ddy;
+        dSyy += static_cast<double>(rowG) * ddy * ddy;
     }
+    Sx += static_cast<float>(dSx);
+    Sy += static_cast<float>(dSy);
+    Sxx += static_cast<float>(dSxx);
+    Sxy += static_cast<float>(dSxy);
+    Syy += static_cast<float>(dSyy);
 }
 
 __device__ __forceinline__ float group_sum(float v, int k) {
@@ -252,20 +313,30 @@ __device__ __forceinline__ int take_item(uint32_t* work, uint32_t limit, int bas
     return base + static_cast<int>(__shfl_sync(0xffffffffu, v, 0));
 }
 
-template <int FC, int MODE>
-__global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_render_bwd(
+// With WIN (the one-pass feathered render, records mode only) each entry's
+// phase-bit patterns come from the forward's entry_pat and select its rows of
+// the log2 window table, kept in shared memory after the warp slots; the
+// window's column terms take 16 more registers (4 CTAs per SM for F <= 4).
+template <int FC, int MODE, bool WIN = false>
+__global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdCfg<FC>::MIN_CTAS) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
     const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted, const int4* __restrict__ items,
     const int32_t* __restrict__ num_items, uint32_t* __restrict__ work, const float* __restrict__ grad_image,
     const int4* __restrict__ aabb, const int32_t* __restrict__ pair_offset, const float* __restrict__ records,
     const int32_t* __restrict__ slots, float* __restrict__ pairgrad, int pstride, float* __restrict__ d_xy,
-    float* __restrict__ d_conic, float* __restrict__ d_feat) {
+    float* __restrict__ d_conic, float* __restrict__ d_feat, const uint16_t* __restrict__ entry_pat,
+    const FeatherTable tab) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int RS = 4 + ((1 + FC + 3) / 4) * 4;  // entry record floats (the forward's layout)
     extern __shared__ float4 s_mem4[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     float* s_go = reinterpret_cast<float*>(s_mem4) + warp * BwdCfg<FC>::SLOT;
+    float* s_lw = reinterpret_cast<float*>(s_mem4) + BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT;
+    if constexpr (WIN) {
+        for (int i = threadIdx.x; i < 8 * kTile; i += BwdCfg<FC>::THREADS) s_lw[i] = tab.lw[i / kTile][i % kTile];
+        __syncthreads();
+    }
     const int n_items = *num_items;
     const uint32_t limit = static_cast<uint32_t>(n_items) - 1u;
     const int grid_warps = static_cast<int>(gridDim.x) * BwdCfg<FC>::WARPS;
@@ -367,6 +438,13 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
         // the same test on (-A, -B/2, -D) = k (a, b, d) with k = 0.5 log2(e) > 0 (records carry no raw conic)
         const bool regular = !active || regular_conic_bwd(g0.x, g0.y, -g0.z, -0.5f * g0.w, -g1.x);
         const bool warp_regular = __all_sync(0xffffffffu, regular);
+        const float* lwx = nullptr;
+        const float* lwy = nullptr;
+        if constexpr (WIN) {
+            const int pat = active ? static_cast<int>(entry_pat[first + e]) : 0;  // idle lanes: an all-zero window
+            lwx = s_lw + (pat & 0xff) * kTile;
+            lwy = s_lw + (pat >> 8) * kTile;
+        }
 
         float dF[FC];
 #pragma unroll
@@ -377,21 +455,24 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, BwdCfg<FC>::MIN_CTAS) k_r
             const float fx0 = static_cast<float>(tx0), fy0 = static_cast<float>(ty0);
             if (warp_regular) {
                 if constexpr (BwdCfg<FC>::PAIRED) {
-                    bwd_rows_full_pk<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
-                                                Syy);
+                    bwd_rows_full_pk<FC, false, WIN>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx,
+                                                     Sxy, Syy, lwx, lwy);
                 } else {
-                    bwd_rows_full<FC, false>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+                    bwd_rows_full<FC, false, WIN>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                                  Syy, lwx, lwy);
                 }
             } else {
                 if constexpr (BwdCfg<FC>::PAIRED) {
-                    bwd_rows_full_pk<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
-                                               Syy);
+                    bwd_rows_full_pk<FC, true, WIN>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx,
+                                                    Sxy, Syy, lwx, lwy);
                 } else {
-                    bwd_rows_full<FC, true>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+                    bwd_rows_full<FC, true, WIN>(s_go, r0, r1, fx0, fy0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy,
+                                                 Syy, lwx, lwy);
                 }
             }
         } else {
-            bwd_rows_edge<FC>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy);
+            bwd_rows_edge<FC, WIN>(s_go, r0, r1, ncol, tx0, ty0, g0.x, g0.y, A, B, D, fv, dF, Sx, Sy, Sxx, Sxy, Syy,
+                                   lwx, lwy);
         }
         if (k > 1) {  // combine the k row bands of each entry (all lanes take part)
             Sx = group_sum(Sx, k);
@@ -592,11 +673,12 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
                                                          float* __restrict__ d_xy, float* __restrict__ d_conic,
                                                          float* __restrict__ d_feat, float* __restrict__ d_opacity,
                                                          float* __restrict__ d_scale, float* __restrict__ d_rot,
-                                                         int rows_dxy) {
+                                                         int rows_dxy, int vstride) {
     const int g = blockIdx.x * 256 + threadIdx.x;
     if (g >= n) return;
-    const int beg = pair_offset[g];
-    const int end = pair_offset[g + 1];
+    // a Gaussian's rows: its vstride virtual Gaussians' rows, contiguous in gid-major order
+    const int beg = pair_offset[static_cast<int64_t>(g) * vstride];
+    const int end = pair_offset[static_cast<int64_t>(g + 1) * vstride];
     // per-Gaussian inputs of the epilogue, loaded ahead of the row sums so their
     // latency overlaps them
     const float4 k1 = reinterpret_cast<const float4*>(geo + static_cast<int64_t>(g) * 8)[1];
@@ -607,10 +689,12 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
         sc = make_float2(scale[2 * g], scale[2 * g + 1]);
         th = rot[g];
     }
-    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
-    float dF[FC];
+    // the rows of a Gaussian are summed in double: a handful of adds per Gaussian,
+    // and the per-pair partials often cancel
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0, s4 = 0.0;
+    double dF[FC];
 #pragma unroll
-    for (int c = 0; c < FC; ++c) dF[c] = 0.0f;
+    for (int c = 0; c < FC; ++c) dF[c] = 0.0;
     if (FC <= 3) {
         // rows four at a time, all loads issued before the (in-order) sums
         for (int p = beg; p < end; p += 4) {
@@ -655,24 +739,25 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
     }
     // (s0, s1) = (sum Sx, sum Sy); the raw conic (a, b, d) is geo[g][5..7].  Rows of
     // weights other than exp(-q/2) hold d_xy itself (rows_dxy).
-    d_xy[2 * g + 0] = rows_dxy ? s0 : fmaf(k1.y, s0, k1.z * s1);
-    d_xy[2 * g + 1] = rows_dxy ? s1 : fmaf(k1.z, s0, k1.w * s1);
-    d_conic[3 * g + 0] = s2;
-    d_conic[3 * g + 1] = s3;
-    d_conic[3 * g + 2] = s4;
-    float dop = 0.0f;
+    d_xy[2 * g + 0] = static_cast<float>(rows_dxy ? s0 : static_cast<double>(k1.y) * s0 + static_cast<double>(k1.z) * s1);
+    d_xy[2 * g + 1] = static_cast<float>(rows_dxy ? s1 : static_cast<double>(k1.z) * s0 + static_cast<double>(k1.w) * s1);
+    const float c2 = static_cast<float>(s2), c3 = static_cast<float>(s3), c4 = static_cast<float>(s4);
+    d_conic[3 * g + 0] = c2;
+    d_conic[3 * g + 1] = c3;
+    d_conic[3 * g + 2] = c4;
+    double dop = 0.0;
 #pragma unroll
     for (int c = 0; c < FC; ++c) {
         if (c < F) {
             const int64_t kk = static_cast<int64_t>(g) * F + c;
-            d_feat[kk] = dF[c] * op;
-            dop = fmaf(dF[c], feat[kk], dop);
+            d_feat[kk] = static_cast<float>(dF[c] * static_cast<double>(op));
+            dop += dF[c] * static_cast<double>(feat[kk]);
         }
     }
-    if (d_opacity != nullptr) d_opacity[g] = dop;
+    if (d_opacity != nullptr) d_opacity[g] = static_cast<float>(dop);
     if (d_scale != nullptr) {
         float dsx, dsy, dr;
-        conic_grad_to_scale_rot(sc.x, sc.y, th, s2, s3, s4, dsx, dsy, dr);
+        conic_grad_to_scale_rot_f64(sc.x, sc.y, th, s2, s3, s4, dsx, dsy, dr);
         d_scale[2 * g + 0] = dsx;
         d_scale[2 * g + 1] = dsy;
         d_rot[g] = dr;
@@ -681,7 +766,7 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
 
 // Persistent grid of the backward: as many CTAs as fit on the device at once
 // (cached per device), never more than the table's largest item count needs.
-template <int FC, int MODE>
+template <int FC, int MODE, bool WIN = false>
 int bwd_grid(int64_t max_items, int smem) {
     static int cached[64] = {0};
     const int64_t need = div_up(max_items, BwdCfg<FC>::WARPS);
@@ -690,7 +775,7 @@ int bwd_grid(int64_t max_items, int smem) {
     if (cached[dev] == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE>, BwdCfg<FC>::THREADS, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE, WIN>, BwdCfg<FC>::THREADS, smem);
         cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
     }
     return static_cast<int>(need < cached[dev] ? need : cached[dev]);
@@ -708,7 +793,25 @@ cudaError_t launch_bwd_mode(int f, int h, int w, int ntx, int64_t max_items, con
     const unsigned blocks = static_cast<unsigned>(bwd_grid<FC, MODE>(max_items, smem));
     kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
         f, h, w, ntx, geo, feat, opacity, gid_sorted, items, num_items, work, grad_image,
-        reinterpret_cast<const int4*>(aabb), pair_offset, records, slots, pairgrad, pstride, d_xy, d_conic, d_feat);
+        reinterpret_cast<const int4*>(aabb), pair_offset, records, slots, pairgrad, pstride, d_xy, d_conic, d_feat,
+        nullptr, FeatherTable{});
+    return cudaGetLastError();
+}
+
+template <int FC>
+cudaError_t launch_bwd_win(int f, int h, int w, int ntx, int64_t max_items, const int32_t* gid_sorted,
+                           const int4* items, const int32_t* num_items, uint32_t* work, const float* grad_image,
+                           const int32_t* aabb, const int32_t* pair_offset, const float* records,
+                           const uint16_t* entry_pat, const FeatherTable& tab, float* pairgrad, int pstride,
+                           cudaStream_t stream) {
+    const int smem = (BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT + 8 * kTile) * static_cast<int>(sizeof(float));
+    auto kern = k_render_bwd<FC, kDetRecords, true>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const unsigned blocks = static_cast<unsigned>(bwd_grid<FC, kDetRecords, true>(max_items, smem));
+    kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
+        f, h, w, ntx, nullptr, nullptr, nullptr, gid_sorted, items, num_items, work, grad_image,
+        reinterpret_cast<const int4*>(aabb), pair_offset, records, nullptr, pairgrad, pstride, nullptr, nullptr,
+        nullptr, entry_pat, tab);
     return cudaGetLastError();
 }
 
@@ -738,10 +841,10 @@ template <int FC>
 cudaError_t launch_reduce_fc(int n, int f, const float* pairgrad, int pstride, const int32_t* pair_offset,
                              const float* geo, const float* feat, const float* opacity, const float* scale,
                              const float* rot, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
-                             float* d_scale, float* d_rot, bool rows_dxy, cudaStream_t stream) {
+                             float* d_scale, float* d_rot, bool rows_dxy, int vstride, cudaStream_t stream) {
     k_reduce_gaussian<FC><<<static_cast<unsigned>(div_up(n, 256)), 256, 0, stream>>>(
         n, f, pairgrad, pstride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, d_feat, d_opacity,
-        d_scale, d_rot, rows_dxy ? 1 : 0);
+        d_scale, d_rot, rows_dxy ? 1 : 0, vstride);
     return cudaGetLastError();
 }
 
@@ -803,6 +906,34 @@ cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pair
 #undef OSS_BWD_CALL
 }
 
+cudaError_t launch_render_backward_feathered(int f, int h, int w, int64_t total_pairs, const FeatherTable& tab,
+                                            const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                            const float* grad_image, const int32_t* vaabb, const int32_t* vpair_offset,
+                                            const float* records, const uint16_t* entry_pat, float* pairgrad,
+                                            int pair_stride, void* items_scratch, cudaStream_t stream) {
+    (void)tile_offsets;
+    const int ntx = static_cast<int>(div_up(w, kTile));
+    const int nty = static_cast<int>(div_up(h, kTile));
+    const int num_tiles = ntx * nty;
+    if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
+    const int64_t max_items = backward_max_items(total_pairs, num_tiles);
+    Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
+    const int4* items = arena.take<int4>(max_items);
+    int32_t* counters = arena.take<int32_t>(2);
+    const int32_t* num_items = counters;
+    uint32_t* work = reinterpret_cast<uint32_t*>(counters + 1);
+#define OSS_BWD_WIN(FC)                                                                                           \
+    launch_bwd_win<FC>(f, h, w, ntx, max_items, gid_sorted, items, num_items, work, grad_image, vaabb, vpair_offset, \
+                       records, entry_pat, tab, pairgrad, pair_stride, stream)
+    if (f <= 1) return OSS_BWD_WIN(1);
+    if (f <= 3) return OSS_BWD_WIN(3);
+    if (f <= 4) return OSS_BWD_WIN(4);
+    if (f <= 8) return OSS_BWD_WIN(8);
+    if (f <= 16) return OSS_BWD_WIN(16);
+    return cudaErrorInvalidValue;
+#undef OSS_BWD_WIN
+}
+
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo, const float* feat,
                                          const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
@@ -820,11 +951,11 @@ cudaError_t launch_reduce_gaussian_grads(int n, int f, const float* pairgrad, in
                                          const int32_t* pair_offset, const float* geo, const float* feat,
                                          const float* opacity, const float* scale, const float* rot, float* d_xy,
                                          float* d_conic, float* d_feat, float* d_opacity, float* d_scale,
-                                         float* d_rot, cudaStream_t stream, bool rows_dxy) {
+                                         float* d_rot, cudaStream_t stream, bool rows_dxy, int vstride) {
     if (n == 0) return cudaSuccess;
 #define OSS_RED_CALL(FC)                                                                                          \
     launch_reduce_fc<FC>(n, f, pairgrad, pair_stride, pair_offset, geo, feat, opacity, scale, rot, d_xy, d_conic, \
-                         d_feat, d_opacity, d_scale, d_rot, rows_dxy, stream)
+                         d_feat, d_opacity, d_scale, d_rot, rows_dxy, vstride, stream)
     return OSS_DISPATCH_FC(f, OSS_RED_CALL);
 #undef OSS_RED_CALL
 }

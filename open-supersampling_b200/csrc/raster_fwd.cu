@@ -126,18 +126,49 @@ __device__ __forceinline__ void fwd_batch(int cnt, const float4* __restrict__ s_
     }
 }
 
-// fwd_batch on pixel pairs: acc2[p][c] holds pixels 2p and 2p+1.
-template <int FC, bool CHECK, bool SKIP>
+// Feather window of the one-pass overlapped render (csrc/feather.cu): per entry
+// the phase-bit patterns of its tile column and row ranges (s_pat), and the
+// tables of log2 window weights by pattern for this thread's column (s_lwx,
+// [pattern][column]) and for its PX rows (s_lwy, [pattern][row step][PX]).
+struct FwdWin {
+    const uchar2* pat;
+    const float* lwx;
+    const float* lwy;
+    int lx, ly;
+};
+
+// fwd_batch on pixel pairs: acc2[p][c] holds pixels 2p and 2p+1.  With WIN the
+// log2 window weights of the entry's column and rows are added to q'.
+template <int FC, bool CHECK, bool SKIP, bool WIN = false>
 __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__ s_geo,
                                              const float* __restrict__ s_df,
                                              const unsigned char* __restrict__ s_skip, float fpx,
                                              const float2 (&fpy2)[FwdCfg<FC>::PX / 2],
-                                             float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
-    constexpr int NP = FwdCfg<FC>::PX / 2;
+                                             float2 (&acc2)[FwdCfg<FC>::PX / 2][FC], FwdWin win = {}) {
+    constexpr int PX = FwdCfg<FC>::PX;
+    constexpr int NP = PX / 2;
     constexpr int S = FwdCfg<FC>::S;
+    constexpr int ROWSTEP = kTile / PX;
 #pragma unroll 4
     for (int j = 0; j < cnt; ++j) {
         if (SKIP && s_skip[j]) continue;  // exact zero at every pixel of the tile (same for every thread)
+        float lw[PX];
+        float lwc = 0.0f;
+        if constexpr (WIN) {
+            const uchar2 pt = win.pat[j];
+            lwc = win.lwx[pt.x * kTile + win.lx];
+            const float* ly = win.lwy + (pt.y * ROWSTEP + win.ly) * PX;
+            if constexpr (PX == 4) {
+                const float4 t = *reinterpret_cast<const float4*>(ly);
+                lw[0] = t.x;
+                lw[1] = t.y;
+                lw[2 % PX] = t.z;
+                lw[3 % PX] = t.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < PX; ++k) lw[k] = ly[k];
+            }
+        }
         const float4 g0 = s_geo[j];
         const float4* df4 = reinterpret_cast<const float4*>(s_df + j * S);
         float r[S];
@@ -156,17 +187,33 @@ __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__
         const float2 D2 = make_float2(r[0], r[0]);
         const float2 b2 = make_float2(bdx, bdx);
         const float2 a2 = make_float2(adx2, adx2);
+        const float2 c2 = make_float2(adx2 + lwc, adx2 + lwc);
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
             const float2 dy = __fadd2_rn(fpy2[p], ngy);
-            const float2 q = __ffma2_rn(dy, __ffma2_rn(D2, dy, b2), a2);
             float2 w;
-            if (CHECK) {
-                w.x = q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f;
-                w.y = q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f;
+            if constexpr (WIN) {
+                // q' with the window's log2 weights: the column's folded into the constant
+                // term, the row's added per pixel pair
+                const float2 t = __ffma2_rn(D2, dy, b2);
+                const float2 q = __ffma2_rn(dy, t, __fadd2_rn(c2, make_float2(lw[2 * p], lw[2 * p + 1])));
+                if (CHECK) {
+                    const float2 q0 = __ffma2_rn(dy, t, a2);  // the reference's q >= 0 test, without the window
+                    w.x = q0.x <= 0.0f ? ex2_ftz(q.x) : 0.0f;
+                    w.y = q0.y <= 0.0f ? ex2_ftz(q.y) : 0.0f;
+                } else {
+                    w.x = ex2_ftz(q.x);
+                    w.y = ex2_ftz(q.y);
+                }
             } else {
-                w.x = ex2_ftz(q.x);
-                w.y = ex2_ftz(q.y);
+                const float2 q = __ffma2_rn(dy, __ffma2_rn(D2, dy, b2), a2);
+                if (CHECK) {
+                    w.x = q.x <= 0.0f ? ex2_ftz(q.x) : 0.0f;
+                    w.y = q.y <= 0.0f ? ex2_ftz(q.y) : 0.0f;
+                } else {
+                    w.x = ex2_ftz(q.x);
+                    w.y = ex2_ftz(q.y);
+                }
             }
 #pragma unroll
             for (int c = 0; c < FC; ++c) acc2[p][c] = __ffma2_rn(w, make_float2(r[1 + c], r[1 + c]), acc2[p][c]);
@@ -176,17 +223,17 @@ __device__ __forceinline__ void fwd_batch_pk(int cnt, const float4* __restrict__
 
 // Batch loop with its per-pixel sign test only where a conic is irregular and
 // its entry skip only where some entry of the batch is zero over the tile.
-template <int FC>
+template <int FC, bool WIN = false>
 __device__ __forceinline__ void fwd_batch_pk_sel(bool regular, bool skip, int cnt, const float4* s_geo,
                                                  const float* s_df, const unsigned char* s_skip, float fpx,
                                                  const float2 (&fpy2)[FwdCfg<FC>::PX / 2],
-                                                 float2 (&acc2)[FwdCfg<FC>::PX / 2][FC]) {
+                                                 float2 (&acc2)[FwdCfg<FC>::PX / 2][FC], FwdWin win = {}) {
     if (regular) {
-        if (skip) fwd_batch_pk<FC, false, true>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
-        else fwd_batch_pk<FC, false, false>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+        if (skip) fwd_batch_pk<FC, false, true, WIN>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2, win);
+        else fwd_batch_pk<FC, false, false, WIN>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2, win);
     } else {
-        if (skip) fwd_batch_pk<FC, true, true>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
-        else fwd_batch_pk<FC, true, false>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2);
+        if (skip) fwd_batch_pk<FC, true, true, WIN>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2, win);
+        else fwd_batch_pk<FC, true, false, WIN>(cnt, s_geo, s_df, s_skip, fpx, fpy2, acc2, win);
     }
 }
 
@@ -375,13 +422,21 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
-template <int FC>
+// With WIN (the one-pass feathered render, csrc/feather.cu) every entry also
+// carries its virtual Gaussian's packed phase ranges (win, staged beside the
+// record), from which the staging pass derives the entry's phase-bit patterns
+// for this tile (and stores them for the backward in entry_pat, with the
+// records); the math adds the tabulated log2 window weights to q'.
+template <int FC, bool WIN>
 __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H, int W, int ntx, int num_tiles,
                                                                      const float* __restrict__ prec,
                                                                      const int32_t* __restrict__ gid_sorted,
                                                                      const int32_t* __restrict__ tile_offsets,
                                                                      float* __restrict__ image,
-                                                                     float* __restrict__ records) {
+                                                                     float* __restrict__ records,
+                                                                     const int4* __restrict__ win,
+                                                                     uint16_t* __restrict__ entry_pat,
+                                                                     const FeatherTable tab) {
     constexpr int PX = FwdCfg<FC>::PX;
     static_assert(PX % 2 == 0, "pipelined forward runs the packed pixel-pair path");
     constexpr int NT = FwdCfg<FC>::NT;
@@ -391,13 +446,27 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
     constexpr int PER = PB / NT;             // entries per thread and batch
     constexpr int ROWSTEP = kTile / PX;
     constexpr int NP = PX / 2;
+    constexpr int WB = WIN ? PB : 1;
     __shared__ float4 s_geo[2][PB];
     __shared__ __align__(16) float s_df[2][PB * S];
     __shared__ unsigned char s_skip[2][PB];
+    __shared__ int4 s_win[2][WB];
+    __shared__ uchar2 s_pat[2][WB];
+    __shared__ __align__(16) float s_lwx[WIN ? 8 * kTile : 1];
+    __shared__ __align__(16) float s_lwy[WIN ? 8 * kTile : 1];
 
     const int G = gridDim.x;
     const int lx = threadIdx.x & (kTile - 1);
     const int ly = threadIdx.x >> 4;
+    if constexpr (WIN) {
+        // window tables: by column, and by this thread layout's rows (pattern, row step, PX rows)
+        for (int i = threadIdx.x; i < 8 * kTile; i += NT) {
+            const int p = i / kTile, c = i % kTile;
+            s_lwx[i] = tab.lw[p][c];
+            const int l = c / PX, k = c % PX;  // s_lwy[(p * ROWSTEP + l) * PX + k] = row l + k * ROWSTEP
+            s_lwy[i] = tab.lw[p][l + k * ROWSTEP];
+        }
+    }
 
     // register pipeline: offsets of the current, next and next-but-one tile, gids of the next
     int t = blockIdx.x;
@@ -418,10 +487,12 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         for (int k = 0; k < PER; ++k) {
             const int j = threadIdx.x + k * NT;
             if (j < cnt) {
-                const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(gid_sorted[oc0 + j]) * RS);
+                const int g = gid_sorted[oc0 + j];
+                const float4* pr = reinterpret_cast<const float4*>(prec + static_cast<int64_t>(g) * RS);
                 cp_async16(&s_geo[0][j], pr);
 #pragma unroll
                 for (int v = 0; v < S / 4; ++v) cp_async16(&s_df[0][j * S + 4 * v], pr + 1 + v);
+                if constexpr (WIN) cp_async16(&s_win[0][j], win + g);
             }
         }
         cp_async_commit();
@@ -440,6 +511,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                     cp_async16(&s_geo[buf ^ 1][j], pr);
 #pragma unroll
                     for (int v = 0; v < S / 4; ++v) cp_async16(&s_df[buf ^ 1][j * S + 4 * v], pr + 1 + v);
+                    if constexpr (WIN) cp_async16(&s_win[buf ^ 1][j], win + gn[k]);
                 }
             }
             cp_async_commit();
@@ -484,6 +556,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         bool regular = true;
         bool skip_any = false;
         const bool try_skip = cur1 - cur0 > kSkipMinList;  // the same for the whole CTA
+        const int tile_x = t % ntx, tile_y = t / ntx;
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
             const int j = threadIdx.x + k * NT;
@@ -492,9 +565,16 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 const float4* d4 = reinterpret_cast<const float4*>(&s_df[buf][j * S]);
                 const bool reg = regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
                 regular = regular && reg;
-                const bool sk = try_skip && reg &&
-                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
-                                                   static_cast<float>(ty0));
+                bool sk = try_skip && reg &&
+                          entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
+                                             static_cast<float>(ty0));
+                if constexpr (WIN) {
+                    const int4 wv = s_win[buf][j];
+                    const int px_ = feather_pattern(wv.x, wv.y, tile_x), py_ = feather_pattern(wv.z, wv.w, tile_y);
+                    s_pat[buf][j] = make_uchar2(static_cast<unsigned char>(px_), static_cast<unsigned char>(py_));
+                    sk = sk || px_ == 0 || py_ == 0;  // the window is zero over the whole tile
+                    if (entry_pat != nullptr) entry_pat[cur0 + j] = static_cast<uint16_t>(px_ | (py_ << 8));
+                }
                 s_skip[buf][j] = sk;
                 skip_any = skip_any || sk;
                 if (records != nullptr) {
@@ -505,9 +585,11 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 }
             }
         }
+        const bool gate = WIN || try_skip;
         bool all_regular = __syncthreads_and(regular ? 1 : 0) != 0;
-        bool any_skip = try_skip && __syncthreads_or(skip_any ? 1 : 0) != 0;
-        fwd_batch_pk_sel<FC>(all_regular, any_skip, n0, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2);
+        bool any_skip = gate && __syncthreads_or(skip_any ? 1 : 0) != 0;
+        const FwdWin fw{s_pat[buf], s_lwx, s_lwy, lx, ly};
+        fwd_batch_pk_sel<FC, WIN>(all_regular, any_skip, n0, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2, fw);
         // 4. later batches of a long list, staged in place
         for (int b = cur0 + PB; b < cur1; b += PB) {
             const int cnt = min(PB, cur1 - b);
@@ -524,9 +606,16 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 for (int v = 0; v < S / 4; ++v) d4[v] = pr[1 + v];
                 const bool rg = regular_scaled(g0.x, g0.y, g0.z, g0.w, d4[0].x);
                 reg = reg && rg;
-                const bool sk = try_skip && rg &&
-                                entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
-                                                   static_cast<float>(ty0));
+                bool sk = try_skip && rg &&
+                          entry_zero_in_tile(g0.x, g0.y, g0.z, g0.w, d4[0].x, static_cast<float>(tx0),
+                                             static_cast<float>(ty0));
+                if constexpr (WIN) {
+                    const int4 wv = win[gid_sorted[e]];
+                    const int px_ = feather_pattern(wv.x, wv.y, tile_x), py_ = feather_pattern(wv.z, wv.w, tile_y);
+                    s_pat[buf][j] = make_uchar2(static_cast<unsigned char>(px_), static_cast<unsigned char>(py_));
+                    sk = sk || px_ == 0 || py_ == 0;
+                    if (entry_pat != nullptr) entry_pat[e] = static_cast<uint16_t>(px_ | (py_ << 8));
+                }
                 s_skip[buf][j] = sk;
                 skp = skp || sk;
                 if (records != nullptr) {
@@ -537,8 +626,9 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                 }
             }
             all_regular = __syncthreads_and(reg ? 1 : 0) != 0;
-            any_skip = try_skip && __syncthreads_or(skp ? 1 : 0) != 0;
-            fwd_batch_pk_sel<FC>(all_regular, any_skip, cnt, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2);
+            any_skip = gate && __syncthreads_or(skp ? 1 : 0) != 0;
+            fwd_batch_pk_sel<FC, WIN>(all_regular, any_skip, cnt, s_geo[buf], s_df[buf], s_skip[buf], fpx, fpy2, acc2,
+                                      fw);
         }
         // 5. image
         const int px = tx0 + lx;
@@ -564,7 +654,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
 }
 
 // CTAs per SM the pipelined forward runs with (queried once per device).
-template <int FC>
+template <int FC, bool WIN = false>
 int pipe_grid(int num_tiles) {
     static int cached[64] = {0};
     int dev = 0;
@@ -572,7 +662,7 @@ int pipe_grid(int num_tiles) {
     if (cached[dev] == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC>, FwdCfg<FC>::NT, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC, WIN>, FwdCfg<FC>::NT, 0);
         cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
     }
     return num_tiles < cached[dev] ? num_tiles : cached[dev];
@@ -585,8 +675,9 @@ cudaError_t launch_fwd_fc(int f, int h, int w, int ntx, int num_tiles, const flo
                           const float* prec, cudaStream_t stream) {
     if constexpr (FwdCfg<FC>::PX % 2 == 0) {
         if (prec != nullptr && slots == nullptr) {
-            k_render_fwd_pipe<FC><<<static_cast<unsigned>(pipe_grid<FC>(num_tiles)), FwdCfg<FC>::NT, 0, stream>>>(
-                f, h, w, ntx, num_tiles, prec, gid_sorted, tile_offsets, image, records);
+            k_render_fwd_pipe<FC, false><<<static_cast<unsigned>(pipe_grid<FC>(num_tiles)), FwdCfg<FC>::NT, 0,
+                                           stream>>>(f, h, w, ntx, num_tiles, prec, gid_sorted, tile_offsets, image,
+                                                     records, nullptr, nullptr, FeatherTable{});
             return cudaGetLastError();
         }
     }
@@ -611,6 +702,28 @@ int entry_record_floats(int f) {
     if (f <= 16) return record_floats_fc<16>();
     if (f <= 32) return record_floats_fc<32>();
     return record_floats_fc<64>();
+}
+
+cudaError_t launch_render_forward_feathered(int f, int h, int w, const FeatherTable& tab, const float* vprec,
+                                           const int32_t* vwin, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                                           float* image, float* records, uint16_t* entry_pat, cudaStream_t stream) {
+    const int ntx = static_cast<int>(div_up(w, kTile));
+    const int nty = static_cast<int>(div_up(h, kTile));
+    const int num_tiles = ntx * nty;
+    if (num_tiles == 0 || f == 0) return cudaSuccess;
+    const int4* win = reinterpret_cast<const int4*>(vwin);
+#define OSS_FWD_WIN(FC)                                                                                            \
+    (k_render_fwd_pipe<FC, true><<<static_cast<unsigned>(pipe_grid<FC, true>(num_tiles)), FwdCfg<FC>::NT, 0,      \
+                                   stream>>>(f, h, w, ntx, num_tiles, vprec, gid_sorted, tile_offsets, image,      \
+                                             records, win, entry_pat, tab),                                        \
+     cudaGetLastError())
+    if (f <= 1) return OSS_FWD_WIN(1);
+    if (f <= 3) return OSS_FWD_WIN(3);
+    if (f <= 4) return OSS_FWD_WIN(4);
+    if (f <= 8) return OSS_FWD_WIN(8);
+    if (f <= 16) return OSS_FWD_WIN(16);
+    return cudaErrorInvalidValue;  // the feathered render takes at most 16 channels per call
+#undef OSS_FWD_WIN
 }
 
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat, const float* opacity,

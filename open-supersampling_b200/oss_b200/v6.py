@@ -4,8 +4,9 @@ Drop-in for oss/sr/v6/rasterizer.py:17-345 (``V6Rasterizer``): the same
 constructor arguments, ``forward(canvas, active_mask, output_hw,
 return_weight_sum)`` contract, sanitisation rules, weight-sum channel, the
 4-phase feathered overlap render and the batch expand.  Every render goes
-through ``oss_cuda.rasterize_gaussians`` (liboss_b200.so); the masking,
-sanitising and feather compositing are elementwise PyTorch glue around it.
+through ``oss_cuda.rasterize_gaussians`` (liboss_b200.so), the feathered
+overlap in one pass; the masking and sanitising are elementwise PyTorch glue
+around it.
 
 ``spawn_offset`` shifts all means by a per-frame integer
 offset before rendering, the effect of the spawner offset of
@@ -33,12 +34,13 @@ def render(xy, scale, rot, feat, h, w, binning=None, opacity=None):
 
 
 def render_overlapped(xy, scale, rot, feat, h, w, overlap, binning=None, opacity=None):
-    """Feathered overlapping-tile render (rasterizer.py:159-210) through `render`:
-    four renders whose 16-px tile grids are shifted by (0|-o, 0|-o), each cropped
-    back to (h, w) and blended by its feather mask, then normalised by the mask
-    sum (oss_cuda.overlap)."""
-    return render_overlapped_with(lambda x, s, r, f, hh, ww: render(x, s, r, f, hh, ww, binning, opacity),
-                                  xy, scale, rot, feat, h, w, overlap)
+    """Feathered overlapping-tile render (rasterizer.py:159-210): the blend of four
+    renders whose 16-px tile grids are shifted by (0|-o, 0|-o), each cropped back
+    to (h, w), weighted by its feather mask and normalised by the mask sum --
+    computed in one pass by rasterize_gaussians(overlap=o) (csrc/feather.cu),
+    with the scale floor of the reference's oss_cuda backend."""
+    return rasterize_gaussians(xy, scale.clamp_min(_MIN_PIXEL_SCALE), rot, feat, h, w, TILE_SIZE, True,
+                               binning=binning, opacity=opacity, overlap=overlap)
 
 
 class V6Rasterizer(nn.Module):

@@ -109,6 +109,17 @@ SIGNATURES = {
     "oss_apply_prune_spawn": (
         ctypes.c_int,
         [_i64, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_feather_supported": (ctypes.c_int, [_i32, _i64, _i64, _i64]),
+    "oss_feather_virtual_count": (_i64, [_i64]),
+    "oss_render_prepare_feathered_scratch_bytes": (_i64, [_i64]),
+    "oss_render_prepare_feathered": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i32, _i32, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_render_forward_feathered": (ctypes.c_int, [_i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_backward_feathered": (
+        ctypes.c_int, [_i64, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_reduce_pair_grads_feathered": (
+        ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_tile_bin_counting_sort_noalloc": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p]),
     "oss_tile_bin_counting_sort_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_tile_bin_counting_sort": (ctypes.c_int, [_i64, _i64, _p, _p, _p, _p, _p, _i64, _p]),

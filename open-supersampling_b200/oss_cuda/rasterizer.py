@@ -34,7 +34,7 @@ from importlib import import_module
 import torch
 from torch.autograd import Function
 
-from . import _raster
+from . import _feather, _raster
 
 try:
     from . import _C
@@ -173,11 +173,26 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
     if overlap > 0:
         if blend != "sum":
             raise ValueError("overlap applies to blend='sum' only")
+        _raster.check_gaussians(xy, scale, rot, feat)
+        _raster.check_hw(h, w, tile_size)
+        if weight == "gaussian" and _feather.supported(overlap, int(feat.size(1)), h, w):
+            # one pass: every Gaussian once, with its separable feather window
+            if opacity is not None:
+                _raster.check_float_cuda(opacity, "opacity")
+                if opacity.dim() != 1 or opacity.size(0) != xy.size(0):
+                    raise RuntimeError("opacity must be (N,)")
+            if pair_capacity is not None:
+                pair_capacity = int(pair_capacity)
+                if pair_capacity < 0 or pair_capacity > _raster.INT32_MAX:
+                    raise ValueError("pair_capacity must be in [0, 2**31 - 1]")
+            return _feather.RasterizeFeathered.apply(xy, scale, rot, feat, opacity, h, w, _raster.binning_mode(binning),
+                                                     overlap, pair_capacity)
+        # wider channel counts or overlaps: the reference's composition of four phase renders
         from .overlap import render_overlapped_with
 
         def one(x, s, r, f, hh, ww):
             return rasterize_gaussians(x, s, r, f, hh, ww, tile_size, topk_norm, binning=binning, opacity=opacity,
-                                       pair_capacity=pair_capacity)
+                                       pair_capacity=pair_capacity, weight=weight)
 
         return render_overlapped_with(one, xy, scale, rot, feat, h, w, overlap)
     _raster.check_gaussians(xy, scale, rot, feat)

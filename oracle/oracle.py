@@ -52,6 +52,9 @@ def lib():
         _lib.orc_full_pairs.argtypes = [i64, i64, p, p]
         _lib.orc_render_forward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_render_backward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
+        _lib.orc_render_backward_f32.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64, i32]
+        _lib.orc_render_backward_exact.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
+        _lib.orc_render_backward_fma.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_conic_to_scale_rot_grad.argtypes = [i64, p, p, p, p, p]
         _lib.orc_render_alpha_forward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
         _lib.orc_render_alpha_backward.argtypes = [i64, i32, i32, i32, p, p, p, p, p, p, p, p, p, p, p, p, i64, i64]
@@ -172,20 +175,35 @@ def render_forward(xy, conic, feat, gid, offs, h, w, opacity=None, tile_range=No
     return out
 
 
-def render_backward(xy, conic, feat, gid, offs, grad, h, w, opacity=None, tile_range=None):
-    """(d_xy, d_conic, d_feat, d_opacity) -- rasterizer_bwd.cu:78-109, double sums."""
+def render_backward(xy, conic, feat, gid, offs, grad, h, w, opacity=None, tile_range=None, sums="f64"):
+    """(d_xy, d_conic, d_feat, d_opacity) -- rasterizer_bwd.cu:78-109, double sums.
+    sums="f32" / "f32r" sum in fp32 one pixel term at a time, as the reference's
+    atomics do, in one order they may run in or in its reverse (the fp32
+    evaluations the parity bar is judged beside); sums="exact" evaluates every
+    per-pixel quantity in double too (the exact value at the fp32 inputs), and
+    sums="f64fma" sums the terms whose q is formed with fused multiply-adds (as
+    the reference's CUDA build contracts it)."""
     xy, conic, feat, grad = _f32(xy), _f32(conic), _f32(feat), _f32(grad)
     gid, offs = _i32(gid), _i32(offs)
     op = None if opacity is None else _f32(opacity)
     n, f = feat.shape
     _, _, t = tiles(h, w)
     lo, hi = (0, t) if tile_range is None else tile_range
-    d_xy = np.empty((n, 2), np.float32)
-    d_conic = np.empty((n, 3), np.float32)
-    d_feat = np.empty((n, f), np.float32)
-    d_op = np.empty((n,), np.float32) if op is not None else None
-    lib().orc_render_backward(n, f, h, w, _p(xy), _p(conic), _p(feat), _p(op), _p(gid), _p(offs), _p(grad),
-                              _p(d_xy), _p(d_conic), _p(d_feat), _p(d_op), lo, hi)
+    dt = np.float64 if sums == "exact" else np.float32  # the exact value is returned unrounded
+    d_xy = np.empty((n, 2), dt)
+    d_conic = np.empty((n, 3), dt)
+    d_feat = np.empty((n, f), dt)
+    d_op = np.empty((n,), dt) if op is not None else None
+    args = (n, f, h, w, _p(xy), _p(conic), _p(feat), _p(op), _p(gid), _p(offs), _p(grad), _p(d_xy), _p(d_conic),
+            _p(d_feat), _p(d_op), lo, hi)
+    if sums == "f64":
+        lib().orc_render_backward(*args)
+    elif sums == "exact":
+        lib().orc_render_backward_exact(*args)
+    elif sums == "f64fma":
+        lib().orc_render_backward_fma(*args)
+    else:
+        lib().orc_render_backward_f32(*args, 1 if sums == "f32r" else 0)
     return d_xy, d_conic, d_feat, d_op
 
 
@@ -196,6 +214,53 @@ def conic_to_scale_rot_grad(scale, rot, d_conic):
     d_rot = np.empty((n,), np.float32)
     lib().orc_conic_to_scale_rot_grad(n, _p(scale), _p(rot), _p(d_conic), _p(d_scale), _p(d_rot))
     return d_scale, d_rot
+
+
+def conic_to_scale_rot_grad_f64(scale, rot, d_conic):
+    """The chain rule of rasterizer_bwd.cu:128-153 evaluated in float64 (the
+    truth the fp32 d_scale / d_rot are judged against)."""
+    raw = np.asarray(scale, np.float64)
+    th = np.asarray(rot, np.float32).astype(np.float64)
+    dc = np.asarray(d_conic, np.float64)
+    s = np.maximum(raw, 1e-6)
+    inv2 = 1.0 / (s * s)
+    diff = inv2[:, 0] - inv2[:, 1]
+    c, sn = np.cos(th), np.sin(th)
+    cc, ss, cs = c * c, sn * sn, c * sn
+    dca, dcb, dcd = dc[:, 0], dc[:, 1], dc[:, 2]
+    d_isx = cc * dca + cs * dcb + ss * dcd
+    d_isy = ss * dca - cs * dcb + cc * dcd
+    with np.errstate(divide="ignore", invalid="ignore"):
+        d_sx = np.where(raw[:, 0] > 1e-6, d_isx * (-2.0 / raw[:, 0] ** 3), 0.0)
+        d_sy = np.where(raw[:, 1] > 1e-6, d_isy * (-2.0 / raw[:, 1] ** 3), 0.0)
+    d_rot = dca * (-2.0 * cs * diff) + dcb * diff * (cc - ss) + dcd * (2.0 * cs * diff)
+    return np.stack([d_sx, d_sy], 1), d_rot
+
+
+# the reference's fp32 evaluations the gradient bar is judged beside (render_backward sums=)
+FP32_EVALUATIONS = ("f32", "f32r", "f64", "f64fma")
+
+
+def grads_with_fp32_evaluation(xy, scale, rot, conic, feat, gid, offs, grad, h, w, opacity=None, tile_range=None):
+    """{name: (truth, [fp32, ...])} for d_xy, d_scale, d_rot, d_feat, d_opacity
+    and d_conic on the given lists: `truth` is the exact value at the fp32
+    inputs (render_backward sums="exact", float64 chain rule), the parity
+    target.  The list holds the reference's own fp32 arithmetic: its fp32
+    per-pixel terms summed one at a time in two orders its atomics may take
+    ("f32", "f32r"), summed exactly ("f64"), and with q contracted into fused
+    multiply-adds as its CUDA build forms it ("f64fma"), each through the fp32
+    chain rule -- the yardstick for elements whose terms cancel."""
+    t = render_backward(xy, conic, feat, gid, offs, grad, h, w, opacity, tile_range, sums="exact")
+    rs = [render_backward(xy, conic, feat, gid, offs, grad, h, w, opacity, tile_range, sums=k)
+          for k in FP32_EVALUATIONS]
+    t_scale, t_rot = conic_to_scale_rot_grad_f64(scale, rot, t[1])
+    r_sr = [conic_to_scale_rot_grad(scale, rot, r[1]) for r in rs]
+    out = {"d_xy": (t[0], [r[0] for r in rs]), "d_conic": (t[1], [r[1] for r in rs]),
+           "d_feat": (t[2], [r[2] for r in rs]), "d_scale": (t_scale, [a for a, _ in r_sr]),
+           "d_rot": (t_rot, [b for _, b in r_sr])}
+    if opacity is not None:
+        out["d_opacity"] = (t[3], [r[3] for r in rs])
+    return out
 
 
 def tile_bin_counting_sort(tile_id, gid, num_tiles):
@@ -292,3 +357,100 @@ def render_alpha_grads(xy, scale, rot, feat, opacity, grad, h, w, depth=None, ba
 if __name__ == "__main__":
     if "--build" in sys.argv:
         print(build(force=True))
+
+
+# ----------------------------------------------------------------------------- feathered overlap
+
+OVERLAP_TILE = 16
+
+
+def phase_origins(overlap: int):
+    """(origin_y, origin_x) of the four phase renders, oss/sr/v6/rasterizer.py:181."""
+    o = int(overlap)
+    return ((0, 0), (-o, 0), (0, -o), (-o, -o))
+
+
+def phase_mask(h: int, w: int, origin, overlap: int) -> np.ndarray:
+    """(h, w) fp32 feather weight of one phase, rasterizer.py:212-242: a cosine
+    ramp over the distance of each pixel centre to the nearest tile edge of
+    that phase's grid, per axis, multiplied."""
+    tile = np.float32(OVERLAP_TILE)
+    o = np.float32(overlap)
+
+    def axis(n, org):
+        p = np.remainder(np.arange(n, dtype=np.float32) + np.float32(0.5) - np.float32(org), tile)
+        d = np.minimum(p, tile - p)
+        t = np.clip(d / o, np.float32(0.0), np.float32(1.0))
+        return (np.float32(0.5) - np.float32(0.5) * np.cos(t * np.float32(np.pi))).astype(np.float32)
+
+    return (axis(h, origin[0])[:, None] * axis(w, origin[1])[None, :]).astype(np.float32)
+
+
+def render_overlapped_band(xy, scale, rot, feat, opacity, h, w, overlap, rows, grad=None, mode=TIGHT):
+    """The feathered 4-phase render of oss/sr/v6/rasterizer.py:159-210 over the
+    output rows [rows[0], rows[1]) only: every phase renders the means
+    xy - origin (fp32) on its crop rounded up to 16 with the oracle's own lists,
+    the tiles covering the band are evaluated, and the crops are weighted by
+    phase_mask and normalised by the weight sum (clamped at 1e-6).
+
+    Returns {"image": (F, r1-r0, w)} and, with `grad` (F, r1-r0, w) = dL/d(band
+    rows of the output, zero elsewhere), the gradients of xy, scale, rot, feat
+    and opacity as {name: (truth, [fp32, ...])} pairs, as in
+    grads_with_fp32_evaluation (the exact value with float64 weights, and the
+    reference's fp32 arithmetic beside it)."""
+    xy = _f32(xy)
+    r0, r1 = int(rows[0]), int(rows[1])
+    f = np.asarray(feat).shape[1]
+    accum = np.zeros((f, r1 - r0, w), np.float32)
+    wsum = np.zeros((r1 - r0, w), np.float32)
+    phases = []
+    for oy, ox in phase_origins(overlap):
+        crop_h = -(-(h - min(oy, 0)) // OVERLAP_TILE) * OVERLAP_TILE
+        crop_w = -(-(w - min(ox, 0)) // OVERLAP_TILE) * OVERLAP_TILE
+        local = xy.copy()
+        local[:, 0] = local[:, 0] - np.float32(ox)
+        local[:, 1] = local[:, 1] - np.float32(oy)
+        conic, _, _, gid, offs = lists(local, scale, rot, crop_h, crop_w, mode)
+        ys, xs = -min(oy, 0), -min(ox, 0)
+        ntx = crop_w // OVERLAP_TILE
+        tr = ((r0 + ys) // OVERLAP_TILE * ntx, -(-(r1 + ys) // OVERLAP_TILE) * ntx)
+        img = render_forward(local, conic, feat, gid, offs, crop_h, crop_w, opacity, tr)
+        band = img[:, r0 + ys:r1 + ys, xs:xs + w]
+        mask = phase_mask(h, w, (oy, ox), overlap)[r0:r1]
+        accum += band * mask
+        wsum += mask
+        phases.append((local, conic, gid, offs, crop_h, crop_w, ys, xs, tr, mask))
+    out = {"image": accum / np.maximum(wsum, np.float32(1e-6))}
+    if grad is None:
+        return out
+    grad = np.asarray(grad, np.float32)
+    wsum64 = np.zeros((r1 - r0, w), np.float64)
+    for p in phases:
+        wsum64 += p[-1].astype(np.float64)
+    tot = {}
+    for local, conic, gid, offs, crop_h, crop_w, ys, xs, tr, mask in phases:
+        for kind in ("exact",) + FP32_EVALUATIONS:
+            if kind in ("exact", "f64", "f64fma"):
+                g_band = grad.astype(np.float64) * mask / np.maximum(wsum64, 1e-6)
+            else:
+                g_band = grad * (mask / np.maximum(wsum, np.float32(1e-6)))
+            g_full = np.zeros((f, crop_h, crop_w), np.float32)
+            g_full[:, r0 + ys:r1 + ys, xs:xs + w] = g_band.astype(np.float32)
+            d = render_backward(local, conic, feat, gid, offs, g_full, crop_h, crop_w, opacity, tr, sums=kind)
+            acc = tot.setdefault(kind, [np.zeros(a.shape, np.float64) if a is not None else None for a in d])
+            for i, a in enumerate(d):
+                if a is not None:
+                    acc[i] += a
+    t_xy, t_conic, t_feat, t_op = tot["exact"]
+    t_scale, t_rot = conic_to_scale_rot_grad_f64(scale, rot, t_conic)
+    fp32 = {"d_xy": [], "d_scale": [], "d_rot": [], "d_feat": [], "d_opacity": []}
+    for kind in FP32_EVALUATIONS:
+        r_xy, r_conic, r_feat, r_op = (None if a is None else a.astype(np.float32) for a in tot[kind])
+        r_scale, r_rot = conic_to_scale_rot_grad(scale, rot, r_conic)
+        for k, v in (("d_xy", r_xy), ("d_scale", r_scale), ("d_rot", r_rot), ("d_feat", r_feat), ("d_opacity", r_op)):
+            fp32[k].append(v)
+    out.update({"d_xy": (t_xy, fp32["d_xy"]), "d_scale": (t_scale, fp32["d_scale"]), "d_rot": (t_rot, fp32["d_rot"]),
+                "d_feat": (t_feat, fp32["d_feat"])})
+    if opacity is not None:
+        out["d_opacity"] = (t_op, fp32["d_opacity"])
+    return out

@@ -169,6 +169,12 @@ static float quad_of(const float* k, float dx, float dy) {
     return k[0] * dx * dx + 2.0f * k[1] * dx * dy + k[2] * dy * dy;
 }
 
+/* The same expression with its products folded into fused multiply-adds, as a
+ * CUDA build contracts it by default (the reference's op is compiled that way). */
+static float quad_of_fma(const float* k, float dx, float dy) {
+    return fmaf(k[2] * dy, dy, fmaf(2.0f * k[1] * dx, dy, (k[0] * dx) * dx));
+}
+
 /*
  * Additive forward over per-tile lists: out[c][p] = sum over the tile's list,
  * in list order, of feat'[g][c] * exp(-q/2) with q < 0 or non-finite giving 0
@@ -220,10 +226,60 @@ void orc_render_forward(int64_t n, int f, int h, int w, const float* xy, const f
  * Gaussian over list entries in list order.  d_feat = opacity * d_feat',
  * d_opacity = sum_c d_feat'_c feat_c.  Gradient outputs are overwritten.
  */
+/* Gradients summed in double; written in double (d_*64, any may be null) and/or
+ * rounded to fp32 (d_*32, any may be null).  exact_math: 0 = the reference's fp32
+ * per-pixel terms, 1 = every per-pixel quantity in double, 2 = fp32 terms with q
+ * formed by fused multiply-adds. */
+static void render_backward_double(int64_t n, int f, int h, int w, const float* xy, const float* conic,
+                                   const float* feat, const float* opacity, const int32_t* gid_sorted,
+                                   const int32_t* tile_offsets, const float* grad, float* d_xy, float* d_conic,
+                                   float* d_feat, float* d_opacity, double* d_xy64, double* d_conic64,
+                                   double* d_feat64, double* d_opacity64, int64_t tile_lo, int64_t tile_hi,
+                                   int exact_math);
+
 void orc_render_backward(int64_t n, int f, int h, int w, const float* xy, const float* conic, const float* feat,
                          const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
                          const float* grad, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
                          int64_t tile_lo, int64_t tile_hi) {
+    render_backward_double(n, f, h, w, xy, conic, feat, opacity, gid_sorted, tile_offsets, grad, d_xy, d_conic,
+                           d_feat, d_opacity, NULL, NULL, NULL, NULL, tile_lo, tile_hi, 0);
+}
+
+/*
+ * The same gradients with every per-pixel quantity in double as well: offsets,
+ * q, the weight exp(-q/2) and the terms, from the fp32 inputs (means, conic,
+ * features, dL/dimage).  This is the exact value of the reference's formula at
+ * its fp32 inputs; orc_render_backward instead sums the terms the reference's
+ * fp32 arithmetic forms (its q keeps fp32 rounding, which for a thin Gaussian
+ * cancels terms of both signs).  The parity bar is judged against this value,
+ * with the reference's fp32 evaluations beside it.
+ */
+void orc_render_backward_exact(int64_t n, int f, int h, int w, const float* xy, const float* conic, const float* feat,
+                               const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                               const float* grad, double* d_xy, double* d_conic, double* d_feat, double* d_opacity,
+                               int64_t tile_lo, int64_t tile_hi) {
+    /* outputs stay in double: a thin Gaussian's d_scale / d_rot cancel d_conic terms */
+    render_backward_double(n, f, h, w, xy, conic, feat, opacity, gid_sorted, tile_offsets, grad, NULL, NULL, NULL,
+                           NULL, d_xy, d_conic, d_feat, d_opacity, tile_lo, tile_hi, 1);
+}
+
+/* Double sums of the per-pixel terms with q formed by fused multiply-adds
+ * (quad_of_fma): the terms of the reference's CUDA build, another fp32
+ * evaluation of its formula. */
+void orc_render_backward_fma(int64_t n, int f, int h, int w, const float* xy, const float* conic, const float* feat,
+                             const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                             const float* grad, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                             int64_t tile_lo, int64_t tile_hi) {
+    render_backward_double(n, f, h, w, xy, conic, feat, opacity, gid_sorted, tile_offsets, grad, d_xy, d_conic,
+                           d_feat, d_opacity, NULL, NULL, NULL, NULL, tile_lo, tile_hi, 2);
+}
+
+static void render_backward_double(int64_t n, int f, int h, int w, const float* xy, const float* conic,
+                                   const float* feat, const float* opacity, const int32_t* gid_sorted,
+                                   const int32_t* tile_offsets, const float* grad, float* d_xy, float* d_conic,
+                                   float* d_feat, float* d_opacity, double* d_xy64, double* d_conic64,
+                                   double* d_feat64, double* d_opacity64, int64_t tile_lo, int64_t tile_hi,
+                                   int exact_math) {
     const int ntx = num_tiles_1d(w);
     const int64_t plane = (int64_t)h * w;
     const int stride = 5 + f;
@@ -244,11 +300,22 @@ void orc_render_backward(int64_t n, int f, int h, int w, const float* xy, const 
                 for (int lx = 0; lx < ORC_TILE; ++lx) {
                     const int px = tx0 + lx;
                     if (px >= w) break;
-                    const float dx = (float)px - xy[2 * g];
-                    const float dy = (float)py - xy[2 * g + 1];
-                    const float q = quad_of(k, dx, dy);
-                    if (!isfinite(q) || q < 0.0f) continue;
-                    const double wgt = (double)expf(-0.5f * q);
+                    double dx, dy, wgt;
+                    if (exact_math == 1) {
+                        dx = (double)px - (double)xy[2 * g];
+                        dy = (double)py - (double)xy[2 * g + 1];
+                        const double q = (double)k[0] * dx * dx + 2.0 * (double)k[1] * dx * dy + (double)k[2] * dy * dy;
+                        if (!isfinite(q) || q < 0.0) continue;
+                        wgt = exp(-0.5 * q);
+                    } else {
+                        const float fdx = (float)px - xy[2 * g];
+                        const float fdy = (float)py - xy[2 * g + 1];
+                        const float q = exact_math == 2 ? quad_of_fma(k, fdx, fdy) : quad_of(k, fdx, fdy);
+                        if (!isfinite(q) || q < 0.0f) continue;
+                        dx = fdx;
+                        dy = fdy;
+                        wgt = (double)expf(-0.5f * q);
+                    }
                     double dldw = 0.0;
                     const int64_t pix = (int64_t)py * w + px;
                     for (int c = 0; c < f; ++c) {
@@ -273,21 +340,121 @@ void orc_render_backward(int64_t n, int f, int h, int w, const float* xy, const 
     }
     for (int64_t g = 0; g < n; ++g) {
         const double* a = gacc + g * stride;
-        d_xy[2 * g] = (float)a[0];
-        d_xy[2 * g + 1] = (float)a[1];
-        d_conic[3 * g] = (float)a[2];
-        d_conic[3 * g + 1] = (float)a[3];
-        d_conic[3 * g + 2] = (float)a[4];
         const double op = opacity ? (double)opacity[g] : 1.0;
         double dop = 0.0;
         for (int c = 0; c < f; ++c) {
-            d_feat[g * f + c] = (float)(a[5 + c] * op);
+            const double v = a[5 + c] * op;
+            if (d_feat) d_feat[g * f + c] = (float)v;
+            if (d_feat64) d_feat64[g * f + c] = v;
             dop += a[5 + c] * (double)feat[g * f + c];
         }
+        for (int i = 0; i < 2; ++i) {
+            if (d_xy) d_xy[2 * g + i] = (float)a[i];
+            if (d_xy64) d_xy64[2 * g + i] = a[i];
+        }
+        for (int i = 0; i < 3; ++i) {
+            if (d_conic) d_conic[3 * g + i] = (float)a[2 + i];
+            if (d_conic64) d_conic64[3 * g + i] = a[2 + i];
+        }
         if (d_opacity) d_opacity[g] = (float)dop;
+        if (d_opacity64) d_opacity64[g] = dop;
     }
     free(gacc);
     free(pacc);
+}
+
+/*
+ * The same backward summed the way the reference's kernel sums it: in fp32,
+ * one term per pixel and list entry added straight into the Gaussian's
+ * accumulator (rasterizer_bwd.cu:95-108 adds them with float atomics; this is
+ * one order those atomics may run in: tiles ascending, pixels row-major, list
+ * entries in list order; with `reverse` every one of those orders reversed).  The opacity unfold is the fp32 product and dot
+ * product the reference's callers get from autograd.  This is not the parity
+ * target (orc_render_backward's double sums are): it measures how far the
+ * reference's own fp32 evaluation lies from those sums, element by element.
+ * Threads own the Gaussians g = tid (mod threads), so every accumulator is
+ * added to in the order above.
+ */
+void orc_render_backward_f32(int64_t n, int f, int h, int w, const float* xy, const float* conic, const float* feat,
+                             const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets,
+                             const float* grad, float* d_xy, float* d_conic, float* d_feat, float* d_opacity,
+                             int64_t tile_lo, int64_t tile_hi, int reverse) {
+    const int ntx = num_tiles_1d(w);
+    const int64_t plane = (int64_t)h * w;
+    const int stride = 5 + f;
+    float* acc = (float*)calloc((size_t)(n * stride + 1), sizeof(float));
+#pragma omp parallel
+    {
+        int nt = 1, tid = 0;
+#ifdef _OPENMP
+        nt = omp_get_num_threads();
+        tid = omp_get_thread_num();
+#endif
+        int cap = 0;
+        int32_t* mine = NULL;  /* this thread's Gaussians of the tile's list, in list order */
+        for (int64_t tt = tile_lo; tt < tile_hi; ++tt) {
+            const int64_t t = reverse ? tile_hi - 1 - (tt - tile_lo) : tt;
+            const int tx0 = (int)(t % ntx) * ORC_TILE, ty0 = (int)(t / ntx) * ORC_TILE;
+            const int beg = tile_offsets[t], end = tile_offsets[t + 1];
+            if (end - beg > cap) {
+                cap = end - beg;
+                mine = (int32_t*)realloc(mine, sizeof(int32_t) * (size_t)cap);
+            }
+            int m = 0;
+            for (int j = beg; j < end; ++j) {
+                if (gid_sorted[j] % nt == tid) mine[m++] = gid_sorted[j];
+            }
+            if (m == 0) continue;
+            for (int p = 0; p < ORC_TILE * ORC_TILE; ++p) {
+                const int pp = reverse ? ORC_TILE * ORC_TILE - 1 - p : p;
+                const int py = ty0 + pp / ORC_TILE, px = tx0 + pp % ORC_TILE;
+                if (py >= h || px >= w) continue;
+                {
+                    const int64_t pix = (int64_t)py * w + px;
+                    for (int ii = 0; ii < m; ++ii) {
+                        const int g = mine[reverse ? m - 1 - ii : ii];
+                        const float* k = conic + 3 * g;
+                        const float op = opacity ? opacity[g] : 1.0f;
+                        const float dx = (float)px - xy[2 * g];
+                        const float dy = (float)py - xy[2 * g + 1];
+                        const float q = quad_of(k, dx, dy);
+                        if (!isfinite(q) || q < 0.0f) continue;
+                        const float wgt = expf(-0.5f * q);
+                        float* a = acc + (int64_t)g * stride;
+                        float dldw = 0.0f;
+                        for (int c = 0; c < f; ++c) {
+                            const float go = grad[c * plane + pix];
+                            dldw += go * (feat[(int64_t)g * f + c] * op);
+                            a[5 + c] += wgt * go;
+                        }
+                        const float dldq = -0.5f * wgt * dldw;
+                        a[0] -= dldq * (2.0f * k[0] * dx + 2.0f * k[1] * dy);
+                        a[1] -= dldq * (2.0f * k[1] * dx + 2.0f * k[2] * dy);
+                        a[2] += dldq * dx * dx;
+                        a[3] += dldq * 2.0f * dx * dy;
+                        a[4] += dldq * dy * dy;
+                    }
+                }
+            }
+        }
+        free(mine);
+    }
+    for (int64_t g = 0; g < n; ++g) {
+        const float* a = acc + g * stride;
+        d_xy[2 * g] = a[0];
+        d_xy[2 * g + 1] = a[1];
+        d_conic[3 * g] = a[2];
+        d_conic[3 * g + 1] = a[3];
+        d_conic[3 * g + 2] = a[4];
+        const float op = opacity ? opacity[g] : 1.0f;
+        float dop = 0.0f;
+        for (int c = 0; c < f; ++c) {
+            d_feat[g * f + c] = a[5 + c] * op;
+            dop += a[5 + c] * feat[g * f + c];
+        }
+        if (d_opacity) d_opacity[g] = dop;
+    }
+    free(acc);
 }
 
 /*

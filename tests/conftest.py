@@ -48,14 +48,46 @@ def golden_case(data: dict, name: str) -> dict:
     return {k[len(pre):]: v for k, v in data.items() if k.startswith(pre)}
 
 
-def assert_close_grad(actual, expected, what=""):
-    """Gradient parity: the image bar plus an absolute slack of 1e-6 of the
-    tensor's largest magnitude.  Gradients are fp32 sums of up to 256 x (list
-    length) terms; elements that cancel to a small value (d_rot is a difference
-    of d_conic terms) keep the summation noise of their large terms."""
+# An element outside the bar passes only where the reference's own fp32
+# arithmetic is outside it too, and then at most this many times as far from
+# the exact value as the reference's farthest evaluation (two valid fp32
+# evaluations of an ill-conditioned element routinely differ by that factor).
+FP32_NOISE_FACTOR = 2.0
+
+
+def assert_close_grad(actual, expected, what="", ref32=None):
+    """Gradient parity against `expected`, the oracle's exact value (float64
+    throughout, at the fp32 inputs): |a - e| <= ATOL + RTOL |e| at every
+    element.  An element outside that bar passes only with float64 evidence
+    that the reference's own fp32 arithmetic is outside the bar at that element
+    too, and `actual` is at most FP32_NOISE_FACTOR times as far from the exact
+    value as the farthest of those evaluations.  `ref32` holds fp32 evaluations
+    of the reference (an array or a list: the oracle's one-term-at-a-time sums
+    in orders the reference's float atomics may take, its terms summed exactly
+    or with q contracted as its CUDA build forms it, its golden autograd
+    output).  Elements of thin Gaussians (q cancels) and elements whose terms
+    cancel (d_rot is a difference of d_conic terms) carry that much fp32 noise
+    in any evaluation; no blanket slack is given."""
+    a = np.asarray(actual, dtype=np.float64)
     e = np.asarray(expected, dtype=np.float64)
-    scale = float(np.abs(e).max()) if e.size else 0.0
-    assert_close(actual, expected, atol=ATOL + 1e-6 * scale, rtol=RTOL, what=what)
+    assert a.shape == e.shape, f"{what}: shape {a.shape} vs {e.shape}"
+    if a.size == 0:
+        return
+    err = np.abs(a - e)
+    bar = ATOL + RTOL * np.abs(e)
+    bad = err > bar
+    refs = [] if ref32 is None else ([ref32] if isinstance(ref32, np.ndarray) else list(ref32))
+    err32 = None
+    if refs and bad.any():
+        err32 = np.max([np.abs(np.asarray(r, dtype=np.float64) - e) for r in refs], axis=0)
+        bad = bad & ~((err32 > bar) & (err <= FP32_NOISE_FACTOR * err32))
+    if bad.any():
+        i = np.unravel_index(np.argmax(np.where(bad, err - bar, -np.inf)), a.shape)
+        extra = "" if err32 is None else f", fp32 reference error {err32[i]!r}"
+        raise AssertionError(
+            f"{what}: {int(bad.sum())}/{a.size} outside atol={ATOL} rtol={RTOL} without fp32 evidence; "
+            f"worst at {i}: got {a[i]!r} expected {e[i]!r}{extra} (max abs err {err.max():.3e})"
+        )
 
 
 def assert_close(actual, expected, atol=ATOL, rtol=RTOL, what=""):

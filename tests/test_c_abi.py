@@ -44,7 +44,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_clean_error_state():
     lib = _lib.lib()
-    assert lib.oss_abi_version() == 7
+    assert lib.oss_abi_version() == 8
 
 
 def test_rejects_tile_size_other_than_16():

@@ -202,11 +202,17 @@ def test_backward_matches_oracle(cuda_device, mode, n, h, w, f):
     xy, scale, rot, feat = random_gaussians(n, h, w, f, seed=n + 11 * f)
     grad = np.random.default_rng(n).standard_normal((f, h, w)).astype(np.float32)
     _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(xy, scale, rot, feat, grad, h, w, mode)
-    r_xy, r_scale, r_rot, r_feat, _, _ = orc.render_grads(xy, scale, rot, feat, grad, h, w, MODES[mode])
-    assert_close_grad(d_xy, r_xy, what="d_xy")
-    assert_close_grad(d_scale, r_scale, what="d_scale")
-    assert_close_grad(d_rot, r_rot, what="d_rot")
-    assert_close_grad(d_feat, r_feat, what="d_feat")
+    conic, _, _, gid, offs = orc.lists(xy, scale, rot, h, w, MODES[mode])
+    ref = orc.grads_with_fp32_evaluation(xy, scale, rot, conic, feat, gid, offs, grad, h, w)
+    check_grads({"d_xy": d_xy, "d_scale": d_scale, "d_rot": d_rot, "d_feat": d_feat}, ref)
+
+
+def check_grads(got: dict, ref: dict, prefix: str = ""):
+    """Each gradient against the oracle's float64 sum, elements outside the bar
+    judged beside the reference's fp32 evaluation (conftest.assert_close_grad)."""
+    for name, value in got.items():
+        truth, fp32 = ref[name]
+        assert_close_grad(value, truth, what=f"{prefix}{name}", ref32=fp32)
 
 
 def test_backward_with_opacity_matches_oracle(cuda_device):
@@ -217,13 +223,8 @@ def test_backward_with_opacity_matches_oracle(cuda_device):
                                                             opacity=opacity)
     conic, _, _, gid, offs = orc.lists(xy, scale, rot, h, w, orc.TIGHT)
     assert_close(img, orc.render_forward(xy, conic, rgb, gid, offs, h, w, opacity), what="image")
-    r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, gid, offs, grad, h, w, opacity)
-    r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
-    assert_close_grad(d_xy, r_xy, what="d_xy")
-    assert_close_grad(d_scale, r_scale, what="d_scale")
-    assert_close_grad(d_rot, r_rot, what="d_rot")
-    assert_close_grad(d_rgb, r_rgb, what="d_rgb")
-    assert_close_grad(d_op, r_op, what="d_opacity")
+    ref = orc.grads_with_fp32_evaluation(xy, scale, rot, conic, rgb, gid, offs, grad, h, w, opacity)
+    check_grads({"d_xy": d_xy, "d_scale": d_scale, "d_rot": d_rot, "d_feat": d_rgb, "d_opacity": d_op}, ref)
 
 
 def test_backward_matches_reference_golden(cuda_device):
@@ -233,10 +234,15 @@ def test_backward_matches_reference_golden(cuda_device):
         h, w = (int(v) for v in c["hw"])
         _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
                                                          "exact")
-        assert_close_grad(d_xy, c["d_xy"], what=f"{name} d_xy")
-        assert_close_grad(d_scale, c["d_scale"], what=f"{name} d_scale")
-        assert_close_grad(d_rot, c["d_rot"], what=f"{name} d_rot")
-        assert_close_grad(d_feat, c["d_feat"], what=f"{name} d_feat")
+        # against the float64 sums; the reference's own fp32 autograd output (the
+        # golden value) joins the fp32 yardstick
+        conic, _, _, gid, offs = orc.lists(c["xy"], c["scale"], c["rot"], h, w, orc.EXACT)
+        ref = orc.grads_with_fp32_evaluation(c["xy"], c["scale"], c["rot"], conic, c["feat"], gid, offs, c["grad"],
+                                             h, w)
+        for k, got in (("d_xy", d_xy), ("d_scale", d_scale), ("d_rot", d_rot), ("d_feat", d_feat)):
+            truth, fp32 = ref[k]
+            assert_close_grad(got, truth, what=f"{name} {k}", ref32=fp32 + [c[k]])
+            assert_close_grad(c[k], truth, what=f"{name} golden {k}", ref32=fp32 + [c[k]])
 
 
 def test_rasterize_backward_lists_dconic(cuda_device):
@@ -252,11 +258,12 @@ def test_rasterize_backward_lists_dconic(cuda_device):
         _, gid, offs, _ = _C.rasterize_forward(xy, scale, rot, feat, h, w, 16, True)
         d_xy, d_conic, d_feat = _C.rasterize_backward(xy, scale, rot, feat, dev(c["conic"]), gid, offs,
                                                       dev(c["grad"]), h, w, 16)
-        assert_close_grad(host(d_conic), c["d_conic"], what=f"{name} d_conic")
+        ref = orc.grads_with_fp32_evaluation(c["xy"], c["scale"], c["rot"], c["conic"], c["feat"], host(gid),
+                                             host(offs), c["grad"], h, w)
         d_scale, d_rot = _C.conic_to_scale_rot_grad(scale, rot, d_conic)
-        assert_close_grad(host(d_scale), c["d_scale"], what=f"{name} d_scale")
-        assert_close_grad(host(d_rot), c["d_rot"], what=f"{name} d_rot")
-        assert_close_grad(host(d_feat), c["d_feat"], what=f"{name} d_feat")
+        for k, got in (("d_conic", d_conic), ("d_scale", d_scale), ("d_rot", d_rot), ("d_feat", d_feat)):
+            truth, fp32 = ref[k]
+            assert_close_grad(host(got), truth, what=f"{name} {k}", ref32=fp32 + [c[k]])
 
 
 def test_conic_to_scale_rot_known_answer(cuda_device):
@@ -322,13 +329,9 @@ def test_config2_full_size_parity(cuda_device):
     img, (d_xy, d_scale, d_rot, d_rgb, d_op) = run_autograd(xy, scale, rot, rgb, grad, h, w, "tight3sigma",
                                                             opacity=opacity)
     assert_close(img, orc.render_forward(xy, conic, rgb, g_ref, o_ref, h, w, opacity), what="config2 image")
-    r_xy, r_conic, r_rgb, r_op = orc.render_backward(xy, conic, rgb, g_ref, o_ref, grad, h, w, opacity)
-    r_scale, r_rot = orc.conic_to_scale_rot_grad(scale, rot, r_conic)
-    assert_close_grad(d_xy, r_xy, what="config2 d_xy")
-    assert_close_grad(d_scale, r_scale, what="config2 d_scale")
-    assert_close_grad(d_rot, r_rot, what="config2 d_rot")
-    assert_close_grad(d_rgb, r_rgb, what="config2 d_rgb")
-    assert_close_grad(d_op, r_op, what="config2 d_opacity")
+    ref = orc.grads_with_fp32_evaluation(xy, scale, rot, conic, rgb, g_ref, o_ref, grad, h, w, opacity)
+    check_grads({"d_xy": d_xy, "d_scale": d_scale, "d_rot": d_rot, "d_feat": d_rgb, "d_opacity": d_op}, ref,
+                "config2 ")
     # size-independent identity: <grad, image> == <d_feat', feat'> (image is linear in feat')
     lhs = float(np.sum(grad.astype(np.float64) * img))
     rhs = float(np.sum(d_op.astype(np.float64) * opacity))

@@ -144,46 +144,6 @@ def test_oracle_tile_bin_counting_sort_semantics():
     np.testing.assert_array_equal(out, gid[order])
 
 
-def overlap_oracle(xy, scale, rot, feat, grad, h, w, overlap, mode=orc.EXACT):
-    """V6Rasterizer._render_overlapped (oss/sr/v6/rasterizer.py:159-234) over oracle renders."""
-    tile = 16.0
-    origins = ((0, 0), (-overlap, 0), (0, -overlap), (-overlap, -overlap))
-    f = feat.shape[1]
-    accum = np.zeros((f, h, w), np.float32)
-    wsum = np.zeros((1, h, w), np.float32)
-    masks, crops = [], []
-    for oy, ox in origins:
-        ch = -(-(h - min(oy, 0)) // 16) * 16
-        cw = -(-(w - min(ox, 0)) // 16) * 16
-        lxy = xy.copy()
-        lxy[:, 0] -= float(ox)
-        lxy[:, 1] -= float(oy)
-        img = orc.render(lxy, scale, rot, feat, ch, cw, mode)
-        ys, xs = -min(oy, 0), -min(ox, 0)
-        img = img[:, ys:ys + h, xs:xs + w]
-        py = np.remainder(np.arange(h, dtype=np.float32) + 0.5 - oy, tile)
-        px = np.remainder(np.arange(w, dtype=np.float32) + 0.5 - ox, tile)
-        dy = np.minimum(py, tile - py)
-        dx = np.minimum(px, tile - px)
-        ramp = lambda t: 0.5 - 0.5 * np.cos(t * math.pi)
-        m = (ramp(np.clip(dy / overlap, 0, 1))[:, None] * ramp(np.clip(dx / overlap, 0, 1))[None, :])[None]
-        accum += img * m
-        wsum += m
-        masks.append(m.astype(np.float32))
-        crops.append((oy, ox, ch, cw, lxy))
-    den = np.maximum(wsum, 1e-6)
-    image = accum / den
-    grads = [np.zeros_like(xy), np.zeros_like(scale), np.zeros_like(rot), np.zeros_like(feat)]
-    for m, (oy, ox, ch, cw, lxy) in zip(masks, crops):
-        g = np.zeros((f, ch, cw), np.float32)
-        ys, xs = -min(oy, 0), -min(ox, 0)
-        g[:, ys:ys + h, xs:xs + w] = grad * m / den
-        d_xy, d_scale, d_rot, d_feat, _, _ = orc.render_grads(lxy, scale, rot, feat, g, ch, cw, mode)
-        for acc, d in zip(grads, (d_xy, d_scale, d_rot, d_feat)):
-            acc += d
-    return image, grads
-
-
 WARP = load_golden("warp_cases.npz")
 
 
@@ -218,10 +178,56 @@ def test_oracle_warp_matches_reference(name):
 def test_oracle_overlap_matches_reference(name):
     c = golden_case(OVERLAP, name)
     h, w = (int(v) for v in c["hw"])
-    image, (d_xy, d_scale, d_rot, d_feat) = overlap_oracle(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
-                                                           int(c["overlap"]))
-    assert_close(image, c["image"], what="overlap image")
-    assert_close(d_xy, c["d_xy"], what="overlap d_xy")
-    assert_close(d_scale, c["d_scale"], what="overlap d_scale")
-    assert_close(d_rot, c["d_rot"], what="overlap d_rot")
-    assert_close(d_feat, c["d_feat"], what="overlap d_feat")
+    out = orc.render_overlapped_band(c["xy"], c["scale"], c["rot"], c["feat"], None, h, w, int(c["overlap"]), (0, h),
+                                     grad=c["grad"], mode=orc.EXACT)
+    assert_close(out["image"], c["image"], what="overlap image")
+    for k in ("xy", "scale", "rot", "feat"):
+        assert_close(out[f"d_{k}"][0], c[f"d_{k}"], what=f"overlap d_{k}")
+        for r in out[f"d_{k}"][1]:
+            assert_close(r, c[f"d_{k}"], what=f"overlap d_{k} (fp32 evaluation)")
+
+
+def test_oracle_overlap_band_is_a_slice_of_the_frame():
+    """A band of rows renders those rows of the whole frame, and its gradients
+    are the frame's gradients under a dL/dimage that is zero off the band."""
+    rng = np.random.default_rng(21)
+    h, w, n, o = 70, 90, 400, 4
+    xy = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    scale = np.exp(rng.standard_normal((n, 2)) * 0.5 + np.log(2.5)).astype(np.float32)
+    rot = (rng.random(n) * np.pi).astype(np.float32)
+    rgb = rng.random((n, 3)).astype(np.float32)
+    op = rng.random(n).astype(np.float32)
+    grad = rng.standard_normal((3, h, w)).astype(np.float32)
+    rows = (21, 45)
+    g_band = grad[:, rows[0]:rows[1]]
+    full_grad = np.zeros_like(grad)
+    full_grad[:, rows[0]:rows[1]] = g_band
+    full = orc.render_overlapped_band(xy, scale, rot, rgb, op, h, w, o, (0, h), grad=full_grad)
+    band = orc.render_overlapped_band(xy, scale, rot, rgb, op, h, w, o, rows, grad=g_band)
+    np.testing.assert_array_equal(band["image"], full["image"][:, rows[0]:rows[1]])
+    for k in ("d_xy", "d_scale", "d_rot", "d_feat", "d_opacity"):
+        assert_close(band[k][0], full[k][0], what=k)
+        assert np.abs(band[k][0]).max() > 0
+
+
+@pytest.mark.parametrize("name", [str(n) for n in RENDER["names"]])
+def test_oracle_fp32_evaluation_matches_reference(name):
+    """The fp32 one-term-at-a-time backward (the yardstick of the gradient bar)
+    against the reference's own fp32 autograd gradients, and the float64 chain
+    rule against the fp32 one."""
+    c = golden_case(RENDER, name)
+    h, w = (int(v) for v in c["hw"])
+    conic, _, _, gid, offs = orc.lists(c["xy"], c["scale"], c["rot"], h, w, orc.EXACT)
+    ref = orc.grads_with_fp32_evaluation(c["xy"], c["scale"], c["rot"], conic, c["feat"], gid, offs, c["grad"], h, w)
+    for k in ("xy", "scale", "rot", "feat"):
+        assert_close(ref[f"d_{k}"][0], c[f"d_{k}"], what=f"double sums d_{k}")
+        # the same fp32 computation as the reference's autograd in other summation
+        # orders: equal up to fp32 noise, which d_scale (x 2/s^3) and d_rot amplify
+        for r in ref[f"d_{k}"][1]:
+            assert_close(r, c[f"d_{k}"], atol=1e-5, rtol=1e-3, what=f"fp32 evaluation d_{k}")
+    for r in ref["d_xy"][1] + ref["d_feat"][1]:
+        assert r.shape in (c["d_xy"].shape, c["d_feat"].shape)
+    for r in ref["d_xy"][1]:
+        assert_close(r, c["d_xy"], what="fp32 evaluation d_xy")
+    for r in ref["d_feat"][1]:
+        assert_close(r, c["d_feat"], what="fp32 evaluation d_feat")
