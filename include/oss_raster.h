@@ -408,6 +408,25 @@ OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, in
                             float* out_opacities, float* out_colors, int32_t* out_count,
                             void* scratch, int64_t scratch_bytes, void* stream);
 
+/* Backward of oss_warp_canvas: the gradients autograd takes through
+ * canvas_warp.py:177-254 and covariance_resampling.py:76-116.  g_* are the
+ * gradients of the compacted outputs (out_count rows; any may be null for zero);
+ * d_* receive the gradients of the n inputs (dropped Gaussians get zero) and
+ * d_motion_lr[2][h_lr][w_lr] that of the motion (null: not wanted; sums of
+ * fp64 atomics, so its last bits may vary from run to run).  forward_scratch is the scratch
+ * of the forward call, unchanged since.  The reconstruction covariance is a
+ * constant here.  Where the resampled covariance is exactly isotropic the
+ * rotation's gradient is 0 (atan2 has none there). */
+OSS_API int64_t oss_warp_canvas_backward_scratch_bytes(int64_t h, int64_t w);
+OSS_API int oss_warp_canvas_backward(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h, int64_t w,
+                                     const float* motion_lr, float alpha, const float* recon,
+                                     const float* positions, const float* scales, const float* rotations,
+                                     const void* forward_scratch, const float* g_positions, const float* g_scales,
+                                     const float* g_rotations, const float* g_opacities, const float* g_colors,
+                                     float* d_positions, float* d_scales, float* d_rotations, float* d_opacities,
+                                     float* d_colors, float* d_motion_lr, void* scratch, int64_t scratch_bytes,
+                                     void* stream);
+
 /* ---------------------------------------------------------------------------
  * Position-only warp: replaces oss/gaussian/canvas/warp.py:28-91
  * (warp_positions); motion[2][h][w] at the output resolution, times alpha

@@ -696,6 +696,47 @@ int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h,
     return OSS_OK;
 }
 
+int64_t oss_warp_canvas_backward_scratch_bytes(int64_t h, int64_t w) {
+    return oss::warp_backward_scratch_bytes(h < 0 ? 0 : h, w < 0 ? 0 : w);
+}
+
+int oss_warp_canvas_backward(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h, int64_t w,
+                             const float* motion_lr, float alpha, const float* recon, const float* positions,
+                             const float* scales, const float* rotations, const void* forward_scratch,
+                             const float* g_positions, const float* g_scales, const float* g_rotations,
+                             const float* g_opacities, const float* g_colors, float* d_positions, float* d_scales,
+                             float* d_rotations, float* d_opacities, float* d_colors, float* d_motion_lr,
+                             void* scratch, int64_t scratch_bytes, void* stream) {
+    OSS_CHECK(n >= 0 && f >= 0, OSS_ERR_INVALID, "canvas.count must be non-negative");
+    OSS_CHECK(n <= INT_MAX && f <= INT_MAX / (n > 0 ? n : 1), OSS_ERR_RANGE, "canvas size exceeds int32 range");
+    OSS_CHECK(h > 0 && w > 0, OSS_ERR_INVALID, "output_hw must be positive");
+    OSS_CHECK(h_lr > 0 && w_lr > 0, OSS_ERR_INVALID, "motion_lr must be (B, 2, H, W) with H, W > 0");
+    OSS_CHECK(h <= INT_MAX && w <= INT_MAX && h_lr <= INT_MAX && w_lr <= INT_MAX && 6 * h * w <= INT64_MAX / 8,
+              OSS_ERR_RANGE, "motion or output size exceeds int32 range");
+    OSS_CHECK(recon != nullptr, OSS_ERR_INVALID, "recon must point to 4 host floats");
+    OSS_CHECK(scratch_bytes >= oss_warp_canvas_backward_scratch_bytes(h, w), OSS_ERR_SCRATCH,
+              "warp_canvas_backward scratch too small");
+    OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
+    if (n > 0) {
+        OSS_CHECK(motion_lr != nullptr && positions != nullptr && scales != nullptr && rotations != nullptr &&
+                      forward_scratch != nullptr,
+                  OSS_ERR_INVALID, "canvas inputs and the forward's scratch must be non-null");
+        OSS_CHECK(d_positions != nullptr && d_scales != nullptr && d_rotations != nullptr &&
+                      (f == 0 || d_colors != nullptr),
+                  OSS_ERR_INVALID, "gradient outputs must be non-null");
+        OSS_CHECK(aligned(positions, 8) && aligned(scales, 8) && aligned(d_positions, 8) && aligned(d_scales, 8) &&
+                      (g_positions == nullptr || aligned(g_positions, 8)) &&
+                      (g_scales == nullptr || aligned(g_scales, 8)) && aligned(forward_scratch, 16),
+                  OSS_ERR_INVALID, "positions, scales, their gradients and the forward scratch must be aligned");
+    }
+    OSS_CUDA_TRY(oss::launch_warp_canvas_backward(
+        static_cast<int>(n), static_cast<int>(f), static_cast<int>(h_lr), static_cast<int>(w_lr), static_cast<int>(h),
+        static_cast<int>(w), motion_lr, alpha, recon, positions, scales, rotations, forward_scratch, g_positions,
+        g_scales, g_rotations, g_opacities, g_colors, d_positions, d_scales, d_rotations, d_opacities, d_colors,
+        d_motion_lr, scratch, as_stream(stream)));
+    return OSS_OK;
+}
+
 int oss_warp_positions(int64_t n, int64_t h, int64_t w, const float* motion, float alpha, const float* xy,
                        float* out_xy, uint8_t* in_frame, void* stream) {
     OSS_CHECK(n >= 0, OSS_ERR_INVALID, "N must be non-negative");

@@ -179,6 +179,16 @@ cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const
                                const float* ops, const float* colors, float* out_pos, float* out_scales,
                                float* out_rots, float* out_ops, float* out_colors, int32_t* out_count,
                                void* scratch, cudaStream_t stream);
+// Backward of launch_warp_canvas (fwd_scratch: the forward's scratch, which
+// holds the survivor offsets); d_motion (LR, may be null) is written, d_hr
+// planes live in `scratch` (warp_backward_scratch_bytes).
+int64_t warp_backward_scratch_bytes(int64_t h, int64_t w);
+cudaError_t launch_warp_canvas_backward(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                                        const float* recon4, const float* pos, const float* scales, const float* rots,
+                                        const void* fwd_scratch, const float* g_pos, const float* g_scales,
+                                        const float* g_rots, const float* g_ops, const float* g_colors, float* d_pos,
+                                        float* d_scales, float* d_rots, float* d_ops, float* d_colors,
+                                        float* d_motion, void* scratch, cudaStream_t stream);
 cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, float alpha, const float* xy,
                                   float* out_xy, uint8_t* in_frame, cudaStream_t stream);
 

@@ -46,7 +46,7 @@ struct BwdCfg {
     static constexpr int SLOT = kTile * ROW;              // floats per warp slot
     static constexpr int WARPS = SLOT * 4 * 4 <= 200 * 1024 ? 4 : 2;  // warps (slots) per CTA
     static constexpr int THREADS = WARPS * 32;
-    static constexpr int MIN_CTAS = FC <= 4 ? 5 : 1;  // 5 x 4 warps per SM (<= 96 registers) for F <= 4
+    static constexpr int MIN_CTAS = FC <= 4 ? 4 : 1;  // 4 x 4 warps per SM (<= 128 registers) for F <= 4
     // F <= 4 runs the packed f32x2 path: the staged block is interleaved by
     // column pairs, [go_k(c), go_k(c+1)] for k = 0..SG-1 per pair of columns.
     static constexpr bool PAIRED = FC <= 4;
@@ -149,7 +149,7 @@ __device__ __forceinline__ void bwd_rows_full_pk(const float* __restrict__ s_go,
         }
         const float rowGx = rowGx2.x + rowGx2.y;
         const float rowG = rowG2.x + rowG2.y;
-        // every moment is summed per row first (16 terms), then over the rows
+        // every moment is summed per row first, then over the rows
         Sxx += rowGxx2.x + rowGxx2.y;
         Sx += rowGx;
         Sxy = fmaf(rowGx, dy, Sxy);

@@ -22,6 +22,7 @@ struct Field {
     int hl, wl, h, w;
     float alpha, scale_y, scale_x;
     int same;
+    double scale_y_d, scale_x_d;  // hl / h and wl / w in double (the backward's exact weights)
 };
 
 __device__ __forceinline__ float lr_at(const Field& f, int ch, int y, int x) {
@@ -169,6 +170,331 @@ __global__ void __launch_bounds__(kThreads) k_warp_positions(int n, Field fld, c
     in_frame[g] = (nx >= 0.0f && nx < static_cast<float>(fld.w) && ny >= 0.0f && ny < static_cast<float>(fld.h)) ? 1 : 0;
 }
 
+// ---------------------------------------------------------------------------
+// Backward of the canvas warp (the gradients PyTorch's autograd takes through
+// canvas_warp.py:177-254 and covariance_resampling.py:76-116).
+//
+// One thread per input Gaussian recomputes its forward values.  A survivor
+// (output slot k = offs[g]) receives the upstream gradients of slot k; a dropped
+// Gaussian gets zero.  The motion sample and the four Jacobian samples are
+// bilinear in the position and linear in their fields: their position
+// derivatives add to d_pos, and their field weights are added (fp64 atomics)
+// into six HR gradient planes in double (motion x/y, d/dx of motion x/y, d/dy of
+// motion x/y).  k_warp_motion_grad then folds the central differences back onto the
+// motion planes and k_warp_lr_grad transposes the bilinear upsampling by a
+// gather per LR texel, so only the Gaussians' atomics depend on order.
+// ---------------------------------------------------------------------------
+
+// The fields in double, for the backward's derivatives: the Jacobian path
+// differentiates sampled central differences (second differences of the
+// upsampled motion), where fp32 rounding of each texel would dominate.
+__device__ double hr_at_f64(const Field& f, int ch, int i, int j) {
+    auto lr = [&](int y, int x) {
+        return static_cast<double>(f.alpha) * static_cast<double>(__ldg(f.m + (static_cast<int64_t>(ch) * f.hl + y) * f.wl + x));
+    };
+    if (f.same) return lr(i, j);
+    float sy = __fsub_rn(__fmul_rn(f.scale_y, __fadd_rn(static_cast<float>(i), 0.5f)), 0.5f);
+    if (sy < 0.0f) sy = 0.0f;
+    float sx = __fsub_rn(__fmul_rn(f.scale_x, __fadd_rn(static_cast<float>(j), 0.5f)), 0.5f);
+    if (sx < 0.0f) sx = 0.0f;
+    // taps as the forward chooses them (fp32), weights exact
+    const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
+    const int y1 = y0 + (y0 < f.hl - 1 ? 1 : 0), x1 = x0 + (x0 < f.wl - 1 ? 1 : 0);
+    const double syd = fmax(f.scale_y_d * (static_cast<double>(i) + 0.5) - 0.5, 0.0);
+    const double sxd = fmax(f.scale_x_d * (static_cast<double>(j) + 0.5) - 0.5, 0.0);
+    const double ly1 = fmin(syd - y0, 1.0), lx1 = fmin(sxd - x0, 1.0);
+    const double ly0 = 1.0 - ly1, lx0 = 1.0 - lx1;
+    return ly0 * (lx0 * lr(y0, x0) + lx1 * lr(y0, x1)) + ly1 * (lx0 * lr(y1, x0) + lx1 * lr(y1, x1));
+}
+
+__device__ double field_at_f64(const Field& f, int kind, int ch, int i, int j) {
+    if (kind == 0) return hr_at_f64(f, ch, i, j);
+    if (kind == 1) {
+        const int jp = j + 1 < f.w ? j + 1 : f.w - 1, jm = j - 1 >= 0 ? j - 1 : 0;
+        return 0.5 * (hr_at_f64(f, ch, i, jp) - hr_at_f64(f, ch, i, jm));
+    }
+    const int ip = i + 1 < f.h ? i + 1 : f.h - 1, im = i - 1 >= 0 ? i - 1 : 0;
+    return 0.5 * (hr_at_f64(f, ch, ip, j) - hr_at_f64(f, ch, im, j));
+}
+
+// grid_sample's backward (bilinear, align_corners=False): returns d out / d x and
+// d out / d y of the sample at (x, y) and, when `dfield` is non-null, adds
+// g * (tap weight) into the tapped texels of dfield (an HR plane).  Border mode
+// clips the source coordinate and, as PyTorch does, passes no gradient through a
+// clipped coordinate (the borders themselves count as out of range).
+__device__ float2 grid_sample_grad(const Field& f, int kind, int ch, float x, float y, bool border, float g,
+                                   double* __restrict__ dfield) {
+    const float gx = __fsub_rn(__fmul_rn(__fdiv_rn(x, static_cast<float>(f.w)), 2.0f), 1.0f);
+    const float gy = __fsub_rn(__fmul_rn(__fdiv_rn(y, static_cast<float>(f.h)), 2.0f), 1.0f);
+    float ix = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gx, 1.0f), static_cast<float>(f.w)), 1.0f), 2.0f);
+    float iy = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gy, 1.0f), static_cast<float>(f.h)), 1.0f), 2.0f);
+    float mx = 1.0f, my = 1.0f;
+    if (border) {
+        if (ix <= 0.0f) { ix = 0.0f; mx = 0.0f; }
+        else if (ix >= static_cast<float>(f.w - 1)) { ix = static_cast<float>(f.w - 1); mx = 0.0f; }
+        if (iy <= 0.0f) { iy = 0.0f; my = 0.0f; }
+        else if (iy >= static_cast<float>(f.h - 1)) { iy = static_cast<float>(f.h - 1); my = 0.0f; }
+    }
+    const float x0 = floorf(ix), y0 = floorf(iy);
+    if (!(x0 > -2.0f && x0 < static_cast<float>(f.w) && y0 > -2.0f && y0 < static_cast<float>(f.h))) {
+        return make_float2(0.0f, 0.0f);
+    }
+    const int xi = static_cast<int>(x0), yi = static_cast<int>(y0);
+    // the forward's taps with exact weights: the source coordinate is x - 1/2 (or
+    // the border it was clipped to)
+    const double wx = (mx == 0.0f ? static_cast<double>(ix) : static_cast<double>(x) - 0.5) - x0;
+    const double wy = (my == 0.0f ? static_cast<double>(iy) : static_cast<double>(y) - 0.5) - y0;
+    const double ex = 1.0 - wx, sy = 1.0 - wy;
+    const double wts[4] = {sy * ex, sy * wx, wy * ex, wy * wx};
+    // d weight / d ix and d weight / d iy of the four taps
+    const double dwx[4] = {-sy, sy, -wy, wy};
+    const double dwy[4] = {-ex, -wx, ex, wx};
+    double dix = 0.0, diy = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int xx = xi + (k & 1), yy = yi + (k >> 1);
+        if (xx >= 0 && xx < f.w && yy >= 0 && yy < f.h) {
+            const double v = field_at_f64(f, kind, ch, yy, xx);
+            dix += v * dwx[k];
+            diy += v * dwy[k];
+            if (dfield != nullptr) {
+                atomicAdd(dfield + static_cast<int64_t>(yy) * f.w + xx, static_cast<double>(g) * wts[k]);
+            }
+        }
+    }
+    // ix = x - 1/2 and iy = y - 1/2 up to rounding: d ix / d x = 1
+    return make_float2(static_cast<float>(g * dix * mx), static_cast<float>(g * diy * my));
+}
+
+// grid_sample's value with the field in double (bilinear, align_corners=False).
+__device__ double grid_sample_f64(const Field& f, int kind, int ch, float x, float y, bool border) {
+    const float gx = __fsub_rn(__fmul_rn(__fdiv_rn(x, static_cast<float>(f.w)), 2.0f), 1.0f);
+    const float gy = __fsub_rn(__fmul_rn(__fdiv_rn(y, static_cast<float>(f.h)), 2.0f), 1.0f);
+    float ix = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gx, 1.0f), static_cast<float>(f.w)), 1.0f), 2.0f);
+    float iy = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gy, 1.0f), static_cast<float>(f.h)), 1.0f), 2.0f);
+    bool cx = false, cy = false;
+    if (border) {
+        const float bx = fminf(static_cast<float>(f.w - 1), fmaxf(ix, 0.0f));
+        const float by = fminf(static_cast<float>(f.h - 1), fmaxf(iy, 0.0f));
+        cx = bx != ix;
+        cy = by != iy;
+        ix = bx;
+        iy = by;
+    }
+    const float x0 = floorf(ix), y0 = floorf(iy);
+    if (!(x0 > -2.0f && x0 < static_cast<float>(f.w) && y0 > -2.0f && y0 < static_cast<float>(f.h))) return 0.0;
+    // the source coordinate is x - 1/2 exactly (or the border it was clipped to); the
+    // taps are the forward's
+    const double ixd = cx ? static_cast<double>(ix) : static_cast<double>(x) - 0.5;
+    const double iyd = cy ? static_cast<double>(iy) : static_cast<double>(y) - 0.5;
+    const double wx = ixd - x0, wy = iyd - y0;
+    const double wts[4] = {(1.0 - wy) * (1.0 - wx), (1.0 - wy) * wx, wy * (1.0 - wx), wy * wx};
+    const int xi = static_cast<int>(x0), yi = static_cast<int>(y0);
+    double out = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int xx = xi + (k & 1), yy = yi + (k >> 1);
+        if (xx >= 0 && xx < f.w && yy >= 0 && yy < f.h) out += field_at_f64(f, kind, ch, yy, xx) * wts[k];
+    }
+    return out;
+}
+
+__global__ void __launch_bounds__(kThreads) k_warp_backward(
+    int n, int f, Field fld, float4 recon, const float2* __restrict__ pos, const float2* __restrict__ scales,
+    const float* __restrict__ rots, const int32_t* __restrict__ offs, const float2* __restrict__ g_pos,
+    const float2* __restrict__ g_scales, const float* __restrict__ g_rots, const float* __restrict__ g_ops,
+    const float* __restrict__ g_colors, float2* __restrict__ d_pos, float2* __restrict__ d_scales,
+    float* __restrict__ d_rots, float* __restrict__ d_ops, float* __restrict__ d_colors, double* __restrict__ d_hr) {
+    const int g = blockIdx.x * kThreads + threadIdx.x;
+    if (g >= n) return;
+    const int k = offs[g];
+    if (offs[g + 1] == k) {  // dropped: the outputs do not depend on it
+        d_pos[g] = make_float2(0.0f, 0.0f);
+        d_scales[g] = make_float2(0.0f, 0.0f);
+        d_rots[g] = 0.0f;
+        if (d_ops != nullptr) d_ops[g] = 0.0f;
+        for (int c = 0; c < f; ++c) d_colors[static_cast<int64_t>(g) * f + c] = 0.0f;
+        return;
+    }
+    const float2 gp = g_pos != nullptr ? g_pos[k] : make_float2(0.0f, 0.0f);
+    const float2 gs = g_scales != nullptr ? g_scales[k] : make_float2(0.0f, 0.0f);
+    const float gr = g_rots != nullptr ? g_rots[k] : 0.0f;
+    if (d_ops != nullptr) d_ops[g] = g_ops != nullptr ? g_ops[k] : 0.0f;
+    for (int c = 0; c < f; ++c) {
+        d_colors[static_cast<int64_t>(g) * f + c] = g_colors != nullptr ? g_colors[static_cast<int64_t>(k) * f + c] : 0.0f;
+    }
+    const int64_t plane = static_cast<int64_t>(fld.h) * fld.w;
+    const float2 p = pos[g];
+    // new position = p + m(p): d p = g_pos + (d m / d p)^T g_pos
+    float2 dp = gp;
+    {
+        const float2 a = grid_sample_grad(fld, 0, 0, p.x, p.y, false, gp.x, d_hr);
+        const float2 b = grid_sample_grad(fld, 0, 1, p.x, p.y, false, gp.y, d_hr + plane);
+        dp.x += a.x + b.x;
+        dp.y += a.y + b.y;
+    }
+    const float j00 = __fadd_rn(1.0f, grid_sample(fld, 1, 0, p.x, p.y, true));
+    const float j10 = __fadd_rn(0.0f, grid_sample(fld, 1, 1, p.x, p.y, true));
+    const float j01 = __fadd_rn(0.0f, grid_sample(fld, 2, 0, p.x, p.y, true));
+    const float j11 = __fadd_rn(1.0f, grid_sample(fld, 2, 1, p.x, p.y, true));
+    const float2 s = scales[g];
+    const float th = rots[g];
+    const float dev = fmaxf(fmaxf(fabsf(__fsub_rn(j00, 1.0f)), fabsf(j01)), fmaxf(fabsf(j10), fabsf(__fsub_rn(j11, 1.0f))));
+    if (dev < 1.0e-5f) {  // identity Jacobian: scales and rotation pass through
+        d_pos[g] = dp;
+        d_scales[g] = gs;
+        d_rots[g] = gr;
+        return;
+    }
+    // the covariance chain again, in double: the eigendecomposition's derivatives
+    // are ill-conditioned where the resampled covariance is nearly isotropic, so
+    // fp32 rounding of J, U and the eigenvalues would dominate them
+    const double J00 = 1.0 + grid_sample_f64(fld, 1, 0, p.x, p.y, true);
+    const double J10 = grid_sample_f64(fld, 1, 1, p.x, p.y, true);
+    const double J01 = grid_sample_f64(fld, 2, 0, p.x, p.y, true);
+    const double J11 = 1.0 + grid_sample_f64(fld, 2, 1, p.x, p.y, true);
+    double sn, c;
+    sincos(static_cast<double>(th), &sn, &c);
+    const double a0 = fmax(static_cast<double>(s.x), 0.0), a1 = fmax(static_cast<double>(s.y), 0.0);
+    const double v0 = a0 * a0, v1 = a1 * a1;
+    const double q00 = c * c * v0 + sn * sn * v1, q01 = c * sn * (v0 - v1), q11 = sn * sn * v0 + c * c * v1;
+    const double t00 = J00 * q00 + J01 * q01, t01 = J00 * q01 + J01 * q11;
+    const double t10 = J10 * q00 + J11 * q01, t11 = J10 * q01 + J11 * q11;
+    const double u00 = t00 * J00 + t01 * J01 + recon.x;
+    const double u01 = t00 * J10 + t01 * J11 + recon.y;
+    const double u10 = t10 * J00 + t11 * J01 + recon.z;
+    const double u11 = t10 * J10 + t11 * J11 + recon.w;
+    const double a = u00 + 1.0e-7, b = 0.5 * (u01 + u10), cc = u11 + 1.0e-7;
+    const double ht = 0.5 * (a + cc), hd = 0.5 * (a - cc);
+    const double rad = sqrt(hd * hd + b * b + 1.0e-12);
+    const double e0 = ht + rad, e1 = ht - rad;
+    // backward of the eigendecomposition: s_i = sqrt(max(e_i, 1e-12)), r = atan2(2b, a - c) / 2
+    const double d_e0 = e0 >= 1.0e-12 ? gs.x * 0.5 / sqrt(e0) : 0.0;
+    const double d_e1 = e1 >= 1.0e-12 ? gs.y * 0.5 / sqrt(e1) : 0.0;
+    const double d_ht = d_e0 + d_e1, d_rad = d_e0 - d_e1;
+    const double d_hd = d_rad * hd / rad;
+    double d_b = d_rad * b / rad;
+    const double ax = a - cc, ay = 2.0 * b, r2 = ax * ax + ay * ay;
+    double d_ax = 0.0;
+    if (r2 > 0.0) {  // atan2 has no derivative where both arguments vanish (exactly isotropic)
+        d_b += 0.5 * gr * 2.0 * ax / r2;
+        d_ax = 0.5 * gr * (-ay) / r2;
+    }
+    const double d_a = 0.5 * d_ht + 0.5 * d_hd + d_ax;
+    const double d_c = 0.5 * d_ht - 0.5 * d_hd - d_ax;
+    // U = J Q J^T + R, symmetrised: dU = [[d_a, d_b / 2], [d_b / 2, d_c]]
+    const double g00 = d_a, g01 = 0.5 * d_b, g11 = d_c;
+    // dJ = 2 dU J Q (dU and Q symmetric)
+    const double m00 = g00 * J00 + g01 * J10, m01 = g00 * J01 + g01 * J11;
+    const double m10 = g01 * J00 + g11 * J10, m11 = g01 * J01 + g11 * J11;
+    const float dj00 = static_cast<float>(2.0 * (m00 * q00 + m01 * q01));
+    const float dj01 = static_cast<float>(2.0 * (m00 * q01 + m01 * q11));
+    const float dj10 = static_cast<float>(2.0 * (m10 * q00 + m11 * q01));
+    const float dj11 = static_cast<float>(2.0 * (m10 * q01 + m11 * q11));
+    // dQ = J^T dU J
+    const double w00 = J00 * g00 + J10 * g01, w01 = J00 * g01 + J10 * g11;
+    const double w10 = J01 * g00 + J11 * g01, w11 = J01 * g01 + J11 * g11;
+    const double dq00 = w00 * J00 + w01 * J10, dq01 = w00 * J01 + w01 * J11;
+    const double dq10 = w10 * J00 + w11 * J10, dq11 = w10 * J01 + w11 * J11;
+    // Q = R diag(v) R^T, v = max(s, 0)^2
+    const double dqs = dq01 + dq10;
+    const double dv0 = c * c * dq00 + c * sn * dqs + sn * sn * dq11;
+    const double dv1 = sn * sn * dq00 - c * sn * dqs + c * c * dq11;
+    d_scales[g] = make_float2(s.x >= 0.0f ? static_cast<float>(2.0 * a0 * dv0) : 0.0f,
+                              s.y >= 0.0f ? static_cast<float>(2.0 * a1 * dv1) : 0.0f);
+    d_rots[g] = static_cast<float>((v0 - v1) * (-2.0 * c * sn * dq00 + (c * c - sn * sn) * dqs + 2.0 * c * sn * dq11));
+    // J = I + [d/dx m, d/dy m] sampled with border padding
+    float2 t;
+    t = grid_sample_grad(fld, 1, 0, p.x, p.y, true, dj00, d_hr + 2 * plane);
+    dp.x += t.x;
+    dp.y += t.y;
+    t = grid_sample_grad(fld, 1, 1, p.x, p.y, true, dj10, d_hr + 3 * plane);
+    dp.x += t.x;
+    dp.y += t.y;
+    t = grid_sample_grad(fld, 2, 0, p.x, p.y, true, dj01, d_hr + 4 * plane);
+    dp.x += t.x;
+    dp.y += t.y;
+    t = grid_sample_grad(fld, 2, 1, p.x, p.y, true, dj11, d_hr + 5 * plane);
+    dp.x += t.x;
+    dp.y += t.y;
+    d_pos[g] = dp;
+}
+
+// Gradient of the HR motion planes: the motion sample's plane plus the central
+// differences (with replicate padding) transposed onto their taps:
+// dmdx[i][j] = (m[i][min(j + 1, w - 1)] - m[i][max(j - 1, 0)]) / 2, and dmdy alike.
+// Writes planes 0 and 1 of d_hr in place of the sample's.
+__global__ void __launch_bounds__(kThreads) k_warp_motion_grad(int h, int w, double* __restrict__ d_hr) {
+    const int64_t plane = static_cast<int64_t>(h) * w;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (idx >= 2 * plane) return;
+    const int ch = static_cast<int>(idx / plane);
+    const int64_t pix = idx - ch * plane;
+    const int i = static_cast<int>(pix / w), j = static_cast<int>(pix - static_cast<int64_t>(i) * w);
+    const double* gx = d_hr + (2 + ch) * plane + static_cast<int64_t>(i) * w;  // row i of d(dm/dx)
+    const double* gy = d_hr + (4 + ch) * plane;                              // d(dm/dy)
+    double v = d_hr[idx];
+    // texel j is the + tap of column j - 1 (and of w - 1 itself at the right edge) and
+    // the - tap of column j + 1 (and of 0 itself at the left edge)
+    if (j >= 1) v += 0.5 * gx[j - 1];
+    if (j == w - 1) v += 0.5 * gx[w - 1];
+    if (j + 1 <= w - 1) v -= 0.5 * gx[j + 1];
+    if (j == 0) v -= 0.5 * gx[0];
+    if (i >= 1) v += 0.5 * gy[static_cast<int64_t>(i - 1) * w + j];
+    if (i == h - 1) v += 0.5 * gy[static_cast<int64_t>(h - 1) * w + j];
+    if (i + 1 <= h - 1) v -= 0.5 * gy[static_cast<int64_t>(i + 1) * w + j];
+    if (i == 0) v -= 0.5 * gy[j];
+    d_hr[idx] = v;
+}
+
+// One LR axis of F.interpolate(bilinear, align_corners=False): the two LR taps of
+// HR index i and their weights (the forward's hr_at arithmetic).
+__device__ __forceinline__ void lr_taps(float scale, int i, int nl, int& t0, int& t1, float& w0, float& w1) {
+    float sp = __fsub_rn(__fmul_rn(scale, __fadd_rn(static_cast<float>(i), 0.5f)), 0.5f);
+    if (sp < 0.0f) sp = 0.0f;
+    t0 = static_cast<int>(sp);
+    t1 = t0 + (t0 < nl - 1 ? 1 : 0);
+    w1 = fminf(__fsub_rn(sp, static_cast<float>(t0)), 1.0f);
+    w0 = __fsub_rn(1.0f, w1);
+}
+
+// d motion_lr = alpha * (upsampling)^T d motion_hr, one thread per LR texel
+// gathering the HR texels whose taps include it (a window of rows and columns
+// around its image under the upsampling), in a fixed order.
+__global__ void __launch_bounds__(kThreads) k_warp_lr_grad(Field f, const double* __restrict__ d_hr,
+                                                            float* __restrict__ d_motion) {
+    const int64_t lplane = static_cast<int64_t>(f.hl) * f.wl;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (idx >= 2 * lplane) return;
+    const int ch = static_cast<int>(idx / lplane);
+    const int64_t pix = idx - ch * lplane;
+    const int y = static_cast<int>(pix / f.wl), x = static_cast<int>(pix - static_cast<int64_t>(y) * f.wl);
+    const int64_t plane = static_cast<int64_t>(f.h) * f.w;
+    // HR rows whose taps can reach LR row y: sp = s (i + 1/2) - 1/2 in [y - 1, y + 1]
+    const int ilo = max(0, static_cast<int>(floorf((static_cast<float>(y) - 0.5f) / f.scale_y - 0.5f)) - 1);
+    const int ihi = min(f.h - 1, static_cast<int>(ceilf((static_cast<float>(y) + 1.5f) / f.scale_y - 0.5f)) + 1);
+    const int jlo = max(0, static_cast<int>(floorf((static_cast<float>(x) - 0.5f) / f.scale_x - 0.5f)) - 1);
+    const int jhi = min(f.w - 1, static_cast<int>(ceilf((static_cast<float>(x) + 1.5f) / f.scale_x - 0.5f)) + 1);
+    double acc = 0.0;
+    for (int i = ilo; i <= ihi; ++i) {
+        int r0, r1;
+        float wr0, wr1;
+        lr_taps(f.scale_y, i, f.hl, r0, r1, wr0, wr1);
+        const double wy = (r0 == y ? wr0 : 0.0f) + (r1 == y ? wr1 : 0.0f);
+        if (wy == 0.0) continue;
+        double row = 0.0;
+        for (int j = jlo; j <= jhi; ++j) {
+            int c0, c1;
+            float wc0, wc1;
+            lr_taps(f.scale_x, j, f.wl, c0, c1, wc0, wc1);
+            const double wx = (c0 == x ? wc0 : 0.0f) + (c1 == x ? wc1 : 0.0f);
+            if (wx != 0.0) row += wx * d_hr[ch * plane + static_cast<int64_t>(i) * f.w + j];
+        }
+        acc += wy * row;
+    }
+    d_motion[idx] = static_cast<float>(static_cast<double>(f.alpha) * acc);
+}
+
 Field make_field(const float* m, int hl, int wl, int h, int w, float alpha) {
     Field f;
     f.m = m;
@@ -180,6 +506,8 @@ Field make_field(const float* m, int hl, int wl, int h, int w, float alpha) {
     f.scale_y = static_cast<float>(hl) / static_cast<float>(h);
     f.scale_x = static_cast<float>(wl) / static_cast<float>(w);
     f.same = (hl == h && wl == w) ? 1 : 0;
+    f.scale_y_d = static_cast<double>(hl) / static_cast<double>(h);
+    f.scale_x_d = static_cast<double>(wl) / static_cast<double>(w);
     return f;
 }
 
@@ -217,6 +545,41 @@ cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const
         if (err != cudaSuccess) return err;
     }
     return cudaMemcpyAsync(out_count, flags + n, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
+}
+
+int64_t warp_backward_scratch_bytes(int64_t h, int64_t w) { return arena_bytes(6 * h * w, sizeof(double)); }
+
+cudaError_t launch_warp_canvas_backward(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                                        const float* recon4, const float* pos, const float* scales, const float* rots,
+                                        const void* fwd_scratch, const float* g_pos, const float* g_scales,
+                                        const float* g_rots, const float* g_ops, const float* g_colors, float* d_pos,
+                                        float* d_scales, float* d_rots, float* d_ops, float* d_colors,
+                                        float* d_motion, void* scratch, cudaStream_t stream) {
+    // the forward's survivor offsets sit after its per-Gaussian records (launch_warp_canvas)
+    Arena fwd{static_cast<char*>(const_cast<void*>(fwd_scratch)), warp_scratch_bytes(n), 0};
+    fwd.take<float4>(static_cast<int64_t>(n) * 2);
+    const int32_t* offs = fwd.take<int32_t>(n + 1);
+    const Field fld = make_field(motion, hl, wl, h, w, alpha);
+    const float4 recon = make_float4(recon4[0], recon4[1], recon4[2], recon4[3]);
+    const int64_t plane = static_cast<int64_t>(h) * w;
+    double* d_hr = static_cast<double*>(scratch);  // six HR gradient planes, accumulated in double
+    cudaError_t err = cudaMemsetAsync(d_hr, 0, sizeof(double) * 6 * plane, stream);
+    if (err != cudaSuccess) return err;
+    if (n > 0) {
+        k_warp_backward<<<static_cast<unsigned>(div_up(n, kThreads)), kThreads, 0, stream>>>(
+            n, f, fld, recon, reinterpret_cast<const float2*>(pos), reinterpret_cast<const float2*>(scales), rots, offs,
+            reinterpret_cast<const float2*>(g_pos), reinterpret_cast<const float2*>(g_scales), g_rots, g_ops, g_colors,
+            reinterpret_cast<float2*>(d_pos), reinterpret_cast<float2*>(d_scales), d_rots, d_ops, d_colors, d_hr);
+        err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+    }
+    if (d_motion == nullptr) return cudaSuccess;
+    k_warp_motion_grad<<<static_cast<unsigned>(div_up(2 * plane, kThreads)), kThreads, 0, stream>>>(h, w, d_hr);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const int64_t lplane = static_cast<int64_t>(hl) * wl;
+    k_warp_lr_grad<<<static_cast<unsigned>(div_up(2 * lplane, kThreads)), kThreads, 0, stream>>>(fld, d_hr, d_motion);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_warp_positions(int n, int h, int w, const float* motion, float alpha, const float* xy,

@@ -6,15 +6,16 @@ warp_canvas   -- drop-in for oss/sr/v6/canvas_warp.py:177-254 (GS-STVSR:
                  ``alpha`` that scales the motion (extrapolation at t + alpha).
 warp_positions -- drop-in for oss/gaussian/canvas/warp.py:28-91.
 
-Forward only: the kernels do not record an autograd graph, so a call with
-inputs that require grad under grad mode raises instead of silently cutting
-the graph.
+warp_canvas is differentiable (its backward is a kernel of its own);
+warp_positions is forward only and raises on inputs that require grad under
+grad mode instead of silently cutting the graph.
 """
 from __future__ import annotations
 
 from typing import Tuple
 
 import torch
+from torch.autograd import Function
 
 from oss_cuda import _lib
 from oss_cuda._raster import aligned, stream_of
@@ -73,6 +74,62 @@ def _recon4(sigma_recon) -> list[float]:
     return [s, 0.0, 0.0, s]
 
 
+class _WarpCanvas(Function):
+    """The canvas warp and its backward on the GPU (oss_warp_canvas /
+    oss_warp_canvas_backward): gradients reach positions, scales, rotations,
+    opacities, colors and the motion field, as autograd's do through the
+    reference's torch ops."""
+
+    @staticmethod
+    def forward(ctx, motion, pos, sc, rt, op, col, h, w, recon4, alpha):
+        n, f = int(pos.shape[0]), int(col.shape[1])
+        dev = pos.device
+        lib = _lib.lib()
+        f32 = dict(device=dev, dtype=torch.float32)
+        outs = [torch.empty((n, 2), **f32), torch.empty((n, 2), **f32), torch.empty((n,), **f32),
+                torch.empty((n,), **f32), torch.empty((n, f), **f32)]
+        out_count = torch.empty((1,), device=dev, dtype=torch.int32)
+        scratch = torch.empty((lib.oss_warp_canvas_scratch_bytes(n),), device=dev, dtype=torch.uint8)
+        recon = torch.tensor(recon4, dtype=torch.float32)
+        _lib.check(
+            lib.oss_warp_canvas(n, f, motion.shape[1], motion.shape[2], h, w, motion.data_ptr(), float(alpha),
+                                recon.data_ptr(), pos.data_ptr(), sc.data_ptr(), rt.data_ptr(), op.data_ptr(),
+                                col.data_ptr() if f > 0 else None, *(o.data_ptr() if o.numel() else None for o in outs),
+                                out_count.data_ptr(), scratch.data_ptr(), scratch.numel(), stream_of(pos)),
+            "oss_warp_canvas",
+        )
+        k = int(out_count.item())
+        ctx.save_for_backward(motion, pos, sc, rt, scratch)
+        ctx.meta = (n, f, h, w, tuple(recon4), float(alpha), k)
+        return tuple(o[:k] for o in outs)
+
+    @staticmethod
+    def backward(ctx, g_pos, g_sc, g_rt, g_op, g_col):
+        motion, pos, sc, rt, scratch = ctx.saved_tensors
+        n, f, h, w, recon4, alpha, k = ctx.meta
+        dev = pos.device
+        lib = _lib.lib()
+        f32 = dict(device=dev, dtype=torch.float32)
+        grads = [None if g is None else _f32c(g) for g in (g_pos, g_sc, g_rt, g_op, g_col)]
+        d = [torch.empty((n, 2), **f32), torch.empty((n, 2), **f32), torch.empty((n,), **f32),
+             torch.empty((n,), **f32), torch.empty((n, f), **f32)]
+        d_motion = torch.empty(motion.shape, **f32) if ctx.needs_input_grad[0] else None
+        bscratch = torch.empty((lib.oss_warp_canvas_backward_scratch_bytes(h, w),), device=dev, dtype=torch.uint8)
+        recon = torch.tensor(recon4, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            _lib.check(lib.oss_warp_canvas_backward(
+                n, f, motion.shape[1], motion.shape[2], h, w, motion.data_ptr(), alpha, recon.data_ptr(),
+                pos.data_ptr(), sc.data_ptr(), rt.data_ptr(), scratch.data_ptr(),
+                *(None if g is None or g.numel() == 0 else g.data_ptr() for g in grads),
+                *(t.data_ptr() if t.numel() else None for t in d), _lib.ptr(d_motion), bscratch.data_ptr(),
+                bscratch.numel(), stream_of(pos)), "oss_warp_canvas_backward")
+        return (d_motion, *d, None, None, None, None)
+
+
+def _f32c(t: torch.Tensor) -> torch.Tensor:
+    return aligned(t.to(dtype=torch.float32).contiguous(), 8)
+
+
 def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
                 sigma_recon: torch.Tensor | float = 0.5, alpha: float = 1.0) -> CanvasState:
     """Warp canvas positions by alpha * motion and resample covariances.
@@ -80,38 +137,26 @@ def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
     Returns a fresh CanvasState holding the Gaussians whose warped centre
     stays inside the frame, in input order (one device->host read of the
     count, as the reference's ``.item()`` at canvas_warp.py:253).
+    Differentiable in the canvas tensors and motion_lr (its first batch item,
+    the one the warp reads); sigma_recon is a constant.
     """
     h, w = _validate_motion(motion_lr, output_hw)
     count = _validate_canvas(canvas)
     src = [canvas.positions[:count], canvas.scales[:count], canvas.rotations[:count], canvas.opacities[:count],
            canvas.colors[:count]]
-    _no_grad_inputs(motion_lr, *src)
+    if isinstance(sigma_recon, torch.Tensor) and sigma_recon.requires_grad and torch.is_grad_enabled():
+        raise RuntimeError("warp_canvas takes sigma_recon as a constant; detach it")
     if count == 0:
         return CanvasState(*(t.clone() for t in src), count=0)
     dev = canvas.positions.device
     if dev.type != "cuda" or motion_lr.device != dev:
         raise RuntimeError("warp_canvas needs canvas and motion_lr on the same CUDA device")
     out_dtypes = [t.dtype for t in src]
-    pos, sc, rt, op, col = (_f32(t) for t in src)
-    motion = _f32(motion_lr[0])
-    f = int(col.shape[1])
-    lib = _lib.lib()
     with torch.cuda.device(dev):
-        f32 = dict(device=dev, dtype=torch.float32)
-        outs = [torch.empty((count, 2), **f32), torch.empty((count, 2), **f32), torch.empty((count,), **f32),
-                torch.empty((count,), **f32), torch.empty((count, f), **f32)]
-        out_count = torch.empty((1,), device=dev, dtype=torch.int32)
-        scratch = torch.empty((lib.oss_warp_canvas_scratch_bytes(count),), device=dev, dtype=torch.uint8)
-        recon = (torch.tensor(_recon4(sigma_recon), dtype=torch.float32))
-        _lib.check(
-            lib.oss_warp_canvas(count, f, motion.shape[1], motion.shape[2], h, w, motion.data_ptr(), float(alpha),
-                                recon.data_ptr(), pos.data_ptr(), sc.data_ptr(), rt.data_ptr(), op.data_ptr(),
-                                col.data_ptr() if f > 0 else None, *(o.data_ptr() if o.numel() else None for o in outs),
-                                out_count.data_ptr(), scratch.data_ptr(), scratch.numel(), stream_of(pos)),
-            "oss_warp_canvas",
-        )
-        k = int(out_count.item())
-    res = [o[:k].to(dtype=dt) for o, dt in zip(outs, out_dtypes)]
+        outs = _WarpCanvas.apply(_f32c(motion_lr[0]), *(_f32c(t) for t in src), h, w, _recon4(sigma_recon),
+                                 float(alpha))
+    k = int(outs[0].shape[0])
+    res = [o.to(dtype=dt) for o, dt in zip(outs, out_dtypes)]
     return CanvasState(*res, count=k)
 
 

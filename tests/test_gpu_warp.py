@@ -117,11 +117,150 @@ def test_warp_identity_and_empty(cuda_device):
     assert empty.count == 0 and empty.positions.shape == (0, 2)
 
 
-def test_warp_refuses_grad_inputs(cuda_device):
+# ------------------------------------------------------------------ gradients
+
+def warp_f64(pos, scales, rots, ops, cols, motion_lr, hw, recon):
+    """The reference's canvas warp (oss/sr/v6/canvas_warp.py:177-254 with
+    covariance_resampling.py:76-116) restated with the same torch operations in
+    float64 on the CPU, so that autograd gives the exact-arithmetic gradients
+    the GPU backward is judged against."""
+    import torch.nn.functional as F
+
+    h, w = hw
+    m = motion_lr[:1]
+    if tuple(m.shape[-2:]) != (h, w):
+        m = F.interpolate(m, size=(h, w), mode="bilinear", align_corners=False)
+    grid = torch.stack([pos[:, 0] / w * 2.0 - 1.0, pos[:, 1] / h * 2.0 - 1.0], -1).view(1, -1, 1, 2)
+    sm = F.grid_sample(m, grid, mode="bilinear", padding_mode="zeros", align_corners=False)
+    new_pos = pos + sm.view(2, -1).t()
+    keep = (new_pos[:, 0] >= 0) & (new_pos[:, 0] < w) & (new_pos[:, 1] >= 0) & (new_pos[:, 1] < h)
+    pad = F.pad(m, (1, 1, 1, 1), mode="replicate")
+    dmdx = (pad[..., 1:-1, 2:] - pad[..., 1:-1, :-2]) * 0.5
+    dmdy = (pad[..., 2:, 1:-1] - pad[..., :-2, 1:-1]) * 0.5
+    sx = F.grid_sample(dmdx, grid, mode="bilinear", padding_mode="border", align_corners=False)[0, :, :, 0].t()
+    sy = F.grid_sample(dmdy, grid, mode="bilinear", padding_mode="border", align_corners=False)[0, :, :, 0].t()
+    j = torch.eye(2, dtype=pos.dtype).expand(pos.shape[0], -1, -1).clone()
+    j[:, 0, 0] += sx[:, 0]
+    j[:, 1, 0] += sx[:, 1]
+    j[:, 0, 1] += sy[:, 0]
+    j[:, 1, 1] += sy[:, 1]
+    ident = (j - torch.eye(2, dtype=pos.dtype)).abs().reshape(-1, 4).amax(-1) < 1e-5
+    c, s = torch.cos(rots), torch.sin(rots)
+    r = torch.stack([torch.stack([c, -s], -1), torch.stack([s, c], -1)], -2)
+    sig = r @ torch.diag_embed(scales.clamp(min=0.0).square()) @ r.transpose(-1, -2)
+    u = j @ sig @ j.transpose(-1, -2) + torch.eye(2, dtype=pos.dtype) * recon
+    u = 0.5 * (u + u.transpose(-1, -2)) + 1e-7 * torch.eye(2, dtype=pos.dtype)
+    u = 0.5 * (u + u.transpose(-1, -2))
+    a, b, cc = u[:, 0, 0], u[:, 0, 1], u[:, 1, 1]
+    ht, hd = 0.5 * (a + cc), 0.5 * (a - cc)
+    rad = torch.sqrt(hd.square() + b.square() + 1e-12)
+    new_sc = torch.sqrt(torch.stack([(ht + rad).clamp(min=1e-12), (ht - rad).clamp(min=1e-12)], -1))
+    new_rot = 0.5 * torch.atan2(2.0 * b, a - cc)
+    new_sc = torch.where(ident[:, None], scales, new_sc)
+    new_rot = torch.where(ident, rots, new_rot)
+    return new_pos[keep], new_sc[keep], new_rot[keep], ops[keep], cols[keep]
+
+
+def _gpu_warp_grads(c, device, alpha=1.0):
     from oss_b200 import CanvasState, warp_canvas
 
-    pos = torch.rand(4, 2, device=cuda_device, requires_grad=True)
-    canvas = CanvasState(pos, torch.ones(4, 2, device=cuda_device), torch.zeros(4, device=cuda_device),
-                         torch.ones(4, device=cuda_device), torch.ones(4, 3, device=cuda_device), 4)
+    names = ("positions", "scales", "rotations", "opacities", "colors", "motion")
+    leaves = [torch.from_numpy(np.ascontiguousarray(c[k])).to(device).requires_grad_(True) for k in names]
+    hw = tuple(int(v) for v in c["hw"])
+    canvas = CanvasState(*leaves[:5], count=int(leaves[0].shape[0]))
+    out = warp_canvas(canvas, leaves[5], hw, sigma_recon=float(c["recon"]), alpha=alpha)
+    assert out.count == int(c["out_count"])
+    outs = (out.positions, out.scales, out.rotations, out.opacities, out.colors)
+    loss = sum((o * torch.from_numpy(c[f"g_{k}"]).to(device)).sum() for o, k in zip(outs, names[:5]))
+    loss.backward()
+    return {k: t.grad.cpu().numpy() for k, t in zip(names, leaves)}
+
+
+def _f64_warp_grads(c, alpha=1.0, dtype=torch.float64):
+    """Autograd gradients of warp_f64 (float64: the exact value; float32: the
+    reference's own fp32 arithmetic, whose floor and comparison decisions match
+    the kernels' where a sample point sits within rounding of a texel edge)."""
+    names = ("positions", "scales", "rotations", "opacities", "colors", "motion")
+    leaves = [torch.from_numpy(np.ascontiguousarray(c[k])).to(dtype).requires_grad_(True) for k in names]
+    hw = tuple(int(v) for v in c["hw"])
+    outs = warp_f64(*leaves[:5], leaves[5] * alpha, hw, float(c["recon"]))
+    loss = sum((o * torch.from_numpy(c[f"g_{k}"]).to(dtype)).sum() for o, k in zip(outs, names[:5]))
+    loss.backward()
+    return {k: t.grad.numpy() for k, t in zip(names, leaves)}
+
+
+def test_warp_backward_matches_reference_autograd(cuda_device):
+    """Every input's gradient (positions, scales, rotations, opacities, colors,
+    motion) against the float64 restatement's autograd, with the reference's own
+    fp32 autograd gradients (golden) as the fp32 yardstick; the golden values
+    themselves agree with the float64 ones."""
+    from conftest import assert_close_grad
+
+    data = load_golden("warp_grad_cases.npz")
+    for name in data["names"]:
+        c = golden_case(data, str(name))
+        got = _gpu_warp_grads(c, cuda_device)
+        exact = _f64_warp_grads(c)
+        for k, v in got.items():
+            assert_close_grad(v, exact[k], what=f"{name} d_{k}", ref32=[c[f"d_{k}"]])
+            assert_close_grad(c[f"d_{k}"], exact[k], what=f"{name} golden d_{k}", ref32=[c[f"d_{k}"]])
+        assert np.abs(got["motion"]).sum() > 0
+
+
+def test_warp_gradient_flow_from_positions_to_motion(cuda_device):
+    """tests/sr/v6/test_canvas_warp.py:94-101 on the GPU: positions.sum()
+    backward reaches motion_lr with finite, non-zero gradients -- the same
+    gradients the reference computes (golden case "flow")."""
+    from oss_b200 import CanvasState, warp_canvas
+
+    c = golden_case(load_golden("warp_grad_cases.npz"), "flow")
+    canvas = CanvasState(*(torch.from_numpy(np.ascontiguousarray(c[k])).to(cuda_device)
+                           for k in ("positions", "scales", "rotations", "opacities", "colors")), count=3)
+    motion = torch.zeros(1, 2, 32, 32, device=cuda_device, requires_grad=True)
+    out = warp_canvas(canvas, motion, output_hw=(64, 64))
+    out.positions.sum().backward()
+    assert motion.grad is not None
+    assert torch.isfinite(motion.grad).all()
+    assert float(motion.grad.abs().sum()) > 0.0
+    assert_close(motion.grad.cpu().numpy(), c["d_motion"], what="d_motion")
+
+
+def test_warp_backward_alpha_and_size(cuda_device):
+    """alpha-scaled motion and a 2x upsampling at a larger size (20k Gaussians,
+    LR 135x240 -> 270x480) against the float64 restatement, and the motion
+    gradient's linearity in alpha."""
+    from conftest import assert_close_grad
+
+    rng = np.random.default_rng(31)
+    n, lr, hr = 20_000, (135, 240), (270, 480)
+    c = {"positions": (rng.random((n, 2)) * np.array([hr[1] + 8, hr[0] + 8]) - 4).astype(np.float32),
+         "scales": np.exp(rng.standard_normal((n, 2)) * 0.4 + math.log(1.5)).astype(np.float32),
+         "rotations": (rng.random(n) * math.pi).astype(np.float32),
+         "opacities": rng.random(n).astype(np.float32), "colors": rng.random((n, 3)).astype(np.float32),
+         "motion": smooth_motion(lr[0], lr[1], 77, max_mag=6.0)[None], "hw": np.array(hr), "recon": 0.5}
+    alpha = 0.5
+    with torch.no_grad():
+        from oss_b200 import CanvasState, warp_canvas
+
+        k = warp_canvas(CanvasState(*(torch.from_numpy(c[key]).to(cuda_device) for key in
+                                      ("positions", "scales", "rotations", "opacities", "colors")), count=n),
+                        torch.from_numpy(c["motion"]).to(cuda_device), hr, 0.5, alpha=alpha).count
+    c["out_count"] = k
+    for key, shape in (("positions", (k, 2)), ("scales", (k, 2)), ("rotations", (k,)), ("opacities", (k,)),
+                       ("colors", (k, 3))):
+        c[f"g_{key}"] = rng.standard_normal(shape).astype(np.float32)
+    got = _gpu_warp_grads(c, cuda_device, alpha=alpha)
+    exact = _f64_warp_grads(c, alpha=alpha)
+    fp32 = _f64_warp_grads(c, alpha=alpha, dtype=torch.float32)
+    for key, v in got.items():
+        assert_close_grad(v, exact[key], what=f"d_{key}", ref32=[fp32[key]])
+
+
+def test_warp_positions_refuses_grad_inputs(cuda_device):
+    """warp_positions stays forward-only: inputs that require grad under grad
+    mode raise instead of silently cutting the graph."""
+    from oss_b200 import warp_positions
+
+    xy = torch.rand(4, 2, device=cuda_device, requires_grad=True)
     with pytest.raises(RuntimeError, match="forward-only"):
-        warp_canvas(canvas, torch.zeros(1, 2, 8, 8, device=cuda_device), (16, 16))
+        warp_positions(xy, torch.zeros(2, 16, 16, device=cuda_device), (16, 16))
