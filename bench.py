@@ -1033,6 +1033,19 @@ def run_config4(args, rank, world):
                      "strong", clocks, ms_per_frame=ms / max(1, len(frames)))
 
 
+def capture_graph(body):
+    """CUDA graph of body() (warmed up once on a side stream first)."""
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        body()
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(graph):
+        body()
+    return graph
+
+
 def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
     """Config 5: 64 frames at 1080p split across ranks; each frame renders its own 200k
     canvas plus a shared 50k canvas (fwd+bwd); the shared canvas's per-Gaussian
@@ -1060,22 +1073,32 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
     ar_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     sl = slice(n_own, n_own + n_shared)
 
-    # size the pair capacity over every frame (host reads of the totals), then capture one
-    # sync-free CUDA graph per frame (the last without its per-Gaussian reduce)
+    # size the pair capacity over every frame (host reads of the totals), then capture the
+    # rank's frames as one sync-free CUDA graph: every frame's step and the accumulation of
+    # its shared-canvas gradients, the last frame reducing its shared Gaussians first; the
+    # last frame's own-canvas reduce is a second graph that runs beside the all-reduce
     for d in per_frame:
         pipe.step(d, sync=True, timed=False)
     torch.cuda.synchronize()
-    graphs = [pipe.capture(d, reduce=(i + 1 < len(per_frame))) for i, d in enumerate(per_frame)]
+
+    def frames_body():
+        d_shared.zero_()
+        for i, d in enumerate(per_frame):
+            last = i + 1 == len(per_frame)
+            pipe.step(d, timed=False, reduce=not last)
+            if last:
+                pipe.reduce_range(d, n_own, n_own + n_shared)
+            d_shared.add_(pack_shared_grads(pipe.grads, sl))
+
+    def own_body():
+        if per_frame:
+            pipe.reduce_range(per_frame[-1], 0, n_own)
+
+    graphs = [capture_graph(frames_body), capture_graph(own_body)]
 
     def step():
         main = torch.cuda.current_stream()
-        d_shared.zero_()
-        for i, g in enumerate(graphs):
-            g.replay()
-            if i + 1 == len(graphs):
-                last = per_frame[i]
-                pipe.reduce_range(last, n_own, n_own + n_shared)
-            d_shared.add_(pack_shared_grads(pipe.grads, sl))
+        graphs[0].replay()
         ev_ready.record(main)
         with torch.cuda.stream(comm):
             comm.wait_event(ev_ready)
@@ -1083,8 +1106,7 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
             reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
             ar_events[1].record(comm)
             ev_done.record(comm)
-        if graphs:
-            pipe.reduce_range(per_frame[-1], 0, n_own)  # the last frame's own canvas, beside the all-reduce
+        graphs[1].replay()  # the last frame's own canvas, beside the all-reduce
         main.wait_event(ev_done)
 
     ms, clocks = timed(step, steps, warmup, device, world)
