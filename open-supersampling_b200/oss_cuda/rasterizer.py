@@ -34,7 +34,7 @@ from importlib import import_module
 import torch
 from torch.autograd import Function
 
-from . import _feather, _raster
+from . import _feather, _raster, ops
 
 try:
     from . import _C
@@ -217,6 +217,10 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
     if blend == "sum":
         if depth is not None or background is not None:
             raise ValueError("depth and background apply to blend='alpha' only")
+        if torch.compiler.is_compiling():
+            # traced by torch.compile: the dispatcher-visible operator (oss_cuda.ops)
+            return ops.rasterize_sum(xy, scale, rot, feat, opacity, h, w, mode,
+                                     -1 if pair_capacity is None else pair_capacity)
         return _RasterizeGaussians.apply(xy, scale, rot, feat, opacity, h, w, tile_size, bool(topk_norm), mode,
                                          pair_capacity)
     if blend != "alpha":
