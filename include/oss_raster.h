@@ -428,6 +428,29 @@ OSS_API int oss_warp_canvas_backward(int64_t n, int64_t f, int64_t h_lr, int64_t
                                      void* stream);
 
 /* ---------------------------------------------------------------------------
+ * V6 front end: replaces the gathers and sanitisation of V6Rasterizer.forward
+ * (oss/sr/v6/rasterizer.py:56-157, _sanitize_active_gaussians :244-291,
+ * _token_features :319-327) without host reads.  For the n live Gaussians:
+ * kept = active_mask (uint8, null: all) and finite position / scale / rotation
+ * / used features and the 3 max|scale| disc overlapping the frame.  A kept
+ * Gaussian is written sanitised (|scale| clamped to [1e-3, max(h, w)], position
+ * clamped to [0, w - 1e-4] x [0, h - 1e-4], rotation wrapped by atan2(sin, cos),
+ * features padded or truncated to f_out, then a ones channel when
+ * ones_channel); a dropped one is parked outside the frame with zero features,
+ * so it bins into no tile.  flags (uint16 [n]) keep what the backward needs:
+ * oss_v6_sanitize_backward maps the render's input gradients (d_feat has
+ * f_out + ones columns; any input may be null for zero) to the canvas tensors
+ * with PyTorch's derivative conventions at clamp bounds and ties. */
+OSS_API int oss_v6_sanitize(int64_t n, int64_t h, int64_t w, int64_t f_in, int64_t f_out, int32_t ones_channel,
+                            const uint8_t* active_mask, const float* positions, const float* scales,
+                            const float* rotations, const float* colors, float* out_xy, float* out_scale,
+                            float* out_rot, float* out_feat, uint16_t* flags, void* stream);
+OSS_API int oss_v6_sanitize_backward(int64_t n, int64_t f_in, int64_t f_out, int32_t ones_channel,
+                                     const uint16_t* flags, const float* d_xy, const float* d_scale,
+                                     const float* d_rot, const float* d_feat, float* d_positions, float* d_scales,
+                                     float* d_rotations, float* d_colors, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Position-only warp: replaces oss/gaussian/canvas/warp.py:28-91
  * (warp_positions); motion[2][h][w] at the output resolution, times alpha
  * (warp_canvas(canvas, motion, alpha), :94-137).  in_frame is uint8 [n].

@@ -696,6 +696,49 @@ int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h,
     return OSS_OK;
 }
 
+int oss_v6_sanitize(int64_t n, int64_t h, int64_t w, int64_t f_in, int64_t f_out, int32_t ones_channel,
+                    const uint8_t* active_mask, const float* positions, const float* scales, const float* rotations,
+                    const float* colors, float* out_xy, float* out_scale, float* out_rot, float* out_feat,
+                    uint16_t* flags, void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N must be in [0, 2^31)");
+    OSS_CHECK(h > 0 && w > 0 && h <= INT_MAX && w <= INT_MAX, OSS_ERR_INVALID, "output_hw must be positive");
+    OSS_CHECK(f_in >= 0 && f_out > 0 && f_out + (ones_channel ? 1 : 0) <= OSS_MAX_CHANNELS, OSS_ERR_INVALID,
+              "feature widths out of range");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(positions != nullptr && scales != nullptr && rotations != nullptr && (f_in == 0 || colors != nullptr),
+              OSS_ERR_INVALID, "canvas inputs must be non-null");
+    OSS_CHECK(out_xy != nullptr && out_scale != nullptr && out_rot != nullptr && out_feat != nullptr &&
+                  flags != nullptr,
+              OSS_ERR_INVALID, "outputs must be non-null");
+    OSS_CHECK(aligned(positions, 8) && aligned(scales, 8) && aligned(out_xy, 8) && aligned(out_scale, 8),
+              OSS_ERR_INVALID, "positions and scales must be 8-byte aligned");
+    OSS_CUDA_TRY(oss::launch_v6_sanitize(static_cast<int>(n), static_cast<int>(h), static_cast<int>(w),
+                                         static_cast<int>(f_in), static_cast<int>(f_out), ones_channel ? 1 : 0,
+                                         active_mask, positions, scales, rotations, colors, out_xy, out_scale,
+                                         out_rot, out_feat, flags, as_stream(stream)));
+    return OSS_OK;
+}
+
+int oss_v6_sanitize_backward(int64_t n, int64_t f_in, int64_t f_out, int32_t ones_channel, const uint16_t* flags,
+                             const float* d_xy, const float* d_scale, const float* d_rot, const float* d_feat,
+                             float* d_positions, float* d_scales, float* d_rotations, float* d_colors,
+                             void* stream) {
+    OSS_CHECK(n >= 0 && n <= INT_MAX, OSS_ERR_RANGE, "N must be in [0, 2^31)");
+    OSS_CHECK(f_in >= 0 && f_out > 0 && f_out + (ones_channel ? 1 : 0) <= OSS_MAX_CHANNELS, OSS_ERR_INVALID,
+              "feature widths out of range");
+    if (n == 0) return OSS_OK;
+    OSS_CHECK(flags != nullptr && d_positions != nullptr && d_scales != nullptr && d_rotations != nullptr &&
+                  (f_in == 0 || d_colors != nullptr),
+              OSS_ERR_INVALID, "flags and gradient outputs must be non-null");
+    OSS_CHECK(aligned(d_positions, 8) && aligned(d_scales, 8) && (d_xy == nullptr || aligned(d_xy, 8)) &&
+                  (d_scale == nullptr || aligned(d_scale, 8)),
+              OSS_ERR_INVALID, "position and scale gradients must be 8-byte aligned");
+    OSS_CUDA_TRY(oss::launch_v6_sanitize_backward(static_cast<int>(n), static_cast<int>(f_in), static_cast<int>(f_out),
+                                                  ones_channel ? 1 : 0, flags, d_xy, d_scale, d_rot, d_feat,
+                                                  d_positions, d_scales, d_rotations, d_colors, as_stream(stream)));
+    return OSS_OK;
+}
+
 int64_t oss_warp_canvas_backward_scratch_bytes(int64_t h, int64_t w) {
     return oss::warp_backward_scratch_bytes(h < 0 ? 0 : h, w < 0 ? 0 : w);
 }

@@ -225,6 +225,19 @@ cudaError_t launch_prepare_feathered(int n, int h, int w, int mode, int overlap,
                                      float* geo, int32_t* vaabb, int32_t* vcount, float* vprec, int32_t* vwin,
                                      long long* block_sums, int32_t* tile_count, cudaStream_t stream);
 
+// ---- v6_front.cu -------------------------------------------------------------
+// V6 front-end sanitisation in place (kept Gaussians sanitised, dropped ones
+// parked outside the frame with zero features) and its backward through the
+// per-Gaussian derivative flags.
+cudaError_t launch_v6_sanitize(int n, int h, int w, int f_in, int f_out, int ones, const uint8_t* mask,
+                               const float* pos, const float* scl, const float* rot, const float* colors,
+                               float* out_xy, float* out_scale, float* out_rot, float* out_feat, uint16_t* flags,
+                               cudaStream_t stream);
+cudaError_t launch_v6_sanitize_backward(int n, int f_in, int f_out, int ones, const uint16_t* flags,
+                                        const float* d_xy, const float* d_scale, const float* d_rot,
+                                        const float* d_feat, float* d_pos, float* d_scl, float* d_rot_in,
+                                        float* d_colors, cudaStream_t stream);
+
 // ---- raster_fwd.cu / raster_bwd.cu ----------------------------------------
 // Entry records (forward -> backward): floats per record for f channels.
 int entry_record_floats(int f);

@@ -5,8 +5,9 @@ constructor arguments, ``forward(canvas, active_mask, output_hw,
 return_weight_sum)`` contract, sanitisation rules, weight-sum channel, the
 4-phase feathered overlap render and the batch expand.  Every render goes
 through ``oss_cuda.rasterize_gaussians`` (liboss_b200.so), the feathered
-overlap in one pass; the masking and sanitising are elementwise PyTorch glue
-around it.
+overlap in one pass; the masking, sanitising and ones channel are one kernel
+(oss_v6_sanitize) that keeps every live Gaussian's slot, so no survivor count
+is read on the host.
 
 ``spawn_offset`` shifts all means by a per-frame integer
 offset before rendering, the effect of the spawner offset of
@@ -18,8 +19,10 @@ from typing import Tuple
 
 import torch
 import torch.nn as nn
+from torch.autograd import Function
 
-from oss_cuda import rasterize_gaussians
+from oss_cuda import _lib, rasterize_gaussians
+from oss_cuda._raster import stream_of
 from oss_cuda.overlap import cosine_ramp, phase_feather_mask, render_overlapped_with  # noqa: F401
 
 TILE_SIZE = 16
@@ -41,6 +44,51 @@ def render_overlapped(xy, scale, rot, feat, h, w, overlap, binning=None, opacity
     with the scale floor of the reference's oss_cuda backend."""
     return rasterize_gaussians(xy, scale.clamp_min(_MIN_PIXEL_SCALE), rot, feat, h, w, TILE_SIZE, True,
                                binning=binning, opacity=opacity, overlap=overlap)
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return t.to(dtype=torch.float32).contiguous()
+
+
+class _V6Sanitize(Function):
+    """oss_v6_sanitize and its backward: the live canvas tensors -> the render's
+    inputs (xy, scale, rot, feat with the optional ones channel), dropped
+    Gaussians parked outside the frame."""
+
+    @staticmethod
+    def forward(ctx, pos, scl, rot, colors, mask, h, w, f_out, ones):
+        n, f_in = int(pos.shape[0]), int(colors.shape[1])
+        dev = pos.device
+        f32 = dict(device=dev, dtype=torch.float32)
+        xy, scale, r = torch.empty((n, 2), **f32), torch.empty((n, 2), **f32), torch.empty((n,), **f32)
+        feat = torch.empty((n, f_out + (1 if ones else 0)), **f32)
+        flags = torch.empty((n,), device=dev, dtype=torch.int16)
+        lib = _lib.lib()
+        with torch.cuda.device(dev):
+            _lib.check(lib.oss_v6_sanitize(n, h, w, f_in, f_out, 1 if ones else 0, mask.data_ptr(), pos.data_ptr(),
+                                           scl.data_ptr(), rot.data_ptr(), colors.data_ptr() if f_in else None,
+                                           xy.data_ptr(), scale.data_ptr(), r.data_ptr(), feat.data_ptr(),
+                                           flags.data_ptr(), stream_of(pos)), "oss_v6_sanitize")
+        ctx.save_for_backward(flags)
+        ctx.meta = (n, f_in, f_out, ones)
+        return xy, scale, r, feat
+
+    @staticmethod
+    def backward(ctx, d_xy, d_scale, d_rot, d_feat):
+        (flags,) = ctx.saved_tensors
+        n, f_in, f_out, ones = ctx.meta
+        dev = flags.device
+        f32 = dict(device=dev, dtype=torch.float32)
+        outs = [torch.empty((n, 2), **f32), torch.empty((n, 2), **f32), torch.empty((n,), **f32),
+                torch.empty((n, f_in), **f32)]
+        ins = [None if t is None else t.contiguous().float() for t in (d_xy, d_scale, d_rot, d_feat)]
+        lib = _lib.lib()
+        with torch.cuda.device(dev):
+            _lib.check(lib.oss_v6_sanitize_backward(n, f_in, f_out, 1 if ones else 0, flags.data_ptr(),
+                                                    *(None if t is None else t.data_ptr() for t in ins),
+                                                    *(t.data_ptr() if t.numel() else None for t in outs),
+                                                    stream_of(flags)), "oss_v6_sanitize_backward")
+        return (*outs, None, None, None, None, None)
 
 
 class V6Rasterizer(nn.Module):
@@ -85,54 +133,29 @@ class V6Rasterizer(nn.Module):
             return feats
 
         n_live = max(0, min(int(canvas.count), int(canvas.positions.shape[0])))
-        if n_live == 0 or not bool(mask[:n_live].any().item()):
+        if n_live == 0:
             return zeros()
-        live = mask[:n_live].to(device=device, dtype=torch.bool)
-        colors = self._token_features(canvas.colors[:n_live])
+        colors = canvas.colors[:n_live]
+        if colors.ndim != 2:
+            raise ValueError(f"canvas.colors must be (N, F); got {tuple(colors.shape)}")
         feat_dtype = colors.dtype
-        pos = canvas.positions[:n_live][live].to(torch.float32)
-        scl = canvas.scales[:n_live][live].to(torch.float32)
-        rot = canvas.rotations[:n_live][live].to(torch.float32)
-        feat = colors[live].to(torch.float32)
-        pos, scl, rot, feat = self._sanitize(pos, scl, rot, feat, (h, w))
-        if pos.shape[0] == 0:
-            return zeros()
+        # the sanitisation and the ones channel on the device: every live Gaussian keeps
+        # its slot (a dropped one bins into no tile), so no count is read on the host
+        pos, scl, rot, feat = _V6Sanitize.apply(
+            _f32(canvas.positions[:n_live]), _f32(canvas.scales[:n_live]), _f32(canvas.rotations[:n_live]),
+            _f32(colors), mask[:n_live].to(device=device, dtype=torch.bool).contiguous(), h, w, self.feature_dim,
+            bool(return_weight_sum))
         if spawn_offset is not None:
             pos = pos + spawn_offset.to(device=device, dtype=torch.float32).view(1, 2)
-        if return_weight_sum:
-            feat = torch.cat([feat, torch.ones((feat.shape[0], 1), device=device, dtype=feat.dtype)], dim=-1)
         if self.overlap > 0:
-            img = render_overlapped(pos.contiguous(), scl.contiguous(), rot.contiguous(), feat.contiguous(), h, w,
-                                    self.overlap, self.binning)
+            img = render_overlapped(pos, scl, rot, feat, h, w, self.overlap, self.binning)
         else:
-            img = render(pos.contiguous(), scl.contiguous(), rot.contiguous(), feat.contiguous(), h, w,
-                         self.binning)
+            img = render(pos, scl, rot, feat, h, w, self.binning)
         img = img.to(dtype=feat_dtype)
         feats = img[: self.feature_dim].unsqueeze(0).expand(batch, -1, -1, -1)
         if return_weight_sum:
             return feats, img[self.feature_dim: self.feature_dim + 1].unsqueeze(0).expand(batch, -1, -1, -1)
         return feats
-
-    @staticmethod
-    def _sanitize(pos, scl, rot, feat, hw):
-        """Drop non-finite entries and those whose 3*max|scale| disc misses the frame;
-        clamp |scale| to [1e-3, max(h, w)], positions into the frame, wrap rotations
-        (rasterizer.py:244-291)."""
-        h, w = hw
-        finite = (torch.isfinite(pos).all(-1) & torch.isfinite(scl).all(-1) & torch.isfinite(rot)
-                  & torch.isfinite(feat).all(-1))
-        scl = scl.abs().clamp(min=_MIN_PIXEL_SCALE, max=float(max(h, w)))
-        r = 3.0 * scl.amax(dim=-1)
-        inside = ((pos[:, 0] + r >= 0.0) & (pos[:, 0] - r < float(w)) & (pos[:, 1] + r >= 0.0)
-                  & (pos[:, 1] - r < float(h)))
-        keep = finite & inside
-        if not bool(keep.any().item()):
-            return pos[:0], scl[:0], rot[:0], feat[:0]
-        pos, scl, rot, feat = pos[keep], scl[keep], rot[keep], feat[keep]
-        hi = pos.new_tensor([max(float(w) - 1.0e-4, 0.0), max(float(h) - 1.0e-4, 0.0)])
-        pos = torch.minimum(pos.clamp_min(0.0), hi)
-        rot = torch.atan2(torch.sin(rot), torch.cos(rot))
-        return pos, scl, rot, feat
 
     @staticmethod
     def _normalize_active_mask(canvas, active_mask: torch.Tensor):

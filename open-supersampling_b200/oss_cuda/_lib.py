@@ -78,6 +78,9 @@ SIGNATURES = {
         [_i64, _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
          _p, _i64, _p],
     ),
+    "oss_v6_sanitize": (ctypes.c_int, [_i64, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                       _p]),
+    "oss_v6_sanitize_backward": (ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_warp_canvas_backward_scratch_bytes": (_i64, [_i64, _i64]),
     "oss_warp_canvas_backward": (
         ctypes.c_int,
