@@ -537,14 +537,27 @@ def reference_cuda_op(inp, h, w, iters=2):
         return float(statistics.median(out))
 
     fwd_ms = med_ms(lambda: ref.rasterize_forward(xy, scale, rot, feat, h, w, 16, True))
+    out = {"public_fwd_ms": fwd_ms, "public_fwd_mpix_s": h * w / (fwd_ms * 1e-3) / 1e6}
+    tiles = ((h + 15) // 16) * ((w + 15) // 16)
+    if xy.shape[0] * tiles <= 40_000_000:
+        # the public autograd step as oss_cuda/rasterizer.py:28-66 runs it: forward, backward on the
+        # forward's full-frame lists, conic -> (scale, rot) chain rule.  Skipped at sizes where the
+        # full-frame backward's per-pixel atomics take tens of seconds.
+        def public_step():
+            _, g, off, conic = ref.rasterize_forward(xy, scale, rot, feat, h, w, 16, True)
+            _, d_conic, _ = ref.rasterize_backward(xy, scale, rot, feat, conic, g, off, grad, h, w, 16)
+            ref.conic_to_scale_rot_grad(scale, rot, d_conic)
+
+        step_ms = med_ms(public_step)
+        out.update(public_fwdbwd_ms=step_ms, public_fwdbwd_mpix_s=h * w / (step_ms * 1e-3) / 1e6)
     g_t, off_t, conic_t, tot_t = ref.pair_construction_only(xy, scale, rot, h, w, 16)
     bin_ms = med_ms(lambda: ref.pair_construction_only(xy, scale, rot, h, w, 16))
     bwd_ms = med_ms(lambda: ref.rasterize_backward(xy, scale, rot, feat, conic_t, g_t, off_t, grad, h, w, 16))
-    return {"public_fwd_ms": fwd_ms, "public_fwd_mpix_s": h * w / (fwd_ms * 1e-3) / 1e6,
-            "tight_binning_ms": bin_ms, "tight_bwd_ms": bwd_ms, "tight_pairs": int(tot_t),
+    return {**out, "tight_binning_ms": bin_ms, "tight_bwd_ms": bwd_ms, "tight_pairs": int(tot_t),
             "what": "oss/cuda/src/{bindings.cpp,rasterizer_fwd.cu,rasterizer_bwd.cu,tile_bin_counting_sort.cu} "
                     "compiled unmodified for sm_100a; public_fwd = _C.rasterize_forward (full-frame lists, "
-                    "bf16-split wmma); tight_bwd = _C.rasterize_backward on pair_construction_only's 3-sigma "
+                    "bf16-split wmma); public_fwdbwd = forward + backward on its full-frame lists + "
+                    "conic_to_scale_rot_grad (small configs only); tight_bwd = _C.rasterize_backward on pair_construction_only's 3-sigma "
                     "lists (per-pixel float atomics); inputs resident, L2 flushed, median of "
                     f"{iters} after a warm-up"}
 
