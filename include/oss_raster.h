@@ -32,6 +32,11 @@
  *                        per Gaussian
  *   OSS_BIN_FULL         every Gaussian in every tile (the reference forward's
  *                        build_full_tile_pairs, rasterizer_fwd.cu:135-149)
+ *   OSS_BIN_EXACT56      tile AABB of the q = 56 ellipse: a contribution left
+ *                        out has weight exp(-q/2) < e^-28 = 6.9e-13, so the image
+ *                        is the full-tail sum to within 6.9e-13 * sum |feat| of
+ *                        the Gaussians left out at a pixel (2.2x the 3-sigma
+ *                        lists at the BASELINE shapes, against 6.3x for q = 176)
  */
 #ifndef OSS_RASTER_H
 #define OSS_RASTER_H
@@ -59,7 +64,8 @@ enum oss_status {
 enum oss_bin_mode {
     OSS_BIN_TIGHT3SIGMA = 0,
     OSS_BIN_EXACT = 1,
-    OSS_BIN_FULL = 2
+    OSS_BIN_FULL = 2,
+    OSS_BIN_EXACT56 = 3
 };
 
 #define OSS_TILE 16
@@ -136,6 +142,28 @@ OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
  * order every tile list by sort_key[g] (a permutation of [0, n)) instead of
  * gid; key_order[k] = the gid with key k.  oss_depth_order makes them for the
  * alpha-blend mode (rank and order of the Gaussians by depth). */
+
+/* ---------------------------------------------------------------------------
+ * oss_render_prepare + oss_bin_pairs in one call for a caller that already
+ * knows a capacity (no host synchronisation): the same outputs (conic, aabb,
+ * pair_offset[n+1], geo, prec, total_pairs, tile_offsets, gid_sorted,
+ * overflow, with the same overflow rule), in three launches instead of five.
+ * The preprocess's last CTA scans the tile counts and the per-warp pair sums;
+ * the scatter writes the pair offsets and sorts each tile list in the warp
+ * whose write completes it.  Replaces the reference's preprocess + pair
+ * construction + sort + searchsorted (rasterizer_fwd.cu:381-476).  mode
+ * OSS_BIN_TIGHT3SIGMA, OSS_BIN_EXACT or OSS_BIN_EXACT56; full-frame lists go through
+ * oss_render_prepare + oss_bin_pairs.  tile_count[oss_tile_count_elems(T)] is
+ * working memory (zeroed by the call).
+ * ------------------------------------------------------------------------- */
+OSS_API int64_t oss_render_bin_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles);
+OSS_API int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode,
+                   const float* xy, const float* scale, const float* rot,
+                   int64_t f, const float* feat, const float* opacity,
+                   float* conic, int32_t* aabb, int32_t* pair_offset, float* geo, float* prec,
+                   int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets,
+                   int64_t capacity, int32_t* gid_sorted, int32_t* overflow,
+                   void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Host-side read of the pair total without a copy engine: a one-thread kernel
  * on `stream` stores *total_pairs (device) into host_total, which must be

@@ -58,8 +58,9 @@ int check_grid(int64_t n, int64_t h, int64_t w, Grid& g) {
 }
 
 int check_mode(int32_t mode) {
-    OSS_CHECK(mode == OSS_BIN_TIGHT3SIGMA || mode == OSS_BIN_EXACT || mode == OSS_BIN_FULL, OSS_ERR_INVALID,
-              "binning mode must be 0 (tight3sigma), 1 (exact) or 2 (full)");
+    OSS_CHECK(mode == OSS_BIN_TIGHT3SIGMA || mode == OSS_BIN_EXACT || mode == OSS_BIN_FULL ||
+                  mode == OSS_BIN_EXACT56,
+              OSS_ERR_INVALID, "binning mode must be 0 (tight3sigma), 1 (exact), 2 (full) or 3 (exact56)");
     return OSS_OK;
 }
 
@@ -78,7 +79,7 @@ extern "C" {
 
 const char* oss_last_error(void) { return g_last_error.c_str(); }
 
-int oss_abi_version(void) { return 8; }
+int oss_abi_version(void) { return 9; }
 
 int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t mode, const float* xy,
                    const float* scale, const float* rot, float* conic, int32_t* aabb, int32_t* pair_count,
@@ -100,7 +101,7 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
 int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_fused_scratch_bytes(n < 0 ? 0 : n); }
 
 int64_t oss_tile_count_elems(int64_t num_tiles) {
-    return (num_tiles < 0 ? 0 : num_tiles) * oss::kTileCountStride;
+    return ((num_tiles < 0 ? 0 : num_tiles) + 1) * oss::kTileCountStride;
 }
 
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
@@ -143,8 +144,7 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
 
 int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
     (void)n;
-    (void)num_tiles;
-    return oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity);
+    return oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity, num_tiles < 0 ? 0 : num_tiles);
 }
 
 int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, int32_t* pair_offset,
@@ -181,8 +181,71 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
     OSS_CHECK((sort_key == nullptr) == (key_order == nullptr), OSS_ERR_INVALID,
               "sort_key and key_order go together");
     OSS_CHECK(mode != OSS_BIN_FULL || sort_key == nullptr, OSS_ERR_INVALID, "full-frame lists take no sort key");
-    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
-                                       sort_key, key_order, gid_sorted, tile_offsets, overflow, scratch, s));
+    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, nullptr, tile_count, total_pairs,
+                                       capacity, sort_key, key_order, gid_sorted, tile_offsets, overflow, scratch, s));
+    return OSS_OK;
+}
+
+int64_t oss_render_bin_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
+    n = n < 0 ? 0 : n;
+    return oss::arena_bytes(oss::preprocess_fused_warps(n), sizeof(long long)) +
+           oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity, num_tiles < 0 ? 0 : num_tiles);
+}
+
+int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
+                   const float* rot, int64_t f, const float* feat, const float* opacity, float* conic, int32_t* aabb,
+                   int32_t* pair_offset, float* geo, float* prec, int64_t* total_pairs, int32_t* tile_count,
+                   int32_t* tile_offsets, int64_t capacity, int32_t* gid_sorted, int32_t* overflow, void* scratch,
+                   int64_t scratch_bytes, void* stream) {
+    Grid g;
+    int rc = check_grid(n, h, w, g);
+    if (rc != OSS_OK) return rc;
+    if ((rc = check_mode(mode)) != OSS_OK) return rc;
+    OSS_CHECK(mode != OSS_BIN_FULL, OSS_ERR_INVALID,
+              "render_bin builds culled lists; use render_prepare + bin_pairs for full-frame lists");
+    if ((rc = check_gaussian_inputs(g.n, xy, scale, rot)) != OSS_OK) return rc;
+    OSS_CHECK(capacity >= 0, OSS_ERR_INVALID, "capacity must be non-negative");
+    OSS_CHECK(capacity <= INT_MAX, OSS_ERR_RANGE, "capacity exceeds int32 range");
+    OSS_CHECK(pair_offset != nullptr && total_pairs != nullptr && tile_count != nullptr && tile_offsets != nullptr &&
+                  overflow != nullptr,
+              OSS_ERR_INVALID, "pair_offset, total_pairs, tile_count, tile_offsets and overflow must be non-null");
+    OSS_CHECK(capacity == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
+    OSS_CHECK(scratch_bytes >= oss_render_bin_scratch_bytes(n, capacity, g.tiles), OSS_ERR_SCRATCH,
+              "render_bin scratch too small");
+    if (g.n > 0) {
+        OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
+        OSS_CHECK(aligned(aabb, 16) && aligned(geo, 16), OSS_ERR_INVALID, "aabb and geo must be 16-byte aligned");
+        OSS_CHECK(prec == nullptr || (aligned(prec, 16) && f >= 0 && f <= OSS_MAX_CHANNELS &&
+                                      (f == 0 || feat != nullptr)),
+                  OSS_ERR_INVALID, "prec (16-byte aligned) needs F in [0, 64] and feat");
+        OSS_CHECK(scratch != nullptr && aligned(scratch, 8), OSS_ERR_INVALID, "scratch must be 8-byte aligned");
+    }
+    cudaStream_t s = as_stream(stream);
+    if (g.n == 0 || g.tiles == 0) {
+        // no pairs: empty lists, zero offsets and total
+        OSS_CUDA_TRY(cudaMemsetAsync(pair_offset, 0, sizeof(int32_t) * (g.n + 1), s));
+        OSS_CUDA_TRY(cudaMemsetAsync(total_pairs, 0, sizeof(int64_t), s));
+        if (g.n > 0) {
+            OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset,
+                                                geo, nullptr, nullptr, static_cast<int>(prec != nullptr ? f : 0), feat,
+                                                opacity, prec, s));
+            OSS_CUDA_TRY(cudaMemsetAsync(pair_offset, 0, sizeof(int32_t) * (g.n + 1), s));
+        }
+        OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, nullptr, tile_count, total_pairs,
+                                           capacity, nullptr, nullptr, gid_sorted, tile_offsets, overflow, scratch,
+                                           s));
+        return OSS_OK;
+    }
+    oss::Arena arena{static_cast<char*>(scratch), scratch_bytes, 0};
+    long long* warp_sums = arena.take<long long>(oss::preprocess_fused_warps(g.n));
+    void* list_scratch = arena.base + arena.used;
+    OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
+    OSS_CUDA_TRY(oss::launch_preprocess_fused(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
+                                              tile_count, tile_offsets, warp_sums, total_pairs,
+                                              static_cast<int>(prec != nullptr ? f : 0), feat, opacity, prec, s));
+    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, warp_sums, tile_count, total_pairs,
+                                       capacity, nullptr, nullptr, gid_sorted, tile_offsets, overflow, list_scratch,
+                                       s));
     return OSS_OK;
 }
 

@@ -48,6 +48,7 @@ cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t 
 
 // Per-tile pair counters are spaced one 128-byte line apart: the preprocess and
 // scatter atomics then spread over num_tiles lines instead of num_tiles / 32.
+// One more line after the tiles' holds the binning's global counters.
 constexpr int kTileCountStride = 32;
 
 // ---- radix.cu --------------------------------------------------------------
@@ -64,6 +65,17 @@ cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy
                               const float* rot, float* conic, int32_t* aabb, int32_t* count,
                               float* geo, long long* block_sums, int32_t* tile_count, int f, const float* feat,
                               const float* opacity, float* prec, cudaStream_t stream);
+// The preprocess of the one-call binning: as launch_preprocess, plus each
+// warp's pair-count sum into warp_sums; the last CTA to finish scans the tile
+// counts into tile_offsets[0..num_tiles] and the warp sums in place into each
+// warp's gid-major pair base, and writes the total to *total_pairs and
+// pair_offset[n].  tile_count (with its extra line) must be zero on entry.
+int64_t preprocess_fused_warps(int64_t n);
+cudaError_t launch_preprocess_fused(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
+                                    const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
+                                    int32_t* tile_count, int32_t* tile_offsets, long long* warp_sums,
+                                    int64_t* total_pairs, int f, const float* feat, const float* opacity,
+                                    float* prec, cudaStream_t stream);
 cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
 cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
                                            const float* d_conic, float* d_scale, float* d_rot,
@@ -85,11 +97,14 @@ cudaError_t launch_copy_i64(const int64_t* src, int64_t* dst, cudaStream_t strea
 // range is emptied and *overflow = 1.
 // With sort_key (a permutation of [0, n)) the lists are ordered by key and
 // mapped back to gids through key_order (key -> gid).
-int64_t tile_lists_scratch_bytes(int64_t capacity);
+// With warp_base (the per-warp pair bases of launch_preprocess_fused) the
+// scatter also writes pair_offset[0..n); without it pair_offset is read only.
+int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles);
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
-                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
-                             const int32_t* sort_key, const int32_t* key_order, int32_t* gid_sorted,
-                             int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream);
+                             const long long* warp_base, int32_t* tile_count, const int64_t* total_pairs,
+                             int64_t capacity, const int32_t* sort_key, const int32_t* key_order,
+                             int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,
+                             cudaStream_t stream);
 // Stable order of the Gaussians by depth (ties by gid): order[i] = gid of rank i,
 // rank[gid] = its position.
 int64_t depth_order_scratch_bytes(int64_t n);

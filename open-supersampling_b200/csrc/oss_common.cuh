@@ -19,10 +19,28 @@ constexpr float kTauTight = 9.0f;        // rasterizer_fwd.cu:92
 // 1.2e-38 per Gaussian.  176 keeps a 0.8% margin over fp32 rounding of q and of
 // the AABB radius.
 constexpr float kTauExact = 176.0f;
+// Cutoff of the exact56 lists: every weight left out is below e^-28 = 6.9e-13.
+constexpr float kTauExact56 = 56.0f;
 // -0.5*log2(e): folds exp(-q/2) = 2^(q * -0.5 log2 e) into the conic.
 constexpr float kNegHalfLog2e = -0.72134752044448170368f;
 
 __host__ __device__ inline int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Asynchronous global -> shared copies (cp.async): they hold no registers while
+// in flight.  cp_async4_zfill copies 4 bytes, or writes 0 when !valid (the
+// source is then not read).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async4_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    const int bytes = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(gmem_src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // Saturating float -> int conversion with NaN -> 0 (the semantics of
 // cvt.rzi.s32.f32, which the reference's static_cast<int> compiles to).
@@ -199,11 +217,13 @@ __device__ __forceinline__ void conic_grad_to_scale_rot_f64(float raw_sx, float 
 }
 
 // Per-mode AABB parameters.
-__host__ __device__ inline float mode_tau(int mode) { return mode == OSS_BIN_EXACT ? kTauExact : kTauTight; }
+__host__ __device__ inline float mode_tau(int mode) {
+    return mode == OSS_BIN_EXACT ? kTauExact : (mode == OSS_BIN_EXACT56 ? kTauExact56 : kTauTight);
+}
 // Fallback radius factor for degenerate conics: 3*max(s) for the 3-sigma lists
 // (rasterizer_fwd.cu:96), sqrt(tau)*max(s) for the exact lists.
 __host__ __device__ inline float mode_fallback(int mode) {
-    return mode == OSS_BIN_EXACT ? 13.266499161421599f : 3.0f;
+    return mode == OSS_BIN_EXACT ? 13.266499161421599f : (mode == OSS_BIN_EXACT56 ? 7.483314773547883f : 3.0f);
 }
 
 }  // namespace oss

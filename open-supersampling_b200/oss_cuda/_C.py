@@ -33,7 +33,8 @@ def rasterize_forward(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True, 
 
     Reference: rasterizer_fwd.cu:478-590.  ``topk_norm`` is accepted and
     ignored, as in the reference (:488).  ``binning`` selects the tile lists:
-    "exact" (default, equal to the reference's full-tail image), "full" (the
+    "exact56" (default: the reference's full-tail image to within 6.9e-13 per
+    unit of feature left out), "exact" (every nonzero fp32 weight), "full" (the
     reference's literal full-frame lists) or "tight3sigma".
     """
     del topk_norm

@@ -16,7 +16,12 @@ OSS_OK = 0
 OSS_BIN_TIGHT3SIGMA = 0
 OSS_BIN_EXACT = 1
 OSS_BIN_FULL = 2
-BINNING_MODES = {"tight3sigma": OSS_BIN_TIGHT3SIGMA, "exact": OSS_BIN_EXACT, "full": OSS_BIN_FULL}
+OSS_BIN_EXACT56 = 3
+BINNING_MODES = {"tight3sigma": OSS_BIN_TIGHT3SIGMA, "exact": OSS_BIN_EXACT, "full": OSS_BIN_FULL,
+                 "exact56": OSS_BIN_EXACT56}
+# the binning of the reference-signature call: its image is the reference's full-tail sum to within
+# 6.9e-13 per unit of feature left out (every weight left out is below e^-28)
+DEFAULT_BINNING = "exact56"
 TILE = 16
 MAX_CHANNELS = 64
 
@@ -37,6 +42,11 @@ SIGNATURES = {
     "oss_bin_pairs_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_bin_pairs": (
         ctypes.c_int, [_i64, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p]),
+    "oss_render_bin_scratch_bytes": (_i64, [_i64, _i64, _i64]),
+    "oss_render_bin": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i32, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _i64,
+         _p]),
     "oss_publish_total": (ctypes.c_int, [_p, _p, _p]),
     "oss_depth_order_scratch_bytes": (_i64, [_i64]),
     "oss_depth_order": (ctypes.c_int, [_i64, _p, _p, _p, _p, _i64, _p]),

@@ -7,7 +7,8 @@ per-pair reduction (no atomics) over the forward's own binning, fused with
 the d_conic -> (d_scale, d_rot) chain rule.
 
 Keyword-only additions (defaults keep the reference call's results):
-  binning     "exact" (default) | "tight3sigma" | "full"
+  binning     "exact56" (default: q <= 56 lists, weights left out < 6.9e-13) |
+              "exact" (q <= 176: every nonzero fp32 weight) | "tight3sigma" | "full"
   opacity     (N,) tensor folded into feat as feat * opacity[:, None], with its
               gradient returned (the fold gaussian_temporal/rasterizer.py:47 does
               in PyTorch)
@@ -213,6 +214,8 @@ def rasterize_gaussians(xy, scale, rot, feat, h, w, tile_size=16, topk_norm=True
             raise ValueError("weight='analytic' applies to blend='sum' without pair_capacity")
         if int(feat.size(1)) > 32:
             raise ValueError("weight='analytic' renders at most 32 channels per call")
+        # the logistic tails of the analytic weight outlast exp(-q/2): its default lists are q <= 176
+        mode = _raster.binning_mode(binning, default="exact")
         return _RasterizeGaussiansAnalytic.apply(xy, scale, rot, feat, opacity, h, w, mode)
     if blend == "sum":
         if depth is not None or background is not None:

@@ -19,8 +19,8 @@ ORACLE_DIR = Path(__file__).resolve().parent
 SRC = ORACLE_DIR / "oss_oracle.c"
 LIB = ORACLE_DIR / "liboss_oracle.so"
 
-TIGHT, EXACT, FULL = 0, 1, 2
-MODES = {"tight3sigma": TIGHT, "exact": EXACT, "full": FULL}
+TIGHT, EXACT, FULL, EXACT56 = 0, 1, 2, 3
+MODES = {"tight3sigma": TIGHT, "exact": EXACT, "full": FULL, "exact56": EXACT56}
 TILE = 16
 
 CFLAGS = ["-O2", "-std=c11", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off", "-fno-fast-math", "-msse2",

@@ -27,8 +27,9 @@
 #define ORC_MIN_SCALE 1.0e-6f
 #define ORC_TAU_TIGHT 9.0f
 #define ORC_TAU_EXACT 176.0f
+#define ORC_TAU_EXACT56 56.0f
 
-enum { ORC_TIGHT = 0, ORC_EXACT = 1, ORC_FULL = 2 };
+enum { ORC_TIGHT = 0, ORC_EXACT = 1, ORC_FULL = 2, ORC_EXACT56 = 3 };
 
 static float clamp_min_keep_nan(float v, float lo) { return v < lo ? lo : v; }
 
@@ -61,6 +62,7 @@ static void conic_of(float raw_sx, float raw_sy, float angle, float* a, float* b
  * preprocess_gaussians, rasterizer_fwd.cu:38-109.  mode ORC_TIGHT uses tau = 9
  * and the 3*max(scale) fallback (the reference); ORC_EXACT uses tau = 176
  * (exp(-q/2) below the smallest normal fp32 outside) and sqrt(176)*max(scale);
+ * ORC_EXACT56 tau = 56 (weights left out below e^-28) and sqrt(56)*max(scale);
  * ORC_FULL
  * writes the full-frame rectangle for every Gaussian.
  */
@@ -68,8 +70,8 @@ void orc_preprocess(int64_t n, int h, int w, int mode, const float* xy, const fl
                     float* conic, int32_t* aabb, int32_t* count) {
     const int ntx = num_tiles_1d(w);
     const int nty = num_tiles_1d(h);
-    const float tau = mode == ORC_EXACT ? ORC_TAU_EXACT : ORC_TAU_TIGHT;
-    const float fb = mode == ORC_EXACT ? 13.266499161421599f : 3.0f;
+    const float tau = mode == ORC_EXACT ? ORC_TAU_EXACT : (mode == ORC_EXACT56 ? ORC_TAU_EXACT56 : ORC_TAU_TIGHT);
+    const float fb = mode == ORC_EXACT ? 13.266499161421599f : (mode == ORC_EXACT56 ? 7.483314773547883f : 3.0f);
 #pragma omp parallel for schedule(static)
     for (int64_t g = 0; g < n; ++g) {
         float a, b, d;

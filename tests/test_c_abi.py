@@ -44,7 +44,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_abi_version_and_clean_error_state():
     lib = _lib.lib()
-    assert lib.oss_abi_version() == 8
+    assert lib.oss_abi_version() == 9
 
 
 def test_rejects_tile_size_other_than_16():
@@ -107,6 +107,26 @@ def test_rejects_scratch_too_small():
     assert lib.oss_alpha_pair_grad_stride(3) == 12
 
 
+def test_render_bin_argument_checks():
+    """The one-call binning refuses bad arguments before touching the device."""
+    lib = _lib.lib()
+    need = lib.oss_render_bin_scratch_bytes(1000, 5000, 16)
+    assert need >= lib.oss_bin_pairs_scratch_bytes(1000, 5000, 16)
+
+    def call(mode=0, capacity=5000, scratch_bytes=need, tile_count=8):
+        return lib.oss_render_bin(1000, 64, 64, mode, 8, 8, 8, 0, None, None, 8, 16, 8, 16, None, 8, tile_count, 8,
+                                  capacity, 8, 8, 16, scratch_bytes, None)
+
+    assert call(scratch_bytes=need - 1) == 4 and "scratch" in lib.oss_last_error().decode()
+    assert call(mode=2) == 1 and "full-frame" in lib.oss_last_error().decode()
+    assert call(mode=7) == 1
+    assert call(capacity=-1) == 1
+    assert call(capacity=1 << 31) == 3 and "int32" in lib.oss_last_error().decode()
+    assert call(tile_count=None) == 1 and "tile_count" in lib.oss_last_error().decode()
+    # one more counter line than the tiles: the binning's global counters
+    assert lib.oss_tile_count_elems(100) == 101 * lib.oss_tile_count_elems(0)
+
+
 def test_scratch_sizes_are_monotone():
     lib = _lib.lib()
     a = lib.oss_bin_pairs_scratch_bytes(1000, 10_000, 500)
@@ -128,5 +148,7 @@ def test_python_checks_mirror_reference_messages():
         _raster.check_hw(32, 32, 8)
     with pytest.raises(ValueError):
         _raster.binning_mode("bogus")
-    assert _raster.binning_mode(None) == _lib.OSS_BIN_EXACT
+    assert _raster.binning_mode(None) == _lib.OSS_BIN_EXACT56
+    assert _raster.binning_mode(None, default="exact") == _lib.OSS_BIN_EXACT
+    assert _raster.binning_mode("exact56") == _lib.OSS_BIN_EXACT56
     assert _raster.binning_mode("tight3sigma") == _lib.OSS_BIN_TIGHT3SIGMA

@@ -17,7 +17,7 @@ from conftest import assert_close, assert_close_grad, golden_case, load_golden
 
 pytestmark = pytest.mark.gpu
 
-MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT, "full": orc.FULL}
+MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT, "full": orc.FULL, "exact56": orc.EXACT56}
 
 
 def dev(a, dtype=torch.float32):
@@ -127,7 +127,7 @@ def test_tile_bin_counting_sort_bit_exact(cuda_device, n, t):
 
 # ------------------------------------------------------------------ forward
 
-@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full"])
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full", "exact56"])
 @pytest.mark.parametrize("n,h,w,f", [(0, 32, 32, 3), (1, 32, 32, 1), (16, 64, 128, 3), (256, 256, 256, 12),
                                      (300, 37, 53, 64), (4096, 270, 480, 3)])
 def test_forward_matches_oracle(cuda_device, mode, n, h, w, f):
@@ -172,7 +172,7 @@ def test_forward_matches_reference_golden(cuda_device):
     for name in data["names"]:
         c = golden_case(data, str(name))
         h, w = (int(v) for v in c["hw"])
-        for binning in ("exact", "full"):
+        for binning in ("exact56", "exact", "full"):
             out = rasterize_gaussians(dev(c["xy"]), dev(c["scale"]), dev(c["rot"]), dev(c["feat"]), h, w,
                                       binning=binning)
             assert_close(host(out), c["image"], what=f"{name} {binning}")
@@ -193,7 +193,7 @@ def run_autograd(xy, scale, rot, feat, grad, h, w, binning, opacity=None):
     return host(out), grads
 
 
-@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full"])
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "full", "exact56"])
 @pytest.mark.parametrize("n,h,w,f", [(1, 16, 16, 1), (16, 32, 32, 3), (256, 64, 128, 3), (200, 37, 53, 12),
                                      (64, 48, 48, 64), (4096, 270, 480, 3)])
 def test_backward_matches_oracle(cuda_device, mode, n, h, w, f):
@@ -227,13 +227,17 @@ def test_backward_with_opacity_matches_oracle(cuda_device):
     check_grads({"d_xy": d_xy, "d_scale": d_scale, "d_rot": d_rot, "d_feat": d_rgb, "d_opacity": d_op}, ref)
 
 
-def test_backward_matches_reference_golden(cuda_device):
+@pytest.mark.parametrize("binning", ["exact", "exact56"])
+def test_backward_matches_reference_golden(cuda_device, binning):
+    """The reference's autograd of its full-tail sum, against the float64 value
+    over the q <= 176 lists (every nonzero fp32 weight): the exact56 lists leave
+    out only weights below e^-28 and meet the same bar."""
     data = load_golden("render_cases.npz")
     for name in data["names"]:
         c = golden_case(data, str(name))
         h, w = (int(v) for v in c["hw"])
         _, (d_xy, d_scale, d_rot, d_feat) = run_autograd(c["xy"], c["scale"], c["rot"], c["feat"], c["grad"], h, w,
-                                                         "exact")
+                                                         binning)
         # against the float64 sums; the reference's own fp32 autograd output (the
         # golden value) joins the fp32 yardstick
         conic, _, _, gid, offs = orc.lists(c["xy"], c["scale"], c["rot"], h, w, orc.EXACT)
@@ -300,6 +304,31 @@ def test_kernel_does_not_reenter_python(cuda_device):
 
 
 # ------------------------------------------------------------------ BASELINE config sizes
+
+def test_default_exact56_lists_match_full_tail(cuda_device):
+    """The reference-signature default (q <= 56 lists) against the full-tail
+    sum: config-1 shapes fwd+bwd against the float64 value over the q <= 176
+    lists, and the config-2 image against the oracle's q <= 176 render.  A
+    weight left out is below e^-28, so both meet the strict bars."""
+    from oss_cuda import rasterize_gaussians
+
+    h, w, n = 540, 960, 16384
+    xy, scale, rot, opacity, rgb = baseline_gaussians(n, h, w, seed=11, log_scale_mean=math.log(1.5))
+    grad = np.random.default_rng(11).standard_normal((3, h, w)).astype(np.float32)
+    img, (d_xy, d_scale, d_rot, d_rgb, d_op) = run_autograd(xy, scale, rot, rgb, grad, h, w, None, opacity=opacity)
+    conic, _, _, g176, o176 = orc.lists(xy, scale, rot, h, w, orc.EXACT)
+    g56 = orc.lists(xy, scale, rot, h, w, orc.EXACT56)[3]
+    assert g56.size < 0.6 * g176.size
+    assert_close(img, orc.render_forward(xy, conic, rgb, g176, o176, h, w, opacity), what="config1 image")
+    ref = orc.grads_with_fp32_evaluation(xy, scale, rot, conic, rgb, g176, o176, grad, h, w, opacity)
+    check_grads({"d_xy": d_xy, "d_scale": d_scale, "d_rot": d_rot, "d_feat": d_rgb, "d_opacity": d_op}, ref,
+                "config1 exact56 ")
+    h, w, n = 1080, 1920, 200_000
+    xy, scale, rot, opacity, rgb = baseline_gaussians(n, h, w, seed=12, log_scale_mean=math.log(2.0))
+    out = rasterize_gaussians(dev(xy), dev(scale), dev(rot), dev(rgb), h, w, opacity=dev(opacity))
+    conic, _, _, g176, o176 = orc.lists(xy, scale, rot, h, w, orc.EXACT)
+    assert_close(host(out), orc.render_forward(xy, conic, rgb, g176, o176, h, w, opacity), what="config2 image")
+
 
 def test_config1_full_size_parity(cuda_device):
     """Config 1: 540x960, N=16384, BASELINE distributions, 3-sigma lists."""

@@ -1,6 +1,8 @@
 """Tile lists by scatter + per-tile sort: bit-exact against the oracle's sorted
 (tile << 32 | gid) lists in every sort tier, the device-side capacity check,
-and the sync-free path captured in a CUDA graph.
+and the sync-free path captured in a CUDA graph.  Every list case runs through
+both the two-call path (oss_render_prepare + oss_bin_pairs) and the one-call
+path (oss_render_bin: last-CTA offset scans, lists sorted inside the scatter).
 """
 from __future__ import annotations
 
@@ -13,7 +15,7 @@ from conftest import assert_close
 
 pytestmark = pytest.mark.gpu
 
-MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT}
+MODES = {"tight3sigma": orc.TIGHT, "exact": orc.EXACT, "exact56": orc.EXACT56}
 
 
 def dev(a, dtype=torch.float32):
@@ -67,13 +69,28 @@ class Lists:
     def set_capacity(self, capacity):
         self.capacity = capacity
         self.gid = torch.full((max(1, capacity),), -7, device="cuda", dtype=torch.int32)
-        nb = self.lib.oss_bin_pairs_scratch_bytes(self.n, capacity, self.tiles)
+        nb = max(self.lib.oss_bin_pairs_scratch_bytes(self.n, capacity, self.tiles),
+                 self.lib.oss_render_bin_scratch_bytes(self.n, capacity, self.tiles))
         self.scratch = torch.empty((max(1, nb),), device="cuda", dtype=torch.uint8)
 
-    def run(self):
+    def run(self, fused=False):
         from oss_cuda import _lib
 
         s = torch.cuda.current_stream().cuda_stream
+        if fused:
+            # garbage in the outputs the one call must write
+            self.pair_offset.fill_(-3)
+            self.tile_offsets.fill_(-3)
+            self.tile_count.fill_(12345)
+            self.chk(self.lib.oss_render_bin(self.n, self.h, self.w, self.mode, self.xy.data_ptr(),
+                                             self.scale.data_ptr(), self.rot.data_ptr(), self.pf, _lib.ptr(self.pfeat),
+                                             _lib.ptr(self.popacity), self.conic.data_ptr(), self.aabb.data_ptr(),
+                                             self.pair_offset.data_ptr(), self.geo.data_ptr(), _lib.ptr(self.prec),
+                                             self.total.data_ptr(), self.tile_count.data_ptr(),
+                                             self.tile_offsets.data_ptr(), self.capacity, self.gid.data_ptr(),
+                                             self.overflow.data_ptr(), self.scratch.data_ptr(), self.scratch.numel(),
+                                             s), "render_bin")
+            return
         self.chk(self.lib.oss_render_prepare(self.n, self.h, self.w, self.mode, self.xy.data_ptr(),
                                              self.scale.data_ptr(), self.rot.data_ptr(), self.pf,
                                              _lib.ptr(self.pfeat), _lib.ptr(self.popacity), self.conic.data_ptr(),
@@ -89,14 +106,24 @@ class Lists:
 
 
 def check_lists(xy, scale, rot, h, w, mode, slack=0):
-    _, _, _, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, MODES[mode])
-    L = Lists(xy, scale, rot, h, w, MODES[mode])
-    L.set_capacity(int(g_ref.size) + slack)
-    L.run()
-    assert int(L.overflow.item()) == 0
-    assert int(L.total.item()) == g_ref.size
-    np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
-    np.testing.assert_array_equal(host(L.gid)[:g_ref.size], g_ref)
+    """Both paths: lists, offsets and total against the oracle; the one-call
+    path also gives the two-call path's pair offsets and per-Gaussian outputs."""
+    conic, aabb, count, g_ref, o_ref = orc.lists(xy, scale, rot, h, w, MODES[mode])
+    pair_ref = np.concatenate([[0], np.cumsum(count.astype(np.int64))]).astype(np.int32)
+    outs = []
+    for fused in (False, True):
+        L = Lists(xy, scale, rot, h, w, MODES[mode])
+        L.set_capacity(int(g_ref.size) + slack)
+        L.run(fused=fused)
+        what = "render_bin" if fused else "prepare + bin_pairs"
+        assert int(L.overflow.item()) == 0, what
+        assert int(L.total.item()) == g_ref.size, what
+        np.testing.assert_array_equal(host(L.tile_offsets), o_ref, err_msg=what)
+        np.testing.assert_array_equal(host(L.gid)[:g_ref.size], g_ref, err_msg=what)
+        np.testing.assert_array_equal(host(L.pair_offset), pair_ref, err_msg=what)
+        outs.append([host(t) for t in (L.conic, L.aabb, L.geo)])
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)
     return o_ref
 
 
@@ -115,7 +142,7 @@ def test_sort_tiers_bit_exact(cuda_device, n, h, w, scale, tier_len):
     assert np.diff(o_ref).max() == tier_len
 
 
-@pytest.mark.parametrize("mode", ["tight3sigma", "exact"])
+@pytest.mark.parametrize("mode", ["tight3sigma", "exact", "exact56"])
 def test_mixed_tiers_in_one_frame(cuda_device, mode):
     """Long lists (a dense cluster of large Gaussians) next to short ones in the
     same CTA's group of tiles."""
@@ -182,6 +209,19 @@ def test_capacity_overflow_empties_lists_and_gradients(cuda_device):
     # the same buffers with enough room: flag cleared, lists exact
     L.set_capacity(int(g_ref.size))
     L.run()
+    assert int(L.overflow.item()) == 0
+    np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
+    np.testing.assert_array_equal(host(L.gid), g_ref)
+    # the one-call path: the same overflow rule, then exact lists again
+    L.set_capacity(int(g_ref.size) - 1)
+    L.overflow.fill_(-1)
+    L.run(fused=True)
+    assert int(L.overflow.item()) == 1
+    assert int(L.total.item()) == g_ref.size
+    assert not host(L.tile_offsets).any()
+    assert not host(L.pair_offset).any()
+    L.set_capacity(int(g_ref.size))
+    L.run(fused=True)
     assert int(L.overflow.item()) == 0
     np.testing.assert_array_equal(host(L.tile_offsets), o_ref)
     np.testing.assert_array_equal(host(L.gid), g_ref)
@@ -275,9 +315,11 @@ def test_packed_records_and_derived_slots_bit_identical(cuda_device, f, dense):
     assert torch.equal(rows[0], rows[1])
 
 
-def test_sync_free_path_replays_in_cuda_graph(cuda_device):
-    """prepare -> bin -> forward captured once, replayed on new Gaussians copied
-    into the same input buffers: lists and image follow the new inputs."""
+@pytest.mark.parametrize("fused", [False, True])
+def test_sync_free_path_replays_in_cuda_graph(cuda_device, fused):
+    """prepare -> bin -> forward (or render_bin -> forward) captured once,
+    replayed on new Gaussians copied into the same input buffers: lists and
+    image follow the new inputs."""
     from oss_cuda import _lib
 
     h, w, n = 128, 192, 4000
@@ -296,7 +338,7 @@ def test_sync_free_path_replays_in_cuda_graph(cuda_device):
     L.set_capacity(4 * int(orc.lists(xy0, s0, r0, h, w, orc.TIGHT)[3].size))
 
     def step():
-        L.run()
+        L.run(fused=fused)
         _lib.check(L.lib.oss_render_forward(n, 3, h, w, L.geo.data_ptr(), feat.data_ptr(), None, None,
                                             L.gid.data_ptr(), L.tile_offsets.data_ptr(), img.data_ptr(), None, None,
                                             None, None, torch.cuda.current_stream().cuda_stream), "forward")
