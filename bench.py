@@ -210,7 +210,6 @@ class Pipeline:
             self.capacity = int(pairs * 1.1) + 1024
             self.gid_sorted = torch.empty((self.capacity,), device=dev, dtype=torch.int32)
             nb = max(self.lib.oss_bin_pairs_scratch_bytes(self.n, self.capacity, self.tiles),
-                     self.lib.oss_render_bin_scratch_bytes(self.n, self.capacity, self.tiles),
                      self.lib.oss_render_backward_scratch_bytes(self.capacity, 3, self.tiles))
             self.scratch = torch.empty((nb,), device=dev, dtype=torch.uint8)
             self.pg_bytes = ((self.capacity * self.lib.oss_pair_grad_stride(3) * 4 + 255) // 256) * 256
@@ -230,21 +229,6 @@ class Pipeline:
         n, h, w = int(d["xy"].shape[0]), self.h, self.w
         self.n_step = n
         self._mark(0, timed)
-        if not (sync or self.capacity == 0):
-            # capacity known: preprocess (packing the forward records x, y, A, B, D, rgb * opacity),
-            # offsets and sorted lists in one call; the stage marks put all of it under "prepare"
-            chk(lib.oss_render_bin(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
-                                   d["rot"].data_ptr(), 3, d["rgb"].data_ptr(), d["opacity"].data_ptr(),
-                                   self.conic.data_ptr(), self.aabb.data_ptr(), self.pair_offset.data_ptr(),
-                                   self.geo.data_ptr(), self.prec.data_ptr(), self.total.data_ptr(),
-                                   self.tile_count.data_ptr(), self.tile_offsets.data_ptr(), self.capacity,
-                                   self.gid_sorted.data_ptr(), self.overflow.data_ptr(), self.scratch.data_ptr(),
-                                   self.scratch.numel(), s), "render_bin")
-            self._mark(1, timed)
-            self._mark(2, timed)
-            self._mark(3, timed)
-            self._after_bin(d, n, backward, timed, reduce)
-            return
         # the preprocess also packs the forward records (x, y, A, B, D, rgb * opacity)
         chk(lib.oss_render_prepare(n, h, w, self.mode, d["xy"].data_ptr(), d["scale"].data_ptr(),
                                    d["rot"].data_ptr(), 3, d["rgb"].data_ptr(), d["opacity"].data_ptr(),
@@ -339,8 +323,8 @@ class Pipeline:
 
     def launches_per_step(self, backward=True):
         """Kernels of liboss_b200.so launched by one step (see csrc/)."""
-        prepare = 1                                   # k_preprocess<fused> (its last CTA scans the offsets)
-        binning = 2                                   # k_scatter_sort, k_sort_big
+        prepare = 2                                   # k_preprocess, k_prepare_scan (pair + tile offsets)
+        binning = 2                                   # k_scatter_pairs, k_sort_tiles
         bwd = 4                                       # k_item_block_sums, k_item_table (beside the forward), k_render_bwd, k_reduce_gaussian
         return prepare + binning + 1 + (bwd if backward else 0)
 

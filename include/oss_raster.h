@@ -147,18 +147,26 @@ OSS_API int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode,
  * oss_render_prepare + oss_bin_pairs in one call for a caller that already
  * knows a capacity (no host synchronisation): the same outputs (conic, aabb,
  * pair_offset[n+1], geo, prec, total_pairs, tile_offsets, gid_sorted,
- * overflow, with the same overflow rule), in three launches instead of five.
- * The preprocess's last CTA scans the tile counts and the per-warp pair sums;
- * the scatter writes the pair offsets and sorts each tile list in the warp
- * whose write completes it.  Replaces the reference's preprocess + pair
- * construction + sort + searchsorted (rasterizer_fwd.cu:381-476).  mode
+ * overflow, with the same overflow rule) from the same launches.  Replaces the
+ * reference's preprocess + pair construction + sort + searchsorted
+ * (rasterizer_fwd.cu:381-476).  mode
  * OSS_BIN_TIGHT3SIGMA, OSS_BIN_EXACT or OSS_BIN_EXACT56; full-frame lists go through
  * oss_render_prepare + oss_bin_pairs.  tile_count[oss_tile_count_elems(T)] is
  * working memory (zeroed by the call).
+ *
+ * frames > 1 bins a batch: Gaussians [frame_offsets[b], frame_offsets[b+1]) of
+ * the concatenated inputs (frame_offsets: frames + 1 non-decreasing int32 on
+ * the device, 0 to n) are drawn into frame b, every frame h x w.  The tile
+ * grid is the frames stacked: T = frames * ceil(h/16) * ceil(w/16) tiles, tile
+ * rows [b ceil(h/16), (b+1) ceil(h/16)) are frame b's, and aabb rows are in
+ * that stacked grid.  Each frame's lists are those a call on its Gaussians
+ * alone would build, with gids offset by frame_offsets[b].  The *_frames
+ * forward and backward entries render such lists into [frames][f][h][w]
+ * images.  frames == 1 takes frame_offsets NULL.
  * ------------------------------------------------------------------------- */
 OSS_API int64_t oss_render_bin_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles);
-OSS_API int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode,
-                   const float* xy, const float* scale, const float* rot,
+OSS_API int oss_render_bin(int64_t n, int64_t h, int64_t w, int64_t frames, const int32_t* frame_offsets,
+                   int32_t mode, const float* xy, const float* scale, const float* rot,
                    int64_t f, const float* feat, const float* opacity,
                    float* conic, int32_t* aabb, int32_t* pair_offset, float* geo, float* prec,
                    int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets,
@@ -202,6 +210,13 @@ OSS_API int oss_depth_order(int64_t n, const float* depth, int32_t* order, int32
  * ------------------------------------------------------------------------- */
 OSS_API int oss_entry_record_floats(int64_t f);
 OSS_API int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w,
+                       const float* geo, const float* feat, const float* opacity, const float* prec,
+                       const int32_t* gid_sorted, const int32_t* tile_offsets,
+                       float* image, const int32_t* aabb, const int32_t* pair_offset,
+                       float* records, int32_t* slots, void* stream);
+/* The same over the lists of oss_render_bin with frames > 1: image is
+ * [frames][f][h][w]. */
+OSS_API int oss_render_forward_frames(int64_t n, int64_t f, int64_t h, int64_t w, int64_t frames,
                        const float* geo, const float* feat, const float* opacity, const float* prec,
                        const int32_t* gid_sorted, const int32_t* tile_offsets,
                        float* image, const int32_t* aabb, const int32_t* pair_offset,
@@ -257,6 +272,19 @@ OSS_API int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w
  * cleared, so a table serves any number of backward launches, one at a time. */
 OSS_API int oss_backward_items(int64_t h, int64_t w, int64_t total_pairs, const int32_t* tile_offsets,
                        void* items, int64_t items_bytes, void* stream);
+/* Stacked frames (oss_render_bin with frames > 1): the item table over all
+ * frames' tiles (items_bytes >= oss_render_backward_pairs_scratch_bytes(
+ * total_pairs, frames * tiles of one frame)), and the backward reading
+ * grad_image as [frames][f][h][w]. */
+OSS_API int oss_backward_items_frames(int64_t h, int64_t w, int64_t frames, int64_t total_pairs,
+                       const int32_t* tile_offsets, void* items, int64_t items_bytes, void* stream);
+OSS_API int oss_render_backward_items_frames(int64_t n, int64_t f, int64_t h, int64_t w, int64_t frames,
+                              const float* geo, const float* feat, const float* opacity,
+                              const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,
+                              const int32_t* gid_sorted, const int32_t* tile_offsets,
+                              const float* records, const int32_t* slots,
+                              const float* grad_image, float* pairgrad,
+                              void* items, int64_t items_bytes, void* stream);
 OSS_API int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w,
                               const float* geo, const float* feat, const float* opacity,
                               const int32_t* aabb, const int32_t* pair_offset, int64_t total_pairs,

@@ -57,6 +57,14 @@ int check_grid(int64_t n, int64_t h, int64_t w, Grid& g) {
     return OSS_OK;
 }
 
+// frames >= 1 stacked frames of g's tile grid, the stacked tile count within int32.
+int check_frames(int64_t frames, const Grid& g) {
+    OSS_CHECK(frames >= 1, OSS_ERR_INVALID, "frames must be positive");
+    OSS_CHECK(frames <= INT_MAX && static_cast<int64_t>(g.tiles) * frames <= INT_MAX, OSS_ERR_RANGE,
+              "number of tiles of all frames exceeds int32 range");
+    return OSS_OK;
+}
+
 int check_mode(int32_t mode) {
     OSS_CHECK(mode == OSS_BIN_TIGHT3SIGMA || mode == OSS_BIN_EXACT || mode == OSS_BIN_FULL ||
                   mode == OSS_BIN_EXACT56,
@@ -101,7 +109,7 @@ int oss_preprocess(int64_t n, int64_t h, int64_t w, int64_t tile_size, int32_t m
 int64_t oss_render_prepare_scratch_bytes(int64_t n) { return oss::scan_fused_scratch_bytes(n < 0 ? 0 : n); }
 
 int64_t oss_tile_count_elems(int64_t num_tiles) {
-    return ((num_tiles < 0 ? 0 : num_tiles) + 1) * oss::kTileCountStride;
+    return (num_tiles < 0 ? 0 : num_tiles) * oss::kTileCountStride;
 }
 
 int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
@@ -144,7 +152,8 @@ int oss_render_prepare(int64_t n, int64_t h, int64_t w, int32_t mode, const floa
 
 int64_t oss_bin_pairs_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
     (void)n;
-    return oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity, num_tiles < 0 ? 0 : num_tiles);
+    (void)num_tiles;
+    return oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity);
 }
 
 int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* aabb, int32_t* pair_offset,
@@ -181,25 +190,27 @@ int oss_bin_pairs(int64_t n, int64_t h, int64_t w, int32_t mode, const int32_t* 
     OSS_CHECK((sort_key == nullptr) == (key_order == nullptr), OSS_ERR_INVALID,
               "sort_key and key_order go together");
     OSS_CHECK(mode != OSS_BIN_FULL || sort_key == nullptr, OSS_ERR_INVALID, "full-frame lists take no sort key");
-    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, nullptr, tile_count, total_pairs,
-                                       capacity, sort_key, key_order, gid_sorted, tile_offsets, overflow, scratch, s));
+    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
+                                       sort_key, key_order, gid_sorted, tile_offsets, overflow, scratch, s));
     return OSS_OK;
 }
 
 int64_t oss_render_bin_scratch_bytes(int64_t n, int64_t capacity, int64_t num_tiles) {
-    n = n < 0 ? 0 : n;
-    return oss::arena_bytes(oss::preprocess_fused_warps(n), sizeof(long long)) +
-           oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity, num_tiles < 0 ? 0 : num_tiles);
+    (void)num_tiles;
+    return oss::scan_fused_scratch_bytes(n < 0 ? 0 : n) + oss::tile_lists_scratch_bytes(capacity < 0 ? 0 : capacity);
 }
 
-int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode, const float* xy, const float* scale,
-                   const float* rot, int64_t f, const float* feat, const float* opacity, float* conic, int32_t* aabb,
-                   int32_t* pair_offset, float* geo, float* prec, int64_t* total_pairs, int32_t* tile_count,
-                   int32_t* tile_offsets, int64_t capacity, int32_t* gid_sorted, int32_t* overflow, void* scratch,
-                   int64_t scratch_bytes, void* stream) {
+int oss_render_bin(int64_t n, int64_t h, int64_t w, int64_t frames, const int32_t* frame_offsets, int32_t mode,
+                   const float* xy, const float* scale, const float* rot, int64_t f, const float* feat,
+                   const float* opacity, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo, float* prec,
+                   int64_t* total_pairs, int32_t* tile_count, int32_t* tile_offsets, int64_t capacity,
+                   int32_t* gid_sorted, int32_t* overflow, void* scratch, int64_t scratch_bytes, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
+    if ((rc = check_frames(frames, g)) != OSS_OK) return rc;
+    OSS_CHECK(frames == 1 || frame_offsets != nullptr, OSS_ERR_INVALID, "frame_offsets must be non-null");
+    const int tiles = g.tiles * static_cast<int>(frames);
     if ((rc = check_mode(mode)) != OSS_OK) return rc;
     OSS_CHECK(mode != OSS_BIN_FULL, OSS_ERR_INVALID,
               "render_bin builds culled lists; use render_prepare + bin_pairs for full-frame lists");
@@ -210,7 +221,7 @@ int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode, const float* x
                   overflow != nullptr,
               OSS_ERR_INVALID, "pair_offset, total_pairs, tile_count, tile_offsets and overflow must be non-null");
     OSS_CHECK(capacity == 0 || gid_sorted != nullptr, OSS_ERR_INVALID, "gid_sorted must be non-null");
-    OSS_CHECK(scratch_bytes >= oss_render_bin_scratch_bytes(n, capacity, g.tiles), OSS_ERR_SCRATCH,
+    OSS_CHECK(scratch_bytes >= oss_render_bin_scratch_bytes(n, capacity, tiles), OSS_ERR_SCRATCH,
               "render_bin scratch too small");
     if (g.n > 0) {
         OSS_CHECK(conic != nullptr && aabb != nullptr && geo != nullptr, OSS_ERR_INVALID, "outputs must be non-null");
@@ -221,31 +232,19 @@ int oss_render_bin(int64_t n, int64_t h, int64_t w, int32_t mode, const float* x
         OSS_CHECK(scratch != nullptr && aligned(scratch, 8), OSS_ERR_INVALID, "scratch must be 8-byte aligned");
     }
     cudaStream_t s = as_stream(stream);
-    if (g.n == 0 || g.tiles == 0) {
-        // no pairs: empty lists, zero offsets and total
-        OSS_CUDA_TRY(cudaMemsetAsync(pair_offset, 0, sizeof(int32_t) * (g.n + 1), s));
-        OSS_CUDA_TRY(cudaMemsetAsync(total_pairs, 0, sizeof(int64_t), s));
-        if (g.n > 0) {
-            OSS_CUDA_TRY(oss::launch_preprocess(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset,
-                                                geo, nullptr, nullptr, static_cast<int>(prec != nullptr ? f : 0), feat,
-                                                opacity, prec, s));
-            OSS_CUDA_TRY(cudaMemsetAsync(pair_offset, 0, sizeof(int32_t) * (g.n + 1), s));
-        }
-        OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, nullptr, tile_count, total_pairs,
-                                           capacity, nullptr, nullptr, gid_sorted, tile_offsets, overflow, scratch,
-                                           s));
-        return OSS_OK;
-    }
     oss::Arena arena{static_cast<char*>(scratch), scratch_bytes, 0};
-    long long* warp_sums = arena.take<long long>(oss::preprocess_fused_warps(g.n));
+    long long* block_sums = arena.take<long long>(oss::scan_fused_scratch_bytes(g.n) / sizeof(long long));
     void* list_scratch = arena.base + arena.used;
-    OSS_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(int32_t) * oss_tile_count_elems(g.tiles), s));
-    OSS_CUDA_TRY(oss::launch_preprocess_fused(g.n, g.ntx, g.nty, mode, xy, scale, rot, conic, aabb, pair_offset, geo,
-                                              tile_count, tile_offsets, warp_sums, total_pairs,
-                                              static_cast<int>(prec != nullptr ? f : 0), feat, opacity, prec, s));
-    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, g.tiles, aabb, pair_offset, warp_sums, tile_count, total_pairs,
-                                       capacity, nullptr, nullptr, gid_sorted, tile_offsets, overflow, list_scratch,
-                                       s));
+    int32_t* counts = tiles > 0 ? tile_count : nullptr;
+    if (counts != nullptr) OSS_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * oss_tile_count_elems(tiles), s));
+    OSS_CUDA_TRY(oss::launch_preprocess_frames(g.n, g.ntx, g.nty, static_cast<int>(frames), frame_offsets, mode, xy,
+                                               scale, rot, conic, aabb, pair_offset, geo, block_sums, counts,
+                                               static_cast<int>(prec != nullptr ? f : 0), feat, opacity, prec, s));
+    OSS_CUDA_TRY(oss::scan_apply_with_block_sums(pair_offset, pair_offset, g.n, block_sums, total_pairs, counts,
+                                                 oss::kTileCountStride, tiles, counts != nullptr ? tile_offsets : nullptr,
+                                                 s));
+    OSS_CUDA_TRY(oss::build_tile_lists(g.n, g.ntx, tiles, aabb, pair_offset, tile_count, total_pairs, capacity,
+                                       nullptr, nullptr, gid_sorted, tile_offsets, overflow, list_scratch, s));
     return OSS_OK;
 }
 
@@ -347,9 +346,18 @@ int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* 
                        const float* opacity, const float* prec, const int32_t* gid_sorted,
                        const int32_t* tile_offsets, float* image, const int32_t* aabb, const int32_t* pair_offset,
                        float* records, int32_t* slots, void* stream) {
+    return oss_render_forward_frames(n, f, h, w, 1, geo, feat, opacity, prec, gid_sorted, tile_offsets, image, aabb,
+                                     pair_offset, records, slots, stream);
+}
+
+int oss_render_forward_frames(int64_t n, int64_t f, int64_t h, int64_t w, int64_t frames, const float* geo,
+                              const float* feat, const float* opacity, const float* prec, const int32_t* gid_sorted,
+                              const int32_t* tile_offsets, float* image, const int32_t* aabb,
+                              const int32_t* pair_offset, float* records, int32_t* slots, void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
+    if ((rc = check_frames(frames, g)) != OSS_OK) return rc;
     OSS_CHECK(f >= 0, OSS_ERR_INVALID, "F must be non-negative");
     OSS_CHECK(f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be <= 64");
     if (g.tiles == 0 || f == 0) return OSS_OK;
@@ -363,7 +371,7 @@ int oss_render_forward(int64_t n, int64_t f, int64_t h, int64_t w, const float* 
               "slots need aabb (16-byte aligned) and pair_offset");
     OSS_CUDA_TRY(oss::launch_render_forward(static_cast<int>(f), g.h, g.w, geo, feat, opacity, gid_sorted,
                                             tile_offsets, image, aabb, pair_offset, records, slots, prec,
-                                            as_stream(stream)));
+                                            as_stream(stream), static_cast<int>(frames)));
     return OSS_OK;
 }
 
@@ -446,16 +454,24 @@ int oss_render_backward_pairs(int64_t n, int64_t f, int64_t h, int64_t w, const 
 
 int oss_backward_items(int64_t h, int64_t w, int64_t total_pairs, const int32_t* tile_offsets, void* items,
                        int64_t items_bytes, void* stream) {
+    return oss_backward_items_frames(h, w, 1, total_pairs, tile_offsets, items, items_bytes, stream);
+}
+
+int oss_backward_items_frames(int64_t h, int64_t w, int64_t frames, int64_t total_pairs, const int32_t* tile_offsets,
+                              void* items, int64_t items_bytes, void* stream) {
     Grid g;
     int rc = check_grid(0, h, w, g);
     if (rc != OSS_OK) return rc;
+    if ((rc = check_frames(frames, g)) != OSS_OK) return rc;
+    const int64_t tiles = static_cast<int64_t>(g.tiles) * frames;
     OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
-    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, tiles), OSS_ERR_SCRATCH,
               "backward item table too small");
-    if (total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    if (total_pairs == 0 || tiles == 0) return OSS_OK;
     OSS_CHECK(tile_offsets != nullptr && items != nullptr && aligned(items, 16), OSS_ERR_INVALID,
               "tile_offsets and items (16-byte aligned) must be non-null");
-    OSS_CUDA_TRY(oss::launch_backward_items(g.h, g.w, total_pairs, tile_offsets, items, as_stream(stream)));
+    OSS_CUDA_TRY(oss::launch_backward_items(g.h, g.w, total_pairs, tile_offsets, items, as_stream(stream),
+                                            static_cast<int>(frames)));
     return OSS_OK;
 }
 
@@ -464,14 +480,27 @@ int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w, const 
                               int64_t total_pairs, const int32_t* gid_sorted, const int32_t* tile_offsets,
                               const float* records, const int32_t* slots, const float* grad_image, float* pairgrad,
                               void* items, int64_t items_bytes, void* stream) {
+    return oss_render_backward_items_frames(n, f, h, w, 1, geo, feat, opacity, aabb, pair_offset, total_pairs,
+                                            gid_sorted, tile_offsets, records, slots, grad_image, pairgrad, items,
+                                            items_bytes, stream);
+}
+
+int oss_render_backward_items_frames(int64_t n, int64_t f, int64_t h, int64_t w, int64_t frames, const float* geo,
+                                     const float* feat, const float* opacity, const int32_t* aabb,
+                                     const int32_t* pair_offset, int64_t total_pairs, const int32_t* gid_sorted,
+                                     const int32_t* tile_offsets, const float* records, const int32_t* slots,
+                                     const float* grad_image, float* pairgrad, void* items, int64_t items_bytes,
+                                     void* stream) {
     Grid g;
     int rc = check_grid(n, h, w, g);
     if (rc != OSS_OK) return rc;
+    if ((rc = check_frames(frames, g)) != OSS_OK) return rc;
+    const int64_t tiles = static_cast<int64_t>(g.tiles) * frames;
     OSS_CHECK(f >= 0 && f <= OSS_MAX_CHANNELS, OSS_ERR_INVALID, "F must be in [0, 64]");
     OSS_CHECK(total_pairs >= 0 && total_pairs <= INT_MAX, OSS_ERR_RANGE, "total pair count exceeds int32 range");
-    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, g.tiles), OSS_ERR_SCRATCH,
+    OSS_CHECK(items_bytes >= oss_render_backward_pairs_scratch_bytes(total_pairs, tiles), OSS_ERR_SCRATCH,
               "backward item table too small");
-    if (g.n == 0 || total_pairs == 0 || g.tiles == 0) return OSS_OK;
+    if (g.n == 0 || total_pairs == 0 || tiles == 0) return OSS_OK;
     OSS_CHECK(geo != nullptr && aligned(geo, 16) && aabb != nullptr && aligned(aabb, 16) && pair_offset != nullptr,
               OSS_ERR_INVALID, "geo, aabb (16-byte aligned) and pair_offset must be non-null");
     OSS_CHECK(f == 0 || feat != nullptr, OSS_ERR_INVALID, "feat must be non-null");
@@ -484,7 +513,7 @@ int oss_render_backward_items(int64_t n, int64_t f, int64_t h, int64_t w, const 
     OSS_CUDA_TRY(oss::launch_render_backward_items(static_cast<int>(f), g.h, g.w, total_pairs, geo, feat, opacity,
                                                    gid_sorted, tile_offsets, grad_image, aabb, pair_offset, records,
                                                    slots, pairgrad, oss_pair_grad_stride(f), nullptr, nullptr, nullptr,
-                                                   items, as_stream(stream)));
+                                                   items, as_stream(stream), static_cast<int>(frames)));
     return OSS_OK;
 }
 

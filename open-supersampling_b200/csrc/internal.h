@@ -48,7 +48,6 @@ cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t 
 
 // Per-tile pair counters are spaced one 128-byte line apart: the preprocess and
 // scatter atomics then spread over num_tiles lines instead of num_tiles / 32.
-// One more line after the tiles' holds the binning's global counters.
 constexpr int kTileCountStride = 32;
 
 // ---- radix.cu --------------------------------------------------------------
@@ -65,17 +64,14 @@ cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy
                               const float* rot, float* conic, int32_t* aabb, int32_t* count,
                               float* geo, long long* block_sums, int32_t* tile_count, int f, const float* feat,
                               const float* opacity, float* prec, cudaStream_t stream);
-// The preprocess of the one-call binning: as launch_preprocess, plus each
-// warp's pair-count sum into warp_sums; the last CTA to finish scans the tile
-// counts into tile_offsets[0..num_tiles] and the warp sums in place into each
-// warp's gid-major pair base, and writes the total to *total_pairs and
-// pair_offset[n].  tile_count (with its extra line) must be zero on entry.
-int64_t preprocess_fused_warps(int64_t n);
-cudaError_t launch_preprocess_fused(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
-                                    const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                                    int32_t* tile_count, int32_t* tile_offsets, long long* warp_sums,
-                                    int64_t* total_pairs, int f, const float* feat, const float* opacity,
-                                    float* prec, cudaStream_t stream);
+// frames > 1: Gaussians [frame_offsets[b], frame_offsets[b+1]) are frame b's,
+// binned into tile rows [b nty, (b+1) nty) of `frames` stacked frames (aabb
+// rows are in that stacked grid; nty is one frame's tile rows).
+cudaError_t launch_preprocess_frames(int n, int ntx, int nty, int frames, const int32_t* frame_offsets, int mode,
+                                     const float* xy, const float* scale, const float* rot, float* conic,
+                                     int32_t* aabb, int32_t* count, float* geo, long long* block_sums,
+                                     int32_t* tile_count, int f, const float* feat, const float* opacity,
+                                     float* prec, cudaStream_t stream);
 cudaError_t launch_make_geo(int n, const float* xy, const float* conic, float* geo, cudaStream_t stream);
 cudaError_t launch_conic_to_scale_rot_grad(int n, const float* scale, const float* rot,
                                            const float* d_conic, float* d_scale, float* d_rot,
@@ -97,14 +93,11 @@ cudaError_t launch_copy_i64(const int64_t* src, int64_t* dst, cudaStream_t strea
 // range is emptied and *overflow = 1.
 // With sort_key (a permutation of [0, n)) the lists are ordered by key and
 // mapped back to gids through key_order (key -> gid).
-// With warp_base (the per-warp pair bases of launch_preprocess_fused) the
-// scatter also writes pair_offset[0..n); without it pair_offset is read only.
-int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles);
+int64_t tile_lists_scratch_bytes(int64_t capacity);
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
-                             const long long* warp_base, int32_t* tile_count, const int64_t* total_pairs,
-                             int64_t capacity, const int32_t* sort_key, const int32_t* key_order,
-                             int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,
-                             cudaStream_t stream);
+                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
+                             const int32_t* sort_key, const int32_t* key_order, int32_t* gid_sorted,
+                             int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream);
 // Stable order of the Gaussians by depth (ties by gid): order[i] = gid of rank i,
 // rank[gid] = its position.
 int64_t depth_order_scratch_bytes(int64_t n);
@@ -262,7 +255,7 @@ cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const f
                                   const float* opacity, const int32_t* gid_sorted,
                                   const int32_t* tile_offsets, float* image, const int32_t* aabb,
                                   const int32_t* pair_offset, float* records, int32_t* slots,
-                                  const float* prec, cudaStream_t stream);
+                                  const float* prec, cudaStream_t stream, int frames = 1);
 
 // The windowed forward of the one-pass feathered render over virtual Gaussians
 // (launch_prepare_feathered): f <= 16.  With records, entry_pat receives each
@@ -278,14 +271,16 @@ cudaError_t launch_render_forward_feathered(int f, int h, int w, const FeatherTa
 // work-item table (backward_items_scratch_bytes): launch_render_backward_tiles
 // builds it and runs the backward; the two halves are also exposed so that the
 // table (which needs only tile_offsets) can be built beside the forward.
+// frames > 1: `frames` stacked h x w frames (tile rows [b nty, (b+1) nty) are
+// frame b's; images and dL/dimage are [frames][f][h][w]).
 cudaError_t launch_backward_items(int h, int w, int64_t total_pairs, const int32_t* tile_offsets, void* items_scratch,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, int frames = 1);
 cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pairs, const float* geo,
                                          const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
                                          const int32_t* pair_offset, const float* records, const int32_t* slots,
                                          float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
-                                         void* items_scratch, cudaStream_t stream);
+                                         void* items_scratch, cudaStream_t stream, int frames = 1);
 cudaError_t launch_render_backward_tiles(int f, int h, int w, int64_t total_pairs, const float* geo,
                                          const float* feat, const float* opacity, const int32_t* gid_sorted,
                                          const int32_t* tile_offsets, const float* grad_image,

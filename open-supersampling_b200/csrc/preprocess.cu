@@ -35,99 +35,26 @@ __device__ __forceinline__ void write_prec(float* prec, int prs, int g, float x,
     }
 }
 
-// Exclusive scans of two sequences at once by one CTA of kPreprocThreads
-// threads: a[i] = ca[i * sa] (int32 counters, scanned into oa[0..ma)) and
-// cb[0..mb) (int64, scanned in place).  Passes of 4 contiguous values per
-// thread, all loads of a pass in flight together, read through L2 (other CTAs
-// wrote them).  Returns both totals.
-__device__ void cta_scan_two(const int32_t* __restrict__ ca, int sa, int64_t ma, int32_t* __restrict__ oa,
-                             long long* __restrict__ cb, int64_t mb, long long& tot_a, long long& tot_b) {
-    constexpr int NT = kPreprocThreads;
-    constexpr int kPer = 4;  // keeps the kernel within 32 registers (two 1024-thread CTAs per SM)
-    constexpr int kWarps = NT / 32;
-    __shared__ long long s_wa[kWarps];
-    __shared__ long long s_wb[kWarps];
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    long long carry_a = 0, carry_b = 0;
-    const int64_t m = ma > mb ? ma : mb;
-    for (int64_t base = 0; base < m; base += static_cast<int64_t>(NT) * kPer) {
-        const int64_t lo = base + static_cast<int64_t>(threadIdx.x) * kPer;
-        int32_t va[kPer];
-        long long vb[kPer];
-        long long sum_a = 0, sum_b = 0;
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            va[k] = lo + k < ma ? __ldcg(ca + (lo + k) * sa) : 0;
-            vb[k] = lo + k < mb ? __ldcg(cb + lo + k) : 0;
-        }
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            sum_a += va[k];
-            sum_b += vb[k];
-        }
-        // inclusive warp scans, then the warps' totals
-        long long xa = sum_a, xb = sum_b;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const long long ya = __shfl_up_sync(0xffffffffu, xa, off);
-            const long long yb = __shfl_up_sync(0xffffffffu, xb, off);
-            if (lane >= off) {
-                xa += ya;
-                xb += yb;
-            }
-        }
-        if (lane == 31) {
-            s_wa[warp] = xa;
-            s_wb[warp] = xb;
-        }
-        __syncthreads();
-        long long pa = 0, pb = 0, ta = 0, tb = 0;
-#pragma unroll 8
-        for (int w = 0; w < kWarps; ++w) {
-            const long long wa = s_wa[w], wb = s_wb[w];
-            pa += w < warp ? wa : 0;
-            pb += w < warp ? wb : 0;
-            ta += wa;
-            tb += wb;
-        }
-        __syncthreads();  // s_wa / s_wb are rewritten by the next pass
-        long long ra = carry_a + pa + xa - sum_a;
-        long long rb = carry_b + pb + xb - sum_b;
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            if (lo + k < ma) oa[lo + k] = static_cast<int32_t>(ra);
-            if (lo + k < mb) cb[lo + k] = rb;
-            ra += va[k];
-            rb += vb[k];
-        }
-        carry_a += ta;
-        carry_b += tb;
+// Frame of Gaussian g: the last b with frame_offsets[b] <= g (offsets non-decreasing).
+__device__ __forceinline__ int frame_of(const int32_t* __restrict__ frame_offsets, int frames, int g) {
+    int lo = 0, hi = frames - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(frame_offsets + mid) <= g) lo = mid;
+        else hi = mid - 1;
     }
-    tot_a = carry_a;
-    tot_b = carry_b;
+    return lo;
 }
-
-// Outputs of the fused preprocess beyond those of the plain one.
-struct FusedScan {
-    long long* warp_sums;     // [ceil(n / 32)]: pair-count sums, then (last CTA) exclusive bases
-    int32_t* tile_offsets;    // [num_tiles + 1]
-    int32_t* pair_offset;     // pair_offset[n] = total
-    int64_t* total_pairs;
-    unsigned int* arrivals;   // CTA arrival counter, zero on entry
-};
 
 // One CTA per kPrepTile Gaussians, one Gaussian per thread.  With block_sums
 // non-null the CTA also writes the sum of its pair counts: the reduce half of
 // the gid-major pair-offset scan.  With
 // tile_count non-null every Gaussian adds one to each tile of its rectangle
 // (fire-and-forget reductions into counters kTileCountStride ints apart): the
-// per-tile list lengths.  FUSED: each warp writes the sum of its 32 pair counts
-// instead, and the last CTA to arrive (every CTA fences its writes and
-// reductions, then counts itself in) scans the tile counts and the warp sums;
-// nothing waits.
-template <bool FUSED>
-__global__ void __launch_bounds__(kPreprocThreads, 2) k_preprocess(int n, int ntx, int nty, int mode,
+// per-tile list lengths.  frames > 1: Gaussians [frame_offsets[b],
+// frame_offsets[b+1]) are frame b's, whose tiles are rows [b nty, (b+1) nty) of
+// the frames stacked; the rectangle moves into those rows.
+__global__ void __launch_bounds__(kPreprocThreads) k_preprocess(int n, int ntx, int nty, int mode,
                                                               const float2* __restrict__ xy,
                                                               const float2* __restrict__ scale,
                                                               const float* __restrict__ rot,
@@ -139,7 +66,9 @@ __global__ void __launch_bounds__(kPreprocThreads, 2) k_preprocess(int n, int nt
                                                               int32_t* __restrict__ tile_count, int F, int prs,
                                                               const float* __restrict__ feat,
                                                               const float* __restrict__ opacity,
-                                                              float* __restrict__ prec, FusedScan fs) {
+                                                              float* __restrict__ prec,
+                                                              const int32_t* __restrict__ frame_offsets,
+                                                              int frames) {
     long long local = 0;
     const int g = blockIdx.x * kPrepTile + threadIdx.x;
     if (g < n) {
@@ -156,42 +85,26 @@ __global__ void __launch_bounds__(kPreprocThreads, 2) k_preprocess(int n, int nt
             cnt = ntx * nty;
         } else {
             box = tile_aabb(c.x, c.y, s.x, s.y, k, mode_tau(mode), mode_fallback(mode), ntx, nty, cnt);
+            if (frames > 1) {
+                const int row0 = frame_of(frame_offsets, frames, g) * nty;  // this frame's tile rows
+                box.y += row0;
+                box.w += row0;
+            }
         }
         aabb[g] = box;
-        if (!FUSED) count[g] = cnt;
+        count[g] = cnt;
         local += cnt;
         if (geo != nullptr) write_geo(geo, g, c.x, c.y, k);
         if (prec != nullptr) write_prec(prec, prs, g, c.x, c.y, k, F, feat, opacity);
         if (tile_count != nullptr && cnt > 0) {
             for (int ty = box.y; ty < box.w; ++ty) {
                 for (int tx = box.x; tx < box.z; ++tx) {
-                    atomicAdd(&tile_count[static_cast<int64_t>(ty * ntx + tx) * kTileCountStride], 1);
+                    atomicAdd(&tile_count[(static_cast<int64_t>(ty) * ntx + tx) * kTileCountStride], 1);
                 }
             }
         }
     }
-    if (FUSED) {
-        __shared__ int s_last;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
-        const int w0 = g & ~31;
-        if ((threadIdx.x & 31) == 0 && w0 < n) fs.warp_sums[w0 >> 5] = local;
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) s_last = atomicAdd(fs.arrivals, 1u) == gridDim.x - 1 ? 1 : 0;
-        __syncthreads();
-        if (s_last == 0) return;
-        __threadfence();
-        const int64_t num_tiles = static_cast<int64_t>(ntx) * nty;
-        long long tot_tiles, tot_pairs;
-        cta_scan_two(tile_count, kTileCountStride, num_tiles, fs.tile_offsets, fs.warp_sums, div_up(n, 32),
-                     tot_tiles, tot_pairs);
-        if (threadIdx.x == 0) {
-            fs.tile_offsets[num_tiles] = static_cast<int32_t>(tot_tiles);
-            fs.pair_offset[n] = static_cast<int32_t>(tot_pairs);
-            *fs.total_pairs = static_cast<int64_t>(tot_pairs);
-        }
-    } else if (block_sums != nullptr) {
+    if (block_sums != nullptr) {
         __shared__ long long s_part[kPreprocThreads / 32];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) local += __shfl_down_sync(0xffffffffu, local, off);
@@ -241,28 +154,24 @@ cudaError_t launch_preprocess(int n, int ntx, int nty, int mode, const float* xy
                               const float* opacity, float* prec, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
     const int prs = prec != nullptr ? entry_record_floats(f) : 0;
-    k_preprocess<false><<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
+    k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
         conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count, f, prs, feat, opacity, prec,
-        FusedScan{});
+        nullptr, 1);
     return cudaGetLastError();
 }
 
-int64_t preprocess_fused_warps(int64_t n) { return div_up(n, 32); }
-
-cudaError_t launch_preprocess_fused(int n, int ntx, int nty, int mode, const float* xy, const float* scale,
-                                    const float* rot, float* conic, int32_t* aabb, int32_t* pair_offset, float* geo,
-                                    int32_t* tile_count, int32_t* tile_offsets, long long* warp_sums,
-                                    int64_t* total_pairs, int f, const float* feat, const float* opacity,
-                                    float* prec, cudaStream_t stream) {
+cudaError_t launch_preprocess_frames(int n, int ntx, int nty, int frames, const int32_t* frame_offsets, int mode,
+                                     const float* xy, const float* scale, const float* rot, float* conic,
+                                     int32_t* aabb, int32_t* count, float* geo, long long* block_sums,
+                                     int32_t* tile_count, int f, const float* feat, const float* opacity,
+                                     float* prec, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
     const int prs = prec != nullptr ? entry_record_floats(f) : 0;
-    const int64_t num_tiles = static_cast<int64_t>(ntx) * nty;
-    FusedScan fs{warp_sums, tile_offsets, pair_offset, total_pairs,
-                 reinterpret_cast<unsigned int*>(tile_count + num_tiles * kTileCountStride)};
-    k_preprocess<true><<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
+    k_preprocess<<<static_cast<unsigned>(div_up(n, kPrepTile)), kPreprocThreads, 0, stream>>>(
         n, ntx, nty, mode, reinterpret_cast<const float2*>(xy), reinterpret_cast<const float2*>(scale), rot,
-        conic, reinterpret_cast<int4*>(aabb), nullptr, geo, nullptr, tile_count, f, prs, feat, opacity, prec, fs);
+        conic, reinterpret_cast<int4*>(aabb), count, geo, block_sums, tile_count, f, prs, feat, opacity, prec,
+        frame_offsets, frames);
     return cudaGetLastError();
 }
 

@@ -47,9 +47,6 @@ struct BwdCfg {
     static constexpr int WARPS = SLOT * 4 * 4 <= 200 * 1024 ? 4 : 2;  // warps (slots) per CTA
     static constexpr int THREADS = WARPS * 32;
     static constexpr int MIN_CTAS = FC <= 4 ? 4 : 1;  // 4 x 4 warps per SM (<= 128 registers) for F <= 4
-    // Two slots per warp where they fit: the next item's block is copied in
-    // (cp.async) while the current one is summed.
-    static constexpr int NBUF = 2 * WARPS * SLOT * 4 <= 200 * 1024 ? 2 : 1;
     // F <= 4 runs the packed f32x2 path: the staged block is interleaved by
     // column pairs, [go_k(c), go_k(c+1)] for k = 0..SG-1 per pair of columns.
     static constexpr bool PAIRED = FC <= 4;
@@ -310,32 +307,6 @@ enum BwdMode { kAtomicGather = 0, kDetGather = 1, kDetRecords = 2 };
 // takes one index past the end before it leaves, so a launch increments the
 // counter exactly num_items times, and atomicInc's wrap limit (num_items - 1)
 // puts it back to 0 for the next launch.
-// Issues the copies of a tile's dL/dimage block into a warp slot (zeros outside
-// the image and for channels >= F); the caller commits and waits.
-template <int FC>
-__device__ __forceinline__ void stage_go_async(float* __restrict__ s_go, const float* __restrict__ grad_image, int F,
-                                               int H, int W, int ntx, int tile, int lane) {
-    constexpr int SG = BwdCfg<FC>::SG;
-    constexpr int kPerLane = kTilePixels / 32;
-    const int tx0 = (tile % ntx) * kTile;
-    const int ty0 = (tile / ntx) * kTile;
-    const int nrow = min(kTile, H - ty0);
-    const int ncol = min(kTile, W - tx0);
-    const int64_t plane = static_cast<int64_t>(H) * W;
-    const float* gbase = grad_image + static_cast<int64_t>(ty0) * W + tx0;
-#pragma unroll 4
-    for (int c = 0; c < SG; ++c) {
-#pragma unroll
-        for (int i = 0; i < kPerLane; ++i) {
-            const int p = i * 32 + lane;
-            const int ly = p >> 4, lx = p & (kTile - 1);
-            const bool valid = c < F && ly < nrow && lx < ncol;
-            const float* src = valid ? gbase + c * plane + static_cast<int64_t>(ly) * W + lx : grad_image;
-            cp_async4_zfill(s_go + go_index<FC>(ly, lx, c), src, valid);
-        }
-    }
-}
-
 __device__ __forceinline__ int take_item(uint32_t* work, uint32_t limit, int base, int lane) {
     uint32_t v = 0;
     if (lane == 0) v = atomicInc(work, limit);
@@ -357,57 +328,41 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
     const FeatherTable tab) {
     constexpr int SG = BwdCfg<FC>::SG;
     constexpr int RS = 4 + ((1 + FC + 3) / 4) * 4;  // entry record floats (the forward's layout)
-    constexpr int NBUF = BwdCfg<FC>::NBUF;
-    constexpr int SLOT = BwdCfg<FC>::SLOT;
     extern __shared__ float4 s_mem4[];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    float* s_slots = reinterpret_cast<float*>(s_mem4) + warp * NBUF * SLOT;
-    float* s_lw = reinterpret_cast<float*>(s_mem4) + BwdCfg<FC>::WARPS * NBUF * SLOT;
+    float* s_go = reinterpret_cast<float*>(s_mem4) + warp * BwdCfg<FC>::SLOT;
+    float* s_lw = reinterpret_cast<float*>(s_mem4) + BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT;
     if constexpr (WIN) {
         for (int i = threadIdx.x; i < 8 * kTile; i += BwdCfg<FC>::THREADS) s_lw[i] = tab.lw[i / kTile][i % kTile];
         __syncthreads();
     }
     const int n_items = *num_items;
+    const int nty_frame = (H + kTile - 1) / kTile;  // tile rows of one frame (stacked frames)
     const uint32_t limit = static_cast<uint32_t>(n_items) - 1u;
     const int grid_warps = static_cast<int>(gridDim.x) * BwdCfg<FC>::WARPS;
     int item = static_cast<int>(blockIdx.x) * BwdCfg<FC>::WARPS + warp;
-    // two slots: item i+1 is taken and its block copied in while item i is summed
-    int buf = 0;
-    int next = n_items;
-    int next_tile = 0;
-    if constexpr (NBUF == 2) {
-        if (item < n_items) {
-            stage_go_async<FC>(s_slots, grad_image, F, H, W, ntx, items[item].x, lane);
-            next = take_item(work, limit, grid_warps, lane);
-            if (next < n_items) next_tile = items[next].x;
-        }
-        cp_async_commit();
-    }
     while (item < n_items) {
-        __syncwarp();  // the previous item's reads of its slot are done
-        float* s_go = s_slots + buf * SLOT;
+        __syncwarp();  // the previous item's reads of s_go are done
         const int4 it = items[item];
         const int tile = it.x;
         const int first = it.y;
         const int r = it.z;
         const int tile_x = tile % ntx;
-        const int tile_y = tile / ntx;
+        const int tile_y = tile / ntx;  // row in the stacked frames' grid (the pair slot's coordinates)
+        const int frame = tile_y / nty_frame;
         const int tx0 = tile_x * kTile;
-        const int ty0 = tile_y * kTile;
+        const int ty0 = (tile_y - frame * nty_frame) * kTile;
         const int nrow = min(kTile, H - ty0);
         const int ncol = min(kTile, W - tx0);
 
-        if constexpr (NBUF == 2) {
-            if (next < n_items) stage_go_async<FC>(s_slots + (buf ^ 1) * SLOT, grad_image, F, H, W, ntx, next_tile, lane);
-            cp_async_commit();
-            cp_async_wait_one();  // this item's copies (issued one item earlier) have landed
-        } else {
-            // stage this tile's dL/dimage (zero outside the image): all of a lane's
-            // loads are issued before any store, so staging costs one L2 round trip
-            const int64_t plane = static_cast<int64_t>(H) * W;
+        // stage this tile's dL/dimage (zero outside the image): all of a lane's
+        // loads are issued before any store, so staging costs one L2 round trip
+        const int64_t plane = static_cast<int64_t>(H) * W;
+        {
             constexpr int kPerLane = kTilePixels / 32;  // 8 pixels per lane and channel
-            const float* gbase = grad_image + static_cast<int64_t>(ty0) * W + tx0;
+            const float* gbase =
+                grad_image + static_cast<int64_t>(frame) * F * plane + static_cast<int64_t>(ty0) * W + tx0;
 #pragma unroll 1
             for (int c0 = 0; c0 < SG; c0 += 4) {  // groups of 4 channels: 32 loads in flight per lane
                 float v[4][kPerLane];
@@ -433,7 +388,7 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
                 }
             }
         }
-        __syncwarp();  // every lane's copies or stores of the block are visible
+        __syncwarp();
 
         // lanes per entry (k) and this lane's entry and row band
         const int k = r > 16 ? 1 : (r > 8 ? 2 : (r > 4 ? 4 : (r > 2 ? 8 : 16)));
@@ -531,13 +486,8 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
 #pragma unroll
             for (int c = 0; c < FC; ++c) dF[c] = group_sum(dF[c], k);
         }
-        // the next item's index (two slots: the one after it); its latency overlaps the epilogue's loads
-        int after = n_items;
-        if constexpr (NBUF == 2) {
-            if (next < n_items) after = take_item(work, limit, grid_warps, lane);
-        } else {
-            next = take_item(work, limit, grid_warps, lane);
-        }
+        // the next item's index; its latency overlaps the epilogue's loads
+        const int next = take_item(work, limit, grid_warps, lane);
         if (active && band == 0) {
             const float dca = -0.5f * Sxx;
             const float dcb = -Sxy;
@@ -578,13 +528,7 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
             }
         }
         item = next;
-        if constexpr (NBUF == 2) {
-            next = after;
-            if (next < n_items) next_tile = items[next].x;
-            buf ^= 1;
-        }
     }
-    if constexpr (NBUF == 2) cp_async_wait_all();
 }
 
 // Work items of the backward: every tile has ceil(L / 32) items of up to 32
@@ -924,10 +868,10 @@ int64_t backward_items_scratch_bytes(int64_t total_pairs, int64_t num_tiles) {
     ((f) <= 1 ? CALL(1) : (f) <= 3 ? CALL(3) : (f) <= 4 ? CALL(4) : (f) <= 8 ? CALL(8) : (f) <= 16 ? CALL(16) : (f) <= 32 ? CALL(32) : CALL(64))
 
 cudaError_t launch_backward_items(int h, int w, int64_t total_pairs, const int32_t* tile_offsets, void* items_scratch,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, int frames) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
-    const int num_tiles = ntx * nty;
+    const int num_tiles = ntx * nty * frames;
     if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
     const int64_t max_items = backward_max_items(total_pairs, num_tiles);
     Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};
@@ -947,10 +891,10 @@ cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pair
                                          const int32_t* tile_offsets, const float* grad_image, const int32_t* aabb,
                                          const int32_t* pair_offset, const float* records, const int32_t* slots,
                                          float* pairgrad, int pair_stride, float* d_xy, float* d_conic, float* d_feat,
-                                         void* items_scratch, cudaStream_t stream) {
+                                         void* items_scratch, cudaStream_t stream, int frames) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
-    const int num_tiles = ntx * nty;
+    const int num_tiles = ntx * nty * frames;
     if (num_tiles == 0 || total_pairs == 0) return cudaSuccess;
     const int64_t max_items = backward_max_items(total_pairs, num_tiles);
     Arena arena{static_cast<char*>(items_scratch), backward_items_scratch_bytes(total_pairs, num_tiles), 0};

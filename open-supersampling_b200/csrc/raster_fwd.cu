@@ -273,9 +273,14 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
     __shared__ __align__(16) float s_df[BATCH * S];
     __shared__ unsigned char s_skip[BATCH];
 
+    // stacked frames: tile row trow is row trow - frame * nty of frame `frame`
     const int tile = blockIdx.x;
+    const int nty = (H + kTile - 1) / kTile;
+    const int trow = tile / ntx;
+    const int frame = trow / nty;
     const int tx0 = (tile % ntx) * kTile;
-    const int ty0 = (tile / ntx) * kTile;
+    const int ty0 = (trow - frame * nty) * kTile;
+    image += static_cast<int64_t>(frame) * F * H * W;
     const int px = tx0 + (threadIdx.x & (kTile - 1));
     const int ly = threadIdx.x >> 4;  // 0 .. ROWSTEP-1
     const float fpx = static_cast<float>(px);
@@ -452,6 +457,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
     const int G = gridDim.x;
     const int lx = threadIdx.x & (kTile - 1);
     const int ly = threadIdx.x >> 4;
+    const int nty_frame = (H + kTile - 1) / kTile;
     if constexpr (WIN) {
         // window tables: by column, and by this thread layout's rows (pattern, row step, PX rows)
         for (int i = threadIdx.x; i < 8 * kTile; i += NT) {
@@ -529,8 +535,11 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
             oq1 = 0;
         }
 
+        // stacked frames: tile row trow is row trow - frame * nty of frame `frame`
+        const int trow = t / ntx;
+        const int frame = trow / nty_frame;
         const int tx0 = (t % ntx) * kTile;
-        const int ty0 = (t / ntx) * kTile;
+        const int ty0 = (trow - frame * nty_frame) * kTile;
         const float fpx = static_cast<float>(tx0 + lx);
         float2 fpy2[NP];
 #pragma unroll
@@ -550,7 +559,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         bool regular = true;
         bool skip_any = false;
         const bool try_skip = cur1 - cur0 > kSkipMinList;  // the same for the whole CTA
-        const int tile_x = t % ntx, tile_y = t / ntx;
+        const int tile_x = t % ntx, tile_y = trow - frame * nty_frame;
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
             const int j = threadIdx.x + k * NT;
@@ -628,6 +637,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         const int px = tx0 + lx;
         if (px < W) {
             const int64_t plane = static_cast<int64_t>(H) * W;
+            float* __restrict__ img = image + static_cast<int64_t>(frame) * F * plane;
 #pragma unroll
             for (int q = 0; q < NP; ++q) {
 #pragma unroll
@@ -637,7 +647,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
                         const int64_t pix = static_cast<int64_t>(py) * W + px;
 #pragma unroll
                         for (int c = 0; c < FC; ++c) {
-                            if (c < F) image[c * plane + pix] = h2 == 0 ? acc2[q][c].x : acc2[q][c].y;
+                            if (c < F) img[c * plane + pix] = h2 == 0 ? acc2[q][c].x : acc2[q][c].y;
                         }
                     }
                 }
@@ -723,10 +733,10 @@ cudaError_t launch_render_forward_feathered(int f, int h, int w, const FeatherTa
 cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const float* feat, const float* opacity,
                                   const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
                                   const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
-                                  const float* prec, cudaStream_t stream) {
+                                  const float* prec, cudaStream_t stream, int frames) {
     const int ntx = static_cast<int>(div_up(w, kTile));
     const int nty = static_cast<int>(div_up(h, kTile));
-    const int num_tiles = ntx * nty;
+    const int num_tiles = ntx * nty * frames;
     if (num_tiles == 0 || f == 0) return cudaSuccess;
 #define OSS_FWD_CALL(FC)                                                                                           \
     launch_fwd_fc<FC>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, aabb,          \

@@ -5,15 +5,9 @@
 // the Gaussians whose tile rectangle covers the tile.  Here the per-tile counts
 // and their exclusive scan (the list offsets) come from render prepare, each
 // (Gaussian, tile) pair claims a slot of its tile with an atomic (in no
-// particular order), and every tile's list is sorted by the warp whose write
-// completes it, in the same launch (lists above kFusedCap entries by one more
-// launch).  A Gaussian covers a tile at most once, so a sorted list is unique:
-// the output is the reference's list whatever order the atomics ran in.
-//
-// The counters: line t of tile_count (kTileCountStride ints) holds tile t's
-// count (claimed down to 0 by the scatter) and its written-entry count; line
-// num_tiles holds the fused preprocess's CTA arrival count and the number of
-// lists left for k_sort_big.  The caller zeroes all of it before the prepare.
+// particular order), and every tile's list is then sorted.  A Gaussian covers a
+// tile at most once, so a sorted list is unique: the output is the reference's
+// list whatever order the atomics ran in.
 //
 // With a sort key (a permutation of [0, n), e.g. a Gaussian's rank by depth)
 // the lists hold keys while they are sorted and are mapped back to gids through
@@ -39,11 +33,69 @@ constexpr int kSortBuf = 8192;                    // ints of shared memory per C
 constexpr int kWarpCap = 1024;                    // lists up to 1024 sorted by one warp in registers
 constexpr int kCtaCap = kSortBuf;                 // lists up to 8192 sorted by the CTA in shared memory
 constexpr int kWindowBits = kSortBuf * 32;        // gid window of the bitmap path
-constexpr int64_t kSortBigCtas = 4 * 148;         // k_sort_big grid: four CTAs per SM of a B200
 
-// Lists up to kFusedCap entries are sorted by the warp whose write completes
-// them, inside the scatter; longer ones go to k_sort_big.
-constexpr int kFusedCap = 256;
+// One warp per 32 consecutive Gaussians.  The warp's pairs are dealt round-robin
+// to its lanes (lane j of round r takes the warp's pair 32 r + j); the owning
+// Gaussian is found by a binary search over the lanes' pair prefix.
+__global__ void __launch_bounds__(kScatterThreads) k_scatter_pairs(
+    int n, int ntx, int num_tiles, const int4* __restrict__ aabb, int32_t* __restrict__ pair_offset,
+    int32_t* __restrict__ tile_count, int32_t* __restrict__ tile_offsets, const int64_t* __restrict__ total_pairs,
+    int64_t capacity, const int32_t* __restrict__ sort_key, int32_t* __restrict__ unsorted,
+    int32_t* __restrict__ overflow) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kScatterThreads;
+    if (*total_pairs > capacity) {
+        // empty every list and every pair range; the image and gradients come out zero
+        for (int64_t i = tid; i <= num_tiles; i += nthreads) tile_offsets[i] = 0;
+        for (int64_t i = tid; i <= n; i += nthreads) pair_offset[i] = 0;
+        if (tid == 0) *overflow = 1;
+        return;
+    }
+    if (tid == 0) *overflow = 0;
+    const int lane = threadIdx.x & 31;
+    const int g0 = (blockIdx.x * kScatterWarps + (threadIdx.x >> 5)) * 32;
+    const int g = g0 + lane;
+    int4 box = make_int4(0, 0, 0, 0);
+    int key = g;
+    if (g < n) {
+        box = aabb[g];
+        if (sort_key != nullptr) key = sort_key[g];
+    }
+    const int bw = box.z > box.x ? box.z - box.x : 0;
+    const int bh = box.w > box.y ? box.w - box.y : 0;
+    const int cnt = bw * bh;
+    // inclusive then exclusive warp prefix of the pair counts
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+    }
+    const int start = incl - cnt;
+    const int warp_total = __shfl_sync(0xffffffffu, incl, 31);
+    for (int base = 0; base < warp_total; base += 32) {
+        const int j = base + lane;
+        int owner = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int cand = owner + step;
+            const int s = __shfl_sync(0xffffffffu, start, cand);
+            if (s <= j) owner = cand;
+        }
+        const int o_start = __shfl_sync(0xffffffffu, start, owner);
+        const int o_x = __shfl_sync(0xffffffffu, box.x, owner);
+        const int o_y = __shfl_sync(0xffffffffu, box.y, owner);
+        const int o_w = __shfl_sync(0xffffffffu, bw, owner);
+        const int o_key = __shfl_sync(0xffffffffu, key, owner);
+        if (j < warp_total) {
+            const int k = j - o_start;
+            const int dy = k / o_w;
+            const int t = (o_y + dy) * ntx + o_x + (k - dy * o_w);
+            const int slot = atomicSub(&tile_count[static_cast<int64_t>(t) * kTileCountStride], 1) - 1;
+            unsorted[tile_offsets[t] + slot] = o_key;
+        }
+    }
+}
 
 __device__ __forceinline__ int next_pow2(int v) {
     int p = 1;
@@ -115,7 +167,7 @@ __device__ __forceinline__ void warp_sort_list(const int32_t* __restrict__ src, 
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int e = r * 32 + lane;
-        v[r] = e < len ? __ldcg(src + e) : INT_MAX;
+        v[r] = e < len ? src[e] : INT_MAX;
     }
     warp_bitonic<R>(v, lane);
 #pragma unroll
@@ -184,13 +236,31 @@ __device__ void bitmap_sort(const int32_t* __restrict__ in, int32_t* __restrict_
     }
 }
 
-// Sort of one list of len <= MAXLEN (<= kWarpCap) by one warp, src read through L2.
-template <int MAXLEN>
-__device__ __forceinline__ void warp_sort_upto(const int32_t* __restrict__ src, int32_t* __restrict__ dst, int len,
-                                               int lane, const int32_t* __restrict__ key_order) {
+// One warp per tile; lists above kWarpCap are sorted afterwards by the whole CTA.
+__global__ void __launch_bounds__(kSortThreads) k_sort_tiles(int n, int num_tiles,
+                                                              const int32_t* __restrict__ tile_offsets,
+                                                              const int32_t* __restrict__ unsorted,
+                                                              const int32_t* __restrict__ key_order,
+                                                              int32_t* __restrict__ gid_sorted) {
+    __shared__ int32_t s_buf[kSortBuf];
+    __shared__ int s_warp[kSortWarps];
+    __shared__ int s_big;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_big = 0;
+    __syncthreads();
+    const int t = blockIdx.x * kSortWarps + warp;
+    int off = 0;
+    int len = 0;
+    if (t < num_tiles) {
+        off = tile_offsets[t];
+        len = tile_offsets[t + 1] - off;
+    }
+    const int32_t* src = unsorted + off;
+    int32_t* dst = gid_sorted + off;
     if (len <= 32) {
         // rank of each value among the (distinct) values of the warp
-        const int32_t v = lane < len ? __ldcg(src + lane) : INT_MAX;
+        const int32_t v = lane < len ? src[lane] : INT_MAX;
         int rank = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) rank += __shfl_sync(0xffffffffu, v, j) < v ? 1 : 0;
@@ -201,168 +271,32 @@ __device__ __forceinline__ void warp_sort_upto(const int32_t* __restrict__ src, 
         warp_sort_list<4>(src, dst, len, lane, key_order);
     } else if (len <= 256) {
         warp_sort_list<8>(src, dst, len, lane, key_order);
-    } else if constexpr (MAXLEN > 256) {
-        if (len <= 512) {
-            warp_sort_list<16>(src, dst, len, lane, key_order);
+    } else if (len <= 512) {
+        warp_sort_list<16>(src, dst, len, lane, key_order);
+    } else if (len <= kWarpCap) {
+        warp_sort_list<32>(src, dst, len, lane, key_order);
+    } else if (lane == 0) {
+        atomicOr(&s_big, 1 << warp);
+    }
+    __syncthreads();
+    const int big = s_big;
+    for (int wv = 0; wv < kSortWarps; ++wv) {
+        if ((big >> wv & 1) == 0) continue;
+        const int bt = blockIdx.x * kSortWarps + wv;
+        const int boff = tile_offsets[bt];
+        const int blen = tile_offsets[bt + 1] - boff;
+        if (blen <= kCtaCap) {
+            const int lp = next_pow2(blen);
+            for (int i = threadIdx.x; i < lp; i += kSortThreads) s_buf[i] = i < blen ? unsorted[boff + i] : INT_MAX;
+            __syncthreads();
+            cta_bitonic_sort(s_buf, lp);
+            for (int i = threadIdx.x; i < blen; i += kSortThreads) {
+                gid_sorted[boff + i] = key_order != nullptr ? key_order[s_buf[i]] : s_buf[i];
+            }
+            __syncthreads();
         } else {
-            warp_sort_list<32>(src, dst, len, lane, key_order);
+            bitmap_sort(unsorted + boff, gid_sorted + boff, blen, n, s_buf, s_warp, key_order);
         }
-    }
-}
-
-// One warp per 32 consecutive Gaussians.  The warp's pairs are dealt round-robin
-// to its lanes (lane j of round r takes the warp's pair 32 r + j); the owning
-// Gaussian is found by a binary search over the lanes' pair prefix.  A pair
-// claims a slot of its tile (returning atomic on the tile's counter), writes
-// its key there, and then counts itself written on the counter next to it
-// (release: fence, then the atomic).  The pair whose count completes the list
-// (acquire: the atomic, then a fence) hands the tile to its warp, which sorts
-// the list at once (reading it through L2: other SMs wrote it) or, above
-// kFusedCap entries, appends the tile to big_tiles for k_sort_big.  With
-// OFFSETS the warp also writes its Gaussians' gid-major pair offsets from the
-// per-warp bases of the fused preprocess.  Six CTAs per SM: 40 registers, the
-// sorting networks without spills.
-template <bool OFFSETS>
-__global__ void __launch_bounds__(kScatterThreads, 6) k_scatter_sort(
-    int n, int ntx, int num_tiles, const int4* __restrict__ aabb, int32_t* __restrict__ pair_offset,
-    const long long* __restrict__ warp_base, int32_t* __restrict__ tile_count, int32_t* __restrict__ tile_offsets,
-    const int64_t* __restrict__ total_pairs, int64_t capacity, const int32_t* __restrict__ sort_key,
-    const int32_t* __restrict__ key_order, int32_t* __restrict__ unsorted, int32_t* __restrict__ gid_sorted,
-    int32_t* __restrict__ big_tiles, int32_t* __restrict__ overflow) {
-    const int64_t tid = static_cast<int64_t>(blockIdx.x) * kScatterThreads + threadIdx.x;
-    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kScatterThreads;
-    if (*total_pairs > capacity) {
-        // empty every list and every pair range; the image and gradients come out zero
-        for (int64_t i = tid; i <= num_tiles; i += nthreads) tile_offsets[i] = 0;
-        for (int64_t i = tid; i <= n; i += nthreads) pair_offset[i] = 0;
-        if (tid == 0) *overflow = 1;
-        return;
-    }
-    if (tid == 0) *overflow = 0;
-    const int lane = threadIdx.x & 31;
-    const int warp_id = blockIdx.x * kScatterWarps + (threadIdx.x >> 5);
-    const int g = warp_id * 32 + lane;
-    int4 box = make_int4(0, 0, 0, 0);
-    int key = g;
-    if (g < n) {
-        box = aabb[g];
-        if (sort_key != nullptr) key = sort_key[g];
-    }
-    const int bw = box.z > box.x ? box.z - box.x : 0;
-    const int bh = box.w > box.y ? box.w - box.y : 0;
-    const int cnt = bw * bh;
-    // inclusive then exclusive warp prefix of the pair counts
-    int incl = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-    }
-    const int start = incl - cnt;
-    const int warp_total = __shfl_sync(0xffffffffu, incl, 31);
-    if (OFFSETS && g < n) pair_offset[g] = static_cast<int32_t>(warp_base[warp_id] + start);
-    int32_t* big_count = tile_count + static_cast<int64_t>(num_tiles) * kTileCountStride + 1;
-    for (int base = 0; base < warp_total; base += 32) {
-        const int j = base + lane;
-        int owner = 0;
-#pragma unroll
-        for (int step = 16; step > 0; step >>= 1) {
-            const int cand = owner + step;
-            const int s = __shfl_sync(0xffffffffu, start, cand);
-            if (s <= j) owner = cand;
-        }
-        const int o_start = __shfl_sync(0xffffffffu, start, owner);
-        const int o_x = __shfl_sync(0xffffffffu, box.x, owner);
-        const int o_y = __shfl_sync(0xffffffffu, box.y, owner);
-        const int o_w = __shfl_sync(0xffffffffu, bw, owner);
-        const int o_key = __shfl_sync(0xffffffffu, key, owner);
-        bool last = false;
-        int t = 0, off = 0, len = 0;
-        if (j < warp_total) {
-            const int k = j - o_start;
-            const int dy = k / o_w;
-            t = (o_y + dy) * ntx + o_x + (k - dy * o_w);
-            int32_t* line = tile_count + static_cast<int64_t>(t) * kTileCountStride;
-            off = tile_offsets[t];
-            len = tile_offsets[t + 1] - off;
-            const int slot = atomicSub(line, 1) - 1;
-            unsorted[off + slot] = o_key;
-            __threadfence();
-            last = atomicAdd(line + 1, 1) == len - 1;
-        }
-        unsigned done = __ballot_sync(0xffffffffu, last);
-        if (done != 0u) {
-            __threadfence();
-            while (done != 0u) {
-                const int src = __ffs(static_cast<int>(done)) - 1;
-                done &= done - 1u;
-                const int tt = __shfl_sync(0xffffffffu, t, src);
-                const int to = __shfl_sync(0xffffffffu, off, src);
-                const int tl = __shfl_sync(0xffffffffu, len, src);
-                if (tl <= kFusedCap) {
-                    warp_sort_upto<kFusedCap>(unsorted + to, gid_sorted + to, tl, lane, key_order);
-                } else if (lane == 0) {
-                    big_tiles[atomicAdd(big_count, 1)] = tt;
-                }
-            }
-        }
-    }
-}
-
-// The lists the scatter left unsorted (longer than kFusedCap), big_tiles[0 ..
-// *big_count): one warp per list up to kWarpCap, the whole CTA beyond.  With no
-// such list every CTA returns at once.
-__global__ void __launch_bounds__(kSortThreads) k_sort_big(int n, const int32_t* __restrict__ tile_offsets,
-                                                            const int32_t* __restrict__ unsorted,
-                                                            const int32_t* __restrict__ key_order,
-                                                            int32_t* __restrict__ gid_sorted,
-                                                            const int32_t* __restrict__ big_tiles,
-                                                            const int32_t* __restrict__ big_count) {
-    __shared__ int32_t s_buf[kSortBuf];
-    __shared__ int s_warp[kSortWarps];
-    __shared__ int s_big;
-    const int count = *big_count;
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    for (int base = blockIdx.x * kSortWarps; base < count; base += gridDim.x * kSortWarps) {
-        if (threadIdx.x == 0) s_big = 0;
-        __syncthreads();
-        const int i = base + warp;
-        int off = 0;
-        int len = 0;
-        if (i < count) {
-            const int t = big_tiles[i];
-            off = tile_offsets[t];
-            len = tile_offsets[t + 1] - off;
-        }
-        if (len <= kWarpCap) {
-            warp_sort_upto<kWarpCap>(unsorted + off, gid_sorted + off, len, lane, key_order);
-        } else if (lane == 0) {
-            atomicOr(&s_big, 1 << warp);
-        }
-        __syncthreads();
-        const int big = s_big;
-        for (int wv = 0; wv < kSortWarps; ++wv) {
-            if ((big >> wv & 1) == 0) continue;
-            const int bt = big_tiles[base + wv];
-            const int boff = tile_offsets[bt];
-            const int blen = tile_offsets[bt + 1] - boff;
-            if (blen <= kCtaCap) {
-                const int lp = next_pow2(blen);
-                for (int k = threadIdx.x; k < lp; k += kSortThreads) {
-                    s_buf[k] = k < blen ? unsorted[boff + k] : INT_MAX;
-                }
-                __syncthreads();
-                cta_bitonic_sort(s_buf, lp);
-                for (int k = threadIdx.x; k < blen; k += kSortThreads) {
-                    gid_sorted[boff + k] = key_order != nullptr ? key_order[s_buf[k]] : s_buf[k];
-                }
-                __syncthreads();
-            } else {
-                bitmap_sort(unsorted + boff, gid_sorted + boff, blen, n, s_buf, s_warp, key_order);
-            }
-        }
-        __syncthreads();
     }
 }
 
@@ -390,9 +324,7 @@ __global__ void k_empty_lists(int num_tiles, int32_t* __restrict__ tile_offsets,
 
 }  // namespace
 
-int64_t tile_lists_scratch_bytes(int64_t capacity, int64_t num_tiles) {
-    return arena_bytes(capacity, sizeof(int32_t)) + arena_bytes(num_tiles, sizeof(int32_t));
-}
+int64_t tile_lists_scratch_bytes(int64_t capacity) { return arena_bytes(capacity, sizeof(int32_t)); }
 
 int64_t depth_order_scratch_bytes(int64_t n) {
     return arena_bytes(n, sizeof(uint32_t)) + arena_bytes(n, sizeof(int32_t)) + radix_scratch_bytes(n, 0xffffffffu);
@@ -413,35 +345,22 @@ cudaError_t depth_order(int n, const float* depth, int32_t* order, int32_t* rank
 }
 
 cudaError_t build_tile_lists(int n, int ntx, int num_tiles, const int32_t* aabb, int32_t* pair_offset,
-                             const long long* warp_base, int32_t* tile_count, const int64_t* total_pairs,
-                             int64_t capacity, const int32_t* sort_key, const int32_t* key_order,
-                             int32_t* gid_sorted, int32_t* tile_offsets, int32_t* overflow, void* scratch,
-                             cudaStream_t stream) {
+                             int32_t* tile_count, const int64_t* total_pairs, int64_t capacity,
+                             const int32_t* sort_key, const int32_t* key_order, int32_t* gid_sorted,
+                             int32_t* tile_offsets, int32_t* overflow, void* scratch, cudaStream_t stream) {
     if (n == 0 || num_tiles == 0) {
         k_empty_lists<<<static_cast<unsigned>(div_up(static_cast<int64_t>(num_tiles) + 1, 256)), 256, 0, stream>>>(
             num_tiles, tile_offsets, overflow);
         return cudaGetLastError();
     }
-    Arena arena{static_cast<char*>(scratch), tile_lists_scratch_bytes(capacity, num_tiles), 0};
-    int32_t* unsorted = arena.take<int32_t>(capacity);
-    int32_t* big_tiles = arena.take<int32_t>(num_tiles);
-    const unsigned grid = static_cast<unsigned>(div_up(n, kScatterThreads));
-    if (warp_base != nullptr) {
-        k_scatter_sort<true><<<grid, kScatterThreads, 0, stream>>>(
-            n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, warp_base, tile_count, tile_offsets,
-            total_pairs, capacity, sort_key, key_order, unsorted, gid_sorted, big_tiles, overflow);
-    } else {
-        k_scatter_sort<false><<<grid, kScatterThreads, 0, stream>>>(
-            n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, nullptr, tile_count, tile_offsets,
-            total_pairs, capacity, sort_key, key_order, unsorted, gid_sorted, big_tiles, overflow);
-    }
+    int32_t* unsorted = static_cast<int32_t*>(scratch);
+    k_scatter_pairs<<<static_cast<unsigned>(div_up(n, kScatterThreads)), kScatterThreads, 0, stream>>>(
+        n, ntx, num_tiles, reinterpret_cast<const int4*>(aabb), pair_offset, tile_count, tile_offsets, total_pairs,
+        capacity, sort_key, unsorted, overflow);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    const int64_t sort_grid = div_up(num_tiles, kSortWarps) < kSortBigCtas ? div_up(num_tiles, kSortWarps)
-                                                                           : kSortBigCtas;
-    k_sort_big<<<static_cast<unsigned>(sort_grid), kSortThreads, 0, stream>>>(
-        n, tile_offsets, unsorted, key_order, gid_sorted, big_tiles,
-        tile_count + static_cast<int64_t>(num_tiles) * kTileCountStride + 1);
+    k_sort_tiles<<<static_cast<unsigned>(div_up(num_tiles, kSortWarps)), kSortThreads, 0, stream>>>(
+        n, num_tiles, tile_offsets, unsorted, key_order, gid_sorted);
     return cudaGetLastError();
 }
 

@@ -45,8 +45,8 @@ SIGNATURES = {
     "oss_render_bin_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_render_bin": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _i32, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _i64,
-         _p]),
+        [_i64, _i64, _i64, _i64, _p, _i32, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _p,
+         _p, _i64, _p]),
     "oss_publish_total": (ctypes.c_int, [_p, _p, _p]),
     "oss_depth_order_scratch_bytes": (_i64, [_i64]),
     "oss_depth_order": (ctypes.c_int, [_i64, _p, _p, _p, _p, _i64, _p]),
@@ -60,6 +60,8 @@ SIGNATURES = {
     ),
     "oss_entry_record_floats": (ctypes.c_int, [_i64]),
     "oss_render_forward": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "oss_render_forward_frames": (
+        ctypes.c_int, [_i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "oss_render_backward_scratch_bytes": (_i64, [_i64, _i64, _i64]),
     "oss_render_backward": (
         ctypes.c_int,
@@ -68,6 +70,10 @@ SIGNATURES = {
     ),
     "oss_pair_grad_stride": (ctypes.c_int, [_i64]),
     "oss_backward_items": (ctypes.c_int, [_i64, _i64, _i64, _p, _p, _i64, _p]),
+    "oss_backward_items_frames": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _i64, _p]),
+    "oss_render_backward_items_frames": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_render_backward_items": (
         ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "oss_render_backward_pairs_scratch_bytes": (_i64, [_i64, _i64]),

@@ -227,7 +227,8 @@ def bin_gaussians(xy: torch.Tensor, scale: torch.Tensor, rot: torch.Tensor, h: i
         scratch = torch.empty((max(1, lib.oss_render_bin_scratch_bytes(n, capacity, num_tiles)),), device=dev,
                               dtype=torch.uint8)
         _lib.check(
-            lib.oss_render_bin(n, h, w, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(), max(prec_f, 0),
+            lib.oss_render_bin(n, h, w, 1, None, mode, xy.data_ptr(), scale.data_ptr(), rot.data_ptr(),
+                               max(prec_f, 0),
                                _lib.ptr(feat), _lib.ptr(opacity if feat is not None else None), conic.data_ptr(),
                                aabb.data_ptr(), pair_offset.data_ptr(), geo.data_ptr(), _lib.ptr(prec),
                                total.data_ptr(), tile_count.data_ptr(), tile_offsets.data_ptr(), capacity,

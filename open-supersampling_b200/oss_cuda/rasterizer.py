@@ -35,7 +35,7 @@ from importlib import import_module
 import torch
 from torch.autograd import Function
 
-from . import _feather, _raster, ops
+from . import _batched, _feather, _lib, _raster, ops
 
 try:
     from . import _C
@@ -241,11 +241,34 @@ def rasterize_gaussians_batched(xy, scale, rot, feat, offsets, h, w, tile_size=1
     of the concatenated inputs: (B, F, H, W), differentiable like
     rasterize_gaussians (keywords as there; opacity and depth are per Gaussian of
     the concatenation).  offsets is a host sequence or CPU tensor of B+1
-    non-decreasing ints from 0 to N."""
+    non-decreasing ints from 0 to N.
+
+    The additive render (blend="sum", the Gaussian weight, culled lists, no
+    overlap or phase offset) runs as one launch chain over all B frames
+    (oss_cuda._batched), with the same images and gradients as B calls; the
+    other modes call rasterize_gaussians once per frame."""
     offs = [int(v) for v in (offsets.tolist() if torch.is_tensor(offsets) else offsets)]
     n = int(xy.size(0))
     if len(offs) < 1 or offs[0] != 0 or offs[-1] != n or any(b < a for a, b in zip(offs, offs[1:])):
         raise ValueError("offsets must be non-decreasing from 0 to N")
+    h, w, tile_size = int(h), int(w), int(tile_size)
+    if len(offs) > 1 and _one_chain(kwargs):
+        _raster.check_gaussians(xy, scale, rot, feat)
+        _raster.check_hw(h, w, tile_size)
+        opacity = kwargs.get("opacity")
+        if opacity is not None:
+            _raster.check_float_cuda(opacity, "opacity")
+            if opacity.dim() != 1 or opacity.size(0) != n:
+                raise RuntimeError("opacity must be (N,)")
+        if int(feat.size(1)) > _lib.MAX_CHANNELS:
+            raise RuntimeError(f"F must be <= {_lib.MAX_CHANNELS}")
+        mode = _raster.binning_mode(kwargs.get("binning"))
+        capacity = kwargs.get("pair_capacity")
+        if capacity is not None:
+            capacity = int(capacity)
+            if capacity < 0 or capacity > _raster.INT32_MAX:
+                raise ValueError("pair_capacity must be in [0, 2**31 - 1]")
+        return _batched.RasterizeFrames.apply(xy, scale, rot, feat, opacity, tuple(offs), h, w, mode, capacity)
     per_g = {k: kwargs.pop(k) for k in ("opacity", "depth") if kwargs.get(k) is not None}
     frames = []
     for a, b in zip(offs, offs[1:]):
@@ -256,3 +279,17 @@ def rasterize_gaussians_batched(xy, scale, rot, feat, offsets, h, w, tile_size=1
     if not frames:
         return torch.zeros((0, int(feat.size(1)), int(h), int(w)), device=xy.device, dtype=torch.float32)
     return torch.stack(frames, 0)
+
+
+def _one_chain(kwargs) -> bool:
+    """The keywords of rasterize_gaussians_batched that the one-chain path covers."""
+    known = {"binning", "opacity", "pair_capacity", "blend", "weight", "overlap", "phase_offset", "depth", "background"}
+    if set(kwargs) - known or torch.compiler.is_compiling():
+        return False
+    if kwargs.get("blend", "sum") != "sum" or kwargs.get("weight", "gaussian") != "gaussian":
+        return False
+    if int(kwargs.get("overlap", 0)) != 0 or tuple(int(v) for v in kwargs.get("phase_offset", (0, 0))) != (0, 0):
+        return False
+    if kwargs.get("depth") is not None or kwargs.get("background") is not None:
+        return False
+    return _raster.binning_mode(kwargs.get("binning")) != _lib.OSS_BIN_FULL

@@ -113,9 +113,9 @@ def test_render_bin_argument_checks():
     need = lib.oss_render_bin_scratch_bytes(1000, 5000, 16)
     assert need >= lib.oss_bin_pairs_scratch_bytes(1000, 5000, 16)
 
-    def call(mode=0, capacity=5000, scratch_bytes=need, tile_count=8):
-        return lib.oss_render_bin(1000, 64, 64, mode, 8, 8, 8, 0, None, None, 8, 16, 8, 16, None, 8, tile_count, 8,
-                                  capacity, 8, 8, 16, scratch_bytes, None)
+    def call(mode=0, capacity=5000, scratch_bytes=need, tile_count=8, frames=1):
+        return lib.oss_render_bin(1000, 64, 64, frames, None, mode, 8, 8, 8, 0, None, None, 8, 16, 8, 16, None, 8,
+                                  tile_count, 8, capacity, 8, 8, 16, scratch_bytes, None)
 
     assert call(scratch_bytes=need - 1) == 4 and "scratch" in lib.oss_last_error().decode()
     assert call(mode=2) == 1 and "full-frame" in lib.oss_last_error().decode()
@@ -123,8 +123,12 @@ def test_render_bin_argument_checks():
     assert call(capacity=-1) == 1
     assert call(capacity=1 << 31) == 3 and "int32" in lib.oss_last_error().decode()
     assert call(tile_count=None) == 1 and "tile_count" in lib.oss_last_error().decode()
-    # one more counter line than the tiles: the binning's global counters
-    assert lib.oss_tile_count_elems(100) == 101 * lib.oss_tile_count_elems(0)
+    assert call(frames=0) == 1 and "frames" in lib.oss_last_error().decode()
+    assert call(frames=2) == 1 and "frame_offsets" in lib.oss_last_error().decode()
+    assert call(frames=1 << 30) == 3
+    assert lib.oss_render_forward_frames(1, 3, 64, 64, 0, None, None, None, None, None, None, None, None, None,
+                                         None, None, None) == 1
+    assert lib.oss_backward_items_frames(64, 64, -1, 0, None, None, 0, None) == 1
 
 
 def test_scratch_sizes_are_monotone():

@@ -27,20 +27,30 @@ def _leaves(ts):
     return [t.detach().clone().requires_grad_(True) for t in ts]
 
 
-@pytest.mark.parametrize("binning", ["tight3sigma", "exact"])
-def test_batched_equals_per_frame_calls(cuda_device, binning):
-    from oss_cuda import rasterize_gaussians, rasterize_gaussians_batched
+@pytest.mark.parametrize("binning,h,w,f,capacity", [
+    ("tight3sigma", 80, 112, 3, None),
+    ("exact", 80, 112, 3, None),
+    ("exact56", 83, 97, 3, None),  # ragged last tile row and column of every frame
+    ("tight3sigma", 83, 97, 5, None),
+    ("tight3sigma", 80, 112, 3, 20_000),  # sync-free: the device checks the capacity
+])
+def test_batched_equals_per_frame_calls(cuda_device, binning, h, w, f, capacity):
+    """One launch chain over the frames (stacked tile grid) against one call per
+    frame: images and gradients bit for bit."""
+    from oss_cuda import pair_capacity_overflowed, rasterize_gaussians, rasterize_gaussians_batched
 
-    h, w = 80, 112
     sizes = [300, 0, 517, 64]
     offs = [0]
     for s in sizes:
         offs.append(offs[-1] + s)
-    xy, scale, rot, feat, op = _gaussians(offs[-1], h, w, 3, 3)
-    grad = torch.randn((len(sizes), 3, h, w), device="cuda")
+    xy, scale, rot, feat, op = _gaussians(offs[-1], h, w, f, 3)
+    grad = torch.randn((len(sizes), f, h, w), device="cuda")
     a = _leaves((xy, scale, rot, feat, op))
-    img = rasterize_gaussians_batched(a[0], a[1], a[2], a[3], offs, h, w, binning=binning, opacity=a[4])
-    assert img.shape == (len(sizes), 3, h, w)
+    pair_capacity_overflowed()
+    img = rasterize_gaussians_batched(a[0], a[1], a[2], a[3], offs, h, w, binning=binning, opacity=a[4],
+                                      pair_capacity=capacity)
+    assert not pair_capacity_overflowed()
+    assert img.shape == (len(sizes), f, h, w)
     img.backward(grad)
     b = _leaves((xy, scale, rot, feat, op))
     for i, (lo, hi) in enumerate(zip(offs, offs[1:])):

@@ -82,7 +82,7 @@ class Lists:
             self.pair_offset.fill_(-3)
             self.tile_offsets.fill_(-3)
             self.tile_count.fill_(12345)
-            self.chk(self.lib.oss_render_bin(self.n, self.h, self.w, self.mode, self.xy.data_ptr(),
+            self.chk(self.lib.oss_render_bin(self.n, self.h, self.w, 1, None, self.mode, self.xy.data_ptr(),
                                              self.scale.data_ptr(), self.rot.data_ptr(), self.pf, _lib.ptr(self.pfeat),
                                              _lib.ptr(self.popacity), self.conic.data_ptr(), self.aabb.data_ptr(),
                                              self.pair_offset.data_ptr(), self.geo.data_ptr(), _lib.ptr(self.prec),
