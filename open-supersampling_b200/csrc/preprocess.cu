@@ -53,8 +53,9 @@ __device__ __forceinline__ int frame_of(const int32_t* __restrict__ frame_offset
 // (fire-and-forget reductions into counters kTileCountStride ints apart): the
 // per-tile list lengths.  frames > 1: Gaussians [frame_offsets[b],
 // frame_offsets[b+1]) are frame b's, whose tiles are rows [b nty, (b+1) nty) of
-// the frames stacked; the rectangle moves into those rows.
-__global__ void __launch_bounds__(kPreprocThreads) k_preprocess(int n, int ntx, int nty, int mode,
+// the frames stacked; the rectangle moves into those rows.  Two CTAs per SM
+// (32 registers): 196 CTAs at config 2 then run as one wave on 148 SMs.
+__global__ void __launch_bounds__(kPreprocThreads, 2) k_preprocess(int n, int ntx, int nty, int mode,
                                                               const float2* __restrict__ xy,
                                                               const float2* __restrict__ scale,
                                                               const float* __restrict__ rot,

@@ -317,7 +317,9 @@ __device__ __forceinline__ int take_item(uint32_t* work, uint32_t limit, int bas
 // phase-bit patterns come from the forward's entry_pat and select its rows of
 // the log2 window table, kept in shared memory after the warp slots; the
 // window's column terms take 16 more registers (4 CTAs per SM for F <= 4).
-template <int FC, int MODE, bool WIN = false>
+// FRAMES: the items' tiles are those of stacked frames (dL/dimage is
+// [frames][F][H][W]); a separate instance, so the one-frame kernel carries none of it.
+template <int FC, int MODE, bool WIN = false, bool FRAMES = false>
 __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdCfg<FC>::MIN_CTAS) k_render_bwd(
     int F, int H, int W, int ntx, const float* __restrict__ geo, const float* __restrict__ feat,
     const float* __restrict__ opacity, const int32_t* __restrict__ gid_sorted, const int4* __restrict__ items,
@@ -350,7 +352,7 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
         const int r = it.z;
         const int tile_x = tile % ntx;
         const int tile_y = tile / ntx;  // row in the stacked frames' grid (the pair slot's coordinates)
-        const int frame = tile_y / nty_frame;
+        const int frame = FRAMES ? tile_y / nty_frame : 0;
         const int tx0 = tile_x * kTile;
         const int ty0 = (tile_y - frame * nty_frame) * kTile;
         const int nrow = min(kTile, H - ty0);
@@ -361,8 +363,8 @@ __global__ void __launch_bounds__(BwdCfg<FC>::THREADS, WIN && FC <= 4 ? 4 : BwdC
         const int64_t plane = static_cast<int64_t>(H) * W;
         {
             constexpr int kPerLane = kTilePixels / 32;  // 8 pixels per lane and channel
-            const float* gbase =
-                grad_image + static_cast<int64_t>(frame) * F * plane + static_cast<int64_t>(ty0) * W + tx0;
+            const float* gbase = grad_image + (FRAMES ? static_cast<int64_t>(frame) * F * plane : 0) +
+                                 static_cast<int64_t>(ty0) * W + tx0;
 #pragma unroll 1
             for (int c0 = 0; c0 < SG; c0 += 4) {  // groups of 4 channels: 32 loads in flight per lane
                 float v[4][kPerLane];
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
 
 // Persistent grid of the backward: as many CTAs as fit on the device at once
 // (cached per device), never more than the table's largest item count needs.
-template <int FC, int MODE, bool WIN = false>
+template <int FC, int MODE, bool WIN = false, bool FRAMES = false>
 int bwd_grid(int64_t max_items, int smem) {
     static int cached[64] = {0};
     const int64_t need = div_up(max_items, BwdCfg<FC>::WARPS);
@@ -778,22 +780,23 @@ int bwd_grid(int64_t max_items, int smem) {
     if (cached[dev] == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE, WIN>, BwdCfg<FC>::THREADS, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE, WIN, FRAMES>, BwdCfg<FC>::THREADS,
+                                                      smem);
         cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
     }
     return static_cast<int>(need < cached[dev] ? need : cached[dev]);
 }
 
-template <int FC, int MODE>
+template <int FC, int MODE, bool FRAMES>
 cudaError_t launch_bwd_mode(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
                             const float* opacity, const int32_t* gid_sorted, const int4* items,
                             const int32_t* num_items, uint32_t* work, const float* grad_image, const int32_t* aabb,
                             const int32_t* pair_offset, const float* records, const int32_t* slots, float* pairgrad,
                             int pstride, float* d_xy, float* d_conic, float* d_feat, cudaStream_t stream) {
     const int smem = BwdCfg<FC>::WARPS * BwdCfg<FC>::SLOT * static_cast<int>(sizeof(float));
-    auto kern = k_render_bwd<FC, MODE>;
+    auto kern = k_render_bwd<FC, MODE, false, FRAMES>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    const unsigned blocks = static_cast<unsigned>(bwd_grid<FC, MODE>(max_items, smem));
+    const unsigned blocks = static_cast<unsigned>(bwd_grid<FC, MODE, false, FRAMES>(max_items, smem));
     kern<<<blocks, BwdCfg<FC>::THREADS, smem, stream>>>(
         f, h, w, ntx, geo, feat, opacity, gid_sorted, items, num_items, work, grad_image,
         reinterpret_cast<const int4*>(aabb), pair_offset, records, slots, pairgrad, pstride, d_xy, d_conic, d_feat,
@@ -818,7 +821,7 @@ cudaError_t launch_bwd_win(int f, int h, int w, int ntx, int64_t max_items, cons
     return cudaGetLastError();
 }
 
-template <int FC>
+template <int FC, bool FRAMES>
 cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int4* items, const int32_t* num_items,
                           uint32_t* work,
@@ -826,16 +829,16 @@ cudaError_t launch_bwd_fc(int f, int h, int w, int ntx, int64_t max_items, const
                           const float* records, const int32_t* slots, float* pairgrad, int pstride, float* d_xy,
                           float* d_conic, float* d_feat, cudaStream_t stream) {
     if (pairgrad == nullptr) {
-        return launch_bwd_mode<FC, kAtomicGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
+        return launch_bwd_mode<FC, kAtomicGather, FRAMES>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
                                                   num_items, work, grad_image, aabb, pair_offset, records, slots, pairgrad,
                                                   pstride, d_xy, d_conic, d_feat, stream);
     }
     if (records != nullptr) {
-        return launch_bwd_mode<FC, kDetRecords>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
+        return launch_bwd_mode<FC, kDetRecords, FRAMES>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,
                                                 num_items, work, grad_image, aabb, pair_offset, records, slots, pairgrad,
                                                 pstride, d_xy, d_conic, d_feat, stream);
     }
-    return launch_bwd_mode<FC, kDetGather>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items,
+    return launch_bwd_mode<FC, kDetGather, FRAMES>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items,
                                            work, grad_image, aabb, pair_offset, records, slots, pairgrad, pstride, d_xy,
                                            d_conic, d_feat, stream);
 }
@@ -903,8 +906,12 @@ cudaError_t launch_render_backward_items(int f, int h, int w, int64_t total_pair
     const int32_t* num_items = counters;
     uint32_t* work = reinterpret_cast<uint32_t*>(counters + 1);
 #define OSS_BWD_CALL(FC)                                                                                          \
-    launch_bwd_fc<FC>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items, work, grad_image, \
-                      aabb, pair_offset, records, slots, pairgrad, pair_stride, d_xy, d_conic, d_feat, stream)
+    (frames > 1 ? launch_bwd_fc<FC, true>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items, num_items,  \
+                                          work, grad_image, aabb, pair_offset, records, slots, pairgrad, pair_stride, \
+                                          d_xy, d_conic, d_feat, stream)                                              \
+                : launch_bwd_fc<FC, false>(f, h, w, ntx, max_items, geo, feat, opacity, gid_sorted, items,            \
+                                           num_items, work, grad_image, aabb, pair_offset, records, slots, pairgrad,  \
+                                           pair_stride, d_xy, d_conic, d_feat, stream))
     return OSS_DISPATCH_FC(f, OSS_BWD_CALL);
 #undef OSS_BWD_CALL
 }

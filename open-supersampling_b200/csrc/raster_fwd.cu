@@ -251,7 +251,7 @@ __device__ __forceinline__ void fwd_batch_sel(bool regular, bool skip, int cnt, 
     }
 }
 
-template <int FC>
+template <int FC, bool FRAMES = false>
 __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int W, int ntx,
                                                                 const float* __restrict__ geo,
                                                                 const float* __restrict__ feat,
@@ -277,10 +277,10 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd(int F, int H, int
     const int tile = blockIdx.x;
     const int nty = (H + kTile - 1) / kTile;
     const int trow = tile / ntx;
-    const int frame = trow / nty;
+    const int frame = FRAMES ? trow / nty : 0;
     const int tx0 = (tile % ntx) * kTile;
     const int ty0 = (trow - frame * nty) * kTile;
-    image += static_cast<int64_t>(frame) * F * H * W;
+    if (FRAMES) image += static_cast<int64_t>(frame) * F * H * W;
     const int px = tx0 + (threadIdx.x & (kTile - 1));
     const int ly = threadIdx.x >> 4;  // 0 .. ROWSTEP-1
     const float fpx = static_cast<float>(px);
@@ -426,7 +426,10 @@ constexpr int kPipeBatch = 128;
 // record), from which the staging pass derives the entry's phase-bit patterns
 // for this tile (and stores them for the backward in entry_pat, with the
 // records); the math adds the tabulated log2 window weights to q'.
-template <int FC, bool WIN>
+// FRAMES: the tiles are those of stacked frames (a tile row's frame is decoded
+// and the image is [frames][F][H][W]); a separate instance, so the one-frame
+// kernel carries none of it.
+template <int FC, bool WIN, bool FRAMES = false>
 __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H, int W, int ntx, int num_tiles,
                                                                      const float* __restrict__ prec,
                                                                      const int32_t* __restrict__ gid_sorted,
@@ -537,7 +540,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
 
         // stacked frames: tile row trow is row trow - frame * nty of frame `frame`
         const int trow = t / ntx;
-        const int frame = trow / nty_frame;
+        const int frame = FRAMES ? trow / nty_frame : 0;
         const int tx0 = (t % ntx) * kTile;
         const int ty0 = (trow - frame * nty_frame) * kTile;
         const float fpx = static_cast<float>(tx0 + lx);
@@ -637,7 +640,8 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
         const int px = tx0 + lx;
         if (px < W) {
             const int64_t plane = static_cast<int64_t>(H) * W;
-            float* __restrict__ img = image + static_cast<int64_t>(frame) * F * plane;
+            // the frame again from t: keeping it live across the sums costs a register
+            float* __restrict__ img = FRAMES ? image + static_cast<int64_t>((t / ntx) / nty_frame) * F * plane : image;
 #pragma unroll
             for (int q = 0; q < NP; ++q) {
 #pragma unroll
@@ -658,7 +662,7 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
 }
 
 // CTAs per SM the pipelined forward runs with (queried once per device).
-template <int FC, bool WIN = false>
+template <int FC, bool WIN = false, bool FRAMES = false>
 int pipe_grid(int num_tiles) {
     static int cached[64] = {0};
     int dev = 0;
@@ -666,26 +670,27 @@ int pipe_grid(int num_tiles) {
     if (cached[dev] == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC, WIN>, FwdCfg<FC>::NT, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC, WIN, FRAMES>, FwdCfg<FC>::NT, 0);
         cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
     }
     return num_tiles < cached[dev] ? num_tiles : cached[dev];
 }
 
-template <int FC>
+template <int FC, bool FRAMES>
 cudaError_t launch_fwd_fc(int f, int h, int w, int ntx, int num_tiles, const float* geo, const float* feat,
                           const float* opacity, const int32_t* gid_sorted, const int32_t* tile_offsets, float* image,
                           const int32_t* aabb, const int32_t* pair_offset, float* records, int32_t* slots,
                           const float* prec, cudaStream_t stream) {
     if constexpr (FwdCfg<FC>::PX % 2 == 0) {
         if (prec != nullptr && slots == nullptr) {
-            k_render_fwd_pipe<FC, false><<<static_cast<unsigned>(pipe_grid<FC>(num_tiles)), FwdCfg<FC>::NT, 0,
-                                           stream>>>(f, h, w, ntx, num_tiles, prec, gid_sorted, tile_offsets, image,
-                                                     records, nullptr, nullptr, FeatherTable{});
+            k_render_fwd_pipe<FC, false, FRAMES>
+                <<<static_cast<unsigned>(pipe_grid<FC, false, FRAMES>(num_tiles)), FwdCfg<FC>::NT, 0, stream>>>(
+                    f, h, w, ntx, num_tiles, prec, gid_sorted, tile_offsets, image, records, nullptr, nullptr,
+                    FeatherTable{});
             return cudaGetLastError();
         }
     }
-    k_render_fwd<FC><<<static_cast<unsigned>(num_tiles), FwdCfg<FC>::NT, 0, stream>>>(
+    k_render_fwd<FC, FRAMES><<<static_cast<unsigned>(num_tiles), FwdCfg<FC>::NT, 0, stream>>>(
         f, h, w, ntx, geo, feat, opacity, gid_sorted, tile_offsets, image, reinterpret_cast<const int4*>(aabb),
         pair_offset, records, slots, prec);
     return cudaGetLastError();
@@ -739,8 +744,10 @@ cudaError_t launch_render_forward(int f, int h, int w, const float* geo, const f
     const int num_tiles = ntx * nty * frames;
     if (num_tiles == 0 || f == 0) return cudaSuccess;
 #define OSS_FWD_CALL(FC)                                                                                           \
-    launch_fwd_fc<FC>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets, image, aabb,          \
-                      pair_offset, records, slots, prec, stream)
+    (frames > 1 ? launch_fwd_fc<FC, true>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets,    \
+                                          image, aabb, pair_offset, records, slots, prec, stream)                   \
+                : launch_fwd_fc<FC, false>(f, h, w, ntx, num_tiles, geo, feat, opacity, gid_sorted, tile_offsets,   \
+                                           image, aabb, pair_offset, records, slots, prec, stream))
     if (f <= 1) return OSS_FWD_CALL(1);
     if (f <= 3) return OSS_FWD_CALL(3);
     if (f <= 4) return OSS_FWD_CALL(4);

@@ -17,6 +17,22 @@ from . import _lib
 from ._raster import INT32_MAX, aligned, read_total, stream_of, sticky_overflow
 
 
+_FRAME_OFFSETS = {}
+
+
+def frame_offsets_on(device, offsets) -> torch.Tensor:
+    """The frame offsets as a device int32 tensor, made once per device and
+    offsets (a host copy would break CUDA-graph capture of later calls)."""
+    key = (torch.device(device).index, tuple(offsets))
+    t = _FRAME_OFFSETS.get(key)
+    if t is None:
+        if len(_FRAME_OFFSETS) > 64:
+            _FRAME_OFFSETS.clear()
+        t = torch.tensor(offsets, device=device, dtype=torch.int32)
+        _FRAME_OFFSETS[key] = t
+    return t
+
+
 class BinnedFrames:
     """Lists and per-Gaussian records of one batched binning."""
 
@@ -48,7 +64,7 @@ def bin_frames(xy, scale, rot, h, w, mode, offsets, feat, opacity, capacity=None
     f32 = dict(device=dev, dtype=torch.float32)
     i32 = dict(device=dev, dtype=torch.int32)
     f = int(feat.size(1))
-    fo = torch.tensor(offsets, **i32)
+    fo = frame_offsets_on(dev, offsets)
     conic = torch.empty((n, 3), **f32)
     aabb = torch.empty((n, 4), **i32)
     pair_offset = torch.empty((n + 1,), **i32)
