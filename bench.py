@@ -1000,23 +1000,37 @@ def config3_object(rank, world, steps, warmup, binning="tight3sigma"):
     motions = [torch.from_numpy(smooth_motion(540, 960, 300 + f)[None]).to(device) for f in frames]
     pipe = Pipeline(n, h, w, _lib.BINNING_MODES[binning], device)
 
+    # the warp keeps every slot (dropped Gaussians parked outside the frame: the same image as
+    # the compacted canvas) and the render runs on a pair capacity sized once over the frames,
+    # so a step reads nothing on the host between its frames
+    def frame(m, alpha, sync):
+        c = warp_canvas(canvas, m, (h, w), 0.5, alpha, compact=False)
+        pipe.step({"xy": c.positions, "scale": c.scales, "rot": c.rotations, "opacity": c.opacities,
+                   "rgb": c.colors}, backward=False, sync=sync, timed=False)
+
+    with torch.no_grad():
+        for alpha in (1.0, 0.5):
+            for m in motions:
+                frame(m, alpha, True)
+
     def step_at(alpha):
         def step():
             with torch.no_grad():
                 for m in motions:
-                    c = warp_canvas(canvas, m, (h, w), 0.5, alpha)
-                    pipe.step({"xy": c.positions, "scale": c.scales, "rot": c.rotations, "opacity": c.opacities,
-                               "rgb": c.colors}, backward=False, sync=True)
+                    frame(m, alpha, False)
         return step
 
     ms1, clocks = timed(step_at(1.0), steps, warmup, device, world)
     ms05, _ = timed(step_at(0.5), steps, warmup, device, world)
+    pipe.check_overflow()
     return {"value": 8 * h * w / (ms1 * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms1, "steps": steps,
             "frames_per_rank": len(frames), "ms_per_frame": ms1 / max(1, len(frames)),
             "alpha_0p5": {"value": 8 * h * w / (ms05 * 1e-3) / 1e6, "ms_per_step": ms05},
             "scaling": "strong", "clocks": clocks,
             "workload": f"config3: warp (GS-STVSR, LR 540x960 -> {w}x{h}) + forward render, N={n}, alpha=1.0 "
-                        f"(alpha_0p5: 0.5), batch 8 frames split over {world} rank(s), {binning} lists"}
+                        f"(alpha_0p5: 0.5), batch 8 frames split over {world} rank(s), {binning} lists; the warp "
+                        f"parks dropped Gaussians (warp_canvas(compact=False)) and the render runs on a pair "
+                        f"capacity: no host read between frames"}
 
 
 def run_config3(args, rank, world):

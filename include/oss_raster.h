@@ -463,6 +463,18 @@ OSS_API int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, in
                             float* out_positions, float* out_scales, float* out_rotations,
                             float* out_opacities, float* out_colors, int32_t* out_count,
                             void* scratch, int64_t scratch_bytes, void* stream);
+/* The same warp without compaction, for a render that follows on the device:
+ * every input slot g is written at out_*[g]; a Gaussian whose warped centre
+ * leaves the frame is parked at (-1e7, -1e7) with opacity and colours 0, so it
+ * bins into no tile and adds nothing to an image.  No count is produced, so
+ * nothing needs to be read on the host before the render.  Forward only. */
+OSS_API int oss_warp_canvas_parked(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h, int64_t w,
+                            const float* motion_lr, float alpha, const float* recon,
+                            const float* positions, const float* scales, const float* rotations,
+                            const float* opacities, const float* colors,
+                            float* out_positions, float* out_scales, float* out_rotations,
+                            float* out_opacities, float* out_colors,
+                            void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Backward of oss_warp_canvas: the gradients autograd takes through
  * canvas_warp.py:177-254 and covariance_resampling.py:76-116.  g_* are the

@@ -788,6 +788,39 @@ int oss_warp_canvas(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h,
     return OSS_OK;
 }
 
+int oss_warp_canvas_parked(int64_t n, int64_t f, int64_t h_lr, int64_t w_lr, int64_t h, int64_t w,
+                           const float* motion_lr, float alpha, const float* recon, const float* positions,
+                           const float* scales, const float* rotations, const float* opacities, const float* colors,
+                           float* out_positions, float* out_scales, float* out_rotations, float* out_opacities,
+                           float* out_colors, void* scratch, int64_t scratch_bytes, void* stream) {
+    OSS_CHECK(n >= 0 && f >= 0, OSS_ERR_INVALID, "canvas.count must be non-negative");
+    OSS_CHECK(n <= INT_MAX && f <= INT_MAX / (n > 0 ? n : 1), OSS_ERR_RANGE, "canvas size exceeds int32 range");
+    OSS_CHECK(h > 0 && w > 0, OSS_ERR_INVALID, "output_hw must be positive");
+    OSS_CHECK(h_lr > 0 && w_lr > 0, OSS_ERR_INVALID, "motion_lr must be (B, 2, H, W) with H, W > 0");
+    OSS_CHECK(h <= INT_MAX && w <= INT_MAX && h_lr <= INT_MAX && w_lr <= INT_MAX &&
+                  2 * h_lr * w_lr <= (int64_t)1 << 40,
+              OSS_ERR_RANGE, "motion or output size exceeds int32 range");
+    OSS_CHECK(recon != nullptr, OSS_ERR_INVALID, "recon must point to 4 host floats");
+    OSS_CHECK(scratch_bytes >= oss_warp_canvas_scratch_bytes(n), OSS_ERR_SCRATCH, "warp_canvas scratch too small");
+    if (n > 0) {
+        OSS_CHECK(motion_lr != nullptr && positions != nullptr && scales != nullptr && rotations != nullptr &&
+                      opacities != nullptr && (f == 0 || colors != nullptr),
+                  OSS_ERR_INVALID, "canvas inputs must be non-null");
+        OSS_CHECK(out_positions != nullptr && out_scales != nullptr && out_rotations != nullptr &&
+                      out_opacities != nullptr && (f == 0 || out_colors != nullptr),
+                  OSS_ERR_INVALID, "canvas outputs must be non-null");
+        OSS_CHECK(aligned(positions, 8) && aligned(scales, 8) && aligned(out_positions, 8) && aligned(out_scales, 8),
+                  OSS_ERR_INVALID, "positions and scales must be 8-byte aligned");
+        OSS_CHECK(scratch != nullptr && aligned(scratch, 16), OSS_ERR_INVALID, "scratch must be 16-byte aligned");
+    }
+    OSS_CUDA_TRY(oss::launch_warp_canvas_parked(static_cast<int>(n), static_cast<int>(f), static_cast<int>(h_lr),
+                                                static_cast<int>(w_lr), static_cast<int>(h), static_cast<int>(w),
+                                                motion_lr, alpha, recon, positions, scales, rotations, opacities,
+                                                colors, out_positions, out_scales, out_rotations, out_opacities,
+                                                out_colors, scratch, as_stream(stream)));
+    return OSS_OK;
+}
+
 int oss_v6_sanitize(int64_t n, int64_t h, int64_t w, int64_t f_in, int64_t f_out, int32_t ones_channel,
                     const uint8_t* active_mask, const float* positions, const float* scales, const float* rotations,
                     const float* colors, float* out_xy, float* out_scale, float* out_rot, float* out_feat,

@@ -187,6 +187,13 @@ cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const
                                const float* ops, const float* colors, float* out_pos, float* out_scales,
                                float* out_rots, float* out_ops, float* out_colors, int32_t* out_count,
                                void* scratch, cudaStream_t stream);
+// The same without compaction: every input slot written, the dropped ones
+// parked outside the frame with zero opacity and colours (no survivor count).
+cudaError_t launch_warp_canvas_parked(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                                      const float* recon4, const float* pos, const float* scales, const float* rots,
+                                      const float* ops, const float* colors, float* out_pos, float* out_scales,
+                                      float* out_rots, float* out_ops, float* out_colors, void* scratch,
+                                      cudaStream_t stream);
 // Backward of launch_warp_canvas (fwd_scratch: the forward's scratch, which
 // holds the survivor offsets); d_motion (LR, may be null) is written, d_hr
 // planes live in `scratch` (warp_backward_scratch_bytes).

@@ -138,6 +138,11 @@ __global__ void __launch_bounds__(kThreads) k_warp_eval(int n, Field fld, float4
     flag[g] = in_frame ? 1 : 0;
 }
 
+// PARKED: no compaction.  Every Gaussian keeps its slot (offs holds the
+// in-frame flags); a dropped one is written far outside the frame with zero
+// opacity and colours, so it bins into no tile and renders nothing -- the
+// survivors' image without the host read of the survivor count.
+template <bool PARKED>
 __global__ void __launch_bounds__(kThreads) k_warp_scatter(int n, int f, const float4* __restrict__ tmp,
                                                             const int32_t* __restrict__ offs,
                                                             const float* __restrict__ ops,
@@ -148,8 +153,20 @@ __global__ void __launch_bounds__(kThreads) k_warp_scatter(int n, int f, const f
                                                             float* __restrict__ out_colors) {
     const int g = blockIdx.x * kThreads + threadIdx.x;
     if (g >= n) return;
-    const int k = offs[g];
-    if (offs[g + 1] == k) return;  // dropped: new centre outside the frame
+    int k = g;
+    if (PARKED) {
+        if (offs[g] == 0) {
+            out_pos[g] = make_float2(-1.0e7f, -1.0e7f);
+            out_scales[g] = make_float2(1.0f, 1.0f);
+            out_rots[g] = 0.0f;
+            out_ops[g] = 0.0f;
+            for (int c = 0; c < f; ++c) out_colors[static_cast<int64_t>(g) * f + c] = 0.0f;
+            return;
+        }
+    } else {
+        k = offs[g];
+        if (offs[g + 1] == k) return;  // dropped: new centre outside the frame
+    }
     const float4 a = tmp[2 * g];
     out_pos[k] = make_float2(a.x, a.y);
     out_scales[k] = make_float2(a.z, a.w);
@@ -538,13 +555,35 @@ cudaError_t launch_warp_canvas(int n, int f, int hl, int wl, int h, int w, const
     cudaError_t err = scan_exclusive_i32(flags, flags, n, true, nullptr, scan_scratch, stream);
     if (err != cudaSuccess) return err;
     if (n > 0) {
-        k_warp_scatter<<<blocks, kThreads, 0, stream>>>(n, f, tmp, flags, ops, colors, reinterpret_cast<float2*>(out_pos),
-                                                        reinterpret_cast<float2*>(out_scales), out_rots, out_ops,
-                                                        out_colors);
+        k_warp_scatter<false><<<blocks, kThreads, 0, stream>>>(
+            n, f, tmp, flags, ops, colors, reinterpret_cast<float2*>(out_pos), reinterpret_cast<float2*>(out_scales),
+            out_rots, out_ops, out_colors);
         err = cudaGetLastError();
         if (err != cudaSuccess) return err;
     }
     return cudaMemcpyAsync(out_count, flags + n, sizeof(int32_t), cudaMemcpyDeviceToDevice, stream);
+}
+
+cudaError_t launch_warp_canvas_parked(int n, int f, int hl, int wl, int h, int w, const float* motion, float alpha,
+                                      const float* recon4, const float* pos, const float* scales, const float* rots,
+                                      const float* ops, const float* colors, float* out_pos, float* out_scales,
+                                      float* out_rots, float* out_ops, float* out_colors, void* scratch,
+                                      cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    Arena arena{static_cast<char*>(scratch), warp_scratch_bytes(n), 0};
+    float4* tmp = arena.take<float4>(static_cast<int64_t>(n) * 2);
+    int32_t* flags = arena.take<int32_t>(n + 1);
+    const Field fld = make_field(motion, hl, wl, h, w, alpha);
+    const float4 recon = make_float4(recon4[0], recon4[1], recon4[2], recon4[3]);
+    const unsigned blocks = static_cast<unsigned>(div_up(n, kThreads));
+    k_warp_eval<<<blocks, kThreads, 0, stream>>>(n, fld, recon, reinterpret_cast<const float2*>(pos),
+                                                 reinterpret_cast<const float2*>(scales), rots, tmp, flags);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    k_warp_scatter<true><<<blocks, kThreads, 0, stream>>>(
+        n, f, tmp, flags, ops, colors, reinterpret_cast<float2*>(out_pos), reinterpret_cast<float2*>(out_scales),
+        out_rots, out_ops, out_colors);
+    return cudaGetLastError();
 }
 
 int64_t warp_backward_scratch_bytes(int64_t h, int64_t w) { return arena_bytes(6 * h * w, sizeof(double)); }

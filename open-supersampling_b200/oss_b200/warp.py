@@ -131,7 +131,7 @@ def _f32c(t: torch.Tensor) -> torch.Tensor:
 
 
 def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
-                sigma_recon: torch.Tensor | float = 0.5, alpha: float = 1.0) -> CanvasState:
+                sigma_recon: torch.Tensor | float = 0.5, alpha: float = 1.0, compact: bool = True) -> CanvasState:
     """Warp canvas positions by alpha * motion and resample covariances.
 
     Returns a fresh CanvasState holding the Gaussians whose warped centre
@@ -139,6 +139,11 @@ def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
     count, as the reference's ``.item()`` at canvas_warp.py:253).
     Differentiable in the canvas tensors and motion_lr (its first batch item,
     the one the warp reads); sigma_recon is a constant.
+
+    compact=False (forward only) keeps every slot: a Gaussian whose centre
+    leaves the frame is parked far outside it with opacity and colours 0, so a
+    render of the result is the render of the compacted canvas (the same
+    per-tile order of the survivors) and nothing is read on the host.
     """
     h, w = _validate_motion(motion_lr, output_hw)
     count = _validate_canvas(canvas)
@@ -151,6 +156,8 @@ def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
     dev = canvas.positions.device
     if dev.type != "cuda" or motion_lr.device != dev:
         raise RuntimeError("warp_canvas needs canvas and motion_lr on the same CUDA device")
+    if not compact:
+        return _warp_parked(motion_lr, src, h, w, sigma_recon, alpha)
     out_dtypes = [t.dtype for t in src]
     with torch.cuda.device(dev):
         outs = _WarpCanvas.apply(_f32c(motion_lr[0]), *(_f32c(t) for t in src), h, w, _recon4(sigma_recon),
@@ -158,6 +165,32 @@ def warp_canvas(canvas, motion_lr: torch.Tensor, output_hw: Tuple[int, int],
     k = int(outs[0].shape[0])
     res = [o.to(dtype=dt) for o, dt in zip(outs, out_dtypes)]
     return CanvasState(*res, count=k)
+
+
+def _warp_parked(motion_lr, src, h, w, sigma_recon, alpha) -> CanvasState:
+    """warp_canvas(compact=False): oss_warp_canvas_parked, forward only."""
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (motion_lr, *src)):
+        raise RuntimeError("warp_canvas(compact=False) is forward-only; use compact=True for gradients")
+    dev = src[0].device
+    lib = _lib.lib()
+    motion = _f32c(motion_lr[0].detach())
+    pos, sc, rt, op, col = (_f32c(t.detach()) for t in src)
+    n, f = int(pos.shape[0]), int(col.shape[1])
+    f32 = dict(device=dev, dtype=torch.float32)
+    outs = [torch.empty((n, 2), **f32), torch.empty((n, 2), **f32), torch.empty((n,), **f32),
+            torch.empty((n,), **f32), torch.empty((n, f), **f32)]
+    scratch = torch.empty((lib.oss_warp_canvas_scratch_bytes(n),), device=dev, dtype=torch.uint8)
+    recon = torch.tensor(_recon4(sigma_recon), dtype=torch.float32)
+    with torch.cuda.device(dev):
+        _lib.check(
+            lib.oss_warp_canvas_parked(n, f, motion.shape[1], motion.shape[2], h, w, motion.data_ptr(), float(alpha),
+                                       recon.data_ptr(), pos.data_ptr(), sc.data_ptr(), rt.data_ptr(),
+                                       op.data_ptr(), col.data_ptr() if f > 0 else None,
+                                       *(o.data_ptr() if o.numel() else None for o in outs), scratch.data_ptr(),
+                                       scratch.numel(), stream_of(pos)),
+            "oss_warp_canvas_parked",
+        )
+    return CanvasState(*(o.to(dtype=t.dtype) for o, t in zip(outs, src)), count=n)
 
 
 def warp_positions(xy: torch.Tensor, motion: torch.Tensor, hw: Tuple[int, int],

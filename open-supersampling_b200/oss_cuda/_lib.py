@@ -89,6 +89,11 @@ SIGNATURES = {
     "oss_conic_to_scale_rot_grad": (ctypes.c_int, [_i64, _p, _p, _p, _p, _p, _p]),
     "oss_full_tile_pairs": (ctypes.c_int, [_i64, _i64, _p, _p, _p]),
     "oss_warp_canvas_scratch_bytes": (_i64, [_i64]),
+    "oss_warp_canvas_parked": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+         _i64, _p],
+    ),
     "oss_warp_canvas": (
         ctypes.c_int,
         [_i64, _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,

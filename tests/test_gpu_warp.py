@@ -264,3 +264,52 @@ def test_warp_positions_refuses_grad_inputs(cuda_device):
     xy = torch.rand(4, 2, device=cuda_device, requires_grad=True)
     with pytest.raises(RuntimeError, match="forward-only"):
         warp_positions(xy, torch.zeros(2, 16, 16, device=cuda_device), (16, 16))
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("alpha", [1.0, 0.5])
+def test_warp_parked_renders_as_compacted(cuda_device, alpha):
+    """warp_canvas(compact=False) keeps every slot: the survivors' values at
+    their own slots equal the compacted ones bit for bit, the dropped slots are
+    parked with zero opacity and colours, and a render of the parked canvas is
+    the render of the compacted canvas bit for bit (the survivors keep their
+    relative order in every tile list; a parked Gaussian bins into no tile)."""
+    from oss_b200 import CanvasState, warp_canvas
+    from oss_cuda import rasterize_gaussians
+
+    n, h, w, hl, wl = 60_000, 270, 480, 135, 240
+    rng = np.random.default_rng(41)
+    pos = (rng.random((n, 2)) * np.array([w, h])).astype(np.float32)
+    sc = np.exp(rng.standard_normal((n, 2)) * 0.3 + math.log(2.0)).astype(np.float32)
+    rt = (rng.random(n) * math.pi).astype(np.float32)
+    op = (1 / (1 + np.exp(-rng.standard_normal(n)))).astype(np.float32)
+    col = rng.random((n, 3)).astype(np.float32)
+    motion = smooth_motion(hl, wl, seed=42, max_mag=24.0)
+    t = lambda a: torch.from_numpy(a).to(cuda_device)
+    canvas = CanvasState(t(pos), t(sc), t(rt), t(op), t(col), n)
+    packed = warp_canvas(canvas, t(motion[None]), (h, w), 0.5, alpha)
+    parked = warp_canvas(canvas, t(motion[None]), (h, w), 0.5, alpha, compact=False)
+    assert parked.count == n and 0 < packed.count < n
+    keep = (parked.opacities != 0) | (parked.positions[:, 0] > -1.0e6)
+    assert int(keep.sum()) == packed.count
+    for a, b in ((parked.positions, packed.positions), (parked.scales, packed.scales),
+                 (parked.rotations, packed.rotations), (parked.opacities, packed.opacities),
+                 (parked.colors, packed.colors)):
+        assert torch.equal(a[keep], b)
+    assert not parked.opacities[~keep].any() and not parked.colors[~keep].any()
+    for binning in ("tight3sigma", "exact56"):
+        imgs = [rasterize_gaussians(c.positions, c.scales, c.rotations, c.colors, h, w, binning=binning,
+                                    opacity=c.opacities) for c in (packed, parked)]
+        assert torch.equal(imgs[0], imgs[1]), binning
+
+
+def test_warp_parked_is_forward_only(cuda_device):
+    from oss_b200 import CanvasState, warp_canvas
+
+    n = 64
+    pos = torch.rand((n, 2), device=cuda_device) * 32
+    canvas = CanvasState(pos.requires_grad_(True), torch.ones((n, 2), device=cuda_device),
+                         torch.zeros(n, device=cuda_device), torch.ones(n, device=cuda_device),
+                         torch.ones((n, 3), device=cuda_device), n)
+    with pytest.raises(RuntimeError, match="forward-only"):
+        warp_canvas(canvas, torch.zeros((1, 2, 16, 16), device=cuda_device), (32, 32), compact=False)
