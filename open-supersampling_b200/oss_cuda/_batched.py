@@ -165,17 +165,18 @@ class RasterizeFrames(Function):
         with torch.cuda.device(xy.device):
             b = bin_frames(xy, scale, rot, h, w, mode, offsets, feat, opacity, capacity)
             image, records = forward_frames(b, feat, any(ctx.needs_input_grad[:5]))
-        ctx.save_for_backward(xy, scale, rot, feat, opacity, b.conic, b.aabb, b.pair_offset, b.geo, b.prec,
-                              b.gid_sorted, b.tile_offsets, records)
+        # the backward reads the forward's entry records, not the packed per-Gaussian ones
+        ctx.save_for_backward(xy, scale, rot, feat, opacity, b.conic, b.aabb, b.pair_offset, b.geo, b.gid_sorted,
+                              b.tile_offsets, records)
         ctx.meta = (b.n, b.frames, h, w, mode, b.total_pairs, b.prec_f)
         return image
 
     @staticmethod
     def backward(ctx, grad_out):
-        (xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, prec, gid_sorted, tile_offsets,
+        (xy, scale, rot, feat, opacity, conic, aabb, pair_offset, geo, gid_sorted, tile_offsets,
          records) = ctx.saved_tensors
         n, frames, h, w, mode, total_pairs, prec_f = ctx.meta
-        b = BinnedFrames(n, frames, h, w, mode, conic, aabb, pair_offset, geo, prec, prec_f, total_pairs, gid_sorted,
+        b = BinnedFrames(n, frames, h, w, mode, conic, aabb, pair_offset, geo, None, prec_f, total_pairs, gid_sorted,
                          tile_offsets)
         grad = grad_out.contiguous()
         if grad.dtype != torch.float32:

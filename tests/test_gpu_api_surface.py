@@ -62,6 +62,46 @@ def test_batched_equals_per_frame_calls(cuda_device, binning, h, w, f, capacity)
         assert torch.equal(x.grad, y.grad)
 
 
+@pytest.mark.parametrize("sizes", [[700], [0, 0, 400], [250, 0], [37] * 12])
+def test_batched_edge_frames(cuda_device, sizes):
+    """One frame, leading and trailing empty frames, a frame whose Gaussians all
+    lie outside it, many small frames: the one-chain batch equals the per-frame
+    calls bit for bit."""
+    from oss_cuda import rasterize_gaussians, rasterize_gaussians_batched
+
+    h, w = 48, 80
+    offs = [0]
+    for s_ in sizes:
+        offs.append(offs[-1] + s_)
+    xy, scale, rot, feat, op = _gaussians(offs[-1], h, w, 3, 17)
+    if len(sizes) > 1 and sizes[0] > 0:
+        xy[: sizes[0]] += torch.tensor([3.0 * w, 0.0], device="cuda")  # the first frame's Gaussians off screen
+    grad = torch.randn((len(sizes), 3, h, w), device="cuda")
+    a = _leaves((xy, scale, rot, feat, op))
+    img = rasterize_gaussians_batched(a[0], a[1], a[2], a[3], offs, h, w, binning="tight3sigma", opacity=a[4])
+    img.backward(grad)
+    b = _leaves((xy, scale, rot, feat, op))
+    for i, (lo, hi) in enumerate(zip(offs, offs[1:])):
+        one = rasterize_gaussians(b[0][lo:hi], b[1][lo:hi], b[2][lo:hi], b[3][lo:hi], h, w, binning="tight3sigma",
+                                  opacity=b[4][lo:hi])
+        assert torch.equal(one.detach(), img[i].detach())
+        one.backward(grad[i])
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)
+
+
+def test_batched_capacity_overflow_zeroes_and_flags(cuda_device):
+    from oss_cuda import pair_capacity_overflowed, rasterize_gaussians_batched
+
+    h, w = 64, 96
+    xy, scale, rot, feat, op = _gaussians(900, h, w, 3, 19)
+    pair_capacity_overflowed()
+    img = rasterize_gaussians_batched(xy, scale, rot, feat, [0, 450, 900], h, w, binning="tight3sigma",
+                                      opacity=op, pair_capacity=10)
+    assert pair_capacity_overflowed()
+    assert not img.any()
+
+
 def test_batched_rejects_bad_offsets(cuda_device):
     from oss_cuda import rasterize_gaussians_batched
 
