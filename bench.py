@@ -848,6 +848,8 @@ def run_ours(args, rank, world, local):
         torch.cuda.empty_cache()
         line["config3"] = config3_object(rank, world, kb, 3)
         torch.cuda.empty_cache()
+        line["batched_api"] = batched_api_object(rank, world, kb, 3)
+        torch.cuda.empty_cache()
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(inp, h, w, args.binning, budget_s=8.0).items()
@@ -1163,6 +1165,52 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
                         f"N={n_shared}, fwd+bwd, NCCL all-reduce (sum) of the shared canvas gradients "
                         f"({n_shared}x9 fp32) on a side stream beside the last frame's own-canvas reduce, "
                         f"{binning} lists; allreduce_ms from the last timed step"}
+
+
+def batched_api_object(rank, world, steps, warmup, frames_per_rank=8):
+    """The public batched API (oss_cuda.rasterize_gaussians_batched: one launch chain
+    over the frames' stacked tile grid) on config-5 frames: per rank 8 frames of 1080p,
+    each its own 200k Gaussians plus the shared 50k, fwd+bwd through autograd with a
+    pair capacity, the whole step captured in one CUDA graph; ranks independent."""
+    from oss_cuda import pair_capacity_overflowed, rasterize_gaussians_batched
+
+    h, w, lsm, lss = 1080, 1920, math.log(2.0), 0.3
+    n_own, n_shared = 200_000, 50_000
+    device = torch.device("cuda", torch.cuda.current_device())
+    shared = make_inputs(h, w, n_shared, lsm, lss, seed=555)
+    keys = ("xy", "scale", "rot", "rgb", "opacity")
+    parts = {k: [] for k in keys}
+    grads = []
+    for f in range(frames_per_rank):
+        own = make_inputs(h, w, n_own, lsm, lss, seed=20_000 + rank * frames_per_rank + f)
+        for k in keys:
+            parts[k] += [own[k], shared[k]]
+        grads.append(own["grad"])
+    leaves = [torch.from_numpy(np.concatenate(parts[k])).to(device).requires_grad_(True) for k in keys]
+    grad = torch.from_numpy(np.stack(grads)).to(device)
+    n = n_own + n_shared
+    offs = [f * n for f in range(frames_per_rank + 1)]
+    cap = 1_000_000 * frames_per_rank  # about 0.8M pairs per frame
+
+    def body():
+        img = rasterize_gaussians_batched(*leaves[:4], offs, h, w, binning="tight3sigma", opacity=leaves[4],
+                                          pair_capacity=cap)
+        torch.autograd.grad(img, leaves, grad)
+
+    pair_capacity_overflowed()
+    graph = capture_graph(body)
+    ms, clocks = timed(graph.replay, steps, warmup, device, world)
+    overflow = pair_capacity_overflowed()
+    del graph
+    torch.cuda.synchronize()
+    if overflow:
+        raise RuntimeError("batched_api: pair capacity exceeded")
+    return {"value": world * frames_per_rank * h * w / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms,
+            "steps": steps, "frames_per_rank": frames_per_rank, "ms_per_frame": ms / frames_per_rank,
+            "scaling": "weak", "clocks": clocks,
+            "workload": f"oss_cuda.rasterize_gaussians_batched + torch.autograd.grad, {frames_per_rank} frames "
+                        f"{w}x{h} per rank (each own N={n_own} + shared N={n_shared}), fwd+bwd, pair capacity, "
+                        "the step captured in one CUDA graph"}
 
 
 def run_config5(args, rank, world):
