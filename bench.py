@@ -1092,55 +1092,57 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
     """Config 5: 64 frames at 1080p split across ranks; each frame renders its own 200k
     canvas plus a shared 50k canvas (fwd+bwd); the shared canvas's per-Gaussian
     gradients (xy 2, scale 2, rot 1, opacity 1, rgb 3) are summed over the rank's
-    frames and all-reduced over NCCL once per step.  The all-reduce runs on a side
-    stream: the last frame reduces its shared Gaussians' gradients first, the
-    all-reduce starts, and the own canvas's reduce of that frame runs beside it."""
-    from oss_b200.distributed import pack_shared_grads, reduce_shared_grads
-    from oss_cuda import _lib
+    frames and all-reduced over NCCL once per step.  A rank's frames go through the
+    public batched API (oss_cuda.rasterize_gaussians_batched: one launch chain over
+    the frames' stacked tile grid) with autograd and a pair capacity, captured with
+    the sums of the shared rows in one CUDA graph; the all-reduce runs on a side
+    stream after it."""
+    from oss_b200.distributed import SHARED_GRAD_FIELDS, reduce_shared_grads
+    from oss_cuda import _lib, pair_capacity_overflowed, rasterize_gaussians_batched
 
     h, w, lsm, lss = 1080, 1920, math.log(2.0), 0.3
     n_own, n_shared = 200_000, 50_000
+    n = n_own + n_shared
     device = torch.device("cuda", torch.cuda.current_device())
     shared = make_inputs(h, w, n_shared, lsm, lss, seed=555)
     frames = rank_frames(64, rank, world)
-    per_frame = []
+    nf = len(frames)
+    keys = ("xy", "scale", "rot", "rgb", "opacity")
+    parts = {k: [] for k in keys}
+    grads = []
     for f in frames:
         own = make_inputs(h, w, n_own, lsm, lss, seed=10_000 + f)
-        per_frame.append({k: torch.from_numpy(np.concatenate([own[k], shared[k]]) if k != "grad" else own[k]).to(device)
-                          for k in own})
-    pipe = Pipeline(n_own + n_shared, h, w, _lib.BINNING_MODES[binning], device)
+        for k in keys:
+            parts[k] += [own[k], shared[k]]
+        grads.append(own["grad"])
+    leaves = [torch.from_numpy(np.concatenate(parts[k])).to(device).requires_grad_(True) for k in keys]
+    del parts
+    grad = torch.from_numpy(np.stack(grads)).to(device)
+    del grads
+    offs = [b * n for b in range(nf + 1)]
+    cap = 1_000_000 * max(1, nf)  # about 0.8M pairs per frame
     d_shared = torch.zeros((n_shared, 9), device=device, dtype=torch.float32)
     comm = torch.cuda.Stream()
     ev_ready, ev_done = torch.cuda.Event(), torch.cuda.Event()
     ar_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-    sl = slice(n_own, n_own + n_shared)
+    mode_name = binning if binning in _lib.BINNING_MODES else "tight3sigma"
 
-    # size the pair capacity over every frame (host reads of the totals), then capture the
-    # rank's frames as one sync-free CUDA graph: every frame's step and the accumulation of
-    # its shared-canvas gradients, the last frame reducing its shared Gaussians first; the
-    # last frame's own-canvas reduce is a second graph that runs beside the all-reduce
-    for d in per_frame:
-        pipe.step(d, sync=True, timed=False)
-    torch.cuda.synchronize()
+    def body():
+        img = rasterize_gaussians_batched(*leaves[:4], offs, h, w, binning=mode_name, opacity=leaves[4],
+                                          pair_capacity=cap)
+        g = dict(zip(("d_xy", "d_scale", "d_rot", "d_rgb", "d_opacity"), torch.autograd.grad(img, leaves, grad)))
+        col = 0
+        for name, width in SHARED_GRAD_FIELDS:  # the shared rows of every frame, summed
+            v = g[name].reshape(nf, n, width)[:, n_own:]
+            d_shared[:, col:col + width] = v.sum(0)
+            col += width
 
-    def frames_body():
-        d_shared.zero_()
-        for i, d in enumerate(per_frame):
-            last = i + 1 == len(per_frame)
-            pipe.step(d, timed=False, reduce=not last)
-            if last:
-                pipe.reduce_range(d, n_own, n_own + n_shared)
-            d_shared.add_(pack_shared_grads(pipe.grads, sl))
-
-    def own_body():
-        if per_frame:
-            pipe.reduce_range(per_frame[-1], 0, n_own)
-
-    graphs = [capture_graph(frames_body), capture_graph(own_body)]
+    pair_capacity_overflowed()
+    graph = capture_graph(body)
 
     def step():
         main = torch.cuda.current_stream()
-        graphs[0].replay()
+        graph.replay()
         ev_ready.record(main)
         with torch.cuda.stream(comm):
             comm.wait_event(ev_ready)
@@ -1148,23 +1150,25 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
             reduce_shared_grads(d_shared)  # NCCL all-reduce (sum) over ranks
             ar_events[1].record(comm)
             ev_done.record(comm)
-        graphs[1].replay()  # the last frame's own canvas, beside the all-reduce
         main.wait_event(ev_done)
 
     ms, clocks = timed(step, steps, warmup, device, world)
-    pipe.check_overflow()
-    del graphs
+    overflow = pair_capacity_overflowed()
+    del graph
     torch.cuda.synchronize()
+    if overflow:
+        raise RuntimeError("config5: pair capacity exceeded")
     allreduce = ar_events[0].elapsed_time(ar_events[1])
     ar = rank_list(allreduce, world)
     return {"value": 64 * h * w / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms, "steps": steps,
-            "frames_per_rank": len(frames), "ms_per_frame": ms / max(1, len(frames)),
+            "frames_per_rank": nf, "ms_per_frame": ms / max(1, nf),
             "allreduce_ms": max(ar), "allreduce_ms_per_rank": ar, "allreduce_bytes": n_shared * 9 * 4,
             "scaling": "strong", "clocks": clocks,
             "workload": f"config5: 64 frames {w}x{h} split over {world} rank(s), each own N={n_own} + shared "
-                        f"N={n_shared}, fwd+bwd, NCCL all-reduce (sum) of the shared canvas gradients "
-                        f"({n_shared}x9 fp32) on a side stream beside the last frame's own-canvas reduce, "
-                        f"{binning} lists; allreduce_ms from the last timed step"}
+                        f"N={n_shared}, fwd+bwd through oss_cuda.rasterize_gaussians_batched (one chain over the "
+                        f"rank's frames) and autograd, the shared rows' gradients summed over the frames, NCCL "
+                        f"all-reduce (sum) of them ({n_shared}x9 fp32) on a side stream, {mode_name} lists; "
+                        f"allreduce_ms from the last timed step"}
 
 
 def batched_api_object(rank, world, steps, warmup, frames_per_rank=8):
