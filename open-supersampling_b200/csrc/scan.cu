@@ -23,6 +23,9 @@ constexpr int kScanBlocksThreads = 1024;
 constexpr int kSingleItems = 8;
 constexpr int64_t kSingleMax = kScanBlocksThreads * kSingleItems;  // 8192 (32 KB of static shared memory)
 constexpr int64_t kRedundantMaxBlocks = 2048;
+// Tile blocks up to which each block sums the counts before it itself (one frame
+// of 4K has 32 blocks of 1024 tiles).
+constexpr int64_t kTileBlocksRedundant = 16;
 
 // Exclusive block scan of one int64 per thread; returns the block total in `total`.
 template <int NT>
@@ -161,24 +164,31 @@ __global__ void __launch_bounds__(NT) k_scan_apply(const int32_t* in, int32_t* o
 // offsets[t] = sum of the counts before t, offsets[num_tiles] = the total.  The
 // block sums every count before its own range itself (at most num_tiles reads),
 // so the blocks need no second pass.
+// With block_counts (one int per block of TILE tiles, written by k_tile_block_counts)
+// the block sums those instead of every count before its range: linear in the tile
+// count, for the grids of many stacked frames.
 template <int NT, int ITEMS>
 __device__ __forceinline__ void strided_scan_block(const int32_t* __restrict__ count, int stride,
                                                    int64_t num_tiles, int32_t* __restrict__ offsets, int64_t blk,
-                                                   int64_t nblk) {
+                                                   int64_t nblk, const int32_t* __restrict__ block_counts) {
     constexpr int TILE = NT * ITEMS;
     __shared__ long long s_warp[32];
     const int64_t base = blk * TILE;
-    // every count before this block; unrolled so the strided loads overlap
     long long part = 0;
-    int64_t t = threadIdx.x;
-    for (; t + 7 * NT < base; t += 8 * NT) {
-        int32_t c[8];
+    if (block_counts != nullptr) {
+        for (int64_t b = threadIdx.x; b < blk; b += NT) part += block_counts[b * TILE * stride];
+    } else {
+        // every count before this block; unrolled so the strided loads overlap
+        int64_t t = threadIdx.x;
+        for (; t + 7 * NT < base; t += 8 * NT) {
+            int32_t c[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) c[u] = count[(t + u * NT) * stride];
+            for (int u = 0; u < 8; ++u) c[u] = count[(t + u * NT) * stride];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) part += c[u];
+            for (int u = 0; u < 8; ++u) part += c[u];
+        }
+        for (; t < base; t += NT) part += count[t * stride];
     }
-    for (; t < base; t += NT) part += count[t * stride];
     long long prefix;
     block_exclusive_scan<NT>(part, s_warp, prefix);
     int32_t v[ITEMS];
@@ -209,12 +219,31 @@ __global__ void __launch_bounds__(NT) k_prepare_scan(const int32_t* in, int32_t*
                                                      int64_t* __restrict__ total_out,
                                                      const int32_t* __restrict__ tile_count, int count_stride,
                                                      int64_t num_tiles, int32_t* __restrict__ tile_offsets,
-                                                     int64_t ntb) {
+                                                     int64_t ntb, const int32_t* __restrict__ block_counts) {
     if (blockIdx.x < nb) {
         scan_apply_block<NT, ITEMS>(in, out, n, block_sums, 1, nb, 1, total_out, blockIdx.x);
     } else {
-        strided_scan_block<NT, ITEMS>(tile_count, count_stride, num_tiles, tile_offsets, blockIdx.x - nb, ntb);
+        strided_scan_block<NT, ITEMS>(tile_count, count_stride, num_tiles, tile_offsets, blockIdx.x - nb, ntb,
+                                      block_counts);
     }
+}
+
+// Sum of the counts of each block of kPrepTile tiles, stored in the block's
+// first counter line at int 1 (the lines are kTileCountStride ints wide and only
+// int 0 holds a count), for strided_scan_block.
+__global__ void __launch_bounds__(kPrepThreads) k_tile_block_counts(int32_t* __restrict__ tile_count, int stride,
+                                                                     int64_t num_tiles) {
+    __shared__ long long s_warp[32];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kPrepTile;
+    long long sum = 0;
+#pragma unroll
+    for (int k = 0; k < kPrepTile / kPrepThreads; ++k) {
+        const int64_t t = base + k * kPrepThreads + threadIdx.x;
+        if (t < num_tiles) sum += tile_count[t * stride];
+    }
+    long long total;
+    block_exclusive_scan<kPrepThreads>(sum, s_warp, total);
+    if (threadIdx.x == 0) tile_count[base * stride + 1] = static_cast<int32_t>(total);
 }
 
 // Whole scan in one CTA for n <= kSingleMax.
@@ -303,8 +332,16 @@ cudaError_t scan_apply_with_block_sums(const int32_t* in, int32_t* out, int64_t 
     }
     const int64_t nb = div_up(n, kPrepTile);
     if (nb + ntb == 0) return cudaGetLastError();
+    // many tile blocks (stacked frames): per-block tile sums first, so that no block
+    // sums every count before its range
+    const int32_t* block_counts = nullptr;
+    if (ntb > kTileBlocksRedundant) {
+        k_tile_block_counts<<<static_cast<unsigned>(ntb), kPrepThreads, 0, stream>>>(
+            const_cast<int32_t*>(tile_count), count_stride, num_tiles);
+        block_counts = tile_count + 1;
+    }
     k_prepare_scan<kPrepThreads, kItems><<<static_cast<unsigned>(nb + ntb), kPrepThreads, 0, stream>>>(
-        in, out, n, block_sums, nb, total_out, tile_count, count_stride, num_tiles, tile_offsets, ntb);
+        in, out, n, block_sums, nb, total_out, tile_count, count_stride, num_tiles, tile_offsets, ntb, block_counts);
     return cudaGetLastError();
 }
 

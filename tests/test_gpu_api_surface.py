@@ -90,6 +90,29 @@ def test_batched_edge_frames(cuda_device, sizes):
         assert torch.equal(x.grad, y.grad)
 
 
+def test_batched_many_frames(cuda_device):
+    """40 frames of 270x480 (20,400 tiles in the stacked grid: the tile-offset scan
+    takes its per-block sums first) against per-frame calls, images and gradients
+    bit for bit."""
+    from oss_cuda import rasterize_gaussians, rasterize_gaussians_batched
+
+    h, w, frames, per = 270, 480, 40, 500
+    offs = [f * per for f in range(frames + 1)]
+    xy, scale, rot, feat, op = _gaussians(offs[-1], h, w, 3, 23)
+    grad = torch.randn((frames, 3, h, w), device="cuda")
+    a = _leaves((xy, scale, rot, feat, op))
+    img = rasterize_gaussians_batched(a[0], a[1], a[2], a[3], offs, h, w, binning="exact56", opacity=a[4])
+    img.backward(grad)
+    b = _leaves((xy, scale, rot, feat, op))
+    for i, (lo, hi) in enumerate(zip(offs, offs[1:])):
+        one = rasterize_gaussians(b[0][lo:hi], b[1][lo:hi], b[2][lo:hi], b[3][lo:hi], h, w, binning="exact56",
+                                  opacity=b[4][lo:hi])
+        assert torch.equal(one.detach(), img[i].detach())
+        one.backward(grad[i])
+    for x, y in zip(a, b):
+        assert torch.equal(x.grad, y.grad)
+
+
 def test_batched_capacity_overflow_zeroes_and_flags(cuda_device):
     from oss_cuda import pair_capacity_overflowed, rasterize_gaussians_batched
 
