@@ -31,6 +31,8 @@
 // and the conic -> (scale, rot) chain rule and the opacity unfold.  Atomic mode
 // (caller-supplied lists) adds each pair's partials with fp32 atomics: (F+5)
 // atomics per pair instead of the reference's (F+5) per pixel-pair.
+#include <atomic>
+
 #include "internal.h"
 #include "oss_common.cuh"
 
@@ -773,18 +775,20 @@ __global__ void __launch_bounds__(256) k_reduce_gaussian(int n, int F, const flo
 // (cached per device), never more than the table's largest item count needs.
 template <int FC, int MODE, bool WIN = false, bool FRAMES = false>
 int bwd_grid(int64_t max_items, int smem) {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];  // 0 until queried; host threads may race to store the same value
     const int64_t need = div_up(max_items, BwdCfg<FC>::WARPS);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return static_cast<int>(need);
-    if (cached[dev] == 0) {
+    int grid = cached[dev].load(std::memory_order_relaxed);
+    if (grid == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_bwd<FC, MODE, WIN, FRAMES>, BwdCfg<FC>::THREADS,
                                                       smem);
-        cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
+        grid = sms > 0 && per > 0 ? sms * per : 1;
+        cached[dev].store(grid, std::memory_order_relaxed);
     }
-    return static_cast<int>(need < cached[dev] ? need : cached[dev]);
+    return static_cast<int>(need < grid ? need : grid);
 }
 
 template <int FC, int MODE, bool FRAMES>

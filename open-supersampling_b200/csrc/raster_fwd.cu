@@ -33,6 +33,8 @@
 // well-conditioned (det >= 1e-3 * a * d, i.e. axis ratio below ~60) has
 // q' <= 0 at every pixel even after fp32 rounding, so it runs without the
 // per-pixel test; other batches keep it.
+#include <atomic>
+
 #include "internal.h"
 #include "oss_common.cuh"
 
@@ -664,16 +666,18 @@ __global__ void __launch_bounds__(FwdCfg<FC>::NT) k_render_fwd_pipe(int F, int H
 // CTAs per SM the pipelined forward runs with (queried once per device).
 template <int FC, bool WIN = false, bool FRAMES = false>
 int pipe_grid(int num_tiles) {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];  // 0 until queried; host threads may race to store the same value
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_tiles;
-    if (cached[dev] == 0) {
+    int grid = cached[dev].load(std::memory_order_relaxed);
+    if (grid == 0) {
         int sms = 0, per = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_render_fwd_pipe<FC, WIN, FRAMES>, FwdCfg<FC>::NT, 0);
-        cached[dev] = sms > 0 && per > 0 ? sms * per : 1;
+        grid = sms > 0 && per > 0 ? sms * per : 1;
+        cached[dev].store(grid, std::memory_order_relaxed);
     }
-    return num_tiles < cached[dev] ? num_tiles : cached[dev];
+    return num_tiles < grid ? num_tiles : grid;
 }
 
 template <int FC, bool FRAMES>

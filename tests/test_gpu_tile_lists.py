@@ -2,7 +2,8 @@
 (tile << 32 | gid) lists in every sort tier, the device-side capacity check,
 and the sync-free path captured in a CUDA graph.  Every list case runs through
 both the two-call path (oss_render_prepare + oss_bin_pairs) and the one-call
-path (oss_render_bin: last-CTA offset scans, lists sorted inside the scatter).
+path (oss_render_bin: the same kernels behind one entry point, which also
+takes stacked frames).
 """
 from __future__ import annotations
 
