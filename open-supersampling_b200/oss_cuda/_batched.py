@@ -17,19 +17,32 @@ from . import _lib
 from ._raster import INT32_MAX, aligned, read_total, stream_of, sticky_overflow
 
 
-_FRAME_OFFSETS = {}
+_FRAME_OFFSETS = {}  # (device, offsets) -> device tensor, least recently used first
+_CAPTURED = set()  # keys used inside a CUDA-graph capture: the graph reads them on every replay
+_MAX_UNCAPTURED = 64
 
 
 def frame_offsets_on(device, offsets) -> torch.Tensor:
     """The frame offsets as a device int32 tensor, made once per device and
-    offsets (a host copy would break CUDA-graph capture of later calls)."""
-    key = (torch.device(device).index, tuple(offsets))
-    t = _FRAME_OFFSETS.get(key)
+    offsets (a host copy would break CUDA-graph capture of later calls).
+
+    A tensor used while a graph was being captured is kept for the life of the
+    process, since the graph keeps its address; of the others, the least
+    recently used is dropped beyond 64 (kernels already queued that read it
+    keep its memory: the tensor is recorded on each stream that used it)."""
+    dev = torch.device(device)
+    key = (dev.index, tuple(int(v) for v in offsets))
+    t = _FRAME_OFFSETS.pop(key, None)
     if t is None:
-        if len(_FRAME_OFFSETS) > 64:
-            _FRAME_OFFSETS.clear()
-        t = torch.tensor(offsets, device=device, dtype=torch.int32)
-        _FRAME_OFFSETS[key] = t
+        t = torch.tensor(key[1], device=dev, dtype=torch.int32)
+    _FRAME_OFFSETS[key] = t
+    if torch.cuda.is_current_stream_capturing():
+        _CAPTURED.add(key)
+    else:
+        t.record_stream(torch.cuda.current_stream(dev))
+        spare = [k for k in _FRAME_OFFSETS if k not in _CAPTURED]
+        for k in spare[:max(0, len(spare) - _MAX_UNCAPTURED)]:
+            del _FRAME_OFFSETS[k]
     return t
 
 

@@ -125,6 +125,36 @@ def test_batched_capacity_overflow_zeroes_and_flags(cuda_device):
     assert not img.any()
 
 
+def test_batched_graph_outlives_offset_cache_eviction(cuda_device):
+    """A graph captured with one frame split still renders it after 70 other
+    splits have passed through the offsets cache: the captured split's device
+    tensor is kept, the uncaptured ones are dropped beyond 64."""
+    from oss_cuda import _batched, rasterize_gaussians_batched
+
+    h, w, n = 48, 64, 600
+    xy, scale, rot, feat, op = _gaussians(n, h, w, 3, 29)
+    offs = [0, 250, n]
+    kw = dict(binning="tight3sigma", opacity=op, pair_capacity=20_000)
+    want = rasterize_gaussians_batched(xy, scale, rot, feat, offs, h, w, **kw)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        rasterize_gaussians_batched(xy, scale, rot, feat, offs, h, w, **kw)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        got = rasterize_gaussians_batched(xy, scale, rot, feat, offs, h, w, **kw)
+    for k in range(70):
+        rasterize_gaussians_batched(xy, scale, rot, feat, [0, 100 + k, n], h, w, **kw)
+    key = (torch.cuda.current_device(), tuple(offs))
+    assert key in _batched._FRAME_OFFSETS
+    assert sum(k not in _batched._CAPTURED for k in _batched._FRAME_OFFSETS) <= _batched._MAX_UNCAPTURED
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    del graph
+
+
 def test_batched_rejects_bad_offsets(cuda_device):
     from oss_cuda import rasterize_gaussians_batched
 
