@@ -951,8 +951,11 @@ def rank_frames(total, rank, world):
 
 def timed(step, K, W, device, world):
     """W warm-up steps, then K steps each bracketed by CUDA events on the current
-    stream with a 256 MiB L2 flush between them; returns (ms per step, max over
-    ranks), clock summary."""
+    stream with a 256 MiB L2 flush between them, queued back to back with no host
+    synchronisation between steps (as the headline's replays and a training loop
+    run: a per-step host wait would put each rank's wake-up jitter inside the
+    steps that hold a collective); returns (ms per step, max over ranks), clock
+    summary."""
     flush = torch.empty((256 << 20,), device=device, dtype=torch.uint8)
     for _ in range(max(3, W)):
         step()
@@ -961,16 +964,16 @@ def timed(step, K, W, device, world):
         import torch.distributed as dist
 
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    total = 0.0
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     with ClockSampler(device.index) as clocks:
-        for _ in range(K):
+        for e0, e1 in ev:
             flush.zero_()
             e0.record()
             step()
             e1.record()
-            torch.cuda.synchronize()
-            total += e0.elapsed_time(e1)
+        torch.cuda.synchronize()
+    total = sum(e0.elapsed_time(e1) for e0, e1 in ev)
     ms = torch.tensor([total / K], device=device, dtype=torch.float64)
     if world > 1:
         dist.barrier()
