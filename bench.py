@@ -974,6 +974,7 @@ def timed(step, K, W, device, world):
             e1.record()
         torch.cuda.synchronize()
     total = sum(e0.elapsed_time(e1) for e0, e1 in ev)
+    timed.rank_ms = rank_list(total / K, world)  # every rank's own ms per step (every rank gathers)
     ms = torch.tensor([total / K], device=device, dtype=torch.float64)
     if world > 1:
         dist.barrier()
@@ -1164,7 +1165,7 @@ def config5_object(rank, world, steps, warmup, binning="tight3sigma"):
     allreduce = ar_events[0].elapsed_time(ar_events[1])
     ar = rank_list(allreduce, world)
     return {"value": 64 * h * w / (ms * 1e-3) / 1e6, "unit": UNIT, "ms_per_step": ms, "steps": steps,
-            "frames_per_rank": nf, "ms_per_frame": ms / max(1, nf),
+            "frames_per_rank": nf, "ms_per_frame": ms / max(1, nf), "ms_per_rank": timed.rank_ms,
             "allreduce_ms": max(ar), "allreduce_ms_per_rank": ar, "allreduce_bytes": n_shared * 9 * 4,
             "scaling": "strong", "clocks": clocks,
             "workload": f"config5: 64 frames {w}x{h} split over {world} rank(s), each own N={n_own} + shared "
